@@ -1,0 +1,113 @@
+/*
+ * moe_b200.h -- C ABI of libmoe_b200.so, the B200 (sm_100a) implementation of the
+ * routed-expert MoE block of Jakevin/moe-offload.
+ *
+ * Conventions
+ *   - Every device buffer is a raw device pointer owned by the caller (PyTorch tensors on
+ *     the Python side); the library never frees caller memory.
+ *   - bf16 / fp16 tensors are passed as `void *` and are 16-bit IEEE bit patterns;
+ *     `sb_fp16` selects fp16 (1) or bf16 (0) for affine scales and biases.
+ *   - `stream` is a cudaStream_t passed as `void *` (NULL = legacy default stream).
+ *   - Functions returning int return MOE_OK (0) or a negative status; moe_last_error()
+ *     gives a message for the calling thread's last failure.
+ *   - Expert weights use MLX's affine layout with transpose=True, exactly as the reference
+ *     keeps them in its slot buffers (mlx-qwen38/loader.py:332-368):
+ *       gate/up  codes u32 [cap, I, H*bits/32], scales/biases [cap, I, H/group_size]
+ *       down     codes u32 [cap, H, I*bits/32], scales/biases [cap, H, I/group_size]
+ *     `slots` index the leading `cap` axis (expert ids when all experts are resident).
+ *
+ * Citations name files of the reference project (paths inside Jakevin/moe-offload).
+ */
+#ifndef MOE_B200_H
+#define MOE_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define MOE_OK 0
+#define MOE_EIO (-5)
+#define MOE_ENOMEM (-12)
+#define MOE_ENODEV (-19)
+#define MOE_EINVAL (-22)
+#define MOE_ETIMEDOUT (-110)
+#define MOE_ECUDA (-1000)
+
+/* Library version (major*10000 + minor*100 + patch) and the calling thread's last error. */
+int moe_version(void);
+const char *moe_last_error(void);
+
+/* ------------------------------------------------------------------------------------ */
+/* Router: gate matmul + precise softmax + top-k + renormalisation, optionally fused with   */
+/* the next layer's top-M prediction.                                                     */
+/* ------------------------------------------------------------------------------------ */
+
+/*
+ * Bytes of workspace moe_router_topk needs for T tokens, E experts and an optional
+ * prediction of M experts (M = 0: none). The workspace must be zero-filled once before its
+ * first use; every call leaves it zero-filled again.
+ */
+size_t moe_router_workspace_bytes(int T, int E, int M);
+
+/*
+ * Replaces, per token row of x:
+ *   gates = gate(x); gates = softmax(gates, precise=True); inds = argpartition(gates, -K)[-K:];
+ *   scores = take(gates, inds); scores /= scores.sum()          -- mlx-qwen38/loader.py:903-908,
+ *                                                                  cpp/src/layers.cpp:311-325
+ * and, when wn != NULL, topk_sorted_indices(gate_next(x) + pred_bias, M)
+ *                                                               -- loader.py:237-242,950-956,
+ *                                                                  cpp/src/layers.cpp:327-341
+ *   x        bf16 [T, H]
+ *   w        router weight: bf16 [E, H] when rbits == 16, else affine u32 [E, H*rbits/32]
+ *            with w_scales/w_biases [E, H/group_size]
+ *   wn       next layer's router (same format) or NULL; pred_bias fp32 [E] or NULL
+ *   out_logits bf16 [T, E] or NULL; out_probs bf16 [T, E] or NULL
+ *   out_inds  u32 [T, K] (MLX argpartition order), out_scores bf16 [T, K]
+ *   out_pred  u32 [T, M] sorted by value descending, or NULL
+ * Arithmetic: dot products in double, rounded once to bf16; softmax in double, rounded
+ * once to bf16; ties in the top-k resolved toward the higher expert index.
+ */
+int moe_router_topk(const void *x, int T, int H, int E, int K,
+                    const void *w, const void *w_scales, const void *w_biases,
+                    int rbits, int group_size, int sb_fp16,
+                    const void *wn, const void *wn_scales, const void *wn_biases,
+                    int M, const float *pred_bias,
+                    void *out_logits, void *out_probs, uint32_t *out_inds, void *out_scores,
+                    uint32_t *out_pred, void *workspace, size_t workspace_bytes, void *stream);
+
+/* ------------------------------------------------------------------------------------ */
+/* Routed experts, decode (one row of x per token).                                       */
+/* ------------------------------------------------------------------------------------ */
+
+/*
+ * act[t,k,:] = SwiGLU(gate_qmm(x[t], W_gate[slots[t,k]]), up_qmm(x[t], W_up[slots[t,k]]))
+ * Replaces the up/gate gather_qmm + swiglu of mlx_vlm SwitchGLU
+ * (cpp/src/layers.cpp:343-358, cpp/src/kernels.cpp:1027-1040,1090-1094).
+ *   x bf16 [T, H], slots u32 [T, K] (each < cap, the slot-buffer depth), act bf16 [T, K, I].
+ *   bits == 2, group_size == 64. A slot >= cap is not read; its activations are zero.
+ */
+int moe_experts_gateup(const void *x, int T, int H, int I, int K, int cap, const uint32_t *slots,
+                       const uint32_t *wg, const void *sg, const void *bg,
+                       const uint32_t *wu, const void *su, const void *bu,
+                       int bits, int group_size, int sb_fp16, void *act, void *stream);
+
+/*
+ * yk[t,k,:] = down_qmm(act[t,k], W_down[slots[t,k]])               (layers.cpp:359-361)
+ * y[t,:]    = sum_k yk[t,k,:] * scores[t,k] (+ addend[t]) (+ resid[t])
+ *                                          (loader.py:914,965; cpp/src/layers.cpp:400,599)
+ *   act bf16 [T, K, I]; scores bf16 [T, K] or NULL (then y is not written);
+ *   addend / resid bf16 [T, H] or NULL; y bf16 [T, H] or NULL; yk bf16 [T, K, H] or NULL.
+ */
+int moe_experts_down(const void *act, int T, int H, int I, int K, int cap, const uint32_t *slots,
+                     const void *scores, const uint32_t *wd, const void *sd, const void *bd,
+                     int bits, int group_size, int sb_fp16, const void *addend, const void *resid,
+                     void *y, void *yk, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MOE_B200_H */

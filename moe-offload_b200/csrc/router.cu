@@ -1,0 +1,370 @@
+// Router: gate GEMV (exact double accumulation, one bf16 rounding) fused with the
+// precise softmax, MLX-order top-k, renormalisation and the optional next-layer top-M
+// prediction. One launch per layer step:
+//
+//   grid (ceil(R / 8), T), 256 threads; R = E rows of this layer's router plus, when a
+//   prediction is requested, E rows of the next layer's router (same input x, the way
+//   loader.py:950-958 evaluates inds and pred_next in one sync). Each warp produces one
+//   logit; the last CTA to finish a token (atomic ticket in the workspace) runs the
+//   softmax / selection tail for that token and re-arms the ticket.
+//
+// Reference semantics: mlx-qwen38/loader.py:903-908 (router), loader.py:237-242
+// (topk_sorted_indices); cpp/src/layers.cpp:311-341.
+#include "common.cuh"
+
+namespace {
+
+constexpr int kWarps = 8;
+constexpr int kThreads = kWarps * 32;
+constexpr int kMaxE = 4096;              // experts per layer supported by the tail
+constexpr int kMaxPerThread = kMaxE / kThreads;
+
+struct RouterArgs {
+    const uint16_t *x;
+    int T, H, E, K, M, gs;
+    const void *w;
+    const uint16_t *ws, *wb;
+    const void *wn;
+    const uint16_t *wns, *wnb;
+    const float *pred_bias;
+    uint16_t *logits;     // [T, E]
+    uint16_t *plogits;    // [T, E] (prediction rows), may be null when M == 0
+    uint16_t *probs;      // [T, E] or null
+    uint32_t *inds;       // [T, K]
+    uint16_t *scores;     // [T, K]
+    uint32_t *pred;       // [T, M] or null
+    unsigned int *tickets;  // [T], zero between launches
+};
+
+// ---------------------------------------------------------------- row dot products
+
+// bf16 weights: lanes stride over 16-byte chunks (8 values); products exact in double.
+MOE_D double row_dot_bf16(const uint16_t *__restrict__ x, const uint16_t *__restrict__ w, int H,
+                          int lane) {
+    const int nchunk = H >> 3;
+    double acc = 0.0;
+    constexpr int kPre = 16;
+    uint4 wv[kPre];
+#pragma unroll
+    for (int j = 0; j < kPre; ++j) {
+        const int c = lane + 32 * j;
+        wv[j] = (c < nchunk) ? ldg_stream16(w + 8 * c) : make_uint4(0, 0, 0, 0);
+    }
+#pragma unroll
+    for (int j = 0; j < kPre; ++j) {
+        const int c = lane + 32 * j;
+        if (c < nchunk) {
+            const uint4 xv = __ldg(reinterpret_cast<const uint4 *>(x) + c);
+            const uint32_t xs[4] = {xv.x, xv.y, xv.z, xv.w};
+            const uint32_t wsv[4] = {wv[j].x, wv[j].y, wv[j].z, wv[j].w};
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                acc = fma((double)__uint_as_float(xs[q] << 16), (double)__uint_as_float(wsv[q] << 16), acc);
+                acc = fma((double)__uint_as_float(xs[q] & 0xffff0000u), (double)__uint_as_float(wsv[q] & 0xffff0000u), acc);
+            }
+        }
+    }
+    for (int c = lane + 32 * kPre; c < nchunk; c += 32) {   // H > 4096
+        const uint4 xv = __ldg(reinterpret_cast<const uint4 *>(x) + c);
+        const uint4 wv2 = ldg_stream16(w + 8 * c);
+        const uint32_t xs[4] = {xv.x, xv.y, xv.z, xv.w};
+        const uint32_t wsv[4] = {wv2.x, wv2.y, wv2.z, wv2.w};
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            acc = fma((double)__uint_as_float(xs[q] << 16), (double)__uint_as_float(wsv[q] << 16), acc);
+            acc = fma((double)__uint_as_float(xs[q] & 0xffff0000u), (double)__uint_as_float(wsv[q] & 0xffff0000u), acc);
+        }
+    }
+    return acc;
+}
+
+// affine-quantised weights (MLX layout), any bits in {2,4,8}: per 64-code group
+// s * sum(q x) + b * sum(x), every term exact or double-rounded.
+template <bool kFp16>
+MOE_D double row_dot_affine(const uint16_t *__restrict__ x, const uint32_t *__restrict__ w,
+                            const uint16_t *__restrict__ s, const uint16_t *__restrict__ b, int H,
+                            int bits, int gs, int lane) {
+    const int per = 32 / bits;
+    const uint32_t mask = (1u << bits) - 1u;
+    const int ngroups = H / gs;
+    double acc = 0.0;
+    for (int G = lane; G < ngroups; G += 32) {
+        double dq = 0.0, dx = 0.0;
+        for (int j = 0; j < gs; ++j) {
+            const int h = G * gs + j;
+            const double xv = (double)bf16_bits_to_f32(x[h]);
+            const uint32_t q = (__ldg(w + h / per) >> ((h % per) * bits)) & mask;
+            dq = fma((double)q, xv, dq);
+            dx += xv;
+        }
+        acc += (double)sb_to_f32<kFp16>(s[G]) * dq + (double)sb_to_f32<kFp16>(b[G]) * dx;
+    }
+    return acc;
+}
+
+MOE_D double warp_sum_d(double v) {
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+    return v;
+}
+
+// order-preserving 16-bit key of a bf16 value
+MOE_D uint32_t bf16_order_key(uint16_t v) {
+    return (v & 0x8000) ? (uint32_t)(~v & 0xffff) : (uint32_t)(v | 0x8000);
+}
+
+// Selects the n largest of keys[0..E) (all distinct, all > 0) with warp 0; keys of the
+// winners are zeroed in place. Results in descending order.
+MOE_D void warp_select_desc(uint32_t *keys, int E, int n, uint32_t *out) {
+    const int lane = threadIdx.x & 31;
+    for (int r = 0; r < n; ++r) {
+        uint32_t best = 0;
+        for (int e = lane; e < E; e += 32) best = max(best, keys[e]);
+        const uint32_t win = __reduce_max_sync(0xffffffffu, best);
+        if (win != 0 && best == win) {
+            for (int e = lane; e < E; e += 32)
+                if (keys[e] == win) keys[e] = 0;
+        }
+        if (lane == 0) out[r] = win;
+        __syncwarp();
+    }
+}
+
+template <bool kFp16, int kRbits>
+__global__ void __launch_bounds__(kThreads) router_kernel(RouterArgs a) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int t = blockIdx.y;
+    const int rows = a.E * (a.M > 0 ? 2 : 1);
+    const int row = blockIdx.x * kWarps + warp;
+    const uint16_t *x = a.x + (size_t)t * a.H;
+
+    if (row < rows) {
+        const bool next = row >= a.E;
+        const int e = next ? row - a.E : row;
+        double acc;
+        if constexpr (kRbits == 16) {
+            const uint16_t *w = reinterpret_cast<const uint16_t *>(next ? a.wn : a.w) + (size_t)e * a.H;
+            acc = row_dot_bf16(x, w, a.H, lane);
+        } else {
+            const int words = a.H * kRbits / 32, ng = a.H / a.gs;
+            const uint32_t *w = reinterpret_cast<const uint32_t *>(next ? a.wn : a.w) + (size_t)e * words;
+            const uint16_t *s = (next ? a.wns : a.ws) + (size_t)e * ng;
+            const uint16_t *b = (next ? a.wnb : a.wb) + (size_t)e * ng;
+            acc = row_dot_affine<kFp16>(x, w, s, b, a.H, kRbits, a.gs, lane);
+        }
+        acc = warp_sum_d(acc);
+        if (lane == 0) {
+            uint16_t l = f64_to_bf16_bits(acc);
+            if (next) {
+                if (a.pred_bias) l = f32_to_bf16_bits(bf16_bits_to_f32(l) + a.pred_bias[e]);
+                a.plogits[(size_t)t * a.E + e] = l;
+            } else {
+                a.logits[(size_t)t * a.E + e] = l;
+            }
+        }
+    }
+
+    // ------------------------------------------------------------ last CTA of token t
+    __shared__ unsigned int s_last;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        __threadfence();
+        const unsigned int prev = atomicAdd(a.tickets + t, 1u);
+        s_last = (prev == gridDim.x - 1) ? 1u : 0u;
+    }
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+
+    __shared__ uint32_t s_keys[kMaxE];
+    __shared__ float s_red[kWarps];
+    __shared__ double s_redd[kWarps];
+    __shared__ uint32_t s_sel[64];
+    const int E = a.E;
+    const uint16_t *lg = a.logits + (size_t)t * E;
+
+    // max
+    float mx = -INFINITY;
+    float lv[kMaxPerThread];
+#pragma unroll
+    for (int j = 0; j < kMaxPerThread; ++j) {
+        const int e = threadIdx.x + j * kThreads;
+        lv[j] = (e < E) ? bf16_bits_to_f32(__ldcg(lg + e)) : -INFINITY;
+        mx = fmaxf(mx, lv[j]);
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+    if (lane == 0) s_red[warp] = mx;
+    __syncthreads();
+    mx = s_red[0];
+#pragma unroll
+    for (int i = 1; i < kWarps; ++i) mx = fmaxf(mx, s_red[i]);
+
+    // sum of exp in double (fixed reduction order -> deterministic)
+    double ex[kMaxPerThread];
+    double sum = 0.0;
+#pragma unroll
+    for (int j = 0; j < kMaxPerThread; ++j) {
+        const int e = threadIdx.x + j * kThreads;
+        ex[j] = (e < E) ? exp((double)lv[j] - (double)mx) : 0.0;
+        sum += ex[j];
+    }
+    sum = warp_sum_d(sum);
+    if (lane == 0) s_redd[warp] = sum;
+    __syncthreads();
+    sum = 0.0;
+#pragma unroll
+    for (int i = 0; i < kWarps; ++i) sum += s_redd[i];
+
+    // bf16 probabilities and selection keys ((p << 16) | e) + 1, all distinct and > 0
+#pragma unroll
+    for (int j = 0; j < kMaxPerThread; ++j) {
+        const int e = threadIdx.x + j * kThreads;
+        if (e < E) {
+            const uint16_t p = f64_to_bf16_bits(ex[j] / sum);
+            if (a.probs) a.probs[(size_t)t * E + e] = p;
+            s_keys[e] = (((uint32_t)p << 16) | (uint32_t)e) + 1u;
+        }
+    }
+    __syncthreads();
+
+    if (warp == 0) {
+        warp_select_desc(s_keys, E, a.K, s_sel);
+        if (lane == 0) {
+            // MLX order: ascending (p, index)
+            float S = 0.f;
+            for (int k = 0; k < a.K; ++k) {
+                const uint32_t key = s_sel[a.K - 1 - k] - 1u;
+                const float p = bf16_bits_to_f32((uint16_t)(key >> 16));
+                S = (k == 0) ? p : bf16r(S + p);
+            }
+            for (int k = 0; k < a.K; ++k) {
+                const uint32_t key = s_sel[a.K - 1 - k] - 1u;
+                a.inds[(size_t)t * a.K + k] = key & 0xffffu;
+                const float p = bf16_bits_to_f32((uint16_t)(key >> 16));
+                a.scores[(size_t)t * a.K + k] = f32_to_bf16_bits(__fdiv_rn(p, S));
+            }
+        }
+    }
+    __syncthreads();
+
+    if (a.M > 0) {
+        const uint16_t *pl = a.plogits + (size_t)t * E;
+        for (int e = threadIdx.x; e < E; e += kThreads)
+            s_keys[e] = ((bf16_order_key(__ldcg(pl + e)) << 16) | (uint32_t)e) + 1u;
+        __syncthreads();
+        if (warp == 0) {
+            warp_select_desc(s_keys, E, a.M, s_sel);
+            if (lane == 0) {
+                // descending value; equal values in ascending index order
+                int o = 0, i = 0;
+                while (i < a.M) {
+                    const uint32_t v = (s_sel[i] - 1u) >> 16;
+                    int j = i;
+                    while (j + 1 < a.M && ((s_sel[j + 1] - 1u) >> 16) == v) ++j;
+                    for (int q = j; q >= i; --q) a.pred[(size_t)t * a.M + o++] = (s_sel[q] - 1u) & 0xffffu;
+                    i = j + 1;
+                }
+            }
+        }
+    }
+    if (threadIdx.x == 0) a.tickets[t] = 0u;   // re-arm for the next launch
+}
+
+template <bool kFp16>
+cudaError_t launch_router(const RouterArgs &a, int rbits, cudaStream_t st) {
+    const int rows = a.E * (a.M > 0 ? 2 : 1);
+    dim3 grid((rows + kWarps - 1) / kWarps, a.T);
+    switch (rbits) {
+        case 16: router_kernel<kFp16, 16><<<grid, kThreads, 0, st>>>(a); break;
+        case 8: router_kernel<kFp16, 8><<<grid, kThreads, 0, st>>>(a); break;
+        case 4: router_kernel<kFp16, 4><<<grid, kThreads, 0, st>>>(a); break;
+        case 2: router_kernel<kFp16, 2><<<grid, kThreads, 0, st>>>(a); break;
+        default: return cudaErrorInvalidValue;
+    }
+    return cudaGetLastError();
+}
+
+inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+}  // namespace
+
+extern "C" size_t moe_router_workspace_bytes(int T, int E, int M) {
+    if (T <= 0 || E <= 0) return 0;
+    size_t b = align_up((size_t)T * sizeof(unsigned int), 256);        // tickets
+    b += align_up((size_t)T * E * sizeof(uint16_t), 256);               // logits
+    if (M > 0) b += align_up((size_t)T * E * sizeof(uint16_t), 256);    // prediction logits
+    return b;
+}
+
+// Validates arguments and launches with the given ticket/logit buffers; shared by the
+// workspace entry point and any caller that supplies its own scratch.
+int moe_router_launch(const void *x, int T, int H, int E, int K, const void *w,
+                      const void *w_scales, const void *w_biases, int rbits, int group_size,
+                      int sb_fp16, const void *wn, const void *wn_scales, const void *wn_biases,
+                      int M, const float *pred_bias, void *out_logits, void *out_probs,
+                      uint32_t *out_inds, void *out_scores, uint32_t *out_pred,
+                      unsigned int *tickets, uint16_t *logits_buf, uint16_t *plogits_buf,
+                      void *stream) {
+    if (!x || !w || !out_inds || !out_scores || !tickets)
+        return moe_set_error(MOE_EINVAL, "router: null required pointer");
+    if (T <= 0 || H <= 0 || E <= 0 || E > kMaxE || K <= 0 || K > E || K > 64)
+        return moe_set_error(MOE_EINVAL, "router: bad sizes T=%d H=%d E=%d K=%d", T, H, E, K);
+    if (M < 0 || M > E || M > 64 || (M > 0 && (!wn || !out_pred)))
+        return moe_set_error(MOE_EINVAL, "router: bad prediction arguments M=%d", M);
+    if (rbits == 16) {
+        if (H % 8) return moe_set_error(MOE_EINVAL, "router: H=%d must be a multiple of 8", H);
+        if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(w) |
+             reinterpret_cast<uintptr_t>(wn)) & 15)
+            return moe_set_error(MOE_EINVAL, "router: x/w must be 16-byte aligned");
+    } else if (rbits == 8 || rbits == 4 || rbits == 2) {
+        if (group_size <= 0 || H % group_size || group_size % (32 / rbits))
+            return moe_set_error(MOE_EINVAL, "router: bad group_size %d", group_size);
+        if (!w_scales || !w_biases || (M > 0 && (!wn_scales || !wn_biases)))
+            return moe_set_error(MOE_EINVAL, "router: affine router needs scales and biases");
+    } else {
+        return moe_set_error(MOE_EINVAL, "router: rbits=%d unsupported", rbits);
+    }
+    RouterArgs a{};
+    a.x = static_cast<const uint16_t *>(x);
+    a.T = T; a.H = H; a.E = E; a.K = K; a.M = M; a.gs = group_size;
+    a.w = w; a.ws = static_cast<const uint16_t *>(w_scales); a.wb = static_cast<const uint16_t *>(w_biases);
+    a.wn = wn; a.wns = static_cast<const uint16_t *>(wn_scales); a.wnb = static_cast<const uint16_t *>(wn_biases);
+    a.pred_bias = pred_bias;
+    a.logits = out_logits ? static_cast<uint16_t *>(out_logits) : logits_buf;
+    a.plogits = plogits_buf;
+    a.probs = static_cast<uint16_t *>(out_probs);
+    a.inds = out_inds;
+    a.scores = static_cast<uint16_t *>(out_scores);
+    a.pred = out_pred;
+    a.tickets = tickets;
+    if (!a.logits || (M > 0 && !a.plogits))
+        return moe_set_error(MOE_EINVAL, "router: missing logit scratch");
+    cudaError_t e = sb_fp16 ? launch_router<true>(a, rbits, as_stream(stream))
+                            : launch_router<false>(a, rbits, as_stream(stream));
+    if (e != cudaSuccess) return moe_set_cuda_error(e);
+    return MOE_OK;
+}
+
+extern "C" int moe_router_topk(const void *x, int T, int H, int E, int K, const void *w,
+                               const void *w_scales, const void *w_biases, int rbits,
+                               int group_size, int sb_fp16, const void *wn, const void *wn_scales,
+                               const void *wn_biases, int M, const float *pred_bias,
+                               void *out_logits, void *out_probs, uint32_t *out_inds,
+                               void *out_scores, uint32_t *out_pred, void *workspace,
+                               size_t workspace_bytes, void *stream) {
+    if (T <= 0 || E <= 0) return moe_set_error(MOE_EINVAL, "router: bad sizes T=%d E=%d", T, E);
+    const size_t need = moe_router_workspace_bytes(T, E, M);
+    if (!workspace || workspace_bytes < need)
+        return moe_set_error(MOE_EINVAL, "router: workspace of %zu bytes needed, %zu given", need,
+                             workspace_bytes);
+    char *ws = static_cast<char *>(workspace);
+    unsigned int *tickets = reinterpret_cast<unsigned int *>(ws);
+    ws += align_up((size_t)T * sizeof(unsigned int), 256);
+    uint16_t *logits = reinterpret_cast<uint16_t *>(ws);
+    ws += align_up((size_t)T * E * sizeof(uint16_t), 256);
+    uint16_t *plogits = M > 0 ? reinterpret_cast<uint16_t *>(ws) : nullptr;
+    return moe_router_launch(x, T, H, E, K, w, w_scales, w_biases, rbits, group_size, sb_fp16, wn,
+                             wn_scales, wn_biases, M, pred_bias, out_logits, out_probs, out_inds,
+                             out_scores, out_pred, tickets, logits, plogits, stream);
+}

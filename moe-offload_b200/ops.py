@@ -1,0 +1,174 @@
+"""Torch-facing wrappers over the libmoe_b200 C ABI (device tensors in, device tensors out).
+
+Tensor conventions
+  x, act, y      torch.bfloat16
+  expert weights MLX affine layout (transpose=True): codes int32/uint32 [cap, rows, cols*bits/32],
+                 scales/biases float16 or bfloat16 [cap, rows, cols/group_size]
+  indices/slots  int32 (bit-identical to the uint32 the reference uses)
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import torch
+
+from ._lib import call
+
+_CODE_DTYPES = (torch.int32, torch.uint32)
+_SB_DTYPES = (torch.float16, torch.bfloat16)
+
+
+def _ptr(t):
+    return None if t is None else t.data_ptr()
+
+
+def _stream(stream) -> int:
+    s = stream if stream is not None else torch.cuda.current_stream()
+    return s.cuda_stream
+
+
+def _need(t: torch.Tensor, name: str, dtypes, dev=None) -> None:
+    if not t.is_cuda:
+        raise ValueError(f"{name} must be a CUDA tensor")
+    if t.dtype not in dtypes:
+        raise ValueError(f"{name} has dtype {t.dtype}, expected one of {dtypes}")
+    if not t.is_contiguous():
+        raise ValueError(f"{name} must be contiguous")
+    if dev is not None and t.device != dev:
+        raise ValueError(f"{name} is on {t.device}, expected {dev}")
+
+
+@dataclass
+class QMatrix:
+    """One affine-quantised weight stack (codes, scales, biases) in MLX layout."""
+
+    w: torch.Tensor
+    s: torch.Tensor
+    b: torch.Tensor
+    bits: int = 2
+    group_size: int = 64
+
+    @property
+    def sb_fp16(self) -> int:
+        return int(self.s.dtype == torch.float16)
+
+    def check(self, name: str, dev) -> None:
+        _need(self.w, f"{name}.w", _CODE_DTYPES, dev)
+        _need(self.s, f"{name}.s", _SB_DTYPES, dev)
+        _need(self.b, f"{name}.b", (self.s.dtype,), dev)
+
+
+# ----------------------------------------------------------------------------- router
+
+_WS: dict = {}
+
+
+def router_workspace(device, T: int, E: int, M: int) -> torch.Tensor:
+    """Zero-filled router workspace (kept zero by the kernel between calls), cached per
+    (device, T, E, M)."""
+    key = (torch.device(device), T, E, M)
+    ws = _WS.get(key)
+    if ws is None:
+        nbytes = int(call("moe_router_workspace_bytes", T, E, M))
+        ws = torch.zeros(nbytes, dtype=torch.uint8, device=device)
+        _WS[key] = ws
+    return ws
+
+
+def router_topk(x: torch.Tensor, w, K: int, *, w_next=None, M: int = 0, pred_bias=None,
+                want_logits: bool = False, want_probs: bool = False, out: dict | None = None,
+                stream=None) -> dict:
+    """Router for T token rows of x [T, H] bf16.
+
+    w / w_next: bf16 [E, H] tensors, or QMatrix (affine router, 2/4/8 bits).
+    Returns dict with inds int32 [T,K] (MLX argpartition order), scores bf16 [T,K] and,
+    when requested, pred int32 [T,M], logits bf16 [T,E], probs bf16 [T,E]."""
+    _need(x, "x", (torch.bfloat16,))
+    T, H = x.shape
+    dev = x.device
+    if isinstance(w, QMatrix):
+        w.check("w", dev)
+        E = w.w.shape[0]
+        rbits, gs, sbf = w.bits, w.group_size, w.sb_fp16
+        wp, wsp, wbp = w.w.data_ptr(), w.s.data_ptr(), w.b.data_ptr()
+    else:
+        _need(w, "w", (torch.bfloat16,), dev)
+        E = w.shape[0]
+        rbits, gs, sbf = 16, 64, 0
+        wp, wsp, wbp = w.data_ptr(), None, None
+    wnp = wnsp = wnbp = None
+    if M > 0:
+        if w_next is None:
+            raise ValueError("M > 0 needs w_next")
+        if isinstance(w_next, QMatrix):
+            w_next.check("w_next", dev)
+            wnp, wnsp, wnbp = w_next.w.data_ptr(), w_next.s.data_ptr(), w_next.b.data_ptr()
+        else:
+            _need(w_next, "w_next", (torch.bfloat16,), dev)
+            wnp = w_next.data_ptr()
+    if pred_bias is not None:
+        _need(pred_bias, "pred_bias", (torch.float32,), dev)
+    o = out if out is not None else {}
+    if "inds" not in o:
+        o["inds"] = torch.empty((T, K), dtype=torch.int32, device=dev)
+    if "scores" not in o:
+        o["scores"] = torch.empty((T, K), dtype=torch.bfloat16, device=dev)
+    if M > 0 and "pred" not in o:
+        o["pred"] = torch.empty((T, M), dtype=torch.int32, device=dev)
+    if want_logits and "logits" not in o:
+        o["logits"] = torch.empty((T, E), dtype=torch.bfloat16, device=dev)
+    if want_probs and "probs" not in o:
+        o["probs"] = torch.empty((T, E), dtype=torch.bfloat16, device=dev)
+    ws = router_workspace(dev, T, E, M)
+    call("moe_router_topk", x.data_ptr(), T, H, E, K, wp, wsp, wbp, rbits, gs, sbf, wnp, wnsp, wnbp,
+         M, _ptr(pred_bias), _ptr(o.get("logits")), _ptr(o.get("probs")), o["inds"].data_ptr(),
+         o["scores"].data_ptr(), _ptr(o.get("pred")), ws.data_ptr(), ws.numel(), _stream(stream))
+    return o
+
+
+# ----------------------------------------------------------------------------- experts
+
+def experts_gateup(x: torch.Tensor, slots: torch.Tensor, gate: QMatrix, up: QMatrix,
+                   act: torch.Tensor | None = None, stream=None) -> torch.Tensor:
+    """act [T, K, I] = SwiGLU(gate(x), up(x)) for the K routed slots of each token."""
+    _need(x, "x", (torch.bfloat16,))
+    dev = x.device
+    _need(slots, "slots", (torch.int32, torch.uint32), dev)
+    gate.check("gate", dev)
+    up.check("up", dev)
+    T, H = x.shape
+    K = slots.shape[-1]
+    I = gate.w.shape[1]
+    if act is None:
+        act = torch.empty((T, K, I), dtype=torch.bfloat16, device=dev)
+    call("moe_experts_gateup", x.data_ptr(), T, H, I, K, gate.w.shape[0], slots.data_ptr(), gate.w.data_ptr(),
+         gate.s.data_ptr(), gate.b.data_ptr(), up.w.data_ptr(), up.s.data_ptr(), up.b.data_ptr(),
+         gate.bits, gate.group_size, gate.sb_fp16, act.data_ptr(), _stream(stream))
+    return act
+
+
+def experts_down(act: torch.Tensor, slots: torch.Tensor, down: QMatrix, scores=None, *,
+                 addend=None, resid=None, y=None, want_yk: bool = False, yk=None, stream=None):
+    """y [T, H] = sum_k down(act[:, k]) * scores[:, k] (+ addend) (+ resid); optionally the
+    unweighted per-expert outputs yk [T, K, H]. Returns (y, yk)."""
+    _need(act, "act", (torch.bfloat16,))
+    dev = act.device
+    _need(slots, "slots", (torch.int32, torch.uint32), dev)
+    down.check("down", dev)
+    T, K, I = act.shape
+    H = down.w.shape[1]
+    if scores is not None:
+        _need(scores, "scores", (torch.bfloat16,), dev)
+        if y is None:
+            y = torch.empty((T, H), dtype=torch.bfloat16, device=dev)
+    else:
+        y = None
+    if want_yk and yk is None:
+        yk = torch.empty((T, K, H), dtype=torch.bfloat16, device=dev)
+    for name, t in (("addend", addend), ("resid", resid)):
+        if t is not None:
+            _need(t, name, (torch.bfloat16,), dev)
+    call("moe_experts_down", act.data_ptr(), T, H, I, K, down.w.shape[0], slots.data_ptr(), _ptr(scores),
+         down.w.data_ptr(), down.s.data_ptr(), down.b.data_ptr(), down.bits, down.group_size,
+         down.sb_fp16, _ptr(addend), _ptr(resid), _ptr(y), _ptr(yk), _stream(stream))
+    return y, yk

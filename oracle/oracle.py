@@ -1,0 +1,154 @@
+"""ctypes wrapper over oracle/liboracle.so -- TEST INFRASTRUCTURE ONLY.
+
+The CPU restatement of the routed-expert MoE block (see moe_oracle.c for the arithmetic
+model and the reference citations). Only tests/, __graft_entry__.smoke() and bench.py's
+cpu_baseline / --impl reference legs import this module; the product package never does.
+
+All arrays are numpy; bf16 tensors travel as uint16 bit patterns.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import subprocess
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+_LIB = None
+
+
+def build() -> None:
+    """Compile liboracle.so (and the reference LRU under _ref/ when the sources exist)."""
+    subprocess.run(["make", "-s", "-C", HERE], check=True)
+
+
+def lib() -> ctypes.CDLL:
+    global _LIB
+    if _LIB is None:
+        path = os.path.join(HERE, "liboracle.so")
+        if not os.path.exists(path):
+            build()
+        L = ctypes.CDLL(path)
+        P = ctypes.c_void_p
+        I = ctypes.c_int
+        L.orc_router_logits.argtypes = [P, I, I, I, I, P, P, P, I, I, P, P]
+        L.orc_softmax_topk.argtypes = [P, I, I, I, P, P, P]
+        L.orc_topm_sorted.argtypes = [P, I, I, I, P]
+        L.orc_experts.argtypes = [P, I, I, I, I, P, P] + [P] * 9 + [I, I, I, P, P, P, P, P]
+        L.orc_f64_to_bf16.argtypes = [ctypes.c_double]
+        L.orc_f64_to_bf16.restype = ctypes.c_uint16
+        L.orc_f32_to_bf16.argtypes = [ctypes.c_float]
+        L.orc_f32_to_bf16.restype = ctypes.c_uint16
+        L.orc_num_threads.restype = I
+        L.orc_set_num_threads.argtypes = [I]
+        for f in ("orc_router_logits", "orc_softmax_topk", "orc_topm_sorted", "orc_experts"):
+            getattr(L, f).restype = I
+        _LIB = L
+    return _LIB
+
+
+def _p(a):
+    if a is None:
+        return None
+    assert a.flags["C_CONTIGUOUS"], "oracle inputs must be C-contiguous"
+    return a.ctypes.data_as(ctypes.c_void_p)
+
+
+def _chk(rc: int, what: str) -> None:
+    if rc != 0:
+        raise RuntimeError(f"oracle {what} failed with status {rc}")
+
+
+# ---------------------------------------------------------------- bf16 helpers (numpy)
+
+def bf16_to_f32(u16: np.ndarray) -> np.ndarray:
+    return (np.asarray(u16, dtype=np.uint16).astype(np.uint32) << 16).view(np.float32)
+
+
+def f32_to_bf16(f: np.ndarray) -> np.ndarray:
+    u = np.ascontiguousarray(f, dtype=np.float32).view(np.uint32).astype(np.uint64)
+    nan = (u & 0x7F800000) == 0x7F800000
+    nan &= (u & 0x007FFFFF) != 0
+    r = ((u + 0x7FFF + ((u >> 16) & 1)) >> 16).astype(np.uint16)
+    r[nan] = ((u[nan] >> 16) | 0x40).astype(np.uint16)
+    return r
+
+
+def set_threads(n: int) -> None:
+    lib().orc_set_num_threads(int(n))
+
+
+def num_threads() -> int:
+    return int(lib().orc_num_threads())
+
+
+# ---------------------------------------------------------------- router
+
+def router_logits(x_bf16: np.ndarray, w, E: int, rbits: int = 16, scales=None, biases=None,
+                  group_size: int = 64, sb_fp16: bool = False, bias_f32=None) -> np.ndarray:
+    """x [T,H] uint16(bf16); w: bf16 [E,H] (rbits=16) or uint32 [E,H*rbits/32]."""
+    x = np.ascontiguousarray(x_bf16, dtype=np.uint16)
+    T, H = x.shape
+    w = np.ascontiguousarray(w)
+    s = None if scales is None else np.ascontiguousarray(scales, dtype=np.uint16)
+    b = None if biases is None else np.ascontiguousarray(biases, dtype=np.uint16)
+    bias = None if bias_f32 is None else np.ascontiguousarray(bias_f32, dtype=np.float32)
+    out = np.empty((T, E), dtype=np.uint16)
+    _chk(lib().orc_router_logits(_p(x), T, H, E, rbits, _p(w), _p(s), _p(b), group_size,
+                                 int(sb_fp16), _p(bias), _p(out)), "router_logits")
+    return out
+
+
+def softmax_topk(logits_bf16: np.ndarray, K: int):
+    """-> (probs bf16 [T,E], inds u32 [T,K] in MLX argpartition order, scores bf16 [T,K])"""
+    lg = np.ascontiguousarray(logits_bf16, dtype=np.uint16)
+    T, E = lg.shape
+    probs = np.empty((T, E), dtype=np.uint16)
+    inds = np.empty((T, K), dtype=np.uint32)
+    scores = np.empty((T, K), dtype=np.uint16)
+    _chk(lib().orc_softmax_topk(_p(lg), T, E, K, _p(probs), _p(inds), _p(scores)), "softmax_topk")
+    return probs, inds, scores
+
+
+def topm_sorted(logits_bf16: np.ndarray, M: int) -> np.ndarray:
+    lg = np.ascontiguousarray(logits_bf16, dtype=np.uint16)
+    T, E = lg.shape
+    pred = np.empty((T, M), dtype=np.uint32)
+    _chk(lib().orc_topm_sorted(_p(lg), T, E, M, _p(pred)), "topm_sorted")
+    return pred
+
+
+# ---------------------------------------------------------------- experts
+
+def experts(x_bf16, slots, scores_bf16, gate, up, down, bits: int = 2, group_size: int = 64,
+            sb_fp16: bool = True, addend=None, resid=None, want_act=False, want_yk=False):
+    """gate/up/down: (w u32, scales u16, biases u16) slot buffers in MLX layout.
+    Returns dict(y=bf16 [T,H] or None, act=[T,K,I], yk=[T,K,H])."""
+    x = np.ascontiguousarray(x_bf16, dtype=np.uint16)
+    T, H = x.shape
+    sl = np.ascontiguousarray(slots, dtype=np.uint32).reshape(T, -1)
+    K = sl.shape[1]
+    sc = None if scores_bf16 is None else np.ascontiguousarray(scores_bf16, dtype=np.uint16).reshape(T, K)
+    wg, sg, bg = (np.ascontiguousarray(a) for a in gate)
+    wu, su, bu = (np.ascontiguousarray(a) for a in up)
+    wd, sd, bd = (np.ascontiguousarray(a) for a in down)
+    I = wg.shape[-2]
+    ad = None if addend is None else np.ascontiguousarray(addend, dtype=np.uint16).reshape(T, H)
+    rs = None if resid is None else np.ascontiguousarray(resid, dtype=np.uint16).reshape(T, H)
+    y = np.empty((T, H), dtype=np.uint16) if sc is not None else None
+    act = np.empty((T, K, I), dtype=np.uint16) if want_act else None
+    yk = np.empty((T, K, H), dtype=np.uint16) if want_yk else None
+    _chk(lib().orc_experts(_p(x), T, H, I, K, _p(sl), _p(sc), _p(wg), _p(sg), _p(bg), _p(wu),
+                           _p(su), _p(bu), _p(wd), _p(sd), _p(bd), bits, group_size, int(sb_fp16),
+                           _p(ad), _p(rs), _p(y), _p(act), _p(yk)), "experts")
+    return {"y": y, "act": act, "yk": yk}
+
+
+def ref_lru_lib(version: int = 1):
+    """The reference's own expert_io.c compiled under oracle/_ref (None when absent)."""
+    name = "libexpert_io_ref.so" if version == 1 else "libexpert_io_ref_v2.so"
+    path = os.path.join(HERE, "_ref", name)
+    if not os.path.exists(path):
+        return None
+    return ctypes.CDLL(path)
