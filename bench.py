@@ -1,0 +1,358 @@
+#!/usr/bin/env python3
+"""MoE decode throughput on the 28-layer, 512-expert, top-10 resident stack.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+A step is one decode token through all 28 layers (router -> 2-bit gate/up + SwiGLU -> 2-bit
+down + combine, h_{l+1} = h_l + MoE_l(h_l)) with a fresh N(0,1) hidden state per step
+(seed 1), expert weights random-init with the BASELINE distributions (synthetic: the
+reference's checkpoints are not available). For N > 1 (torchrun) every rank runs an
+independent replica of the stack (the batch-1 resident decode path does not shard; expert
+parallelism is a different configuration), so per-GPU work is fixed: weak scaling.
+
+Prints one JSON line (rank 0). `value` is whole-job tokens/s from CUDA events around the
+timed steps (max over ranks); `e2e` is the same metric through DecodeStack.decode() with the
+hidden state copied from pinned host memory and the result copied back every step;
+`roofline` describes the dominant kernel (the gate/up expert GEMV), timed live here.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "MoE decode tok/s (28-layer expert stack); expert GEMV HBM GB/s vs B200 peak"
+UNIT = "tok/s"
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=128)
+    ap.add_argument("--warmup", type=int, default=8)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true")
+    return ap.parse_args()
+
+
+def peaks() -> tuple[float, str]:
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(p) as f:
+            return float(json.load(f)["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+# ------------------------------------------------------------------------- clocks
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms during the timed region."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.f = tempfile.NamedTemporaryFile(mode="w+", suffix=".csv", delete=False)
+        self.p = None
+
+    def start(self):
+        try:
+            self.p = subprocess.Popen(["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.Q}",
+                                       "--format=csv,noheader,nounits", "-lms", "200"],
+                                      stdout=self.f, stderr=subprocess.DEVNULL)
+        except FileNotFoundError:
+            self.p = None
+        time.sleep(0.3)
+
+    def stop(self) -> dict:
+        if self.p is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.25)
+        self.p.terminate()
+        self.p.wait()
+        self.f.flush()
+        self.f.seek(0)
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.f.read().splitlines():
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        os.unlink(self.f.name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ------------------------------------------------------------------------- CPU legs
+
+class CpuLayer:
+    """The oracle port (C restatement, OpenMP on all host cores) of one layer of the c1 shape:
+    512-expert bf16 router + softmax/top-10, then 10 routed 2-bit experts and the combine.
+    64 experts are materialised on the host and the routing is taken modulo 64 (the
+    per-token work is identical: 10 experts' weights are read either way)."""
+
+    def __init__(self):
+        import numpy as np
+
+        from moe_offload_b200.synthetic import C1, np_bf16_normal, np_qmatrix
+        from oracle import oracle as orc
+
+        self.np, self.orc, self.cfg = np, orc, C1
+        self.rng = np.random.default_rng(C1.seed)
+        E, H, I = C1.experts, C1.hidden, C1.inter
+        self.nres = 64
+        self.g = np_qmatrix(self.rng, self.nres, I, H)
+        self.u = np_qmatrix(self.rng, self.nres, I, H)
+        self.d = np_qmatrix(self.rng, self.nres, H, I)
+        self.wr = np_bf16_normal(self.rng, (E, H), 0.02)
+        self.rand = lambda: np_bf16_normal(self.rng, (1, H))
+        orc.set_threads(os.cpu_count() or 1)
+        self.cores = orc.num_threads()
+
+    def token_layer(self) -> float:
+        x = self.rand()
+        t0 = time.perf_counter()
+        lg = self.orc.router_logits(x, self.wr, self.cfg.experts)
+        _, inds, sc = self.orc.softmax_topk(lg, self.cfg.top_k)
+        self.orc.experts(x, inds % self.nres, sc, self.g, self.u, self.d, sb_fp16=True, resid=x)
+        return time.perf_counter() - t0
+
+
+def cpu_layer_sample(seconds: float = 12.0) -> dict:
+    """Bounded CPU baseline: as many token-layers as fit in `seconds`, extrapolated to the
+    28-layer stack."""
+    cl = CpuLayer()
+    cl.token_layer()
+    ts = []
+    t0 = time.perf_counter()
+    while time.perf_counter() - t0 < seconds:
+        ts.append(cl.token_layer())
+    per_layer = statistics.mean(ts)
+    return {"value": round(1.0 / (cl.cfg.layers * per_layer), 4), "unit": UNIT, "cores": cl.cores,
+            "kind": "port",
+            "sample": f"{len(ts)} token-layers of the c1 shape (1 of 28 layers: 512-expert router, top-10 "
+                      f"2-bit experts, combine) in {seconds:.0f}s, extrapolated x28 layers; C restatement "
+                      f"(MLX is not installable here)"}
+
+
+def run_reference(args, rank: int, world: int) -> None:
+    """--impl reference: the reference computes this path with MLX, which is not installable
+    here; its CPU restatement (oracle port) runs on all host cores on rank 0 only. One step
+    = one token through one layer of the c1 shape, reported as 28-layer tok/s."""
+    if rank != 0:
+        return
+    cl = CpuLayer()
+    for _ in range(args.warmup):
+        cl.token_layer()
+    ts = [cl.token_layer() for _ in range(args.steps)]
+    per_layer = statistics.mean(ts)
+    v = 1.0 / (cl.cfg.layers * per_layer)
+    cfg = cl.cfg
+    cpu = {"value": round(v, 4), "unit": UNIT, "cores": cl.cores, "kind": "port",
+           "sample": f"{args.steps} token-layers (1 of 28 layers each), extrapolated x28; C restatement"}
+    line = {"metric": METRIC, "value": round(v, 4), "unit": UNIT, "n_gpus": args.gpus, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(1000.0 * per_layer * cfg.layers, 3),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "u2 codes x bf16 -> f32",
+            "data": "synthetic", "impl": "reference",
+            "config": {"workload": cfg.name, "layers": cfg.layers, "hidden": cfg.hidden, "experts": cfg.experts,
+                       "top_k": cfg.top_k, "inter": cfg.inter, "batch": 1},
+            "cpu_baseline": cpu,
+            "e2e": {"value": round(v, 4), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+# ------------------------------------------------------------------------- GPU leg
+
+def gateup_kernel_roofline(layers, cfg, dev, hbm_peak: float, launches: int = 256) -> dict:
+    """Average duration of the dominant kernel (gate/up GEMV) over back-to-back launches on
+    rotating layers with random expert sets, timed with CUDA events on its stream."""
+    import torch
+
+    from moe_offload_b200 import ops
+    from moe_offload_b200.synthetic import dev_bf16_normal
+
+    E, H, I, K = cfg.experts, cfg.hidden, cfg.inter, cfg.top_k
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(77)
+    x = dev_bf16_normal((1, H), dev, gen)
+    slots = [torch.randperm(E, device=dev, generator=gen)[:K].to(torch.int32).view(1, K) for _ in range(64)]
+    act = torch.empty((1, K, I), dtype=torch.bfloat16, device=dev)
+    L = len(layers)
+
+    def body():
+        for i in range(launches):
+            ly = layers[i % L]
+            ops.experts_gateup(x, slots[i % 64], ly.gate, ly.up, act=act)
+
+    st = torch.cuda.Stream(device=dev)
+    with torch.cuda.stream(st):
+        body()
+    st.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=st):
+        body()
+    with torch.cuda.stream(st):
+        g.replay()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record(st)
+        g.replay()
+        e.record(st)
+    e.synchronize()
+    dur_s = s.elapsed_time(e) / 1000.0 / launches
+    algo = K * 2 * (I * H // 4 + 2 * 2 * I * (H // cfg.group_size))     # codes + fp16 scales/biases
+    achieved = algo / dur_s / 1e9
+    traffic = None
+    tp = os.path.join(ROOT, "profiles", "traffic.json")
+    if os.path.exists(tp):
+        try:
+            traffic = json.load(open(tp)).get("gateup_kernel_bytes_per_launch")
+        except Exception:
+            traffic = None
+    return {"kernel": "gateup_kernel (2-bit gate+up GEMV + SwiGLU, 10 experts)", "bound": "hbm",
+            "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s", "frac": round(achieved / hbm_peak, 4),
+            "traffic": traffic, "algorithmic_bytes_per_launch": algo, "launch_us": round(dur_s * 1e6, 3)}
+
+
+def run_ours(args, rank: int, world: int, local_rank: int) -> None:
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    from moe_offload_b200.stack import DecodeStack
+    from moe_offload_b200.synthetic import C1, dev_bf16_normal, dev_stack
+
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    cfg = C1
+    layers = dev_stack(cfg, dev)
+    stack = DecodeStack(layers, cfg.top_k, dev)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(cfg.seed + 1000 * rank)
+    n_in = args.warmup + args.steps
+    h0 = dev_bf16_normal((n_in, 1, cfg.hidden), dev, gen)
+    torch.cuda.synchronize()
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    for i in range(args.warmup):
+        stack.step_device(h0[i])
+    torch.cuda.synchronize()
+    barrier()
+    clk = ClockSampler(local_rank)
+    clk.start()
+    torch.cuda.synchronize()
+    barrier()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for i in range(args.steps):
+        stack.step_device(h0[args.warmup + i])
+    e.record()
+    torch.cuda.synchronize()
+    barrier()
+    clocks = clk.stop()
+    t_ms = s.elapsed_time(e)
+    if world > 1:
+        tt = torch.tensor([t_ms], device=dev)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        t_ms = float(tt.item())
+    value = world * args.steps / (t_ms / 1000.0)
+
+    e2e = None
+    if not args.no_e2e:
+        hh = h0.cpu().pin_memory()
+        out_host = torch.empty((1, cfg.hidden), dtype=torch.bfloat16, pin_memory=True)
+        for i in range(min(args.warmup, 4)):
+            stack.decode(hh[i], out_host)
+        barrier()
+        torch.cuda.synchronize()
+        s2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s2.record()
+        for i in range(args.steps):
+            stack.decode(hh[args.warmup + i], out_host)
+        e2.record()
+        torch.cuda.synchronize()
+        barrier()
+        t2 = s2.elapsed_time(e2)
+        if world > 1:
+            tt = torch.tensor([t2], device=dev)
+            dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+            t2 = float(tt.item())
+        e2e = {"value": round(world * args.steps / (t2 / 1000.0), 2), "unit": UNIT,
+               "h2d_bytes_per_step": cfg.hidden * 2, "d2h_bytes_per_step": cfg.hidden * 2,
+               "api": "moe_offload_b200.stack.DecodeStack.decode (pinned host in/out, sync per step)"}
+
+    peak, peak_kind = peaks()
+    roof = gateup_kernel_roofline(layers, cfg, dev, peak)
+    roof["peak_source"] = peak_kind
+    step_bytes = cfg.layers * (cfg.top_k * cfg.expert_bytes + cfg.router_bytes)
+    stack_gbs = step_bytes * args.steps / (t_ms / 1000.0) / 1e9
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        cpu = cpu_layer_sample()
+
+    if rank == 0:
+        line = {"metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": round(t_ms / args.steps, 4), "higher_is_better": True,
+                "scaling": "weak", "vs_baseline": None, "dtype": "u2 codes x bf16 -> f32", "data": "synthetic",
+                "config": {"workload": cfg.name, "layers": cfg.layers, "hidden": cfg.hidden, "experts": cfg.experts,
+                           "top_k": cfg.top_k, "inter": cfg.inter, "batch": 1, "group_size": cfg.group_size,
+                           "scales": "fp16", "router": "bf16", "parallelism": f"replicas x{world}",
+                           "l2": "inputs larger than L2: 707 MB of weights per step, 31.7 GB resident"},
+                "roofline": roof,
+                "stack_hbm": {"bytes_per_step": step_bytes, "achieved_gbs": round(stack_gbs, 1),
+                              "frac": round(stack_gbs / peak, 4)},
+                "clocks": clocks, "gpu_launches": stack.launches_per_step * args.steps,
+                "e2e": e2e, "cpu_baseline": cpu}
+        print(json.dumps(line), flush=True)
+
+
+def main() -> int:
+    args = parse()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1 and args.impl == "ours":
+        import datetime
+
+        import torch
+        import torch.distributed as dist
+        torch.cuda.set_device(local_rank)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local_rank))
+    try:
+        if args.impl == "reference":
+            run_reference(args, rank, world)
+        else:
+            run_ours(args, rank, world, local_rank)
+    finally:
+        if world > 1 and args.impl == "ours":
+            import torch.distributed as dist
+            dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -106,6 +106,36 @@ int moe_experts_down(const void *act, int T, int H, int I, int K, int cap, const
                      int bits, int group_size, int sb_fp16, const void *addend, const void *resid,
                      void *y, void *yk, void *stream);
 
+/* ------------------------------------------------------------------------------------ */
+/* Fused decode step of one all-resident layer.                                           */
+/* ------------------------------------------------------------------------------------ */
+
+/* Workspace bytes for moe_decode_layer; zero-fill it once before first use. */
+size_t moe_decode_workspace_bytes(int T, int H, int I, int E, int K, int M);
+
+/*
+ * y = combine(experts(x, router(x))) for a layer whose E experts are all resident (slot id ==
+ * expert id): the decode body of the reference's hook for a resident layer
+ * (mlx-qwen38/loader.py:903-922 router + switch_mlp + combine; cpp/src/engine.cpp:532-571).
+ * Three kernels chained with programmatic dependent launch; the router is bf16 [E, H];
+ * router_next_w / M / pred_bias as in moe_router_topk. Expert weights as in
+ * moe_experts_gateup / moe_experts_down with cap = E. resid/addend optional (bf16 [T, H]).
+ */
+int moe_decode_layer(const void *x, int T, int H, int I, int E, int K, const void *router_w,
+                     const void *router_next_w, int M, const float *pred_bias,
+                     const uint32_t *wg, const void *sg, const void *bg,
+                     const uint32_t *wu, const void *su, const void *bu,
+                     const uint32_t *wd, const void *sd, const void *bd, int sb_fp16,
+                     const void *addend, const void *resid, uint32_t *out_inds, void *out_scores,
+                     uint32_t *out_pred, void *y, void *workspace, size_t workspace_bytes, void *stream);
+
+/*
+ * Device-side error word (bit 1: a bounded mbarrier/flag wait gave up, bit 2: invalid
+ * input seen by a kernel). Returns the current value (>= 0) and clears it when `clear`.
+ * Kernels never trap: they record the condition here and skip the affected work.
+ */
+int moe_device_error(int clear);
+
 #ifdef __cplusplus
 }
 #endif

@@ -36,6 +36,9 @@ SIGNATURES: dict[str, tuple] = {
     "moe_router_topk": (I, [P, I, I, I, I, P, P, P, I, I, I, P, P, P, I, P, P, P, P, P, P, P, SZ, P]),
     "moe_experts_gateup": (I, [P, I, I, I, I, I, P, P, P, P, P, P, P, I, I, I, P, P]),
     "moe_experts_down": (I, [P, I, I, I, I, I, P, P, P, P, P, I, I, I, P, P, P, P, P]),
+    "moe_device_error": (I, [I]),
+    "moe_decode_workspace_bytes": (SZ, [I, I, I, I, I, I]),
+    "moe_decode_layer": (I, [P, I, I, I, I, I, P, P, I, P] + [P] * 9 + [I, P, P, P, P, P, P, P, SZ, P]),
 }
 
 

@@ -20,7 +20,7 @@ NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 def _flags() -> list[str]:
     return ARCH + [
         "-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "-Xcompiler", "-O3",
-        "--expt-relaxed-constexpr", "-I", os.path.join(ROOT, "include"), "-I", CSRC,
+        "--expt-relaxed-constexpr", "-rdc=true", "-I", os.path.join(ROOT, "include"), "-I", CSRC,
         "-ccbin", "/usr/bin/g++",
     ]
 
@@ -56,7 +56,7 @@ def build(verbose: bool = False, ptxas_info: bool = False, jobs: int = 8) -> str
             _drain(procs, verbose or ptxas_info)
     _drain(procs, verbose or ptxas_info)
     if cmds or not os.path.exists(LIB):
-        link = [NVCC] + ARCH + ["-shared", "-o", LIB] + objs + ["-lcuda"]
+        link = [NVCC] + ARCH + ["-shared", "-rdc=true", "-o", LIB] + objs + ["-lcuda"]
         if verbose:
             print(" ".join(link))
         subprocess.run(link, check=True)

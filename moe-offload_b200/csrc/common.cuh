@@ -26,6 +26,11 @@ int moe_set_error(int code, const char *fmt, ...);
 
 static inline cudaStream_t as_stream(void *s) { return reinterpret_cast<cudaStream_t>(s); }
 
+MOE_HD size_t al16(size_t v) { return (v + 15) & ~size_t(15); }
+MOE_HD size_t al128(size_t v) { return (v + 127) & ~size_t(127); }
+MOE_HD size_t al256(size_t v) { return (v + 255) & ~size_t(255); }
+MOE_HD int pad4(int v) { return (v + 3) & ~3; }
+
 // ------------------------------------------------------------------ scalar conversions
 
 MOE_D float bf16_bits_to_f32(uint16_t h) { return __uint_as_float(((uint32_t)h) << 16); }
@@ -149,4 +154,118 @@ MOE_D void stage_bfrag(const uint16_t *__restrict__ v, int n, int ngroups, uint2
             xsum[e >> 4] = xs;
         }
     }
+}
+
+// ------------------------------------------------------------------ TMA bulk copies + mbarrier
+//
+// 1-D bulk copies (cp.async.bulk, no multicast) global -> shared, completing on an mbarrier
+// with a transaction byte count. Every wait is bounded: after kMbarSpinLimit polls the
+// waiter records MOE_DEVERR_MBAR_TIMEOUT in the device error word and gives up, so a kernel
+// never spins forever.
+
+#define MOE_DEVERR_MBAR_TIMEOUT 1u
+#define MOE_DEVERR_BAD_INPUT 2u
+
+extern __device__ unsigned int g_moe_device_error;
+
+constexpr uint32_t kMbarSpinLimit = 1u << 26;
+
+MOE_D uint32_t smem_addr(const void *p) { return static_cast<uint32_t>(__cvta_generic_to_shared(p)); }
+
+MOE_D void mbar_init(uint64_t *bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count) : "memory");
+}
+
+// make barrier initialisation visible to the async (TMA) proxy
+MOE_D void fence_barrier_init() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+MOE_D void mbar_arrive_expect_tx(uint64_t *bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)), "r"(bytes)
+                 : "memory");
+}
+
+MOE_D void tma_load_1d(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+            smem_addr(dst)),
+        "l"(src), "r"(bytes), "r"(smem_addr(bar))
+        : "memory");
+}
+
+MOE_D bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok)
+        : "r"(smem_addr(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// bounded wait for phase `parity`; false (and the device error word set) on timeout
+MOE_D bool mbar_wait(uint64_t *bar, uint32_t parity) {
+    for (uint32_t i = 0; i < kMbarSpinLimit; ++i)
+        if (mbar_try_wait(bar, parity)) return true;
+    atomicOr(&g_moe_device_error, MOE_DEVERR_MBAR_TIMEOUT);
+    return false;
+}
+
+// ------------------------------------------------------------------ programmatic dependent launch
+// The next kernel in the stream may start once every CTA of this one has called
+// pdl_launch_dependents(); it must call pdl_wait() before touching this kernel's outputs.
+MOE_D void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+MOE_D void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+// B records of a vector already resident in shared memory (bf16, `n` values): the same
+// layout as stage_bfrag, built without any global-memory round trip.
+MOE_D void build_bfrag_smem(const uint16_t *v, int ngroups, uint2 *frag, float *corr, float *xsum) {
+    const int nent = ngroups * 16;
+    for (int base = 0; base < nent; base += blockDim.x) {
+        const int e = base + threadIdx.x;
+        float cs = 0.f, xs = 0.f;
+        if (e < nent) {
+            const int G = e >> 4, m = (e >> 2) & 3, mi = e & 3;
+            const int c0 = G * 64 + 16 * m + 2 * mi;
+            const uint32_t p01 = *reinterpret_cast<const uint32_t *>(v + c0);       // v[c0], v[c0+1]
+            const uint32_t p89 = *reinterpret_cast<const uint32_t *>(v + c0 + 8);   // v[c0+8], v[c0+9]
+            const float v0 = __uint_as_float(p01 << 16), v2 = __uint_as_float(p01 & 0xffff0000u);
+            const float v1 = __uint_as_float(p89 << 16), v3 = __uint_as_float(p89 & 0xffff0000u);
+            const float i0 = pair_inv_scale(2 * mi), i1 = pair_inv_scale(2 * mi + 1);
+            const float s0 = v0 * i0, s1 = v1 * i0, s2 = v2 * i1, s3 = v3 * i1;
+            frag[e] = make_uint2(pack_bf16x2(s0, s1), pack_bf16x2(s2, s3));
+            cs = (s0 + s1) + (s2 + s3);
+            xs = (v0 + v1) + (v2 + v3);
+        }
+#pragma unroll
+        for (int off = 8; off > 0; off >>= 1) {
+            cs += __shfl_xor_sync(0xffffffffu, cs, off);
+            xs += __shfl_xor_sync(0xffffffffu, xs, off);
+        }
+        if (e < nent && (e & 15) == 0) {
+            corr[e >> 4] = cs;
+            xsum[e >> 4] = xs;
+        }
+    }
+}
+
+// Launch with the programmatic-stream-serialization attribute (PDL): the kernel may begin
+// while its predecessor in the stream is still running; it must pdl_wait() before reading
+// anything an earlier kernel produced.
+template <typename Kern, typename Args>
+static cudaError_t launch_pdl(Kern kern, dim3 grid, dim3 block, size_t smem, cudaStream_t st, const Args &args) {
+    if (smem > 48 * 1024) {
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return e;
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kern, args);
 }

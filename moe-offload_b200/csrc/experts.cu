@@ -1,120 +1,176 @@
 // Decode expert GEMVs over 2-bit affine (group 64) weights in MLX layout.
 //
-// Both kernels run the dot products on the tensor cores through m16n8k16 bf16 MMAs whose
-// A operand is built in registers from the packed codes (expand_word: 10 integer ops per
-// 16 codes, no per-code shift or convert) and whose B operand is a pre-scaled copy of the
-// input vector staged in shared memory. A GEMV has one useful column; the N dimension is
-// used instead to process four different 64-code groups per MMA: lane quad t of every row
-// supplies group 4j+t, and B column n holds the input of group 4j+n on the k-slots of lane
-// t == n only, so D[row][n] is the row's partial dot over group 4j+n. Each lane loads a
-// full 16-byte group of its row per step, which keeps the weight stream 16-byte coalesced.
+// Data movement: each warp owns a contiguous block of weight rows (8 gate + 8 up rows, or
+// 16 down rows) and pulls it -- codes, scales and biases -- into shared memory with 1-D TMA
+// bulk copies that complete on a per-warp mbarrier; the token's input vector arrives the
+// same way. All copies of a CTA are issued before any compute, so a wave of CTAs keeps the
+// whole layer's weight stream in flight. With programmatic dependent launch the down
+// kernel issues its weight copies while the gate/up kernel is still running.
 //
-//   gate/up  grid (I/8, K, T), kGuWarps warps split the H axis; MMA rows 0-7 are gate rows
-//            r..r+7 of the routed expert, rows 8-15 the matching up rows, so SwiGLU happens
-//            in the epilogue without another pass (layers.cpp:349-358, kernels.cpp:1090).
-//   down     grid (H/16, T), one warp per routed expert over all of I; the CTA combines the
-//            K experts' 16 output rows with the routing scores (loader.py:914,965).
+// Dot products: m16n8k16 bf16 MMAs. The A operand is built in registers from the packed
+// codes (expand_word: 10 integer ops per 16 codes, exact bf16 values 1 + q*c); B holds the
+// input pre-scaled by 1/c, so D = sum(x/c) + sum(q*x) and the per-group constant sum(x/c)
+// ("corr") is subtracted in the epilogue. A GEMV has one useful column; N is used to run
+// four 64-code groups per MMA instead: lane quad t of every row supplies group 4j+t, and B
+// column n carries group 4j+n on lane t == n's k-slots only, so D[row][n] is the row's
+// partial dot over group 4j+n. The per-group affine terms are applied in fp32:
+//   row += s[g] * (D - corr[g]) + b[g] * sum(x[g]).
+//
+//   gate/up  grid (ceil(I/8/kGuWarps), K, T); warp = one block of 8 rows of one routed
+//            expert, MMA rows 0-7 gate, 8-15 up, SwiGLU in the epilogue
+//            (cpp/src/layers.cpp:349-358, cpp/src/kernels.cpp:1090-1094).
+//   down     grid (H/16, T); warp k = routed expert k over all of I for 16 output rows; the
+//            CTA combines the K experts with the routing scores (loader.py:914,965).
 #include "common.cuh"
 
 namespace {
 
-constexpr int kGuWarps = 4;       // K-split warps of the gate/up kernel
-constexpr int kGuMaxSteps = 4;    // 4 groups per step -> H <= kGuWarps*kGuMaxSteps*256 = 4096
-constexpr int kDnMaxSteps = 8;    // down: I <= 8*256 = 2048 (template instances 4 and 8)
-constexpr int kMaxK = 16;         // routed experts per token handled by one down CTA
+constexpr int kGuWarps = 4;        // K-split warps per gate/up CTA (one 8-row block)
+constexpr int kMaxK = 16;
 
-template <bool kFp16>
-struct SB {
-    static MOE_D float get(const uint16_t *p, size_t i) { return sb_to_f32<kFp16>(__ldg(p + i)); }
-};
+
+// One MMA step: the row pair (ra, rb) of this lane against four 64-code groups
+// (lane quad t supplies group G = 4j + t). Four independent accumulator chains (one per
+// 16-code word) keep the tensor-core latency hidden; D[.][n] = partial over group 4j + n.
+MOE_D void mma_step(const uint4 wa, const uint4 wb, const uint2 *xf, bool bok, float d[4]) {
+    float dm[4][4];
+#pragma unroll
+    for (int m = 0; m < 4; ++m) dm[m][0] = dm[m][1] = dm[m][2] = dm[m][3] = 0.f;
+    const uint32_t aw[4] = {wa.x, wa.y, wa.z, wa.w};
+    const uint32_t bw[4] = {wb.x, wb.y, wb.z, wb.w};
+#pragma unroll
+    for (int m = 0; m < 4; ++m) {
+        uint32_t pa[8], pb[8];
+        expand_word(aw[m], pa);
+        expand_word(bw[m], pb);
+        uint4 b01 = make_uint4(0u, 0u, 0u, 0u), b23 = make_uint4(0u, 0u, 0u, 0u);
+        if (bok) {
+            b01 = *reinterpret_cast<const uint4 *>(xf + m * 4);       // entries (m,0),(m,1)
+            b23 = *reinterpret_cast<const uint4 *>(xf + m * 4 + 2);   // entries (m,2),(m,3)
+        }
+        mma_bf16_16816(dm[m], pa[0], pb[0], pa[1], pb[1], b01.x, b01.y);
+        mma_bf16_16816(dm[m], pa[2], pb[2], pa[3], pb[3], b01.z, b01.w);
+        mma_bf16_16816(dm[m], pa[4], pb[4], pa[5], pb[5], b23.x, b23.y);
+        mma_bf16_16816(dm[m], pa[6], pb[6], pa[7], pb[7], b23.z, b23.w);
+    }
+#pragma unroll
+    for (int q = 0; q < 4; ++q) d[q] = (dm[0][q] + dm[1][q]) + (dm[2][q] + dm[3][q]);
+}
 
 // --------------------------------------------------------------------- gate + up
 
+struct GuArgs {
+    const uint16_t *x;
+    const uint2 *xrec;          // optional pre-built B records of x ([T][ngH][16])
+    const float *xcorr, *xsum;  // [T][pad4(ngH)]
+    const uint32_t *slots;
+    const uint32_t *wg, *wu;
+    const uint16_t *sg, *bg, *su, *bu;
+    int H, I, K, cap;
+    uint16_t *act;              // [T][K][I]
+    uint2 *arec;                // optional B records of act ([T][K][ngI][16])
+    float *apart;               // [T][K][ngI][8][2] per-8-row partial (corr, sum)
+};
+
+struct GuLayout {
+    size_t xraw, xfrag, corr, xsum, w, red, total;
+    MOE_HD GuLayout(int H, bool self_stage) {
+        const int ng = H / 64;
+        xraw = 128;
+        xfrag = xraw + (self_stage ? al16((size_t)H * 2) : 0);
+        corr = xfrag + (size_t)ng * 128;
+        xsum = corr + al16((size_t)pad4(ng) * 4);
+        w = al128(xsum + al16((size_t)pad4(ng) * 4));
+        red = w + al16(16 * (size_t)(H / 4) + 4 * 8 * (size_t)ng * 2);
+        total = red + kGuWarps * 8 * 2 * 4;
+    }
+};
+
 template <bool kFp16>
-__global__ void __launch_bounds__(kGuWarps * 32) gateup_kernel(
-    const uint16_t *__restrict__ x, const uint32_t *__restrict__ slots,
-    const uint32_t *__restrict__ wg, const uint16_t *__restrict__ sg, const uint16_t *__restrict__ bg,
-    const uint32_t *__restrict__ wu, const uint16_t *__restrict__ su, const uint16_t *__restrict__ bu,
-    int H, int I, int K, int cap, uint16_t *__restrict__ act) {
-    extern __shared__ __align__(16) unsigned char smem[];
-    const int ngroups = H >> 6;
-    uint2 *xfrag = reinterpret_cast<uint2 *>(smem);                       // [ngroups][16]
-    float *corr = reinterpret_cast<float *>(smem + (size_t)ngroups * 128);  // [ngroups]
-    float *xsum = corr + ngroups;                                          // [ngroups]
-    float *red = xsum + ngroups;                                           // [kGuWarps][8][2]
+__global__ void __launch_bounds__(kGuWarps * 32) gateup_kernel(GuArgs a) {
+    extern __shared__ __align__(128) unsigned char smem[];
+    const int H = a.H, I = a.I, K = a.K;
+    const int ng = H >> 6, rowb = H >> 2;
+    const bool self_stage = (a.xrec == nullptr);
+    const GuLayout L(H, self_stage);
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem);
+    uint16_t *xraw = reinterpret_cast<uint16_t *>(smem + L.xraw);
+    uint2 *xfrag = reinterpret_cast<uint2 *>(smem + L.xfrag);
+    float *corr = reinterpret_cast<float *>(smem + L.corr);
+    float *xsum = reinterpret_cast<float *>(smem + L.xsum);
+    unsigned char *wsm = smem + L.w;
+    float *red = reinterpret_cast<float *>(smem + L.red);
 
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int g = lane >> 2, t = lane & 3;
     const int k = blockIdx.y, tok = blockIdx.z;
-    const int r = blockIdx.x * 8 + g;
-    const uint32_t slot_raw = slots[(size_t)tok * K + k];
-    const bool sok = slot_raw < (uint32_t)cap;          // out-of-range slot: no loads, zero output
-    const bool rok = r < I && sok;
-    const size_t slot = sok ? slot_raw : 0;
+    const int r0 = blockIdx.x * 8;
 
-    const int nsteps = (ngroups + 3) >> 2;
-    const int s0 = (warp * nsteps) / kGuWarps, s1 = ((warp + 1) * nsteps) / kGuWarps;
-
-    // 1) weight stream first: every load of this warp in flight before anything else
-    const size_t row = slot * I + r;
-    const uint4 *gw = reinterpret_cast<const uint4 *>(wg + row * (size_t)(H >> 4));
-    const uint4 *uw = reinterpret_cast<const uint4 *>(wu + row * (size_t)(H >> 4));
-    uint4 ag[kGuMaxSteps], au[kGuMaxSteps];
-#pragma unroll
-    for (int i = 0; i < kGuMaxSteps; ++i) {
-        const int G = 4 * (s0 + i) + t;
-        const bool ok = rok && (s0 + i < s1) && (G < ngroups);
-        ag[i] = ok ? ldg_stream16(gw + G) : make_uint4(0, 0, 0, 0);
-        au[i] = ok ? ldg_stream16(uw + G) : make_uint4(0, 0, 0, 0);
+    if (threadIdx.x == 0) {
+        mbar_init(&bars[0], 1);
+        mbar_init(&bars[1], 1);
+        fence_barrier_init();
     }
-    // scales / biases of the two groups this lane finalises per step (lanes t < 2)
-    float sgv[kGuMaxSteps][2], bgv[kGuMaxSteps][2], suv[kGuMaxSteps][2], buv[kGuMaxSteps][2];
-#pragma unroll
-    for (int i = 0; i < kGuMaxSteps; ++i)
-#pragma unroll
-        for (int c = 0; c < 2; ++c) {
-            const int G = 4 * (s0 + i) + 2 * t + c;
-            const bool ok = rok && t < 2 && (s0 + i < s1) && (G < ngroups);
-            const size_t si = row * ngroups + G;
-            sgv[i][c] = ok ? SB<kFp16>::get(sg, si) : 0.f;
-            bgv[i][c] = ok ? SB<kFp16>::get(bg, si) : 0.f;
-            suv[i][c] = ok ? SB<kFp16>::get(su, si) : 0.f;
-            buv[i][c] = ok ? SB<kFp16>::get(bu, si) : 0.f;
-        }
-
-    // 2) stage the token's input as MMA B records while the weights are in flight
-    stage_bfrag(x + (size_t)tok * H, H, ngroups, xfrag, corr, xsum);
     __syncthreads();
 
-    float accg = 0.f, accu = 0.f;
-    const bool bl = (g == t);   // lanes holding B column n == t
-#pragma unroll
-    for (int i = 0; i < kGuMaxSteps; ++i) {
-        if (s0 + i >= s1) break;
-        const int Gb = 4 * (s0 + i);
-        const bool bok = bl && (Gb + t < ngroups);
-        const uint2 *xf = xfrag + (size_t)(Gb + t) * 16;
-        float d[4] = {0.f, 0.f, 0.f, 0.f};
-        const uint32_t gwd[4] = {ag[i].x, ag[i].y, ag[i].z, ag[i].w};
-        const uint32_t uwd[4] = {au[i].x, au[i].y, au[i].z, au[i].w};
-#pragma unroll
-        for (int m = 0; m < 4; ++m) {
-            uint32_t gp[8], up[8];
-            expand_word(gwd[m], gp);
-            expand_word(uwd[m], up);
-#pragma unroll
-            for (int mi = 0; mi < 4; ++mi) {
-                const uint2 b = bok ? xf[m * 4 + mi] : make_uint2(0u, 0u);
-                mma_bf16_16816(d, gp[2 * mi], up[2 * mi], gp[2 * mi + 1], up[2 * mi + 1], b.x, b.y);
-            }
+    pdl_wait();                       // router (slots, x records) and the producer of x are done
+    pdl_launch_dependents();
+
+    const uint32_t slot_raw = a.slots[(size_t)tok * K + k];
+    const bool sok = slot_raw < (uint32_t)a.cap;
+    const size_t row0 = (size_t)(sok ? slot_raw : 0) * I + r0;
+    const uint32_t cb = 8u * rowb, sb = 8u * ng * 2u;
+    if (threadIdx.x == 0) {
+        if (sok) {
+            mbar_arrive_expect_tx(&bars[1], 2 * cb + 4 * sb);
+            tma_load_1d(wsm, a.wg + row0 * (H >> 4), cb, &bars[1]);
+            tma_load_1d(wsm + cb, a.wu + row0 * (H >> 4), cb, &bars[1]);
+            tma_load_1d(wsm + 2 * cb, a.sg + row0 * ng, sb, &bars[1]);
+            tma_load_1d(wsm + 2 * cb + sb, a.bg + row0 * ng, sb, &bars[1]);
+            tma_load_1d(wsm + 2 * cb + 2 * sb, a.su + row0 * ng, sb, &bars[1]);
+            tma_load_1d(wsm + 2 * cb + 3 * sb, a.bu + row0 * ng, sb, &bars[1]);
         }
-        if (t < 2) {
+        if (self_stage) {
+            mbar_arrive_expect_tx(&bars[0], (uint32_t)H * 2);
+            tma_load_1d(xraw, a.x + (size_t)tok * H, (uint32_t)H * 2, &bars[0]);
+        } else {
+            const uint32_t rb = (uint32_t)ng * 128, cbz = (uint32_t)pad4(ng) * 4;
+            mbar_arrive_expect_tx(&bars[0], rb + 2 * cbz);
+            tma_load_1d(xfrag, a.xrec + (size_t)tok * ng * 16, rb, &bars[0]);
+            tma_load_1d(corr, a.xcorr + (size_t)tok * pad4(ng), cbz, &bars[0]);
+            tma_load_1d(xsum, a.xsum + (size_t)tok * pad4(ng), cbz, &bars[0]);
+        }
+    }
+    const bool xok = mbar_wait(&bars[0], 0);
+    if (self_stage && xok) build_bfrag_smem(xraw, ng, xfrag, corr, xsum);
+    __syncthreads();
+    const bool wok = sok && xok && mbar_wait(&bars[1], 0);
+
+    const uint16_t *sgs = reinterpret_cast<const uint16_t *>(wsm + 2 * cb);
+    const uint16_t *bgs = sgs + 8 * ng, *sus = bgs + 8 * ng, *bus = sus + 8 * ng;
+    float accg = 0.f, accu = 0.f;
+    if (wok) {
+        const uint4 *grow = reinterpret_cast<const uint4 *>(wsm + (size_t)g * rowb);
+        const uint4 *urow = reinterpret_cast<const uint4 *>(wsm + cb + (size_t)g * rowb);
+        const int nsteps = (ng + 3) >> 2;
+        const int s0 = (warp * nsteps) / kGuWarps, s1 = ((warp + 1) * nsteps) / kGuWarps;
+        const bool bl = (g == t);
+        for (int j = s0; j < s1; ++j) {
+            const int G = 4 * j + t;
+            const bool gok = G < ng;
+            const uint4 wv = gok ? grow[G] : make_uint4(0, 0, 0, 0);
+            const uint4 uv = gok ? urow[G] : make_uint4(0, 0, 0, 0);
+            float d[4];
+            mma_step(wv, uv, xfrag + (size_t)G * 16, bl && gok, d);
+            if (t < 2) {
 #pragma unroll
-            for (int c = 0; c < 2; ++c) {
-                const int G = Gb + 2 * t + c;
-                if (G < ngroups) {
-                    accg += sgv[i][c] * (d[c] - corr[G]) + bgv[i][c] * xsum[G];
-                    accu += suv[i][c] * (d[2 + c] - corr[G]) + buv[i][c] * xsum[G];
+                for (int c = 0; c < 2; ++c) {
+                    const int G2 = 4 * j + 2 * t + c;
+                    if (G2 < ng) {
+                        const int si = g * ng + G2;
+                        accg += sb_to_f32<kFp16>(sgs[si]) * (d[c] - corr[G2]) + sb_to_f32<kFp16>(bgs[si]) * xsum[G2];
+                        accu += sb_to_f32<kFp16>(sus[si]) * (d[2 + c] - corr[G2]) + sb_to_f32<kFp16>(bus[si]) * xsum[G2];
+                    }
                 }
             }
         }
@@ -126,9 +182,10 @@ __global__ void __launch_bounds__(kGuWarps * 32) gateup_kernel(
         red[(warp * 8 + g) * 2 + 1] = accu;
     }
     __syncthreads();
-    if (warp == 0 && lane < 8) {
-        const int rr = blockIdx.x * 8 + lane;
-        if (rr < I) {
+    if (warp == 0) {
+        float av = 0.f, scaled = 0.f;
+        const int p = r0 + lane;            // activation index inside I (lanes 0..7)
+        if (lane < 8) {
             float sgsum = 0.f, susum = 0.f;
 #pragma unroll
             for (int w = 0; w < kGuWarps; ++w) {
@@ -138,100 +195,168 @@ __global__ void __launch_bounds__(kGuWarps * 32) gateup_kernel(
             const float gv = bf16r(sgsum), uv = bf16r(susum);
             // SwiGLU rounded after every op, like an MLX bf16 graph
             const float sig = bf16r(1.0f / (1.0f + expf(-gv)));
-            const float a = sok ? bf16r(bf16r(gv * sig) * uv) : 0.f;
-            act[((size_t)tok * K + k) * I + rr] = f32_to_bf16_bits(a);
+            av = wok ? bf16r(bf16r(gv * sig) * uv) : 0.f;
+            a.act[((size_t)tok * K + k) * I + p] = f32_to_bf16_bits(av);
+            if (a.arec) {
+                // scatter into the B record of the down kernel (layout of build_bfrag_smem)
+                const int ngI = I >> 6, G = p >> 6, o = p & 63, m = o >> 4, q = o & 15;
+                const int mi = (q & 7) >> 1;
+                scaled = av * pair_inv_scale(q & 7);
+                const size_t ent = (((size_t)tok * K + k) * ngI + G) * 16 + m * 4 + mi;
+                uint16_t *half = reinterpret_cast<uint16_t *>(a.arec + ent) + (q & 1) * 2 + (q >= 8 ? 1 : 0);
+                *half = f32_to_bf16_bits(scaled);
+            }
+        }
+        if (a.arec) {
+            float cs = scaled, xs = av;
+#pragma unroll
+            for (int off = 4; off > 0; off >>= 1) {
+                cs += __shfl_xor_sync(0xffffffffu, cs, off);
+                xs += __shfl_xor_sync(0xffffffffu, xs, off);
+            }
+            if (lane == 0) {
+                const int ngI = I >> 6, G = r0 >> 6, rbg = (r0 & 63) >> 3;
+                float *pp = a.apart + ((((size_t)tok * K + k) * ngI + G) * 8 + rbg) * 2;
+                pp[0] = cs;
+                pp[1] = xs;
+            }
         }
     }
 }
 
 // --------------------------------------------------------------------- down + combine
 
-template <bool kFp16, int kSteps>
-__global__ void __launch_bounds__(kMaxK * 32) down_kernel(
-    const uint16_t *__restrict__ act, const uint32_t *__restrict__ slots,
-    const uint16_t *__restrict__ scores, const uint32_t *__restrict__ wd,
-    const uint16_t *__restrict__ sd, const uint16_t *__restrict__ bd, int H, int I, int K, int cap,
-    const uint16_t *__restrict__ addend, const uint16_t *__restrict__ resid,
-    uint16_t *__restrict__ y, uint16_t *__restrict__ yk) {
-    extern __shared__ __align__(16) unsigned char smem[];
-    const int ngroups = I >> 6;
-    uint2 *afrag = reinterpret_cast<uint2 *>(smem);                                 // [K][ngroups][16]
-    float *corr = reinterpret_cast<float *>(smem + (size_t)K * ngroups * 128);      // [K][ngroups]
-    float *xsum = corr + K * ngroups;                                               // [K][ngroups]
-    float *yks = xsum + K * ngroups;                                                // [K][16]
+struct DnArgs {
+    const uint16_t *act;
+    const uint2 *arec;          // optional records of act (from the gate/up kernel)
+    const float *apart;         // [T][K][ngI][8][2]
+    const uint32_t *slots;
+    const uint16_t *scores;
+    const uint32_t *wd;
+    const uint16_t *sd, *bd;
+    int H, I, K, cap;
+    const uint16_t *addend, *resid;
+    uint16_t *y, *yk;
+};
 
-    const int lane = threadIdx.x & 31, k = threadIdx.x >> 5;   // warp k <-> routed expert k
+struct DnLayout {
+    size_t araw, afrag, apart, corr, xsum, yks, warps, warp_bytes, total;
+    MOE_HD DnLayout(int I, int K, bool self_stage) {
+        const int ng = I / 64;
+        araw = 256;                                   // after K+1 mbarriers (K <= 16)
+        afrag = araw + (self_stage ? al16((size_t)K * I * 2) : 0);
+        apart = afrag + (size_t)K * ng * 128;
+        corr = apart + (self_stage ? 0 : (size_t)K * ng * 64);
+        xsum = corr + al16((size_t)K * ng * 4);
+        yks = xsum + al16((size_t)K * ng * 4);
+        warps = al128(yks + (size_t)K * 16 * 4);
+        warp_bytes = al128(16 * (size_t)(I / 4) + 2 * 16 * (size_t)ng * 2);
+        total = warps + (size_t)K * warp_bytes;
+    }
+};
+
+template <bool kFp16>
+__global__ void __launch_bounds__(kMaxK * 32) down_kernel(DnArgs a) {
+    extern __shared__ __align__(128) unsigned char smem[];
+    const int H = a.H, I = a.I, K = a.K;
+    const int ng = I >> 6, rowb = I >> 2;
+    const bool self_stage = (a.arec == nullptr);
+    const DnLayout L(I, K, self_stage);
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem);
+    uint16_t *araw = reinterpret_cast<uint16_t *>(smem + L.araw);
+    uint2 *afrag = reinterpret_cast<uint2 *>(smem + L.afrag);
+    float *apart = reinterpret_cast<float *>(smem + L.apart);
+    float *corr = reinterpret_cast<float *>(smem + L.corr);
+    float *xsum = reinterpret_cast<float *>(smem + L.xsum);
+    float *yks = reinterpret_cast<float *>(smem + L.yks);
+
+    const int lane = threadIdx.x & 31, k = threadIdx.x >> 5;
     const int g = lane >> 2, t = lane & 3;
     const int tok = blockIdx.y;
     const int r0 = blockIdx.x * 16;
-    const uint32_t slot_raw = slots[(size_t)tok * K + k];
-    const bool sok = slot_raw < (uint32_t)cap;          // out-of-range slot: rows read as absent
-    const int ra = sok ? r0 + g : H, rb = sok ? r0 + 8 + g : H;
-    const size_t slot = sok ? slot_raw : 0;
-    const int nsteps = (ngroups + 3) >> 2;
+    unsigned char *my = smem + L.warps + (size_t)k * L.warp_bytes;
 
-    const size_t rowa = slot * H + ra, rowb = slot * H + rb;
-    const uint4 *wa = reinterpret_cast<const uint4 *>(wd + rowa * (size_t)(I >> 4));
-    const uint4 *wb = reinterpret_cast<const uint4 *>(wd + rowb * (size_t)(I >> 4));
-    uint4 qa[kSteps], qb[kSteps];
-#pragma unroll
-    for (int i = 0; i < kSteps; ++i) {
-        const int G = 4 * i + t;
-        const bool ok = (i < nsteps) && (G < ngroups);
-        qa[i] = (ok && ra < H) ? ldg_stream16(wa + G) : make_uint4(0, 0, 0, 0);
-        qb[i] = (ok && rb < H) ? ldg_stream16(wb + G) : make_uint4(0, 0, 0, 0);
+    if (threadIdx.x == 0) {
+        for (int i = 0; i <= K; ++i) mbar_init(&bars[i], 1);
+        fence_barrier_init();
     }
-    // scale / bias of the two groups this lane finalises per step (lanes t < 2)
-    float sa[kSteps][2], ba[kSteps][2], sbv[kSteps][2], bbv[kSteps][2];
-#pragma unroll
-    for (int i = 0; i < kSteps; ++i)
-#pragma unroll
-        for (int c = 0; c < 2; ++c) {
-            const int G = 4 * i + 2 * t + c;
-            const bool ok = t < 2 && (i < nsteps) && (G < ngroups);
-            sa[i][c] = (ok && ra < H) ? SB<kFp16>::get(sd, rowa * ngroups + G) : 0.f;
-            ba[i][c] = (ok && ra < H) ? SB<kFp16>::get(bd, rowa * ngroups + G) : 0.f;
-            sbv[i][c] = (ok && rb < H) ? SB<kFp16>::get(sd, rowb * ngroups + G) : 0.f;
-            bbv[i][c] = (ok && rb < H) ? SB<kFp16>::get(bd, rowb * ngroups + G) : 0.f;
-        }
-
-    // stage every routed expert's activation vector (one warp-segment group at a time)
-    for (int kk = 0; kk < K; ++kk)
-        stage_bfrag(act + ((size_t)tok * K + kk) * I, I, ngroups, afrag + (size_t)kk * ngroups * 16,
-                    corr + kk * ngroups, xsum + kk * ngroups);
     __syncthreads();
 
-    const uint2 *xf0 = afrag + (size_t)k * ngroups * 16;
-    const float *ck = corr + k * ngroups, *xk = xsum + k * ngroups;
-    const bool bl = (g == t);
-    float acca = 0.f, accb = 0.f;
+    // The routing (slots) was produced two kernels back and is complete once the gate/up
+    // kernel has started (it waits on the router before triggering this launch), so the
+    // weight copies go out before waiting on the activations.
+    const uint32_t slot_raw = a.slots[(size_t)tok * K + k];
+    const bool sok = slot_raw < (uint32_t)a.cap;
+    const size_t row0 = (size_t)(sok ? slot_raw : 0) * H + r0;
+    const uint32_t cb = 16u * rowb, sb = 16u * ng * 2u;
+    if (lane == 0 && sok) {
+        mbar_arrive_expect_tx(&bars[1 + k], cb + 2 * sb);
+        tma_load_1d(my, a.wd + row0 * (I >> 4), cb, &bars[1 + k]);
+        tma_load_1d(my + cb, a.sd + row0 * ng, sb, &bars[1 + k]);
+        tma_load_1d(my + cb + sb, a.bd + row0 * ng, sb, &bars[1 + k]);
+    }
+
+    pdl_wait();                       // activations (gate/up kernel) are complete
+    pdl_launch_dependents();
+
+    if (threadIdx.x == 0) {
+        if (self_stage) {
+            const uint32_t ab = (uint32_t)K * I * 2;
+            mbar_arrive_expect_tx(&bars[0], ab);
+            tma_load_1d(araw, a.act + (size_t)tok * K * I, ab, &bars[0]);
+        } else {
+            const uint32_t rb = (uint32_t)K * ng * 128, pb = (uint32_t)K * ng * 64;
+            mbar_arrive_expect_tx(&bars[0], rb + pb);
+            tma_load_1d(afrag, a.arec + (size_t)tok * K * ng * 16, rb, &bars[0]);
+            tma_load_1d(apart, a.apart + (size_t)tok * K * ng * 16, pb, &bars[0]);
+        }
+    }
+    const bool aok = mbar_wait(&bars[0], 0);
+    if (aok) {
+        if (self_stage) {
+            build_bfrag_smem(araw, K * ng, afrag, corr, xsum);   // K vectors back to back
+        } else {
+            for (int i = threadIdx.x; i < K * ng; i += blockDim.x) {   // fixed-order sum of 8 partials
+                float cs = 0.f, xs = 0.f;
 #pragma unroll
-    for (int i = 0; i < kSteps; ++i) {
-        if (i >= nsteps) break;
-        const int Gb = 4 * i;
-        const bool bok = bl && (Gb + t < ngroups);
-        const uint2 *xf = xf0 + (size_t)(Gb + t) * 16;
-        float d[4] = {0.f, 0.f, 0.f, 0.f};
-        const uint32_t awd[4] = {qa[i].x, qa[i].y, qa[i].z, qa[i].w};
-        const uint32_t bwd[4] = {qb[i].x, qb[i].y, qb[i].z, qb[i].w};
-#pragma unroll
-        for (int m = 0; m < 4; ++m) {
-            uint32_t pa[8], pb[8];
-            expand_word(awd[m], pa);
-            expand_word(bwd[m], pb);
-#pragma unroll
-            for (int mi = 0; mi < 4; ++mi) {
-                const uint2 b = bok ? xf[m * 4 + mi] : make_uint2(0u, 0u);
-                mma_bf16_16816(d, pa[2 * mi], pb[2 * mi], pa[2 * mi + 1], pb[2 * mi + 1], b.x, b.y);
+                for (int r = 0; r < 8; ++r) {
+                    cs += apart[(i * 8 + r) * 2 + 0];
+                    xs += apart[(i * 8 + r) * 2 + 1];
+                }
+                corr[i] = cs;
+                xsum[i] = xs;
             }
         }
-        if (t < 2) {
+    }
+    __syncthreads();
+    const bool wok = sok && aok && mbar_wait(&bars[1 + k], 0);
+
+    const uint16_t *sds = reinterpret_cast<const uint16_t *>(my + cb);
+    const uint16_t *bds = sds + 16 * ng;
+    float acca = 0.f, accb = 0.f;
+    if (wok) {
+        const uint2 *xf0 = afrag + (size_t)k * ng * 16;
+        const float *ck = corr + k * ng, *xk = xsum + k * ng;
+        const uint4 *rowa = reinterpret_cast<const uint4 *>(my + (size_t)g * rowb);
+        const uint4 *rowbp = reinterpret_cast<const uint4 *>(my + (size_t)(g + 8) * rowb);
+        const int nsteps = (ng + 3) >> 2;
+        const bool bl = (g == t);
+        for (int j = 0; j < nsteps; ++j) {
+            const int G = 4 * j + t;
+            const bool gok = G < ng;
+            const uint4 qa = gok ? rowa[G] : make_uint4(0, 0, 0, 0);
+            const uint4 qb = gok ? rowbp[G] : make_uint4(0, 0, 0, 0);
+            float d[4];
+            mma_step(qa, qb, xf0 + (size_t)G * 16, bl && gok, d);
+            if (t < 2) {
 #pragma unroll
-            for (int c = 0; c < 2; ++c) {
-                const int G = Gb + 2 * t + c;
-                if (G < ngroups) {
-                    acca += sa[i][c] * (d[c] - ck[G]) + ba[i][c] * xk[G];
-                    accb += sbv[i][c] * (d[2 + c] - ck[G]) + bbv[i][c] * xk[G];
+                for (int c = 0; c < 2; ++c) {
+                    const int G2 = 4 * j + 2 * t + c;
+                    if (G2 < ng) {
+                        const int sa = g * ng + G2, sbi = (g + 8) * ng + G2;
+                        acca += sb_to_f32<kFp16>(sds[sa]) * (d[c] - ck[G2]) + sb_to_f32<kFp16>(bds[sa]) * xk[G2];
+                        accb += sb_to_f32<kFp16>(sds[sbi]) * (d[2 + c] - ck[G2]) + sb_to_f32<kFp16>(bds[sbi]) * xk[G2];
+                    }
                 }
             }
         }
@@ -239,72 +364,104 @@ __global__ void __launch_bounds__(kMaxK * 32) down_kernel(
     acca += __shfl_xor_sync(0xffffffffu, acca, 1);
     accb += __shfl_xor_sync(0xffffffffu, accb, 1);
     if (t == 0) {
-        const float ya = bf16r(acca), yb = bf16r(accb);
+        const float ya = wok ? bf16r(acca) : 0.f, yb = wok ? bf16r(accb) : 0.f;
         yks[k * 16 + g] = ya;
         yks[k * 16 + 8 + g] = yb;
-        if (yk) {
-            const int oa = r0 + g, ob = r0 + 8 + g;
-            if (oa < H) yk[((size_t)tok * K + k) * H + oa] = f32_to_bf16_bits(ya);
-            if (ob < H) yk[((size_t)tok * K + k) * H + ob] = f32_to_bf16_bits(yb);
+        if (a.yk) {
+            a.yk[((size_t)tok * K + k) * H + r0 + g] = f32_to_bf16_bits(ya);
+            a.yk[((size_t)tok * K + k) * H + r0 + 8 + g] = f32_to_bf16_bits(yb);
         }
     }
     __syncthreads();
-    if (y && scores && threadIdx.x < 16) {
+    if (a.y && threadIdx.x < 16) {
         const int rr = r0 + threadIdx.x;
-        if (rr < H) {
-            float acc = 0.f;
-            for (int kk = 0; kk < K; ++kk) {
-                const float sc = bf16_bits_to_f32(__ldg(scores + (size_t)tok * K + kk));
-                const float pk = bf16r(yks[kk * 16 + threadIdx.x] * sc);
-                acc = (kk == 0) ? pk : bf16r(acc + pk);
-            }
-            if (addend) acc = bf16r(acc + bf16_bits_to_f32(addend[(size_t)tok * H + rr]));
-            if (resid) acc = bf16r(bf16_bits_to_f32(resid[(size_t)tok * H + rr]) + acc);
-            y[(size_t)tok * H + rr] = f32_to_bf16_bits(acc);
+        float acc = 0.f;
+        for (int kk = 0; kk < K; ++kk) {
+            const float sc = bf16_bits_to_f32(a.scores[(size_t)tok * K + kk]);
+            const float pk = bf16r(yks[kk * 16 + threadIdx.x] * sc);
+            acc = (kk == 0) ? pk : bf16r(acc + pk);
         }
+        if (a.addend) acc = bf16r(acc + bf16_bits_to_f32(a.addend[(size_t)tok * H + rr]));
+        if (a.resid) acc = bf16r(bf16_bits_to_f32(a.resid[(size_t)tok * H + rr]) + acc);
+        a.y[(size_t)tok * H + rr] = f32_to_bf16_bits(acc);
     }
 }
 
-int check_common(int H, int I, int K, int T, int bits, int group_size, const void *p0,
-                 const void *p1, const char *who) {
+int check_common(int H, int I, int K, int T, int cap, int bits, int group_size, const char *who) {
     if (bits != 2 || group_size != 64)
         return moe_set_error(MOE_EINVAL, "%s: only bits=2, group_size=64 are implemented (got %d, %d)", who,
                              bits, group_size);
-    if (T <= 0 || K <= 0 || K > kMaxK || H <= 0 || I <= 0 || H % 64 || I % 64)
-        return moe_set_error(MOE_EINVAL, "%s: bad sizes T=%d H=%d I=%d K=%d", who, T, H, I, K);
-    if ((reinterpret_cast<uintptr_t>(p0) | reinterpret_cast<uintptr_t>(p1)) & 15)
-        return moe_set_error(MOE_EINVAL, "%s: weight codes must be 16-byte aligned", who);
+    if (T <= 0 || K <= 0 || K > kMaxK || H <= 0 || I <= 0 || H % 64 || I % 64 || cap <= 0)
+        return moe_set_error(MOE_EINVAL, "%s: bad sizes T=%d H=%d I=%d K=%d cap=%d", who, T, H, I, K, cap);
     return MOE_OK;
 }
 
+bool misaligned(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15) != 0; }  // null is aligned
+
 }  // namespace
+
+__device__ unsigned int g_moe_device_error = 0;
+
+int moe_experts_gateup_ex(const void *x, const void *xrec, const float *xcorr, const float *xsum, int T,
+                          int H, int I, int K, int cap, const uint32_t *slots, const uint32_t *wg,
+                          const void *sg, const void *bg, const uint32_t *wu, const void *su, const void *bu,
+                          int bits, int group_size, int sb_fp16, void *act, void *arec, float *apart,
+                          void *stream) {
+    int rc = check_common(H, I, K, T, cap, bits, group_size, "experts_gateup");
+    if (rc) return rc;
+    if (!x || !slots || !wg || !wu || !sg || !bg || !su || !bu || !act)
+        return moe_set_error(MOE_EINVAL, "experts_gateup: null pointer");
+    if (misaligned(x) || misaligned(wg) || misaligned(wu) || misaligned(sg) || misaligned(bg) ||
+        misaligned(su) || misaligned(bu) || misaligned(xrec) || misaligned(xcorr) || misaligned(xsum))
+        return moe_set_error(MOE_EINVAL, "experts_gateup: tensors must be 16-byte aligned");
+    if ((xrec != nullptr) != (xcorr != nullptr) || (xrec != nullptr) != (xsum != nullptr) ||
+        (arec != nullptr) != (apart != nullptr))
+        return moe_set_error(MOE_EINVAL, "experts_gateup: incomplete record buffers");
+    const GuLayout L(H, xrec == nullptr);
+    if (L.total > 227 * 1024) return moe_set_error(MOE_EINVAL, "experts_gateup: H=%d too large", H);
+    GuArgs a{static_cast<const uint16_t *>(x), static_cast<const uint2 *>(xrec), xcorr, xsum, slots, wg, wu,
+             static_cast<const uint16_t *>(sg), static_cast<const uint16_t *>(bg),
+             static_cast<const uint16_t *>(su), static_cast<const uint16_t *>(bu), H, I, K, cap,
+             static_cast<uint16_t *>(act), static_cast<uint2 *>(arec), apart};
+    dim3 grid(I / 8, K, T);
+    cudaError_t e = sb_fp16 ? launch_pdl(gateup_kernel<true>, grid, dim3(kGuWarps * 32), L.total, as_stream(stream), a)
+                            : launch_pdl(gateup_kernel<false>, grid, dim3(kGuWarps * 32), L.total, as_stream(stream), a);
+    if (e != cudaSuccess) return moe_set_cuda_error(e);
+    return MOE_OK;
+}
+
+int moe_experts_down_ex(const void *act, const void *arec, const float *apart, int T, int H, int I, int K,
+                        int cap, const uint32_t *slots, const void *scores, const uint32_t *wd,
+                        const void *sd, const void *bd, int bits, int group_size, int sb_fp16,
+                        const void *addend, const void *resid, void *y, void *yk, void *stream) {
+    int rc = check_common(H, I, K, T, cap, bits, group_size, "experts_down");
+    if (rc) return rc;
+    if (!act || !slots || !wd || !sd || !bd) return moe_set_error(MOE_EINVAL, "experts_down: null pointer");
+    if (y && !scores) return moe_set_error(MOE_EINVAL, "experts_down: y needs scores");
+    if (!y && !yk) return moe_set_error(MOE_EINVAL, "experts_down: no output requested");
+    if ((arec != nullptr) != (apart != nullptr))
+        return moe_set_error(MOE_EINVAL, "experts_down: incomplete record buffers");
+    if (misaligned(act) || misaligned(wd) || misaligned(sd) || misaligned(bd) || misaligned(arec) || misaligned(apart))
+        return moe_set_error(MOE_EINVAL, "experts_down: tensors must be 16-byte aligned");
+    const DnLayout L(I, K, arec == nullptr);
+    if (L.total > 227 * 1024) return moe_set_error(MOE_EINVAL, "experts_down: K*I too large");
+    DnArgs a{static_cast<const uint16_t *>(act), static_cast<const uint2 *>(arec), apart, slots,
+             static_cast<const uint16_t *>(scores), wd, static_cast<const uint16_t *>(sd),
+             static_cast<const uint16_t *>(bd), H, I, K, cap, static_cast<const uint16_t *>(addend),
+             static_cast<const uint16_t *>(resid), static_cast<uint16_t *>(y), static_cast<uint16_t *>(yk)};
+    dim3 grid(H / 16, T);
+    cudaError_t e = sb_fp16 ? launch_pdl(down_kernel<true>, grid, dim3(K * 32), L.total, as_stream(stream), a)
+                            : launch_pdl(down_kernel<false>, grid, dim3(K * 32), L.total, as_stream(stream), a);
+    if (e != cudaSuccess) return moe_set_cuda_error(e);
+    return MOE_OK;
+}
 
 extern "C" int moe_experts_gateup(const void *x, int T, int H, int I, int K, int cap, const uint32_t *slots,
                                   const uint32_t *wg, const void *sg, const void *bg,
                                   const uint32_t *wu, const void *su, const void *bu, int bits,
                                   int group_size, int sb_fp16, void *act, void *stream) {
-    int rc = check_common(H, I, K, T, bits, group_size, wg, wu, "experts_gateup");
-    if (rc) return rc;
-    if (!x || !slots || !sg || !bg || !su || !bu || !act)
-        return moe_set_error(MOE_EINVAL, "experts_gateup: null pointer");
-    if (cap <= 0) return moe_set_error(MOE_EINVAL, "experts_gateup: cap=%d", cap);
-    const int ngroups = H / 64, nsteps = (ngroups + 3) / 4;
-    if ((nsteps + kGuWarps - 1) / kGuWarps > kGuMaxSteps)
-        return moe_set_error(MOE_EINVAL, "experts_gateup: H=%d exceeds %d", H, kGuWarps * kGuMaxSteps * 256);
-    const size_t smem = (size_t)ngroups * 128 + (size_t)ngroups * 8 + kGuWarps * 8 * 2 * sizeof(float);
-    dim3 grid((I + 7) / 8, K, T);
-    auto st = as_stream(stream);
-    const auto *xs = static_cast<const uint16_t *>(x);
-    if (sb_fp16)
-        gateup_kernel<true><<<grid, kGuWarps * 32, smem, st>>>(
-            xs, slots, wg, static_cast<const uint16_t *>(sg), static_cast<const uint16_t *>(bg), wu,
-            static_cast<const uint16_t *>(su), static_cast<const uint16_t *>(bu), H, I, K, cap, static_cast<uint16_t *>(act));
-    else
-        gateup_kernel<false><<<grid, kGuWarps * 32, smem, st>>>(
-            xs, slots, wg, static_cast<const uint16_t *>(sg), static_cast<const uint16_t *>(bg), wu,
-            static_cast<const uint16_t *>(su), static_cast<const uint16_t *>(bu), H, I, K, cap, static_cast<uint16_t *>(act));
-    MOE_CUDA_TRY(cudaGetLastError());
-    return MOE_OK;
+    return moe_experts_gateup_ex(x, nullptr, nullptr, nullptr, T, H, I, K, cap, slots, wg, sg, bg, wu, su, bu,
+                                 bits, group_size, sb_fp16, act, nullptr, nullptr, stream);
 }
 
 extern "C" int moe_experts_down(const void *act, int T, int H, int I, int K, int cap, const uint32_t *slots,
@@ -312,37 +469,18 @@ extern "C" int moe_experts_down(const void *act, int T, int H, int I, int K, int
                                 const void *bd, int bits, int group_size, int sb_fp16,
                                 const void *addend, const void *resid, void *y, void *yk,
                                 void *stream) {
-    int rc = check_common(H, I, K, T, bits, group_size, wd, wd, "experts_down");
-    if (rc) return rc;
-    if (!act || !slots || !sd || !bd) return moe_set_error(MOE_EINVAL, "experts_down: null pointer");
-    if (cap <= 0) return moe_set_error(MOE_EINVAL, "experts_down: cap=%d", cap);
-    if (y && !scores) return moe_set_error(MOE_EINVAL, "experts_down: y needs scores");
-    if (!y && !yk) return moe_set_error(MOE_EINVAL, "experts_down: no output requested");
-    const int ngroups = I / 64;
-    if ((ngroups + 3) / 4 > kDnMaxSteps)
-        return moe_set_error(MOE_EINVAL, "experts_down: I=%d exceeds %d", I, kDnMaxSteps * 256);
-    const size_t smem = (size_t)K * ngroups * 128 + (size_t)K * ngroups * 8 + (size_t)K * 16 * sizeof(float);
-    if (smem > 227 * 1024) return moe_set_error(MOE_EINVAL, "experts_down: K*I too large");
-    dim3 grid((H + 15) / 16, T);
-    auto st = as_stream(stream);
-    const int nsteps = (ngroups + 3) / 4;
-    const auto *as = static_cast<const uint16_t *>(act);
-    const auto *sc = static_cast<const uint16_t *>(scores);
-    const auto *sdp = static_cast<const uint16_t *>(sd);
-    const auto *bdp = static_cast<const uint16_t *>(bd);
-    const auto *adp = static_cast<const uint16_t *>(addend);
-    const auto *rsp = static_cast<const uint16_t *>(resid);
-    auto *yp = static_cast<uint16_t *>(y);
-    auto *ykp = static_cast<uint16_t *>(yk);
-    auto go = [&](auto kern) -> int {
-        if (smem > 48 * 1024)
-            MOE_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-        kern<<<grid, K * 32, smem, st>>>(as, slots, sc, wd, sdp, bdp, H, I, K, cap, adp, rsp, yp, ykp);
-        return MOE_OK;
-    };
-    if (sb_fp16) rc = (nsteps <= 4) ? go(down_kernel<true, 4>) : go(down_kernel<true, 8>);
-    else rc = (nsteps <= 4) ? go(down_kernel<false, 4>) : go(down_kernel<false, 8>);
-    if (rc) return rc;
-    MOE_CUDA_TRY(cudaGetLastError());
-    return MOE_OK;
+    return moe_experts_down_ex(act, nullptr, nullptr, T, H, I, K, cap, slots, scores, wd, sd, bd, bits,
+                               group_size, sb_fp16, addend, resid, y, yk, stream);
+}
+
+extern "C" int moe_device_error(int clear) {
+    unsigned int v = 0;
+    cudaError_t e = cudaMemcpyFromSymbol(&v, g_moe_device_error, sizeof(v));
+    if (e != cudaSuccess) return moe_set_cuda_error(e);
+    if (clear) {
+        unsigned int z = 0;
+        e = cudaMemcpyToSymbol(g_moe_device_error, &z, sizeof(z));
+        if (e != cudaSuccess) return moe_set_cuda_error(e);
+    }
+    return (int)v;
 }

@@ -16,8 +16,7 @@ namespace {
 
 constexpr int kWarps = 8;
 constexpr int kThreads = kWarps * 32;
-constexpr int kMaxE = 4096;              // experts per layer supported by the tail
-constexpr int kMaxPerThread = kMaxE / kThreads;
+constexpr int kMaxE = 2048;              // experts per layer supported by the tail
 
 struct RouterArgs {
     const uint16_t *x;
@@ -34,48 +33,48 @@ struct RouterArgs {
     uint16_t *scores;     // [T, K]
     uint32_t *pred;       // [T, M] or null
     unsigned int *tickets;  // [T], zero between launches
+    uint2 *xrec;          // [T, H/64, 16] MMA B records of x, or null (see build_bfrag_smem)
+    float *xcorr, *xsum;  // [T, pad4(H/64)] each
 };
 
 // ---------------------------------------------------------------- row dot products
 
-// bf16 weights: lanes stride over 16-byte chunks (8 values); products exact in double.
-MOE_D double row_dot_bf16(const uint16_t *__restrict__ x, const uint16_t *__restrict__ w, int H,
-                          int lane) {
+// bf16 weights: lanes stride over 16-byte chunks (8 values). A bf16 x bf16 product is exact
+// in fp32 (16 significant bits), so each product is formed in fp32 and accumulated in double.
+constexpr int kPre = 16;              // chunks per lane held in registers (H <= 4096)
+
+MOE_D void preload_row_bf16(const uint16_t *__restrict__ w, int H, int lane, uint4 (&wv)[kPre]) {
     const int nchunk = H >> 3;
-    double acc = 0.0;
-    constexpr int kPre = 16;
-    uint4 wv[kPre];
 #pragma unroll
     for (int j = 0; j < kPre; ++j) {
         const int c = lane + 32 * j;
         wv[j] = (c < nchunk) ? ldg_stream16(w + 8 * c) : make_uint4(0, 0, 0, 0);
     }
+}
+
+MOE_D double dot8_bf16(uint4 xv, uint4 wv, double acc) {
+    const uint32_t xs[4] = {xv.x, xv.y, xv.z, xv.w};
+    const uint32_t ws[4] = {wv.x, wv.y, wv.z, wv.w};
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+        acc += (double)(__uint_as_float(xs[q] << 16) * __uint_as_float(ws[q] << 16));
+        acc += (double)(__uint_as_float(xs[q] & 0xffff0000u) * __uint_as_float(ws[q] & 0xffff0000u));
+    }
+    return acc;
+}
+
+MOE_D double row_dot_bf16(const uint16_t *__restrict__ x, const uint16_t *__restrict__ w, int H, int lane,
+                          const uint4 (&wv)[kPre]) {
+    const int nchunk = H >> 3;
+    double acc[4] = {0.0, 0.0, 0.0, 0.0};        // independent chains
 #pragma unroll
     for (int j = 0; j < kPre; ++j) {
         const int c = lane + 32 * j;
-        if (c < nchunk) {
-            const uint4 xv = __ldg(reinterpret_cast<const uint4 *>(x) + c);
-            const uint32_t xs[4] = {xv.x, xv.y, xv.z, xv.w};
-            const uint32_t wsv[4] = {wv[j].x, wv[j].y, wv[j].z, wv[j].w};
-#pragma unroll
-            for (int q = 0; q < 4; ++q) {
-                acc = fma((double)__uint_as_float(xs[q] << 16), (double)__uint_as_float(wsv[q] << 16), acc);
-                acc = fma((double)__uint_as_float(xs[q] & 0xffff0000u), (double)__uint_as_float(wsv[q] & 0xffff0000u), acc);
-            }
-        }
+        if (c < nchunk) acc[j & 3] = dot8_bf16(__ldg(reinterpret_cast<const uint4 *>(x) + c), wv[j], acc[j & 3]);
     }
-    for (int c = lane + 32 * kPre; c < nchunk; c += 32) {   // H > 4096
-        const uint4 xv = __ldg(reinterpret_cast<const uint4 *>(x) + c);
-        const uint4 wv2 = ldg_stream16(w + 8 * c);
-        const uint32_t xs[4] = {xv.x, xv.y, xv.z, xv.w};
-        const uint32_t wsv[4] = {wv2.x, wv2.y, wv2.z, wv2.w};
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-            acc = fma((double)__uint_as_float(xs[q] << 16), (double)__uint_as_float(wsv[q] << 16), acc);
-            acc = fma((double)__uint_as_float(xs[q] & 0xffff0000u), (double)__uint_as_float(wsv[q] & 0xffff0000u), acc);
-        }
-    }
-    return acc;
+    for (int c = lane + 32 * kPre; c < nchunk; c += 32)   // H > 4096
+        acc[0] = dot8_bf16(__ldg(reinterpret_cast<const uint4 *>(x) + c), ldg_stream16(w + 8 * c), acc[0]);
+    return (acc[0] + acc[1]) + (acc[2] + acc[3]);
 }
 
 // affine-quantised weights (MLX layout), any bits in {2,4,8}: per 64-code group
@@ -113,21 +112,57 @@ MOE_D uint32_t bf16_order_key(uint16_t v) {
     return (v & 0x8000) ? (uint32_t)(~v & 0xffff) : (uint32_t)(v | 0x8000);
 }
 
-// Selects the n largest of keys[0..E) (all distinct, all > 0) with warp 0; keys of the
-// winners are zeroed in place. Results in descending order.
-MOE_D void warp_select_desc(uint32_t *keys, int E, int n, uint32_t *out) {
+// Selects the n largest of keys[0..E) (all distinct, all > 0) with warp 0, results in
+// descending order. Each lane keeps its local maximum; only the winning lane rescans. Keys
+// live in registers when E <= 512 and are rescanned from shared memory otherwise.
+constexpr int kRegKeys = 16;
+
+MOE_D void warp_select_desc(const uint32_t *keys, int E, int n, uint32_t *out) {
     const int lane = threadIdx.x & 31;
-    for (int r = 0; r < n; ++r) {
-        uint32_t best = 0;
-        for (int e = lane; e < E; e += 32) best = max(best, keys[e]);
-        const uint32_t win = __reduce_max_sync(0xffffffffu, best);
-        if (win != 0 && best == win) {
-            for (int e = lane; e < E; e += 32)
-                if (keys[e] == win) keys[e] = 0;
+    if (E <= 32 * kRegKeys) {
+        uint32_t kv[kRegKeys];
+        uint32_t lmax = 0;
+#pragma unroll
+        for (int j = 0; j < kRegKeys; ++j) {
+            const int e = lane + 32 * j;
+            kv[j] = (e < E) ? keys[e] : 0u;
+            lmax = max(lmax, kv[j]);
         }
-        if (lane == 0) out[r] = win;
-        __syncwarp();
+        for (int r = 0; r < n; ++r) {
+            const uint32_t win = __reduce_max_sync(0xffffffffu, lmax);
+            if (lmax == win) {
+                uint32_t nm = 0;
+#pragma unroll
+                for (int j = 0; j < kRegKeys; ++j) {
+                    kv[j] = (kv[j] == win) ? 0u : kv[j];
+                    nm = max(nm, kv[j]);
+                }
+                lmax = nm;
+            }
+            if (lane == 0) out[r] = win;
+        }
+    } else {
+        __shared__ uint32_t taken[64];
+        uint32_t lmax = 0;
+        for (int e = lane; e < E; e += 32) lmax = max(lmax, keys[e]);
+        for (int r = 0; r < n; ++r) {
+            const uint32_t win = __reduce_max_sync(0xffffffffu, lmax);
+            if (lane == 0) taken[r] = win;
+            __syncwarp();
+            if (lmax == win) {
+                uint32_t nm = 0;
+                for (int e = lane; e < E; e += 32) {
+                    const uint32_t kv = keys[e];
+                    bool used = false;
+                    for (int q = 0; q <= r; ++q) used |= (kv == taken[q]);
+                    if (!used) nm = max(nm, kv);
+                }
+                lmax = nm;
+            }
+            if (lane == 0) out[r] = win;
+        }
     }
+    __syncwarp();
 }
 
 template <bool kFp16, int kRbits>
@@ -138,13 +173,53 @@ __global__ void __launch_bounds__(kThreads) router_kernel(RouterArgs a) {
     const int row = blockIdx.x * kWarps + warp;
     const uint16_t *x = a.x + (size_t)t * a.H;
 
+    const bool next = row >= a.E;
+    const int e = next ? row - a.E : row;
+    uint4 wv[kPre];
+    if constexpr (kRbits == 16) {
+        if (row < rows) {
+            const uint16_t *w = reinterpret_cast<const uint16_t *>(next ? a.wn : a.w) + (size_t)e * a.H;
+            preload_row_bf16(w, a.H, lane, wv);   // weights do not depend on earlier kernels
+        }
+    }
+    pdl_wait();                                   // x is complete
+    pdl_launch_dependents();
+
+    if (a.xrec) {
+        // MMA B records of x for the expert kernels: 16 threads per 64-wide group
+        const int ng = a.H >> 6;
+        for (int G0 = blockIdx.x * (kThreads / 16); G0 < ng; G0 += gridDim.x * (kThreads / 16)) {
+            const int G = G0 + (threadIdx.x >> 4), ent = threadIdx.x & 15;
+            float cs = 0.f, xs = 0.f;
+            if (G < ng) {
+                const int m = ent >> 2, mi = ent & 3, c0 = G * 64 + 16 * m + 2 * mi;
+                const uint32_t p01 = __ldg(reinterpret_cast<const uint32_t *>(x + c0));
+                const uint32_t p89 = __ldg(reinterpret_cast<const uint32_t *>(x + c0 + 8));
+                const float v0 = __uint_as_float(p01 << 16), v2 = __uint_as_float(p01 & 0xffff0000u);
+                const float v1 = __uint_as_float(p89 << 16), v3 = __uint_as_float(p89 & 0xffff0000u);
+                const float i0 = pair_inv_scale(2 * mi), i1 = pair_inv_scale(2 * mi + 1);
+                const float s0 = v0 * i0, s1 = v1 * i0, s2 = v2 * i1, s3 = v3 * i1;
+                a.xrec[((size_t)t * ng + G) * 16 + ent] = make_uint2(pack_bf16x2(s0, s1), pack_bf16x2(s2, s3));
+                cs = (s0 + s1) + (s2 + s3);
+                xs = (v0 + v1) + (v2 + v3);
+            }
+#pragma unroll
+            for (int off = 8; off > 0; off >>= 1) {
+                cs += __shfl_xor_sync(0xffffffffu, cs, off);
+                xs += __shfl_xor_sync(0xffffffffu, xs, off);
+            }
+            if (G < ng && ent == 0) {
+                a.xcorr[(size_t)t * pad4(ng) + G] = cs;
+                a.xsum[(size_t)t * pad4(ng) + G] = xs;
+            }
+        }
+    }
+
     if (row < rows) {
-        const bool next = row >= a.E;
-        const int e = next ? row - a.E : row;
         double acc;
         if constexpr (kRbits == 16) {
             const uint16_t *w = reinterpret_cast<const uint16_t *>(next ? a.wn : a.w) + (size_t)e * a.H;
-            acc = row_dot_bf16(x, w, a.H, lane);
+            acc = row_dot_bf16(x, w, a.H, lane, wv);
         } else {
             const int words = a.H * kRbits / 32, ng = a.H / a.gs;
             const uint32_t *w = reinterpret_cast<const uint32_t *>(next ? a.wn : a.w) + (size_t)e * words;
@@ -177,20 +252,19 @@ __global__ void __launch_bounds__(kThreads) router_kernel(RouterArgs a) {
     __threadfence();
 
     __shared__ uint32_t s_keys[kMaxE];
+    __shared__ double s_ex[kMaxE];
     __shared__ float s_red[kWarps];
     __shared__ double s_redd[kWarps];
     __shared__ uint32_t s_sel[64];
     const int E = a.E;
     const uint16_t *lg = a.logits + (size_t)t * E;
 
-    // max
+    // max of the bf16 logits
     float mx = -INFINITY;
-    float lv[kMaxPerThread];
-#pragma unroll
-    for (int j = 0; j < kMaxPerThread; ++j) {
-        const int e = threadIdx.x + j * kThreads;
-        lv[j] = (e < E) ? bf16_bits_to_f32(__ldcg(lg + e)) : -INFINITY;
-        mx = fmaxf(mx, lv[j]);
+    for (int e = threadIdx.x; e < E; e += kThreads) {
+        const float v = bf16_bits_to_f32(__ldcg(lg + e));
+        s_ex[e] = (double)v;
+        mx = fmaxf(mx, v);
     }
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
@@ -201,13 +275,11 @@ __global__ void __launch_bounds__(kThreads) router_kernel(RouterArgs a) {
     for (int i = 1; i < kWarps; ++i) mx = fmaxf(mx, s_red[i]);
 
     // sum of exp in double (fixed reduction order -> deterministic)
-    double ex[kMaxPerThread];
     double sum = 0.0;
-#pragma unroll
-    for (int j = 0; j < kMaxPerThread; ++j) {
-        const int e = threadIdx.x + j * kThreads;
-        ex[j] = (e < E) ? exp((double)lv[j] - (double)mx) : 0.0;
-        sum += ex[j];
+    for (int e = threadIdx.x; e < E; e += kThreads) {
+        const double ev = exp(s_ex[e] - (double)mx);
+        s_ex[e] = ev;
+        sum += ev;
     }
     sum = warp_sum_d(sum);
     if (lane == 0) s_redd[warp] = sum;
@@ -217,14 +289,10 @@ __global__ void __launch_bounds__(kThreads) router_kernel(RouterArgs a) {
     for (int i = 0; i < kWarps; ++i) sum += s_redd[i];
 
     // bf16 probabilities and selection keys ((p << 16) | e) + 1, all distinct and > 0
-#pragma unroll
-    for (int j = 0; j < kMaxPerThread; ++j) {
-        const int e = threadIdx.x + j * kThreads;
-        if (e < E) {
-            const uint16_t p = f64_to_bf16_bits(ex[j] / sum);
-            if (a.probs) a.probs[(size_t)t * E + e] = p;
-            s_keys[e] = (((uint32_t)p << 16) | (uint32_t)e) + 1u;
-        }
+    for (int e = threadIdx.x; e < E; e += kThreads) {
+        const uint16_t p = f64_to_bf16_bits(s_ex[e] / sum);
+        if (a.probs) a.probs[(size_t)t * E + e] = p;
+        s_keys[e] = (((uint32_t)p << 16) | (uint32_t)e) + 1u;
     }
     __syncthreads();
 
@@ -276,24 +344,24 @@ cudaError_t launch_router(const RouterArgs &a, int rbits, cudaStream_t st) {
     const int rows = a.E * (a.M > 0 ? 2 : 1);
     dim3 grid((rows + kWarps - 1) / kWarps, a.T);
     switch (rbits) {
-        case 16: router_kernel<kFp16, 16><<<grid, kThreads, 0, st>>>(a); break;
-        case 8: router_kernel<kFp16, 8><<<grid, kThreads, 0, st>>>(a); break;
-        case 4: router_kernel<kFp16, 4><<<grid, kThreads, 0, st>>>(a); break;
-        case 2: router_kernel<kFp16, 2><<<grid, kThreads, 0, st>>>(a); break;
+        case 16: return launch_pdl(router_kernel<kFp16, 16>, grid, dim3(kThreads), 0, st, a);
+        case 8: return launch_pdl(router_kernel<kFp16, 8>, grid, dim3(kThreads), 0, st, a);
+        case 4: return launch_pdl(router_kernel<kFp16, 4>, grid, dim3(kThreads), 0, st, a);
+        case 2: return launch_pdl(router_kernel<kFp16, 2>, grid, dim3(kThreads), 0, st, a);
         default: return cudaErrorInvalidValue;
     }
-    return cudaGetLastError();
 }
 
-inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+inline size_t al_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
 }  // namespace
 
 extern "C" size_t moe_router_workspace_bytes(int T, int E, int M) {
     if (T <= 0 || E <= 0) return 0;
-    size_t b = align_up((size_t)T * sizeof(unsigned int), 256);        // tickets
-    b += align_up((size_t)T * E * sizeof(uint16_t), 256);               // logits
-    if (M > 0) b += align_up((size_t)T * E * sizeof(uint16_t), 256);    // prediction logits
+    size_t b = al_up((size_t)T * sizeof(unsigned int), 256);        // tickets
+    b += al_up((size_t)T * E * sizeof(uint16_t), 256);               // logits
+    if (M > 0) b += al_up((size_t)T * E * sizeof(uint16_t), 256);    // prediction logits
     return b;
 }
 
@@ -305,7 +373,7 @@ int moe_router_launch(const void *x, int T, int H, int E, int K, const void *w,
                       int M, const float *pred_bias, void *out_logits, void *out_probs,
                       uint32_t *out_inds, void *out_scores, uint32_t *out_pred,
                       unsigned int *tickets, uint16_t *logits_buf, uint16_t *plogits_buf,
-                      void *stream) {
+                      void *xrec, float *xcorr, float *xsum, void *stream) {
     if (!x || !w || !out_inds || !out_scores || !tickets)
         return moe_set_error(MOE_EINVAL, "router: null required pointer");
     if (T <= 0 || H <= 0 || E <= 0 || E > kMaxE || K <= 0 || K > E || K > 64)
@@ -338,6 +406,11 @@ int moe_router_launch(const void *x, int T, int H, int E, int K, const void *w,
     a.scores = static_cast<uint16_t *>(out_scores);
     a.pred = out_pred;
     a.tickets = tickets;
+    a.xrec = static_cast<uint2 *>(xrec);
+    a.xcorr = xcorr;
+    a.xsum = xsum;
+    if (xrec && (H % 64 || !xcorr || !xsum))
+        return moe_set_error(MOE_EINVAL, "router: x records need H %% 64 == 0 and corr/sum buffers");
     if (!a.logits || (M > 0 && !a.plogits))
         return moe_set_error(MOE_EINVAL, "router: missing logit scratch");
     cudaError_t e = sb_fp16 ? launch_router<true>(a, rbits, as_stream(stream))
@@ -360,11 +433,12 @@ extern "C" int moe_router_topk(const void *x, int T, int H, int E, int K, const 
                              workspace_bytes);
     char *ws = static_cast<char *>(workspace);
     unsigned int *tickets = reinterpret_cast<unsigned int *>(ws);
-    ws += align_up((size_t)T * sizeof(unsigned int), 256);
+    ws += al_up((size_t)T * sizeof(unsigned int), 256);
     uint16_t *logits = reinterpret_cast<uint16_t *>(ws);
-    ws += align_up((size_t)T * E * sizeof(uint16_t), 256);
+    ws += al_up((size_t)T * E * sizeof(uint16_t), 256);
     uint16_t *plogits = M > 0 ? reinterpret_cast<uint16_t *>(ws) : nullptr;
     return moe_router_launch(x, T, H, E, K, w, w_scales, w_biases, rbits, group_size, sb_fp16, wn,
                              wn_scales, wn_biases, M, pred_bias, out_logits, out_probs, out_inds,
-                             out_scores, out_pred, tickets, logits, plogits, stream);
+                             out_scores, out_pred, tickets, logits, plogits, nullptr, nullptr, nullptr,
+                             stream);
 }

@@ -172,3 +172,47 @@ def experts_down(act: torch.Tensor, slots: torch.Tensor, down: QMatrix, scores=N
          down.w.data_ptr(), down.s.data_ptr(), down.b.data_ptr(), down.bits, down.group_size,
          down.sb_fp16, _ptr(addend), _ptr(resid), _ptr(y), _ptr(yk), _stream(stream))
     return y, yk
+
+
+# ----------------------------------------------------------------------------- fused layer
+
+_DWS: dict = {}
+
+
+def decode_workspace(device, T: int, H: int, I: int, E: int, K: int, M: int) -> torch.Tensor:
+    key = (torch.device(device), T, H, I, E, K, M)
+    ws = _DWS.get(key)
+    if ws is None:
+        nbytes = int(call("moe_decode_workspace_bytes", T, H, I, E, K, M))
+        ws = torch.zeros(nbytes, dtype=torch.uint8, device=device)
+        _DWS[key] = ws
+    return ws
+
+
+def decode_layer(x: torch.Tensor, router: torch.Tensor, gate: QMatrix, up: QMatrix, down: QMatrix,
+                 K: int, *, router_next=None, M: int = 0, pred_bias=None, addend=None, resid=None,
+                 out: dict | None = None, workspace: torch.Tensor | None = None, stream=None) -> dict:
+    """One decode step of an all-resident layer: router -> experts -> combine (three kernels).
+    Returns dict(y, inds, scores[, pred])."""
+    _need(x, "x", (torch.bfloat16,))
+    dev = x.device
+    T, H = x.shape
+    _need(router, "router", (torch.bfloat16,), dev)
+    E = router.shape[0]
+    I = gate.w.shape[1]
+    for name, q in (("gate", gate), ("up", up), ("down", down)):
+        q.check(name, dev)
+    o = out if out is not None else {}
+    o.setdefault("y", torch.empty((T, H), dtype=torch.bfloat16, device=dev))
+    o.setdefault("inds", torch.empty((T, K), dtype=torch.int32, device=dev))
+    o.setdefault("scores", torch.empty((T, K), dtype=torch.bfloat16, device=dev))
+    if M > 0:
+        _need(router_next, "router_next", (torch.bfloat16,), dev)
+        o.setdefault("pred", torch.empty((T, M), dtype=torch.int32, device=dev))
+    ws = workspace if workspace is not None else decode_workspace(dev, T, H, I, E, K, M)
+    call("moe_decode_layer", x.data_ptr(), T, H, I, E, K, router.data_ptr(), _ptr(router_next if M else None),
+         M, _ptr(pred_bias), gate.w.data_ptr(), gate.s.data_ptr(), gate.b.data_ptr(), up.w.data_ptr(),
+         up.s.data_ptr(), up.b.data_ptr(), down.w.data_ptr(), down.s.data_ptr(), down.b.data_ptr(),
+         gate.sb_fp16, _ptr(addend), _ptr(resid), o["inds"].data_ptr(), o["scores"].data_ptr(),
+         _ptr(o.get("pred")), o["y"].data_ptr(), ws.data_ptr(), ws.numel(), _stream(stream))
+    return o

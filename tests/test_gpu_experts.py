@@ -94,3 +94,34 @@ def test_slot_path_equals_resident_path(dev):
     _, y_res, _ = _run(dev, x, eids, sc, g, u, d, True)
     _, y_slot, _ = _run(dev, x, slot_of[eids].astype(np.uint32), sc, g2, u2, d2, True)
     assert np.array_equal(y_res, y_slot)
+
+
+@pytest.mark.parametrize("H,I,E,K,M", [(2048, 768, 64, 8, 0), (3072, 768, 32, 10, 12), (2688, 1856, 24, 9, 0)])
+def test_fused_decode_layer_vs_oracle(dev, H, I, E, K, M):
+    """router -> gate/up -> down chained with records in the workspace (the stack's layer)."""
+    from moe_offload_b200 import ops
+    from moe_offload_b200.synthetic import (bf16_tensor_to_np, np_bf16_normal, np_qmatrix, np_to_bf16_tensor,
+                                            to_device_qmatrix)
+    rng = np.random.default_rng(H + E)
+    T = 2
+    g, u, d = np_qmatrix(rng, E, I, H), np_qmatrix(rng, E, I, H), np_qmatrix(rng, E, H, I)
+    wr = np_bf16_normal(rng, (E, H), 0.02)
+    wn = np_bf16_normal(rng, (E, H), 0.02)
+    x = np_bf16_normal(rng, (T, H))
+    out = ops.decode_layer(np_to_bf16_tensor(x, dev), np_to_bf16_tensor(wr, dev), to_device_qmatrix(g, dev),
+                           to_device_qmatrix(u, dev), to_device_qmatrix(d, dev), K,
+                           router_next=np_to_bf16_tensor(wn, dev) if M else None, M=M,
+                           resid=np_to_bf16_tensor(x, dev))
+    torch.cuda.synchronize()
+    _, inds, scores = orc.softmax_topk(orc.router_logits(x, wr, E), K)
+    assert np.array_equal(out["inds"].cpu().numpy().astype(np.uint32), inds)
+    assert np.array_equal(bf16_tensor_to_np(out["scores"]), scores)
+    if M:
+        assert np.array_equal(out["pred"].cpu().numpy().astype(np.uint32), orc.topm_sorted(orc.router_logits(x, wn, E), M))
+    ref = orc.experts(x, inds, scores, g, u, d, sb_fp16=True, resid=x)
+    y = bf16_tensor_to_np(out["y"])
+    for t in range(T):
+        # compare the MoE contribution (y - resid) so the residual does not mask errors
+        a = orc.bf16_to_f32(y[t]).astype(np.float64) - orc.bf16_to_f32(x[t])
+        b = orc.bf16_to_f32(ref["y"][t]).astype(np.float64) - orc.bf16_to_f32(x[t])
+        assert np.linalg.norm(a - b) / np.linalg.norm(b) < REL_TOL
