@@ -78,6 +78,27 @@ int moe_router_topk(const void *x, int T, int H, int E, int K,
                     void *out_logits, void *out_probs, uint32_t *out_inds, void *out_scores,
                     uint32_t *out_pred, void *workspace, size_t workspace_bytes, void *stream);
 
+/*
+ * moe_router_topk without a workspace, for callers that cannot allocate device memory: a C
+ * or FFI host that only receives device pointers from elsewhere and has no allocator of
+ * its own, or a process whose device memory is fully reserved by another allocator.
+ * This entry point has no counterpart in the reference (its C library never touches the
+ * GPU). Same arguments, arithmetic and results as moe_router_topk, minus the workspace.
+ * Scratch lives in a fixed array of 257 KiB that every device which loads the library holds
+ * until the process exits; limits: T <= 256 and T * E <= 65536, larger sizes return
+ * MOE_EINVAL. The first call on a device looks up that device's copy of the array (make it
+ * with the device current, before any stream capture). Every call shares the array and it
+ * keeps the last call's contents (the per-token tickets are cleared at the start of each
+ * call); calls that overlap on the GPU race. Allocates nothing (no cudaMalloc/cudaFree).
+ */
+int moe_router_topk_noalloc(const void *x, int T, int H, int E, int K,
+                            const void *w, const void *w_scales, const void *w_biases,
+                            int rbits, int group_size, int sb_fp16,
+                            const void *wn, const void *wn_scales, const void *wn_biases,
+                            int M, const float *pred_bias,
+                            void *out_logits, void *out_probs, uint32_t *out_inds,
+                            void *out_scores, uint32_t *out_pred, void *stream);
+
 /* ------------------------------------------------------------------------------------ */
 /* Routed experts, decode (one row of x per token).                                       */
 /* ------------------------------------------------------------------------------------ */

@@ -34,6 +34,7 @@ SIGNATURES: dict[str, tuple] = {
     "moe_last_error": (ctypes.c_char_p, []),
     "moe_router_workspace_bytes": (SZ, [I, I, I]),
     "moe_router_topk": (I, [P, I, I, I, I, P, P, P, I, I, I, P, P, P, I, P, P, P, P, P, P, P, SZ, P]),
+    "moe_router_topk_noalloc": (I, [P, I, I, I, I, P, P, P, I, I, I, P, P, P, I, P, P, P, P, P, P, P]),
     "moe_experts_gateup": (I, [P, I, I, I, I, I, P, P, P, P, P, P, P, I, I, I, P, P]),
     "moe_experts_down": (I, [P, I, I, I, I, I, P, P, P, P, P, I, I, I, P, P, P, P, P]),
     "moe_device_error": (I, [I]),
