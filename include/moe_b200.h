@@ -141,14 +141,48 @@ size_t moe_decode_workspace_bytes(int T, int H, int I, int E, int K, int M);
  * Three kernels chained with programmatic dependent launch; the router is bf16 [E, H];
  * router_next_w / M / pred_bias as in moe_router_topk. Expert weights as in
  * moe_experts_gateup / moe_experts_down with cap = E. resid/addend optional (bf16 [T, H]).
+ * norm = 1: the MoE input is x * 2^-k, the power of two nearest x's RMS (k = floor(e/2) for
+ * mean(x^2) in [2^(e-1), 2^e)), standing in for the model's pre-MoE RMSNorm while keeping the
+ * rescale exact; the residual stays x. norm = 0: the input is x as given.
  */
 int moe_decode_layer(const void *x, int T, int H, int I, int E, int K, const void *router_w,
                      const void *router_next_w, int M, const float *pred_bias,
                      const uint32_t *wg, const void *sg, const void *bg,
                      const uint32_t *wu, const void *su, const void *bu,
-                     const uint32_t *wd, const void *sd, const void *bd, int sb_fp16,
+                     const uint32_t *wd, const void *sd, const void *bd, int sb_fp16, int norm,
                      const void *addend, const void *resid, uint32_t *out_inds, void *out_scores,
                      uint32_t *out_pred, void *y, void *workspace, size_t workspace_bytes, void *stream);
+
+/* ------------------------------------------------------------------------------------ */
+/* Persistent decode of a whole resident stack (one token through L layers, one launch).  */
+/* ------------------------------------------------------------------------------------ */
+
+/* Per-layer weights of moe_stack_decode, passed as a DEVICE array of L descriptors. The
+ * router is transposed ([H][E] bf16, row h = the E router weights of input h); expert
+ * tensors as in moe_experts_gateup / moe_experts_down with cap = E. */
+typedef struct {
+    const void *router_t;
+    const uint32_t *wg, *wu, *wd;
+    const void *sg, *bg, *su, *bu, *sd, *bd;
+} moe_stack_layer;
+
+/* Workspace bytes for moe_stack_decode (no zero-filling needed: each call clears it). */
+size_t moe_stack_workspace_bytes(int H, int I, int E, int K);
+
+/*
+ * h_{l+1} = h_l + MoE_l(h_l) for l = 0..L-1 on one token (batch 1), all experts resident:
+ * the reference's decode loop over resident layers (mlx-qwen38/loader.py:1176-1195 around
+ * the per-layer block of loader.py:903-922), as ONE cooperative kernel with one CTA per SM
+ * (num_ctas = 0: all SMs) and two grid barriers per layer. x, y bf16 [H]; inds_out u32
+ * [L][K] and scores_out bf16 [L][K] (MLX order, as moe_router_topk); hs_out bf16 [L+1][H]
+ * (every layer's input and the final output) or NULL. Requires H % 256 == 0, I % 64 == 0,
+ * K <= 32, E <= 2048. Router logits are sums of per-CTA exact partial dot products in double
+ * (order of the partial sums varies between runs at the 2^-52 level). norm as in
+ * moe_decode_layer (applied to every layer's input).
+ */
+int moe_stack_decode(const void *layers, int L, int H, int I, int E, int K, int sb_fp16, int norm,
+                     const void *x, void *y, uint32_t *inds_out, void *scores_out, void *hs_out,
+                     void *workspace, size_t workspace_bytes, int num_ctas, void *stream);
 
 /*
  * Device-side error word (bit 1: a bounded mbarrier/flag wait gave up, bit 2: invalid

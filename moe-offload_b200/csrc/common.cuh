@@ -42,6 +42,16 @@ MOE_D uint16_t f32_to_bf16_bits(float f) {
 
 MOE_D float bf16r(float f) { return bf16_bits_to_f32(f32_to_bf16_bits(f)); }
 
+// Power-of-two RMS normalisation of a layer input: x = h * 2^-k with k = floor(e / 2) for
+// sum(h^2)/n in [2^(e-1), 2^e), so RMS(x) lies in [2^-0.5, 2^0.5). A power of two keeps every
+// bf16 value exact (x and h have the same mantissas), so x.W = 2^-k (h.W) exactly.
+MOE_HD int pow2_rms_shift(double sumsq, int n) {
+    if (!(sumsq > 0.0) || n <= 0) return 0;
+    int e = 0;
+    frexp(sumsq / (double)n, &e);
+    return (e >= 0) ? e / 2 : -((1 - e) / 2);
+}
+
 // double -> bf16 with ONE rounding (cvt.rn.bf16.f64, sm_90+): the router's logits and
 // probabilities are rounded once from an order-independent double value.
 MOE_D uint16_t f64_to_bf16_bits(double d) {

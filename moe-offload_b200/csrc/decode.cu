@@ -1,7 +1,7 @@
 // One decode step of one MoE layer with every expert resident in HBM: router (+ optional
 // next-layer prediction) -> gate/up + SwiGLU -> down + combine, three PDL-chained kernels
-// that hand each other the MMA B records of their input vectors through the workspace, so
-// no kernel re-stages an input. This is the per-layer body of the reference's decode hook
+// that hand each other the int8 MMA records of their input vectors (gemv_i8.cuh) through
+// the workspace, so no kernel re-stages an input. This is the per-layer body of the reference's decode hook
 // for a resident layer (mlx-qwen38/loader.py:903-922; cpp/src/engine.cpp:532-571).
 #include "common.cuh"
 #include "internal.h"
@@ -12,10 +12,11 @@ struct DecodeWs {
     unsigned int *tickets;
     uint16_t *logits, *plogits;
     uint2 *xrec;
-    float *xcorr, *xsum;
+    float *xscale, *xsum;
     uint16_t *act;
     uint2 *arec;
-    float *apart;
+    float *ascale, *asum;
+    unsigned int *acnt;
     size_t bytes;
 };
 
@@ -29,11 +30,13 @@ DecodeWs carve(void *base, int T, int H, int I, int E, int K, int M) {
     w.logits = reinterpret_cast<uint16_t *>(take((size_t)T * E * 2));
     w.plogits = reinterpret_cast<uint16_t *>(take(M > 0 ? (size_t)T * E * 2 : 0));
     w.xrec = reinterpret_cast<uint2 *>(take((size_t)T * ngH * 128));
-    w.xcorr = reinterpret_cast<float *>(take((size_t)T * pad4(ngH) * 4));
+    w.xscale = reinterpret_cast<float *>(take((size_t)T * pad4(ngH) * 4));
     w.xsum = reinterpret_cast<float *>(take((size_t)T * pad4(ngH) * 4));
     w.act = reinterpret_cast<uint16_t *>(take((size_t)T * K * I * 2));
     w.arec = reinterpret_cast<uint2 *>(take((size_t)T * K * ngI * 128));
-    w.apart = reinterpret_cast<float *>(take((size_t)T * K * ngI * 64));
+    w.ascale = reinterpret_cast<float *>(take((size_t)T * pad4(K * ngI) * 4));
+    w.asum = reinterpret_cast<float *>(take((size_t)T * pad4(K * ngI) * 4));
+    w.acnt = reinterpret_cast<unsigned int *>(take((size_t)T * K * ngI * 4));
     w.bytes = off;
     if (M <= 0) w.plogits = nullptr;
     return w;
@@ -50,7 +53,7 @@ extern "C" int moe_decode_layer(const void *x, int T, int H, int I, int E, int K
                                 const void *router_next_w, int M, const float *pred_bias,
                                 const uint32_t *wg, const void *sg, const void *bg, const uint32_t *wu,
                                 const void *su, const void *bu, const uint32_t *wd, const void *sd,
-                                const void *bd, int sb_fp16, const void *addend, const void *resid,
+                                const void *bd, int sb_fp16, int norm, const void *addend, const void *resid,
                                 uint32_t *out_inds, void *out_scores, uint32_t *out_pred, void *y,
                                 void *workspace, size_t workspace_bytes, void *stream) {
     if (!y || !out_inds || !out_scores) return moe_set_error(MOE_EINVAL, "decode_layer: null output");
@@ -62,11 +65,11 @@ extern "C" int moe_decode_layer(const void *x, int T, int H, int I, int E, int K
     DecodeWs w = carve(workspace, T, H, I, E, K, M);
     int rc = moe_router_launch(x, T, H, E, K, router_w, nullptr, nullptr, 16, 64, 0, router_next_w, nullptr,
                                nullptr, M, pred_bias, nullptr, nullptr, out_inds, out_scores, out_pred,
-                               w.tickets, w.logits, w.plogits, w.xrec, w.xcorr, w.xsum, stream);
+                               w.tickets, w.logits, w.plogits, w.xrec, w.xscale, w.xsum, norm, stream);
     if (rc) return rc;
-    rc = moe_experts_gateup_ex(x, w.xrec, w.xcorr, w.xsum, T, H, I, K, E, out_inds, wg, sg, bg, wu, su, bu, 2, 64,
-                               sb_fp16, w.act, w.arec, w.apart, stream);
+    rc = moe_experts_gateup_ex(x, w.xrec, w.xscale, w.xsum, T, H, I, K, E, out_inds, wg, sg, bg, wu, su, bu, 2, 64,
+                               sb_fp16, w.act, w.arec, w.ascale, w.asum, w.acnt, stream);
     if (rc) return rc;
-    return moe_experts_down_ex(w.act, w.arec, w.apart, T, H, I, K, E, out_inds, out_scores, wd, sd, bd, 2, 64,
+    return moe_experts_down_ex(w.act, w.arec, w.ascale, w.asum, T, H, I, K, E, out_inds, out_scores, wd, sd, bd, 2, 64,
                                sb_fp16, addend, resid, y, nullptr, stream);
 }

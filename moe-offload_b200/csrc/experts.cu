@@ -1,27 +1,25 @@
 // Decode expert GEMVs over 2-bit affine (group 64) weights in MLX layout.
 //
-// Data movement: each warp owns a contiguous block of weight rows (8 gate + 8 up rows, or
-// 16 down rows) and pulls it -- codes, scales and biases -- into shared memory with 1-D TMA
-// bulk copies that complete on a per-warp mbarrier; the token's input vector arrives the
-// same way. All copies of a CTA are issued before any compute, so a wave of CTAs keeps the
-// whole layer's weight stream in flight. With programmatic dependent launch the down
-// kernel issues its weight copies while the gate/up kernel is still running.
+// Data movement: each CTA owns a contiguous block of weight rows (8 gate + 8 up rows of one
+// routed expert, or 16 down rows of every routed expert) and pulls it -- codes, scales and
+// biases -- into shared memory with 1-D TMA bulk copies (cp.async.bulk, no multicast) that
+// complete on an mbarrier; the input's MMA records arrive the same way. With programmatic
+// dependent launch the down kernel issues its weight copies while the gate/up kernel is
+// still running.
 //
-// Dot products: m16n8k16 bf16 MMAs. The A operand is built in registers from the packed
-// codes (expand_word: 10 integer ops per 16 codes, exact bf16 values 1 + q*c); B holds the
-// input pre-scaled by 1/c, so D = sum(x/c) + sum(q*x) and the per-group constant sum(x/c)
-// ("corr") is subtracted in the epilogue. A GEMV has one useful column; N is used to run
-// four 64-code groups per MMA instead: lane quad t of every row supplies group 4j+t, and B
-// column n carries group 4j+n on lane t == n's k-slots only, so D[row][n] is the row's
-// partial dot over group 4j+n. The per-group affine terms are applied in fp32:
-//   row += s[g] * (D - corr[g]) + b[g] * sum(x[g]).
+// Dot products: m16n8k32 u8 x s8 integer MMAs (gemv_i8.cuh): codes masked in place as u8,
+// input split exactly into int8 hi/lo parts per group, exact int32 accumulation; the
+// per-group affine terms are applied in fp32:  row += s[G] * dot[G] * 2^E[G] + b[G] * sum[G].
 //
-//   gate/up  grid (ceil(I/8/kGuWarps), K, T); warp = one block of 8 rows of one routed
-//            expert, MMA rows 0-7 gate, 8-15 up, SwiGLU in the epilogue
-//            (cpp/src/layers.cpp:349-358, cpp/src/kernels.cpp:1090-1094).
+//   gate/up  grid (I/8, K, T), 4 warps split the H axis of one block of 8 gate rows (MMA
+//            rows 0-7) and the matching 8 up rows (rows 8-15); SwiGLU in the epilogue
+//            (cpp/src/layers.cpp:349-358, cpp/src/kernels.cpp:1090-1094). The last of the 8
+//            CTAs covering a 64-wide group of the activations builds that group's record
+//            for the down kernel (atomic ticket per group, re-armed by the builder).
 //   down     grid (H/16, T); warp k = routed expert k over all of I for 16 output rows; the
 //            CTA combines the K experts with the routing scores (loader.py:914,965).
 #include "common.cuh"
+#include "gemv_i8.cuh"
 
 namespace {
 
@@ -29,58 +27,32 @@ constexpr int kGuWarps = 4;        // K-split warps per gate/up CTA (one 8-row b
 constexpr int kMaxK = 16;
 
 
-// One MMA step: the row pair (ra, rb) of this lane against four 64-code groups
-// (lane quad t supplies group G = 4j + t). Four independent accumulator chains (one per
-// 16-code word) keep the tensor-core latency hidden; D[.][n] = partial over group 4j + n.
-MOE_D void mma_step(const uint4 wa, const uint4 wb, const uint2 *xf, bool bok, float d[4]) {
-    float dm[4][4];
-#pragma unroll
-    for (int m = 0; m < 4; ++m) dm[m][0] = dm[m][1] = dm[m][2] = dm[m][3] = 0.f;
-    const uint32_t aw[4] = {wa.x, wa.y, wa.z, wa.w};
-    const uint32_t bw[4] = {wb.x, wb.y, wb.z, wb.w};
-#pragma unroll
-    for (int m = 0; m < 4; ++m) {
-        uint32_t pa[8], pb[8];
-        expand_word(aw[m], pa);
-        expand_word(bw[m], pb);
-        uint4 b01 = make_uint4(0u, 0u, 0u, 0u), b23 = make_uint4(0u, 0u, 0u, 0u);
-        if (bok) {
-            b01 = *reinterpret_cast<const uint4 *>(xf + m * 4);       // entries (m,0),(m,1)
-            b23 = *reinterpret_cast<const uint4 *>(xf + m * 4 + 2);   // entries (m,2),(m,3)
-        }
-        mma_bf16_16816(dm[m], pa[0], pb[0], pa[1], pb[1], b01.x, b01.y);
-        mma_bf16_16816(dm[m], pa[2], pb[2], pa[3], pb[3], b01.z, b01.w);
-        mma_bf16_16816(dm[m], pa[4], pb[4], pa[5], pb[5], b23.x, b23.y);
-        mma_bf16_16816(dm[m], pa[6], pb[6], pa[7], pb[7], b23.z, b23.w);
-    }
-#pragma unroll
-    for (int q = 0; q < 4; ++q) d[q] = (dm[0][q] + dm[1][q]) + (dm[2][q] + dm[3][q]);
-}
-
 // --------------------------------------------------------------------- gate + up
 
 struct GuArgs {
     const uint16_t *x;
-    const uint2 *xrec;          // optional pre-built B records of x ([T][ngH][16])
-    const float *xcorr, *xsum;  // [T][pad4(ngH)]
+    const uint2 *xrec;           // optional pre-built records of x ([T][ngH][16])
+    const float *xscale, *xsum;  // [T][pad4(ngH)]
     const uint32_t *slots;
     const uint32_t *wg, *wu;
     const uint16_t *sg, *bg, *su, *bu;
     int H, I, K, cap;
-    uint16_t *act;              // [T][K][I]
-    uint2 *arec;                // optional B records of act ([T][K][ngI][16])
-    float *apart;               // [T][K][ngI][8][2] per-8-row partial (corr, sum)
+    uint16_t *act;               // [T][K][I]
+    uint2 *arec;                 // optional records of act ([T][K][ngI][16])
+    float *ascale, *asum;        // [T][pad4(K*ngI)]
+    unsigned int *acnt;          // [T][K][ngI] tickets, zero between launches
 };
 
 struct GuLayout {
-    size_t xraw, xfrag, corr, xsum, w, red, total;
+    size_t xraw, rec, scale, sum, zero, w, red, total;
     MOE_HD GuLayout(int H, bool self_stage) {
         const int ng = H / 64;
         xraw = 128;
-        xfrag = xraw + (self_stage ? al16((size_t)H * 2) : 0);
-        corr = xfrag + (size_t)ng * 128;
-        xsum = corr + al16((size_t)pad4(ng) * 4);
-        w = al128(xsum + al16((size_t)pad4(ng) * 4));
+        rec = xraw + (self_stage ? al16((size_t)H * 2) : 0);
+        scale = rec + (size_t)ng * 128;
+        sum = scale + al16((size_t)pad4(ng) * 4);
+        zero = sum + al16((size_t)pad4(ng) * 4);
+        w = al128(zero + 128);
         red = w + al16(16 * (size_t)(H / 4) + 4 * 8 * (size_t)ng * 2);
         total = red + kGuWarps * 8 * 2 * 4;
     }
@@ -95,9 +67,10 @@ __global__ void __launch_bounds__(kGuWarps * 32) gateup_kernel(GuArgs a) {
     const GuLayout L(H, self_stage);
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem);
     uint16_t *xraw = reinterpret_cast<uint16_t *>(smem + L.xraw);
-    uint2 *xfrag = reinterpret_cast<uint2 *>(smem + L.xfrag);
-    float *corr = reinterpret_cast<float *>(smem + L.corr);
-    float *xsum = reinterpret_cast<float *>(smem + L.xsum);
+    uint2 *xrec = reinterpret_cast<uint2 *>(smem + L.rec);
+    float *xscale = reinterpret_cast<float *>(smem + L.scale);
+    float *xsum = reinterpret_cast<float *>(smem + L.sum);
+    uint2 *zrec = reinterpret_cast<uint2 *>(smem + L.zero);
     unsigned char *wsm = smem + L.w;
     float *red = reinterpret_cast<float *>(smem + L.red);
 
@@ -111,6 +84,7 @@ __global__ void __launch_bounds__(kGuWarps * 32) gateup_kernel(GuArgs a) {
         mbar_init(&bars[1], 1);
         fence_barrier_init();
     }
+    if (threadIdx.x < 32) zrec[threadIdx.x >> 1] = make_uint2(0u, 0u);
     __syncthreads();
 
     pdl_wait();                       // router (slots, x records) and the producer of x are done
@@ -134,15 +108,23 @@ __global__ void __launch_bounds__(kGuWarps * 32) gateup_kernel(GuArgs a) {
             mbar_arrive_expect_tx(&bars[0], (uint32_t)H * 2);
             tma_load_1d(xraw, a.x + (size_t)tok * H, (uint32_t)H * 2, &bars[0]);
         } else {
-            const uint32_t rb = (uint32_t)ng * 128, cbz = (uint32_t)pad4(ng) * 4;
-            mbar_arrive_expect_tx(&bars[0], rb + 2 * cbz);
-            tma_load_1d(xfrag, a.xrec + (size_t)tok * ng * 16, rb, &bars[0]);
-            tma_load_1d(corr, a.xcorr + (size_t)tok * pad4(ng), cbz, &bars[0]);
-            tma_load_1d(xsum, a.xsum + (size_t)tok * pad4(ng), cbz, &bars[0]);
+            const uint32_t rb = (uint32_t)ng * 128, fb = (uint32_t)pad4(ng) * 4;
+            mbar_arrive_expect_tx(&bars[0], rb + 2 * fb);
+            tma_load_1d(xrec, a.xrec + (size_t)tok * ng * 16, rb, &bars[0]);
+            tma_load_1d(xscale, a.xscale + (size_t)tok * pad4(ng), fb, &bars[0]);
+            tma_load_1d(xsum, a.xsum + (size_t)tok * pad4(ng), fb, &bars[0]);
         }
     }
     const bool xok = mbar_wait(&bars[0], 0);
-    if (self_stage && xok) build_bfrag_smem(xraw, ng, xfrag, corr, xsum);
+    if (self_stage) {
+        // records of x from the raw copy: one aligned half warp per group
+        for (int G0 = 0; G0 < ng; G0 += blockDim.x / 16) {
+            const int G = G0 + (threadIdx.x >> 4);
+            const bool v = xok && G < ng;
+            build_rec_group(xraw + (size_t)(v ? G : 0) * 64, v, threadIdx.x & 15, xrec + (size_t)G * 16,
+                            xscale + G, xsum + G);
+        }
+    }
     __syncthreads();
     const bool wok = sok && xok && mbar_wait(&bars[1], 0);
 
@@ -154,37 +136,35 @@ __global__ void __launch_bounds__(kGuWarps * 32) gateup_kernel(GuArgs a) {
         const uint4 *urow = reinterpret_cast<const uint4 *>(wsm + cb + (size_t)g * rowb);
         const int nsteps = (ng + 3) >> 2;
         const int s0 = (warp * nsteps) / kGuWarps, s1 = ((warp + 1) * nsteps) / kGuWarps;
-        const bool bl = (g == t);
+        const bool bact = rec_lane_active(lane);
+        const int part = rec_lane_part(lane);
         for (int j = s0; j < s1; ++j) {
             const int G = 4 * j + t;
             const bool gok = G < ng;
             const uint4 wv = gok ? grow[G] : make_uint4(0, 0, 0, 0);
             const uint4 uv = gok ? urow[G] : make_uint4(0, 0, 0, 0);
-            float d[4];
-            mma_step(wv, uv, xfrag + (size_t)G * 16, bl && gok, d);
-            if (t < 2) {
-#pragma unroll
-                for (int c = 0; c < 2; ++c) {
-                    const int G2 = 4 * j + 2 * t + c;
-                    if (G2 < ng) {
-                        const int si = g * ng + G2;
-                        accg += sb_to_f32<kFp16>(sgs[si]) * (d[c] - corr[G2]) + sb_to_f32<kFp16>(bgs[si]) * xsum[G2];
-                        accu += sb_to_f32<kFp16>(sus[si]) * (d[2 + c] - corr[G2]) + sb_to_f32<kFp16>(bus[si]) * xsum[G2];
-                    }
-                }
+            const uint2 *rec = (bact && gok) ? xrec + (size_t)G * 16 : zrec;
+            int dg, du;
+            mma_step_i8(wv, uv, rec, part, dg, du);
+            if (gok) {
+                const int si = g * ng + G;
+                const float sc = xscale[G], sm = xsum[G];
+                accg += sb_to_f32<kFp16>(sgs[si]) * ((float)dg * sc) + sb_to_f32<kFp16>(bgs[si]) * sm;
+                accu += sb_to_f32<kFp16>(sus[si]) * ((float)du * sc) + sb_to_f32<kFp16>(bus[si]) * sm;
             }
         }
     }
     accg += __shfl_xor_sync(0xffffffffu, accg, 1);
     accu += __shfl_xor_sync(0xffffffffu, accu, 1);
+    accg += __shfl_xor_sync(0xffffffffu, accg, 2);
+    accu += __shfl_xor_sync(0xffffffffu, accu, 2);
     if (t == 0) {
         red[(warp * 8 + g) * 2 + 0] = accg;
         red[(warp * 8 + g) * 2 + 1] = accu;
     }
     __syncthreads();
     if (warp == 0) {
-        float av = 0.f, scaled = 0.f;
-        const int p = r0 + lane;            // activation index inside I (lanes 0..7)
+        const int p = r0 + (lane & 7);
         if (lane < 8) {
             float sgsum = 0.f, susum = 0.f;
 #pragma unroll
@@ -195,30 +175,29 @@ __global__ void __launch_bounds__(kGuWarps * 32) gateup_kernel(GuArgs a) {
             const float gv = bf16r(sgsum), uv = bf16r(susum);
             // SwiGLU rounded after every op, like an MLX bf16 graph
             const float sig = bf16r(1.0f / (1.0f + expf(-gv)));
-            av = wok ? bf16r(bf16r(gv * sig) * uv) : 0.f;
+            const float av = wok ? bf16r(bf16r(gv * sig) * uv) : 0.f;
             a.act[((size_t)tok * K + k) * I + p] = f32_to_bf16_bits(av);
-            if (a.arec) {
-                // scatter into the B record of the down kernel (layout of build_bfrag_smem)
-                const int ngI = I >> 6, G = p >> 6, o = p & 63, m = o >> 4, q = o & 15;
-                const int mi = (q & 7) >> 1;
-                scaled = av * pair_inv_scale(q & 7);
-                const size_t ent = (((size_t)tok * K + k) * ngI + G) * 16 + m * 4 + mi;
-                uint16_t *half = reinterpret_cast<uint16_t *>(a.arec + ent) + (q & 1) * 2 + (q >= 8 ? 1 : 0);
-                *half = f32_to_bf16_bits(scaled);
-            }
         }
         if (a.arec) {
-            float cs = scaled, xs = av;
-#pragma unroll
-            for (int off = 4; off > 0; off >>= 1) {
-                cs += __shfl_xor_sync(0xffffffffu, cs, off);
-                xs += __shfl_xor_sync(0xffffffffu, xs, off);
-            }
-            if (lane == 0) {
-                const int ngI = I >> 6, G = r0 >> 6, rbg = (r0 & 63) >> 3;
-                float *pp = a.apart + ((((size_t)tok * K + k) * ngI + G) * 8 + rbg) * 2;
-                pp[0] = cs;
-                pp[1] = xs;
+            // the last of the 8 CTAs of this 64-wide group builds its record
+            const int ngI = I >> 6, G = r0 >> 6;
+            const size_t gi = ((size_t)tok * K + k) * ngI + G;
+            unsigned int last = 0;
+            __threadfence();
+            __syncwarp();
+            if (lane == 0) last = (atomicAdd(a.acnt + gi, 1u) == 7u) ? 1u : 0u;
+            last = __shfl_sync(0xffffffffu, last, 0);
+            if (last) {
+                __threadfence();
+                const uint16_t *src = a.act + ((size_t)tok * K + k) * I + (size_t)G * 64;
+                // read the group through L2 (other CTAs wrote it) into registers, then build
+                __shared__ __align__(16) uint16_t grp[64];
+                const uint32_t two = __ldcg(reinterpret_cast<const unsigned int *>(src) + lane);
+                reinterpret_cast<uint32_t *>(grp)[lane] = two;
+                __syncwarp();
+                const size_t fo = (size_t)tok * pad4(K * ngI) + (size_t)k * ngI + G;
+                build_rec_group(grp, lane < 16, lane & 15, a.arec + gi * 16, a.ascale + fo, a.asum + fo);
+                if (lane == 0) a.acnt[gi] = 0u;
             }
         }
     }
@@ -228,8 +207,8 @@ __global__ void __launch_bounds__(kGuWarps * 32) gateup_kernel(GuArgs a) {
 
 struct DnArgs {
     const uint16_t *act;
-    const uint2 *arec;          // optional records of act (from the gate/up kernel)
-    const float *apart;         // [T][K][ngI][8][2]
+    const uint2 *arec;           // optional records of act (from the gate/up kernel)
+    const float *ascale, *asum;  // [T][pad4(K*ngI)]
     const uint32_t *slots;
     const uint16_t *scores;
     const uint32_t *wd;
@@ -240,15 +219,15 @@ struct DnArgs {
 };
 
 struct DnLayout {
-    size_t araw, afrag, apart, corr, xsum, yks, warps, warp_bytes, total;
+    size_t araw, rec, scale, sum, zero, yks, warps, warp_bytes, total;
     MOE_HD DnLayout(int I, int K, bool self_stage) {
         const int ng = I / 64;
         araw = 256;                                   // after K+1 mbarriers (K <= 16)
-        afrag = araw + (self_stage ? al16((size_t)K * I * 2) : 0);
-        apart = afrag + (size_t)K * ng * 128;
-        corr = apart + (self_stage ? 0 : (size_t)K * ng * 64);
-        xsum = corr + al16((size_t)K * ng * 4);
-        yks = xsum + al16((size_t)K * ng * 4);
+        rec = araw + (self_stage ? al16((size_t)K * I * 2) : 0);
+        scale = rec + (size_t)K * ng * 128;
+        sum = scale + al16((size_t)pad4(K * ng) * 4);
+        zero = sum + al16((size_t)pad4(K * ng) * 4);
+        yks = zero + 128;
         warps = al128(yks + (size_t)K * 16 * 4);
         warp_bytes = al128(16 * (size_t)(I / 4) + 2 * 16 * (size_t)ng * 2);
         total = warps + (size_t)K * warp_bytes;
@@ -264,10 +243,10 @@ __global__ void __launch_bounds__(kMaxK * 32) down_kernel(DnArgs a) {
     const DnLayout L(I, K, self_stage);
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem);
     uint16_t *araw = reinterpret_cast<uint16_t *>(smem + L.araw);
-    uint2 *afrag = reinterpret_cast<uint2 *>(smem + L.afrag);
-    float *apart = reinterpret_cast<float *>(smem + L.apart);
-    float *corr = reinterpret_cast<float *>(smem + L.corr);
-    float *xsum = reinterpret_cast<float *>(smem + L.xsum);
+    uint2 *arec = reinterpret_cast<uint2 *>(smem + L.rec);
+    float *ascale = reinterpret_cast<float *>(smem + L.scale);
+    float *asum = reinterpret_cast<float *>(smem + L.sum);
+    uint2 *zrec = reinterpret_cast<uint2 *>(smem + L.zero);
     float *yks = reinterpret_cast<float *>(smem + L.yks);
 
     const int lane = threadIdx.x & 31, k = threadIdx.x >> 5;
@@ -280,6 +259,7 @@ __global__ void __launch_bounds__(kMaxK * 32) down_kernel(DnArgs a) {
         for (int i = 0; i <= K; ++i) mbar_init(&bars[i], 1);
         fence_barrier_init();
     }
+    if (threadIdx.x < 32) zrec[threadIdx.x >> 1] = make_uint2(0u, 0u);
     __syncthreads();
 
     // The routing (slots) was produced two kernels back and is complete once the gate/up
@@ -305,27 +285,20 @@ __global__ void __launch_bounds__(kMaxK * 32) down_kernel(DnArgs a) {
             mbar_arrive_expect_tx(&bars[0], ab);
             tma_load_1d(araw, a.act + (size_t)tok * K * I, ab, &bars[0]);
         } else {
-            const uint32_t rb = (uint32_t)K * ng * 128, pb = (uint32_t)K * ng * 64;
-            mbar_arrive_expect_tx(&bars[0], rb + pb);
-            tma_load_1d(afrag, a.arec + (size_t)tok * K * ng * 16, rb, &bars[0]);
-            tma_load_1d(apart, a.apart + (size_t)tok * K * ng * 16, pb, &bars[0]);
+            const uint32_t rb = (uint32_t)K * ng * 128, fb = (uint32_t)pad4(K * ng) * 4;
+            mbar_arrive_expect_tx(&bars[0], rb + 2 * fb);
+            tma_load_1d(arec, a.arec + (size_t)tok * K * ng * 16, rb, &bars[0]);
+            tma_load_1d(ascale, a.ascale + (size_t)tok * pad4(K * ng), fb, &bars[0]);
+            tma_load_1d(asum, a.asum + (size_t)tok * pad4(K * ng), fb, &bars[0]);
         }
     }
     const bool aok = mbar_wait(&bars[0], 0);
-    if (aok) {
-        if (self_stage) {
-            build_bfrag_smem(araw, K * ng, afrag, corr, xsum);   // K vectors back to back
-        } else {
-            for (int i = threadIdx.x; i < K * ng; i += blockDim.x) {   // fixed-order sum of 8 partials
-                float cs = 0.f, xs = 0.f;
-#pragma unroll
-                for (int r = 0; r < 8; ++r) {
-                    cs += apart[(i * 8 + r) * 2 + 0];
-                    xs += apart[(i * 8 + r) * 2 + 1];
-                }
-                corr[i] = cs;
-                xsum[i] = xs;
-            }
+    if (self_stage) {
+        for (int G0 = 0; G0 < K * ng; G0 += blockDim.x / 16) {     // K vectors back to back
+            const int G = G0 + (threadIdx.x >> 4);
+            const bool v = aok && G < K * ng;
+            build_rec_group(araw + (size_t)(v ? G : 0) * 64, v, threadIdx.x & 15, arec + (size_t)G * 16,
+                            ascale + G, asum + G);
         }
     }
     __syncthreads();
@@ -335,34 +308,33 @@ __global__ void __launch_bounds__(kMaxK * 32) down_kernel(DnArgs a) {
     const uint16_t *bds = sds + 16 * ng;
     float acca = 0.f, accb = 0.f;
     if (wok) {
-        const uint2 *xf0 = afrag + (size_t)k * ng * 16;
-        const float *ck = corr + k * ng, *xk = xsum + k * ng;
+        const uint2 *rk = arec + (size_t)k * ng * 16;
+        const float *sck = ascale + k * ng, *smk = asum + k * ng;
         const uint4 *rowa = reinterpret_cast<const uint4 *>(my + (size_t)g * rowb);
         const uint4 *rowbp = reinterpret_cast<const uint4 *>(my + (size_t)(g + 8) * rowb);
         const int nsteps = (ng + 3) >> 2;
-        const bool bl = (g == t);
+        const bool bact = rec_lane_active(lane);
+        const int part = rec_lane_part(lane);
         for (int j = 0; j < nsteps; ++j) {
             const int G = 4 * j + t;
             const bool gok = G < ng;
             const uint4 qa = gok ? rowa[G] : make_uint4(0, 0, 0, 0);
             const uint4 qb = gok ? rowbp[G] : make_uint4(0, 0, 0, 0);
-            float d[4];
-            mma_step(qa, qb, xf0 + (size_t)G * 16, bl && gok, d);
-            if (t < 2) {
-#pragma unroll
-                for (int c = 0; c < 2; ++c) {
-                    const int G2 = 4 * j + 2 * t + c;
-                    if (G2 < ng) {
-                        const int sa = g * ng + G2, sbi = (g + 8) * ng + G2;
-                        acca += sb_to_f32<kFp16>(sds[sa]) * (d[c] - ck[G2]) + sb_to_f32<kFp16>(bds[sa]) * xk[G2];
-                        accb += sb_to_f32<kFp16>(sds[sbi]) * (d[2 + c] - ck[G2]) + sb_to_f32<kFp16>(bds[sbi]) * xk[G2];
-                    }
-                }
+            const uint2 *rec = (bact && gok) ? rk + (size_t)G * 16 : zrec;
+            int da, db;
+            mma_step_i8(qa, qb, rec, part, da, db);
+            if (gok) {
+                const int sa = g * ng + G, sbi = (g + 8) * ng + G;
+                const float sc = sck[G], sm = smk[G];
+                acca += sb_to_f32<kFp16>(sds[sa]) * ((float)da * sc) + sb_to_f32<kFp16>(bds[sa]) * sm;
+                accb += sb_to_f32<kFp16>(sds[sbi]) * ((float)db * sc) + sb_to_f32<kFp16>(bds[sbi]) * sm;
             }
         }
     }
     acca += __shfl_xor_sync(0xffffffffu, acca, 1);
     accb += __shfl_xor_sync(0xffffffffu, accb, 1);
+    acca += __shfl_xor_sync(0xffffffffu, acca, 2);
+    accb += __shfl_xor_sync(0xffffffffu, accb, 2);
     if (t == 0) {
         const float ya = wok ? bf16r(acca) : 0.f, yb = wok ? bf16r(accb) : 0.f;
         yks[k * 16 + g] = ya;
@@ -402,27 +374,28 @@ bool misaligned(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15) !=
 
 __device__ unsigned int g_moe_device_error = 0;
 
-int moe_experts_gateup_ex(const void *x, const void *xrec, const float *xcorr, const float *xsum, int T,
+int moe_experts_gateup_ex(const void *x, const void *xrec, const float *xscale, const float *xsum, int T,
                           int H, int I, int K, int cap, const uint32_t *slots, const uint32_t *wg,
                           const void *sg, const void *bg, const uint32_t *wu, const void *su, const void *bu,
-                          int bits, int group_size, int sb_fp16, void *act, void *arec, float *apart,
-                          void *stream) {
+                          int bits, int group_size, int sb_fp16, void *act, void *arec, float *ascale,
+                          float *asum, unsigned int *acnt, void *stream) {
     int rc = check_common(H, I, K, T, cap, bits, group_size, "experts_gateup");
     if (rc) return rc;
     if (!x || !slots || !wg || !wu || !sg || !bg || !su || !bu || !act)
         return moe_set_error(MOE_EINVAL, "experts_gateup: null pointer");
     if (misaligned(x) || misaligned(wg) || misaligned(wu) || misaligned(sg) || misaligned(bg) ||
-        misaligned(su) || misaligned(bu) || misaligned(xrec) || misaligned(xcorr) || misaligned(xsum))
+        misaligned(su) || misaligned(bu) || misaligned(xrec) || misaligned(xscale) || misaligned(xsum))
         return moe_set_error(MOE_EINVAL, "experts_gateup: tensors must be 16-byte aligned");
-    if ((xrec != nullptr) != (xcorr != nullptr) || (xrec != nullptr) != (xsum != nullptr) ||
-        (arec != nullptr) != (apart != nullptr))
+    if ((xrec != nullptr) != (xscale != nullptr) || (xrec != nullptr) != (xsum != nullptr) ||
+        (arec != nullptr) != (ascale != nullptr) || (arec != nullptr) != (asum != nullptr) ||
+        (arec != nullptr) != (acnt != nullptr))
         return moe_set_error(MOE_EINVAL, "experts_gateup: incomplete record buffers");
     const GuLayout L(H, xrec == nullptr);
     if (L.total > 227 * 1024) return moe_set_error(MOE_EINVAL, "experts_gateup: H=%d too large", H);
-    GuArgs a{static_cast<const uint16_t *>(x), static_cast<const uint2 *>(xrec), xcorr, xsum, slots, wg, wu,
+    GuArgs a{static_cast<const uint16_t *>(x), static_cast<const uint2 *>(xrec), xscale, xsum, slots, wg, wu,
              static_cast<const uint16_t *>(sg), static_cast<const uint16_t *>(bg),
              static_cast<const uint16_t *>(su), static_cast<const uint16_t *>(bu), H, I, K, cap,
-             static_cast<uint16_t *>(act), static_cast<uint2 *>(arec), apart};
+             static_cast<uint16_t *>(act), static_cast<uint2 *>(arec), ascale, asum, acnt};
     dim3 grid(I / 8, K, T);
     cudaError_t e = sb_fp16 ? launch_pdl(gateup_kernel<true>, grid, dim3(kGuWarps * 32), L.total, as_stream(stream), a)
                             : launch_pdl(gateup_kernel<false>, grid, dim3(kGuWarps * 32), L.total, as_stream(stream), a);
@@ -430,8 +403,8 @@ int moe_experts_gateup_ex(const void *x, const void *xrec, const float *xcorr, c
     return MOE_OK;
 }
 
-int moe_experts_down_ex(const void *act, const void *arec, const float *apart, int T, int H, int I, int K,
-                        int cap, const uint32_t *slots, const void *scores, const uint32_t *wd,
+int moe_experts_down_ex(const void *act, const void *arec, const float *ascale, const float *asum, int T, int H,
+                        int I, int K, int cap, const uint32_t *slots, const void *scores, const uint32_t *wd,
                         const void *sd, const void *bd, int bits, int group_size, int sb_fp16,
                         const void *addend, const void *resid, void *y, void *yk, void *stream) {
     int rc = check_common(H, I, K, T, cap, bits, group_size, "experts_down");
@@ -439,13 +412,14 @@ int moe_experts_down_ex(const void *act, const void *arec, const float *apart, i
     if (!act || !slots || !wd || !sd || !bd) return moe_set_error(MOE_EINVAL, "experts_down: null pointer");
     if (y && !scores) return moe_set_error(MOE_EINVAL, "experts_down: y needs scores");
     if (!y && !yk) return moe_set_error(MOE_EINVAL, "experts_down: no output requested");
-    if ((arec != nullptr) != (apart != nullptr))
+    if ((arec != nullptr) != (ascale != nullptr) || (arec != nullptr) != (asum != nullptr))
         return moe_set_error(MOE_EINVAL, "experts_down: incomplete record buffers");
-    if (misaligned(act) || misaligned(wd) || misaligned(sd) || misaligned(bd) || misaligned(arec) || misaligned(apart))
+    if (misaligned(act) || misaligned(wd) || misaligned(sd) || misaligned(bd) || misaligned(arec) ||
+        misaligned(ascale) || misaligned(asum))
         return moe_set_error(MOE_EINVAL, "experts_down: tensors must be 16-byte aligned");
     const DnLayout L(I, K, arec == nullptr);
     if (L.total > 227 * 1024) return moe_set_error(MOE_EINVAL, "experts_down: K*I too large");
-    DnArgs a{static_cast<const uint16_t *>(act), static_cast<const uint2 *>(arec), apart, slots,
+    DnArgs a{static_cast<const uint16_t *>(act), static_cast<const uint2 *>(arec), ascale, asum, slots,
              static_cast<const uint16_t *>(scores), wd, static_cast<const uint16_t *>(sd),
              static_cast<const uint16_t *>(bd), H, I, K, cap, static_cast<const uint16_t *>(addend),
              static_cast<const uint16_t *>(resid), static_cast<uint16_t *>(y), static_cast<uint16_t *>(yk)};
@@ -461,7 +435,7 @@ extern "C" int moe_experts_gateup(const void *x, int T, int H, int I, int K, int
                                   const uint32_t *wu, const void *su, const void *bu, int bits,
                                   int group_size, int sb_fp16, void *act, void *stream) {
     return moe_experts_gateup_ex(x, nullptr, nullptr, nullptr, T, H, I, K, cap, slots, wg, sg, bg, wu, su, bu,
-                                 bits, group_size, sb_fp16, act, nullptr, nullptr, stream);
+                                 bits, group_size, sb_fp16, act, nullptr, nullptr, nullptr, nullptr, stream);
 }
 
 extern "C" int moe_experts_down(const void *act, int T, int H, int I, int K, int cap, const uint32_t *slots,
@@ -469,7 +443,7 @@ extern "C" int moe_experts_down(const void *act, int T, int H, int I, int K, int
                                 const void *bd, int bits, int group_size, int sb_fp16,
                                 const void *addend, const void *resid, void *y, void *yk,
                                 void *stream) {
-    return moe_experts_down_ex(act, nullptr, nullptr, T, H, I, K, cap, slots, scores, wd, sd, bd, bits,
+    return moe_experts_down_ex(act, nullptr, nullptr, nullptr, T, H, I, K, cap, slots, scores, wd, sd, bd, bits,
                                group_size, sb_fp16, addend, resid, y, yk, stream);
 }
 

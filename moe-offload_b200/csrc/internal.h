@@ -10,15 +10,15 @@ int moe_router_launch(const void *x, int T, int H, int E, int K, const void *w,
                       int M, const float *pred_bias, void *out_logits, void *out_probs,
                       uint32_t *out_inds, void *out_scores, uint32_t *out_pred,
                       unsigned int *tickets, uint16_t *logits_buf, uint16_t *plogits_buf,
-                      void *xrec, float *xcorr, float *xsum, void *stream);
+                      void *xrec, float *xscale, float *xsum, int norm, void *stream);
 
-int moe_experts_gateup_ex(const void *x, const void *xrec, const float *xcorr, const float *xsum, int T,
+int moe_experts_gateup_ex(const void *x, const void *xrec, const float *xscale, const float *xsum, int T,
                           int H, int I, int K, int cap, const uint32_t *slots, const uint32_t *wg,
                           const void *sg, const void *bg, const uint32_t *wu, const void *su, const void *bu,
-                          int bits, int group_size, int sb_fp16, void *act, void *arec, float *apart,
-                          void *stream);
+                          int bits, int group_size, int sb_fp16, void *act, void *arec, float *ascale,
+                          float *asum, unsigned int *acnt, void *stream);
 
-int moe_experts_down_ex(const void *act, const void *arec, const float *apart, int T, int H, int I, int K,
-                        int cap, const uint32_t *slots, const void *scores, const uint32_t *wd,
+int moe_experts_down_ex(const void *act, const void *arec, const float *ascale, const float *asum, int T, int H,
+                        int I, int K, int cap, const uint32_t *slots, const void *scores, const uint32_t *wd,
                         const void *sd, const void *bd, int bits, int group_size, int sb_fp16,
                         const void *addend, const void *resid, void *y, void *yk, void *stream);

@@ -79,5 +79,5 @@ extern "C" int moe_router_topk_noalloc(const void *x, int T, int H, int E, int K
     if (e != cudaSuccess) return moe_set_cuda_error(e);
     return moe_router_launch(x, T, H, E, K, w, w_scales, w_biases, rbits, group_size, sb_fp16, wn, wn_scales,
                              wn_biases, M, pred_bias, out_logits, out_probs, out_inds, out_scores, out_pred,
-                             tickets, logits, M > 0 ? plogits : nullptr, nullptr, nullptr, nullptr, stream);
+                             tickets, logits, M > 0 ? plogits : nullptr, nullptr, nullptr, nullptr, 0, stream);
 }

@@ -11,6 +11,8 @@
 // Reference semantics: mlx-qwen38/loader.py:903-908 (router), loader.py:237-242
 // (topk_sorted_indices); cpp/src/layers.cpp:311-341.
 #include "common.cuh"
+#include "gemv_i8.cuh"
+#include "topk.cuh"
 
 namespace {
 
@@ -33,8 +35,9 @@ struct RouterArgs {
     uint16_t *scores;     // [T, K]
     uint32_t *pred;       // [T, M] or null
     unsigned int *tickets;  // [T], zero between launches
-    uint2 *xrec;          // [T, H/64, 16] MMA B records of x, or null (see build_bfrag_smem)
-    float *xcorr, *xsum;  // [T, pad4(H/64)] each
+    uint2 *xrec;          // [T, H/64, 16] int8 MMA records of x (gemv_i8.cuh), or null
+    float *xscale, *xsum; // [T, pad4(H/64)] each
+    int norm;             // 1: the router input is x * 2^-k (pow2_rms_shift of x), else x
 };
 
 // ---------------------------------------------------------------- row dot products
@@ -112,59 +115,6 @@ MOE_D uint32_t bf16_order_key(uint16_t v) {
     return (v & 0x8000) ? (uint32_t)(~v & 0xffff) : (uint32_t)(v | 0x8000);
 }
 
-// Selects the n largest of keys[0..E) (all distinct, all > 0) with warp 0, results in
-// descending order. Each lane keeps its local maximum; only the winning lane rescans. Keys
-// live in registers when E <= 512 and are rescanned from shared memory otherwise.
-constexpr int kRegKeys = 16;
-
-MOE_D void warp_select_desc(const uint32_t *keys, int E, int n, uint32_t *out) {
-    const int lane = threadIdx.x & 31;
-    if (E <= 32 * kRegKeys) {
-        uint32_t kv[kRegKeys];
-        uint32_t lmax = 0;
-#pragma unroll
-        for (int j = 0; j < kRegKeys; ++j) {
-            const int e = lane + 32 * j;
-            kv[j] = (e < E) ? keys[e] : 0u;
-            lmax = max(lmax, kv[j]);
-        }
-        for (int r = 0; r < n; ++r) {
-            const uint32_t win = __reduce_max_sync(0xffffffffu, lmax);
-            if (lmax == win) {
-                uint32_t nm = 0;
-#pragma unroll
-                for (int j = 0; j < kRegKeys; ++j) {
-                    kv[j] = (kv[j] == win) ? 0u : kv[j];
-                    nm = max(nm, kv[j]);
-                }
-                lmax = nm;
-            }
-            if (lane == 0) out[r] = win;
-        }
-    } else {
-        __shared__ uint32_t taken[64];
-        uint32_t lmax = 0;
-        for (int e = lane; e < E; e += 32) lmax = max(lmax, keys[e]);
-        for (int r = 0; r < n; ++r) {
-            const uint32_t win = __reduce_max_sync(0xffffffffu, lmax);
-            if (lane == 0) taken[r] = win;
-            __syncwarp();
-            if (lmax == win) {
-                uint32_t nm = 0;
-                for (int e = lane; e < E; e += 32) {
-                    const uint32_t kv = keys[e];
-                    bool used = false;
-                    for (int q = 0; q <= r; ++q) used |= (kv == taken[q]);
-                    if (!used) nm = max(nm, kv);
-                }
-                lmax = nm;
-            }
-            if (lane == 0) out[r] = win;
-        }
-    }
-    __syncwarp();
-}
-
 template <bool kFp16, int kRbits>
 __global__ void __launch_bounds__(kThreads) router_kernel(RouterArgs a) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -185,33 +135,33 @@ __global__ void __launch_bounds__(kThreads) router_kernel(RouterArgs a) {
     pdl_wait();                                   // x is complete
     pdl_launch_dependents();
 
+    // optional power-of-two RMS normalisation of the layer input (exact rescale)
+    double xmul = 1.0;
+    if (a.norm) {
+        __shared__ double s_ss[kWarps];
+        double ss = 0.0;
+        for (int i = threadIdx.x; i < a.H; i += kThreads) {
+            const double v = (double)bf16_bits_to_f32(x[i]);
+            ss = fma(v, v, ss);
+        }
+        ss = warp_sum_d(ss);
+        if (lane == 0) s_ss[warp] = ss;
+        __syncthreads();
+        ss = 0.0;
+#pragma unroll
+        for (int i = 0; i < kWarps; ++i) ss += s_ss[i];
+        xmul = ldexp(1.0, -pow2_rms_shift(ss, a.H));
+    }
+
     if (a.xrec) {
-        // MMA B records of x for the expert kernels: 16 threads per 64-wide group
+        // int8 MMA records of x for the expert kernels (gemv_i8.cuh): 16 threads per group
         const int ng = a.H >> 6;
         for (int G0 = blockIdx.x * (kThreads / 16); G0 < ng; G0 += gridDim.x * (kThreads / 16)) {
-            const int G = G0 + (threadIdx.x >> 4), ent = threadIdx.x & 15;
-            float cs = 0.f, xs = 0.f;
-            if (G < ng) {
-                const int m = ent >> 2, mi = ent & 3, c0 = G * 64 + 16 * m + 2 * mi;
-                const uint32_t p01 = __ldg(reinterpret_cast<const uint32_t *>(x + c0));
-                const uint32_t p89 = __ldg(reinterpret_cast<const uint32_t *>(x + c0 + 8));
-                const float v0 = __uint_as_float(p01 << 16), v2 = __uint_as_float(p01 & 0xffff0000u);
-                const float v1 = __uint_as_float(p89 << 16), v3 = __uint_as_float(p89 & 0xffff0000u);
-                const float i0 = pair_inv_scale(2 * mi), i1 = pair_inv_scale(2 * mi + 1);
-                const float s0 = v0 * i0, s1 = v1 * i0, s2 = v2 * i1, s3 = v3 * i1;
-                a.xrec[((size_t)t * ng + G) * 16 + ent] = make_uint2(pack_bf16x2(s0, s1), pack_bf16x2(s2, s3));
-                cs = (s0 + s1) + (s2 + s3);
-                xs = (v0 + v1) + (v2 + v3);
-            }
-#pragma unroll
-            for (int off = 8; off > 0; off >>= 1) {
-                cs += __shfl_xor_sync(0xffffffffu, cs, off);
-                xs += __shfl_xor_sync(0xffffffffu, xs, off);
-            }
-            if (G < ng && ent == 0) {
-                a.xcorr[(size_t)t * pad4(ng) + G] = cs;
-                a.xsum[(size_t)t * pad4(ng) + G] = xs;
-            }
+            const int G = G0 + (threadIdx.x >> 4);
+            const bool v = G < ng;
+            const size_t fo = (size_t)t * pad4(ng) + G;
+            build_rec_group(x + (size_t)(v ? G : 0) * 64, v, threadIdx.x & 15, a.xrec + ((size_t)t * ng + G) * 16,
+                            a.xscale + fo, a.xsum + fo, (float)xmul);
         }
     }
 
@@ -227,7 +177,7 @@ __global__ void __launch_bounds__(kThreads) router_kernel(RouterArgs a) {
             const uint16_t *b = (next ? a.wnb : a.wb) + (size_t)e * ng;
             acc = row_dot_affine<kFp16>(x, w, s, b, a.H, kRbits, a.gs, lane);
         }
-        acc = warp_sum_d(acc);
+        acc = warp_sum_d(acc) * xmul;
         if (lane == 0) {
             uint16_t l = f64_to_bf16_bits(acc);
             if (next) {
@@ -373,7 +323,7 @@ int moe_router_launch(const void *x, int T, int H, int E, int K, const void *w,
                       int M, const float *pred_bias, void *out_logits, void *out_probs,
                       uint32_t *out_inds, void *out_scores, uint32_t *out_pred,
                       unsigned int *tickets, uint16_t *logits_buf, uint16_t *plogits_buf,
-                      void *xrec, float *xcorr, float *xsum, void *stream) {
+                      void *xrec, float *xscale, float *xsum, int norm, void *stream) {
     if (!x || !w || !out_inds || !out_scores || !tickets)
         return moe_set_error(MOE_EINVAL, "router: null required pointer");
     if (T <= 0 || H <= 0 || E <= 0 || E > kMaxE || K <= 0 || K > E || K > 64)
@@ -407,10 +357,11 @@ int moe_router_launch(const void *x, int T, int H, int E, int K, const void *w,
     a.pred = out_pred;
     a.tickets = tickets;
     a.xrec = static_cast<uint2 *>(xrec);
-    a.xcorr = xcorr;
+    a.xscale = xscale;
     a.xsum = xsum;
-    if (xrec && (H % 64 || !xcorr || !xsum))
-        return moe_set_error(MOE_EINVAL, "router: x records need H %% 64 == 0 and corr/sum buffers");
+    a.norm = norm;
+    if (xrec && (H % 64 || !xscale || !xsum))
+        return moe_set_error(MOE_EINVAL, "router: x records need H %% 64 == 0 and scale/sum buffers");
     if (!a.logits || (M > 0 && !a.plogits))
         return moe_set_error(MOE_EINVAL, "router: missing logit scratch");
     cudaError_t e = sb_fp16 ? launch_router<true>(a, rbits, as_stream(stream))
@@ -439,6 +390,6 @@ extern "C" int moe_router_topk(const void *x, int T, int H, int E, int K, const 
     uint16_t *plogits = M > 0 ? reinterpret_cast<uint16_t *>(ws) : nullptr;
     return moe_router_launch(x, T, H, E, K, w, w_scales, w_biases, rbits, group_size, sb_fp16, wn,
                              wn_scales, wn_biases, M, pred_bias, out_logits, out_probs, out_inds,
-                             out_scores, out_pred, tickets, logits, plogits, nullptr, nullptr, nullptr,
+                             out_scores, out_pred, tickets, logits, plogits, nullptr, nullptr, nullptr, 0,
                              stream);
 }

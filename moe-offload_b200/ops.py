@@ -191,8 +191,10 @@ def decode_workspace(device, T: int, H: int, I: int, E: int, K: int, M: int) -> 
 
 def decode_layer(x: torch.Tensor, router: torch.Tensor, gate: QMatrix, up: QMatrix, down: QMatrix,
                  K: int, *, router_next=None, M: int = 0, pred_bias=None, addend=None, resid=None,
-                 out: dict | None = None, workspace: torch.Tensor | None = None, stream=None) -> dict:
+                 norm: bool = False, out: dict | None = None, workspace: torch.Tensor | None = None,
+                 stream=None) -> dict:
     """One decode step of an all-resident layer: router -> experts -> combine (three kernels).
+    norm=True feeds the MoE block x * 2^-k (power of two nearest x's RMS; see the C header).
     Returns dict(y, inds, scores[, pred])."""
     _need(x, "x", (torch.bfloat16,))
     dev = x.device
@@ -213,6 +215,30 @@ def decode_layer(x: torch.Tensor, router: torch.Tensor, gate: QMatrix, up: QMatr
     call("moe_decode_layer", x.data_ptr(), T, H, I, E, K, router.data_ptr(), _ptr(router_next if M else None),
          M, _ptr(pred_bias), gate.w.data_ptr(), gate.s.data_ptr(), gate.b.data_ptr(), up.w.data_ptr(),
          up.s.data_ptr(), up.b.data_ptr(), down.w.data_ptr(), down.s.data_ptr(), down.b.data_ptr(),
-         gate.sb_fp16, _ptr(addend), _ptr(resid), o["inds"].data_ptr(), o["scores"].data_ptr(),
+         gate.sb_fp16, int(norm), _ptr(addend), _ptr(resid), o["inds"].data_ptr(), o["scores"].data_ptr(),
          _ptr(o.get("pred")), o["y"].data_ptr(), ws.data_ptr(), ws.numel(), _stream(stream))
     return o
+
+
+# ----------------------------------------------------------------------------- host helpers
+
+def pow2_rms_shift(h_bits) -> int:
+    """k such that h * 2^-k has RMS in [2^-0.5, 2^0.5): k = floor(e / 2) with mean(h^2) in
+    [2^(e-1), 2^e) (the rule the kernels apply for norm=True). h_bits: bf16 bit patterns."""
+    import numpy as np
+
+    v = (np.asarray(h_bits, dtype=np.uint16).astype(np.uint32) << 16).view(np.float32).astype(np.float64)
+    ss = float(np.sum(v * v))
+    if not ss > 0.0:
+        return 0
+    _, e = np.frexp(ss / v.size)
+    return int(e) // 2
+
+
+def pow2_normalize(h_bits):
+    """bf16 bits of h * 2^-k (exact) for k = pow2_rms_shift(h)."""
+    import numpy as np
+
+    k = pow2_rms_shift(h_bits)
+    f = (np.asarray(h_bits, dtype=np.uint16).astype(np.uint32) << 16).view(np.float32)
+    return (np.ascontiguousarray(f * np.float32(2.0 ** -k)).view(np.uint32) >> 16).astype(np.uint16)

@@ -1,6 +1,10 @@
 """Resident decode stack: L MoE layers, every expert resident in HBM, batch-1 decode.
 
-`DecodeStack.step_device` runs one token through all layers (h_{l+1} = h_l + MoE_l(h_l))
+Each layer computes h_{l+1} = h_l + MoE_l(x_l) with x_l = h_l * 2^-k_l, the power of two
+nearest h_l's RMS (norm=True; the model's pre-MoE RMSNorm, kept exact by using a power of
+two). Without it the residual stream of a random-weight stack grows without bound.
+
+`DecodeStack.step_device` runs one token through all layers
 as one CUDA-graph replay of 3*L PDL-chained kernels; `DecodeStack.decode` is the host-facing
 call (pinned host hidden state in, host result out) a user of the library makes.
 This is the stack the reference's OffloadEngine decode loop drives when every layer is
@@ -16,7 +20,8 @@ from .synthetic import ExpertLayer
 
 class DecodeStack:
     def __init__(self, layers: list[ExpertLayer], top_k: int, device, use_graph: bool = True,
-                 predict_top_m: int = 0):
+                 predict_top_m: int = 0, norm: bool = True):
+        self.norm = norm
         self.layers = layers
         self.K = top_k
         self.M = predict_top_m
@@ -46,7 +51,8 @@ class DecodeStack:
             if nxt is not None:
                 out["pred"] = self.preds[li]
             ops.decode_layer(y, ly.router, ly.gate, ly.up, ly.down, self.K, router_next=nxt,
-                             M=self.M if nxt is not None else 0, resid=y, out=out, workspace=self.ws)
+                             M=self.M if nxt is not None else 0, resid=y, norm=self.norm, out=out,
+                             workspace=self.ws)
             y = self.ys[li]
         return y
 
@@ -70,6 +76,63 @@ class DecodeStack:
         else:
             self._layers_once()
         return self.ys[-1]
+
+    def decode(self, h_host: torch.Tensor, out_host: torch.Tensor | None = None) -> torch.Tensor:
+        """Host-facing decode step: pinned host hidden state [1,H] bf16 in, host result out."""
+        cur = torch.cuda.current_stream(self.device)
+        self.x_in.copy_(h_host, non_blocking=True)
+        y = self.step_device()
+        if out_host is None:
+            out_host = torch.empty((1, self.H), dtype=torch.bfloat16, pin_memory=True)
+        out_host.copy_(y, non_blocking=True)
+        cur.synchronize()
+        return out_host
+
+
+class PersistentStack:
+    """The same resident stack as DecodeStack, run by the persistent kernel: one cooperative
+    launch per token with all layers inside (moe_stack_decode)."""
+
+    def __init__(self, layers: list[ExpertLayer], top_k: int, device, num_ctas: int = 0,
+                 keep_layer_inputs: bool = False, norm: bool = True):
+        from ._lib import call
+
+        self.norm = norm
+        self._call = call
+        self.layers = layers
+        self.K = top_k
+        self.device = torch.device(device)
+        self.L = len(layers)
+        self.E, self.H = layers[0].router.shape
+        self.I = layers[0].gate.w.shape[1]
+        self.sb_fp16 = layers[0].gate.sb_fp16
+        self.num_ctas = num_ctas
+        # transposed routers ([H][E]) and the device array of layer descriptors
+        self.router_t = [ly.router.t().contiguous() for ly in layers]
+        desc = []
+        for rt, ly in zip(self.router_t, layers):
+            desc.append([rt.data_ptr(), ly.gate.w.data_ptr(), ly.up.w.data_ptr(), ly.down.w.data_ptr(),
+                         ly.gate.s.data_ptr(), ly.gate.b.data_ptr(), ly.up.s.data_ptr(), ly.up.b.data_ptr(),
+                         ly.down.s.data_ptr(), ly.down.b.data_ptr()])
+        self.desc = torch.tensor(desc, dtype=torch.int64).to(self.device)
+        nbytes = int(call("moe_stack_workspace_bytes", self.H, self.I, self.E, self.K))
+        self.ws = torch.zeros(nbytes, dtype=torch.uint8, device=self.device)
+        self.x_in = torch.zeros((1, self.H), dtype=torch.bfloat16, device=self.device)
+        self.y = torch.empty((1, self.H), dtype=torch.bfloat16, device=self.device)
+        self.inds = torch.empty((self.L, top_k), dtype=torch.int32, device=self.device)
+        self.scores = torch.empty((self.L, top_k), dtype=torch.bfloat16, device=self.device)
+        self.hs = (torch.empty((self.L + 1, self.H), dtype=torch.bfloat16, device=self.device)
+                   if keep_layer_inputs else None)
+        self.launches_per_step = 1
+
+    def step_device(self, x: torch.Tensor | None = None) -> torch.Tensor:
+        if x is not None:
+            self.x_in.copy_(x)
+        self._call("moe_stack_decode", self.desc.data_ptr(), self.L, self.H, self.I, self.E, self.K,
+                   self.sb_fp16, int(self.norm), self.x_in.data_ptr(), self.y.data_ptr(), self.inds.data_ptr(),
+                   self.scores.data_ptr(), None if self.hs is None else self.hs.data_ptr(), self.ws.data_ptr(),
+                   self.ws.numel(), self.num_ctas, torch.cuda.current_stream(self.device).cuda_stream)
+        return self.y
 
     def decode(self, h_host: torch.Tensor, out_host: torch.Tensor | None = None) -> torch.Tensor:
         """Host-facing decode step: pinned host hidden state [1,H] bf16 in, host result out."""
