@@ -157,13 +157,28 @@ int moe_decode_layer(const void *x, int T, int H, int I, int E, int K, const voi
 /* Persistent decode of a whole resident stack (one token through L layers, one launch).  */
 /* ------------------------------------------------------------------------------------ */
 
-/* Per-layer weights of moe_stack_decode, passed as a DEVICE array of L descriptors. The
- * router is transposed ([H][E] bf16, row h = the E router weights of input h); expert
- * tensors as in moe_experts_gateup / moe_experts_down with cap = E. */
+/* Packed expert layout used by moe_stack_decode: one contiguous block per expert holding,
+ * for each 64-wide group G of the expert's intermediate dimension, the 64 gate and 64 up
+ * rows of G and the down matrix's 64 columns of G for all H rows, ordered as the decode
+ * kernel reads them (codes and 16-bit scales / biases, same byte count as the MLX layout).
+ * No reference counterpart: the reference reads each expert's nine MLX tensors
+ * (mlx-qwen38/expert_io.c:34-71 pread per tensor). Bytes per expert (H % 256 == 0 and
+ * I % 64 == 0, else 0). */
+size_t moe_packed_expert_bytes(int H, int I);
+
+/* Packs E experts from the MLX layout of moe_experts_gateup / moe_experts_down (cap = E)
+ * into out[E][moe_packed_expert_bytes(H, I)] on the stream. Code arrays and out 16-byte
+ * aligned. */
+int moe_pack_experts(int E, int H, int I, const uint32_t *wg, const void *sg, const void *bg,
+                     const uint32_t *wu, const void *su, const void *bu, const uint32_t *wd,
+                     const void *sd, const void *bd, void *out, void *stream);
+
+/* Per-layer weights of moe_stack_decode, passed as a DEVICE array of L descriptors: the
+ * transposed router ([H][E] bf16, row h = the E router weights of input h) and the layer's
+ * E packed experts. Both 16-byte aligned. */
 typedef struct {
     const void *router_t;
-    const uint32_t *wg, *wu, *wd;
-    const void *sg, *bg, *su, *bu, *sd, *bd;
+    const void *experts;
 } moe_stack_layer;
 
 /* Workspace bytes for moe_stack_decode (no zero-filling needed: each call clears it). */
@@ -175,8 +190,8 @@ size_t moe_stack_workspace_bytes(int H, int I, int E, int K);
  * the per-layer block of loader.py:903-922), as ONE cooperative kernel with one CTA per SM
  * (num_ctas = 0: all SMs) and two grid barriers per layer. x, y bf16 [H]; inds_out u32
  * [L][K] and scores_out bf16 [L][K] (MLX order, as moe_router_topk); hs_out bf16 [L+1][H]
- * (every layer's input and the final output) or NULL. Requires H % 256 == 0, I % 64 == 0,
- * K <= 32, E <= 2048. Router logits are sums of per-CTA exact partial dot products in double
+ * (every layer's input and the final output) or NULL. Requires H % 256 == 0, H <= 4096,
+ * I % 64 == 0, K <= 32, E <= 2048 and at least H/32 CTAs. Router logits are sums of per-CTA exact partial dot products in double
  * (order of the partial sums varies between runs at the 2^-52 level). norm as in
  * moe_decode_layer (applied to every layer's input).
  */

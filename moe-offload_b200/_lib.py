@@ -40,6 +40,8 @@ SIGNATURES: dict[str, tuple] = {
     "moe_device_error": (I, [I]),
     "moe_decode_workspace_bytes": (SZ, [I, I, I, I, I, I]),
     "moe_decode_layer": (I, [P, I, I, I, I, I, P, P, I, P] + [P] * 9 + [I, I, P, P, P, P, P, P, P, SZ, P]),
+    "moe_packed_expert_bytes": (SZ, [I, I]),
+    "moe_pack_experts": (I, [I, I, I, P, P, P, P, P, P, P, P, P, P, P]),
     "moe_stack_workspace_bytes": (SZ, [I, I, I, I]),
     "moe_stack_decode": (I, [P, I, I, I, I, I, I, I, P, P, P, P, P, P, SZ, I, P]),
 }

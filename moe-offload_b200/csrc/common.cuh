@@ -214,6 +214,7 @@ MOE_D bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
 
 // bounded wait for phase `parity`; false (and the device error word set) on timeout
 MOE_D bool mbar_wait(uint64_t *bar, uint32_t parity) {
+#pragma unroll 1
     for (uint32_t i = 0; i < kMbarSpinLimit; ++i)
         if (mbar_try_wait(bar, parity)) return true;
     atomicOr(&g_moe_device_error, MOE_DEVERR_MBAR_TIMEOUT);

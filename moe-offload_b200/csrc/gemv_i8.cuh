@@ -136,92 +136,83 @@ MOE_D void build_rec_group(const uint16_t *v, bool valid, int ent, uint2 *rec, f
     }
 }
 
-// Copies n bf16 values (n % 8 == 0, both pointers 16-byte aligned) from global memory into
-// shared memory through L2 (another SM may have written them earlier in the same kernel),
-// every thread of the block issuing 16-byte loads; caller synchronises afterwards.
-MOE_D void stage_vec_l2(const uint16_t *src, int n, uint16_t *dst) {
-    const uint4 *s4 = reinterpret_cast<const uint4 *>(src);
-    uint4 *d4 = reinterpret_cast<uint4 *>(dst);
-    for (int i = threadIdx.x; i < (n >> 3); i += blockDim.x) d4[i] = __ldcg(s4 + i);
-}
-
-// Block-wide record builder for `ngroups` consecutive 64-value groups of v (the same records
-// as build_rec_group, laid out back to back): step 1 computes each group's maximum exponent
-// and sum with 4 threads per group, step 2 packs all 16 entries of every group in parallel.
-// kL2: v is global memory another SM wrote in this kernel (read through L2). gexp: shared
-// scratch of ngroups ints. Call with every thread of the block; synchronises internally and
-// leaves the outputs visible to the whole block on return.
-template <bool kL2>
-MOE_D uint4 rec_ld16(const uint16_t *p) {
-    if constexpr (kL2) return __ldcg(reinterpret_cast<const uint4 *>(p));
-    else return *reinterpret_cast<const uint4 *>(p);
-}
-
-template <bool kL2>
-MOE_D void build_recs_block(const uint16_t *v, int ngroups, uint2 *rec, float *scale, float *sum, float mul,
-                            int *gexp) {
-    const int nt = blockDim.x;
-    // step 1: 4 threads per group, 16 values each
-    for (int base = 0; base < ngroups * 4; base += nt) {
-        const int idx = base + threadIdx.x, G = idx >> 2, q = idx & 3;
-        float mx = 0.f, sm = 0.f;
-        if (G < ngroups) {
-            const uint16_t *p = v + (size_t)G * 64 + q * 16;
-            const uint4 a = rec_ld16<kL2>(p), b = rec_ld16<kL2>(p + 8);
-            const uint32_t w[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+// Record of one 64-value group whose values are spread over an aligned half warp: lane
+// ent = lane & 15 holds values 4*ent .. 4*ent+3 as two bf16 pairs (q.x = values 0, 1;
+// q.y = values 2, 3). Produces the same record, scale and sum as build_rec_group (the sum
+// is taken in a different order); entry ent goes to rec[ent * stride] (stride 1: the
+// record's 128 bytes back to back; larger: an entry-major table of several groups). All 32
+// lanes call it, each half warp with its own group; `valid` is uniform within a half warp.
+static __device__ __noinline__ void rec_from_regs(uint2 q, bool valid, uint2 *rec, float *scale, float *sum, float mul,
+                                           int stride = 1) {
+    const int lane = threadIdx.x & 31, ent = lane & 15, hb = lane & 16;
+    const float f0 = __uint_as_float(q.x << 16), f1 = __uint_as_float(q.x & 0xffff0000u);
+    const float f2 = __uint_as_float(q.y << 16), f3 = __uint_as_float(q.y & 0xffff0000u);
+    float mx = fmaxf(fmaxf(fabsf(f0), fabsf(f1)), fmaxf(fabsf(f2), fabsf(f3)));
+    float sm = (f0 + f1) + (f2 + f3);
 #pragma unroll
-            for (int i = 0; i < 8; ++i) {
-                const float lo = __uint_as_float(w[i] << 16), hi = __uint_as_float(w[i] & 0xffff0000u);
-                mx = fmaxf(mx, fmaxf(fabsf(lo), fabsf(hi)));
-                sm += lo + hi;
-            }
+    for (int off = 8; off > 0; off >>= 1) {
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+        sm += __shfl_xor_sync(0xffffffffu, sm, off);
+    }
+    // entry (c, i, h) takes word c of lanes 4i + j (values 16i + 4j + 2c + r, r = 0, 1)
+    const int c = ent >> 3, i = (ent >> 1) & 3, h = ent & 1;
+    uint32_t src[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        const uint32_t wx = __shfl_sync(0xffffffffu, q.x, hb + 4 * i + j);
+        const uint32_t wy = __shfl_sync(0xffffffffu, q.y, hb + 4 * i + j);
+        src[j] = c ? wy : wx;
+    }
+    if (!valid) return;
+    int E = 0;
+    float inv = 1.0f;
+    if (mx > 0.f) {
+        const int be = (int)((__float_as_uint(mx) >> 23) & 0xffu);
+        if (be > 0) {
+            E = be - 127 - 13;
+        } else {                                      // subnormal group maximum
+            int emax = 0;
+            frexpf(mx, &emax);
+            E = emax - 1 - 13;
         }
-        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
-        sm += __shfl_xor_sync(0xffffffffu, sm, 1);
-        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
-        sm += __shfl_xor_sync(0xffffffffu, sm, 2);
-        if (G < ngroups && q == 0) {
-            int E = 0;
-            if (mx > 0.f) {
-                const int be = (int)((__float_as_uint(mx) >> 23) & 0xffu);
-                if (be > 0) {
-                    E = be - 127 - 13;
-                } else {
-                    int emax = 0;
-                    frexpf(mx, &emax);
-                    E = emax - 1 - 13;
-                }
-            }
-            gexp[G] = E;
-            scale[G] = ((E >= -126 && E <= 127) ? __uint_as_float((uint32_t)(E + 127) << 23) : ldexpf(1.0f, E)) * mul;
-            sum[G] = sm * mul;
+        const int ib = 127 - E;                       // biased exponent of 2^-E
+        inv = (ib >= 1 && ib <= 254) ? __uint_as_float((uint32_t)ib << 23) : ldexpf(1.0f, -E);
+    }
+    uint32_t bytes[2] = {0u, 0u};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+#pragma unroll
+        for (int r = 0; r < 2; ++r) {
+            const float f = __uint_as_float(r ? (src[j] & 0xffff0000u) : (src[j] << 16));
+            const int u = __float2int_rn(f * inv);
+            const int hi = u >> 7, lo = u - hi * 128;
+            bytes[r] |= (uint32_t)((h ? lo : hi) & 0xff) << (8 * j);
         }
     }
-    __syncthreads();
-    // step 2: every entry of every group
-    for (int e = threadIdx.x; e < ngroups * 16; e += nt) {
-        const int G = e >> 4, ent = e & 15;
-        const int c = ent >> 3, i = (ent >> 1) & 3, h = ent & 1;
-        const int E = gexp[G];
-        const int ib = 127 - E;
-        const float inv = (ib >= 1 && ib <= 254) ? __uint_as_float((uint32_t)ib << 23) : ldexpf(1.0f, -E);
-        const uint16_t *p = v + (size_t)G * 64 + 16 * i;
-        const uint4 a = rec_ld16<kL2>(p), b = rec_ld16<kL2>(p + 8);
-        // values 16i + 4j + 2c + r, j = 0..3, r = 0..1  ->  word (2j + c) of the 16, half r
-        const uint32_t w[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
-        uint32_t bytes[2] = {0u, 0u};
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            const uint32_t word = w[2 * j + c];
-#pragma unroll
-            for (int r = 0; r < 2; ++r) {
-                const float f = __uint_as_float(r ? (word & 0xffff0000u) : (word << 16));
-                const int u = __float2int_rn(f * inv);
-                const int hi = u >> 7, lo = u - hi * 128;
-                bytes[r] |= (uint32_t)((h ? lo : hi) & 0xff) << (8 * j);
-            }
-        }
-        rec[e] = make_uint2(bytes[0], bytes[1]);
+    rec[ent * stride] = make_uint2(bytes[0], bytes[1]);
+    if (ent == 0) {
+        *scale = ((E >= -126 && E <= 127) ? __uint_as_float((uint32_t)(E + 127) << 23) : ldexpf(1.0f, E)) * mul;
+        *sum = sm * mul;
     }
-    __syncthreads();
+}
+
+// mma_step_i8 with the records in an entry-major table: entry e of this lane's B group at
+// rt[e * stride]. Lanes that are not rec_lane_active (act = false) load nothing.
+MOE_D void mma_step_i8t(const uint4 wa, const uint4 wb, const uint2 *rt, int stride, bool act, int part, int &dg,
+                        int &db) {
+    int dx[4] = {0, 0, 0, 0}, dy[4] = {0, 0, 0, 0};
+    const uint32_t aw[4] = {wa.x, wa.y, wa.z, wa.w};
+    const uint32_t bw[4] = {wb.x, wb.y, wb.z, wb.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const uint32_t a = aw[i], a2 = aw[i] >> 2, b = bw[i], b2 = bw[i] >> 2;
+        const uint2 rx = act ? rt[((0 * 4 + i) * 2 + part) * stride] : make_uint2(0u, 0u);
+        const uint2 ry = act ? rt[((1 * 4 + i) * 2 + part) * stride] : make_uint2(0u, 0u);
+        mma_u8s8_16832(dx, a & 0x03030303u, b & 0x03030303u, a2 & 0x03030303u, b2 & 0x03030303u, rx.x, rx.y);
+        mma_u8s8_16832(dy, a & 0x30303030u, b & 0x30303030u, a2 & 0x30303030u, b2 & 0x30303030u, ry.x, ry.y);
+    }
+    const int c0 = dx[0] + (dy[0] >> 4), c1 = dx[1] + (dy[1] >> 4);
+    const int c2 = dx[2] + (dy[2] >> 4), c3 = dx[3] + (dy[3] >> 4);
+    dg = c0 * 128 + c1;
+    db = c2 * 128 + c3;
 }

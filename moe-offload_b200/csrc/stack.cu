@@ -1,18 +1,23 @@
 // Persistent decode kernel: one token through all L resident MoE layers in ONE cooperative
-// launch (one CTA per SM), two grid barriers per layer. Per layer l:
+// launch (one CTA per SM), two grid barriers per layer. Expert weights are in the packed
+// layout of moe_pack_experts. Per layer l:
 //
-//   phase A  every CTA reads the layer's router logits (fp64 accumulators, see phase B),
-//            rounds them once to bf16 and runs the softmax / MLX-order top-k / renorm
-//            itself (no extra synchronisation); issues 1-D TMA bulk copies for its share of
-//            the routed gate/up rows (units = 8 gate + 8 up rows of one expert), builds the
-//            int8 MMA records of h_l, runs the units (2 warps per unit, H split in halves),
-//            writes its act values, then issues the TMA copies of its down rows into the
-//            freed unit buffers                                        -> grid barrier
-//   phase B  builds the records of all K activation vectors, runs its down blocks (16
-//            output rows x K experts), combines with the routing scores and the residual
-//            into its rows of h_{l+1}, and adds its rows' contribution to layer l+1's
-//            router logits (prefetched slice of the transposed router, exact products,
-//            fp64 atomics)                                             -> grid barrier
+//   phase A  every CTA loads the layer's router logits (fp64 accumulators, see phase B) and
+//            h_l through L2, rounds the logits once to bf16 and runs the softmax / MLX-order
+//            top-k / renorm itself. Work item q = (routed expert k, activation group G of
+//            64 values), K * I/64 items over the CTAs: the CTA fetches the item's packed
+//            slice with 1-D TMA bulk copies (8 gate/up units + the down slice), builds the
+//            int8 MMA records of h_l while they are in flight, runs the 8 units (one warp
+//            pair each, as soon as its bytes land), keeps the 64 SwiGLU activations in
+//            shared memory, builds their one record, and runs the down slice: a split-K
+//            partial of expert k's output over all H rows, written to global memory
+//                                                                     -> grid barrier
+//   phase B  each CTA owns 16-row blocks of h: sums the I/64 partials of every routed
+//            expert for its rows (fixed order), rounds each expert output to bf16,
+//            combines with the routing scores and the residual into its rows of h_{l+1}
+//            (kept in shared memory across layers), and adds its rows' contribution to
+//            layer l+1's router logits (transposed router slices fetched during phase A,
+//            exact products, fp64 atomics)                             -> grid barrier
 //
 // The router logit of expert e is the double-precision sum of per-CTA partial sums, each an
 // exact product sum; the bf16 rounding of that value equals the single rounding of the
@@ -21,26 +26,45 @@
 //
 // Reference semantics: the resident-layer decode body of mlx-qwen38/loader.py:903-922 run
 // for every layer of the stack (OffloadEngine.generate_greedy, loader.py:1176-1195).
+#include <algorithm>
+
 #include "common.cuh"
 #include "gemv_i8.cuh"
-#include "topk.cuh"
 
 namespace {
 
 constexpr int kThreads = 512;
 constexpr int kWarps = kThreads / 32;
-constexpr int kPairs = kWarps / 2;        // gate/up units in flight per CTA
-constexpr int kMaxBlocks = 2;             // down blocks (16 rows) per CTA
+constexpr int kUnits = 8;                   // gate/up units (8 rows) per activation group
+constexpr int kMaxBlocks = 2;               // 16-row blocks of h per CTA in phase B
 constexpr int kMaxE = 2048;
+constexpr int kMaxK = 32;
+constexpr int kMaxH = 4096;
+constexpr int kHPass = kMaxH / 64 / (kThreads / 16);   // record passes over h
 constexpr uint32_t kGridSpinLimit = 1u << 24;
+constexpr int kAccCopies = 4;               // replicas of the logit accumulators (spread the atomics)
+static_assert(kWarps == 2 * kUnits, "one warp pair per unit");
 
 // device-side copy of moe_stack_layer (include/moe_b200.h), same layout
 struct StackLayer {
     const uint16_t *router_t;             // [H][E] bf16 (router transposed)
-    const uint32_t *wg, *wu, *wd;
-    const uint16_t *sg, *bg, *su, *bu, *sd, *bd;
+    const unsigned char *experts;         // [E] packed experts (moe_pack_experts)
 };
 static_assert(sizeof(StackLayer) == sizeof(moe_stack_layer), "layer descriptor layout");
+
+// packed expert layout (pack.cu)
+struct PackDims {
+    uint32_t ub, dco, dso, dbytes, gbytes;
+    size_t ebytes;
+    MOE_HD PackDims(int H, int I) {
+        ub = 5u * (uint32_t)H;            // unit: gate codes, up codes, scale records
+        dco = 8u * ub;                    // down codes of the group (16 bytes per row)
+        dso = dco + 16u * (uint32_t)H;    // down scale pairs (4 bytes per row)
+        dbytes = 20u * (uint32_t)H;
+        gbytes = 60u * (uint32_t)H;
+        ebytes = (size_t)(I / 64) * gbytes;
+    }
+};
 
 struct StackArgs {
     const StackLayer *layers;
@@ -50,48 +74,42 @@ struct StackArgs {
     uint32_t *inds_out;                   // [L][K]
     uint16_t *scores_out;                 // [L][K]
     uint16_t *hs_out;                     // [L+1][H] every layer's input (+ final output), or null
-    double *acc;                          // [2][E]   zero at launch
+    double *acc;                          // [2][kAccCopies][E] zero at launch
     double *ss;                           // [2]      sum of squares of h_l (norm), zero at launch
     int norm;                             // power-of-two RMS normalisation of each layer's input
     uint16_t *hbuf;                       // [2][H]
-    uint16_t *act;                        // [K][I]
+    float *yp;                            // [K][I/64][H] partial down outputs (work item q = k * I/64 + G)
     unsigned int *bar;                    // grid barrier counter, zero at launch
+    unsigned int region;                  // bytes of the weight region in shared memory
 };
 
+// stride (in entries) of the entry-major record table of h: = 4 (mod 16) so that the eight
+// B lanes of an MMA step read eight different bank pairs
+MOE_HD int rec_stride(int ngroups) { return (ngroups + 15) / 16 * 16 + 4; }
+
 struct SmemLayout {
-    size_t bars, ubuf, ubytes, dbytes, rbuf, xrec, xscale, xsum, arec, ascale, asum, zrec, yk, hnew, red,
-        keys, sel, prob, sinds, sscores, redd, cand, gexp, total;
-    int ngH, ngI, umax;
-    MOE_HD SmemLayout(int H, int I, int E, int K, int G) {
-        ngH = H / 64;
-        ngI = I / 64;
-        const int U = K * (I / 8);
-        umax = (U + G - 1) / G;
-        ubytes = al128(16 * (size_t)(H / 4) + 4 * 8 * (size_t)ngH * 2);           // one gate/up unit
-        dbytes = al128((size_t)K * (16 * (size_t)(I / 4) + 2 * 16 * (size_t)ngI * 2));  // one down block
-        bars = 0;                                                                   // 16 mbarriers
-        ubuf = 128;
-        const size_t ureg = (size_t)umax * ubytes, dreg = kMaxBlocks * dbytes;
-        rbuf = ubuf + (ureg > dreg ? ureg : dreg);
-        xrec = rbuf + al128((size_t)kMaxBlocks * 16 * E * 2);
-        xscale = xrec + (size_t)ngH * 128;
-        xsum = xscale + al16((size_t)pad4(ngH) * 4);
-        arec = xsum + al128((size_t)pad4(ngH) * 4);
-        ascale = arec + (size_t)K * ngI * 128;
-        asum = ascale + al16((size_t)pad4(K * ngI) * 4);
-        zrec = asum + al128((size_t)pad4(K * ngI) * 4);
-        yk = zrec + 128;
-        hnew = yk + al16((size_t)kMaxBlocks * K * 16 * 4);
-        red = hnew + kMaxBlocks * 16 * 8;
-        keys = red + (size_t)kPairs * 2 * 8 * 2 * 4;
-        sel = keys + al16((size_t)E * 4);
-        prob = sel + 64 * 4;
-        sinds = prob + al16((size_t)E * 8);
-        sscores = sinds + 64 * 4;
-        redd = sscores + 64 * 4;
-        cand = redd + kWarps * 8 + 64;                // kWarps * 32 selection candidates
-        gexp = cand + kWarps * 32 * 4;                // per-group exponents for the record builder
-        total = gexp + al16((size_t)4 * (ngH > K * ngI ? ngH : K * ngI));
+    size_t bars, region, xrec, xscale, xsum, arec, ascale, sact, ypart, hown, red, cand, comp, redu, redd, sinds,
+        sscores, total;
+    MOE_HD SmemLayout(int H, int I, int K, size_t region_bytes) {
+        const int ngH = H / 64, ngI = I / 64;
+        bars = 0;                                                 // 16 mbarriers
+        region = 128;
+        xrec = region + al128(region_bytes);
+        xscale = xrec + (size_t)16 * rec_stride(ngH) * 8;
+        xsum = xscale + al16((size_t)ngH * 4);
+        arec = xsum + al128((size_t)ngH * 4);
+        ascale = arec + 128;                                      // scale, sum
+        sact = ascale + 16;
+        ypart = sact + 128;
+        hown = ypart + al16((size_t)K * kMaxBlocks * 16 * 4);
+        red = hown + al16((size_t)kMaxBlocks * 16 * 4);
+        cand = red + (size_t)kUnits * 2 * 8 * 2 * 4;
+        comp = cand + (size_t)kWarps * kMaxK * 4;
+        redu = comp + (size_t)kWarps * kMaxK * 4;
+        redd = redu + kWarps * 4;
+        sinds = redd + kWarps * 8;
+        sscores = sinds + kMaxK * 4;
+        total = sscores + kMaxK * 4;
     }
 };
 
@@ -107,21 +125,24 @@ MOE_D unsigned int ld_acquire(const unsigned int *p) {
 MOE_D void grid_sync(unsigned int *bar, unsigned int n) {
     __syncthreads();
     if (threadIdx.x == 0) {
-        __threadfence();
-        atomicAdd(bar, 1u);
+        // release: the block's writes (ordered before by the block barrier) become visible
+        // to every CTA whose acquire load observes this arrival
+        asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(bar) : "memory");
         const unsigned int target = (n + 1) * gridDim.x;
         uint32_t it = 0;
+#pragma unroll 1
         while (ld_acquire(bar) < target) {
             if (++it > kGridSpinLimit) {
                 atomicOr(&g_moe_device_error, MOE_DEVERR_MBAR_TIMEOUT);
                 break;
             }
-            __nanosleep(20);
         }
-        __threadfence();
     }
     __syncthreads();
 }
+
+// barrier over the two warps of unit pair p (named barriers 1..kUnits)
+MOE_D void pair_sync(int p) { asm volatile("bar.sync %0, 64;" ::"r"(1 + p) : "memory"); }
 
 MOE_D double block_sum_d(double v, double *redd) {
 #pragma unroll
@@ -136,339 +157,407 @@ MOE_D double block_sum_d(double v, double *redd) {
     return s;
 }
 
-MOE_D float block_max_f(float v, double *redd) {
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, off));
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    float *r = reinterpret_cast<float *>(redd);
-    __syncthreads();
-    if (lane == 0) r[warp] = v;
-    __syncthreads();
-    float m = r[0];
-#pragma unroll
-    for (int i = 1; i < kWarps; ++i) m = fmaxf(m, r[i]);
-    return m;
+// order-preserving map of floats to unsigned integers
+MOE_D uint32_t f2ord(float f) {
+    const uint32_t u = __float_as_uint(f);
+    return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
 }
+MOE_D float ord2f(uint32_t o) { return __uint_as_float((o & 0x80000000u) ? (o & 0x7fffffffu) : ~o); }
 
-// softmax (double, one bf16 rounding) + MLX-order top-k + renorm of one token's logits held
-// in fp64 accumulators; results in sinds / sscores (shared memory) of every CTA.
-MOE_D void softmax_topk(const double *acc, double xmul, int E, int K, uint32_t *keys, uint32_t *sel,
-                        uint32_t *cand, double *prob, uint32_t *sinds, float *sscores, double *redd) {
+// Softmax (double, one bf16 rounding per probability) + MLX-order top-k + renorm of one
+// token's logits. kKeysT logits per thread: av[j] holds the fp64 logit accumulator of expert
+// tid + j * kThreads; xmul rescales them (power of two). Every warp selects its K largest
+// keys; warp 0 merges the sorted lists and writes the K experts in MLX order (ascending
+// probability, then index) with their renormalised scores to sinds / sscores. All selection
+// rounds are branch-free. Four block synchronisations; the results are visible to the whole
+// block on return.
+template <int kKeysT>
+MOE_D void route(const double (&av)[kKeysT], double xmul, int E, int K, uint32_t *redu, double *redd,
+                 uint32_t *cand, uint32_t *comp, uint32_t *sinds, float *sscores) {
+    static_assert(kWarps <= 32, "one list head per lane");
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    float lg[kKeysT];
     float mx = -INFINITY;
-    for (int e = threadIdx.x; e < E; e += kThreads) {
-        const float l = bf16_bits_to_f32(f64_to_bf16_bits(__ldcg(acc + e) * xmul));
-        prob[e] = (double)l;
-        mx = fmaxf(mx, l);
+#pragma unroll
+    for (int j = 0; j < kKeysT; ++j) {
+        const int e = tid + j * kThreads;
+        lg[j] = (e < E) ? bf16_bits_to_f32(f64_to_bf16_bits(av[j] * xmul)) : -INFINITY;
+        mx = fmaxf(mx, lg[j]);
     }
-    mx = block_max_f(mx, redd);
-    double s = 0.0;
-    for (int e = threadIdx.x; e < E; e += kThreads) {
-        const double v = exp(prob[e] - (double)mx);
-        prob[e] = v;
-        s += v;
-    }
-    s = block_sum_d(s, redd);
-    for (int e = threadIdx.x; e < E; e += kThreads) {
-        const uint16_t p = f64_to_bf16_bits(prob[e] / s);
-        keys[e] = (((uint32_t)p << 16) | (uint32_t)e) + 1u;
-    }
+    uint32_t om = __reduce_max_sync(0xffffffffu, f2ord(mx));
+    if (lane == 0) redu[warp] = om;
     __syncthreads();
-    if (E <= kThreads) {
-        block_select_desc(keys, E, K, cand, sel);    // descending keys (+1 offset)
-    } else {
-        if (threadIdx.x < 32) warp_select_desc(keys, E, K, sel);
-        __syncthreads();
+    om = redu[0];
+#pragma unroll
+    for (int w = 1; w < kWarps; ++w) om = max(om, redu[w]);
+    const double mxd = (double)ord2f(om);
+    double ev[kKeysT];
+    double s = 0.0;
+#pragma unroll
+    for (int j = 0; j < kKeysT; ++j) {
+        ev[j] = (tid + j * kThreads < E) ? exp((double)lg[j] - mxd) : 0.0;
+        s += ev[j];
     }
-    if (threadIdx.x < 32) {
-        const int lane = threadIdx.x;
-        // MLX order = ascending (p, index): lane k takes the k-th smallest selected key
-        const uint32_t key = (lane < K) ? sel[K - 1 - lane] - 1u : 0u;
-        const float p = bf16_bits_to_f32((uint16_t)(key >> 16));
-        float S = 0.f;
-        for (int k = 0; k < K; ++k) {                 // sequential bf16 sum in that order
-            const float pk = __shfl_sync(0xffffffffu, p, k);
-            S = (k == 0) ? pk : bf16r(S + pk);
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
+    if (lane == 0) redd[warp] = s;
+    __syncthreads();
+    s = 0.0;
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) s += redd[w];
+    // keys ((p_bf16 << 16) | e) + 1: larger probability first, ties to the larger index
+    uint32_t key[kKeysT];
+    uint32_t lmax = 0;
+#pragma unroll
+    for (int j = 0; j < kKeysT; ++j) {
+        const int e = tid + j * kThreads;
+        key[j] = (e < E) ? ((((uint32_t)f64_to_bf16_bits(ev[j] / s)) << 16) | (uint32_t)e) + 1u : 0u;
+        lmax = max(lmax, key[j]);
+    }
+    // this warp's K largest, descending, lane r holding the r-th
+    uint32_t mine = 0;
+#pragma unroll 1
+    for (int r = 0; r < K; ++r) {
+        const uint32_t w = __reduce_max_sync(0xffffffffu, lmax);
+        mine = (lane == r) ? w : mine;
+        lmax = 0;
+#pragma unroll
+        for (int j = 0; j < kKeysT; ++j) {
+            key[j] = (key[j] == w) ? 0u : key[j];
+            lmax = max(lmax, key[j]);
         }
+    }
+    if (lane < K) cand[warp * K + lane] = mine;
+    __syncthreads();
+    if (warp == 0) {
+        // merge of the kWarps sorted lists: lane w < kWarps holds the head of list w and has the
+        // element after it loaded already; K rounds of one warp-wide max
+        const int lw = lane < kWarps ? lane : 0;
+        uint32_t head = (lane < kWarps) ? cand[lw * K] : 0u;
+        uint32_t nxt = (lane < kWarps && K > 1) ? cand[lw * K + 1] : 0u;
+        int ptr = 1;                                  // list position of nxt
+        uint32_t sel = 0;
+#pragma unroll 1
+        for (int r = 0; r < K; ++r) {
+            const uint32_t w = __reduce_max_sync(0xffffffffu, head);
+            sel = (lane == K - 1 - r) ? w - 1u : sel;         // lane k: MLX position k (ascending)
+            const bool win = head == w;
+            head = win ? nxt : head;
+            ptr += win ? 1 : 0;
+            const uint32_t ld = cand[lw * K + min(ptr, K - 1)];
+            nxt = win ? ((ptr < K) ? ld : 0u) : nxt;
+        }
+        __syncwarp();
+        if (lane < K) comp[lane] = sel;
+        __syncwarp();
+        // renorm: sequential bf16 sum in MLX order, then bf16(p / S)
+        float S = bf16_bits_to_f32((uint16_t)(comp[0] >> 16));
+#pragma unroll 4
+        for (int k = 1; k < K; ++k) S = bf16r(S + bf16_bits_to_f32((uint16_t)(comp[k] >> 16)));
         if (lane < K) {
-            sinds[lane] = key & 0xffffu;
-            sscores[lane] = bf16r(__fdiv_rn(p, S));
+            sinds[lane] = sel & 0xffffu;
+            sscores[lane] = bf16r(__fdiv_rn(bf16_bits_to_f32((uint16_t)(sel >> 16)), S));
         }
     }
     __syncthreads();
 }
 
-template <bool kFp16>
+// This CTA's rows' contribution to the next layer's router logits: waits for the router
+// slices, then every thread adds sum_r router_t[row r][e] * h[row r] (exact fp32 products of
+// bf16 values, double sums) into acc[e] with one fp64 atomic per expert.
+MOE_D void router_partial(uint64_t *rbar, uint32_t &rphase, const unsigned char *rbuf, const float *hown, int nrows,
+                          int E, double *acc) {
+    const bool ok = mbar_wait(rbar, rphase);
+    rphase ^= 1u;
+    if (!ok) return;
+    const uint16_t *rs = reinterpret_cast<const uint16_t *>(rbuf);
+#pragma unroll 1
+    for (int e = threadIdx.x; e < E; e += kThreads) {
+        double p[4] = {0.0, 0.0, 0.0, 0.0};
+#pragma unroll 1
+        for (int r0 = 0; r0 < nrows; r0 += 4) {
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+                if (r0 + i < nrows) p[i] += (double)(bf16_bits_to_f32(rs[(size_t)(r0 + i) * E + e]) * hown[r0 + i]);
+        }
+        atomicAdd(acc + e, (p[0] + p[1]) + (p[2] + p[3]));
+    }
+}
+
+// issues the copies of work item q's packed slice (threads 0..kUnits)
+MOE_D void issue_item(const StackLayer &ly, const PackDims &P, const uint32_t *sinds, int q, int ngI,
+                      unsigned char *region, uint64_t *ubar, uint64_t *dbar) {
+    const int tid = threadIdx.x;
+    if (tid > kUnits) return;
+    const int k = q / ngI, G = q % ngI;
+    const unsigned char *src = ly.experts + (size_t)sinds[k] * P.ebytes + (size_t)G * P.gbytes;
+    if (tid < kUnits) {
+        mbar_arrive_expect_tx(&ubar[tid], P.ub);
+        tma_load_1d(region + (size_t)tid * P.ub, src + (size_t)tid * P.ub, P.ub, &ubar[tid]);
+    } else {
+        mbar_arrive_expect_tx(dbar, P.dbytes);
+        tma_load_1d(region + P.dco, src + P.dco, P.dbytes, dbar);
+    }
+}
+
+template <bool kFp16, int kKeysT>
 __global__ void __launch_bounds__(kThreads, 1) stack_kernel(StackArgs a) {
     extern __shared__ __align__(128) unsigned char smem[];
     const int H = a.H, I = a.I, E = a.E, K = a.K, L = a.L;
     const int G = gridDim.x, c = blockIdx.x;
-    const SmemLayout S(H, I, E, K, G);
-    const int ngH = S.ngH, ngI = S.ngI;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int g = lane >> 2, t = lane & 3;
+    const int ngH = H / 64, ngI = I / 64, NQ = K * ngI, NB = H / 16;
+    const int xst = rec_stride(ngH);
+    const PackDims P(H, I);
+    const SmemLayout S(H, I, K, a.region);
+    const int b0 = (int)((long long)c * NB / G), nb = (int)((long long)(c + 1) * NB / G) - b0;
+    const int nrows = nb * 16;
 
-    uint64_t *ubar = reinterpret_cast<uint64_t *>(smem + S.bars);          // [kPairs] units
-    uint64_t *dbar = ubar + kPairs;                                         // [kMaxBlocks] down blocks
-    uint64_t *rbar = dbar + kMaxBlocks;                                     // [1] router slices
-    unsigned char *ubuf = smem + S.ubuf;
-    unsigned char *rbuf = smem + S.rbuf;
-    uint2 *xrec = reinterpret_cast<uint2 *>(smem + S.xrec);
+    uint64_t *ubar = reinterpret_cast<uint64_t *>(smem + S.bars);          // [kUnits]
+    uint64_t *dbar = ubar + kUnits;                                         // [1]
+    uint64_t *rbar = dbar + 1;                                              // [1]
+    unsigned char *region = smem + S.region;
+    uint2 *xrec = reinterpret_cast<uint2 *>(smem + S.xrec);                // [16][xst]
     float *xscale = reinterpret_cast<float *>(smem + S.xscale);
     float *xsum = reinterpret_cast<float *>(smem + S.xsum);
     uint2 *arec = reinterpret_cast<uint2 *>(smem + S.arec);
     float *ascale = reinterpret_cast<float *>(smem + S.ascale);
-    float *asum = reinterpret_cast<float *>(smem + S.asum);
-    uint2 *zrec = reinterpret_cast<uint2 *>(smem + S.zrec);
-    float *yk = reinterpret_cast<float *>(smem + S.yk);
-    double *hnew = reinterpret_cast<double *>(smem + S.hnew);
+    uint16_t *sact = reinterpret_cast<uint16_t *>(smem + S.sact);
+    float *ypart = reinterpret_cast<float *>(smem + S.ypart);
+    float *hown = reinterpret_cast<float *>(smem + S.hown);
     float *red = reinterpret_cast<float *>(smem + S.red);
-    uint32_t *keys = reinterpret_cast<uint32_t *>(smem + S.keys);
-    uint32_t *sel = reinterpret_cast<uint32_t *>(smem + S.sel);
-    double *prob = reinterpret_cast<double *>(smem + S.prob);
+    uint32_t *cand = reinterpret_cast<uint32_t *>(smem + S.cand);
+    uint32_t *comp = reinterpret_cast<uint32_t *>(smem + S.comp);
+    uint32_t *redu = reinterpret_cast<uint32_t *>(smem + S.redu);
+    double *redd = reinterpret_cast<double *>(smem + S.redd);
     uint32_t *sinds = reinterpret_cast<uint32_t *>(smem + S.sinds);
     float *sscores = reinterpret_cast<float *>(smem + S.sscores);
-    double *redd = reinterpret_cast<double *>(smem + S.redd);
-    uint32_t *cand = reinterpret_cast<uint32_t *>(smem + S.cand);
-    int *gexp = reinterpret_cast<int *>(smem + S.gexp);
-
-    // static work split: gate/up units u = k * (I/8) + rb, down blocks b (16 rows of H)
-    const int U = K * (I / 8), NB = H / 16;
-    const int u0 = (int)((long)c * U / G), u1 = (int)((long)(c + 1) * U / G);
-    const int b0 = (int)((long)c * NB / G), b1 = (int)((long)(c + 1) * NB / G);
-    const int nu = u1 - u0, nb = b1 - b0;
-    const uint32_t ucb = 8u * (H / 4), usb = 8u * ngH * 2u;          // unit: code / scale bytes per matrix
-    const uint32_t dcb = 16u * (I / 4), dsb = 16u * ngI * 2u;         // down: per expert
-    const size_t dexp = al16((size_t)dcb + 2 * dsb);                   // bytes per expert inside a block
-    const uint32_t rsb = 16u * E * 2u;                                  // router slice per block
 
     if (tid == 0) {
-        for (int i = 0; i < kPairs; ++i) mbar_init(&ubar[i], 1);
-        for (int i = 0; i < kMaxBlocks; ++i) mbar_init(&dbar[i], (uint32_t)K);   // one arrival per expert
-        mbar_init(rbar, 1);
+        for (int i = 0; i < kUnits + 2; ++i) mbar_init(&ubar[i], 1);
         fence_barrier_init();
     }
-    if (tid < 32) zrec[tid >> 1] = make_uint2(0u, 0u);
     __syncthreads();
 
     unsigned int nbar = 0;
-    uint32_t rphase = 0;
+    uint32_t rphase = 0, qphase = 0;
+    const uint32_t rsb = 16u * (uint32_t)E * 2u;   // router slice of one 16-row block
 
     // --------------------------------------------------------------- prologue: h_0 and layer-0 logits
     if (tid == 0 && nb > 0) {
         mbar_arrive_expect_tx(rbar, rsb * nb);
+#pragma unroll 1
         for (int bi = 0; bi < nb; ++bi)
-            tma_load_1d(rbuf + (size_t)bi * rsb, a.layers[0].router_t + (size_t)(b0 + bi) * 16 * E, rsb, rbar);
+            tma_load_1d(region + (size_t)bi * rsb, a.layers[0].router_t + (size_t)(b0 + bi) * 16 * E, rsb, rbar);
     }
     double ssp = 0.0;
-    for (int r = tid; r < nb * 16; r += kThreads) {
+#pragma unroll 1
+    for (int r = tid; r < nrows; r += kThreads) {
         const uint16_t v = a.x_in[b0 * 16 + r];
         a.hbuf[b0 * 16 + r] = v;
         if (a.hs_out) a.hs_out[b0 * 16 + r] = v;
-        hnew[r] = (double)bf16_bits_to_f32(v);
-        ssp = fma(hnew[r], hnew[r], ssp);
+        hown[r] = bf16_bits_to_f32(v);
+        ssp = fma((double)hown[r], (double)hown[r], ssp);
     }
     ssp = block_sum_d(ssp, redd);
     if (tid == 0 && a.norm && nb > 0) atomicAdd(a.ss, ssp);
     __syncthreads();
-    if (nb > 0) {
-        const bool ok = mbar_wait(rbar, rphase);
-        rphase ^= 1u;
-        if (ok) {
-            const uint16_t *rs = reinterpret_cast<const uint16_t *>(rbuf);
-            for (int e = tid; e < E; e += kThreads) {
-                double p = 0.0;
-                for (int r = 0; r < nb * 16; ++r) p = fma((double)bf16_bits_to_f32(rs[(size_t)r * E + e]), hnew[r], p);
-                atomicAdd(a.acc + e, p);
-            }
-        }
-    }
+    if (nb > 0) router_partial(rbar, rphase, region, hown, nrows, E, a.acc + (size_t)(c % kAccCopies) * E);
     grid_sync(a.bar, nbar++);
 
+#pragma unroll 1
     for (int l = 0; l < L; ++l) {
         const StackLayer ly = a.layers[l];
-        const double *accl = a.acc + (size_t)(l & 1) * E;
+        const double *accl = a.acc + (size_t)(l & 1) * kAccCopies * E;
         const uint16_t *hcur = a.hbuf + (size_t)(l & 1) * H;
         uint16_t *hnext = a.hbuf + (size_t)((l + 1) & 1) * H;
-        const uint32_t lphase = (uint32_t)(l & 1);
 
         // ---------------------------------------------------------- phase A
+        // loads through L2 (written by other SMs): logits, h_l, sum of squares
+        double av[kKeysT];
+#pragma unroll
+        for (int j = 0; j < kKeysT; ++j) {
+            const int e = tid + j * kThreads;
+            av[j] = 0.0;
+            if (e < E) {
+#pragma unroll
+                for (int r = 0; r < kAccCopies; ++r) av[j] += __ldcg(accl + (size_t)r * E + e);
+            }
+        }
+        uint2 hq[kHPass];
+#pragma unroll
+        for (int p = 0; p < kHPass; ++p) {
+            const int Gp = (tid >> 4) + p * (kThreads / 16);
+            hq[p] = (Gp < ngH) ? __ldcg(reinterpret_cast<const uint2 *>(hcur + (size_t)Gp * 64) + (tid & 15))
+                               : make_uint2(0u, 0u);
+        }
         const double xmul = a.norm ? ldexp(1.0, -pow2_rms_shift(__ldcg(a.ss + (l & 1)), H)) : 1.0;
-        softmax_topk(accl, xmul, E, K, keys, sel, cand, prob, sinds, sscores, redd);
+
+        route<kKeysT>(av, xmul, E, K, redu, redd, cand, comp, sinds, sscores);
         if (c == 0 && tid < K) {
             a.inds_out[(size_t)l * K + tid] = sinds[tid];
             a.scores_out[(size_t)l * K + tid] = f32_to_bf16_bits(sscores[tid]);
         }
-        {
-            const int p = warp >> 1;
-            if ((warp & 1) == 0 && lane == 0 && p < nu) {
-                fence_barrier_init();   // generic reads of the buffers happened before these async writes
-                const int u = u0 + p, k = u / (I / 8), rb = u % (I / 8);
-                const size_t row0 = (size_t)sinds[k] * I + (size_t)rb * 8;
-                unsigned char *dst = ubuf + (size_t)p * S.ubytes;
-                mbar_arrive_expect_tx(&ubar[p], 2 * ucb + 4 * usb);
-                tma_load_1d(dst, ly.wg + row0 * (H / 16), ucb, &ubar[p]);
-                tma_load_1d(dst + ucb, ly.wu + row0 * (H / 16), ucb, &ubar[p]);
-                tma_load_1d(dst + 2 * ucb, ly.sg + row0 * ngH, usb, &ubar[p]);
-                tma_load_1d(dst + 2 * ucb + usb, ly.bg + row0 * ngH, usb, &ubar[p]);
-                tma_load_1d(dst + 2 * ucb + 2 * usb, ly.su + row0 * ngH, usb, &ubar[p]);
-                tma_load_1d(dst + 2 * ucb + 3 * usb, ly.bu + row0 * ngH, usb, &ubar[p]);
-            }
-            if (warp == kWarps - 1 && lane == 0 && l + 1 < L && nb > 0) {
-                fence_barrier_init();
-                mbar_arrive_expect_tx(rbar, rsb * nb);
-                for (int bi = 0; bi < nb; ++bi)
-                    tma_load_1d(rbuf + (size_t)bi * rsb, a.layers[l + 1].router_t + (size_t)(b0 + bi) * 16 * E, rsb,
-                                rbar);
-            }
+        if (c < NQ) issue_item(ly, P, sinds, c, ngI, region, ubar, dbar);
+        // records of h_l * xmul (entry-major) while the copies are in flight
+#pragma unroll
+        for (int p = 0; p < kHPass; ++p) {
+            const int Gp = (tid >> 4) + p * (kThreads / 16);
+            if (p * (kThreads / 16) < ngH)
+                rec_from_regs(hq[p], Gp < ngH, xrec + Gp, xscale + Gp, xsum + Gp, (float)xmul, xst);
         }
-        // records of h_l (written by every CTA in the previous phase B; read through L2)
-        build_recs_block<true>(hcur, ngH, xrec, xscale, xsum, (float)xmul, gexp);
-        {
-            const int p = warp >> 1, half = warp & 1;
-            float accg = 0.f, accu = 0.f;
-            bool wok = false;
-            if (p < nu) {
-                wok = mbar_wait(&ubar[p], lphase);
-                const unsigned char *base = ubuf + (size_t)p * S.ubytes;
-                const uint4 *grow = reinterpret_cast<const uint4 *>(base + (size_t)g * (H / 4));
-                const uint4 *urow = reinterpret_cast<const uint4 *>(base + ucb + (size_t)g * (H / 4));
-                const uint16_t *sgs = reinterpret_cast<const uint16_t *>(base + 2 * ucb);
-                const uint16_t *bgs = sgs + 8 * ngH, *sus = bgs + 8 * ngH, *bus = sus + 8 * ngH;
-                const int nsteps = (ngH + 3) >> 2;
+        __syncthreads();
+#pragma unroll 1
+        for (int q = c; q < NQ; q += G) {
+            // gate/up unit p = warp pair, H split in halves between the two warps
+            {
+                const int p = warp >> 1, half = warp & 1;
+                const bool wok = mbar_wait(&ubar[p], qphase);
+                const unsigned char *ubase = region + (size_t)p * P.ub;
+                const uint4 *gc = reinterpret_cast<const uint4 *>(ubase);
+                const uint4 *uc = reinterpret_cast<const uint4 *>(ubase + 2 * H);
+                const uint2 *sr = reinterpret_cast<const uint2 *>(ubase + 4 * H);
+                const int nsteps = ngH >> 2;
                 const int s0 = half * nsteps / 2, s1 = (half + 1) * nsteps / 2;
                 const bool bact = rec_lane_active(lane);
                 const int part = rec_lane_part(lane);
+                float accg = 0.f, accu = 0.f;
                 if (wok) {
+#pragma unroll 1
                     for (int j = s0; j < s1; ++j) {
                         const int Gj = 4 * j + t;
-                        const bool gok = Gj < ngH;
-                        const uint4 wv = gok ? grow[Gj] : make_uint4(0, 0, 0, 0);
-                        const uint4 uv = gok ? urow[Gj] : make_uint4(0, 0, 0, 0);
-                        const uint2 *rec = (bact && gok) ? xrec + (size_t)Gj * 16 : zrec;
+                        const uint4 wv = gc[j * 32 + lane], uv = uc[j * 32 + lane];
+                        const uint2 sb = sr[j * 32 + lane];
                         int dg, du;
-                        mma_step_i8(wv, uv, rec, part, dg, du);
-                        if (gok) {
-                            const int si = g * ngH + Gj;
-                            const float sc = xscale[Gj], sm = xsum[Gj];
-                            accg += sb_to_f32<kFp16>(sgs[si]) * ((float)dg * sc) + sb_to_f32<kFp16>(bgs[si]) * sm;
-                            accu += sb_to_f32<kFp16>(sus[si]) * ((float)du * sc) + sb_to_f32<kFp16>(bus[si]) * sm;
-                        }
+                        mma_step_i8t(wv, uv, xrec + Gj, xst, bact, part, dg, du);
+                        const float sc = xscale[Gj], sm = xsum[Gj];
+                        accg += sb_to_f32<kFp16>((uint16_t)sb.x) * ((float)dg * sc) +
+                                sb_to_f32<kFp16>((uint16_t)(sb.x >> 16)) * sm;
+                        accu += sb_to_f32<kFp16>((uint16_t)sb.y) * ((float)du * sc) +
+                                sb_to_f32<kFp16>((uint16_t)(sb.y >> 16)) * sm;
+                    }
+                }
+                accg += __shfl_xor_sync(0xffffffffu, accg, 1);
+                accu += __shfl_xor_sync(0xffffffffu, accu, 1);
+                accg += __shfl_xor_sync(0xffffffffu, accg, 2);
+                accu += __shfl_xor_sync(0xffffffffu, accu, 2);
+                if (t == 0) {
+                    red[((p * 2 + half) * 8 + g) * 2 + 0] = accg;
+                    red[((p * 2 + half) * 8 + g) * 2 + 1] = accu;
+                }
+                pair_sync(p);
+                if (half == 0 && lane < 8) {
+                    const float gs = red[((p * 2) * 8 + lane) * 2 + 0] + red[((p * 2 + 1) * 8 + lane) * 2 + 0];
+                    const float us = red[((p * 2) * 8 + lane) * 2 + 1] + red[((p * 2 + 1) * 8 + lane) * 2 + 1];
+                    const float gv = bf16r(gs), uv = bf16r(us);
+                    const float sig = bf16r(1.0f / (1.0f + expf(-gv)));
+                    const float avv = wok ? bf16r(bf16r(gv * sig) * uv) : 0.f;
+                    sact[p * 8 + lane] = f32_to_bf16_bits(avv);
+                }
+            }
+            __syncthreads();
+            // the one record of the 64 activations
+            if (warp == 0) {
+                const uint2 qv = (lane < 16) ? reinterpret_cast<const uint2 *>(sact)[lane] : make_uint2(0u, 0u);
+                rec_from_regs(qv, lane < 16, arec, ascale, ascale + 1, 1.0f);
+            }
+            __syncthreads();
+            // down slice: split-K partial of expert k's output over all H rows. One MMA pair per
+            // 16 rows: lane (g, t) feeds word t of rows g and g+8; B columns 0 / 1 carry the
+            // record's hi / lo parts (lanes 0..7), so D columns 0 / 1 of lane quad t = 0 hold
+            // the row's integer dot.
+            {
+                const bool wok = mbar_wait(dbar, qphase);
+                const uint32_t *dc = reinterpret_cast<const uint32_t *>(region + P.dco);
+                const uint32_t *ds = reinterpret_cast<const uint32_t *>(region + P.dso);
+                const int n = lane >> 2;
+                const uint2 bx = (lane < 8) ? arec[(0 * 4 + t) * 2 + n] : make_uint2(0u, 0u);
+                const uint2 by = (lane < 8) ? arec[(1 * 4 + t) * 2 + n] : make_uint2(0u, 0u);
+                const float asc = ascale[0], asm_ = ascale[1];
+                float *ypq = a.yp + (size_t)q * H;
+#pragma unroll 2
+                for (int tile = warp; tile < NB; tile += kWarps) {
+                    const uint32_t wa = dc[tile * 64 + lane], wb = dc[tile * 64 + 32 + lane];
+                    int dx[4] = {0, 0, 0, 0}, dy[4] = {0, 0, 0, 0};
+                    mma_u8s8_16832(dx, wa & 0x03030303u, wb & 0x03030303u, (wa >> 2) & 0x03030303u,
+                                   (wb >> 2) & 0x03030303u, bx.x, bx.y);
+                    mma_u8s8_16832(dy, wa & 0x30303030u, wb & 0x30303030u, (wa >> 2) & 0x30303030u,
+                                   (wb >> 2) & 0x30303030u, by.x, by.y);
+                    if (t == 0) {
+                        const int da = (dx[0] + (dy[0] >> 4)) * 128 + (dx[1] + (dy[1] >> 4));
+                        const int db = (dx[2] + (dy[2] >> 4)) * 128 + (dx[3] + (dy[3] >> 4));
+                        const uint32_t sa = ds[tile * 16 + g], sbb = ds[tile * 16 + 8 + g];
+                        const float ya = sb_to_f32<kFp16>((uint16_t)sa) * ((float)da * asc) +
+                                         sb_to_f32<kFp16>((uint16_t)(sa >> 16)) * asm_;
+                        const float yb = sb_to_f32<kFp16>((uint16_t)sbb) * ((float)db * asc) +
+                                         sb_to_f32<kFp16>((uint16_t)(sbb >> 16)) * asm_;
+                        ypq[tile * 16 + g] = wok ? ya : 0.f;
+                        ypq[tile * 16 + 8 + g] = wok ? yb : 0.f;
                     }
                 }
             }
-            accg += __shfl_xor_sync(0xffffffffu, accg, 1);
-            accu += __shfl_xor_sync(0xffffffffu, accu, 1);
-            accg += __shfl_xor_sync(0xffffffffu, accg, 2);
-            accu += __shfl_xor_sync(0xffffffffu, accu, 2);
-            if (p < nu && t == 0) {
-                red[((p * 2 + half) * 8 + g) * 2 + 0] = accg;
-                red[((p * 2 + half) * 8 + g) * 2 + 1] = accu;
-            }
             __syncthreads();
-            if (p < nu && half == 0 && lane < 8) {
-                const float gs = red[((p * 2) * 8 + lane) * 2 + 0] + red[((p * 2 + 1) * 8 + lane) * 2 + 0];
-                const float us = red[((p * 2) * 8 + lane) * 2 + 1] + red[((p * 2 + 1) * 8 + lane) * 2 + 1];
-                const float gv = bf16r(gs), uv = bf16r(us);
-                const float sig = bf16r(1.0f / (1.0f + expf(-gv)));
-                const float av = wok ? bf16r(bf16r(gv * sig) * uv) : 0.f;
-                const int u = u0 + p, k = u / (I / 8), rb = u % (I / 8);
-                a.act[(size_t)k * I + rb * 8 + lane] = f32_to_bf16_bits(av);
-            }
+            qphase ^= 1u;
+            if (q + G < NQ) issue_item(ly, P, sinds, q + G, ngI, region, ubar, dbar);
         }
-        __syncthreads();
-        // down rows into the freed unit buffers: one (block, expert) per warp, in parallel
-        for (int task = warp; task < nb * K; task += kWarps) {
-            if (lane == 0) {
-                const int bi = task / K, k = task % K;
-                fence_barrier_init();   // the unit buffers were read by the generic proxy above
-                const size_t row0 = (size_t)sinds[k] * H + (size_t)(b0 + bi) * 16;
-                unsigned char *dst = ubuf + (size_t)bi * S.dbytes + (size_t)k * dexp;
-                mbar_arrive_expect_tx(&dbar[bi], dcb + 2 * dsb);
-                tma_load_1d(dst, ly.wd + row0 * (I / 16), dcb, &dbar[bi]);
-                tma_load_1d(dst + dcb, ly.sd + row0 * ngI, dsb, &dbar[bi]);
-                tma_load_1d(dst + dcb + dsb, ly.bd + row0 * ngI, dsb, &dbar[bi]);
-            }
+        // next layer's router slices into the consumed weight region
+        if (tid == 0 && l + 1 < L && nb > 0) {
+            mbar_arrive_expect_tx(rbar, rsb * nb);
+#pragma unroll 1
+            for (int bi = 0; bi < nb; ++bi)
+                tma_load_1d(region + (size_t)bi * rsb, a.layers[l + 1].router_t + (size_t)(b0 + bi) * 16 * E, rsb,
+                            rbar);
         }
         grid_sync(a.bar, nbar++);
 
         // ---------------------------------------------------------- phase B
-        build_recs_block<true>(a.act, K * ngI, arec, ascale, asum, 1.0f, gexp);
-        for (int task = warp; task < nb * K; task += kWarps) {
-            const int bi = task / K, k = task % K;
-            const bool wok = mbar_wait(&dbar[bi], lphase);
-            const unsigned char *base = ubuf + (size_t)bi * S.dbytes + (size_t)k * dexp;
-            const uint16_t *sds = reinterpret_cast<const uint16_t *>(base + dcb);
-            const uint16_t *bds = sds + 16 * ngI;
-            const uint4 *rowa = reinterpret_cast<const uint4 *>(base + (size_t)g * (I / 4));
-            const uint4 *rowbp = reinterpret_cast<const uint4 *>(base + (size_t)(g + 8) * (I / 4));
-            const uint2 *rk = arec + (size_t)k * ngI * 16;
-            const float *sck = ascale + k * ngI, *smk = asum + k * ngI;
-            const bool bact = rec_lane_active(lane);
-            const int part = rec_lane_part(lane);
-            float acca = 0.f, accb = 0.f;
-            if (wok) {
-                for (int j = 0; j < (ngI + 3) >> 2; ++j) {
-                    const int Gj = 4 * j + t;
-                    const bool gok = Gj < ngI;
-                    const uint4 qa = gok ? rowa[Gj] : make_uint4(0, 0, 0, 0);
-                    const uint4 qb = gok ? rowbp[Gj] : make_uint4(0, 0, 0, 0);
-                    const uint2 *rec = (bact && gok) ? rk + (size_t)Gj * 16 : zrec;
-                    int da, db;
-                    mma_step_i8(qa, qb, rec, part, da, db);
-                    if (gok) {
-                        const int sa = g * ngI + Gj, sbi = (g + 8) * ngI + Gj;
-                        const float sc = sck[Gj], sm = smk[Gj];
-                        acca += sb_to_f32<kFp16>(sds[sa]) * ((float)da * sc) + sb_to_f32<kFp16>(bds[sa]) * sm;
-                        accb += sb_to_f32<kFp16>(sds[sbi]) * ((float)db * sc) + sb_to_f32<kFp16>(bds[sbi]) * sm;
-                    }
-                }
+        // expert outputs for this CTA's rows: thread (k, r) sums the I/64 partials of work
+        // items (k, 0..) in a fixed order straight from L2 and rounds once to bf16
+#pragma unroll 1
+        for (int x = tid; x < K * nrows; x += kThreads) {
+            const int k = x / nrows, r = x % nrows;
+            const float *src = a.yp + (size_t)k * ngI * H + b0 * 16 + r;
+            float v[4];
+            float yk = 0.f;
+#pragma unroll 1
+            for (int g0 = 0; g0 < ngI; g0 += 4) {
+#pragma unroll
+                for (int i = 0; i < 4; ++i) v[i] = (g0 + i < ngI) ? __ldcg(src + (size_t)(g0 + i) * H) : 0.f;
+#pragma unroll
+                for (int i = 0; i < 4; ++i) yk += v[i];
             }
-            acca += __shfl_xor_sync(0xffffffffu, acca, 1);
-            accb += __shfl_xor_sync(0xffffffffu, accb, 1);
-            acca += __shfl_xor_sync(0xffffffffu, acca, 2);
-            accb += __shfl_xor_sync(0xffffffffu, accb, 2);
-            if (t == 0) {
-                yk[(bi * K + k) * 16 + g] = wok ? bf16r(acca) : 0.f;
-                yk[(bi * K + k) * 16 + 8 + g] = wok ? bf16r(accb) : 0.f;
-            }
+            ypart[k * nrows + r] = bf16r(yk);
         }
         __syncthreads();
         double ssn = 0.0;
-        for (int r = tid; r < nb * 16; r += kThreads) {
-            const int bi = r >> 4, rr = r & 15, row = (b0 + bi) * 16 + rr;
+#pragma unroll 1
+        for (int r = tid; r < nrows; r += kThreads) {
+            const int row = b0 * 16 + r;
             float accv = 0.f;
+#pragma unroll 4
             for (int k = 0; k < K; ++k) {
-                const float pk = bf16r(yk[(bi * K + k) * 16 + rr] * sscores[k]);
+                const float pk = bf16r(ypart[k * nrows + r] * sscores[k]);
                 accv = (k == 0) ? pk : bf16r(accv + pk);
             }
-            accv = bf16r(bf16_bits_to_f32(__ldcg(hcur + row)) + accv);
+            accv = bf16r(hown[r] + accv);
             const uint16_t hb = f32_to_bf16_bits(accv);
             hnext[row] = hb;
             if (a.hs_out) a.hs_out[(size_t)(l + 1) * H + row] = hb;
             if (l + 1 == L) a.y_out[row] = hb;
-            hnew[r] = (double)accv;
-            ssn = fma(hnew[r], hnew[r], ssn);
+            hown[r] = accv;
+            ssn = fma((double)accv, (double)accv, ssn);
         }
         ssn = block_sum_d(ssn, redd);
         if (tid == 0 && a.norm && nb > 0 && l + 1 < L) atomicAdd(a.ss + ((l + 1) & 1), ssn);
         __syncthreads();
-        if (l + 1 < L && nb > 0) {
-            const bool ok = mbar_wait(rbar, rphase);
-            rphase ^= 1u;
-            double *accn = a.acc + (size_t)((l + 1) & 1) * E;
-            if (ok) {
-                const uint16_t *rs = reinterpret_cast<const uint16_t *>(rbuf);
-                for (int e = tid; e < E; e += kThreads) {
-                    double p = 0.0;
-                    for (int r = 0; r < nb * 16; ++r)
-                        p = fma((double)bf16_bits_to_f32(rs[(size_t)r * E + e]), hnew[r], p);
-                    atomicAdd(accn + e, p);
-                }
-            }
-        }
+        if (l + 1 < L && nb > 0)
+            router_partial(rbar, rphase, region, hown, nrows, E,
+                           a.acc + ((size_t)((l + 1) & 1) * kAccCopies + c % kAccCopies) * E);
         if (c == 0) {   // layer l's accumulators were consumed in phase A; ready them for l + 2
-            double *accz = a.acc + (size_t)(l & 1) * E;
-            for (int e = tid; e < E; e += kThreads) accz[e] = 0.0;
+            double *accz = a.acc + (size_t)(l & 1) * kAccCopies * E;
+#pragma unroll 1
+            for (int e = tid; e < kAccCopies * E; e += kThreads) accz[e] = 0.0;
             if (tid == 0) a.ss[l & 1] = 0.0;
         }
         if (l + 1 < L) grid_sync(a.bar, nbar++);
@@ -477,7 +566,8 @@ __global__ void __launch_bounds__(kThreads, 1) stack_kernel(StackArgs a) {
 
 struct StackWs {
     double *acc, *ss;
-    uint16_t *hbuf, *act;
+    uint16_t *hbuf;
+    float *yp;
     unsigned int *bar;
     size_t bytes;
 };
@@ -487,17 +577,17 @@ StackWs carve(void *base, int H, int I, int E, int K) {
     char *p = static_cast<char *>(base);
     size_t off = 0;
     auto take = [&](size_t n) { char *q = p ? p + off : nullptr; off += al256(n); return q; };
-    w.acc = reinterpret_cast<double *>(take((size_t)(2 * E + 2) * 8));
-    w.ss = w.acc + 2 * E;
+    w.acc = reinterpret_cast<double *>(take((size_t)(2 * kAccCopies * E + 2) * 8));
+    w.ss = w.acc + 2 * kAccCopies * E;
     w.bar = reinterpret_cast<unsigned int *>(take(256));
     w.hbuf = reinterpret_cast<uint16_t *>(take((size_t)2 * H * 2));
-    w.act = reinterpret_cast<uint16_t *>(take((size_t)K * I * 2));
+    w.yp = reinterpret_cast<float *>(take((size_t)K * (I / 64) * H * 4));
     w.bytes = off;
     return w;
 }
 
 // bytes of the acc + barrier prefix that must be zero before every launch
-size_t zero_prefix(int E) { return al256((size_t)(2 * E + 2) * 8) + 256; }
+size_t zero_prefix(int E) { return al256((size_t)(2 * kAccCopies * E + 2) * 8) + 256; }
 
 }  // namespace
 
@@ -511,7 +601,7 @@ extern "C" int moe_stack_decode(const void *layers, int L, int H, int I, int E, 
                                 void *workspace, size_t workspace_bytes, int num_ctas, void *stream) {
     if (!layers || !x || !y || !inds_out || !scores_out || !workspace)
         return moe_set_error(MOE_EINVAL, "stack_decode: null pointer");
-    if (L <= 0 || H % 256 || I % 64 || E <= 0 || E > kMaxE || K <= 0 || K > 32 || K > E)
+    if (L <= 0 || H % 256 || H > kMaxH || I % 64 || I <= 0 || E <= 0 || E > kMaxE || K <= 0 || K > kMaxK || K > E)
         return moe_set_error(MOE_EINVAL, "stack_decode: bad sizes L=%d H=%d I=%d E=%d K=%d", L, H, I, E, K);
     const size_t need = moe_stack_workspace_bytes(H, I, E, K);
     if (workspace_bytes < need)
@@ -522,10 +612,11 @@ extern "C" int moe_stack_decode(const void *layers, int L, int H, int I, int E, 
     MOE_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
     const int G = num_ctas > 0 ? num_ctas : sms;
     if (G > sms) return moe_set_error(MOE_EINVAL, "stack_decode: %d CTAs > %d SMs", G, sms);
-    const int U = K * (I / 8), NB = H / 16;
-    if ((U + G - 1) / G > kPairs || (NB + G - 1) / G > kMaxBlocks)
-        return moe_set_error(MOE_EINVAL, "stack_decode: %d CTAs too few for %d units / %d blocks", G, U, NB);
-    const SmemLayout S(H, I, E, K, G);
+    if ((H / 16 + G - 1) / G > kMaxBlocks)
+        return moe_set_error(MOE_EINVAL, "stack_decode: %d CTAs too few for %d row blocks", G, H / 16);
+    const PackDims P(H, I);
+    const size_t region = std::max((size_t)P.gbytes, (size_t)kMaxBlocks * 16 * E * 2);
+    const SmemLayout S(H, I, K, region);
     if (S.total > 227 * 1024)
         return moe_set_error(MOE_EINVAL, "stack_decode: %zu bytes of shared memory needed", S.total);
     StackWs w = carve(workspace, H, I, E, K);
@@ -533,11 +624,12 @@ extern "C" int moe_stack_decode(const void *layers, int L, int H, int I, int E, 
     MOE_CUDA_TRY(cudaMemsetAsync(workspace, 0, zero_prefix(E), st));
     StackArgs a{static_cast<const StackLayer *>(layers), L, H, I, E, K, static_cast<const uint16_t *>(x),
                 static_cast<uint16_t *>(y), inds_out, static_cast<uint16_t *>(scores_out),
-                static_cast<uint16_t *>(hs_out), w.acc, w.ss, norm, w.hbuf, w.act, w.bar};
+                static_cast<uint16_t *>(hs_out), w.acc, w.ss, norm, w.hbuf, w.yp, w.bar, (unsigned int)region};
     void *kargs[] = {&a};
-    auto kern = sb_fp16 ? (const void *)stack_kernel<true> : (const void *)stack_kernel<false>;
+    const void *kern = (E <= kThreads) ? (sb_fp16 ? (const void *)stack_kernel<true, 1> : (const void *)stack_kernel<false, 1>)
+                                       : (sb_fp16 ? (const void *)stack_kernel<true, kMaxE / kThreads>
+                                                  : (const void *)stack_kernel<false, kMaxE / kThreads>);
     MOE_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)S.total));
     MOE_CUDA_TRY(cudaLaunchCooperativeKernel(kern, dim3(G), dim3(kThreads), kargs, S.total, st));
     return MOE_OK;
 }
-

@@ -56,38 +56,3 @@ MOE_D void warp_select_desc(const uint32_t *keys, int E, int n, uint32_t *out) {
     __syncwarp();
 }
 
-
-// Block-level selection of the K largest of keys[0..E) (distinct, > 0) for E <= 32 * (number
-// of warps) and K <= 32: every warp sorts its 32 keys with a bitonic network over shuffles,
-// keeps its K largest in cand[], then warp 0 merges the sorted lists (K rounds of one
-// warp-wide max over the list heads). out[0..K) receives the keys in descending order.
-// Call with every thread of the block; synchronises internally.
-MOE_D void block_select_desc(const uint32_t *keys, int E, int K, uint32_t *cand, uint32_t *out) {
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
-    uint32_t key = (warp * 32 + lane < E) ? keys[warp * 32 + lane] : 0u;
-#pragma unroll
-    for (int k = 2; k <= 32; k <<= 1) {
-#pragma unroll
-        for (int j = k >> 1; j > 0; j >>= 1) {
-            const uint32_t other = __shfl_xor_sync(0xffffffffu, key, j);
-            const bool lower = (lane & j) == 0, asc = (lane & k) == 0;
-            key = (lower == asc) ? min(key, other) : max(key, other);
-        }
-    }
-    // ascending within the warp: lane 31 - i holds the i-th largest
-    if (lane >= 32 - K) cand[warp * K + (31 - lane)] = key;
-    __syncthreads();
-    if (warp == 0) {
-        int ptr = 0;
-        uint32_t head = (lane < nw) ? cand[lane * K] : 0u;
-        for (int r = 0; r < K; ++r) {
-            const uint32_t win = __reduce_max_sync(0xffffffffu, head);
-            if (lane < nw && head == win && win != 0u) {
-                ++ptr;
-                head = (ptr < K) ? cand[lane * K + ptr] : 0u;
-            }
-            if (lane == 0) out[r] = win;
-        }
-    }
-    __syncthreads();
-}

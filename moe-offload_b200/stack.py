@@ -89,17 +89,34 @@ class DecodeStack:
         return out_host
 
 
+def pack_layer_experts(layer: ExpertLayer, device) -> torch.Tensor:
+    """The layer's E experts in the packed layout of moe_pack_experts ([E, expert_bytes] u8)."""
+    from ._lib import call
+
+    E, H = layer.router.shape
+    I = layer.gate.w.shape[1]
+    nbytes = int(call("moe_packed_expert_bytes", H, I))
+    out = torch.empty((E, nbytes), dtype=torch.uint8, device=device)
+    g, u, d = layer.gate, layer.up, layer.down
+    call("moe_pack_experts", E, H, I, g.w.data_ptr(), g.s.data_ptr(), g.b.data_ptr(), u.w.data_ptr(),
+         u.s.data_ptr(), u.b.data_ptr(), d.w.data_ptr(), d.s.data_ptr(), d.b.data_ptr(), out.data_ptr(),
+         torch.cuda.current_stream(device).cuda_stream)
+    return out
+
+
 class PersistentStack:
     """The same resident stack as DecodeStack, run by the persistent kernel: one cooperative
-    launch per token with all layers inside (moe_stack_decode)."""
+    launch per token with all layers inside (moe_stack_decode). The experts are repacked once
+    at construction (pack_layer_experts); with release_unpacked the MLX-layout tensors of
+    `layers` are dropped afterwards (their memory is freed when the caller holds no other
+    reference)."""
 
     def __init__(self, layers: list[ExpertLayer], top_k: int, device, num_ctas: int = 0,
-                 keep_layer_inputs: bool = False, norm: bool = True):
+                 keep_layer_inputs: bool = False, norm: bool = True, release_unpacked: bool = False):
         from ._lib import call
 
         self.norm = norm
         self._call = call
-        self.layers = layers
         self.K = top_k
         self.device = torch.device(device)
         self.L = len(layers)
@@ -107,13 +124,16 @@ class PersistentStack:
         self.I = layers[0].gate.w.shape[1]
         self.sb_fp16 = layers[0].gate.sb_fp16
         self.num_ctas = num_ctas
-        # transposed routers ([H][E]) and the device array of layer descriptors
+        # transposed routers ([H][E]), packed experts and the device array of layer descriptors
         self.router_t = [ly.router.t().contiguous() for ly in layers]
-        desc = []
-        for rt, ly in zip(self.router_t, layers):
-            desc.append([rt.data_ptr(), ly.gate.w.data_ptr(), ly.up.w.data_ptr(), ly.down.w.data_ptr(),
-                         ly.gate.s.data_ptr(), ly.gate.b.data_ptr(), ly.up.s.data_ptr(), ly.up.b.data_ptr(),
-                         ly.down.s.data_ptr(), ly.down.b.data_ptr()])
+        self.packed = []
+        for i in range(self.L):
+            self.packed.append(pack_layer_experts(layers[i], self.device))
+            if release_unpacked:
+                torch.cuda.current_stream(self.device).synchronize()
+                layers[i] = None
+        self.layers = None if release_unpacked else layers
+        desc = [[rt.data_ptr(), pk.data_ptr()] for rt, pk in zip(self.router_t, self.packed)]
         self.desc = torch.tensor(desc, dtype=torch.int64).to(self.device)
         nbytes = int(call("moe_stack_workspace_bytes", self.H, self.I, self.E, self.K))
         self.ws = torch.zeros(nbytes, dtype=torch.uint8, device=self.device)
