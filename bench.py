@@ -10,10 +10,12 @@ reference's checkpoints are not available). For N > 1 (torchrun) every rank runs
 independent replica of the stack (the batch-1 resident decode path does not shard; expert
 parallelism is a different configuration), so per-GPU work is fixed: weak scaling.
 
-Prints one JSON line (rank 0). `value` is whole-job tokens/s from CUDA events around the
-timed steps (max over ranks); `e2e` is the same metric through DecodeStack.decode() with the
-hidden state copied from pinned host memory and the result copied back every step;
-`roofline` describes the dominant kernel (the gate/up expert GEMV), timed live here.
+The step is ONE launch of the persistent kernel (moe_stack_decode: all 28 layers inside,
+experts in the packed layout). Prints one JSON line (rank 0). `value` is whole-job tokens/s
+from CUDA events around the timed steps (max over ranks); `e2e` is the same metric through
+PersistentStack.decode() with the hidden state copied from pinned host memory and the
+result copied back every step; `roofline` is that kernel's algorithmic bytes per launch over
+its live launch time.
 """
 from __future__ import annotations
 
@@ -41,6 +43,8 @@ def parse():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--layers", type=int, default=0,
+                    help="profiling aid: run only the first N layers of the stack (0 = all 28)")
     return ap.parse_args()
 
 
@@ -183,69 +187,26 @@ def run_reference(args, rank: int, world: int) -> None:
 
 # ------------------------------------------------------------------------- GPU leg
 
-def gateup_kernel_roofline(layers, cfg, dev, hbm_peak: float, launches: int = 256) -> dict:
-    """Average duration of the dominant kernel (gate/up GEMV) over back-to-back launches on
-    rotating layers with random expert sets, timed with CUDA events on its stream."""
-    import torch
-
-    from moe_offload_b200 import ops
-    from moe_offload_b200.synthetic import dev_bf16_normal
-
-    E, H, I, K = cfg.experts, cfg.hidden, cfg.inter, cfg.top_k
-    gen = torch.Generator(device=dev)
-    gen.manual_seed(77)
-    x = dev_bf16_normal((1, H), dev, gen)
-    slots = [torch.randperm(E, device=dev, generator=gen)[:K].to(torch.int32).view(1, K) for _ in range(64)]
-    act = torch.empty((1, K, I), dtype=torch.bfloat16, device=dev)
-    L = len(layers)
-
-    def body():
-        for i in range(launches):
-            ly = layers[i % L]
-            ops.experts_gateup(x, slots[i % 64], ly.gate, ly.up, act=act)
-
-    st = torch.cuda.Stream(device=dev)
-    with torch.cuda.stream(st):
-        body()
-    st.synchronize()
-    g = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(g, stream=st):
-        body()
-    with torch.cuda.stream(st):
-        g.replay()
-        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        s.record(st)
-        g.replay()
-        e.record(st)
-    e.synchronize()
-    dur_s = s.elapsed_time(e) / 1000.0 / launches
-    algo = K * 2 * (I * H // 4 + 2 * 2 * I * (H // cfg.group_size))     # codes + fp16 scales/biases
-    achieved = algo / dur_s / 1e9
-    traffic = None
-    tp = os.path.join(ROOT, "profiles", "traffic.json")
-    if os.path.exists(tp):
-        try:
-            traffic = json.load(open(tp)).get("gateup_kernel_bytes_per_launch")
-        except Exception:
-            traffic = None
-    return {"kernel": "gateup_kernel (2-bit gate+up GEMV + SwiGLU, 10 experts)", "bound": "hbm",
-            "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s", "frac": round(achieved / hbm_peak, 4),
-            "traffic": traffic, "algorithmic_bytes_per_launch": algo, "launch_us": round(dur_s * 1e6, 3)}
+STACK_KERNEL = "stack_kernel (persistent: router + top-10 + 2-bit gate/up/down + combine, 28 layers)"
 
 
 def run_ours(args, rank: int, world: int, local_rank: int) -> None:
-    import numpy as np
     import torch
     import torch.distributed as dist
 
-    from moe_offload_b200.stack import DecodeStack
+    from moe_offload_b200.stack import PersistentStack
     from moe_offload_b200.synthetic import C1, dev_bf16_normal, dev_stack
 
     dev = torch.device("cuda", local_rank)
     torch.cuda.set_device(dev)
     cfg = C1
+    if args.layers:
+        import dataclasses
+        cfg = dataclasses.replace(cfg, name=f"{cfg.name}_first{args.layers}", layers=args.layers)
     layers = dev_stack(cfg, dev)
-    stack = DecodeStack(layers, cfg.top_k, dev)
+    stack = PersistentStack(layers, cfg.top_k, dev, release_unpacked=True)
+    del layers
+    torch.cuda.empty_cache()
     gen = torch.Generator(device=dev)
     gen.manual_seed(cfg.seed + 1000 * rank)
     n_in = args.warmup + args.steps
@@ -278,6 +239,8 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
         dist.all_reduce(tt, op=dist.ReduceOp.MAX)
         t_ms = float(tt.item())
     value = world * args.steps / (t_ms / 1000.0)
+    from moe_offload_b200 import _lib
+    dev_err = int(_lib.call("moe_device_error", 1))
 
     e2e = None
     if not args.no_e2e:
@@ -301,13 +264,25 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
             t2 = float(tt.item())
         e2e = {"value": round(world * args.steps / (t2 / 1000.0), 2), "unit": UNIT,
                "h2d_bytes_per_step": cfg.hidden * 2, "d2h_bytes_per_step": cfg.hidden * 2,
-               "api": "moe_offload_b200.stack.DecodeStack.decode (pinned host in/out, sync per step)"}
+               "api": "moe_offload_b200.stack.PersistentStack.decode (pinned host in/out, sync per step)"}
 
+    # roofline of the one kernel of the step: algorithmic bytes of a token (every routed
+    # expert's packed bytes + every router, 28 layers) over the step's device time (the
+    # kernel plus the 24 KB workspace clear before it)
     peak, peak_kind = peaks()
-    roof = gateup_kernel_roofline(layers, cfg, dev, peak)
-    roof["peak_source"] = peak_kind
     step_bytes = cfg.layers * (cfg.top_k * cfg.expert_bytes + cfg.router_bytes)
-    stack_gbs = step_bytes * args.steps / (t_ms / 1000.0) / 1e9
+    launch_s = t_ms / 1000.0 / args.steps
+    achieved = step_bytes / launch_s / 1e9
+    traffic = None
+    tp = os.path.join(ROOT, "profiles", "traffic.json")
+    if os.path.exists(tp):
+        try:
+            traffic = json.load(open(tp)).get("stack_kernel_bytes_per_launch")
+        except Exception:
+            traffic = None
+    roof = {"kernel": STACK_KERNEL, "bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+            "frac": round(achieved / peak, 4), "traffic": traffic, "algorithmic_bytes_per_launch": step_bytes,
+            "launch_us": round(launch_s * 1e6, 2), "peak_source": peak_kind}
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
@@ -320,12 +295,10 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
                 "config": {"workload": cfg.name, "layers": cfg.layers, "hidden": cfg.hidden, "experts": cfg.experts,
                            "top_k": cfg.top_k, "inter": cfg.inter, "batch": 1, "group_size": cfg.group_size,
                            "scales": "fp16", "router": "bf16", "parallelism": f"replicas x{world}",
+                           "layout": "packed experts (moe_pack_experts), transposed routers",
                            "l2": "inputs larger than L2: 707 MB of weights per step, 31.7 GB resident"},
-                "roofline": roof,
-                "stack_hbm": {"bytes_per_step": step_bytes, "achieved_gbs": round(stack_gbs, 1),
-                              "frac": round(stack_gbs / peak, 4)},
-                "clocks": clocks, "gpu_launches": stack.launches_per_step * args.steps,
-                "e2e": e2e, "cpu_baseline": cpu}
+                "roofline": roof, "clocks": clocks, "gpu_launches": stack.launches_per_step * args.steps,
+                "device_error": dev_err, "e2e": e2e, "cpu_baseline": cpu}
         print(json.dumps(line), flush=True)
 
 
