@@ -199,6 +199,109 @@ int moe_stack_decode(const void *layers, int L, int H, int I, int E, int K, int 
                      const void *x, void *y, uint32_t *inds_out, void *scores_out, void *hs_out,
                      void *workspace, size_t workspace_bytes, int num_ctas, void *stream);
 
+/* ------------------------------------------------------------------------------------ */
+/* Per-layer LRU expert-slot cache with its state on the GPU.                             */
+/* ------------------------------------------------------------------------------------ */
+
+/* Device bytes of one layer's cache state (E experts, cap slots; E <= 2048, cap <= E), 0 if
+ * invalid. Allocate 16-byte aligned device memory of this size per layer. */
+size_t moe_lru_state_bytes(int E, int cap);
+
+/* Initialises a layer's state: empty cache (free stack pops slots 0, 1, 2, ...), zero counters;
+ * expert_bytes is the unit of the byte counters. Replaces c_layer_init's cache part
+ * (mlx-qwen38/expert_io.c:497-520, reset 450-468). */
+int moe_lru_init(void *state, int E, int cap, uint64_t expert_bytes, void *stream);
+
+/* what = 0: empty the cache (expert_io.c:450-468); 1: zero the counters (470-495). */
+int moe_lru_reset(void *state, int E, int cap, int what, void *stream);
+
+/* One decode step (expert_io.c:583-676, c_layer_step_decode_ex): eids = device u32 [k]
+ * (the router's output, read in place), k <= 32 and k <= cap. Writes out_slots (device u32
+ * [k]) and out_miss = device i32 [1 + 2k] {n_miss, missing eids (request order) .., their
+ * slots ..}. Hit/prefetch-hit/miss counting against the last prefetch's snapshot, eviction
+ * from the LRU end skipping this step's experts, all as the reference. An eid >= E sets the
+ * device error word and writes n_miss = -1 without touching the cache. */
+int moe_lru_step(void *state, int E, int cap, const uint32_t *eids, int k, uint32_t *out_slots,
+                 int32_t *out_miss, void *stream);
+
+/* Router-driven prefetch (expert_io.c:527-581, c_layer_start_prefetch): pred = device i32 [n]
+ * (ranked predictions, n <= 64), 1 <= max_fetch <= 32. Writes out_fetch = device i32
+ * [1 + 2*max_fetch] {count, eids .., slots ..} of the experts to fill (inserted in reverse
+ * rank order). */
+int moe_lru_prefetch(void *state, int E, int cap, const int32_t *pred, int n, int max_fetch,
+                     int32_t *out_fetch, void *stream);
+
+/* out = device i32 [1 + 2*cap] {count, eids (LRU -> MRU) .., slots ..}
+ * (expert_io.c:726-747, c_layer_get_lru_state). */
+int moe_lru_get_state(void *state, int E, int cap, int32_t *out, void *stream);
+
+/* Rebuilds the cache from device arrays eids/slots [n] in LRU -> MRU order and adds to the
+ * prefill counters (expert_io.c:749-789, c_layer_set_lru_state). */
+int moe_lru_set_state(void *state, int E, int cap, const int32_t *eids, const int32_t *slots, int n,
+                      uint64_t add_req, uint64_t add_hits, uint64_t add_misses, void *stream);
+
+/* out18 = device u64 [18], the counters in c_layer_get_stats order (expert_io.c:791-812). */
+int moe_lru_get_stats(void *state, int E, int cap, uint64_t *out18, void *stream);
+
+/* counters[index] += value (the prefill byte accounting of c_layer_load_sync). */
+int moe_lru_add_stat(void *state, int E, int cap, int index, uint64_t value, void *stream);
+
+/* Fills the experts of a list {n, eids[stride], slots[stride]} (device memory, as written
+ * by moe_lru_step / moe_lru_prefetch) from a pinned host pool into device slot buffers, for
+ * ntensors (<= 9) per-expert row arrays: row e of tensor t at host_src[t] + e * row_bytes[t]
+ * goes to dev_dst[t] + slot * row_bytes[t]. A kernel reads the list and the mapped pinned
+ * pool (no host round trip). Replaces the pread pool (expert_io.c:113-356). host_src, dev_dst
+ * and row_bytes are host arrays; bases and row bytes 16-byte aligned. num_ctas 0 = all SMs. */
+int moe_fill_slots(const int32_t *list, int stride, int E, int cap, int ntensors,
+                   const void *const *host_src, void *const *dev_dst, const uint64_t *row_bytes,
+                   int num_ctas, void *stream);
+
+/* Same fill for a list in host memory: one cudaMemcpyAsync per (expert, tensor) on stream. */
+int moe_fill_slots_host(const int32_t *list_host, int stride, int E, int cap, int ntensors,
+                        const void *const *host_src, void *const *dev_dst, const uint64_t *row_bytes,
+                        void *stream);
+
+/* ------------------------------------------------------------------------------------ */
+/* The reference's expert cache C ABI, drop-in (mlx-qwen38/expert_io.c:428-852; the       */
+/* waits of cpp/third_party/expert_io.c:1048). Same names, signatures and conventions     */
+/* (one calling thread, layers 0..63, bad layer ids ignored); the cache state is on the   */
+/* GPU and expert bytes come from a pinned host pool by cudaMemcpyAsync.                  */
+/* ------------------------------------------------------------------------------------ */
+
+void c_io_init(int num_threads);
+/* fd and base_offsets are accepted and unused (no SSD shard): register the pinned host pool
+ * with c_layer_set_host_pool. E = 512 and a 1,536,000-byte counter unit, as the reference. */
+void c_layer_init(int layer_idx, int fd, int capacity, const uint64_t *base_offsets,
+                  const uint64_t *row_bytes, const uint64_t *base_ptrs, uint64_t slot_inds_ptr);
+/* Extension: any E, counter unit, tensor count, and the host pool at once. */
+int c_layer_init_ex(int layer_idx, int num_experts, int capacity, uint64_t expert_bytes, int ntensors,
+                    const uint64_t *row_bytes, const uint64_t *base_ptrs, const uint64_t *host_ptrs,
+                    uint64_t slot_inds_ptr);
+/* Extension: pinned host pool bases per tensor (row e of tensor t at host_ptrs[t] + e*row_bytes[t]). */
+void c_layer_set_host_pool(int layer_idx, const uint64_t *host_ptrs);
+void c_layer_reset_cache(int layer_idx);
+void c_layer_reset_stats(int layer_idx);
+void c_layer_wait_prefetch(int layer_idx);
+void c_layer_wait_demand(int layer_idx);
+void c_layer_start_prefetch(int layer_idx, const int32_t *pred_eids, int pred_count, int max_fetch);
+void c_layer_start_prefetch10(int layer_idx, int max_fetch, int32_t e0, int32_t e1, int32_t e2, int32_t e3,
+                              int32_t e4, int32_t e5, int32_t e6, int32_t e7, int32_t e8, int32_t e9);
+void c_layer_start_prefetch12(int layer_idx, int max_fetch, int32_t e0, int32_t e1, int32_t e2, int32_t e3,
+                              int32_t e4, int32_t e5, int32_t e6, int32_t e7, int32_t e8, int32_t e9,
+                              int32_t e10, int32_t e11);
+int c_layer_step_decode_ex(int layer_idx, const uint32_t *eids, int k, int async_io);
+int c_layer_step_decode(int layer_idx, const uint32_t *eids, int k);
+int c_layer_step_decode10(int layer_idx, uint32_t e0, uint32_t e1, uint32_t e2, uint32_t e3, uint32_t e4,
+                          uint32_t e5, uint32_t e6, uint32_t e7, uint32_t e8, uint32_t e9);
+int c_layer_step_decode10_async(int layer_idx, uint32_t e0, uint32_t e1, uint32_t e2, uint32_t e3,
+                                uint32_t e4, uint32_t e5, uint32_t e6, uint32_t e7, uint32_t e8, uint32_t e9);
+void c_layer_load_sync(int layer_idx, const int32_t *eids, const int32_t *slots, int count, int is_prefill);
+void c_layer_get_lru_state(int layer_idx, int32_t *out_eids, int32_t *out_slots, int *out_count);
+void c_layer_set_lru_state(int layer_idx, const int32_t *ordered_eids, const int32_t *ordered_slots, int count,
+                           uint64_t add_prefill_requests, uint64_t add_prefill_hits, uint64_t add_prefill_misses);
+void c_layer_get_stats(int layer_idx, uint64_t *out_stats);
+void c_get_decode_totals(int num_layers, uint64_t *out6);
+
 /*
  * Device-side error word (bit 1: a bounded mbarrier/flag wait gave up, bit 2: invalid
  * input seen by a kernel). Returns the current value (>= 0) and clears it when `clear`.

@@ -15,6 +15,8 @@ P = ctypes.c_void_p
 I = ctypes.c_int
 SZ = ctypes.c_size_t
 U64 = ctypes.c_uint64
+U32 = ctypes.c_uint32
+I32 = ctypes.c_int32
 
 _lock = threading.Lock()
 _lib = None
@@ -42,6 +44,38 @@ SIGNATURES: dict[str, tuple] = {
     "moe_decode_layer": (I, [P, I, I, I, I, I, P, P, I, P] + [P] * 9 + [I, I, P, P, P, P, P, P, P, SZ, P]),
     "moe_packed_expert_bytes": (SZ, [I, I]),
     "moe_pack_experts": (I, [I, I, I, P, P, P, P, P, P, P, P, P, P, P]),
+    "moe_lru_state_bytes": (SZ, [I, I]),
+    "moe_lru_init": (I, [P, I, I, U64, P]),
+    "moe_lru_reset": (I, [P, I, I, I, P]),
+    "moe_lru_step": (I, [P, I, I, P, I, P, P, P]),
+    "moe_lru_prefetch": (I, [P, I, I, P, I, I, P, P]),
+    "moe_lru_get_state": (I, [P, I, I, P, P]),
+    "moe_lru_set_state": (I, [P, I, I, P, P, I, U64, U64, U64, P]),
+    "moe_lru_get_stats": (I, [P, I, I, P, P]),
+    "moe_lru_add_stat": (I, [P, I, I, I, U64, P]),
+    "moe_fill_slots": (I, [P, I, I, I, I, P, P, P, I, P]),
+    "moe_fill_slots_host": (I, [P, I, I, I, I, P, P, P, P]),
+    # the reference's expert cache C ABI (void functions: restype None)
+    "c_io_init": (None, [I]),
+    "c_layer_init": (None, [I, I, I, P, P, P, U64]),
+    "c_layer_init_ex": (I, [I, I, I, U64, I, P, P, P, U64]),
+    "c_layer_set_host_pool": (None, [I, P]),
+    "c_layer_reset_cache": (None, [I]),
+    "c_layer_reset_stats": (None, [I]),
+    "c_layer_wait_prefetch": (None, [I]),
+    "c_layer_wait_demand": (None, [I]),
+    "c_layer_start_prefetch": (None, [I, P, I, I]),
+    "c_layer_start_prefetch10": (None, [I, I] + [I32] * 10),
+    "c_layer_start_prefetch12": (None, [I, I] + [I32] * 12),
+    "c_layer_step_decode_ex": (I, [I, P, I, I]),
+    "c_layer_step_decode": (I, [I, P, I]),
+    "c_layer_step_decode10": (I, [I] + [U32] * 10),
+    "c_layer_step_decode10_async": (I, [I] + [U32] * 10),
+    "c_layer_load_sync": (None, [I, P, P, I, I]),
+    "c_layer_get_lru_state": (None, [I, P, P, P]),
+    "c_layer_set_lru_state": (None, [I, P, P, I, U64, U64, U64]),
+    "c_layer_get_stats": (None, [I, P]),
+    "c_get_decode_totals": (None, [I, P]),
     "moe_stack_workspace_bytes": (SZ, [I, I, I, I]),
     "moe_stack_decode": (I, [P, I, I, I, I, I, I, I, P, P, P, P, P, P, SZ, I, P]),
 }

@@ -1,0 +1,474 @@
+// Per-layer LRU expert-slot cache with its state in device memory.
+//
+// Semantics are those of the reference's host-side cache (mlx-qwen38/expert_io.c): a doubly
+// linked list over slots (head = least recently used), eid -> slot and slot -> eid tables, a
+// free stack that pops slots 0, 1, 2, ... after a reset, eviction that walks from the head
+// skipping protected experts (falling back to the head), demand steps that count LRU hits,
+// prefetch hits and demand misses against a residency snapshot taken by the last prefetch,
+// and prefetches that take the first <= max_fetch missing predictions in rank order and
+// insert them in reverse rank order. Every operation is inherently sequential (each
+// allocation depends on the list state the previous one left), so one thread runs it on a
+// shared-memory copy of the layer's state: one launch per call, no host round trip, the
+// router's indices read where the router wrote them.
+//
+// Device state of one layer (moe_lru_state_bytes): a header, then int16 tables and u64
+// bitmaps sized by E and cap, then 18 u64 counters in the order of c_layer_get_stats
+// (expert_io.c:791-812).
+#include <algorithm>
+
+#include "common.cuh"
+
+namespace {
+
+constexpr int kLruMaxE = 2048;
+constexpr int kLruMaxK = 32;        // experts per demand step
+constexpr int kLruMaxPred = 64;     // predictions per prefetch call
+constexpr int kLruThreads = 128;
+
+struct LruHeader {
+    int32_t E, cap, head, tail, free_count, has_snap, pad0, pad1;
+    uint64_t expert_bytes;
+};
+
+struct LruLayout {
+    size_t e2s, s2e, prev, next, freel, pre, pred, fet, stats, total;
+    MOE_HD LruLayout(int E, int cap) {
+        const size_t nb = (size_t)(E + 63) / 64;
+        e2s = sizeof(LruHeader);
+        s2e = al16(e2s + (size_t)E * 2);
+        prev = al16(s2e + (size_t)cap * 2);
+        next = al16(prev + (size_t)cap * 2);
+        freel = al16(next + (size_t)cap * 2);
+        pre = al16(freel + (size_t)cap * 2);
+        pred = pre + nb * 8;
+        fet = pred + nb * 8;
+        stats = fet + nb * 8;
+        total = al16(stats + 18 * 8);
+    }
+};
+
+enum Stat {
+    kDecReq = 0, kDecLruHits, kDecPrefHits, kDecMiss, kDecMissBytes, kDecPrefBytes,
+    kPreReq, kPreHits, kPreMiss, kPreMissBytes, kPredHits, kPredActual, kPredTotal,
+    kMissPrefHits, kMissPrefActualMisses, kMissPrefFetched, kUncoalesced, kCoalesced
+};
+
+// Shared-memory view of one layer's state; loaded and stored by the whole block, operated
+// on by thread 0.
+struct Lru {
+    LruHeader *h;
+    int16_t *e2s, *s2e, *prev, *next, *freel;
+    uint64_t *pre, *pred, *fet, *stats;
+    int nb;
+
+    MOE_D void bind(unsigned char *base, int E, int cap) {
+        const LruLayout Ly(E, cap);
+        h = reinterpret_cast<LruHeader *>(base);
+        e2s = reinterpret_cast<int16_t *>(base + Ly.e2s);
+        s2e = reinterpret_cast<int16_t *>(base + Ly.s2e);
+        prev = reinterpret_cast<int16_t *>(base + Ly.prev);
+        next = reinterpret_cast<int16_t *>(base + Ly.next);
+        freel = reinterpret_cast<int16_t *>(base + Ly.freel);
+        pre = reinterpret_cast<uint64_t *>(base + Ly.pre);
+        pred = reinterpret_cast<uint64_t *>(base + Ly.pred);
+        fet = reinterpret_cast<uint64_t *>(base + Ly.fet);
+        stats = reinterpret_cast<uint64_t *>(base + Ly.stats);
+        nb = (E + 63) / 64;
+    }
+
+    MOE_D void remove(int s) {
+        const int p = prev[s], n = next[s];
+        if (p >= 0) next[p] = (int16_t)n; else h->head = n;
+        if (n >= 0) prev[n] = (int16_t)p; else h->tail = p;
+        prev[s] = -1;
+        next[s] = -1;
+    }
+    MOE_D void append_mru(int s) {
+        prev[s] = (int16_t)h->tail;
+        next[s] = -1;
+        if (h->tail >= 0) next[h->tail] = (int16_t)s; else h->head = s;
+        h->tail = s;
+    }
+    MOE_D void move_to_mru(int s) {
+        if (h->tail == s) return;
+        remove(s);
+        append_mru(s);
+    }
+    MOE_D void insert(int eid, int s) {
+        if (e2s[eid] >= 0) {
+            move_to_mru(e2s[eid]);
+            return;
+        }
+        e2s[eid] = (int16_t)s;
+        s2e[s] = (int16_t)eid;
+        append_mru(s);
+    }
+    MOE_D static bool has(const uint64_t *bm, int e) { return (bm[e >> 6] >> (e & 63)) & 1ull; }
+    MOE_D int alloc(const uint64_t *prot) {
+        if (h->free_count > 0) return freel[--h->free_count];
+        for (int cur = h->head; cur >= 0; cur = next[cur]) {
+            const int eid = s2e[cur];
+            if (eid >= 0 && !has(prot, eid)) {
+                remove(cur);
+                e2s[eid] = -1;
+                s2e[cur] = -1;
+                return cur;
+            }
+        }
+        const int victim = h->head;             // every resident expert is protected: the oldest goes
+        const int eid = s2e[victim];
+        remove(victim);
+        if (eid >= 0) e2s[eid] = -1;
+        s2e[victim] = -1;
+        return victim;
+    }
+    MOE_D void reset_tables() {
+        for (int i = 0; i < h->E; ++i) e2s[i] = -1;
+        for (int i = 0; i < h->cap; ++i) s2e[i] = prev[i] = next[i] = -1;
+        h->head = h->tail = -1;
+        h->has_snap = 0;
+    }
+};
+
+// whole-block copy of the state between global and shared memory (16-byte multiples)
+MOE_D void copy16(void *dst, const void *src, size_t bytes) {
+    uint4 *d = reinterpret_cast<uint4 *>(dst);
+    const uint4 *s = reinterpret_cast<const uint4 *>(src);
+    for (size_t i = threadIdx.x; i < bytes / 16; i += blockDim.x) d[i] = s[i];
+}
+
+enum Op { kOpReset = 0, kOpResetStats, kOpStep, kOpPrefetch, kOpGetState, kOpSetState, kOpStats, kOpAddStat };
+
+struct LruArgs {
+    unsigned char *state;
+    int E, cap, op;
+    const uint32_t *eids;      // step: [k] (device)   prefetch: [n] predictions   set: [n] ordered eids
+    const int32_t *slots_in;   // set: [n] ordered slots
+    int n;                     // k / prediction count / set count (when count_dev is null)
+    const int32_t *count_dev;  // set: count on the device (optional)
+    int max_fetch;
+    uint32_t *out_slots;       // step: [k] slot per expert
+    int32_t *out_list;         // step: [1 + 2*k] {n_miss, eids.., slots..}; prefetch: [1 + 2*max] fetched
+                               // get: [1 + 2*cap] {count, eids (LRU->MRU).., slots..}
+    uint64_t *out_stats;       // stats: [18]
+    uint64_t add_req, add_hits, add_misses;
+};
+
+__global__ void __launch_bounds__(kLruThreads) lru_kernel(LruArgs a) {
+    extern __shared__ __align__(16) unsigned char sm[];
+    const LruLayout Ly(a.E, a.cap);
+    copy16(sm, a.state, Ly.total);
+    __syncthreads();
+    Lru L;
+    L.bind(sm, a.E, a.cap);
+    if (threadIdx.x == 0) {
+        LruHeader *h = L.h;
+        const int E = a.E;
+        switch (a.op) {
+            case kOpReset: {     // expert_io.c:450-468
+                L.reset_tables();
+                h->free_count = h->cap;
+                for (int i = 0; i < h->cap; ++i) L.freel[i] = (int16_t)(h->cap - 1 - i);
+                break;
+            }
+            case kOpResetStats: {   // expert_io.c:470-495
+                for (int i = 0; i < 18; ++i) L.stats[i] = 0;
+                break;
+            }
+            case kOpStep: {      // expert_io.c:583-676
+                const int k = a.n;
+                L.stats[kDecReq] += (uint64_t)k;
+                uint64_t act[kLruMaxE / 64];
+                for (int b = 0; b < L.nb; ++b) act[b] = 0;
+                bool bad = false;
+                for (int i = 0; i < k; ++i) {
+                    const uint32_t e = a.eids[i];
+                    if (e >= (uint32_t)E) { bad = true; continue; }
+                    act[e >> 6] |= 1ull << (e & 63);
+                }
+                if (bad) {
+                    atomicOr(&g_moe_device_error, MOE_DEVERR_BAD_INPUT);
+                    a.out_list[0] = -1;
+                    break;
+                }
+                int miss_e[kLruMaxK], miss_s[kLruMaxK], nm = 0;
+                if (h->has_snap) {
+                    uint64_t ov = 0, ta = 0, tp = 0, mh = 0, tam = 0, tf = 0;
+                    for (int b = 0; b < L.nb; ++b) {
+                        const uint64_t am = act[b] & ~L.pre[b];
+                        ov += __popcll(act[b] & L.pred[b]);
+                        ta += __popcll(act[b]);
+                        tp += __popcll(L.pred[b]);
+                        mh += __popcll(am & L.fet[b]);
+                        tam += __popcll(am);
+                        tf += __popcll(L.fet[b]);
+                    }
+                    L.stats[kPredHits] += ov;
+                    L.stats[kPredActual] += ta;
+                    L.stats[kPredTotal] += tp;
+                    L.stats[kMissPrefHits] += mh;
+                    L.stats[kMissPrefActualMisses] += tam;
+                    L.stats[kMissPrefFetched] += tf;
+                    for (int i = 0; i < k; ++i) {
+                        const int e = (int)a.eids[i];
+                        if (L.e2s[e] >= 0) {
+                            if (Lru::has(L.pre, e)) ++L.stats[kDecLruHits];
+                            else ++L.stats[kDecPrefHits];
+                        } else {
+                            ++L.stats[kDecMiss];
+                            miss_e[nm++] = e;
+                        }
+                    }
+                    h->has_snap = 0;
+                } else {
+                    for (int i = 0; i < k; ++i) {
+                        const int e = (int)a.eids[i];
+                        if (L.e2s[e] >= 0) {
+                            ++L.stats[kDecLruHits];
+                        } else {
+                            ++L.stats[kDecMiss];
+                            miss_e[nm++] = e;
+                        }
+                    }
+                }
+                for (int i = 0; i < nm; ++i) {
+                    const int s = L.alloc(act);
+                    L.insert(miss_e[i], s);
+                    miss_s[i] = s;
+                }
+                L.stats[kDecMissBytes] += (uint64_t)nm * h->expert_bytes;
+                for (int i = 0; i < k; ++i) {
+                    const int s = L.e2s[a.eids[i]];
+                    L.move_to_mru(s);
+                    a.out_slots[i] = (uint32_t)s;
+                }
+                a.out_list[0] = nm;
+                for (int i = 0; i < nm; ++i) {
+                    a.out_list[1 + i] = miss_e[i];
+                    a.out_list[1 + k + i] = miss_s[i];
+                }
+                break;
+            }
+            case kOpPrefetch: {  // expert_io.c:527-581
+                for (int b = 0; b < L.nb; ++b) {
+                    L.pre[b] = 0;
+                    L.pred[b] = 0;
+                    L.fet[b] = 0;
+                }
+                for (int e = 0; e < E; ++e)
+                    if (L.e2s[e] >= 0) L.pre[e >> 6] |= 1ull << (e & 63);
+                h->has_snap = 1;
+                uint64_t prot[kLruMaxE / 64];
+                for (int b = 0; b < L.nb; ++b) prot[b] = 0;
+                const int cap_fetch = (a.max_fetch > 0 && a.max_fetch < 32) ? a.max_fetch : 32;
+                int miss[32], nm = 0;
+                for (int i = 0; i < a.n; ++i) {
+                    const int32_t e = (int32_t)a.eids[i];
+                    if (e < 0 || e >= E) continue;
+                    L.pred[e >> 6] |= 1ull << (e & 63);
+                    prot[e >> 6] |= 1ull << (e & 63);
+                    if (L.e2s[e] < 0 && nm < cap_fetch) {
+                        miss[nm++] = e;
+                        L.fet[e >> 6] |= 1ull << (e & 63);
+                    }
+                }
+                a.out_list[0] = nm;
+                for (int i = 0; i < nm; ++i) {      // reverse rank order: the best prediction is newest
+                    const int e = miss[nm - 1 - i];
+                    const int s = L.alloc(prot);
+                    L.insert(e, s);
+                    a.out_list[1 + i] = e;
+                    a.out_list[1 + a.max_fetch + i] = s;
+                }
+                L.stats[kDecPrefBytes] += (uint64_t)nm * h->expert_bytes;
+                break;
+            }
+            case kOpGetState: {  // expert_io.c:726-747
+                int cnt = 0;
+                for (int cur = h->head; cur >= 0; cur = L.next[cur]) {
+                    a.out_list[1 + cnt] = L.s2e[cur];
+                    a.out_list[1 + a.cap + cnt] = cur;
+                    ++cnt;
+                }
+                a.out_list[0] = cnt;
+                break;
+            }
+            case kOpSetState: {  // expert_io.c:749-789
+                const int cnt = a.count_dev ? *a.count_dev : a.n;
+                L.stats[kPreReq] += a.add_req;
+                L.stats[kPreHits] += a.add_hits;
+                L.stats[kPreMiss] += a.add_misses;
+                L.reset_tables();
+                uint8_t used[kLruMaxE];
+                for (int s = 0; s < h->cap; ++s) used[s] = 0;
+                bool bad = cnt < 0 || cnt > h->cap;
+                for (int i = 0; i < cnt && !bad; ++i) {
+                    const int e = (int)a.eids[i], s = a.slots_in[i];
+                    if (e < 0 || e >= E || s < 0 || s >= h->cap) { bad = true; break; }
+                    used[s] = 1;
+                    L.insert(e, s);
+                }
+                if (bad) atomicOr(&g_moe_device_error, MOE_DEVERR_BAD_INPUT);
+                h->free_count = 0;
+                for (int s = h->cap - 1; s >= 0; --s)
+                    if (!used[s]) L.freel[h->free_count++] = (int16_t)s;
+                break;
+            }
+            case kOpStats: {
+                for (int i = 0; i < 18; ++i) a.out_stats[i] = L.stats[i];
+                break;
+            }
+            case kOpAddStat: {   // counter a.n += a.add_req (prefill accounting of c_layer_load_sync)
+                if (a.n >= 0 && a.n < 18) L.stats[a.n] += a.add_req;
+                break;
+            }
+        }
+    }
+    __syncthreads();
+    if (a.op != kOpGetState && a.op != kOpStats) copy16(a.state, sm, Ly.total);
+}
+
+int lru_launch(LruArgs a, void *stream) {
+    if (!a.state) return moe_set_error(MOE_EINVAL, "lru: null state");
+    const LruLayout Ly(a.E, a.cap);
+    MOE_CUDA_TRY(cudaFuncSetAttribute(lru_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)Ly.total));
+    lru_kernel<<<1, kLruThreads, Ly.total, as_stream(stream)>>>(a);
+    MOE_CUDA_TRY(cudaGetLastError());
+    return MOE_OK;
+}
+
+int check_dims(int E, int cap) {
+    if (E <= 0 || E > kLruMaxE || cap <= 0 || cap > E || cap > 32767)
+        return moe_set_error(MOE_EINVAL, "lru: bad sizes E=%d cap=%d", E, cap);
+    return MOE_OK;
+}
+
+// host-side header written by moe_lru_init
+__global__ void lru_header_kernel(unsigned char *state, int E, int cap, uint64_t expert_bytes) {
+    LruHeader *h = reinterpret_cast<LruHeader *>(state);
+    h->E = E;
+    h->cap = cap;
+    h->expert_bytes = expert_bytes;
+}
+
+}  // namespace
+
+extern "C" size_t moe_lru_state_bytes(int E, int cap) {
+    if (E <= 0 || E > kLruMaxE || cap <= 0 || cap > E) return 0;
+    return LruLayout(E, cap).total;
+}
+
+extern "C" int moe_lru_init(void *state, int E, int cap, uint64_t expert_bytes, void *stream) {
+    if (int rc = check_dims(E, cap)) return rc;
+    if (!state || reinterpret_cast<uintptr_t>(state) % 16)
+        return moe_set_error(MOE_EINVAL, "lru_init: state must be a 16-byte aligned device pointer");
+    MOE_CUDA_TRY(cudaMemsetAsync(state, 0, LruLayout(E, cap).total, as_stream(stream)));
+    lru_header_kernel<<<1, 1, 0, as_stream(stream)>>>(static_cast<unsigned char *>(state), E, cap, expert_bytes);
+    MOE_CUDA_TRY(cudaGetLastError());
+    LruArgs a{};
+    a.state = static_cast<unsigned char *>(state);
+    a.E = E;
+    a.cap = cap;
+    a.op = kOpReset;
+    return lru_launch(a, stream);
+}
+
+extern "C" int moe_lru_reset(void *state, int E, int cap, int what, void *stream) {
+    if (int rc = check_dims(E, cap)) return rc;
+    LruArgs a{};
+    a.state = static_cast<unsigned char *>(state);
+    a.E = E;
+    a.cap = cap;
+    a.op = what == 1 ? kOpResetStats : kOpReset;
+    return lru_launch(a, stream);
+}
+
+extern "C" int moe_lru_step(void *state, int E, int cap, const uint32_t *eids, int k, uint32_t *out_slots,
+                            int32_t *out_miss, void *stream) {
+    if (int rc = check_dims(E, cap)) return rc;
+    if (k <= 0 || k > kLruMaxK || k > cap || !eids || !out_slots || !out_miss)
+        return moe_set_error(MOE_EINVAL, "lru_step: bad arguments (k=%d cap=%d)", k, cap);
+    LruArgs a{};
+    a.state = static_cast<unsigned char *>(state);
+    a.E = E;
+    a.cap = cap;
+    a.op = kOpStep;
+    a.eids = eids;
+    a.n = k;
+    a.out_slots = out_slots;
+    a.out_list = out_miss;
+    return lru_launch(a, stream);
+}
+
+extern "C" int moe_lru_prefetch(void *state, int E, int cap, const int32_t *pred, int n, int max_fetch,
+                                int32_t *out_fetch, void *stream) {
+    if (int rc = check_dims(E, cap)) return rc;
+    if (n < 0 || n > kLruMaxPred || (n > 0 && !pred) || !out_fetch || max_fetch <= 0 || max_fetch > 32)
+        return moe_set_error(MOE_EINVAL, "lru_prefetch: bad arguments (n=%d max_fetch=%d)", n, max_fetch);
+    LruArgs a{};
+    a.state = static_cast<unsigned char *>(state);
+    a.E = E;
+    a.cap = cap;
+    a.op = kOpPrefetch;
+    a.eids = reinterpret_cast<const uint32_t *>(pred);
+    a.n = n;
+    a.max_fetch = max_fetch;
+    a.out_list = out_fetch;
+    return lru_launch(a, stream);
+}
+
+extern "C" int moe_lru_get_state(void *state, int E, int cap, int32_t *out, void *stream) {
+    if (int rc = check_dims(E, cap)) return rc;
+    if (!out) return moe_set_error(MOE_EINVAL, "lru_get_state: null output");
+    LruArgs a{};
+    a.state = static_cast<unsigned char *>(state);
+    a.E = E;
+    a.cap = cap;
+    a.op = kOpGetState;
+    a.out_list = out;
+    return lru_launch(a, stream);
+}
+
+extern "C" int moe_lru_set_state(void *state, int E, int cap, const int32_t *eids, const int32_t *slots, int n,
+                                 uint64_t add_req, uint64_t add_hits, uint64_t add_misses, void *stream) {
+    if (int rc = check_dims(E, cap)) return rc;
+    if (n < 0 || n > cap || (n > 0 && (!eids || !slots)))
+        return moe_set_error(MOE_EINVAL, "lru_set_state: bad arguments (n=%d cap=%d)", n, cap);
+    LruArgs a{};
+    a.state = static_cast<unsigned char *>(state);
+    a.E = E;
+    a.cap = cap;
+    a.op = kOpSetState;
+    a.eids = reinterpret_cast<const uint32_t *>(eids);
+    a.slots_in = slots;
+    a.n = n;
+    a.add_req = add_req;
+    a.add_hits = add_hits;
+    a.add_misses = add_misses;
+    return lru_launch(a, stream);
+}
+
+extern "C" int moe_lru_get_stats(void *state, int E, int cap, uint64_t *out18, void *stream) {
+    if (int rc = check_dims(E, cap)) return rc;
+    if (!out18) return moe_set_error(MOE_EINVAL, "lru_get_stats: null output");
+    LruArgs a{};
+    a.state = static_cast<unsigned char *>(state);
+    a.E = E;
+    a.cap = cap;
+    a.op = kOpStats;
+    a.out_stats = out18;
+    return lru_launch(a, stream);
+}
+
+extern "C" int moe_lru_add_stat(void *state, int E, int cap, int index, uint64_t value, void *stream) {
+    if (int rc = check_dims(E, cap)) return rc;
+    if (index < 0 || index >= 18) return moe_set_error(MOE_EINVAL, "lru_add_stat: counter %d", index);
+    LruArgs a{};
+    a.state = static_cast<unsigned char *>(state);
+    a.E = E;
+    a.cap = cap;
+    a.op = kOpAddStat;
+    a.n = index;
+    a.add_req = value;
+    return lru_launch(a, stream);
+}

@@ -1,0 +1,391 @@
+"""Offload path: per-layer LRU expert-slot caches on the GPU filled from a pinned host pool
+The reference's surface, B200-native underneath:
+
+  compute_layer_capacities  mlx-qwen38/loader.py:245-303 (same rule, parametrised sizes)
+  CachedSwitchGLU           loader.py:306-748: slot buffers in HBM, the LRU state on the GPU
+                            (moe_lru_*), demand fills by a kernel reading the miss list where
+                            the LRU kernel wrote it (moe_fill_slots), prefetches on a side
+                            stream; __call__ returns the unweighted [B, L, K, H] expert outputs
+  OffloadStack              the decode loop of OffloadEngine.generate_greedy
+                            (loader.py:1125-1244) over the synthetic stack: layer 0 pinned,
+                            layers 1.. cached, router-driven next-layer prefetch
+
+No step reads anything back to the host: router -> LRU step -> fill -> experts -> prefetch
+is stream-ordered on the device (the reference synchronises on the router's indices every
+layer, loader.py:958).
+"""
+from __future__ import annotations
+
+import math
+
+import numpy as np
+import torch
+
+from . import ops
+from ._lib import call
+from .ops import QMatrix
+from .synthetic import ExpertLayer
+
+# the reference's compile-time model constants (expert_io.c:18-23, loader.py:77-84)
+NUM_LAYERS_REF = 48
+NUM_EXPERTS_REF = 512
+EXPERT_BYTES_REF = 1_536_000
+
+STAT_NAMES = ["decode_requests", "decode_lru_hits", "decode_prefetch_hits", "decode_demand_misses",
+              "decode_demand_bytes", "decode_prefetch_bytes", "prefill_requests", "prefill_lru_hits",
+              "prefill_demand_misses", "prefill_demand_bytes", "pred_top16_hits", "pred_top16_total_actual",
+              "pred_top16_total_pred", "miss_pref_hits", "miss_pref_total_actual_misses",
+              "miss_pref_total_fetched", "uncoalesced_tensor_reads", "coalesced_preadv_calls"]
+
+
+def compute_layer_capacities(budget_gb: float | None = None, budget_pct: float | None = None,
+                             alloc_mode: str = "even", *, num_layers: int = NUM_LAYERS_REF,
+                             num_experts: int = NUM_EXPERTS_REF, expert_bytes: int = EXPERT_BYTES_REF,
+                             weights=None) -> dict[int, int]:
+    """Slots per cached layer 1..num_layers-1 (layer 0 is pinned), as loader.py:245-303.
+
+    budget_pct (a percentage, or a fraction <= 1) of num_experts per layer, else budget_gb
+    (decimal GB, default 7.5) over all cached layers; 'even' splits the total equally (the
+    first layers get the remainder), 'proportional' by `weights` (the reference reads the
+    per-layer active-expert counts of its analysis_summary.json; without weights it falls
+    back to 'even', as the reference does when that file is absent). Clamped to [16, E]."""
+    n = num_layers - 1
+    if budget_pct is not None:
+        frac = budget_pct / 100.0 if budget_pct > 1.0 else budget_pct
+        per_layer = max(16, min(num_experts, round(frac * num_experts)))
+        total = n * per_layer
+    else:
+        if budget_gb is None:
+            budget_gb = 7.5
+        total = int(round((budget_gb * 1e9) / expert_bytes))
+        total = max(n * 16, min(n * num_experts, total))
+    if alloc_mode == "proportional" and weights is not None:
+        w = np.asarray(weights, dtype=np.float64)
+        if w.shape != (n,):
+            raise ValueError(f"weights must have {n} entries (layers 1..{num_layers - 1})")
+        raw = w / w.sum() * total
+        caps = np.clip(np.floor(raw).astype(int), 16, num_experts)
+        rem = total - int(caps.sum())
+        fr = raw - np.floor(raw)
+        if rem > 0:
+            for i in np.argsort(-fr):
+                if rem == 0:
+                    break
+                if caps[i] < num_experts:
+                    caps[i] += 1
+                    rem -= 1
+        elif rem < 0:
+            for i in np.argsort(fr):
+                if rem == 0:
+                    break
+                if caps[i] > 16:
+                    caps[i] -= 1
+                    rem += 1
+        return {il: int(caps[il - 1]) for il in range(1, num_layers)}
+    base, rem = divmod(total, n)
+    return {il: min(num_experts, max(16, base + (1 if (il - 1) < rem else 0))) for il in range(1, num_layers)}
+
+
+class HostExpertPool:
+    """One layer's E experts in pinned host memory, MLX layout: the nine per-expert row arrays
+    (gate/up/down codes, scales, biases). Replaces the reference's experts-XX.safetensors
+    shard read with pread (loader.py:318-366)."""
+
+    NAMES = ("gate.w", "gate.s", "gate.b", "up.w", "up.s", "up.b", "down.w", "down.s", "down.b")
+
+    def __init__(self, tensors: list[torch.Tensor], bits: int = 2, group_size: int = 64):
+        if len(tensors) != 9:
+            raise ValueError("nine tensors expected")
+        self.t = [t if t.is_pinned() else t.pin_memory() for t in tensors]
+        self.E = self.t[0].shape[0]
+        self.bits, self.group_size = bits, group_size
+        self.row_bytes = [t[0].numel() * t.element_size() for t in self.t]
+        self.expert_bytes = sum(self.row_bytes)
+
+    @classmethod
+    def from_layer(cls, layer: ExpertLayer) -> "HostExpertPool":
+        ts = []
+        for q in (layer.gate, layer.up, layer.down):
+            ts += [q.w.cpu(), q.s.cpu(), q.b.cpu()]
+        return cls(ts, layer.gate.bits, layer.gate.group_size)
+
+    def empty_slots(self, cap: int, device) -> list[torch.Tensor]:
+        return [torch.empty((cap,) + tuple(t.shape[1:]), dtype=t.dtype, device=device) for t in self.t]
+
+
+class CachedSwitchGLU:
+    """LRU-cached routed experts of one layer (reference CachedSwitchGLU, loader.py:306-748)."""
+
+    def __init__(self, layer_idx: int, capacity: int, pool: HostExpertPool, device, top_k: int,
+                 expert_bytes: int | None = None, prefetch_stream: torch.cuda.Stream | None = None):
+        self.layer_idx = layer_idx
+        self.capacity = int(capacity)
+        self.pool = pool
+        self.device = torch.device(device)
+        self.E = pool.E
+        self.K = top_k
+        if not (0 < top_k <= self.capacity <= self.E):
+            raise ValueError(f"need 0 < K={top_k} <= capacity={capacity} <= E={self.E}")
+        self.expert_bytes = int(expert_bytes or pool.expert_bytes)
+        sl = pool.empty_slots(self.capacity, self.device)
+        self.slots = sl
+        self.gate = QMatrix(sl[0], sl[1], sl[2], pool.bits, pool.group_size)
+        self.up = QMatrix(sl[3], sl[4], sl[5], pool.bits, pool.group_size)
+        self.down = QMatrix(sl[6], sl[7], sl[8], pool.bits, pool.group_size)
+        nbytes = int(call("moe_lru_state_bytes", self.E, self.capacity))
+        self.state = torch.empty(nbytes, dtype=torch.uint8, device=self.device)
+        self._slot_inds_buf = torch.zeros((1, 1, top_k), dtype=torch.int32, device=self.device)
+        self._miss = torch.zeros(1 + 2 * top_k, dtype=torch.int32, device=self.device)
+        self._pref = torch.zeros(1 + 2 * 32, dtype=torch.int32, device=self.device)
+        import ctypes
+        self._src = (ctypes.c_void_p * 9)(*[t.data_ptr() for t in pool.t])
+        self._dst = (ctypes.c_void_p * 9)(*[t.data_ptr() for t in sl])
+        self._rows = (ctypes.c_uint64 * 9)(*pool.row_bytes)
+        self.pstream = prefetch_stream or torch.cuda.Stream(device=self.device)
+        self._pevent = torch.cuda.Event()
+        self._pending = False
+        self._act = torch.empty((1, top_k, self.gate.w.shape[1]), dtype=torch.bfloat16, device=self.device)
+        call("moe_lru_init", self.state.data_ptr(), self.E, self.capacity, self.expert_bytes, self._cs())
+
+    def _cs(self, stream=None) -> int:
+        return (stream or torch.cuda.current_stream(self.device)).cuda_stream
+
+    # ---------------------------------------------------------------- cache management
+    def reset_cache(self) -> None:
+        self.wait_prefetch()
+        call("moe_lru_reset", self.state.data_ptr(), self.E, self.capacity, 0, self._cs())
+
+    def reset_stats(self) -> None:
+        self.wait_prefetch()
+        call("moe_lru_reset", self.state.data_ptr(), self.E, self.capacity, 1, self._cs())
+
+    def get_lru_state(self) -> tuple[list[int], list[int]]:
+        """(eids, slots) from least to most recently used (c_layer_get_lru_state)."""
+        self.wait_prefetch()
+        out = torch.empty(1 + 2 * self.capacity, dtype=torch.int32, device=self.device)
+        call("moe_lru_get_state", self.state.data_ptr(), self.E, self.capacity, out.data_ptr(), self._cs())
+        o = out.cpu().tolist()
+        n = o[0]
+        return o[1:1 + n], o[1 + self.capacity:1 + self.capacity + n]
+
+    def set_lru_state(self, eids, slots, add_requests: int = 0, add_hits: int = 0, add_misses: int = 0) -> None:
+        self.wait_prefetch()
+        e = torch.tensor(list(eids), dtype=torch.int32).to(self.device)
+        s = torch.tensor(list(slots), dtype=torch.int32).to(self.device)
+        call("moe_lru_set_state", self.state.data_ptr(), self.E, self.capacity, e.data_ptr(), s.data_ptr(),
+             len(e), add_requests, add_hits, add_misses, self._cs())
+        torch.cuda.current_stream(self.device).synchronize()
+
+    def raw_stats(self) -> list[int]:
+        self.wait_prefetch()
+        out = torch.empty(18, dtype=torch.int64, device=self.device)
+        call("moe_lru_get_stats", self.state.data_ptr(), self.E, self.capacity, out.data_ptr(), self._cs())
+        return [int(v) for v in out.cpu().tolist()]
+
+    def sync_stats_from_c(self) -> None:
+        for name, v in zip(STAT_NAMES, self.raw_stats()):
+            setattr(self, name, v)
+
+    def get_layer_stats(self) -> dict:
+        """The reference's per-layer stats dict (loader.py:701-739)."""
+        self.sync_stats_from_c()
+        dr = max(1, self.decode_requests)
+        pr = max(1, self.prefill_requests)
+        return {
+            "layer": self.layer_idx, "capacity_experts": self.capacity,
+            "capacity_mb": round(self.capacity * self.expert_bytes / 1e6, 3),
+            "decode_requests": self.decode_requests, "decode_lru_hits": self.decode_lru_hits,
+            "decode_prefetch_hits": self.decode_prefetch_hits, "decode_demand_misses": self.decode_demand_misses,
+            "decode_pure_hit_rate": round(self.decode_lru_hits / dr, 5),
+            "decode_effective_hit_rate": round((self.decode_lru_hits + self.decode_prefetch_hits) / dr, 5),
+            "decode_demand_bytes": self.decode_demand_bytes, "decode_prefetch_bytes": self.decode_prefetch_bytes,
+            "decode_total_bytes": self.decode_demand_bytes + self.decode_prefetch_bytes,
+            "prefill_requests": self.prefill_requests, "prefill_lru_hits": self.prefill_lru_hits,
+            "prefill_demand_misses": self.prefill_demand_misses,
+            "prefill_hit_rate": round(self.prefill_lru_hits / pr, 5),
+            "prefill_demand_bytes": self.prefill_demand_bytes,
+            "top16_router_recall": round(self.pred_top16_hits / max(1, self.pred_top16_total_actual), 5),
+            "top16_router_precision": round(self.pred_top16_hits / max(1, self.pred_top16_total_pred), 5),
+            "miss_prefetch_recall": round(self.miss_pref_hits / max(1, self.miss_pref_total_actual_misses), 5),
+            "miss_prefetch_precision": round(self.miss_pref_hits / max(1, self.miss_pref_total_fetched), 5),
+            "uncoalesced_tensor_reads": self.uncoalesced_tensor_reads,
+            "coalesced_preadv_calls": self.coalesced_preadv_calls,
+        }
+
+    # ---------------------------------------------------------------- prefetch
+    def start_prefetch(self, pred: torch.Tensor, max_fetch: int = 3) -> None:
+        """Router-driven prefetch (c_layer_start_prefetch): pred = device int32 [M] ranked
+        predictions. The LRU insertion and the fills run on the prefetch stream, after the
+        work that produced `pred` on the current stream."""
+        self.wait_prefetch()
+        n = int(pred.numel())
+        self.pstream.wait_stream(torch.cuda.current_stream(self.device))
+        ps = self.pstream.cuda_stream
+        call("moe_lru_prefetch", self.state.data_ptr(), self.E, self.capacity, pred.data_ptr(), n, max_fetch,
+             self._pref.data_ptr(), ps)
+        call("moe_fill_slots", self._pref.data_ptr(), max_fetch, self.E, self.capacity, 9, self._src, self._dst,
+             self._rows, 0, ps)
+        self._pevent.record(self.pstream)
+        self._pending = True
+
+    def wait_prefetch(self) -> None:
+        if self._pending:
+            torch.cuda.current_stream(self.device).wait_event(self._pevent)
+            self._pending = False
+
+    # ---------------------------------------------------------------- decode
+    def step(self, indices: torch.Tensor) -> torch.Tensor:
+        """LRU step + demand fill for device int32 indices [.., K]: the slot ids ([1, 1, K])."""
+        self.wait_prefetch()
+        cs = self._cs()
+        call("moe_lru_step", self.state.data_ptr(), self.E, self.capacity, indices.data_ptr(), self.K,
+             self._slot_inds_buf.data_ptr(), self._miss.data_ptr(), cs)
+        call("moe_fill_slots", self._miss.data_ptr(), self.K, self.E, self.capacity, 9, self._src, self._dst,
+             self._rows, 0, cs)
+        return self._slot_inds_buf
+
+    def __call__(self, x: torch.Tensor, indices: torch.Tensor) -> torch.Tensor:
+        """x [1, 1, H] bf16, indices [1, 1, K] int32 (device) -> unweighted expert outputs
+        [1, 1, K, H] bf16 (the reference returns them unweighted; the caller applies scores)."""
+        B, L, K = indices.shape
+        if B != 1 or L != 1 or K != self.K:
+            raise ValueError("decode path: indices [1, 1, K]")
+        slots = self.step(indices)
+        act = ops.experts_gateup(x.reshape(1, -1), slots.view(1, K), self.gate, self.up, act=self._act)
+        _, yk = ops.experts_down(act, slots.view(1, K), self.down, None, want_yk=True)
+        return yk.view(1, 1, K, -1)
+
+    def forward_combined(self, x: torch.Tensor, indices: torch.Tensor, scores: torch.Tensor, *,
+                         resid=None, y=None) -> torch.Tensor:
+        """The hook's fused form: sum_k scores_k * expert_k(x) (+ resid), x [1, H]."""
+        slots = self.step(indices)
+        K = self.K
+        act = ops.experts_gateup(x, slots.view(1, K), self.gate, self.up, act=self._act)
+        out, _ = ops.experts_down(act, slots.view(1, K), self.down, scores.view(1, K), resid=resid, y=y)
+        return out
+
+    def close(self) -> None:
+        self.wait_prefetch()
+
+
+class OffloadStack:
+    """Decode over a stack with layer 0 pinned in HBM and layers 1.. behind CachedSwitchGLU
+    caches (the OffloadEngine decode loop, loader.py:1125-1244 with hooked_layer_call
+    855-992): per layer the router (with the next layer's top-M prediction), the LRU step and
+    fills, the experts and combine, then the prefetch of the next layer's predicted experts.
+
+    routers: bf16 [E, H] per layer (device); layer0: the pinned layer's experts (device);
+    pools: HostExpertPool per layer 1..L-1. `inject` (optional) replaces the routed experts by
+    given eids (BASELINE c2 drives the cache with a synthetic Zipf routing; the router still
+    runs). pred_bias: optional float32 [L, E] added to the next layer's logits before top-M."""
+
+    def __init__(self, routers: list[torch.Tensor], layer0: ExpertLayer, pools: list[HostExpertPool],
+                 capacities: dict[int, int], top_k: int, device, prefetch: bool = True, prefetch_top_m: int = 12,
+                 prefetch_cap: int = 3, norm: bool = True, expert_bytes: int | None = None):
+        self.device = torch.device(device)
+        self.routers = routers
+        self.layer0 = layer0
+        self.L = len(routers)
+        self.K = top_k
+        self.M = prefetch_top_m
+        self.prefetch = prefetch
+        self.prefetch_cap = prefetch_cap
+        self.norm = norm
+        self.H = routers[0].shape[1]
+        self.E = routers[0].shape[0]
+        ps = torch.cuda.Stream(device=self.device)
+        self.layers = [None] + [CachedSwitchGLU(l, capacities[l], pools[l - 1], self.device, top_k, expert_bytes,
+                                                prefetch_stream=ps) for l in range(1, self.L)]
+        self.capacities = capacities
+        self.hs = [torch.empty((1, self.H), dtype=torch.bfloat16, device=self.device) for _ in range(self.L + 1)]
+        self.r_out = [{} for _ in range(self.L)]
+        self.pred_bias = None
+
+    def reset_caches(self) -> None:
+        for c in self.layers[1:]:
+            c.reset_cache()
+
+    def reset_stats(self) -> None:
+        for c in self.layers[1:]:
+            c.reset_stats()
+
+    def decode_token(self, h: torch.Tensor, inject: torch.Tensor | None = None) -> torch.Tensor:
+        """h [1, H] bf16 (device) -> output of the last layer; inject: device int32 [L, K]."""
+        self.hs[0].copy_(h)
+        for l in range(self.L):
+            x = self.hs[l]
+            xin = x
+            if self.norm:
+                xin = _pow2_normalize_dev(x)
+            nxt = self.routers[l + 1] if (self.prefetch and l + 1 < self.L) else None
+            pb = self.pred_bias[l + 1] if (nxt is not None and self.pred_bias is not None) else None
+            r = ops.router_topk(xin, self.routers[l], self.K, w_next=nxt, M=self.M if nxt is not None else 0,
+                                pred_bias=pb, out=self.r_out[l])
+            eids = inject[l].view(1, self.K) if inject is not None else r["inds"]
+            if l == 0:
+                act = ops.experts_gateup(xin, eids, self.layer0.gate, self.layer0.up)
+                ops.experts_down(act, eids, self.layer0.down, r["scores"], resid=x, y=self.hs[l + 1])
+            else:
+                self.layers[l].forward_combined(xin, eids, r["scores"], resid=x, y=self.hs[l + 1])
+            if nxt is not None:
+                self.layers[l + 1].start_prefetch(r["pred"].view(-1), self.prefetch_cap)
+        return self.hs[self.L]
+
+    def layer_stats(self) -> list[dict]:
+        return [c.get_layer_stats() for c in self.layers[1:]]
+
+    def decode_totals(self) -> dict:
+        """c_get_decode_totals over the cached layers."""
+        keys = ("decode_lru_hits", "decode_prefetch_hits", "decode_demand_misses", "decode_requests",
+                "decode_demand_bytes", "decode_prefetch_bytes")
+        tot = dict.fromkeys(keys, 0)
+        for c in self.layers[1:]:
+            s = dict(zip(STAT_NAMES, c.raw_stats()))
+            for k in keys:
+                tot[k] += s[k]
+        return tot
+
+    def close(self) -> None:
+        for c in self.layers[1:]:
+            c.close()
+
+
+def _pow2_normalize_dev(h: torch.Tensor) -> torch.Tensor:
+    """Power-of-two RMS normalisation on the device (same rule as ops.pow2_normalize): the
+    exponent comes from the float64 sum of squares; the product is exact in bf16."""
+    ss = h.double().pow(2).sum()
+    n = h.numel()
+    m, e = torch.frexp(ss / n)
+    k = torch.where(e >= 0, torch.div(e, 2, rounding_mode="floor"), -torch.div(1 - e, 2, rounding_mode="floor"))
+    k = torch.where(ss > 0, k, torch.zeros_like(k))
+    return (h.double() * torch.pow(2.0, -k.double())).to(torch.bfloat16)
+
+
+def zipf_routing(seed: int, layers: int, tokens: int, E: int, K: int, s: float = 1.1, reuse: float = 0.3):
+    """BASELINE c2 synthetic routing: per layer a fixed random permutation of the experts with
+    Zipf(s) popularity; per token K distinct draws, each reusing one of the previous token's
+    experts with probability `reuse`. Returns int32 [tokens, layers, K] and the per-layer
+    popularity (log) used as the prediction bias, float32 [layers, E]."""
+    rng = np.random.default_rng(seed)
+    ranks = np.arange(1, E + 1, dtype=np.float64)
+    pop = ranks ** -s
+    pop /= pop.sum()
+    perms = [rng.permutation(E) for _ in range(layers)]
+    out = np.zeros((tokens, layers, K), dtype=np.int32)
+    prev = [None] * layers
+    for t in range(tokens):
+        for l in range(layers):
+            chosen: list[int] = []
+            while len(chosen) < K:
+                if prev[l] is not None and rng.random() < reuse:
+                    e = int(prev[l][rng.integers(0, K)])
+                else:
+                    e = int(perms[l][rng.choice(E, p=pop)])
+                if e not in chosen:
+                    chosen.append(e)
+            prev[l] = chosen
+            out[t, l] = chosen
+    bias = np.zeros((layers, E), dtype=np.float32)
+    for l in range(layers):
+        bias[l, perms[l]] = np.log(pop).astype(np.float32) - math.log(pop[-1])
+    return out, bias
