@@ -12,8 +12,10 @@
 // variants and for prefetches, waited by c_layer_wait_demand / c_layer_wait_prefetch or at
 // the start of the next call, as the reference's wait_async_batch does). slot_inds_ptr may
 // be device memory (written by the kernel) or host memory (written after the read-back).
+#include <algorithm>
 #include <cstring>
 #include <mutex>
+#include <vector>
 
 #include <cuda_runtime.h>
 
@@ -286,6 +288,18 @@ void c_layer_load_sync(int layer_idx, const int32_t *eids, const int32_t *slots,
         g.h_list[1 + i] = eids[i];
         g.h_list[1 + count + i] = slots[i];
     }
+    // the reference's I/O accounting of the fill (expert_io.c:186-233): 9 reads per expert and
+    // 9 per run of consecutive expert ids
+    int runs = 0;
+    {
+        std::vector<int32_t> s(eids, eids + count);
+        std::sort(s.begin(), s.end());
+        runs = 1;
+        for (int i = 1; i < count; ++i) runs += (s[i] != s[i - 1] + 1) ? 1 : 0;
+    }
+    moe_lru_add_stat(L->state, L->E, L->cap, 16, (uint64_t)count * 9, g.st);
+    moe_lru_add_stat(L->state, L->E, L->cap, 17, (uint64_t)runs * 9, g.st);
+    cudaStreamSynchronize(g.st);
     issue_fills(L, count, false);
 }
 

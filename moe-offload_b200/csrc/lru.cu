@@ -130,6 +130,27 @@ struct Lru {
     }
 };
 
+// The reference's I/O accounting of one fill of n experts (expert_io.c:186-233): nine tensor
+// reads per expert, and nine reads per run of consecutive expert ids once sorted (its
+// coalesced preadv calls). Counted the same way here so the counters stay comparable.
+constexpr int kRefTensors = 9;
+MOE_D void count_fill(uint64_t *stats, const int *eids, int n) {
+    if (n <= 0) return;
+    int s[32];
+    for (int i = 0; i < n; ++i) {
+        int j = i - 1;
+        while (j >= 0 && s[j] > eids[i]) {
+            s[j + 1] = s[j];
+            --j;
+        }
+        s[j + 1] = eids[i];
+    }
+    int runs = 1;
+    for (int i = 1; i < n; ++i) runs += (s[i] != s[i - 1] + 1) ? 1 : 0;
+    stats[kUncoalesced] += (uint64_t)n * kRefTensors;
+    stats[kCoalesced] += (uint64_t)runs * kRefTensors;
+}
+
 // whole-block copy of the state between global and shared memory (16-byte multiples)
 MOE_D void copy16(void *dst, const void *src, size_t bytes) {
     uint4 *d = reinterpret_cast<uint4 *>(dst);
@@ -237,6 +258,7 @@ __global__ void __launch_bounds__(kLruThreads) lru_kernel(LruArgs a) {
                     miss_s[i] = s;
                 }
                 L.stats[kDecMissBytes] += (uint64_t)nm * h->expert_bytes;
+                count_fill(L.stats, miss_e, nm);
                 for (int i = 0; i < k; ++i) {
                     const int s = L.e2s[a.eids[i]];
                     L.move_to_mru(s);
@@ -273,6 +295,7 @@ __global__ void __launch_bounds__(kLruThreads) lru_kernel(LruArgs a) {
                     }
                 }
                 a.out_list[0] = nm;
+                count_fill(L.stats, miss, nm);
                 for (int i = 0; i < nm; ++i) {      // reverse rank order: the best prediction is newest
                     const int e = miss[nm - 1 - i];
                     const int s = L.alloc(prot);

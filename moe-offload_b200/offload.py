@@ -104,9 +104,13 @@ class HostExpertPool:
 
     @classmethod
     def from_layer(cls, layer: ExpertLayer) -> "HostExpertPool":
+        """Copies a layer's experts (device or host tensors) into freshly pinned host memory."""
         ts = []
         for q in (layer.gate, layer.up, layer.down):
-            ts += [q.w.cpu(), q.s.cpu(), q.b.cpu()]
+            for t in (q.w, q.s, q.b):
+                h = torch.empty(t.shape, dtype=t.dtype, pin_memory=True)
+                h.copy_(t)
+                ts.append(h)
         return cls(ts, layer.gate.bits, layer.gate.group_size)
 
     def empty_slots(self, cap: int, device) -> list[torch.Tensor]:
