@@ -14,6 +14,9 @@
 //     the given (copy) stream, i.e. the copy engines.
 // A "tensor" is any per-expert row array: the nine MLX tensors (row = one expert's slice),
 // or the packed layout (one tensor, row = one whole expert).
+#include <mutex>
+#include <unordered_set>
+
 #include "common.cuh"
 
 namespace {
@@ -82,6 +85,25 @@ int fill_tensors(FillArgs &a, int nt, const void *const *src, void *const *dst, 
     return MOE_OK;
 }
 
+std::mutex g_src_mu;
+std::unordered_set<const void *> g_src_ok;
+
+int check_source(const void *p, int t) {
+    {
+        std::lock_guard<std::mutex> lk(g_src_mu);
+        if (g_src_ok.count(p)) return MOE_OK;
+    }
+    cudaPointerAttributes pa{};
+    MOE_CUDA_TRY(cudaPointerGetAttributes(&pa, p));
+    if (pa.type != cudaMemoryTypeHost && pa.type != cudaMemoryTypeDevice && pa.type != cudaMemoryTypeManaged)
+        return moe_set_error(MOE_EINVAL, "fill_slots: tensor %d source is pageable host memory", t);
+    if (pa.type == cudaMemoryTypeHost && pa.devicePointer != p)
+        return moe_set_error(MOE_EINVAL, "fill_slots: tensor %d pinned source is not mapped at its host address", t);
+    std::lock_guard<std::mutex> lk(g_src_mu);
+    g_src_ok.insert(p);
+    return MOE_OK;
+}
+
 }  // namespace
 
 extern "C" int moe_fill_slots(const int32_t *list, int stride, int E, int cap, int ntensors,
@@ -96,19 +118,16 @@ extern "C" int moe_fill_slots(const int32_t *list, int stride, int E, int cap, i
     a.cap = cap;
     if (int rc = fill_tensors(a, ntensors, host_src, dev_dst, row_bytes)) return rc;
     // the pool must be reachable from the device: pinned (page-locked) host memory, whose
-    // device address equals the host address under unified addressing, or device memory
-    for (int t = 0; t < ntensors; ++t) {
-        cudaPointerAttributes pa{};
-        MOE_CUDA_TRY(cudaPointerGetAttributes(&pa, host_src[t]));
-        if (pa.type != cudaMemoryTypeHost && pa.type != cudaMemoryTypeDevice && pa.type != cudaMemoryTypeManaged)
-            return moe_set_error(MOE_EINVAL, "fill_slots: tensor %d source is pageable host memory", t);
-        if (pa.type == cudaMemoryTypeHost && pa.devicePointer != host_src[t])
-            return moe_set_error(MOE_EINVAL, "fill_slots: tensor %d pinned source is not mapped at its host address",
-                                 t);
+    // device address equals the host address under unified addressing, or device memory.
+    // Checked once per base address (later calls may be inside a stream capture).
+    for (int t = 0; t < ntensors; ++t)
+        if (int rc = check_source(host_src[t], t)) return rc;
+    static int sms = 0;
+    if (sms == 0) {
+        int dev = 0;
+        MOE_CUDA_TRY(cudaGetDevice(&dev));
+        MOE_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
     }
-    int dev = 0, sms = 0;
-    MOE_CUDA_TRY(cudaGetDevice(&dev));
-    MOE_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
     const int grid = num_ctas > 0 ? num_ctas : sms;
     fill_kernel<<<grid, 256, 0, as_stream(stream)>>>(a);
     MOE_CUDA_TRY(cudaGetLastError());

@@ -354,7 +354,13 @@ __global__ void __launch_bounds__(kLruThreads) lru_kernel(LruArgs a) {
 int lru_launch(LruArgs a, void *stream) {
     if (!a.state) return moe_set_error(MOE_EINVAL, "lru: null state");
     const LruLayout Ly(a.E, a.cap);
-    MOE_CUDA_TRY(cudaFuncSetAttribute(lru_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)Ly.total));
+    // raise the dynamic shared-memory limit once (not per launch: launches may be captured)
+    static int configured = 0;
+    if (Ly.total > 48 * 1024 && !configured) {
+        MOE_CUDA_TRY(cudaFuncSetAttribute(lru_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          (int)LruLayout(kLruMaxE, kLruMaxE).total));
+        configured = 1;
+    }
     lru_kernel<<<1, kLruThreads, Ly.total, as_stream(stream)>>>(a);
     MOE_CUDA_TRY(cudaGetLastError());
     return MOE_OK;

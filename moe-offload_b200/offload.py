@@ -335,6 +335,29 @@ class OffloadStack:
                 self.layers[l + 1].start_prefetch(r["pred"].view(-1), self.prefetch_cap)
         return self.hs[self.L]
 
+    def capture(self) -> None:
+        """Records one decode_token as a CUDA graph over static input buffers (the token's
+        hidden state and injected experts); decode_graph() then replays it. Every step of
+        the token is device-side, so the graph needs no host decisions."""
+        self.h_static = torch.zeros((1, self.H), dtype=torch.bfloat16, device=self.device)
+        self.inj_static = torch.zeros((self.L, self.K), dtype=torch.int32, device=self.device)
+        s = torch.cuda.Stream(device=self.device)
+        s.wait_stream(torch.cuda.current_stream(self.device))
+        with torch.cuda.stream(s):
+            self.decode_token(self.h_static, self.inj_static)       # warm: workspaces, attributes
+        s.synchronize()
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph, stream=s):
+            self.decode_token(self.h_static, self.inj_static)
+        torch.cuda.current_stream(self.device).wait_stream(s)
+
+    def decode_graph(self, h: torch.Tensor, inject: torch.Tensor | None) -> torch.Tensor:
+        self.h_static.copy_(h)
+        if inject is not None:
+            self.inj_static.copy_(inject)
+        self.graph.replay()
+        return self.hs[self.L]
+
     def layer_stats(self) -> list[dict]:
         return [c.get_layer_stats() for c in self.layers[1:]]
 

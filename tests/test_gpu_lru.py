@@ -232,3 +232,54 @@ def test_cached_layer_matches_resident_layer(dev):
     assert st["decode_requests"] == 40 * K
     assert st["decode_lru_hits"] + st["decode_prefetch_hits"] + st["decode_demand_misses"] == 40 * K
     assert int(__import__("moe_offload_b200")._lib.call("moe_device_error", 1)) == 0
+
+
+def test_offload_stack_graph_matches_eager_and_resident(dev):
+    """OffloadStack (layer 0 pinned, cached layers behind the GPU LRU, prefetch on a side
+    stream): the captured graph gives the eager results, and both equal the all-resident
+    per-layer path with the same routing."""
+    from moe_offload_b200 import ops
+    from moe_offload_b200.offload import HostExpertPool, OffloadStack, _pow2_normalize_dev, zipf_routing
+    from moe_offload_b200.synthetic import (ExpertLayer, np_bf16_normal, np_qmatrix, np_to_bf16_tensor,
+                                            to_device_qmatrix)
+    rng = np.random.default_rng(21)
+    L, E, H, I, K, cap = 3, 64, 1024, 256, 8, 16
+    layers = []
+    for _ in range(L):
+        layers.append(ExpertLayer(np_to_bf16_tensor(np_bf16_normal(rng, (E, H), 0.02), dev),
+                                  to_device_qmatrix(np_qmatrix(rng, E, I, H), dev),
+                                  to_device_qmatrix(np_qmatrix(rng, E, I, H), dev),
+                                  to_device_qmatrix(np_qmatrix(rng, E, H, I), dev)))
+    pools = [HostExpertPool.from_layer(layers[l]) for l in range(1, L)]
+    caps = {l: cap for l in range(1, L)}
+    routing, bias = zipf_routing(seed=5, layers=L, tokens=24, E=E, K=K)
+    inj = torch.from_numpy(routing).to(dev)
+    hs = [np_to_bf16_tensor(np_bf16_normal(rng, (1, H)), dev) for _ in range(24)]
+
+    def make():
+        st = OffloadStack([ly.router for ly in layers], layers[0], pools, caps, K, dev)
+        st.pred_bias = torch.from_numpy(bias).to(dev)
+        return st
+
+    eager, graphed = make(), make()
+    graphed.capture()
+    graphed.reset_caches()
+    graphed.reset_stats()
+    for t in range(24):
+        ye = eager.decode_token(hs[t], inj[t]).clone()
+        yg = graphed.decode_graph(hs[t], inj[t]).clone()
+        # resident reference for the same token and routing
+        x = hs[t]
+        for l in range(L):
+            xin = _pow2_normalize_dev(x)
+            r = ops.router_topk(xin, layers[l].router, K)
+            e = inj[t][l].view(1, K)
+            act = ops.experts_gateup(xin, e, layers[l].gate, layers[l].up)
+            x, _ = ops.experts_down(act, e, layers[l].down, r["scores"], resid=x)
+        torch.cuda.synchronize()
+        assert torch.equal(ye, yg), t
+        assert torch.equal(ye, x), t
+    te, tg = eager.decode_totals(), graphed.decode_totals()
+    assert te == tg
+    assert te["decode_requests"] == 24 * K * (L - 1)
+    assert int(__import__("moe_offload_b200")._lib.call("moe_device_error", 1)) == 0
