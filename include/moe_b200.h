@@ -200,6 +200,30 @@ int moe_stack_decode(const void *layers, int L, int H, int I, int E, int K, int 
                      void *workspace, size_t workspace_bytes, int num_ctas, void *stream);
 
 /* ------------------------------------------------------------------------------------ */
+/* Prefill: T tokens through one layer's routed experts as expert-grouped tcgen05 GEMMs.  */
+/* ------------------------------------------------------------------------------------ */
+
+/* Workspace bytes for moe_prefill_experts (bucketing, tile lists, act [T*K][I], yk [T*K][H]). */
+size_t moe_prefill_workspace_bytes(int T, int H, int I, int E, int K);
+
+/*
+ * The prefill branch of the MoE block (mlx-qwen38/loader.py:566-699, cpp/src/layers.cpp:403-600;
+ * gather_qmm per expert group as prefill_qproj.py:18-40): x bf16 [T][H], inds u32 [T][K] and
+ * scores bf16 [T][K] from the router (moe_router_topk), experts in the MLX layout with
+ * cap = E. Assignments are grouped by expert on the device; gate/up and down run as GEMMs
+ * with M = 128 weight rows and N = the expert's tokens on the tensor cores (weights
+ * dequantised to bf16 in shared memory, fp32 accumulation in TMEM); y bf16 [T][H] =
+ * resid + sum_k bf16(expert_k(x) * score_k) (sequential bf16 in MLX order). resid may be
+ * NULL; act_out (bf16 [T*K][I], positions in expert order) may be NULL. H, I multiples of
+ * 64; x and code arrays 16-byte aligned.
+ */
+int moe_prefill_experts(const void *x, int T, int H, int I, int E, int K, const uint32_t *inds,
+                        const void *scores, const uint32_t *wg, const void *sg, const void *bg,
+                        const uint32_t *wu, const void *su, const void *bu, const uint32_t *wd,
+                        const void *sd, const void *bd, int sb_fp16, const void *resid, void *y,
+                        void *act_out, void *workspace, size_t workspace_bytes, void *stream);
+
+/* ------------------------------------------------------------------------------------ */
 /* Per-layer LRU expert-slot cache with its state on the GPU.                             */
 /* ------------------------------------------------------------------------------------ */
 

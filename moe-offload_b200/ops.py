@@ -242,3 +242,40 @@ def pow2_normalize(h_bits):
     k = pow2_rms_shift(h_bits)
     f = (np.asarray(h_bits, dtype=np.uint16).astype(np.uint32) << 16).view(np.float32)
     return (np.ascontiguousarray(f * np.float32(2.0 ** -k)).view(np.uint32) >> 16).astype(np.uint16)
+
+
+# ----------------------------------------------------------------------------- prefill
+
+_PWS: dict = {}
+
+
+def prefill_experts(x: torch.Tensor, inds: torch.Tensor, scores: torch.Tensor, gate: QMatrix, up: QMatrix,
+                    down: QMatrix, *, resid=None, y=None, stream=None) -> torch.Tensor:
+    """Prefill of T tokens through the routed experts (expert-grouped tcgen05 GEMMs):
+    y [T, H] = (resid +) sum_k bf16(expert_k(x) * scores[:, k]). x bf16 [T, H], inds int32
+    [T, K], scores bf16 [T, K] (router order), experts in the MLX layout [E, ...]."""
+    _need(x, "x", (torch.bfloat16,))
+    dev = x.device
+    _need(inds, "inds", (torch.int32, torch.uint32), dev)
+    _need(scores, "scores", (torch.bfloat16,), dev)
+    for n, q in (("gate", gate), ("up", up), ("down", down)):
+        q.check(n, dev)
+    T, H = x.shape
+    K = inds.shape[-1]
+    E, I = gate.w.shape[0], gate.w.shape[1]
+    if resid is not None:
+        _need(resid, "resid", (torch.bfloat16,), dev)
+    if y is None:
+        y = torch.empty((T, H), dtype=torch.bfloat16, device=dev)
+    nb = int(call("moe_prefill_workspace_bytes", T, H, I, E, K))
+    key = (dev, nb)
+    ws = _PWS.get(key)
+    if ws is None:
+        ws = torch.empty(nb, dtype=torch.uint8, device=dev)
+        _PWS.clear()
+        _PWS[key] = ws
+    call("moe_prefill_experts", x.data_ptr(), T, H, I, E, K, inds.data_ptr(), scores.data_ptr(),
+         gate.w.data_ptr(), gate.s.data_ptr(), gate.b.data_ptr(), up.w.data_ptr(), up.s.data_ptr(),
+         up.b.data_ptr(), down.w.data_ptr(), down.s.data_ptr(), down.b.data_ptr(), gate.sb_fp16,
+         _ptr(resid), y.data_ptr(), None, ws.data_ptr(), ws.numel(), _stream(stream))
+    return y
