@@ -43,8 +43,10 @@ def parse():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
-    ap.add_argument("--config", choices=["c1", "c2"], default="c1",
-                    help="c1: resident stack (the headline); c2: offload stack with the LRU slot caches")
+    ap.add_argument("--config", choices=["c1", "c2", "c3", "c3n"], default="c1",
+                    help="c1: resident stack (the headline); c2: offload stack with the LRU slot caches; "
+                         "c3: 2048-token prefill through the resident 28-layer stack; c3n: the Nemotron-shaped "
+                         "prefill layer (240 experts, top-9, 1024 tokens)")
     ap.add_argument("--layers", type=int, default=0,
                     help="profiling aid: run only the first N layers of the stack (0 = all 28)")
     return ap.parse_args()
@@ -396,6 +398,127 @@ def run_c2(args, rank: int, world: int, local_rank: int) -> None:
     stack.close()
 
 
+def run_c3(args, rank: int, world: int, local_rank: int) -> None:
+    """prefill of a 2048-token prompt through the resident 28 x 512 x top-10
+    stack (c3), or one Nemotron-shaped layer (c3n: 240 experts, top-9, H 2688, I 1856, 1024
+    tokens). A step = every layer's moe_prefill_layer (per-row power-of-two RMS input
+    normalisation, router + exact top-k, expert-grouped tcgen05 GEMMs, combine + residual)."""
+    import dataclasses
+
+    import torch
+
+    from moe_offload_b200 import ops
+    from moe_offload_b200.synthetic import C3, C3_TOKENS, NEMOTRON, NEMOTRON_TOKENS, dev_bf16_normal, dev_stack
+
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    cfg, T = (C3, C3_TOKENS) if args.config == "c3" else (NEMOTRON, NEMOTRON_TOKENS)
+    if args.layers:
+        cfg = dataclasses.replace(cfg, name=f"{cfg.name}_first{args.layers}", layers=args.layers)
+    layers = dev_stack(cfg, dev)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(cfg.seed + 1000 * rank)
+    n_in = args.warmup + args.steps
+    h0 = dev_bf16_normal((n_in, T, cfg.hidden), dev, gen)
+    bufs = [dict(), dict()]
+
+    def step(h):
+        for li, ly in enumerate(layers):
+            o = ops.prefill_layer(h, ly.router, ly.gate, ly.up, ly.down, cfg.top_k, norm=True, resid=h,
+                                  out=bufs[li & 1])
+            h = o["y"]
+        return h
+
+    for i in range(args.warmup):
+        step(h0[i])
+    torch.cuda.synchronize()
+    clk = ClockSampler(local_rank)
+    clk.start()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for i in range(args.steps):
+        step(h0[args.warmup + i])
+    e.record()
+    torch.cuda.synchronize()
+    clocks = clk.stop()
+    t_ms = s.elapsed_time(e)
+    value = args.steps * T / (t_ms / 1000.0)
+
+    # breakdown on the first layer: router (with the normalisation) vs the expert GEMMs
+    ly = layers[0]
+    x = h0[0]
+    n_rep = 3
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+    r = ops.router_topk(x, ly.router, cfg.top_k)
+    ops.prefill_experts(x, r["inds"], r["scores"], ly.gate, ly.up, ly.down, resid=x)
+    torch.cuda.synchronize()
+    ev[0].record()
+    for _ in range(n_rep):
+        r = ops.router_topk(x, ly.router, cfg.top_k, out=r)
+    ev[1].record()
+    for _ in range(n_rep):
+        ops.prefill_experts(x, r["inds"], r["scores"], ly.gate, ly.up, ly.down, resid=x)
+    ev[2].record()
+    torch.cuda.synchronize()
+    router_ms = ev[0].elapsed_time(ev[1]) / n_rep
+    experts_ms = ev[1].elapsed_time(ev[2]) / n_rep
+
+    # e2e through the public API: the prompt's hidden states from pinned host memory, the
+    # final hidden states back to pinned host memory, every step
+    e2e = None
+    if not args.no_e2e:
+        hh = torch.empty((2, T, cfg.hidden), dtype=torch.bfloat16, pin_memory=True)
+        hh.copy_(h0[:2])
+        out_host = torch.empty((T, cfg.hidden), dtype=torch.bfloat16, pin_memory=True)
+        s2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s2.record()
+        for i in range(args.steps):
+            hd = hh[i & 1].to(dev, non_blocking=True)
+            out_host.copy_(step(hd), non_blocking=True)
+        e2.record()
+        torch.cuda.synchronize()
+        t2 = s2.elapsed_time(e2)
+        e2e = {"value": round(args.steps * T / (t2 / 1000.0), 2), "unit": "tok/s",
+               "h2d_bytes_per_step": T * cfg.hidden * 2, "d2h_bytes_per_step": T * cfg.hidden * 2,
+               "api": "moe_offload_b200.ops.prefill_layer per layer (pinned host prompt in, hidden states out)"}
+
+    H, I, K, E = cfg.hidden, cfg.inter, cfg.top_k, cfg.experts
+    flops_layer = 2.0 * T * K * 3 * H * I
+    bytes_layer = E * cfg.expert_bytes
+    tf_peak = 1661.3
+    try:
+        tf_peak = float(json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))["bf16_tflops"])
+        tf_src = "measured"
+    except Exception:
+        tf_src = "fallback"
+    hbm_peak, _ = peaks()
+    achieved = flops_layer / (experts_ms / 1000.0) / 1e12
+    roof = {"kernel": "moe_prefill_experts (bucketing + grouped tcgen05 gate/up and down GEMMs + combine)",
+            "bound": "tensor", "achieved": round(achieved, 2), "peak": tf_peak, "unit": "TFLOP/s",
+            "frac": round(achieved / tf_peak, 4), "traffic": None,
+            "algorithmic_flops_per_launch": flops_layer, "algorithmic_bytes_per_launch": bytes_layer,
+            "launch_ms": round(experts_ms, 4), "hbm_frac": round(bytes_layer / (experts_ms / 1000.0) / 1e9 / hbm_peak, 4),
+            "router_ms_per_layer": round(router_ms, 4), "peak_source": tf_src}
+    from moe_offload_b200 import _lib
+    dev_err = int(_lib.call("moe_device_error", 1))
+    cpu = None
+    if not args.no_cpu:
+        cpu = cpu_layer_sample()
+        cpu["sample"] += "; the restatement computes each prompt token like a decode token"
+    line = {"metric": f"MoE prefill tok/s ({cfg.layers}-layer stack, {T}-token prompt)", "value": round(value, 2),
+            "unit": "tok/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(t_ms / args.steps, 4), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "u2 codes -> bf16 x bf16 -> f32", "data": "synthetic",
+            "config": {"workload": cfg.name, "layers": cfg.layers, "tokens": T, "hidden": H, "experts": E,
+                       "top_k": K, "inter": I, "group_size": cfg.group_size, "scales": "fp16", "router": "bf16",
+                       "l2": f"inputs larger than L2: {cfg.layers * bytes_layer / 1e9:.1f} GB of weights per step"},
+            "roofline": roof, "clocks": clocks,
+            # per layer: row normalisation, router, count, scan, scatter, gate/up GEMM, down GEMM, combine
+            "gpu_launches": 8 * cfg.layers * args.steps, "device_error": dev_err, "e2e": e2e,
+            "cpu_baseline": cpu}
+    print(json.dumps(line), flush=True)
+
+
 def main() -> int:
     args = parse()
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -414,6 +537,8 @@ def main() -> int:
             run_reference(args, rank, world)
         elif args.config == "c2":
             run_c2(args, rank, world, local_rank)
+        elif args.config in ("c3", "c3n"):
+            run_c3(args, rank, world, local_rank)
         else:
             run_ours(args, rank, world, local_rank)
     finally:

@@ -223,6 +223,24 @@ int moe_prefill_experts(const void *x, int T, int H, int I, int E, int K, const 
                         const void *sd, const void *bd, int sb_fp16, const void *resid, void *y,
                         void *act_out, void *workspace, size_t workspace_bytes, void *stream);
 
+/* Workspace bytes for moe_prefill_layer; zero-fill it once before first use (the router's
+ * tickets inside it are left at zero by every call). */
+size_t moe_prefill_layer_workspace_bytes(int T, int H, int I, int E, int K);
+
+/*
+ * One resident layer's prefill: router over the T rows (bf16 [E, H] router, exact softmax /
+ * MLX-order top-k as moe_router_topk) then moe_prefill_experts, i.e. the prefill branch of
+ * the reference's hook for a layer whose experts are all resident (mlx-qwen38/loader.py:
+ * 903-908 router + 566-699 experts; cpp/src/layers.cpp:403-600). norm = 1 feeds router and
+ * experts x[t] * 2^-k(t) (the per-row power-of-two RMS rule of moe_decode_layer); resid may
+ * be NULL or x. Outputs: inds u32 [T][K], scores bf16 [T][K], y bf16 [T][H].
+ */
+int moe_prefill_layer(const void *x, int T, int H, int I, int E, int K, const void *router_w,
+                      const uint32_t *wg, const void *sg, const void *bg, const uint32_t *wu,
+                      const void *su, const void *bu, const uint32_t *wd, const void *sd, const void *bd,
+                      int sb_fp16, int norm, const void *resid, uint32_t *out_inds, void *out_scores,
+                      void *y, void *workspace, size_t workspace_bytes, void *stream);
+
 /* ------------------------------------------------------------------------------------ */
 /* Per-layer LRU expert-slot cache with its state on the GPU.                             */
 /* ------------------------------------------------------------------------------------ */

@@ -46,6 +46,8 @@ SIGNATURES: dict[str, tuple] = {
     "moe_pack_experts": (I, [I, I, I, P, P, P, P, P, P, P, P, P, P, P]),
     "moe_prefill_workspace_bytes": (SZ, [I, I, I, I, I]),
     "moe_prefill_experts": (I, [P, I, I, I, I, I, P, P, P, P, P, P, P, P, P, P, P, I, P, P, P, P, SZ, P]),
+    "moe_prefill_layer_workspace_bytes": (SZ, [I, I, I, I, I]),
+    "moe_prefill_layer": (I, [P, I, I, I, I, I, P] + [P] * 9 + [I, I, P, P, P, P, P, SZ, P]),
     "moe_lru_state_bytes": (SZ, [I, I]),
     "moe_lru_init": (I, [P, I, I, U64, P]),
     "moe_lru_reset": (I, [P, I, I, I, P]),

@@ -21,6 +21,7 @@
 // matrix (16 KB), B = up to 256 token rows x 64 bf16 (32 KB); two stages alternate so the
 // dequantisation of block kb+1 overlaps the MMAs of block kb (tcgen05.commit -> mbarrier).
 #include "common.cuh"
+#include "internal.h"
 
 namespace {
 
@@ -400,6 +401,31 @@ size_t gemm_smem(bool gateup) {
 
 }  // namespace
 
+// x_n[t] = x[t] * 2^-k(t), the power-of-two RMS normalisation of every row (exact)
+static __global__ void __launch_bounds__(256) pow2_rows_kernel(const uint16_t *x, int H, uint16_t *xn) {
+    __shared__ double red[8];
+    const int t = blockIdx.x;
+    const uint16_t *xr = x + (size_t)t * H;
+    double ss = 0.0;
+    for (int i = threadIdx.x; i < H; i += blockDim.x) {
+        const double v = (double)bf16_bits_to_f32(xr[i]);
+        ss = fma(v, v, ss);
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+    __syncthreads();
+    ss = 0.0;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) ss += red[i];
+    const float mul = ldexpf(1.0f, -pow2_rms_shift(ss, H));
+    for (int i = threadIdx.x; i < H; i += blockDim.x) xn[(size_t)t * H + i] = f32_to_bf16_bits(bf16_bits_to_f32(xr[i]) * mul);
+}
+
+static size_t layer_prefix_bytes(int T, int H, int E) {
+    return al256((size_t)T * 4) + al256((size_t)T * E * 2) + al256((size_t)T * H * 2);
+}
+
 extern "C" size_t moe_prefill_workspace_bytes(int T, int H, int I, int E, int K) {
     if (T <= 0 || H <= 0 || I <= 0 || E <= 0 || K <= 0) return 0;
     return carve(nullptr, T, H, I, E, K).bytes;
@@ -457,4 +483,39 @@ extern "C" int moe_prefill_experts(const void *x, int T, int H, int I, int E, in
                                              static_cast<const uint16_t *>(resid), T, K, H, static_cast<uint16_t *>(y));
     MOE_CUDA_TRY(cudaGetLastError());
     return MOE_OK;
+}
+
+extern "C" size_t moe_prefill_layer_workspace_bytes(int T, int H, int I, int E, int K) {
+    const size_t p = moe_prefill_workspace_bytes(T, H, I, E, K);
+    return p ? layer_prefix_bytes(T, H, E) + p : 0;
+}
+
+extern "C" int moe_prefill_layer(const void *x, int T, int H, int I, int E, int K, const void *router_w,
+                                 const uint32_t *wg, const void *sg, const void *bg, const uint32_t *wu,
+                                 const void *su, const void *bu, const uint32_t *wd, const void *sd, const void *bd,
+                                 int sb_fp16, int norm, const void *resid, uint32_t *out_inds, void *out_scores,
+                                 void *y, void *workspace, size_t workspace_bytes, void *stream) {
+    if (!x || !router_w || !out_inds || !out_scores || !y || !workspace)
+        return moe_set_error(MOE_EINVAL, "prefill_layer: null pointer");
+    const size_t need = moe_prefill_layer_workspace_bytes(T, H, I, E, K);
+    if (!need || workspace_bytes < need)
+        return moe_set_error(MOE_EINVAL, "prefill_layer: workspace of %zu bytes needed, %zu given", need,
+                             workspace_bytes);
+    char *ws = static_cast<char *>(workspace);
+    unsigned int *tickets = reinterpret_cast<unsigned int *>(ws);
+    uint16_t *logits = reinterpret_cast<uint16_t *>(ws + al256((size_t)T * 4));
+    uint16_t *xn = reinterpret_cast<uint16_t *>(ws + al256((size_t)T * 4) + al256((size_t)T * E * 2));
+    void *pws = ws + layer_prefix_bytes(T, H, E);
+    const void *xin = x;
+    if (norm) {
+        pow2_rows_kernel<<<T, 256, 0, as_stream(stream)>>>(static_cast<const uint16_t *>(x), H, xn);
+        MOE_CUDA_TRY(cudaGetLastError());
+        xin = xn;
+    }
+    int rc = moe_router_launch(xin, T, H, E, K, router_w, nullptr, nullptr, 16, 64, 0, nullptr, nullptr, nullptr, 0,
+                               nullptr, nullptr, nullptr, out_inds, out_scores, nullptr, tickets, logits, nullptr,
+                               nullptr, nullptr, nullptr, 0, stream);
+    if (rc) return rc;
+    return moe_prefill_experts(xin, T, H, I, E, K, out_inds, out_scores, wg, sg, bg, wu, su, bu, wd, sd, bd, sb_fp16,
+                               resid, y, nullptr, pws, workspace_bytes - layer_prefix_bytes(T, H, E), stream);
 }

@@ -279,3 +279,40 @@ def prefill_experts(x: torch.Tensor, inds: torch.Tensor, scores: torch.Tensor, g
          up.b.data_ptr(), down.w.data_ptr(), down.s.data_ptr(), down.b.data_ptr(), gate.sb_fp16,
          _ptr(resid), y.data_ptr(), None, ws.data_ptr(), ws.numel(), _stream(stream))
     return y
+
+
+_PLWS: dict = {}
+
+
+def prefill_layer(x: torch.Tensor, router: torch.Tensor, gate: QMatrix, up: QMatrix, down: QMatrix, K: int, *,
+                  norm: bool = True, resid=None, out: dict | None = None, stream=None) -> dict:
+    """One resident layer's prefill of T rows: router (bit-exact top-k) -> expert-grouped
+    tcgen05 GEMMs -> combine. norm=True feeds router and experts the per-row power-of-two
+    RMS normalisation of x; resid (bf16 [T, H], typically x) is added once. Returns
+    dict(y, inds, scores)."""
+    _need(x, "x", (torch.bfloat16,))
+    dev = x.device
+    T, H = x.shape
+    _need(router, "router", (torch.bfloat16,), dev)
+    E = router.shape[0]
+    I = gate.w.shape[1]
+    for n, q in (("gate", gate), ("up", up), ("down", down)):
+        q.check(n, dev)
+    if resid is not None:
+        _need(resid, "resid", (torch.bfloat16,), dev)
+    o = out if out is not None else {}
+    o.setdefault("y", torch.empty((T, H), dtype=torch.bfloat16, device=dev))
+    o.setdefault("inds", torch.empty((T, K), dtype=torch.int32, device=dev))
+    o.setdefault("scores", torch.empty((T, K), dtype=torch.bfloat16, device=dev))
+    nb = int(call("moe_prefill_layer_workspace_bytes", T, H, I, E, K))
+    key = (dev, T, H, I, E, K)
+    ws = _PLWS.get(key)
+    if ws is None:
+        ws = torch.zeros(nb, dtype=torch.uint8, device=dev)
+        _PLWS.clear()
+        _PLWS[key] = ws
+    call("moe_prefill_layer", x.data_ptr(), T, H, I, E, K, router.data_ptr(), gate.w.data_ptr(), gate.s.data_ptr(),
+         gate.b.data_ptr(), up.w.data_ptr(), up.s.data_ptr(), up.b.data_ptr(), down.w.data_ptr(), down.s.data_ptr(),
+         down.b.data_ptr(), gate.sb_fp16, int(norm), _ptr(resid), o["inds"].data_ptr(), o["scores"].data_ptr(),
+         o["y"].data_ptr(), ws.data_ptr(), ws.numel(), _stream(stream))
+    return o

@@ -51,7 +51,10 @@ class StackConfig:
 C0 = StackConfig("c0_single_layer_h2048_e64_top8", 1, 2048, 64, 8, 768, seed=0)
 C1 = StackConfig("c1_qwen38_shape_28x512_top10", 28, 3072, 512, 10, 768, seed=1)
 C2 = StackConfig("c2_offload_28x512_top10_cap102", 28, 3072, 512, 10, 768, seed=2)
+C3 = StackConfig("c3_prefill_28x512_top10_T2048", 28, 3072, 512, 10, 768, seed=3)
+C3_TOKENS = 2048
 NEMOTRON = StackConfig("c3_nemotron_shape_240_top9", 1, 2688, 240, 9, 1856, seed=3)
+NEMOTRON_TOKENS = 1024
 
 
 # ------------------------------------------------------------------------------ numpy

@@ -103,3 +103,34 @@ def test_prefill_c3_nemotron_shape_sampled(dev):
     row_err, rel = _case(dev, rng, 1024, 2688, 1856, 240, 9, sample=16)
     assert row_err <= 0.02 and rel <= 1e-2, (row_err, rel)
     assert int(__import__("moe_offload_b200")._lib.call("moe_device_error", 1)) == 0
+
+
+def test_prefill_layer_norm_router_and_residual(dev):
+    """moe_prefill_layer = per-row power-of-two normalisation + router + experts + residual:
+    indices bit-exact with the oracle's router on the normalised rows, output within the
+    tolerance of the oracle's expert block on those rows plus the residual."""
+    from moe_offload_b200 import ops
+    from moe_offload_b200.ops import pow2_normalize
+    from moe_offload_b200.synthetic import (bf16_tensor_to_np, np_bf16_normal, np_qmatrix, np_to_bf16_tensor,
+                                            to_device_qmatrix)
+    rng = np.random.default_rng(11)
+    T, H, I, E, K = 96, 512, 256, 32, 4
+    x = (orc.bf16_to_f32(np_bf16_normal(rng, (T, H))) * np.float32(3.0) ** rng.integers(-3, 4, size=(T, 1))
+         ).astype(np.float32)
+    x = orc.f32_to_bf16(x)
+    wr = np_bf16_normal(rng, (E, H), 0.02)
+    g, u, d = np_qmatrix(rng, E, I, H), np_qmatrix(rng, E, I, H), np_qmatrix(rng, E, H, I)
+    xt = np_to_bf16_tensor(x, dev)
+    o = ops.prefill_layer(xt, np_to_bf16_tensor(wr, dev), *[to_device_qmatrix(m, dev) for m in (g, u, d)], K,
+                          norm=True, resid=xt)
+    torch.cuda.synchronize()
+    xn = np.stack([pow2_normalize(x[t]) for t in range(T)])
+    _, ri, rs = orc.softmax_topk(orc.router_logits(xn, wr, E), K)
+    assert np.array_equal(o["inds"].cpu().numpy().astype(np.uint32), ri), "prefill_layer indices differ"
+    assert np.array_equal(bf16_tensor_to_np(o["scores"]), rs), "prefill_layer scores differ"
+    ref = orc.experts(xn, ri, rs, g, u, d, sb_fp16=True, resid=x)["y"]
+    a = orc.bf16_to_f32(bf16_tensor_to_np(o["y"])).astype(np.float64) - orc.bf16_to_f32(x)
+    b = orc.bf16_to_f32(ref).astype(np.float64) - orc.bf16_to_f32(x)
+    rel = np.linalg.norm(a - b) / np.linalg.norm(b)
+    assert rel <= 1e-2, rel
+    assert int(__import__("moe_offload_b200")._lib.call("moe_device_error", 1)) == 0
