@@ -43,10 +43,12 @@ def parse():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
-    ap.add_argument("--config", choices=["c1", "c2", "c3", "c3n"], default="c1",
+    ap.add_argument("--config", choices=["c1", "c2", "c3", "c3n", "c4"], default="c1",
                     help="c1: resident stack (the headline); c2: offload stack with the LRU slot caches; "
                          "c3: 2048-token prefill through the resident 28-layer stack; c3n: the Nemotron-shaped "
-                         "prefill layer (240 experts, top-9, 1024 tokens)")
+                         "prefill layer (240 experts, top-9, 1024 tokens); c4: expert-parallel decode (experts "
+                         "split across the ranks; the default for N > 1)")
+    ap.add_argument("--batch", type=int, default=0, help="c4: tokens per decode step (default: one per GPU)")
     ap.add_argument("--layers", type=int, default=0,
                     help="profiling aid: run only the first N layers of the stack (0 = all 28)")
     return ap.parse_args()
@@ -519,6 +521,117 @@ def run_c3(args, rank: int, world: int, local_rank: int) -> None:
     print(json.dumps(line), flush=True)
 
 
+def run_c4(args, rank: int, world: int, local_rank: int) -> None:
+    """the 28 x 512 x top-10 stack with the experts split across the N
+    ranks (512/N each, contiguous blocks), the routers replicated, decode batches of B tokens
+    (default B = N: a fixed expert load per GPU as N grows). A step = the batch through all 28
+    layers: per layer router + top-k, local experts, and one kernel that exchanges the expert
+    outputs over NVLink (peer stores) and combines them -- the whole step one CUDA graph."""
+    import torch
+    import torch.distributed as dist
+
+    from moe_offload_b200.ep import EPDecodeStack, expert_shard
+    from moe_offload_b200.synthetic import C4, dev_bf16_normal, dev_stack_shard
+
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    cfg = C4
+    L = args.layers or cfg.layers
+    B = args.batch or world
+    first, n = expert_shard(cfg.experts, rank, world)
+    layers = dev_stack_shard(cfg, dev, first, n, layers=L)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(cfg.seed)                       # the same batch on every rank
+    n_in = args.warmup + args.steps
+    h0 = dev_bf16_normal((n_in, B, cfg.hidden), dev, gen)
+    st = EPDecodeStack(layers, cfg.experts, first, cfg.top_k, B, dev)
+    torch.cuda.synchronize()
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    for i in range(args.warmup):
+        st.step_device(h0[i])
+    torch.cuda.synchronize()
+    barrier()
+    clk = ClockSampler(local_rank)
+    clk.start()
+    torch.cuda.synchronize()
+    barrier()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for i in range(args.steps):
+        st.step_device(h0[args.warmup + i])
+    e.record()
+    torch.cuda.synchronize()
+    barrier()
+    clocks = clk.stop()
+    t_ms = s.elapsed_time(e)
+    # expert bytes this rank had to read in the last step: its unique routed experts per layer
+    inds = st.inds.cpu().numpy()
+    uniq = sum(len({int(v) for v in inds[l].ravel() if first <= v < first + n}) for l in range(L))
+    stats = torch.tensor([t_ms, float(uniq)], dtype=torch.float64, device=dev)
+    if world > 1:
+        tmax = stats[:1].clone()
+        dist.all_reduce(tmax, op=dist.ReduceOp.MAX)
+        usum = stats[1:].clone()
+        dist.all_reduce(usum, op=dist.ReduceOp.SUM)
+        t_ms, uniq_all = float(tmax.item()), float(usum.item())
+    else:
+        uniq_all = float(uniq)
+    value = B * args.steps / (t_ms / 1000.0)
+    from moe_offload_b200 import _lib
+    dev_err = int(_lib.call("moe_device_error", 1))
+
+    e2e = None
+    if not args.no_e2e:
+        hh = h0.cpu().pin_memory()
+        out_host = torch.empty((B, cfg.hidden), dtype=torch.bfloat16, pin_memory=True)
+        for i in range(min(args.warmup, 3)):
+            st.decode(hh[i], out_host)
+        torch.cuda.synchronize()
+        barrier()
+        s2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s2.record()
+        for i in range(args.steps):
+            st.decode(hh[args.warmup + i], out_host)
+        e2.record()
+        torch.cuda.synchronize()
+        barrier()
+        t2 = s2.elapsed_time(e2)
+        if world > 1:
+            tt = torch.tensor([t2], device=dev)
+            dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+            t2 = float(tt.item())
+        e2e = {"value": round(B * args.steps / (t2 / 1000.0), 2), "unit": UNIT,
+               "h2d_bytes_per_step": B * cfg.hidden * 2, "d2h_bytes_per_step": B * cfg.hidden * 2,
+               "api": "moe_offload_b200.ep.EPDecodeStack.decode (pinned host in/out, sync per step, every rank)"}
+    peak, peak_kind = peaks()
+    step_bytes = uniq_all * cfg.expert_bytes + world * L * cfg.router_bytes
+    achieved = step_bytes / (t_ms / 1000.0 / args.steps) / 1e9
+    roof = {"kernel": "expert-parallel step (router, gate/up, down, NVLink exchange + combine per layer)",
+            "bound": "hbm", "achieved": round(achieved, 1), "peak": round(peak * world, 1), "unit": "GB/s",
+            "frac": round(achieved / (peak * world), 4), "traffic": None,
+            "algorithmic_bytes_per_launch": int(step_bytes), "peak_source": f"{peak_kind} x {world} GPUs",
+            "unique_experts_per_layer": round(uniq_all / L, 2)}
+    if rank == 0:
+        line = {"metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": round(t_ms / args.steps, 4), "higher_is_better": True,
+                "scaling": "weak" if not args.batch else "strong", "vs_baseline": None,
+                "dtype": "u2 codes x bf16 -> f32", "data": "synthetic",
+                "config": {"workload": f"{cfg.name}_batch{B}", "layers": L, "hidden": cfg.hidden,
+                           "experts": cfg.experts, "top_k": cfg.top_k, "inter": cfg.inter, "batch": B,
+                           "group_size": cfg.group_size, "scales": "fp16", "router": "bf16 (replicated)",
+                           "parallelism": f"ep{world} (experts {cfg.experts}/{world} per GPU)",
+                           "exchange": "peer stores over NVLink + epoch flags (CUDA IPC), no library collective",
+                           "l2": "inputs larger than L2"},
+                "roofline": roof, "clocks": clocks, "gpu_launches": st.launches_per_step * args.steps,
+                "device_error": dev_err, "e2e": e2e, "cpu_baseline": None}
+        print(json.dumps(line), flush=True)
+    st.close()
+
+
 def main() -> int:
     args = parse()
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -532,6 +645,8 @@ def main() -> int:
         torch.cuda.set_device(local_rank)
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
                                 device_id=torch.device("cuda", local_rank))
+    if world > 1 and args.config == "c1":
+        args.config = "c4"          # the resident stack at N > 1 runs expert-parallel
     try:
         if args.impl == "reference":
             run_reference(args, rank, world)
@@ -539,6 +654,8 @@ def main() -> int:
             run_c2(args, rank, world, local_rank)
         elif args.config in ("c3", "c3n"):
             run_c3(args, rank, world, local_rank)
+        elif args.config == "c4":
+            run_c4(args, rank, world, local_rank)
         else:
             run_ours(args, rank, world, local_rank)
     finally:

@@ -242,6 +242,50 @@ int moe_prefill_layer(const void *x, int T, int H, int I, int E, int K, const vo
                       void *y, void *workspace, size_t workspace_bytes, void *stream);
 
 /* ------------------------------------------------------------------------------------ */
+/* Expert parallelism: one process per GPU, experts split in contiguous blocks.           */
+/* ------------------------------------------------------------------------------------ */
+
+/* Bytes of a CUDA IPC handle as moe_ep_buffer_alloc writes it. */
+#define MOE_EP_HANDLE_BYTES 64
+
+/* Bytes of one rank's exchange buffer for batches of up to T tokens (flags + two receive
+ * buffers [T][K][H] bf16). */
+size_t moe_ep_buffer_bytes(int T, int K, int H);
+
+/* Allocates (cudaMalloc) and zero-fills an exchange buffer on the current device and writes
+ * its CUDA IPC handle (MOE_EP_HANDLE_BYTES) to out_handle for the other ranks. */
+int moe_ep_buffer_alloc(size_t bytes, void **out_ptr, void *out_handle);
+
+/* Maps another rank's exchange buffer from its handle (cudaIpcOpenMemHandle, peer access
+ * enabled); moe_ep_buffer_close unmaps it, moe_ep_buffer_free frees this rank's own. */
+int moe_ep_buffer_open(const void *handle, void **out_ptr);
+int moe_ep_buffer_close(void *ptr);
+int moe_ep_buffer_free(void *ptr);
+
+/* Workspace bytes for moe_ep_decode_layer; zero-fill it once before first use. */
+size_t moe_ep_workspace_bytes(int T, int H, int I, int E, int K);
+
+/*
+ * One decode step of a layer whose E experts are split across nranks GPUs: this rank holds
+ * experts [e_begin, e_begin + e_count) (weights in the MLX layout, indexed from e_begin) and
+ * the whole bf16 router [E, H]. Router (+ norm as in moe_decode_layer) and top-k run on every
+ * rank (identical results), the local experts run on their (token, k) slots, and one kernel
+ * exchanges the unweighted expert outputs over NVLink (peer stores into every rank's exchange
+ * buffer, bounded waits on per-rank epoch flags) and combines them in MLX order:
+ * y = bf16(resid + sum_k bf16(yk * score_k)), the same bits on every rank and as
+ * moe_decode_layer. peers: device array [nranks] of exchange-buffer pointers (this rank's own
+ * at [rank], the others from moe_ep_buffer_open), all sized for at least T tokens. Every rank
+ * must call this the same number of times, in the same order, with the same T. Replaces the
+ * per-layer decode body of mlx-qwen38/loader.py:903-922 (single device in the reference).
+ */
+int moe_ep_decode_layer(const void *x, int T, int H, int I, int E, int K, int e_begin, int e_count,
+                        const void *router_w, const uint32_t *wg, const void *sg, const void *bg,
+                        const uint32_t *wu, const void *su, const void *bu, const uint32_t *wd,
+                        const void *sd, const void *bd, int sb_fp16, int norm, const void *resid,
+                        void *const *peers, int rank, int nranks, uint32_t *out_inds, void *out_scores,
+                        void *y, void *workspace, size_t workspace_bytes, void *stream);
+
+/* ------------------------------------------------------------------------------------ */
 /* Per-layer LRU expert-slot cache with its state on the GPU.                             */
 /* ------------------------------------------------------------------------------------ */
 
@@ -346,7 +390,7 @@ void c_get_decode_totals(int num_layers, uint64_t *out6);
 
 /*
  * Device-side error word (bit 1: a bounded mbarrier/flag wait gave up, bit 2: invalid
- * input seen by a kernel). Returns the current value (>= 0) and clears it when `clear`.
+ * input seen by a kernel, bit 4: an expert-parallel peer did not signal within 2 s). Returns the current value (>= 0) and clears it when `clear`.
  * Kernels never trap: they record the condition here and skip the affected work.
  */
 int moe_device_error(int clear);

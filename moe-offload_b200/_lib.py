@@ -48,6 +48,13 @@ SIGNATURES: dict[str, tuple] = {
     "moe_prefill_experts": (I, [P, I, I, I, I, I, P, P, P, P, P, P, P, P, P, P, P, I, P, P, P, P, SZ, P]),
     "moe_prefill_layer_workspace_bytes": (SZ, [I, I, I, I, I]),
     "moe_prefill_layer": (I, [P, I, I, I, I, I, P] + [P] * 9 + [I, I, P, P, P, P, P, SZ, P]),
+    "moe_ep_buffer_bytes": (SZ, [I, I, I]),
+    "moe_ep_buffer_alloc": (I, [SZ, P, P]),
+    "moe_ep_buffer_open": (I, [P, P]),
+    "moe_ep_buffer_close": (I, [P]),
+    "moe_ep_buffer_free": (I, [P]),
+    "moe_ep_workspace_bytes": (SZ, [I, I, I, I, I]),
+    "moe_ep_decode_layer": (I, [P, I, I, I, I, I, I, I, P] + [P] * 9 + [I, I, P, P, I, I, P, P, P, P, SZ, P]),
     "moe_lru_state_bytes": (SZ, [I, I]),
     "moe_lru_init": (I, [P, I, I, U64, P]),
     "moe_lru_reset": (I, [P, I, I, I, P]),

@@ -89,6 +89,7 @@ MOE_D uint16_t ldg_u16(const uint16_t *p) { return __ldg(p); }
 
 #define MOE_DEVERR_MBAR_TIMEOUT 1u
 #define MOE_DEVERR_BAD_INPUT 2u
+#define MOE_DEVERR_PEER_TIMEOUT 4u      // an expert-parallel peer did not signal within the limit
 
 extern __device__ unsigned int g_moe_device_error;
 

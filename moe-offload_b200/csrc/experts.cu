@@ -20,6 +20,7 @@
 //            CTA combines the K experts with the routing scores (loader.py:914,965).
 #include "common.cuh"
 #include "gemv_i8.cuh"
+#include "internal.h"
 
 namespace {
 
@@ -41,6 +42,7 @@ struct GuArgs {
     uint2 *arec;                 // optional records of act ([T][K][ngI][16])
     float *ascale, *asum;        // [T][pad4(K*ngI)]
     unsigned int *acnt;          // [T][K][ngI] tickets, zero between launches
+    uint32_t slot_base;          // slot = slots[] - slot_base (expert-parallel shards); >= cap: skipped
 };
 
 struct GuLayout {
@@ -90,7 +92,7 @@ __global__ void __launch_bounds__(kGuWarps * 32) gateup_kernel(GuArgs a) {
     pdl_wait();                       // router (slots, x records) and the producer of x are done
     pdl_launch_dependents();
 
-    const uint32_t slot_raw = a.slots[(size_t)tok * K + k];
+    const uint32_t slot_raw = a.slots[(size_t)tok * K + k] - a.slot_base;
     const bool sok = slot_raw < (uint32_t)a.cap;
     const size_t row0 = (size_t)(sok ? slot_raw : 0) * I + r0;
     const uint32_t cb = 8u * rowb, sb = 8u * ng * 2u;
@@ -216,6 +218,7 @@ struct DnArgs {
     int H, I, K, cap;
     const uint16_t *addend, *resid;
     uint16_t *y, *yk;
+    uint32_t slot_base;          // as GuArgs::slot_base
 };
 
 struct DnLayout {
@@ -265,7 +268,7 @@ __global__ void __launch_bounds__(kMaxK * 32) down_kernel(DnArgs a) {
     // The routing (slots) was produced two kernels back and is complete once the gate/up
     // kernel has started (it waits on the router before triggering this launch), so the
     // weight copies go out before waiting on the activations.
-    const uint32_t slot_raw = a.slots[(size_t)tok * K + k];
+    const uint32_t slot_raw = a.slots[(size_t)tok * K + k] - a.slot_base;
     const bool sok = slot_raw < (uint32_t)a.cap;
     const size_t row0 = (size_t)(sok ? slot_raw : 0) * H + r0;
     const uint32_t cb = 16u * rowb, sb = 16u * ng * 2u;
@@ -378,7 +381,7 @@ int moe_experts_gateup_ex(const void *x, const void *xrec, const float *xscale, 
                           int H, int I, int K, int cap, const uint32_t *slots, const uint32_t *wg,
                           const void *sg, const void *bg, const uint32_t *wu, const void *su, const void *bu,
                           int bits, int group_size, int sb_fp16, void *act, void *arec, float *ascale,
-                          float *asum, unsigned int *acnt, void *stream) {
+                          float *asum, unsigned int *acnt, void *stream, uint32_t slot_base) {
     int rc = check_common(H, I, K, T, cap, bits, group_size, "experts_gateup");
     if (rc) return rc;
     if (!x || !slots || !wg || !wu || !sg || !bg || !su || !bu || !act)
@@ -395,7 +398,7 @@ int moe_experts_gateup_ex(const void *x, const void *xrec, const float *xscale, 
     GuArgs a{static_cast<const uint16_t *>(x), static_cast<const uint2 *>(xrec), xscale, xsum, slots, wg, wu,
              static_cast<const uint16_t *>(sg), static_cast<const uint16_t *>(bg),
              static_cast<const uint16_t *>(su), static_cast<const uint16_t *>(bu), H, I, K, cap,
-             static_cast<uint16_t *>(act), static_cast<uint2 *>(arec), ascale, asum, acnt};
+             static_cast<uint16_t *>(act), static_cast<uint2 *>(arec), ascale, asum, acnt, slot_base};
     dim3 grid(I / 8, K, T);
     cudaError_t e = sb_fp16 ? launch_pdl(gateup_kernel<true>, grid, dim3(kGuWarps * 32), L.total, as_stream(stream), a)
                             : launch_pdl(gateup_kernel<false>, grid, dim3(kGuWarps * 32), L.total, as_stream(stream), a);
@@ -406,7 +409,8 @@ int moe_experts_gateup_ex(const void *x, const void *xrec, const float *xscale, 
 int moe_experts_down_ex(const void *act, const void *arec, const float *ascale, const float *asum, int T, int H,
                         int I, int K, int cap, const uint32_t *slots, const void *scores, const uint32_t *wd,
                         const void *sd, const void *bd, int bits, int group_size, int sb_fp16,
-                        const void *addend, const void *resid, void *y, void *yk, void *stream) {
+                        const void *addend, const void *resid, void *y, void *yk, void *stream,
+                        uint32_t slot_base) {
     int rc = check_common(H, I, K, T, cap, bits, group_size, "experts_down");
     if (rc) return rc;
     if (!act || !slots || !wd || !sd || !bd) return moe_set_error(MOE_EINVAL, "experts_down: null pointer");
@@ -422,7 +426,8 @@ int moe_experts_down_ex(const void *act, const void *arec, const float *ascale, 
     DnArgs a{static_cast<const uint16_t *>(act), static_cast<const uint2 *>(arec), ascale, asum, slots,
              static_cast<const uint16_t *>(scores), wd, static_cast<const uint16_t *>(sd),
              static_cast<const uint16_t *>(bd), H, I, K, cap, static_cast<const uint16_t *>(addend),
-             static_cast<const uint16_t *>(resid), static_cast<uint16_t *>(y), static_cast<uint16_t *>(yk)};
+             static_cast<const uint16_t *>(resid), static_cast<uint16_t *>(y), static_cast<uint16_t *>(yk),
+             slot_base};
     dim3 grid(H / 16, T);
     cudaError_t e = sb_fp16 ? launch_pdl(down_kernel<true>, grid, dim3(K * 32), L.total, as_stream(stream), a)
                             : launch_pdl(down_kernel<false>, grid, dim3(K * 32), L.total, as_stream(stream), a);

@@ -12,13 +12,17 @@ int moe_router_launch(const void *x, int T, int H, int E, int K, const void *w,
                       unsigned int *tickets, uint16_t *logits_buf, uint16_t *plogits_buf,
                       void *xrec, float *xscale, float *xsum, int norm, void *stream);
 
+// slot_base: the kernels use slots[] - slot_base as the slot id (a rank holding experts
+// [slot_base, slot_base + cap) of an expert-parallel shard); ids outside the shard are skipped
+// (their outputs are zero).
 int moe_experts_gateup_ex(const void *x, const void *xrec, const float *xscale, const float *xsum, int T,
                           int H, int I, int K, int cap, const uint32_t *slots, const uint32_t *wg,
                           const void *sg, const void *bg, const uint32_t *wu, const void *su, const void *bu,
                           int bits, int group_size, int sb_fp16, void *act, void *arec, float *ascale,
-                          float *asum, unsigned int *acnt, void *stream);
+                          float *asum, unsigned int *acnt, void *stream, uint32_t slot_base = 0);
 
 int moe_experts_down_ex(const void *act, const void *arec, const float *ascale, const float *asum, int T, int H,
                         int I, int K, int cap, const uint32_t *slots, const void *scores, const uint32_t *wd,
                         const void *sd, const void *bd, int bits, int group_size, int sb_fp16,
-                        const void *addend, const void *resid, void *y, void *yk, void *stream);
+                        const void *addend, const void *resid, void *y, void *yk, void *stream,
+                        uint32_t slot_base = 0);

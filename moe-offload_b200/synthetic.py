@@ -55,6 +55,7 @@ C3 = StackConfig("c3_prefill_28x512_top10_T2048", 28, 3072, 512, 10, 768, seed=3
 C3_TOKENS = 2048
 NEMOTRON = StackConfig("c3_nemotron_shape_240_top9", 1, 2688, 240, 9, 1856, seed=3)
 NEMOTRON_TOKENS = 1024
+C4 = StackConfig("c4_expert_parallel_28x512_top10", 28, 3072, 512, 10, 768, seed=4)
 
 
 # ------------------------------------------------------------------------------ numpy
@@ -138,5 +139,23 @@ def dev_stack(cfg: StackConfig, device, layers: int | None = None) -> list[Exper
         gate = dev_qmatrix(cfg.experts, cfg.inter, cfg.hidden, device, gen, cfg.bits, cfg.group_size)
         up = dev_qmatrix(cfg.experts, cfg.inter, cfg.hidden, device, gen, cfg.bits, cfg.group_size)
         down = dev_qmatrix(cfg.experts, cfg.hidden, cfg.inter, device, gen, cfg.bits, cfg.group_size)
+        out.append(ExpertLayer(router, gate, up, down))
+    return out
+
+
+def dev_stack_shard(cfg: StackConfig, device, first: int, count: int, layers: int | None = None) -> list[ExpertLayer]:
+    """An expert-parallel rank's part of a synthetic stack: every layer's whole router (the
+    same on every rank: one generator seeded with cfg.seed) and experts [first, first + count)
+    (a generator seeded with the seed and the block's first expert)."""
+    gr = torch.Generator(device=device)
+    gr.manual_seed(cfg.seed)
+    ge = torch.Generator(device=device)
+    ge.manual_seed(cfg.seed * 1_000_003 + first)
+    out = []
+    for _ in range(cfg.layers if layers is None else layers):
+        router = dev_bf16_normal((cfg.experts, cfg.hidden), device, gr, 0.02)
+        gate = dev_qmatrix(count, cfg.inter, cfg.hidden, device, ge, cfg.bits, cfg.group_size)
+        up = dev_qmatrix(count, cfg.inter, cfg.hidden, device, ge, cfg.bits, cfg.group_size)
+        down = dev_qmatrix(count, cfg.hidden, cfg.inter, device, ge, cfg.bits, cfg.group_size)
         out.append(ExpertLayer(router, gate, up, down))
     return out
