@@ -56,7 +56,7 @@ def build(verbose: bool = False, ptxas_info: bool = False, jobs: int = 8) -> str
             _drain(procs, verbose or ptxas_info)
     _drain(procs, verbose or ptxas_info)
     if cmds or not os.path.exists(LIB):
-        link = [NVCC] + ARCH + ["-shared", "-rdc=true", "-o", LIB] + objs + ["-lcuda"]
+        link = [NVCC] + ARCH + ["-shared", "-rdc=true", "-o", LIB] + objs
         if verbose:
             print(" ".join(link))
         subprocess.run(link, check=True)

@@ -1,5 +1,5 @@
 // Prefill experts: T tokens x K routed experts as expert-grouped GEMMs on the 5th-generation
-// tensor cores (tcgen05.mma, accumulators in TMEM).
+// tensor cores (tcgen05.mma, accumulators in TMEM), fed by TMA.
 //
 // Reference semantics: the prefill branch of CachedSwitchGLU (mlx-qwen38/loader.py:566-699;
 // C++ run_moe_prefill, cpp/src/layers.cpp:403-600) sorts the (token, k) assignments by
@@ -7,39 +7,47 @@
 // weights by the routing scores. Here:
 //
 //   bucket   assignments grouped by expert (counts, exclusive scan, scatter) and a tile list
-//            (expert, 128-row block of the weight matrix, block of <= 256 of its tokens)
-//   gateup   per tile D_g = Wg[rows] . X^T and D_u = Wu[rows] . X^T with M = 128 weight rows
-//            and N = the expert's tokens (padded to 16): the 2-bit codes are dequantised to
-//            bf16 (w = s*q + b, one rounding) straight into shared memory in the canonical
-//            K-major core-matrix layout, the tokens' rows of x are gathered next to them,
-//            one thread issues the MMAs (K = 16 each) into two TMEM accumulators, and the
-//            epilogue (tcgen05.ld) applies SwiGLU with MLX's bf16 roundings -> act[pos][I]
+//            (expert, 128-row block of the weight matrix, block of <= 128 of its tokens)
+//   gateup   per tile D_g = Wg[rows] . X^T and D_u = Wu[rows] . X^T, M = 128 weight rows,
+//            N = the expert's tokens (padded to 16), K = H in blocks of 64 (one 2-bit group)
 //   down     the same GEMM with Wd and the act rows (contiguous per expert) -> yk[pos][H]
 //   combine  y[t] = resid[t] + sum_k bf16(yk[pos(t,k)] * s[t,k]), sequential bf16 in MLX order
 //
-// Shared memory per K-block stage (64 columns of K): A = 128 rows x 64 bf16 per weight
-// matrix (16 KB), B = up to 256 token rows x 64 bf16 (32 KB); two stages alternate so the
-// dequantisation of block kb+1 overlaps the MMAs of block kb (tcgen05.commit -> mbarrier).
+// The GEMM kernel is persistent (one CTA per SM) and warp-specialised:
+//   warp 0      TMA producer: raw 2-bit codes of the tile's 128 rows, 8 K-blocks (128 bytes
+//               of codes per row) per 2-D box, 128-byte swizzled; the B operand per K-block in
+//               16-row boxes of expert-ordered rows (gate/up: x rows gathered into position
+//               order by one copy kernel; down: the act rows), 128-byte swizzled
+//   warps 6-13  dequantise one K-block of codes to bf16, w = bf16(s * q + b) with one
+//               rounding, into the 128-byte-swizzled K-major layout the MMA reads: the four
+//               values of a (row, group) are built once and every pair of codes becomes a
+//               bf16x2 word with one byte permute (selectors built 8 codes at a time)
+//   warp 1      one thread issues the tcgen05.mma (K = 16 each) into TMEM; the accumulators
+//               are double-buffered across tiles
+//   warps 2-5   epilogue: tcgen05.ld of the accumulators, SwiGLU with MLX's bf16 roundings
+//               (gate/up) or the bf16 rounding (down), stores to global
+// Stages hand over through mbarriers (TMA transaction counts, tcgen05.commit, warp
+// arrivals); every wait is bounded.
+#include <cuda.h>
+
 #include "common.cuh"
 #include "internal.h"
 
 namespace {
 
-constexpr int kThreads = 256;
 constexpr int kBM = 128;          // weight rows per tile (MMA M)
-constexpr int kBK = 64;           // K per stage (one 2-bit group)
-constexpr int kMaxBN = 256;       // tokens per tile (MMA N)
-constexpr int kATile = kBM * kBK * 2;          // 16 KB
-constexpr int kBTile = kMaxBN * kBK * 2;       // 32 KB
-constexpr uint32_t kTmemCols = 512;
+constexpr int kBK = 64;           // K per block (one 2-bit group)
+constexpr int kMaxBN = 128;       // tokens per tile (MMA N)
 
-// ------------------------------------------------------------------ tcgen05 helpers (PTX)
+// ------------------------------------------------------------------ tcgen05 / TMA helpers (PTX)
 
-MOE_D uint64_t smem_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
-    // K-major, no swizzle: start, leading (K-chunk) and stride (8-row group) byte offsets in
-    // 16-byte units, descriptor version 1 (bits 46-47), layout type 0 (bits 61-63)
-    return (uint64_t)((saddr >> 4) & 0x3FFF) | ((uint64_t)((lbo >> 4) & 0x3FFF) << 16) |
-           ((uint64_t)((sbo >> 4) & 0x3FFF) << 32) | (1ull << 46);
+// Shared-memory matrix descriptor for a K-major operand in the 128-byte-swizzle layout: rows
+// of 128 bytes (64 bf16 of K), 8-row groups 1024 bytes apart (stride byte offset), descriptor
+// version 1 (bits 46-47), layout type 2 = SWIZZLE_128B (bits 61-63). The K = 16 steps inside
+// a 64-wide block advance the start address by 32 bytes.
+MOE_D uint64_t desc_sw128(uint32_t saddr) {
+    return (uint64_t)((saddr >> 4) & 0x3FFF) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) | (1ull << 46) |
+           (2ull << 61);
 }
 
 // instruction descriptor, kind::f16: D f32, A and B bf16, both K-major, N, M = 128
@@ -73,6 +81,55 @@ MOE_D void tmem_ld16(uint32_t taddr, float (&v)[16]) {
 
 MOE_D void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 MOE_D void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+MOE_D void mbar_arrive(uint64_t *bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
+}
+
+// 2-D tiled TMA load (no multicast) completing on an mbarrier; x is the innermost coordinate
+MOE_D void tma_load_2d(void *dst, const CUtensorMap *map, int x, int y, uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::
+            "r"(smem_addr(dst)),
+        "l"(map), "r"(x), "r"(y), "r"(smem_addr(bar))
+        : "memory");
+}
+
+MOE_D uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
+    uint32_t d;
+    asm("prmt.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(sel));
+    return d;
+}
+
+// byte offset of 16-byte chunk c of row r in a 128-byte-swizzled tile of 128-byte rows
+MOE_D uint32_t sw128(int r, int c) { return (uint32_t)((r >> 3) * 1024 + (r & 7) * 128 + ((c ^ (r & 7)) << 4)); }
+
+// Dequantisation tables of one (row, group): tlo / thi hold the low / high bytes of the four
+// bf16 values v_q = bf16(s * q + b), q = 0..3 (byte q).
+template <bool kFp16>
+MOE_D void dq_tables(uint16_t sraw, uint16_t braw, uint32_t &tlo, uint32_t &thi) {
+    const float s = sb_to_f32<kFp16>(sraw), b = sb_to_f32<kFp16>(braw);
+    const uint32_t p01 = (uint32_t)f32_to_bf16_bits(b) | ((uint32_t)f32_to_bf16_bits(s + b) << 16);
+    const uint32_t p23 = (uint32_t)f32_to_bf16_bits(fmaf(s, 2.f, b)) | ((uint32_t)f32_to_bf16_bits(fmaf(s, 3.f, b)) << 16);
+    tlo = prmt(p01, p23, 0x6420u);
+    thi = prmt(p01, p23, 0x7531u);
+}
+
+// 16 codes (code j in bits 2j..2j+1) -> 16 bf16 (two 16-byte chunks, element j at j).
+// Output word m (elements 2m, 2m+1) = prmt(tlo, thi, [q_2m, q_2m + 4, q_2m+1, q_2m+1 + 4]).
+MOE_D void dq_word(uint32_t w, uint32_t tlo, uint32_t thi, uint4 &c0, uint4 &c1) {
+    const uint32_t Y = w & 0x33333333u;             // nibble j: code 2j
+    const uint32_t Z = (w >> 2) & 0x33333333u;      // nibble j: code 2j + 1
+    // byte b: [q, q + 4] nibble pairs of codes 4b (YYe), 4b + 2 (YYo), 4b + 1 (ZZe), 4b + 3 (ZZo)
+    const uint32_t YYe = (Y & 0x0F0F0F0Fu) * 0x11u + 0x40404040u;
+    const uint32_t YYo = ((Y >> 4) & 0x0F0F0F0Fu) * 0x11u + 0x40404040u;
+    const uint32_t ZZe = (Z & 0x0F0F0F0Fu) * 0x11u + 0x40404040u;
+    const uint32_t ZZo = ((Z >> 4) & 0x0F0F0F0Fu) * 0x11u + 0x40404040u;
+    const uint32_t s02 = prmt(YYe, ZZe, 0x5140u), s46 = prmt(YYe, ZZe, 0x7362u);
+    const uint32_t s13 = prmt(YYo, ZZo, 0x5140u), s57 = prmt(YYo, ZZo, 0x7362u);
+    c0 = make_uint4(prmt(tlo, thi, s02), prmt(tlo, thi, s13), prmt(tlo, thi, s02 >> 16), prmt(tlo, thi, s13 >> 16));
+    c1 = make_uint4(prmt(tlo, thi, s46), prmt(tlo, thi, s57), prmt(tlo, thi, s46 >> 16), prmt(tlo, thi, s57 >> 16));
+}
 
 // ------------------------------------------------------------------ bucketing
 
@@ -164,185 +221,269 @@ __global__ void scatter_kernel(const uint32_t *inds, int TK, int E, const int *o
     }
 }
 
+// xs[p] = x[src_of[p] / K]: the B rows of the gate/up GEMM in expert order (16-byte copies)
+__global__ void gather_rows_kernel(const uint16_t *x, const int *src_of, int TK, int K, int H, uint16_t *xs) {
+    const int cpr = H / 8;
+    const size_t n = (size_t)TK * cpr;
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
+        const size_t p = i / cpr;
+        const int c = (int)(i % cpr);
+        const int src = src_of[p];
+        if (src < 0) continue;
+        *reinterpret_cast<uint4 *>(xs + p * H + (size_t)c * 8) =
+            *reinterpret_cast<const uint4 *>(x + (size_t)(src / K) * H + (size_t)c * 8);
+    }
+}
+
 // ------------------------------------------------------------------ grouped GEMM
+
+constexpr int kRawK = 8;                         // K-blocks per raw code stage (128 B of codes per row)
+constexpr int kRS = 2;                           // raw code stages
+constexpr int kGemmThreads = 448;                // 14 warps
+constexpr int kDqWarp0 = 6, kDqWarps = 8;
+constexpr int kEpiWarp0 = 2;
+constexpr int kTile = kBM * 128;                 // one 128-row x 128-byte tile: 16 KB
+constexpr uint32_t kTmemCols = 512;              // two accumulator buffers of 256 columns
 
 struct GemmArgs {
     const Tile *tiles;
     const int *ntiles;
-    int Kdim, R;                      // reduction length, weight rows per expert
-    const uint32_t *w0, *w1;          // codes [E][R][Kdim/16] (w1: up, gate/up GEMM only)
-    const uint16_t *s0, *b0, *s1, *b1;
-    const uint16_t *xrows;            // B rows: x [T][Kdim] (gather via src_of / K) or act [pos][Kdim]
-    const int *src_of;                // gate/up: assignment index of each position (token = idx / K)
-    int K;
+    int Kdim, R, K;                   // reduction length, weight rows per expert, top-k
+    const uint16_t *s0, *b0, *s1, *b1;   // scales / biases [E][R][Kdim/64] (1: up, gate/up only)
     uint16_t *out;                    // gate/up: act [pos][R]; down: yk [pos][R]
 };
 
-// Dequantises chunks [c0, c0 + nc) (8 codes each) of tile row r for K-block kb (group kb of
-// the row) into the canonical K-major layout: element (row, k) at chunk (k / 8) * LBO +
-// (row / 8) * 128 + (row % 8) * 16 + (k % 8) * 2, LBO = 128 / 8 * 128 = 2048 bytes.
-// w = bf16(s * q + b), one rounding.
-template <bool kFp16>
-MOE_D void dequant_row(const uint32_t *w, const uint16_t *s, const uint16_t *b, int row0, int e, int R, int Kdim,
-                       int kb, unsigned char *dst, int r, int c0, int nc) {
-    const int row = row0 + r;
-    uint32_t words[4] = {0u, 0u, 0u, 0u};
-    float sc = 0.f, bi = 0.f;
-    if (row < R) {
-        const uint4 q = *reinterpret_cast<const uint4 *>(w + ((size_t)e * R + row) * (Kdim / 16) + (size_t)kb * 4);
-        words[0] = q.x;
-        words[1] = q.y;
-        words[2] = q.z;
-        words[3] = q.w;
-        const size_t si = ((size_t)e * R + row) * (Kdim / 64) + kb;
-        sc = sb_to_f32<kFp16>(s[si]);
-        bi = sb_to_f32<kFp16>(b[si]);
-    }
-#pragma unroll
-    for (int cc = 0; cc < 8; ++cc) {
-        if (cc < c0 || cc >= c0 + nc) continue;
-        const uint32_t bits = words[cc >> 1] >> ((cc & 1) * 16);     // codes 8cc .. 8cc+7
-        uint32_t o[4];
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            const float v0 = fmaf(sc, (float)((bits >> (4 * j)) & 3u), bi);
-            const float v1 = fmaf(sc, (float)((bits >> (4 * j + 2)) & 3u), bi);
-            o[j] = (uint32_t)f32_to_bf16_bits(v0) | ((uint32_t)f32_to_bf16_bits(v1) << 16);
-        }
-        *reinterpret_cast<uint4 *>(dst + cc * 2048 + (r >> 3) * 128 + (r & 7) * 16) = make_uint4(o[0], o[1], o[2], o[3]);
-    }
-}
-
-// B stage: n token rows x 64 bf16 of K-block kb, zero beyond n; layout chunk c at c * LBOB,
-// LBOB = BN / 8 * 128
-MOE_D void load_b_stage(const uint16_t *xrows, const int *src_of, int K, bool gather, int pos0, int n, int BN,
-                        int Kdim, int kb, unsigned char *dst, int tid_in, int nthr) {
-    const uint32_t lbo = (uint32_t)(BN / 8) * 128u;
-    for (int it = tid_in; it < BN * 8; it += nthr) {
-        const int tok = it % BN, c = it / BN;
-        uint4 v = make_uint4(0u, 0u, 0u, 0u);
-        if (tok < n) {
-            const int p = pos0 + tok;
-            const size_t row = gather ? (size_t)(src_of[p] / K) : (size_t)p;
-            v = *reinterpret_cast<const uint4 *>(xrows + row * Kdim + (size_t)kb * 64 + c * 8);
-        }
-        *reinterpret_cast<uint4 *>(dst + c * lbo + (tok >> 3) * 128 + (tok & 7) * 16) = v;
-    }
-}
+template <bool kGateUp>
+struct GemmSmem {
+    static constexpr int kNM = kGateUp ? 2 : 1;       // weight matrices per tile
+    static constexpr int kKS = kGateUp ? 3 : 4;       // K-block stages
+    static constexpr size_t raw = 0;                                       // [kRS][kNM] tiles
+    static constexpr size_t a = raw + (size_t)kRS * kNM * kTile;           // [kKS][kNM] tiles
+    static constexpr size_t b = a + (size_t)kKS * kNM * kTile;             // [kKS] tiles
+    static constexpr size_t bars = b + (size_t)kKS * kTile;
+    // raw_full, raw_empty [kRS]; full, empty [kKS]; acc_full, acc_empty [2]; tmem slot
+    static constexpr size_t total = bars + (2 * kRS + 2 * kKS + 4) * 8 + 16;
+    static constexpr size_t alloc = total + 1024;      // + alignment slack
+};
 
 template <bool kGateUp, bool kFp16>
-__global__ void __launch_bounds__(kThreads, 1) gemm_kernel(GemmArgs a) {
-    extern __shared__ __align__(1024) unsigned char smem[];
-    constexpr int nA = kGateUp ? 2 : 1;
-    unsigned char *stA[2], *stB[2];
-    for (int s = 0; s < 2; ++s) {
-        stA[s] = smem + s * (nA * kATile + kBTile);
-        stB[s] = stA[s] + nA * kATile;
-    }
-    uint64_t *mbar = reinterpret_cast<uint64_t *>(smem + 2 * (nA * kATile + kBTile));   // [2]
-    uint32_t *tslot = reinterpret_cast<uint32_t *>(mbar + 2);
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    gemm_kernel(const __grid_constant__ CUtensorMap map_w0, const __grid_constant__ CUtensorMap map_w1,
+                const __grid_constant__ CUtensorMap map_b, GemmArgs a) {
+    using SL = GemmSmem<kGateUp>;
+    constexpr int kNM = SL::kNM, kKS = SL::kKS;
+    extern __shared__ unsigned char smem_raw[];
+    unsigned char *smem = reinterpret_cast<unsigned char *>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+    uint64_t *raw_full = reinterpret_cast<uint64_t *>(smem + SL::bars);
+    uint64_t *raw_empty = raw_full + kRS;
+    uint64_t *full = raw_empty + kRS;
+    uint64_t *empty = full + kKS;
+    uint64_t *acc_full = empty + kKS;
+    uint64_t *acc_empty = acc_full + 2;
+    uint32_t *tslot = reinterpret_cast<uint32_t *>(acc_empty + 2);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
 
-    if (warp == 0) {
+    if (tid == 0) {
+        for (int i = 0; i < kRS; ++i) {
+            mbar_init(&raw_full[i], 1);
+            mbar_init(&raw_empty[i], kDqWarps);
+        }
+        for (int i = 0; i < kKS; ++i) {
+            mbar_init(&full[i], kDqWarps + 1);
+            mbar_init(&empty[i], 1);
+        }
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(&acc_full[i], 1);
+            mbar_init(&acc_empty[i], 4);
+        }
+        fence_barrier_init();
+    }
+    if (warp == 1) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(tslot)),
                      "r"(kTmemCols));
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::);
-    }
-    if (tid == 0) {
-        mbar_init(&mbar[0], 1);
-        mbar_init(&mbar[1], 1);
-        fence_barrier_init();
     }
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tslot;
-    uint32_t phase[2] = {0u, 0u};
-    int uses[2] = {0, 0};
     const int ntiles = *a.ntiles;
     const int nkb = a.Kdim / kBK;
 
-    for (int ti = blockIdx.x; ti < ntiles; ti += gridDim.x) {
-        const Tile tl = a.tiles[ti];
-        const int BN = (tl.n + 15) & ~15;
-        const uint32_t idesc = instr_desc_bf16(BN);
-        const uint32_t lboB = (uint32_t)(BN / 8) * 128u;
-        for (int kb = 0; kb < nkb; ++kb) {
-            const int s = kb & 1;
-            // the MMAs that read this stage two blocks ago must be done
-            if (uses[s] > 0) {
-                mbar_wait(&mbar[s], phase[s]);
-                phase[s] ^= 1u;
-                uses[s] = 0;
-            }
-            if (kGateUp) {           // threads 0..127: gate row tid, 128..255: up row tid - 128
-                if (tid < kBM) dequant_row<kFp16>(a.w0, a.s0, a.b0, tl.row0, tl.e, a.R, a.Kdim, kb, stA[s], tid, 0, 8);
-                else dequant_row<kFp16>(a.w1, a.s1, a.b1, tl.row0, tl.e, a.R, a.Kdim, kb, stA[s] + kATile, tid - kBM, 0, 8);
-            } else {                 // row tid % 128, chunks 0..3 or 4..7
-                dequant_row<kFp16>(a.w0, a.s0, a.b0, tl.row0, tl.e, a.R, a.Kdim, kb, stA[s], tid & (kBM - 1),
-                                   (tid >> 7) * 4, 4);
-            }
-            load_b_stage(a.xrows, a.src_of, a.K, kGateUp, tl.pos0, tl.n, BN, a.Kdim, kb, stB[s], tid, kThreads);
-            fence_barrier_init();        // generic-proxy smem writes -> visible to the tensor core (async proxy)
-            __syncthreads();
-            if (tid == 0) {
-                tc_fence_after();
-                const uint32_t aaddr = smem_addr(stA[s]), baddr = smem_addr(stB[s]);
-#pragma unroll
-                for (int j = 0; j < kBK / 16; ++j) {
-                    const uint64_t bd = smem_desc(baddr + 2 * j * lboB, lboB, 128);
-                    const uint32_t acc = (kb > 0 || j > 0) ? 1u : 0u;
-                    mma_bf16(tmem, smem_desc(aaddr + 2 * j * 2048, 2048, 128), bd, idesc, acc);
-                    if (kGateUp)
-                        mma_bf16(tmem + 256, smem_desc(aaddr + kATile + 2 * j * 2048, 2048, 128), bd, idesc, acc);
+    if (warp == 0) {
+        // ------------------------------------------------------------ TMA producer
+        uint32_t g = 0, rc = 0;
+        for (int ti = blockIdx.x; ti < ntiles; ti += gridDim.x) {
+            const Tile tl = a.tiles[ti];
+            const int wrow = tl.e * a.R + tl.row0;
+            const int nbox = (tl.n + 15) >> 4;
+            for (int kb = 0; kb < nkb; ++kb) {
+                if (kb % kRawK == 0) {
+                    const int rs = rc % kRS;
+                    mbar_wait(&raw_empty[rs], ((rc / kRS) & 1u) ^ 1u);
+                    if (lane == 0) {
+                        mbar_arrive_expect_tx(&raw_full[rs], kNM * kTile);
+                        tma_load_2d(smem + SL::raw + (size_t)(rs * kNM) * kTile, &map_w0, kb * 4, wrow, &raw_full[rs]);
+                        if (kGateUp)
+                            tma_load_2d(smem + SL::raw + (size_t)(rs * kNM + 1) * kTile, &map_w1, kb * 4, wrow,
+                                        &raw_full[rs]);
+                    }
+                    ++rc;
                 }
-                mma_commit(&mbar[s]);
+                const int s = g % kKS;
+                mbar_wait(&empty[s], ((g / kKS) & 1u) ^ 1u);
+                unsigned char *bst = smem + SL::b + (size_t)s * kTile;
+                if (lane == 0) mbar_arrive_expect_tx(&full[s], (uint32_t)nbox * 2048u);
+                __syncwarp();
+                // the tile's B rows: 16-row boxes of the expert-ordered rows (x gathered per
+                // position for gate/up, act for down)
+                if (lane < nbox) tma_load_2d(bst + (size_t)lane * 2048, &map_b, kb * 64, tl.pos0 + 16 * lane, &full[s]);
+                ++g;
             }
-            uses[s] = 1;
         }
-        // wait for the last block's MMAs (the commit of the final stage covers all earlier ones)
-        const int sl = (nkb - 1) & 1;
-        mbar_wait(&mbar[sl], phase[sl]);
-        phase[sl] ^= 1u;
-        uses[sl] = 0;
-        if (nkb > 1 && uses[sl ^ 1]) {
-            mbar_wait(&mbar[sl ^ 1], phase[sl ^ 1]);
-            phase[sl ^ 1] ^= 1u;
-            uses[sl ^ 1] = 0;
+    } else if (warp == 1) {
+        // ------------------------------------------------------------ MMA issuer
+        uint32_t g = 0, tc = 0;
+        for (int ti = blockIdx.x; ti < ntiles; ti += gridDim.x) {
+            const Tile tl = a.tiles[ti];
+            const int BN = (tl.n + 15) & ~15;
+            const uint32_t idesc = instr_desc_bf16(BN);
+            const int buf = tc & 1;
+            mbar_wait(&acc_empty[buf], ((tc >> 1) & 1u) ^ 1u);
+            tc_fence_after();
+            const uint32_t dg = tmem + (uint32_t)buf * 256u;
+            for (int kb = 0; kb < nkb; ++kb) {
+                const int s = g % kKS;
+                mbar_wait(&full[s], (g / kKS) & 1u);
+                tc_fence_after();
+                if (lane == 0) {
+                    const uint32_t a0 = smem_addr(smem + SL::a + (size_t)(s * kNM) * kTile);
+                    const uint32_t b0 = smem_addr(smem + SL::b + (size_t)s * kTile);
+#pragma unroll
+                    for (int j = 0; j < kBK / 16; ++j) {
+                        const uint32_t acc = (kb > 0 || j > 0) ? 1u : 0u;
+                        const uint64_t bd = desc_sw128(b0 + 32u * j);
+                        mma_bf16(dg, desc_sw128(a0 + 32u * j), bd, idesc, acc);
+                        if (kGateUp) mma_bf16(dg + 128u, desc_sw128(a0 + kTile + 32u * j), bd, idesc, acc);
+                    }
+                    mma_commit(&empty[s]);
+                }
+                __syncwarp();
+                ++g;
+            }
+            if (lane == 0) mma_commit(&acc_full[buf]);
+            __syncwarp();
+            ++tc;
         }
-        tc_fence_after();
-        // epilogue: warps 0..3 own TMEM lanes 32w..32w+31 = weight rows of the tile
-        if (warp < 4) {
-            const int r = warp * 32 + lane;
-            const int row = tl.row0 + r;
-            const uint32_t lane_addr = tmem + ((uint32_t)(warp * 32) << 16);
-            for (int c0 = 0; c0 < BN; c0 += 16) {
-                float g[16], u[16];
-                tmem_ld16(lane_addr + c0, g);
-                if (kGateUp) tmem_ld16(lane_addr + 256 + c0, u);
+    } else if (warp >= kEpiWarp0 && warp < kEpiWarp0 + 4) {
+        // ------------------------------------------------------------ epilogue
+        const int quarter = warp & 3;                 // TMEM lanes 32*quarter .. +31
+        uint32_t tc = 0;
+        for (int ti = blockIdx.x; ti < ntiles; ti += gridDim.x) {
+            const Tile tl = a.tiles[ti];
+            const int buf = tc & 1;
+            mbar_wait(&acc_full[buf], (tc >> 1) & 1u);
+            tc_fence_after();
+            const int row = tl.row0 + quarter * 32 + lane;
+            const uint32_t taddr = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)buf * 256u;
+            for (int c0 = 0; c0 < tl.n; c0 += 16) {
+                float gv[16], uv[16];
+                tmem_ld16(taddr + c0, gv);
+                if (kGateUp) tmem_ld16(taddr + 128 + c0, uv);
 #pragma unroll
                 for (int j = 0; j < 16; ++j) {
                     const int tok = c0 + j;
                     if (tok < tl.n && row < a.R) {
                         float v;
                         if (kGateUp) {
-                            const float gv = bf16r(g[j]), uv = bf16r(u[j]);
-                            const float sig = bf16r(1.0f / (1.0f + expf(-gv)));
-                            v = bf16r(bf16r(gv * sig) * uv);
+                            const float g1 = bf16r(gv[j]), u1 = bf16r(uv[j]);
+                            const float sig = bf16r(1.0f / (1.0f + expf(-g1)));
+                            v = bf16r(bf16r(g1 * sig) * u1);
                         } else {
-                            v = bf16r(g[j]);
+                            v = bf16r(gv[j]);
                         }
                         a.out[(size_t)(tl.pos0 + tok) * a.R + row] = f32_to_bf16_bits(v);
                     }
                 }
             }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&acc_empty[buf]);
+            ++tc;
         }
-        tc_fence_before();
-        __syncthreads();
-        tc_fence_after();
+    } else if (warp >= kDqWarp0) {
+        // ------------------------------------------------------------ dequantisation
+        const int dt = tid - kDqWarp0 * 32;             // 0..255
+        const int m = kGateUp ? dt >> 7 : 0;            // weight matrix (gate / up)
+        const int r = dt & (kBM - 1);                   // tile row
+        const int w0 = kGateUp ? 0 : 2 * (dt >> 7);     // first code word of the K-block this thread expands
+        constexpr int kWords = kGateUp ? 4 : 2;
+        const uint16_t *sp = m ? a.s1 : a.s0;
+        const uint16_t *bp = m ? a.b1 : a.b0;
+        const int ngk = a.Kdim / 64;
+        uint32_t g = 0, rc = 0;
+        for (int ti = blockIdx.x; ti < ntiles; ti += gridDim.x) {
+            const Tile tl = a.tiles[ti];
+            const bool rok = tl.row0 + r < a.R;
+            const size_t sbase = ((size_t)tl.e * a.R + tl.row0 + (rok ? r : 0)) * ngk;
+            // scale / bias of K-blocks kb, kb + 1, kb + 2 (prefetched ahead of use)
+            uint16_t sq0 = sp[sbase], bq0 = bp[sbase];
+            uint16_t sq1 = nkb > 1 ? sp[sbase + 1] : 0, bq1 = nkb > 1 ? bp[sbase + 1] : 0;
+            uint16_t sq2 = nkb > 2 ? sp[sbase + 2] : 0, bq2 = nkb > 2 ? bp[sbase + 2] : 0;
+            for (int kb = 0; kb < nkb; ++kb) {
+                const int rs = rc % kRS;
+                if (kb % kRawK == 0) mbar_wait(&raw_full[rs], (rc / kRS) & 1u);
+                const int s = g % kKS;
+                mbar_wait(&empty[s], ((g / kKS) & 1u) ^ 1u);
+                const unsigned char *src = smem + SL::raw + (size_t)(rs * kNM + m) * kTile + sw128(r, kb % kRawK);
+                uint32_t wd[kWords];
+                if (kGateUp) {
+                    const uint4 q = *reinterpret_cast<const uint4 *>(src);
+                    wd[0] = q.x;
+                    wd[1] = q.y;
+                    if constexpr (kWords == 4) {
+                        wd[2] = q.z;
+                        wd[3] = q.w;
+                    }
+                } else {
+                    const uint2 q = *reinterpret_cast<const uint2 *>(src + 4 * w0);
+                    wd[0] = q.x;
+                    wd[1] = q.y;
+                }
+                uint32_t tlo, thi;
+                dq_tables<kFp16>(sq0, bq0, tlo, thi);
+                unsigned char *dst = smem + SL::a + (size_t)(s * kNM + m) * kTile;
+#pragma unroll
+                for (int i = 0; i < kWords; ++i) {
+                    uint4 c0, c1;
+                    dq_word(rok ? wd[i] : 0u, tlo, thi, c0, c1);
+                    *reinterpret_cast<uint4 *>(dst + sw128(r, 2 * (w0 + i))) = c0;
+                    *reinterpret_cast<uint4 *>(dst + sw128(r, 2 * (w0 + i) + 1)) = c1;
+                }
+                fence_barrier_init();     // generic-proxy smem writes -> visible to the tensor core
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&full[s]);
+                if (kb % kRawK == kRawK - 1 || kb == nkb - 1) {
+                    if (lane == 0) mbar_arrive(&raw_empty[rs]);
+                    ++rc;
+                }
+                ++g;
+                sq0 = sq1;
+                bq0 = bq1;
+                sq1 = sq2;
+                bq1 = bq2;
+                if (kb + 3 < nkb) {
+                    sq2 = sp[sbase + kb + 3];
+                    bq2 = bp[sbase + kb + 3];
+                }
+            }
+        }
     }
+    tc_fence_before();
     __syncthreads();
-    if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols));
+    tc_fence_after();
+    if (warp == 1) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols));
 }
 
 // y[t][h] = bf16(resid + sum_k bf16(yk * s_k)) with the k sum sequential in bf16 (MLX order)
@@ -395,8 +536,44 @@ PrefillWs carve(void *base, int T, int H, int I, int E, int K) {
     return w;
 }
 
-size_t gemm_smem(bool gateup) {
-    return 2 * ((gateup ? 2 : 1) * kATile + kBTile) + 64;
+// 2-D tensor map over a row-major [rows][cols] array with a box of box_cols x box_rows
+// elements and 128-byte swizzling (box_cols * element size = 128 bytes)
+int make_map(CUtensorMap *m, CUtensorMapDataType dt, size_t esize, const void *base, uint64_t cols, uint64_t rows,
+             uint32_t box_cols, uint32_t box_rows) {
+    const cuuint64_t dims[2] = {cols, rows};
+    const cuuint64_t strides[1] = {cols * esize};
+    const cuuint32_t box[2] = {box_cols, box_rows};
+    const cuuint32_t estr[2] = {1, 1};
+    // the driver entry point is looked up through the runtime, so the library does not link
+    // libcuda directly (it loads on hosts without a driver; calls then fail with an error)
+    using EncodeFn = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                  const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+    static EncodeFn encode = nullptr;
+    if (!encode) {
+        void *fn = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        MOE_CUDA_TRY(cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q));
+        if (q != cudaDriverEntryPointSuccess || !fn)
+            return moe_set_error(MOE_ECUDA, "prefill: cuTensorMapEncodeTiled not available from the driver");
+        encode = reinterpret_cast<EncodeFn>(fn);
+    }
+    const CUresult r = encode(m, dt, 2, const_cast<void *>(base), dims, strides, box, estr,
+                              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return moe_set_error(MOE_ECUDA, "prefill: cuTensorMapEncodeTiled failed (%d)", (int)r);
+    return MOE_OK;
+}
+
+template <bool kGateUp, bool kFp16>
+int launch_gemm(const CUtensorMap &m0, const CUtensorMap &m1, const CUtensorMap &mb, const GemmArgs &g, int grid,
+                cudaStream_t st) {
+    auto kern = gemm_kernel<kGateUp, kFp16>;
+    const size_t smem = GemmSmem<kGateUp>::alloc;
+    MOE_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    kern<<<grid, kGemmThreads, smem, st>>>(m0, m1, mb, g);
+    MOE_CUDA_TRY(cudaGetLastError());
+    return MOE_OK;
 }
 
 }  // namespace
@@ -454,31 +631,34 @@ extern "C" int moe_prefill_experts(const void *x, int T, int H, int I, int E, in
     MOE_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
     MOE_CUDA_TRY(cudaMemsetAsync(w.counts, 0, (size_t)E * 4, st));
     MOE_CUDA_TRY(cudaMemsetAsync(w.pos_of, 0xff, (size_t)TK * 4, st));
+    MOE_CUDA_TRY(cudaMemsetAsync(w.src_of, 0xff, (size_t)TK * 4, st));
     count_kernel<<<(TK + 255) / 256, 256, 0, st>>>(inds, TK, E, w.counts);
     scan_kernel<<<1, 1024, 0, st>>>(w.counts, E, I, H, w.offsets, w.cursor, w.tiles1, w.ntiles, w.tiles2, w.ntiles + 1);
     scatter_kernel<<<(TK + 255) / 256, 256, 0, st>>>(inds, TK, E, w.offsets, w.cursor, w.pos_of, w.src_of);
     MOE_CUDA_TRY(cudaGetLastError());
 
     uint16_t *act = act_out ? static_cast<uint16_t *>(act_out) : w.act;
-    GemmArgs g1{w.tiles1, w.ntiles, H, I, wg, wu, static_cast<const uint16_t *>(sg), static_cast<const uint16_t *>(bg),
-                static_cast<const uint16_t *>(su), static_cast<const uint16_t *>(bu),
-                static_cast<const uint16_t *>(x), w.src_of, K, act};
-    GemmArgs g2{w.tiles2, w.ntiles + 1, I, H, wd, nullptr, static_cast<const uint16_t *>(sd),
-                static_cast<const uint16_t *>(bd), nullptr, nullptr, act, nullptr, K, w.yk};
-    const void *k1 = sb_fp16 ? (const void *)gemm_kernel<true, true> : (const void *)gemm_kernel<true, false>;
-    const void *k2 = sb_fp16 ? (const void *)gemm_kernel<false, true> : (const void *)gemm_kernel<false, false>;
-    static int configured = 0;
-    if (!configured) {
-        MOE_CUDA_TRY(cudaFuncSetAttribute(gemm_kernel<true, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gemm_smem(true)));
-        MOE_CUDA_TRY(cudaFuncSetAttribute(gemm_kernel<true, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gemm_smem(true)));
-        MOE_CUDA_TRY(cudaFuncSetAttribute(gemm_kernel<false, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gemm_smem(false)));
-        MOE_CUDA_TRY(cudaFuncSetAttribute(gemm_kernel<false, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gemm_smem(false)));
-        configured = 1;
-    }
-    void *a1[] = {&g1};
-    void *a2[] = {&g2};
-    MOE_CUDA_TRY(cudaLaunchKernel(k1, dim3(sms), dim3(kThreads), a1, gemm_smem(true), st));
-    MOE_CUDA_TRY(cudaLaunchKernel(k2, dim3(sms), dim3(kThreads), a2, gemm_smem(false), st));
+    // tensor maps: codes [E*R rows][Kdim/16 words] (box 32 words x 128 rows = 8 K-blocks), the
+    // expert-ordered x rows [T*K][H] and act [T*K][I] (16-row boxes)
+    CUtensorMap mg, mu, mx, md, ma;
+    int rc = make_map(&mg, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, wg, (uint64_t)H / 16, (uint64_t)E * I, 32, kBM);
+    if (!rc) rc = make_map(&mu, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, wu, (uint64_t)H / 16, (uint64_t)E * I, 32, kBM);
+    // the gate/up B rows in expert order live in the yk buffer until the down GEMM overwrites it
+    uint16_t *xs = w.yk;
+    if (!rc) rc = make_map(&mx, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, xs, (uint64_t)H, (uint64_t)TK, 64, 16);
+    if (!rc) rc = make_map(&md, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, wd, (uint64_t)I / 16, (uint64_t)E * H, 32, kBM);
+    if (!rc) rc = make_map(&ma, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, act, (uint64_t)I, (uint64_t)TK, 64, 16);
+    if (rc) return rc;
+    if (reinterpret_cast<uintptr_t>(act) % 16) return moe_set_error(MOE_EINVAL, "prefill_experts: act_out not aligned");
+    GemmArgs g1{w.tiles1, w.ntiles, H, I, K, static_cast<const uint16_t *>(sg), static_cast<const uint16_t *>(bg),
+                static_cast<const uint16_t *>(su), static_cast<const uint16_t *>(bu), act};
+    GemmArgs g2{w.tiles2, w.ntiles + 1, I, H, K, static_cast<const uint16_t *>(sd), static_cast<const uint16_t *>(bd),
+                nullptr, nullptr, w.yk};
+    gather_rows_kernel<<<sms * 4, 256, 0, st>>>(static_cast<const uint16_t *>(x), w.src_of, TK, K, H, xs);
+    MOE_CUDA_TRY(cudaGetLastError());
+    rc = sb_fp16 ? launch_gemm<true, true>(mg, mu, mx, g1, sms, st) : launch_gemm<true, false>(mg, mu, mx, g1, sms, st);
+    if (!rc) rc = sb_fp16 ? launch_gemm<false, true>(md, md, ma, g2, sms, st) : launch_gemm<false, false>(md, md, ma, g2, sms, st);
+    if (rc) return rc;
     combine_kernel<<<sms * 4, 256, 0, st>>>(w.yk, w.pos_of, static_cast<const uint16_t *>(scores),
                                              static_cast<const uint16_t *>(resid), T, K, H, static_cast<uint16_t *>(y));
     MOE_CUDA_TRY(cudaGetLastError());
