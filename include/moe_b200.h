@@ -211,11 +211,13 @@ size_t moe_prefill_workspace_bytes(int T, int H, int I, int E, int K);
  * gather_qmm per expert group as prefill_qproj.py:18-40): x bf16 [T][H], inds u32 [T][K] and
  * scores bf16 [T][K] from the router (moe_router_topk), experts in the MLX layout with
  * cap = E. Assignments are grouped by expert on the device; gate/up and down run as GEMMs
- * with M = 128 weight rows and N = the expert's tokens on the tensor cores (weights
- * dequantised to bf16 in shared memory, fp32 accumulation in TMEM); y bf16 [T][H] =
- * resid + sum_k bf16(expert_k(x) * score_k) (sequential bf16 in MLX order). resid may be
- * NULL; act_out (bf16 [T*K][I], positions in expert order) may be NULL. H, I multiples of
- * 64; x and code arrays 16-byte aligned.
+ * with M = 128 weight rows and N = the expert's tokens on the tensor cores (weight codes
+ * and activations staged by TMA, weights dequantised to bf16 into tensor memory, fp32
+ * accumulation in TMEM); y bf16 [T][H] = resid + sum_k bf16(expert_k(x) * score_k)
+ * (sequential bf16 in MLX order). resid may be NULL. act_out (bf16 [T*K][I], positions in
+ * expert order) may be NULL; its columns are in the GEMMs' K order: inside every 16-column
+ * group, column c holds activation [0,4,8,12,1,5,9,13,2,6,10,14,3,7,11,15][c]. H, I
+ * multiples of 64; x and code arrays 16-byte aligned.
  */
 int moe_prefill_experts(const void *x, int T, int H, int I, int E, int K, const uint32_t *inds,
                         const void *scores, const uint32_t *wg, const void *sg, const void *bg,

@@ -7,10 +7,11 @@
 // weights by the routing scores. Here:
 //
 //   bucket   assignments grouped by expert (counts, exclusive scan, scatter) and a tile list
-//            (expert, 128-row block of the weight matrix, block of <= 128 of its tokens)
-//   gateup   per tile D_g = Wg[rows] . X^T and D_u = Wu[rows] . X^T, M = 128 weight rows,
+//            (expert, row block of the weight matrix, block of <= 128 of its tokens)
+//   gateup   per tile D_g = Wg[rows] . X^T and D_u = Wu[rows] . X^T, M = 128 weight rows each,
 //            N = the expert's tokens (padded to 16), K = H in blocks of 64 (one 2-bit group)
-//   down     the same GEMM with Wd and the act rows (contiguous per expert) -> yk[pos][H]
+//   down     the same GEMM with Wd (two 128-row blocks per tile) and the act rows
+//            (contiguous per expert) -> yk[pos][H]
 //   combine  y[t] = resid[t] + sum_k bf16(yk[pos(t,k)] * s[t,k]), sequential bf16 in MLX order
 //
 // The GEMM kernel is persistent (one CTA per SM) and warp-specialised:
@@ -62,6 +63,14 @@ MOE_D void mma_bf16(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc, uin
         "l"(a), "l"(b), "r"(idesc), "r"(acc));
 }
 
+// A from tensor memory (lane = row, two bf16 of K per 32-bit column), B from shared memory
+MOE_D void mma_bf16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b, uint32_t idesc, uint32_t acc) {
+    asm volatile(
+        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+        " tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n}\n" ::"r"(d_tmem),
+        "r"(a_tmem), "l"(b), "r"(idesc), "r"(acc));
+}
+
 MOE_D void mma_commit(uint64_t *bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_addr(bar))
                  : "memory");
@@ -78,6 +87,29 @@ MOE_D void tmem_ld16(uint32_t taddr, float (&v)[16]) {
 #pragma unroll
     for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
+
+// this warp's 32 TMEM lanes, 16 / 32 consecutive 32-bit columns from taddr
+MOE_D void tmem_st16(uint32_t taddr, const uint32_t (&v)[16]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(
+            taddr),
+        "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]),
+        "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
+        : "memory");
+}
+
+MOE_D void tmem_st32(uint32_t taddr, const uint32_t (&v)[32]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+        "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+        "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]),
+        "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15]), "r"(v[16]), "r"(v[17]), "r"(v[18]),
+        "r"(v[19]), "r"(v[20]), "r"(v[21]), "r"(v[22]), "r"(v[23]), "r"(v[24]), "r"(v[25]), "r"(v[26]), "r"(v[27]),
+        "r"(v[28]), "r"(v[29]), "r"(v[30]), "r"(v[31])
+        : "memory");
+}
+
+MOE_D void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
 MOE_D void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 MOE_D void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
@@ -115,20 +147,21 @@ MOE_D void dq_tables(uint16_t sraw, uint16_t braw, uint32_t &tlo, uint32_t &thi)
     thi = prmt(p01, p23, 0x7531u);
 }
 
-// 16 codes (code j in bits 2j..2j+1) -> 16 bf16 (two 16-byte chunks, element j at j).
-// Output word m (elements 2m, 2m+1) = prmt(tlo, thi, [q_2m, q_2m + 4, q_2m+1, q_2m+1 + 4]).
-MOE_D void dq_word(uint32_t w, uint32_t tlo, uint32_t thi, uint4 &c0, uint4 &c1) {
-    const uint32_t Y = w & 0x33333333u;             // nibble j: code 2j
-    const uint32_t Z = (w >> 2) & 0x33333333u;      // nibble j: code 2j + 1
-    // byte b: [q, q + 4] nibble pairs of codes 4b (YYe), 4b + 2 (YYo), 4b + 1 (ZZe), 4b + 3 (ZZo)
-    const uint32_t YYe = (Y & 0x0F0F0F0Fu) * 0x11u + 0x40404040u;
-    const uint32_t YYo = ((Y >> 4) & 0x0F0F0F0Fu) * 0x11u + 0x40404040u;
-    const uint32_t ZZe = (Z & 0x0F0F0F0Fu) * 0x11u + 0x40404040u;
-    const uint32_t ZZo = ((Z >> 4) & 0x0F0F0F0Fu) * 0x11u + 0x40404040u;
-    const uint32_t s02 = prmt(YYe, ZZe, 0x5140u), s46 = prmt(YYe, ZZe, 0x7362u);
-    const uint32_t s13 = prmt(YYo, ZZo, 0x5140u), s57 = prmt(YYo, ZZo, 0x7362u);
-    c0 = make_uint4(prmt(tlo, thi, s02), prmt(tlo, thi, s13), prmt(tlo, thi, s02 >> 16), prmt(tlo, thi, s13 >> 16));
-    c1 = make_uint4(prmt(tlo, thi, s46), prmt(tlo, thi, s57), prmt(tlo, thi, s46 >> 16), prmt(tlo, thi, s57 >> 16));
+// K order inside every 16-element group of the GEMMs: position 2c + j of the group holds
+// element t + 8h + 4j for c = 2t + h (t < 4, h, j < 2), i.e. [0,4,8,12,1,5,9,13,2,6,10,14,3,7,
+// 11,15]. A and B use the same order, so the products are unchanged; it lets one byte permute
+// expand a pair of codes whose selector comes from one mask and one multiply-add.
+MOE_HD int kperm_pos(int e) { return 4 * (e & 3) + 2 * ((e >> 3) & 1) + ((e >> 2) & 1); }
+
+// 16 codes (code e in bits 2e..2e+1) -> 8 bf16x2 words in the permuted K order: word 2t + h
+// = (v[code t + 8h], v[code t + 8h + 4]). Selector of the pair: nibbles [q, q + 4, q', q' + 4].
+MOE_D void dq_word(uint32_t w, uint32_t tlo, uint32_t thi, uint32_t *o) {
+#pragma unroll
+    for (int t = 0; t < 4; ++t) {
+        const uint32_t S = ((w >> (2 * t)) & 0x03030303u) * 0x11u + 0x40404040u;
+        o[2 * t] = prmt(tlo, thi, S);
+        o[2 * t + 1] = prmt(tlo, thi, S >> 16);
+    }
 }
 
 // ------------------------------------------------------------------ bucketing
@@ -179,7 +212,7 @@ __global__ void __launch_bounds__(1024) scan_kernel(const int *counts, int E, in
                                                     int *ntiles2) {
     __shared__ int ws[32];
     int off0 = 0, t10 = 0, t20 = 0;
-    const int rb1 = (R1 + kBM - 1) / kBM, rb2 = (R2 + kBM - 1) / kBM;
+    const int rb1 = (R1 + kBM - 1) / kBM, rb2 = (R2 + 2 * kBM - 1) / (2 * kBM);
     for (int e0 = 0; e0 < E; e0 += blockDim.x) {
         const int e = e0 + threadIdx.x;
         const int c = (e < E) ? counts[e] : 0;
@@ -195,7 +228,7 @@ __global__ void __launch_bounds__(1024) scan_kernel(const int *counts, int E, in
             for (int p = 0; p < c; p += kMaxBN) {
                 const int n = min(kMaxBN, c - p);
                 for (int r = 0; r < rb1; ++r) tiles1[i1++] = Tile{e, r * kBM, o + p, n};
-                for (int r = 0; r < rb2; ++r) tiles2[i2++] = Tile{e, r * kBM, o + p, n};
+                for (int r = 0; r < rb2; ++r) tiles2[i2++] = Tile{e, r * 2 * kBM, o + p, n};
             }
         }
         off0 += tot_c;
@@ -221,17 +254,23 @@ __global__ void scatter_kernel(const uint32_t *inds, int TK, int E, const int *o
     }
 }
 
-// xs[p] = x[src_of[p] / K]: the B rows of the gate/up GEMM in expert order (16-byte copies)
+// xs[p] = x[src_of[p] / K] in the permuted K order: the B rows of the gate/up GEMM in expert
+// order, one 16-element group (two 16-byte chunks) per work item
 __global__ void gather_rows_kernel(const uint16_t *x, const int *src_of, int TK, int K, int H, uint16_t *xs) {
-    const int cpr = H / 8;
-    const size_t n = (size_t)TK * cpr;
+    const int gpr = H / 16;
+    const size_t n = (size_t)TK * gpr;
     for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
-        const size_t p = i / cpr;
-        const int c = (int)(i % cpr);
+        const size_t p = i / gpr;
+        const int gi = (int)(i % gpr);
         const int src = src_of[p];
         if (src < 0) continue;
-        *reinterpret_cast<uint4 *>(xs + p * H + (size_t)c * 8) =
-            *reinterpret_cast<const uint4 *>(x + (size_t)(src / K) * H + (size_t)c * 8);
+        const uint4 *in = reinterpret_cast<const uint4 *>(x + (size_t)(src / K) * H + (size_t)gi * 16);
+        const uint4 lo = in[0], hi = in[1];
+        uint4 *out = reinterpret_cast<uint4 *>(xs + p * H + (size_t)gi * 16);
+        out[0] = make_uint4(prmt(lo.x, lo.z, 0x5410u), prmt(hi.x, hi.z, 0x5410u), prmt(lo.x, lo.z, 0x7632u),
+                            prmt(hi.x, hi.z, 0x7632u));
+        out[1] = make_uint4(prmt(lo.y, lo.w, 0x5410u), prmt(hi.y, hi.w, 0x5410u), prmt(lo.y, lo.w, 0x7632u),
+                            prmt(hi.y, hi.w, 0x7632u));
     }
 }
 
@@ -239,11 +278,17 @@ __global__ void gather_rows_kernel(const uint16_t *x, const int *src_of, int TK,
 
 constexpr int kRawK = 8;                         // K-blocks per raw code stage (128 B of codes per row)
 constexpr int kRS = 2;                           // raw code stages
+constexpr int kKS = 4;                           // A stages (dequantised weights in TMEM)
+constexpr int kBS = 8;                           // B stages (activation rows in shared memory, TMA)
 constexpr int kGemmThreads = 448;                // 14 warps
 constexpr int kDqWarp0 = 6, kDqWarps = 8;
 constexpr int kEpiWarp0 = 2;
 constexpr int kTile = kBM * 128;                 // one 128-row x 128-byte tile: 16 KB
-constexpr uint32_t kTmemCols = 512;              // two accumulator buffers of 256 columns
+constexpr uint32_t kTmemCols = 512;
+// TMEM columns: accumulators [0, 128) (gate, or down rows 0..127 of the tile) and [128, 256)
+// (up, or down rows 128..255); the dequantised A operand of K-block stage s at 256 + 64 s
+// (matrix 0: +0, matrix 1: +32; 32 columns = 64 bf16 of K)
+constexpr uint32_t kTmemA = 256, kTmemAStage = 64;
 
 struct GemmArgs {
     const Tile *tiles;
@@ -255,14 +300,13 @@ struct GemmArgs {
 
 template <bool kGateUp>
 struct GemmSmem {
-    static constexpr int kNM = kGateUp ? 2 : 1;       // weight matrices per tile
-    static constexpr int kKS = kGateUp ? 3 : 4;       // K-block stages
+    static constexpr int kNM = 2;   // weight matrices per tile: gate + up, or two 128-row blocks of down
     static constexpr size_t raw = 0;                                       // [kRS][kNM] tiles
-    static constexpr size_t a = raw + (size_t)kRS * kNM * kTile;           // [kKS][kNM] tiles
-    static constexpr size_t b = a + (size_t)kKS * kNM * kTile;             // [kKS] tiles
-    static constexpr size_t bars = b + (size_t)kKS * kTile;
-    // raw_full, raw_empty [kRS]; full, empty [kKS]; acc_full, acc_empty [2]; tmem slot
-    static constexpr size_t total = bars + (2 * kRS + 2 * kKS + 4) * 8 + 16;
+    static constexpr size_t b = raw + (size_t)kRS * kNM * kTile;           // [kBS] tiles
+    static constexpr size_t bars = b + (size_t)kBS * kTile;
+    // raw_full, raw_empty [kRS]; full, empty [kKS]; b_full, b_empty [kBS]; acc_full, acc_empty;
+    // tmem slot
+    static constexpr size_t total = bars + (2 * kRS + 2 * kKS + 2 * kBS + 2) * 8 + 16;
     static constexpr size_t alloc = total + 1024;      // + alignment slack
 };
 
@@ -271,7 +315,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap map_w0, const __grid_constant__ CUtensorMap map_w1,
                 const __grid_constant__ CUtensorMap map_b, GemmArgs a) {
     using SL = GemmSmem<kGateUp>;
-    constexpr int kNM = SL::kNM, kKS = SL::kKS;
+    constexpr int kNM = SL::kNM;
     extern __shared__ unsigned char smem_raw[];
     unsigned char *smem = reinterpret_cast<unsigned char *>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -279,9 +323,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     uint64_t *raw_empty = raw_full + kRS;
     uint64_t *full = raw_empty + kRS;
     uint64_t *empty = full + kKS;
-    uint64_t *acc_full = empty + kKS;
-    uint64_t *acc_empty = acc_full + 2;
-    uint32_t *tslot = reinterpret_cast<uint32_t *>(acc_empty + 2);
+    uint64_t *b_full = empty + kKS;
+    uint64_t *b_empty = b_full + kBS;
+    uint64_t *acc_full = b_empty + kBS;
+    uint64_t *acc_empty = acc_full + 1;
+    uint32_t *tslot = reinterpret_cast<uint32_t *>(acc_empty + 1);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
 
     if (tid == 0) {
@@ -290,13 +336,15 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             mbar_init(&raw_empty[i], kDqWarps);
         }
         for (int i = 0; i < kKS; ++i) {
-            mbar_init(&full[i], kDqWarps + 1);
+            mbar_init(&full[i], kDqWarps);
             mbar_init(&empty[i], 1);
         }
-        for (int i = 0; i < 2; ++i) {
-            mbar_init(&acc_full[i], 1);
-            mbar_init(&acc_empty[i], 4);
+        for (int i = 0; i < kBS; ++i) {
+            mbar_init(&b_full[i], 1);
+            mbar_init(&b_empty[i], 1);
         }
+        mbar_init(acc_full, 1);
+        mbar_init(acc_empty, 4);
         fence_barrier_init();
     }
     if (warp == 1) {
@@ -325,20 +373,19 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                     if (lane == 0) {
                         mbar_arrive_expect_tx(&raw_full[rs], kNM * kTile);
                         tma_load_2d(smem + SL::raw + (size_t)(rs * kNM) * kTile, &map_w0, kb * 4, wrow, &raw_full[rs]);
-                        if (kGateUp)
-                            tma_load_2d(smem + SL::raw + (size_t)(rs * kNM + 1) * kTile, &map_w1, kb * 4, wrow,
-                                        &raw_full[rs]);
+                        tma_load_2d(smem + SL::raw + (size_t)(rs * kNM + 1) * kTile, kGateUp ? &map_w1 : &map_w0,
+                                    kb * 4, kGateUp ? wrow : wrow + kBM, &raw_full[rs]);
                     }
                     ++rc;
                 }
-                const int s = g % kKS;
-                mbar_wait(&empty[s], ((g / kKS) & 1u) ^ 1u);
+                const int s = g % kBS;
+                mbar_wait(&b_empty[s], ((g / kBS) & 1u) ^ 1u);
                 unsigned char *bst = smem + SL::b + (size_t)s * kTile;
-                if (lane == 0) mbar_arrive_expect_tx(&full[s], (uint32_t)nbox * 2048u);
+                if (lane == 0) mbar_arrive_expect_tx(&b_full[s], (uint32_t)nbox * 2048u);
                 __syncwarp();
                 // the tile's B rows: 16-row boxes of the expert-ordered rows (x gathered per
                 // position for gate/up, act for down)
-                if (lane < nbox) tma_load_2d(bst + (size_t)lane * 2048, &map_b, kb * 64, tl.pos0 + 16 * lane, &full[s]);
+                if (lane < nbox) tma_load_2d(bst + (size_t)lane * 2048, &map_b, kb * 64, tl.pos0 + 16 * lane, &b_full[s]);
                 ++g;
             }
         }
@@ -349,30 +396,30 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             const Tile tl = a.tiles[ti];
             const int BN = (tl.n + 15) & ~15;
             const uint32_t idesc = instr_desc_bf16(BN);
-            const int buf = tc & 1;
-            mbar_wait(&acc_empty[buf], ((tc >> 1) & 1u) ^ 1u);
+            mbar_wait(acc_empty, (tc & 1u) ^ 1u);
             tc_fence_after();
-            const uint32_t dg = tmem + (uint32_t)buf * 256u;
             for (int kb = 0; kb < nkb; ++kb) {
-                const int s = g % kKS;
+                const int s = g % kKS, sb = g % kBS;
+                mbar_wait(&b_full[sb], (g / kBS) & 1u);
                 mbar_wait(&full[s], (g / kKS) & 1u);
                 tc_fence_after();
                 if (lane == 0) {
-                    const uint32_t a0 = smem_addr(smem + SL::a + (size_t)(s * kNM) * kTile);
-                    const uint32_t b0 = smem_addr(smem + SL::b + (size_t)s * kTile);
+                    const uint32_t at = tmem + kTmemA + (uint32_t)s * kTmemAStage;
+                    const uint32_t b0 = smem_addr(smem + SL::b + (size_t)sb * kTile);
+                    // one accumulator at a time: consecutive MMAs into the same TMEM columns
 #pragma unroll
-                    for (int j = 0; j < kBK / 16; ++j) {
-                        const uint32_t acc = (kb > 0 || j > 0) ? 1u : 0u;
-                        const uint64_t bd = desc_sw128(b0 + 32u * j);
-                        mma_bf16(dg, desc_sw128(a0 + 32u * j), bd, idesc, acc);
-                        if (kGateUp) mma_bf16(dg + 128u, desc_sw128(a0 + kTile + 32u * j), bd, idesc, acc);
-                    }
+                    for (int mm = 0; mm < 2; ++mm)
+#pragma unroll
+                        for (int j = 0; j < kBK / 16; ++j)
+                            mma_bf16_ts(tmem + 128u * mm, at + 32u * mm + 8u * j, desc_sw128(b0 + 32u * j), idesc,
+                                        (kb > 0 || j > 0) ? 1u : 0u);
                     mma_commit(&empty[s]);
+                    mma_commit(&b_empty[sb]);
                 }
                 __syncwarp();
                 ++g;
             }
-            if (lane == 0) mma_commit(&acc_full[buf]);
+            if (lane == 0) mma_commit(acc_full);
             __syncwarp();
             ++tc;
         }
@@ -382,101 +429,105 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         uint32_t tc = 0;
         for (int ti = blockIdx.x; ti < ntiles; ti += gridDim.x) {
             const Tile tl = a.tiles[ti];
-            const int buf = tc & 1;
-            mbar_wait(&acc_full[buf], (tc >> 1) & 1u);
+            mbar_wait(acc_full, tc & 1u);
             tc_fence_after();
             const int row = tl.row0 + quarter * 32 + lane;
-            const uint32_t taddr = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)buf * 256u;
+            const uint32_t taddr = tmem + ((uint32_t)(quarter * 32) << 16);
+            // gate/up: act column of I-row `row` in the permuted K order of the down GEMM
+            const int acol = (row & ~15) + kperm_pos(row & 15);
             for (int c0 = 0; c0 < tl.n; c0 += 16) {
                 float gv[16], uv[16];
                 tmem_ld16(taddr + c0, gv);
-                if (kGateUp) tmem_ld16(taddr + 128 + c0, uv);
+                tmem_ld16(taddr + 128 + c0, uv);
 #pragma unroll
                 for (int j = 0; j < 16; ++j) {
                     const int tok = c0 + j;
-                    if (tok < tl.n && row < a.R) {
-                        float v;
-                        if (kGateUp) {
+                    if (tok >= tl.n) continue;
+                    uint16_t *orow = a.out + (size_t)(tl.pos0 + tok) * a.R;
+                    if (kGateUp) {
+                        if (row < a.R) {
                             const float g1 = bf16r(gv[j]), u1 = bf16r(uv[j]);
                             const float sig = bf16r(1.0f / (1.0f + expf(-g1)));
-                            v = bf16r(bf16r(g1 * sig) * u1);
-                        } else {
-                            v = bf16r(gv[j]);
+                            orow[acol] = f32_to_bf16_bits(bf16r(bf16r(g1 * sig) * u1));
                         }
-                        a.out[(size_t)(tl.pos0 + tok) * a.R + row] = f32_to_bf16_bits(v);
+                    } else {
+                        if (row < a.R) orow[row] = f32_to_bf16_bits(gv[j]);
+                        if (row + kBM < a.R) orow[row + kBM] = f32_to_bf16_bits(uv[j]);
                     }
                 }
             }
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(&acc_empty[buf]);
+            if (lane == 0) mbar_arrive(acc_empty);
             ++tc;
         }
     } else if (warp >= kDqWarp0) {
         // ------------------------------------------------------------ dequantisation
-        const int dt = tid - kDqWarp0 * 32;             // 0..255
-        const int m = kGateUp ? dt >> 7 : 0;            // weight matrix (gate / up)
-        const int r = dt & (kBM - 1);                   // tile row
-        const int w0 = kGateUp ? 0 : 2 * (dt >> 7);     // first code word of the K-block this thread expands
-        constexpr int kWords = kGateUp ? 4 : 2;
-        const uint16_t *sp = m ? a.s1 : a.s0;
-        const uint16_t *bp = m ? a.b1 : a.b0;
+        // warp -> TMEM lane quarter (rows 32q .. 32q+31 of a matrix); the two groups of four
+        // warps take the tile's two matrices (gate / up, or the two 128-row blocks of down)
+        const int quarter = warp & 3;
+        const int m = (warp - kDqWarp0) >> 2;
+        const int r = quarter * 32 + lane;              // row within the matrix = TMEM lane
+        const int roff = kGateUp ? r : r + kBM * m;     // row within the tile's weight rows
+        const uint16_t *sp = (kGateUp && m) ? a.s1 : a.s0;
+        const uint16_t *bp = (kGateUp && m) ? a.b1 : a.b0;
         const int ngk = a.Kdim / 64;
+        const int nst = (nkb + kRawK - 1) / kRawK;
+        const uint32_t tcol = tmem + ((uint32_t)(quarter * 32) << 16) + kTmemA + 32u * m;
+        // scale / bias of the 8 K-blocks of a raw stage, loaded one stage ahead
+        uint16_t cs[kRawK], cb[kRawK], ns[kRawK], nb[kRawK];
+        auto load_sb = [&](const Tile &t, int st) {
+            const bool rok = t.row0 + roff < a.R;
+            const size_t base = ((size_t)t.e * a.R + (rok ? t.row0 + roff : 0)) * ngk + (size_t)st * kRawK;
+#pragma unroll
+            for (int i = 0; i < kRawK; ++i) {
+                const bool ok = st * kRawK + i < nkb;
+                ns[i] = ok ? sp[base + i] : (uint16_t)0;
+                nb[i] = ok ? bp[base + i] : (uint16_t)0;
+            }
+        };
         uint32_t g = 0, rc = 0;
+        if ((int)blockIdx.x < ntiles) load_sb(a.tiles[blockIdx.x], 0);
         for (int ti = blockIdx.x; ti < ntiles; ti += gridDim.x) {
             const Tile tl = a.tiles[ti];
-            const bool rok = tl.row0 + r < a.R;
-            const size_t sbase = ((size_t)tl.e * a.R + tl.row0 + (rok ? r : 0)) * ngk;
-            // scale / bias of K-blocks kb, kb + 1, kb + 2 (prefetched ahead of use)
-            uint16_t sq0 = sp[sbase], bq0 = bp[sbase];
-            uint16_t sq1 = nkb > 1 ? sp[sbase + 1] : 0, bq1 = nkb > 1 ? bp[sbase + 1] : 0;
-            uint16_t sq2 = nkb > 2 ? sp[sbase + 2] : 0, bq2 = nkb > 2 ? bp[sbase + 2] : 0;
-            for (int kb = 0; kb < nkb; ++kb) {
-                const int rs = rc % kRS;
-                if (kb % kRawK == 0) mbar_wait(&raw_full[rs], (rc / kRS) & 1u);
-                const int s = g % kKS;
-                mbar_wait(&empty[s], ((g / kKS) & 1u) ^ 1u);
-                const unsigned char *src = smem + SL::raw + (size_t)(rs * kNM + m) * kTile + sw128(r, kb % kRawK);
-                uint32_t wd[kWords];
-                if (kGateUp) {
-                    const uint4 q = *reinterpret_cast<const uint4 *>(src);
-                    wd[0] = q.x;
-                    wd[1] = q.y;
-                    if constexpr (kWords == 4) {
-                        wd[2] = q.z;
-                        wd[3] = q.w;
-                    }
-                } else {
-                    const uint2 q = *reinterpret_cast<const uint2 *>(src + 4 * w0);
-                    wd[0] = q.x;
-                    wd[1] = q.y;
-                }
-                uint32_t tlo, thi;
-                dq_tables<kFp16>(sq0, bq0, tlo, thi);
-                unsigned char *dst = smem + SL::a + (size_t)(s * kNM + m) * kTile;
+            const bool rok = tl.row0 + roff < a.R;
+            for (int st = 0; st < nst; ++st) {
 #pragma unroll
-                for (int i = 0; i < kWords; ++i) {
-                    uint4 c0, c1;
-                    dq_word(rok ? wd[i] : 0u, tlo, thi, c0, c1);
-                    *reinterpret_cast<uint4 *>(dst + sw128(r, 2 * (w0 + i))) = c0;
-                    *reinterpret_cast<uint4 *>(dst + sw128(r, 2 * (w0 + i) + 1)) = c1;
+                for (int i = 0; i < kRawK; ++i) {
+                    cs[i] = ns[i];
+                    cb[i] = nb[i];
                 }
-                fence_barrier_init();     // generic-proxy smem writes -> visible to the tensor core
+                if (st + 1 < nst) load_sb(tl, st + 1);
+                else if (ti + (int)gridDim.x < ntiles) load_sb(a.tiles[ti + gridDim.x], 0);
+                const int rs = rc % kRS;
+                mbar_wait(&raw_full[rs], (rc / kRS) & 1u);
+                const unsigned char *rbase = smem + SL::raw + (size_t)(rs * kNM + m) * kTile;
+#pragma unroll
+                for (int i = 0; i < kRawK; ++i) {
+                    if (st * kRawK + i < nkb) {
+                        const int s = g % kKS;
+                        mbar_wait(&empty[s], ((g / kKS) & 1u) ^ 1u);
+                        tc_fence_after();
+                        uint4 q = *reinterpret_cast<const uint4 *>(rbase + sw128(r, i));
+                        if (!rok) q = make_uint4(0u, 0u, 0u, 0u);
+                        uint32_t tlo, thi;
+                        dq_tables<kFp16>(cs[i], cb[i], tlo, thi);
+                        uint32_t out[32];
+                        dq_word(q.x, tlo, thi, out);
+                        dq_word(q.y, tlo, thi, out + 8);
+                        dq_word(q.z, tlo, thi, out + 16);
+                        dq_word(q.w, tlo, thi, out + 24);
+                        tmem_st32(tcol + (uint32_t)s * kTmemAStage, out);
+                        tmem_st_wait();
+                        tc_fence_before();
+                        __syncwarp();
+                        if (lane == 0) mbar_arrive(&full[s]);
+                        ++g;
+                    }
+                }
                 __syncwarp();
-                if (lane == 0) mbar_arrive(&full[s]);
-                if (kb % kRawK == kRawK - 1 || kb == nkb - 1) {
-                    if (lane == 0) mbar_arrive(&raw_empty[rs]);
-                    ++rc;
-                }
-                ++g;
-                sq0 = sq1;
-                bq0 = bq1;
-                sq1 = sq2;
-                bq1 = bq2;
-                if (kb + 3 < nkb) {
-                    sq2 = sp[sbase + kb + 3];
-                    bq2 = bp[sbase + kb + 3];
-                }
+                if (lane == 0) mbar_arrive(&raw_empty[rs]);
+                ++rc;
             }
         }
     }
@@ -486,25 +537,45 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     if (warp == 1) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols));
 }
 
-// y[t][h] = bf16(resid + sum_k bf16(yk * s_k)) with the k sum sequential in bf16 (MLX order)
+// y[t][h] = bf16(resid + sum_k bf16(yk * s_k)) with the k sum sequential in bf16 (MLX order),
+// 8 columns (16 bytes) of one token per work item
 __global__ void combine_kernel(const uint16_t *yk, const int *pos_of, const uint16_t *scores, const uint16_t *resid,
                                int T, int K, int H, uint16_t *y) {
-    const size_t n = (size_t)T * H;
+    const int cpr = H / 8;
+    const size_t n = (size_t)T * cpr;
     const int TK = T * K;
     for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
-        const int t = (int)(i / H), h = (int)(i % H);
-        float acc = 0.f;
+        const int t = (int)(i / cpr), c = (int)(i % cpr);
+        float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
         for (int k = 0; k < K; ++k) {
             const int p = pos_of[t * K + k];
             if (p < 0 || p >= TK) {            // an expert id >= E was never scattered
                 atomicOr(&g_moe_device_error, MOE_DEVERR_BAD_INPUT);
                 continue;
             }
-            const float pk = bf16r(bf16_bits_to_f32(yk[(size_t)p * H + h]) * bf16_bits_to_f32(scores[t * K + k]));
-            acc = (k == 0) ? pk : bf16r(acc + pk);
+            const float sc = bf16_bits_to_f32(scores[t * K + k]);
+            const uint4 v = *reinterpret_cast<const uint4 *>(yk + (size_t)p * H + (size_t)c * 8);
+            const uint32_t vw[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const float pk = bf16r(bf16_bits_to_f32((uint16_t)(vw[j >> 1] >> (16 * (j & 1)))) * sc);
+                acc[j] = (k == 0) ? pk : bf16r(acc[j] + pk);
+            }
         }
-        if (resid) acc = bf16r(bf16_bits_to_f32(resid[i]) + acc);
-        y[i] = f32_to_bf16_bits(acc);
+        uint32_t ow[4];
+        const uint4 rv = resid ? *reinterpret_cast<const uint4 *>(resid + (size_t)t * H + (size_t)c * 8)
+                               : make_uint4(0u, 0u, 0u, 0u);
+        const uint32_t rw[4] = {rv.x, rv.y, rv.z, rv.w};
+#pragma unroll
+        for (int j = 0; j < 8; j += 2) {
+            float a0 = acc[j], a1 = acc[j + 1];
+            if (resid) {
+                a0 = bf16r(bf16_bits_to_f32((uint16_t)rw[j >> 1]) + a0);
+                a1 = bf16r(bf16_bits_to_f32((uint16_t)(rw[j >> 1] >> 16)) + a1);
+            }
+            ow[j >> 1] = (uint32_t)f32_to_bf16_bits(a0) | ((uint32_t)f32_to_bf16_bits(a1) << 16);
+        }
+        *reinterpret_cast<uint4 *>(y + (size_t)t * H + (size_t)c * 8) = make_uint4(ow[0], ow[1], ow[2], ow[3]);
     }
 }
 
@@ -529,7 +600,7 @@ PrefillWs carve(void *base, int T, int H, int I, int E, int K) {
     w.src_of = reinterpret_cast<int *>(take(TK * 4));
     w.ntiles = reinterpret_cast<int *>(take(2 * 4));
     w.tiles1 = reinterpret_cast<Tile *>(take(maxt * ((I + kBM - 1) / kBM) * sizeof(Tile)));
-    w.tiles2 = reinterpret_cast<Tile *>(take(maxt * ((H + kBM - 1) / kBM) * sizeof(Tile)));
+    w.tiles2 = reinterpret_cast<Tile *>(take(maxt * ((H + 2 * kBM - 1) / (2 * kBM)) * sizeof(Tile)));
     w.act = reinterpret_cast<uint16_t *>(take(TK * I * 2));
     w.yk = reinterpret_cast<uint16_t *>(take(TK * H * 2));
     w.bytes = off;

@@ -8,6 +8,9 @@
 //   logit; the last CTA to finish a token (atomic ticket in the workspace) runs the
 //   softmax / selection tail for that token and re-arms the ticket.
 //
+// For batches of 64 tokens or more (bf16 router, no fused normalisation / records) the GEMV
+// becomes a tiled double-precision GEMM plus one softmax / selection block per token.
+//
 // Reference semantics: mlx-qwen38/loader.py:903-908 (router), loader.py:237-242
 // (topk_sorted_indices); cpp/src/layers.cpp:311-341.
 #include "common.cuh"
@@ -115,91 +118,10 @@ MOE_D uint32_t bf16_order_key(uint16_t v) {
     return (v & 0x8000) ? (uint32_t)(~v & 0xffff) : (uint32_t)(v | 0x8000);
 }
 
-template <bool kFp16, int kRbits>
-__global__ void __launch_bounds__(kThreads) router_kernel(RouterArgs a) {
+// Softmax (double, fixed reduction order), bf16 probabilities, MLX-order top-k, renorm and the
+// optional sorted top-M prediction of token t, from its bf16 logits (whole block).
+MOE_D void router_tail(const RouterArgs &a, int t) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int t = blockIdx.y;
-    const int rows = a.E * (a.M > 0 ? 2 : 1);
-    const int row = blockIdx.x * kWarps + warp;
-    const uint16_t *x = a.x + (size_t)t * a.H;
-
-    const bool next = row >= a.E;
-    const int e = next ? row - a.E : row;
-    uint4 wv[kPre];
-    if constexpr (kRbits == 16) {
-        if (row < rows) {
-            const uint16_t *w = reinterpret_cast<const uint16_t *>(next ? a.wn : a.w) + (size_t)e * a.H;
-            preload_row_bf16(w, a.H, lane, wv);   // weights do not depend on earlier kernels
-        }
-    }
-    pdl_wait();                                   // x is complete
-    pdl_launch_dependents();
-
-    // optional power-of-two RMS normalisation of the layer input (exact rescale)
-    double xmul = 1.0;
-    if (a.norm) {
-        __shared__ double s_ss[kWarps];
-        double ss = 0.0;
-        for (int i = threadIdx.x; i < a.H; i += kThreads) {
-            const double v = (double)bf16_bits_to_f32(x[i]);
-            ss = fma(v, v, ss);
-        }
-        ss = warp_sum_d(ss);
-        if (lane == 0) s_ss[warp] = ss;
-        __syncthreads();
-        ss = 0.0;
-#pragma unroll
-        for (int i = 0; i < kWarps; ++i) ss += s_ss[i];
-        xmul = ldexp(1.0, -pow2_rms_shift(ss, a.H));
-    }
-
-    if (a.xrec) {
-        // int8 MMA records of x for the expert kernels (gemv_i8.cuh): 16 threads per group
-        const int ng = a.H >> 6;
-        for (int G0 = blockIdx.x * (kThreads / 16); G0 < ng; G0 += gridDim.x * (kThreads / 16)) {
-            const int G = G0 + (threadIdx.x >> 4);
-            const bool v = G < ng;
-            const size_t fo = (size_t)t * pad4(ng) + G;
-            build_rec_group(x + (size_t)(v ? G : 0) * 64, v, threadIdx.x & 15, a.xrec + ((size_t)t * ng + G) * 16,
-                            a.xscale + fo, a.xsum + fo, (float)xmul);
-        }
-    }
-
-    if (row < rows) {
-        double acc;
-        if constexpr (kRbits == 16) {
-            const uint16_t *w = reinterpret_cast<const uint16_t *>(next ? a.wn : a.w) + (size_t)e * a.H;
-            acc = row_dot_bf16(x, w, a.H, lane, wv);
-        } else {
-            const int words = a.H * kRbits / 32, ng = a.H / a.gs;
-            const uint32_t *w = reinterpret_cast<const uint32_t *>(next ? a.wn : a.w) + (size_t)e * words;
-            const uint16_t *s = (next ? a.wns : a.ws) + (size_t)e * ng;
-            const uint16_t *b = (next ? a.wnb : a.wb) + (size_t)e * ng;
-            acc = row_dot_affine<kFp16>(x, w, s, b, a.H, kRbits, a.gs, lane);
-        }
-        acc = warp_sum_d(acc) * xmul;
-        if (lane == 0) {
-            uint16_t l = f64_to_bf16_bits(acc);
-            if (next) {
-                if (a.pred_bias) l = f32_to_bf16_bits(bf16_bits_to_f32(l) + a.pred_bias[e]);
-                a.plogits[(size_t)t * a.E + e] = l;
-            } else {
-                a.logits[(size_t)t * a.E + e] = l;
-            }
-        }
-    }
-
-    // ------------------------------------------------------------ last CTA of token t
-    __shared__ unsigned int s_last;
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        __threadfence();
-        const unsigned int prev = atomicAdd(a.tickets + t, 1u);
-        s_last = (prev == gridDim.x - 1) ? 1u : 0u;
-    }
-    __syncthreads();
-    if (!s_last) return;
-    __threadfence();
 
     __shared__ uint32_t s_keys[kMaxE];
     __shared__ double s_ex[kMaxE];
@@ -286,11 +208,204 @@ __global__ void __launch_bounds__(kThreads) router_kernel(RouterArgs a) {
             }
         }
     }
+}
+
+template <bool kFp16, int kRbits>
+__global__ void __launch_bounds__(kThreads) router_kernel(RouterArgs a) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int t = blockIdx.y;
+    const int rows = a.E * (a.M > 0 ? 2 : 1);
+    const int row = blockIdx.x * kWarps + warp;
+    const uint16_t *x = a.x + (size_t)t * a.H;
+
+    const bool next = row >= a.E;
+    const int e = next ? row - a.E : row;
+    uint4 wv[kPre];
+    if constexpr (kRbits == 16) {
+        if (row < rows) {
+            const uint16_t *w = reinterpret_cast<const uint16_t *>(next ? a.wn : a.w) + (size_t)e * a.H;
+            preload_row_bf16(w, a.H, lane, wv);   // weights do not depend on earlier kernels
+        }
+    }
+    pdl_wait();                                   // x is complete
+    pdl_launch_dependents();
+
+    // optional power-of-two RMS normalisation of the layer input (exact rescale)
+    double xmul = 1.0;
+    if (a.norm) {
+        __shared__ double s_ss[kWarps];
+        double ss = 0.0;
+        for (int i = threadIdx.x; i < a.H; i += kThreads) {
+            const double v = (double)bf16_bits_to_f32(x[i]);
+            ss = fma(v, v, ss);
+        }
+        ss = warp_sum_d(ss);
+        if (lane == 0) s_ss[warp] = ss;
+        __syncthreads();
+        ss = 0.0;
+#pragma unroll
+        for (int i = 0; i < kWarps; ++i) ss += s_ss[i];
+        xmul = ldexp(1.0, -pow2_rms_shift(ss, a.H));
+    }
+
+    if (a.xrec) {
+        // int8 MMA records of x for the expert kernels (gemv_i8.cuh): 16 threads per group
+        const int ng = a.H >> 6;
+        for (int G0 = blockIdx.x * (kThreads / 16); G0 < ng; G0 += gridDim.x * (kThreads / 16)) {
+            const int G = G0 + (threadIdx.x >> 4);
+            const bool v = G < ng;
+            const size_t fo = (size_t)t * pad4(ng) + G;
+            build_rec_group(x + (size_t)(v ? G : 0) * 64, v, threadIdx.x & 15, a.xrec + ((size_t)t * ng + G) * 16,
+                            a.xscale + fo, a.xsum + fo, (float)xmul);
+        }
+    }
+
+    if (row < rows) {
+        double acc;
+        if constexpr (kRbits == 16) {
+            const uint16_t *w = reinterpret_cast<const uint16_t *>(next ? a.wn : a.w) + (size_t)e * a.H;
+            acc = row_dot_bf16(x, w, a.H, lane, wv);
+        } else {
+            const int words = a.H * kRbits / 32, ng = a.H / a.gs;
+            const uint32_t *w = reinterpret_cast<const uint32_t *>(next ? a.wn : a.w) + (size_t)e * words;
+            const uint16_t *s = (next ? a.wns : a.ws) + (size_t)e * ng;
+            const uint16_t *b = (next ? a.wnb : a.wb) + (size_t)e * ng;
+            acc = row_dot_affine<kFp16>(x, w, s, b, a.H, kRbits, a.gs, lane);
+        }
+        acc = warp_sum_d(acc) * xmul;
+        if (lane == 0) {
+            uint16_t l = f64_to_bf16_bits(acc);
+            if (next) {
+                if (a.pred_bias) l = f32_to_bf16_bits(bf16_bits_to_f32(l) + a.pred_bias[e]);
+                a.plogits[(size_t)t * a.E + e] = l;
+            } else {
+                a.logits[(size_t)t * a.E + e] = l;
+            }
+        }
+    }
+
+    // ------------------------------------------------------------ last CTA of token t
+    __shared__ unsigned int s_last;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        __threadfence();
+        const unsigned int prev = atomicAdd(a.tickets + t, 1u);
+        s_last = (prev == gridDim.x - 1) ? 1u : 0u;
+    }
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+    router_tail(a, t);
     if (threadIdx.x == 0) a.tickets[t] = 0u;   // re-arm for the next launch
+}
+
+// ---------------------------------------------------------------- batched path (T >= 64)
+//
+// For many tokens the router is a GEMM: logits[T][E] = x . W^T. Tiles of 64 tokens x 128
+// rows per CTA, every thread a 4 x 8 micro-tile of double accumulators; the operands are
+// converted exactly to double once when staged in shared memory, so each term is an exact
+// product and the sum is a double sum (the same arithmetic as the per-token kernel, in
+// another order: the bf16 rounding of the result differs only for a value within ~2^-45 of
+// a rounding midpoint). Then one block per token runs router_tail.
+constexpr int kGT = 64, kGE = 128, kGK = 32;      // tokens, rows, K per stage
+constexpr size_t kGemmSmem = (size_t)kGK * (kGT + kGE) * sizeof(double);
+
+__global__ void __launch_bounds__(256) router_gemm_kernel(RouterArgs a) {
+    extern __shared__ double gsm[];
+    double *xs = gsm;                  // [kGK][kGT]
+    double *ws = gsm + kGK * kGT;      // [kGK][kGE]
+    const int tid = threadIdx.x;
+    const int t0 = blockIdx.y * kGT, r0 = blockIdx.x * kGE;
+    const int rows = a.E * (a.M > 0 ? 2 : 1);
+    const int tt = tid & 15, te = tid >> 4;         // tokens tt*4 .. +3, rows te*8 .. +7
+    const uint16_t *w = static_cast<const uint16_t *>(a.w);
+    const uint16_t *wn = static_cast<const uint16_t *>(a.wn);
+    pdl_wait();
+    pdl_launch_dependents();
+    double acc[4][8];
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[i][j] = 0.0;
+    for (int k0 = 0; k0 < a.H; k0 += kGK) {
+        // x tile: 64 tokens x 32 values (8 per thread), w tile: 128 rows x 32 values (16 per thread)
+        {
+            const int tok = tid >> 2, c = (tid & 3) * 8;
+            const int gt = t0 + tok;
+            uint4 v = make_uint4(0u, 0u, 0u, 0u);
+            if (gt < a.T && k0 + c < a.H) v = *reinterpret_cast<const uint4 *>(a.x + (size_t)gt * a.H + k0 + c);
+            const uint32_t vv[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                xs[(c + 2 * q) * kGT + tok] = (double)__uint_as_float(vv[q] << 16);
+                xs[(c + 2 * q + 1) * kGT + tok] = (double)__uint_as_float(vv[q] & 0xffff0000u);
+            }
+        }
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            const int rr = (tid >> 2) + 64 * h, c = (tid & 3) * 8;
+            const int gr = r0 + rr;
+            uint4 v = make_uint4(0u, 0u, 0u, 0u);
+            if (gr < rows && k0 + c < a.H) {
+                const uint16_t *src = (gr < a.E) ? w + (size_t)gr * a.H : wn + (size_t)(gr - a.E) * a.H;
+                v = *reinterpret_cast<const uint4 *>(src + k0 + c);
+            }
+            const uint32_t vv[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                ws[(c + 2 * q) * kGE + rr] = (double)__uint_as_float(vv[q] << 16);
+                ws[(c + 2 * q + 1) * kGE + rr] = (double)__uint_as_float(vv[q] & 0xffff0000u);
+            }
+        }
+        __syncthreads();
+#pragma unroll 4
+        for (int k = 0; k < kGK; ++k) {
+            double xa[4], wb[8];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) xa[i] = xs[k * kGT + tt * 4 + i];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) wb[j] = ws[k * kGE + te * 8 + j];
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+#pragma unroll
+                for (int j = 0; j < 8; ++j) acc[i][j] = fma(xa[i], wb[j], acc[i][j]);
+        }
+        __syncthreads();
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const int gt = t0 + tt * 4 + i;
+        if (gt >= a.T) continue;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const int gr = r0 + te * 8 + j;
+            if (gr >= rows) continue;
+            uint16_t l = f64_to_bf16_bits(acc[i][j]);
+            if (gr >= a.E) {
+                if (a.pred_bias) l = f32_to_bf16_bits(bf16_bits_to_f32(l) + a.pred_bias[gr - a.E]);
+                a.plogits[(size_t)gt * a.E + gr - a.E] = l;
+            } else {
+                a.logits[(size_t)gt * a.E + gr] = l;
+            }
+        }
+    }
+}
+
+__global__ void __launch_bounds__(kThreads) router_select_kernel(RouterArgs a) {
+    pdl_wait();
+    pdl_launch_dependents();
+    router_tail(a, blockIdx.x);
 }
 
 template <bool kFp16>
 cudaError_t launch_router(const RouterArgs &a, int rbits, cudaStream_t st) {
+    if (rbits == 16 && a.T >= kGT && !a.xrec && !a.norm && (a.H % 8) == 0) {
+        const int rows = a.E * (a.M > 0 ? 2 : 1);
+        dim3 grid((rows + kGE - 1) / kGE, (a.T + kGT - 1) / kGT);
+        cudaError_t e = launch_pdl(router_gemm_kernel, grid, dim3(256), kGemmSmem, st, a);
+        if (e != cudaSuccess) return e;
+        return launch_pdl(router_select_kernel, dim3(a.T), dim3(kThreads), 0, st, a);
+    }
     const int rows = a.E * (a.M > 0 ? 2 : 1);
     dim3 grid((rows + kWarps - 1) / kWarps, a.T);
     switch (rbits) {
