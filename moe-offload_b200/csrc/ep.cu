@@ -26,6 +26,8 @@
 // reference itself runs on one device.
 #include <string.h>
 
+#include <algorithm>
+
 #include "common.cuh"
 #include "internal.h"
 
@@ -85,7 +87,9 @@ __global__ void __launch_bounds__(kExThreads) exchange_combine_kernel(ExArgs a) 
     const size_t nwork = (size_t)a.T * a.K * cpr;
     const size_t stride = (size_t)gridDim.x * blockDim.x;
 
-    // owned rows -> every rank's receive buffer (this rank's included)
+    // owned rows -> every rank's receive buffer (this rank's included); only threads that
+    // stored need the system-scope fence that orders their stores before the signal
+    bool stored = false;
     for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < nwork; i += stride) {
         const size_t row = i / cpr;
         const int c = (int)(i % cpr);
@@ -93,8 +97,9 @@ __global__ void __launch_bounds__(kExThreads) exchange_combine_kernel(ExArgs a) 
         const uint4 v = *reinterpret_cast<const uint4 *>(a.yk + row * a.H + (size_t)c * 8);
         const size_t off = par_off + (row * a.H + (size_t)c * 8) * 2;
         for (int p = 0; p < a.nranks; ++p) *reinterpret_cast<uint4 *>(a.peers[p] + off) = v;
+        stored = true;
     }
-    __threadfence_system();
+    if (stored) __threadfence_system();
     __syncthreads();
     if (threadIdx.x == 0) {
         const unsigned int old = atomicAdd(&hdr->arrive, 1u);
@@ -250,7 +255,11 @@ extern "C" int moe_ep_decode_layer(const void *x, int T, int H, int I, int E, in
              (uint32_t)e_count, out_inds, static_cast<const uint16_t *>(out_scores), w.yk,
              static_cast<const uint16_t *>(resid), static_cast<uint16_t *>(y)};
     void *kargs[] = {&a};
-    MOE_CUDA_TRY(cudaLaunchCooperativeKernel((const void *)exchange_combine_kernel, dim3(sms), dim3(kExThreads), kargs,
+    // grid sized to the work (16-byte chunks of the T*K rows and 8 outputs per thread), at
+    // most one CTA per SM (the CTAs wait for one another: cooperative launch)
+    const size_t chunks = (size_t)T * K * (H / 8);
+    const int grid = (int)std::min<size_t>((size_t)sms, std::max<size_t>(2, (chunks + 4 * kExThreads - 1) / (4 * kExThreads)));
+    MOE_CUDA_TRY(cudaLaunchCooperativeKernel((const void *)exchange_combine_kernel, dim3(grid), dim3(kExThreads), kargs,
                                              0, as_stream(stream)));
     return MOE_OK;
 }
