@@ -274,8 +274,9 @@ size_t moe_ep_workspace_bytes(int T, int H, int I, int E, int K);
  * rank (identical results), the local experts run on their (token, k) slots, and one kernel
  * exchanges the unweighted expert outputs over NVLink (peer stores into every rank's exchange
  * buffer, bounded waits on per-rank epoch flags) and combines them in MLX order:
- * y = bf16(resid + sum_k bf16(yk * score_k)), the same bits on every rank and as
- * moe_decode_layer. peers: device array [nranks] of exchange-buffer pointers (this rank's own
+ * y = bf16(resid + sum_k bf16(yk * score_k)), the same bits on every rank and, for T < 32,
+ * as moe_decode_layer; from T = 32 up the local experts run as the grouped tensor-core GEMMs
+ * of the prefill path and the result equals moe_prefill_layer's. peers: device array [nranks] of exchange-buffer pointers (this rank's own
  * at [rank], the others from moe_ep_buffer_open), all sized for at least T tokens. Every rank
  * must call this the same number of times, in the same order, with the same T. Replaces the
  * per-layer decode body of mlx-qwen38/loader.py:903-922 (single device in the reference).

@@ -21,6 +21,11 @@
 // e + 2 into a buffer after every rank has signalled e + 1, which each rank does only after
 // its kernel for epoch e (the last reader of that parity) has finished.
 //
+// Batches of kEpGemmT tokens or more run the local experts as the prefill path's grouped
+// tensor-core GEMMs (each routed expert's weights read once for all of its tokens; the
+// arithmetic of moe_prefill_layer), smaller batches as per-slot int8 GEMVs (the arithmetic of
+// moe_decode_layer); the exchange and combine are the same.
+//
 // Reference semantics: the decode body of the reference's hook (mlx-qwen38/loader.py:903-922)
 // with the experts split across devices, as the expert-parallel configuration asks; the
 // reference itself runs on one device.
@@ -139,6 +144,10 @@ __global__ void __launch_bounds__(kExThreads) exchange_combine_kernel(ExArgs a) 
     }
 }
 
+// batches of at least this many tokens run the local experts as grouped tensor-core GEMMs
+// (each routed expert's weights read once for all its tokens) instead of per-slot GEMVs
+constexpr int kEpGemmT = 32;
+
 struct EpWs {
     unsigned int *tickets;
     uint16_t *logits;
@@ -149,6 +158,9 @@ struct EpWs {
     float *ascale, *asum;
     unsigned int *acnt;
     uint16_t *yk;
+    uint16_t *xn;            // normalised rows (GEMM path)
+    void *pws;               // grouped-GEMM workspace (GEMM path)
+    size_t pws_bytes;
     size_t bytes;
 };
 
@@ -169,6 +181,11 @@ EpWs carve(void *base, int T, int H, int I, int E, int K) {
     w.ascale = reinterpret_cast<float *>(take((size_t)T * pad4(K * ngI) * 4));
     w.asum = reinterpret_cast<float *>(take((size_t)T * pad4(K * ngI) * 4));
     w.yk = reinterpret_cast<uint16_t *>(take((size_t)T * K * H * 2));
+    if (T >= kEpGemmT) {
+        w.xn = reinterpret_cast<uint16_t *>(take((size_t)T * H * 2));
+        w.pws_bytes = moe_prefill_workspace_bytes(T, H, I, E, K);
+        w.pws = take(w.pws_bytes);
+    }
     w.bytes = off;
     return w;
 }
@@ -238,16 +255,36 @@ extern "C" int moe_ep_decode_layer(const void *x, int T, int H, int I, int E, in
         return moe_set_error(MOE_EINVAL, "ep_decode_layer: workspace of %zu bytes needed, %zu given", need,
                              workspace_bytes);
     EpWs w = carve(workspace, T, H, I, E, K);
-    int rc = moe_router_launch(x, T, H, E, K, router_w, nullptr, nullptr, 16, 64, 0, nullptr, nullptr, nullptr, 0,
+    int rc;
+    if (T >= kEpGemmT) {
+        // normalised rows, router on them, local experts as grouped GEMMs (the arithmetic of
+        // moe_prefill_layer), unweighted outputs in assignment order for the exchange
+        const void *xin = x;
+        if (norm) {
+            rc = moe_pow2_rows_launch(x, T, H, w.xn, stream);
+            if (rc) return rc;
+            xin = w.xn;
+        }
+        rc = moe_router_launch(xin, T, H, E, K, router_w, nullptr, nullptr, 16, 64, 0, nullptr, nullptr, nullptr, 0,
+                               nullptr, nullptr, nullptr, out_inds, out_scores, nullptr, w.tickets, w.logits, nullptr,
+                               nullptr, nullptr, nullptr, 0, stream);
+        if (rc) return rc;
+        rc = moe_prefill_experts_ex(xin, T, H, I, e_count, K, out_inds, (uint32_t)e_begin, 0, nullptr, wg, sg, bg, wu,
+                                    su, bu, wd, sd, bd, sb_fp16, nullptr, nullptr, w.yk, nullptr, w.pws, w.pws_bytes,
+                                    stream);
+        if (rc) return rc;
+    } else {
+        rc = moe_router_launch(x, T, H, E, K, router_w, nullptr, nullptr, 16, 64, 0, nullptr, nullptr, nullptr, 0,
                                nullptr, nullptr, nullptr, out_inds, out_scores, nullptr, w.tickets, w.logits, nullptr,
                                w.xrec, w.xscale, w.xsum, norm, stream);
-    if (rc) return rc;
-    rc = moe_experts_gateup_ex(x, w.xrec, w.xscale, w.xsum, T, H, I, K, e_count, out_inds, wg, sg, bg, wu, su, bu, 2,
-                               64, sb_fp16, w.act, w.arec, w.ascale, w.asum, w.acnt, stream, (uint32_t)e_begin);
-    if (rc) return rc;
-    rc = moe_experts_down_ex(w.act, w.arec, w.ascale, w.asum, T, H, I, K, e_count, out_inds, nullptr, wd, sd, bd, 2,
-                             64, sb_fp16, nullptr, nullptr, nullptr, w.yk, stream, (uint32_t)e_begin);
-    if (rc) return rc;
+        if (rc) return rc;
+        rc = moe_experts_gateup_ex(x, w.xrec, w.xscale, w.xsum, T, H, I, K, e_count, out_inds, wg, sg, bg, wu, su, bu,
+                                   2, 64, sb_fp16, w.act, w.arec, w.ascale, w.asum, w.acnt, stream, (uint32_t)e_begin);
+        if (rc) return rc;
+        rc = moe_experts_down_ex(w.act, w.arec, w.ascale, w.asum, T, H, I, K, e_count, out_inds, nullptr, wd, sd, bd, 2,
+                                 64, sb_fp16, nullptr, nullptr, nullptr, w.yk, stream, (uint32_t)e_begin);
+        if (rc) return rc;
+    }
     int dev = 0, sms = 0;
     MOE_CUDA_TRY(cudaGetDevice(&dev));
     MOE_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));

@@ -26,3 +26,15 @@ int moe_experts_down_ex(const void *act, const void *arec, const float *ascale, 
                         const void *sd, const void *bd, int bits, int group_size, int sb_fp16,
                         const void *addend, const void *resid, void *y, void *yk, void *stream,
                         uint32_t slot_base = 0);
+
+// Grouped expert GEMMs (prefill.cu): experts [e_begin, e_begin + E) of the routing, weights
+// indexed from e_begin; strict = 0 skips other assignments; y (combine + resid) and / or
+// yk_out [T*K][H] (unweighted expert outputs in assignment order).
+int moe_prefill_experts_ex(const void *x, int T, int H, int I, int E, int K, const uint32_t *inds, uint32_t e_begin,
+                           int strict, const void *scores, const uint32_t *wg, const void *sg, const void *bg,
+                           const uint32_t *wu, const void *su, const void *bu, const uint32_t *wd, const void *sd,
+                           const void *bd, int sb_fp16, const void *resid, void *y, void *yk_out, void *act_out,
+                           void *workspace, size_t workspace_bytes, void *stream);
+
+// xn[t] = x[t] * 2^-k(t), the per-row power-of-two RMS normalisation (prefill.cu)
+int moe_pow2_rows_launch(const void *x, int T, int H, void *xn, void *stream);

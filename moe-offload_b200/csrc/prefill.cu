@@ -170,11 +170,13 @@ struct Tile {
     int e, row0, pos0, n;   // expert, first weight row, first assignment position, tokens
 };
 
-__global__ void count_kernel(const uint32_t *inds, int TK, int E, int *counts) {
+// expert ids are taken relative to e_begin (a rank's block of the experts); ids outside
+// [e_begin, e_begin + E) are skipped when `strict` is 0 and flagged as bad input otherwise
+__global__ void count_kernel(const uint32_t *inds, int TK, int E, uint32_t e_begin, int strict, int *counts) {
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < TK; i += gridDim.x * blockDim.x) {
-        const uint32_t e = inds[i];
+        const uint32_t e = inds[i] - e_begin;
         if (e < (uint32_t)E) atomicAdd(&counts[e], 1);
-        else atomicOr(&g_moe_device_error, MOE_DEVERR_BAD_INPUT);
+        else if (strict) atomicOr(&g_moe_device_error, MOE_DEVERR_BAD_INPUT);
     }
 }
 
@@ -243,10 +245,10 @@ __global__ void __launch_bounds__(1024) scan_kernel(const int *counts, int E, in
 }
 
 // assignment i = t*K + k goes to position offsets[e] + (arrival order within e)
-__global__ void scatter_kernel(const uint32_t *inds, int TK, int E, const int *offsets, int *cursor, int *pos_of,
-                               int *src_of) {
+__global__ void scatter_kernel(const uint32_t *inds, int TK, int E, uint32_t e_begin, const int *offsets, int *cursor,
+                               int *pos_of, int *src_of) {
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < TK; i += gridDim.x * blockDim.x) {
-        const uint32_t e = inds[i];
+        const uint32_t e = inds[i] - e_begin;
         if (e >= (uint32_t)E) continue;
         const int p = offsets[e] + atomicAdd(&cursor[e], 1);
         pos_of[i] = p;
@@ -579,6 +581,20 @@ __global__ void combine_kernel(const uint16_t *yk, const int *pos_of, const uint
     }
 }
 
+// yk_out[i] = yk[pos_of[i]] for every assignment i = t*K + k that was bucketed (16-byte copies)
+__global__ void unsort_kernel(const uint16_t *yk, const int *pos_of, int TK, int H, uint16_t *yk_out) {
+    const int cpr = H / 8;
+    const size_t n = (size_t)TK * cpr;
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
+        const size_t a = i / cpr;
+        const int c = (int)(i % cpr);
+        const int p = pos_of[a];
+        if (p < 0) continue;
+        *reinterpret_cast<uint4 *>(yk_out + a * H + (size_t)c * 8) =
+            *reinterpret_cast<const uint4 *>(yk + (size_t)p * H + (size_t)c * 8);
+    }
+}
+
 struct PrefillWs {
     int *counts, *offsets, *cursor, *pos_of, *src_of, *ntiles;
     Tile *tiles1, *tiles2;
@@ -679,12 +695,17 @@ extern "C" size_t moe_prefill_workspace_bytes(int T, int H, int I, int E, int K)
     return carve(nullptr, T, H, I, E, K).bytes;
 }
 
-extern "C" int moe_prefill_experts(const void *x, int T, int H, int I, int E, int K, const uint32_t *inds,
-                                   const void *scores, const uint32_t *wg, const void *sg, const void *bg,
-                                   const uint32_t *wu, const void *su, const void *bu, const uint32_t *wd,
-                                   const void *sd, const void *bd, int sb_fp16, const void *resid, void *y,
-                                   void *act_out, void *workspace, size_t workspace_bytes, void *stream) {
-    if (!x || !inds || !scores || !wg || !sg || !bg || !wu || !su || !bu || !wd || !sd || !bd || !y || !workspace)
+// The grouped expert GEMMs of T rows; experts [e_begin, e_begin + E) of the routing are
+// this call's (weights indexed from e_begin); strict = 0 skips the other assignments.
+// Output: y = combine (+ resid) when y is given, and/or the unweighted expert output of every
+// bucketed assignment i = t*K + k in yk_out [T*K][H].
+int moe_prefill_experts_ex(const void *x, int T, int H, int I, int E, int K, const uint32_t *inds, uint32_t e_begin,
+                           int strict, const void *scores, const uint32_t *wg, const void *sg, const void *bg,
+                           const uint32_t *wu, const void *su, const void *bu, const uint32_t *wd, const void *sd,
+                           const void *bd, int sb_fp16, const void *resid, void *y, void *yk_out, void *act_out,
+                           void *workspace, size_t workspace_bytes, void *stream) {
+    if (!x || !inds || !wg || !sg || !bg || !wu || !su || !bu || !wd || !sd || !bd || !workspace || (!y && !yk_out) ||
+        (y && !scores))
         return moe_set_error(MOE_EINVAL, "prefill_experts: null pointer");
     if (T <= 0 || E <= 0 || K <= 0 || K > 64 || H % 64 || I % 64 || H < 64 || I < 64)
         return moe_set_error(MOE_EINVAL, "prefill_experts: bad sizes T=%d H=%d I=%d E=%d K=%d", T, H, I, E, K);
@@ -703,9 +724,9 @@ extern "C" int moe_prefill_experts(const void *x, int T, int H, int I, int E, in
     MOE_CUDA_TRY(cudaMemsetAsync(w.counts, 0, (size_t)E * 4, st));
     MOE_CUDA_TRY(cudaMemsetAsync(w.pos_of, 0xff, (size_t)TK * 4, st));
     MOE_CUDA_TRY(cudaMemsetAsync(w.src_of, 0xff, (size_t)TK * 4, st));
-    count_kernel<<<(TK + 255) / 256, 256, 0, st>>>(inds, TK, E, w.counts);
+    count_kernel<<<(TK + 255) / 256, 256, 0, st>>>(inds, TK, E, e_begin, strict, w.counts);
     scan_kernel<<<1, 1024, 0, st>>>(w.counts, E, I, H, w.offsets, w.cursor, w.tiles1, w.ntiles, w.tiles2, w.ntiles + 1);
-    scatter_kernel<<<(TK + 255) / 256, 256, 0, st>>>(inds, TK, E, w.offsets, w.cursor, w.pos_of, w.src_of);
+    scatter_kernel<<<(TK + 255) / 256, 256, 0, st>>>(inds, TK, E, e_begin, w.offsets, w.cursor, w.pos_of, w.src_of);
     MOE_CUDA_TRY(cudaGetLastError());
 
     uint16_t *act = act_out ? static_cast<uint16_t *>(act_out) : w.act;
@@ -730,8 +751,27 @@ extern "C" int moe_prefill_experts(const void *x, int T, int H, int I, int E, in
     rc = sb_fp16 ? launch_gemm<true, true>(mg, mu, mx, g1, sms, st) : launch_gemm<true, false>(mg, mu, mx, g1, sms, st);
     if (!rc) rc = sb_fp16 ? launch_gemm<false, true>(md, md, ma, g2, sms, st) : launch_gemm<false, false>(md, md, ma, g2, sms, st);
     if (rc) return rc;
-    combine_kernel<<<sms * 4, 256, 0, st>>>(w.yk, w.pos_of, static_cast<const uint16_t *>(scores),
-                                             static_cast<const uint16_t *>(resid), T, K, H, static_cast<uint16_t *>(y));
+    if (y)
+        combine_kernel<<<sms * 4, 256, 0, st>>>(w.yk, w.pos_of, static_cast<const uint16_t *>(scores),
+                                                 static_cast<const uint16_t *>(resid), T, K, H, static_cast<uint16_t *>(y));
+    if (yk_out)
+        unsort_kernel<<<sms * 4, 256, 0, st>>>(w.yk, w.pos_of, TK, H, static_cast<uint16_t *>(yk_out));
+    MOE_CUDA_TRY(cudaGetLastError());
+    return MOE_OK;
+}
+
+extern "C" int moe_prefill_experts(const void *x, int T, int H, int I, int E, int K, const uint32_t *inds,
+                                   const void *scores, const uint32_t *wg, const void *sg, const void *bg,
+                                   const uint32_t *wu, const void *su, const void *bu, const uint32_t *wd,
+                                   const void *sd, const void *bd, int sb_fp16, const void *resid, void *y,
+                                   void *act_out, void *workspace, size_t workspace_bytes, void *stream) {
+    if (!y || !scores) return moe_set_error(MOE_EINVAL, "prefill_experts: null pointer");
+    return moe_prefill_experts_ex(x, T, H, I, E, K, inds, 0u, 1, scores, wg, sg, bg, wu, su, bu, wd, sd, bd, sb_fp16,
+                                  resid, y, nullptr, act_out, workspace, workspace_bytes, stream);
+}
+
+int moe_pow2_rows_launch(const void *x, int T, int H, void *xn, void *stream) {
+    pow2_rows_kernel<<<T, 256, 0, as_stream(stream)>>>(static_cast<const uint16_t *>(x), H, static_cast<uint16_t *>(xn));
     MOE_CUDA_TRY(cudaGetLastError());
     return MOE_OK;
 }

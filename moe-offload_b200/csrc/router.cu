@@ -8,7 +8,7 @@
 //   logit; the last CTA to finish a token (atomic ticket in the workspace) runs the
 //   softmax / selection tail for that token and re-arms the ticket.
 //
-// For batches of 64 tokens or more (bf16 router, no fused normalisation / records) the GEMV
+// For batches of 1024 tokens or more (bf16 router, no fused normalisation / records) the GEMV
 // becomes a tiled double-precision GEMM plus one softmax / selection block per token.
 //
 // Reference semantics: mlx-qwen38/loader.py:903-908 (router), loader.py:237-242
@@ -299,7 +299,7 @@ __global__ void __launch_bounds__(kThreads) router_kernel(RouterArgs a) {
     if (threadIdx.x == 0) a.tickets[t] = 0u;   // re-arm for the next launch
 }
 
-// ---------------------------------------------------------------- batched path (T >= 64)
+// ---------------------------------------------------------------- batched path (T >= 1024)
 //
 // For many tokens the router is a GEMM: logits[T][E] = x . W^T. Tiles of 64 tokens x 128
 // rows per CTA, every thread a 4 x 8 micro-tile of double accumulators; the operands are
@@ -308,6 +308,7 @@ __global__ void __launch_bounds__(kThreads) router_kernel(RouterArgs a) {
 // another order: the bf16 rounding of the result differs only for a value within ~2^-45 of
 // a rounding midpoint). Then one block per token runs router_tail.
 constexpr int kGT = 64, kGE = 128, kGK = 32;      // tokens, rows, K per stage
+constexpr int kGemmMinT = 1024;                    // batches from this size use the GEMM
 constexpr size_t kGemmSmem = (size_t)kGK * (kGT + kGE) * sizeof(double);
 
 __global__ void __launch_bounds__(256) router_gemm_kernel(RouterArgs a) {
@@ -399,7 +400,9 @@ __global__ void __launch_bounds__(kThreads) router_select_kernel(RouterArgs a) {
 
 template <bool kFp16>
 cudaError_t launch_router(const RouterArgs &a, int rbits, cudaStream_t st) {
-    if (rbits == 16 && a.T >= kGT && !a.xrec && !a.norm && (a.H % 8) == 0) {
+    // the tiled GEMM only pays once its tile grid covers most SMs (64 tokens x 128 rows per CTA);
+    // smaller batches keep one warp per (row, token)
+    if (rbits == 16 && a.T >= kGemmMinT && !a.xrec && !a.norm && (a.H % 8) == 0) {
         const int rows = a.E * (a.M > 0 ? 2 : 1);
         dim3 grid((rows + kGE - 1) / kGE, (a.T + kGT - 1) / kGT);
         cudaError_t e = launch_pdl(router_gemm_kernel, grid, dim3(256), kGemmSmem, st, a);

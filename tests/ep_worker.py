@@ -35,11 +35,14 @@ def main() -> int:
     xs = [np_to_bf16_tensor(np_bf16_normal(rng, (T, H)), dev) for _ in range(3)]
     bad = []
 
-    # single layer calls, twice in a row (the epochs advance), batch sizes T and 1
-    xbuf = ExchangeBuffers(T, K, H, dev)
-    for x in (xs[0], xs[1][:1], xs[0]):
+    # single layer calls, twice in a row (the epochs advance), batch sizes T and 1, and a
+    # batch of 40 (grouped-GEMM path, compared with the single-GPU prefill layer)
+    xb = np_to_bf16_tensor(np_bf16_normal(rng, (40, H)), dev)
+    xbuf = ExchangeBuffers(40, K, H, dev)
+    for x in (xs[0], xs[1][:1], xs[0], xb, xb):
         o = ep_decode_layer(x, local[0], E, first, K, xbuf, norm=True, resid=x)
-        r = ops.decode_layer(x, full[0].router, full[0].gate, full[0].up, full[0].down, K, norm=True, resid=x)
+        ref = ops.decode_layer if x.shape[0] < 32 else ops.prefill_layer
+        r = ref(x, full[0].router, full[0].gate, full[0].up, full[0].down, K, norm=True, resid=x)
         torch.cuda.synchronize()
         for key in ("inds", "scores", "y"):
             if not torch.equal(o[key], r[key]):

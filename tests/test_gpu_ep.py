@@ -1,5 +1,6 @@
 """Expert-parallel decode (moe_ep_decode_layer): on one GPU the single-rank form must equal the
-single-GPU decode layer bit for bit; on two GPUs (when present) every rank, holding half of
+single-GPU decode layer bit for bit (below 32 tokens; from 32 tokens up, the grouped-GEMM
+path, the single-GPU prefill layer); on two GPUs (when present) every rank, holding half of
 the experts, must produce the same bits as the single-GPU layer (tests/ep_worker.py)."""
 import os
 import socket
@@ -20,7 +21,7 @@ def dev():
     return torch.device("cuda:0")
 
 
-@pytest.mark.parametrize("T", [1, 5])
+@pytest.mark.parametrize("T", [1, 5, 31, 32, 40])
 def test_ep_single_rank_equals_decode_layer(dev, T):
     from moe_offload_b200 import _lib, ops
     from moe_offload_b200.ep import ExchangeBuffers, ep_decode_layer
@@ -35,7 +36,10 @@ def test_ep_single_rank_equals_decode_layer(dev, T):
         for rep in range(3):
             x = np_to_bf16_tensor(np_bf16_normal(rng, (T, H)), dev)
             o = ep_decode_layer(x, ly, E, 0, K, xbuf, norm=True, resid=x)
-            r = ops.decode_layer(x, ly.router, ly.gate, ly.up, ly.down, K, norm=True, resid=x)
+            if T < 32:
+                r = ops.decode_layer(x, ly.router, ly.gate, ly.up, ly.down, K, norm=True, resid=x)
+            else:
+                r = ops.prefill_layer(x, ly.router, ly.gate, ly.up, ly.down, K, norm=True, resid=x)
             torch.cuda.synchronize()
             for key in ("inds", "scores", "y"):
                 assert torch.equal(o[key], r[key]), f"call {rep}: {key} differs"
