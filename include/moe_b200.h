@@ -243,6 +243,29 @@ int moe_prefill_layer(const void *x, int T, int H, int I, int E, int K, const vo
                       int sb_fp16, int norm, const void *resid, uint32_t *out_inds, void *out_scores,
                       void *y, void *workspace, size_t workspace_bytes, void *stream);
 
+/*
+ * The cached-layer form of the prefill GEMMs (CachedSwitchGLU.__call__ with L > 1,
+ * mlx-qwen38/loader.py:566-699): experts in slot buffers [cap][...] (MLX layout), slots u32
+ * [T][K] = the slot of each (token, k) assignment, or any value >= cap to skip it. Writes the
+ * unweighted expert outputs of the assignments it runs to yk_out bf16 [T*K][H] (assignment
+ * order t*K + k) and leaves the other rows untouched, so chunks of a prompt's experts can be
+ * run one after another into the same buffer. Workspace: moe_prefill_workspace_bytes(T, H, I,
+ * cap, K).
+ */
+int moe_prefill_experts_slots(const void *x, int T, int H, int I, int cap, int K, const uint32_t *slots,
+                              const uint32_t *wg, const void *sg, const void *bg, const uint32_t *wu,
+                              const void *su, const void *bu, const uint32_t *wd, const void *sd,
+                              const void *bd, int sb_fp16, void *yk_out, void *workspace,
+                              size_t workspace_bytes, void *stream);
+
+/* y[t] = bf16(resid[t] + sum_k bf16(yk[t*K + k] * scores[t][k])), the sum sequential in bf16
+ * over k in MLX order (loader.py:914,965); resid may be NULL. */
+int moe_combine_rows(const void *yk, int T, int K, int H, const void *scores, const void *resid, void *y,
+                     void *stream);
+
+/* xn[t] = x[t] * 2^-k(t): the per-row power-of-two RMS normalisation of moe_decode_layer. */
+int moe_pow2_rows(const void *x, int T, int H, void *xn, void *stream);
+
 /* ------------------------------------------------------------------------------------ */
 /* Expert parallelism: one process per GPU, experts split in contiguous blocks.           */
 /* ------------------------------------------------------------------------------------ */

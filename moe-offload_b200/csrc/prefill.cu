@@ -550,7 +550,7 @@ __global__ void combine_kernel(const uint16_t *yk, const int *pos_of, const uint
         const int t = (int)(i / cpr), c = (int)(i % cpr);
         float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
         for (int k = 0; k < K; ++k) {
-            const int p = pos_of[t * K + k];
+            const int p = pos_of ? pos_of[t * K + k] : t * K + k;   // null: rows in assignment order
             if (p < 0 || p >= TK) {            // an expert id >= E was never scattered
                 atomicOr(&g_moe_device_error, MOE_DEVERR_BAD_INPUT);
                 continue;
@@ -809,4 +809,38 @@ extern "C" int moe_prefill_layer(const void *x, int T, int H, int I, int E, int 
     if (rc) return rc;
     return moe_prefill_experts(xin, T, H, I, E, K, out_inds, out_scores, wg, sg, bg, wu, su, bu, wd, sd, bd, sb_fp16,
                                resid, y, nullptr, pws, workspace_bytes - layer_prefix_bytes(T, H, E), stream);
+}
+
+extern "C" int moe_prefill_experts_slots(const void *x, int T, int H, int I, int cap, int K, const uint32_t *slots,
+                                         const uint32_t *wg, const void *sg, const void *bg, const uint32_t *wu,
+                                         const void *su, const void *bu, const uint32_t *wd, const void *sd,
+                                         const void *bd, int sb_fp16, void *yk_out, void *workspace,
+                                         size_t workspace_bytes, void *stream) {
+    if (!yk_out) return moe_set_error(MOE_EINVAL, "prefill_experts_slots: null output");
+    return moe_prefill_experts_ex(x, T, H, I, cap, K, slots, 0u, 0, nullptr, wg, sg, bg, wu, su, bu, wd, sd, bd,
+                                  sb_fp16, nullptr, nullptr, yk_out, nullptr, workspace, workspace_bytes, stream);
+}
+
+extern "C" int moe_combine_rows(const void *yk, int T, int K, int H, const void *scores, const void *resid, void *y,
+                                void *stream) {
+    if (!yk || !scores || !y) return moe_set_error(MOE_EINVAL, "combine_rows: null pointer");
+    if (T <= 0 || K <= 0 || H <= 0 || H % 8)
+        return moe_set_error(MOE_EINVAL, "combine_rows: bad sizes T=%d K=%d H=%d", T, K, H);
+    const void *al[] = {yk, resid, y};
+    for (const void *p : al)
+        if (reinterpret_cast<uintptr_t>(p) % 16) return moe_set_error(MOE_EINVAL, "combine_rows: 16-byte alignment");
+    int dev = 0, sms = 0;
+    MOE_CUDA_TRY(cudaGetDevice(&dev));
+    MOE_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+    combine_kernel<<<sms * 4, 256, 0, as_stream(stream)>>>(static_cast<const uint16_t *>(yk), nullptr,
+                                                           static_cast<const uint16_t *>(scores),
+                                                           static_cast<const uint16_t *>(resid), T, K, H,
+                                                           static_cast<uint16_t *>(y));
+    MOE_CUDA_TRY(cudaGetLastError());
+    return MOE_OK;
+}
+
+extern "C" int moe_pow2_rows(const void *x, int T, int H, void *xn, void *stream) {
+    if (!x || !xn || T <= 0 || H <= 0) return moe_set_error(MOE_EINVAL, "pow2_rows: bad arguments");
+    return moe_pow2_rows_launch(x, T, H, xn, stream);
 }

@@ -268,6 +268,85 @@ class CachedSwitchGLU:
         out, _ = ops.experts_down(act, slots.view(1, K), self.down, scores.view(1, K), resid=resid, y=y)
         return out
 
+    # ---------------------------------------------------------------- prefill
+    def _load_sync(self, eids: list[int], slots: list[int]) -> None:
+        """Synchronous fill of (eid -> slot) with the reference's prefill accounting
+        (c_layer_load_sync, expert_io.c:710-724: prefill bytes; 9 reads per expert and 9 per
+        run of consecutive expert ids)."""
+        import ctypes
+        n = len(eids)
+        lst = (ctypes.c_int32 * (1 + 2 * n))(n, *eids, *slots)
+        cs = self._cs()
+        call("moe_fill_slots_host", lst, n, self.E, self.capacity, 9, self._src, self._dst, self._rows, cs)
+        se = sorted(eids)
+        runs = 1 + sum(1 for a, b in zip(se, se[1:]) if b != a + 1)
+        for idx, v in ((9, n * self.expert_bytes), (16, 9 * n), (17, 9 * runs)):
+            call("moe_lru_add_stat", self.state.data_ptr(), self.E, self.capacity, idx, v, cs)
+
+    def prefill(self, x: torch.Tensor, indices: torch.Tensor) -> torch.Tensor:
+        """The L > 1 branch of the reference's __call__ (loader.py:566-699): x [T, H] bf16
+        (the layer's normalised input), indices [T, K] int32 (device) -> unweighted expert
+        outputs [T, K, H] bf16. The prompt's unique experts (ascending id) are run in chunks of
+        `capacity`: the chunk's i-th expert goes to slot i (a synchronous fill unless it is
+        there already), the chunk's assignments run as grouped tensor-core GEMMs on the slot
+        buffers (moe_prefill_experts_slots), and afterwards the LRU is rebuilt from the final
+        slot contents with the last chunk most recently used, together with the prompt's
+        hit / miss counts (c_layer_set_lru_state)."""
+        self.wait_prefetch()
+        T, K = indices.shape
+        H = x.shape[1]
+        I = self.gate.w.shape[1]
+        eids0, slots0 = self.get_lru_state()
+        lru = dict(zip(eids0, slots0))
+        slot_to_eid = {sl: e for e, sl in lru.items()}
+        eid_to_slot = dict(lru)
+        idx = indices.reshape(-1).cpu().numpy().astype(np.int64)
+        uniq, counts = np.unique(idx, return_counts=True)
+        prior = set(lru)
+        add_req, add_hits, add_misses = int(idx.size), 0, 0
+        for e, c in zip(uniq.tolist(), counts.tolist()):
+            if e in prior:
+                add_hits += c
+            else:
+                add_misses += 1
+                add_hits += c - 1
+        yk = torch.empty((T * K, H), dtype=torch.bfloat16, device=self.device)
+        nb = int(call("moe_prefill_workspace_bytes", T, H, I, self.capacity, K))
+        ws = torch.empty(nb, dtype=torch.uint8, device=self.device)
+        g, u, d = self.gate, self.up, self.down
+        last = 0
+        for u0 in range(0, len(uniq), self.capacity):
+            chunk = uniq[u0:u0 + self.capacity]
+            last = len(chunk)
+            load_e, load_s = [], []
+            for s_idx, e in enumerate(chunk.tolist()):
+                if slot_to_eid.get(s_idx) != e:
+                    old = slot_to_eid.get(s_idx)
+                    if old is not None and eid_to_slot.get(old) == s_idx:
+                        del eid_to_slot[old]
+                    prev = eid_to_slot.get(e)
+                    if prev is not None and prev != s_idx:
+                        slot_to_eid.pop(prev, None)
+                    slot_to_eid[s_idx] = e
+                    eid_to_slot[e] = s_idx
+                    load_e.append(e)
+                    load_s.append(s_idx)
+            if load_e:
+                self._load_sync(load_e, load_s)
+            pos = np.searchsorted(chunk, idx)
+            inside = (pos < len(chunk)) & (chunk[np.minimum(pos, len(chunk) - 1)] == idx)
+            sl = np.where(inside, pos, self.capacity).astype(np.int32)
+            sl_dev = torch.from_numpy(sl).to(self.device)
+            call("moe_prefill_experts_slots", x.data_ptr(), T, H, I, self.capacity, K, sl_dev.data_ptr(),
+                 g.w.data_ptr(), g.s.data_ptr(), g.b.data_ptr(), u.w.data_ptr(), u.s.data_ptr(), u.b.data_ptr(),
+                 d.w.data_ptr(), d.s.data_ptr(), d.b.data_ptr(), g.sb_fp16, yk.data_ptr(), ws.data_ptr(), ws.numel(),
+                 self._cs())
+        # rebuild the LRU: slots last.. in slot order, then the last chunk's slots (MRU end)
+        order = [s_ for s_ in range(last, self.capacity) if s_ in slot_to_eid] + \
+                [s_ for s_ in range(last) if s_ in slot_to_eid]
+        self.set_lru_state([slot_to_eid[s_] for s_ in order], order, add_req, add_hits, add_misses)
+        return yk.view(T, K, H)
+
     def close(self) -> None:
         self.wait_prefetch()
 
@@ -334,6 +413,30 @@ class OffloadStack:
             if nxt is not None:
                 self.layers[l + 1].start_prefetch(r["pred"].view(-1), self.prefetch_cap)
         return self.hs[self.L]
+
+    def prefill(self, h: torch.Tensor) -> torch.Tensor:
+        """The prompt's rows h [T, H] bf16 through every layer (the prefill of
+        OffloadEngine.generate_greedy, loader.py:1150-1156): layer 0 (pinned) with the resident
+        grouped GEMMs, layers 1.. through their caches' prefill (CachedSwitchGLU.prefill) and
+        the MLX-order combine with the residual. Returns the last layer's output [T, H]."""
+        x = h.contiguous()
+        T = x.shape[0]
+        for l in range(self.L):
+            xin = x
+            if self.norm:
+                xin = torch.empty_like(x)
+                call("moe_pow2_rows", x.data_ptr(), T, self.H, xin.data_ptr(), torch.cuda.current_stream(self.device).cuda_stream)
+            r = ops.router_topk(xin, self.routers[l], self.K)
+            if l == 0:
+                x = ops.prefill_experts(xin, r["inds"], r["scores"], self.layer0.gate, self.layer0.up,
+                                        self.layer0.down, resid=x)
+                continue
+            yk = self.layers[l].prefill(xin, r["inds"])
+            y = torch.empty_like(x)
+            call("moe_combine_rows", yk.data_ptr(), T, self.K, self.H, r["scores"].data_ptr(), x.data_ptr(),
+                 y.data_ptr(), torch.cuda.current_stream(self.device).cuda_stream)
+            x = y
+        return x
 
     def capture(self) -> None:
         """Records one decode_token as a CUDA graph over static input buffers (the token's
