@@ -12,7 +12,7 @@
 //            shared memory, builds their one record, and runs the down slice: a split-K
 //            partial of expert k's output over all H rows, written to global memory
 //                                                                     -> grid barrier
-//   phase B  each CTA owns 16-row blocks of h: sums the I/64 partials of every routed
+//   phase B  each CTA owns 8-row blocks of h: sums the I/64 partials of every routed
 //            expert for its rows (fixed order), rounds each expert output to bf16,
 //            combines with the routing scores and the residual into its rows of h_{l+1}
 //            (kept in shared memory across layers), and adds its rows' contribution to
@@ -36,7 +36,7 @@ namespace {
 constexpr int kThreads = 512;
 constexpr int kWarps = kThreads / 32;
 constexpr int kUnits = 8;                   // gate/up units (8 rows) per activation group
-constexpr int kMaxBlocks = 2;               // 16-row blocks of h per CTA in phase B
+constexpr int kMaxBlocks = 4;               // 8-row blocks of h per CTA in phase B
 constexpr int kMaxE = 2048;
 constexpr int kMaxK = 32;
 constexpr int kMaxH = 4096;
@@ -101,8 +101,8 @@ struct SmemLayout {
         ascale = arec + 128;                                      // scale, sum
         sact = ascale + 16;
         ypart = sact + 128;
-        hown = ypart + al16((size_t)K * kMaxBlocks * 16 * 4);
-        red = hown + al16((size_t)kMaxBlocks * 16 * 4);
+        hown = ypart + al16((size_t)K * kMaxBlocks * 8 * 4);
+        red = hown + al16((size_t)kMaxBlocks * 8 * 4);
         cand = red + (size_t)kUnits * 2 * 8 * 2 * 4;
         comp = cand + (size_t)kWarps * kMaxK * 4;
         redu = comp + (size_t)kWarps * kMaxK * 4;
@@ -307,12 +307,13 @@ __global__ void __launch_bounds__(kThreads, 1) stack_kernel(StackArgs a) {
     const int G = gridDim.x, c = blockIdx.x;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int g = lane >> 2, t = lane & 3;
-    const int ngH = H / 64, ngI = I / 64, NQ = K * ngI, NB = H / 16;
+    // NB: 8-row blocks of h (phase B); NT: 16-row MMA tiles of the down slice (phase A)
+    const int ngH = H / 64, ngI = I / 64, NQ = K * ngI, NB = H / 8, NT = H / 16;
     const int xst = rec_stride(ngH);
     const PackDims P(H, I);
     const SmemLayout S(H, I, K, a.region);
     const int b0 = (int)((long long)c * NB / G), nb = (int)((long long)(c + 1) * NB / G) - b0;
-    const int nrows = nb * 16;
+    const int nrows = nb * 8;
 
     uint64_t *ubar = reinterpret_cast<uint64_t *>(smem + S.bars);          // [kUnits]
     uint64_t *dbar = ubar + kUnits;                                         // [1]
@@ -342,21 +343,21 @@ __global__ void __launch_bounds__(kThreads, 1) stack_kernel(StackArgs a) {
 
     unsigned int nbar = 0;
     uint32_t rphase = 0, qphase = 0;
-    const uint32_t rsb = 16u * (uint32_t)E * 2u;   // router slice of one 16-row block
+    const uint32_t rsb = 8u * (uint32_t)E * 2u;    // router slice of one 8-row block
 
     // --------------------------------------------------------------- prologue: h_0 and layer-0 logits
     if (tid == 0 && nb > 0) {
         mbar_arrive_expect_tx(rbar, rsb * nb);
 #pragma unroll 1
         for (int bi = 0; bi < nb; ++bi)
-            tma_load_1d(region + (size_t)bi * rsb, a.layers[0].router_t + (size_t)(b0 + bi) * 16 * E, rsb, rbar);
+            tma_load_1d(region + (size_t)bi * rsb, a.layers[0].router_t + (size_t)(b0 + bi) * 8 * E, rsb, rbar);
     }
     double ssp = 0.0;
 #pragma unroll 1
     for (int r = tid; r < nrows; r += kThreads) {
-        const uint16_t v = a.x_in[b0 * 16 + r];
-        a.hbuf[b0 * 16 + r] = v;
-        if (a.hs_out) a.hs_out[b0 * 16 + r] = v;
+        const uint16_t v = a.x_in[b0 * 8 + r];
+        a.hbuf[b0 * 8 + r] = v;
+        if (a.hs_out) a.hs_out[b0 * 8 + r] = v;
         hown[r] = bf16_bits_to_f32(v);
         ssp = fma((double)hown[r], (double)hown[r], ssp);
     }
@@ -477,7 +478,7 @@ __global__ void __launch_bounds__(kThreads, 1) stack_kernel(StackArgs a) {
                 const float asc = ascale[0], asm_ = ascale[1];
                 float *ypq = a.yp + (size_t)q * H;
 #pragma unroll 2
-                for (int tile = warp; tile < NB; tile += kWarps) {
+                for (int tile = warp; tile < NT; tile += kWarps) {
                     const uint32_t wa = dc[tile * 64 + lane], wb = dc[tile * 64 + 32 + lane];
                     int dx[4] = {0, 0, 0, 0}, dy[4] = {0, 0, 0, 0};
                     mma_u8s8_16832(dx, wa & 0x03030303u, wb & 0x03030303u, (wa >> 2) & 0x03030303u,
@@ -506,7 +507,7 @@ __global__ void __launch_bounds__(kThreads, 1) stack_kernel(StackArgs a) {
             mbar_arrive_expect_tx(rbar, rsb * nb);
 #pragma unroll 1
             for (int bi = 0; bi < nb; ++bi)
-                tma_load_1d(region + (size_t)bi * rsb, a.layers[l + 1].router_t + (size_t)(b0 + bi) * 16 * E, rsb,
+                tma_load_1d(region + (size_t)bi * rsb, a.layers[l + 1].router_t + (size_t)(b0 + bi) * 8 * E, rsb,
                             rbar);
         }
         grid_sync(a.bar, nbar++);
@@ -517,7 +518,7 @@ __global__ void __launch_bounds__(kThreads, 1) stack_kernel(StackArgs a) {
 #pragma unroll 1
         for (int x = tid; x < K * nrows; x += kThreads) {
             const int k = x / nrows, r = x % nrows;
-            const float *src = a.yp + (size_t)k * ngI * H + b0 * 16 + r;
+            const float *src = a.yp + (size_t)k * ngI * H + b0 * 8 + r;
             float v[4];
             float yk = 0.f;
 #pragma unroll 1
@@ -533,7 +534,7 @@ __global__ void __launch_bounds__(kThreads, 1) stack_kernel(StackArgs a) {
         double ssn = 0.0;
 #pragma unroll 1
         for (int r = tid; r < nrows; r += kThreads) {
-            const int row = b0 * 16 + r;
+            const int row = b0 * 8 + r;
             float accv = 0.f;
 #pragma unroll 4
             for (int k = 0; k < K; ++k) {
@@ -612,10 +613,10 @@ extern "C" int moe_stack_decode(const void *layers, int L, int H, int I, int E, 
     MOE_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
     const int G = num_ctas > 0 ? num_ctas : sms;
     if (G > sms) return moe_set_error(MOE_EINVAL, "stack_decode: %d CTAs > %d SMs", G, sms);
-    if ((H / 16 + G - 1) / G > kMaxBlocks)
-        return moe_set_error(MOE_EINVAL, "stack_decode: %d CTAs too few for %d row blocks", G, H / 16);
+    if ((H / 8 + G - 1) / G > kMaxBlocks)
+        return moe_set_error(MOE_EINVAL, "stack_decode: %d CTAs too few for %d row blocks", G, H / 8);
     const PackDims P(H, I);
-    const size_t region = std::max((size_t)P.gbytes, (size_t)kMaxBlocks * 16 * E * 2);
+    const size_t region = std::max((size_t)P.gbytes, (size_t)kMaxBlocks * 8 * E * 2);
     const SmemLayout S(H, I, K, region);
     if (S.total > 227 * 1024)
         return moe_set_error(MOE_EINVAL, "stack_decode: %zu bytes of shared memory needed", S.total);
