@@ -89,7 +89,7 @@ MOE_HD int rec_stride(int ngroups) { return (ngroups + 15) / 16 * 16 + 4; }
 
 struct SmemLayout {
     size_t bars, region, xrec, xscale, xsum, arec, ascale, sact, ypart, hown, red, cand, comp, redu, redd, sinds,
-        sscores, total;
+        sscores, dtr, total;
     MOE_HD SmemLayout(int H, int I, int K, size_t region_bytes) {
         const int ngH = H / 64, ngI = I / 64;
         bars = 0;                                                 // 16 mbarriers
@@ -109,7 +109,8 @@ struct SmemLayout {
         redd = redu + kWarps * 4;
         sinds = redd + kWarps * 8;
         sscores = sinds + kMaxK * 4;
-        total = sscores + kMaxK * 4;
+        dtr = al16(sscores + kMaxK * 4);                          // [kWarps][64] int dot products
+        total = dtr + (size_t)kWarps * 64 * 4;
     }
 };
 
@@ -264,7 +265,9 @@ MOE_D void route(const double (&av)[kKeysT], double xmul, int E, int K, uint32_t
 
 // This CTA's rows' contribution to the next layer's router logits: waits for the router
 // slices, then every thread adds sum_r router_t[row r][e] * h[row r] (exact fp32 products of
-// bf16 values, double sums) into acc[e] with one fp64 atomic per expert.
+// bf16 values, double sums) into acc[e] with one fp64 atomic per expert. The loop is bound by
+// instruction issue and the f32 -> f64 conversions: the eight shared loads of a row group go
+// out before any arithmetic (twice as fast as a load-convert-add chain per row).
 MOE_D void router_partial(uint64_t *rbar, uint32_t &rphase, const unsigned char *rbuf, const float *hown, int nrows,
                           int E, double *acc) {
     const bool ok = mbar_wait(rbar, rphase);
@@ -274,12 +277,17 @@ MOE_D void router_partial(uint64_t *rbar, uint32_t &rphase, const unsigned char 
 #pragma unroll 1
     for (int e = threadIdx.x; e < E; e += kThreads) {
         double p[4] = {0.0, 0.0, 0.0, 0.0};
+        int r0 = 0;
 #pragma unroll 1
-        for (int r0 = 0; r0 < nrows; r0 += 4) {
+        for (; r0 + 8 <= nrows; r0 += 8) {
+            uint32_t w[8];
 #pragma unroll
-            for (int i = 0; i < 4; ++i)
-                if (r0 + i < nrows) p[i] += (double)(bf16_bits_to_f32(rs[(size_t)(r0 + i) * E + e]) * hown[r0 + i]);
+            for (int i = 0; i < 8; ++i) w[i] = rs[(r0 + i) * E + e];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) p[i & 3] += (double)(bf16_bits_to_f32((uint16_t)w[i]) * hown[r0 + i]);
         }
+#pragma unroll 1
+        for (; r0 < nrows; ++r0) p[0] += (double)(bf16_bits_to_f32(rs[r0 * E + e]) * hown[r0]);
         atomicAdd(acc + e, (p[0] + p[1]) + (p[2] + p[3]));
     }
 }
@@ -334,6 +342,7 @@ __global__ void __launch_bounds__(kThreads, 1) stack_kernel(StackArgs a) {
     double *redd = reinterpret_cast<double *>(smem + S.redd);
     uint32_t *sinds = reinterpret_cast<uint32_t *>(smem + S.sinds);
     float *sscores = reinterpret_cast<float *>(smem + S.sscores);
+    int *dtr = reinterpret_cast<int *>(smem + S.dtr);
 
     if (tid == 0) {
         for (int i = 0; i < kUnits + 2; ++i) mbar_init(&ubar[i], 1);
@@ -467,7 +476,9 @@ __global__ void __launch_bounds__(kThreads, 1) stack_kernel(StackArgs a) {
             // down slice: split-K partial of expert k's output over all H rows. One MMA pair per
             // 16 rows: lane (g, t) feeds word t of rows g and g+8; B columns 0 / 1 carry the
             // record's hi / lo parts (lanes 0..7), so D columns 0 / 1 of lane quad t = 0 hold
-            // the row's integer dot.
+            // the row's integer dot. A warp runs the MMAs of up to four of its tiles, parks the
+            // 64 dots in its transpose buffer, and then every lane finishes two adjacent rows
+            // (one 8-byte scale load, one 8-byte store) instead of 8 lanes per tile.
             {
                 const bool wok = mbar_wait(dbar, qphase);
                 const uint32_t *dc = reinterpret_cast<const uint32_t *>(region + P.dco);
@@ -477,25 +488,42 @@ __global__ void __launch_bounds__(kThreads, 1) stack_kernel(StackArgs a) {
                 const uint2 by = (lane < 8) ? arec[(1 * 4 + t) * 2 + n] : make_uint2(0u, 0u);
                 const float asc = ascale[0], asm_ = ascale[1];
                 float *ypq = a.yp + (size_t)q * H;
-#pragma unroll 2
-                for (int tile = warp; tile < NT; tile += kWarps) {
-                    const uint32_t wa = dc[tile * 64 + lane], wb = dc[tile * 64 + 32 + lane];
-                    int dx[4] = {0, 0, 0, 0}, dy[4] = {0, 0, 0, 0};
-                    mma_u8s8_16832(dx, wa & 0x03030303u, wb & 0x03030303u, (wa >> 2) & 0x03030303u,
-                                   (wb >> 2) & 0x03030303u, bx.x, bx.y);
-                    mma_u8s8_16832(dy, wa & 0x30303030u, wb & 0x30303030u, (wa >> 2) & 0x30303030u,
-                                   (wb >> 2) & 0x30303030u, by.x, by.y);
-                    if (t == 0) {
-                        const int da = (dx[0] + (dy[0] >> 4)) * 128 + (dx[1] + (dy[1] >> 4));
-                        const int db = (dx[2] + (dy[2] >> 4)) * 128 + (dx[3] + (dy[3] >> 4));
-                        const uint32_t sa = ds[tile * 16 + g], sbb = ds[tile * 16 + 8 + g];
-                        const float ya = sb_to_f32<kFp16>((uint16_t)sa) * ((float)da * asc) +
-                                         sb_to_f32<kFp16>((uint16_t)(sa >> 16)) * asm_;
-                        const float yb = sb_to_f32<kFp16>((uint16_t)sbb) * ((float)db * asc) +
-                                         sb_to_f32<kFp16>((uint16_t)(sbb >> 16)) * asm_;
-                        ypq[tile * 16 + g] = wok ? ya : 0.f;
-                        ypq[tile * 16 + 8 + g] = wok ? yb : 0.f;
+                int *yb = dtr + warp * 64;
+                const int ntw = NT / kWarps;               // tiles per warp (H is a multiple of 256)
+#pragma unroll 1
+                for (int j0 = 0; j0 < ntw; j0 += 4) {
+                    const int jn = min(4, ntw - j0);
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        if (j < jn) {                      // warp-uniform
+                            const int tile = warp + (j0 + j) * kWarps;
+                            const uint32_t wa = dc[tile * 64 + lane], wb = dc[tile * 64 + 32 + lane];
+                            int dx[4] = {0, 0, 0, 0}, dy[4] = {0, 0, 0, 0};
+                            mma_u8s8_16832(dx, wa & 0x03030303u, wb & 0x03030303u, (wa >> 2) & 0x03030303u,
+                                           (wb >> 2) & 0x03030303u, bx.x, bx.y);
+                            mma_u8s8_16832(dy, wa & 0x30303030u, wb & 0x30303030u, (wa >> 2) & 0x30303030u,
+                                           (wb >> 2) & 0x30303030u, by.x, by.y);
+                            if (t == 0) {
+                                yb[j * 16 + g] = (dx[0] + (dy[0] >> 4)) * 128 + (dx[1] + (dy[1] >> 4));
+                                yb[j * 16 + 8 + g] = (dx[2] + (dy[2] >> 4)) * 128 + (dx[3] + (dy[3] >> 4));
+                            }
+                        }
                     }
+                    __syncwarp();
+                    const int j = lane >> 3, rr = 2 * (lane & 7);
+                    if (j < jn) {
+                        const int row = (warp + (j0 + j) * kWarps) * 16 + rr;
+                        const int2 dd = *reinterpret_cast<const int2 *>(yb + j * 16 + rr);
+                        const uint2 sp = *reinterpret_cast<const uint2 *>(ds + row);
+                        float2 o;
+                        o.x = sb_to_f32<kFp16>((uint16_t)sp.x) * ((float)dd.x * asc) +
+                              sb_to_f32<kFp16>((uint16_t)(sp.x >> 16)) * asm_;
+                        o.y = sb_to_f32<kFp16>((uint16_t)sp.y) * ((float)dd.y * asc) +
+                              sb_to_f32<kFp16>((uint16_t)(sp.y >> 16)) * asm_;
+                        if (!wok) o = make_float2(0.f, 0.f);
+                        *reinterpret_cast<float2 *>(ypq + row) = o;
+                    }
+                    __syncwarp();
                 }
             }
             __syncthreads();
@@ -519,14 +547,15 @@ __global__ void __launch_bounds__(kThreads, 1) stack_kernel(StackArgs a) {
         for (int x = tid; x < K * nrows; x += kThreads) {
             const int k = x / nrows, r = x % nrows;
             const float *src = a.yp + (size_t)k * ngI * H + b0 * 8 + r;
-            float v[4];
+            float v[16];                           // all partial loads of a row in flight at once
             float yk = 0.f;
 #pragma unroll 1
-            for (int g0 = 0; g0 < ngI; g0 += 4) {
+            for (int g0 = 0; g0 < ngI; g0 += 16) {
 #pragma unroll
-                for (int i = 0; i < 4; ++i) v[i] = (g0 + i < ngI) ? __ldcg(src + (size_t)(g0 + i) * H) : 0.f;
+                for (int i = 0; i < 16; ++i) v[i] = (g0 + i < ngI) ? __ldcg(src + (size_t)(g0 + i) * H) : 0.f;
 #pragma unroll
-                for (int i = 0; i < 4; ++i) yk += v[i];
+                for (int i = 0; i < 16; ++i)
+                    if (g0 + i < ngI) yk += v[i];
             }
             ypart[k * nrows + r] = bf16r(yk);
         }
