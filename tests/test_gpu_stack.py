@@ -32,8 +32,9 @@ def _dev_layers(np_layers, dev):
                         to_device_qmatrix(ly["u"], dev), to_device_qmatrix(ly["d"], dev)) for ly in np_layers]
 
 
+# ctas = 0: all SMs (CTAs without a work item exist); (2, 512, 256, 32, 4, 16): one item per CTA
 @pytest.mark.parametrize("L,H,I,E,K,ctas", [(3, 3072, 768, 64, 10, 0), (6, 2048, 768, 64, 8, 0),
-                                           (2, 1024, 256, 32, 4, 40)])
+                                           (2, 1024, 256, 32, 4, 40), (2, 512, 256, 32, 4, 16)])
 def test_persistent_stack_vs_oracle(dev, L, H, I, E, K, ctas):
     from moe_offload_b200.ops import pow2_normalize
     from moe_offload_b200.stack import PersistentStack
