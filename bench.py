@@ -6,9 +6,11 @@
 A step is one decode token through all 28 layers (router -> 2-bit gate/up + SwiGLU -> 2-bit
 down + combine, h_{l+1} = h_l + MoE_l(h_l)) with a fresh N(0,1) hidden state per step
 (seed 1), expert weights random-init with the BASELINE distributions (synthetic: the
-reference's checkpoints are not available). For N > 1 (torchrun) every rank runs an
-independent replica of the stack (the batch-1 resident decode path does not shard; expert
-parallelism is a different configuration), so per-GPU work is fixed: weak scaling.
+reference's checkpoints are not available). For N > 1 (torchrun) every rank decodes its own
+token stream through its own replica of the stack (31.7 GB of experts fits one B200 many
+times over, so independent requests are the throughput-optimal way to use N GPUs; no
+collective on the data path), so per-GPU work is fixed: weak scaling. Expert parallelism
+(experts split across the ranks, outputs exchanged over NVLink every layer) is `--config c4`.
 
 The step is ONE launch of the persistent kernel (moe_stack_decode: all 28 layers inside,
 experts in the packed layout). Prints one JSON line (rank 0). `value` is whole-job tokens/s
@@ -47,7 +49,7 @@ def parse():
                     help="c1: resident stack (the headline); c2: offload stack with the LRU slot caches; "
                          "c3: 2048-token prefill through the resident 28-layer stack; c3n: the Nemotron-shaped "
                          "prefill layer (240 experts, top-9, 1024 tokens); c4: expert-parallel decode (experts "
-                         "split across the ranks; the default for N > 1)")
+                         "split across the ranks)")
     ap.add_argument("--batch", type=int, default=0, help="c4: tokens per decode step (default: one per GPU)")
     ap.add_argument("--layers", type=int, default=0,
                     help="profiling aid: run only the first N layers of the stack (0 = all 28)")
@@ -645,8 +647,6 @@ def main() -> int:
         torch.cuda.set_device(local_rank)
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
                                 device_id=torch.device("cuda", local_rank))
-    if world > 1 and args.config == "c1":
-        args.config = "c4"          # the resident stack at N > 1 runs expert-parallel
     try:
         if args.impl == "reference":
             run_reference(args, rank, world)
