@@ -415,6 +415,62 @@ void c_layer_get_stats(int layer_idx, uint64_t *out_stats);
 void c_get_decode_totals(int num_layers, uint64_t *out6);
 
 /*
+ * P1 I/O scheduler (replaces qwen38::P1IoScheduler, mlx-qwen38/cpp/src/io_sched.h:46-245;
+ * semantics of mlx-qwen38/cpp/src/io_sched.cpp, tested by mlx-qwen38/cpp/tests/test_io_sched.cpp):
+ * URGENT / PREFETCH copy queues drained by worker threads and by waiting callers, prefetch
+ * cancel / promote, per-slot pins with a reader-wait callback, LRU slot cache per layer
+ * (layers 0..63, experts 0..511, up to 9 tensors per expert). Each method of the reference
+ * class is one function taking the handle; void methods return 0 (or a negative status for a
+ * null handle / pointer). Rows come from a file (fd, byte offsets: moe_p1_layer_init, the
+ * reference's form, host slot buffers) or from a host pool (addresses of expert 0 of every
+ * tensor: moe_p1_layer_init_pool) into host or device slot buffers (device copies run on a
+ * non-blocking stream of the executing thread).
+ */
+#define MOE_P1_STATS 16
+/* stats order: decode_requests, lru_hits, urgent_reads, prefetch_issued, prefetch_cancelled,
+ * prefetch_promoted, prefetch_used, prefetch_wasted, pin_waits, bytes, io_wait_ns,
+ * forced_invalidations, prefill_requests, prefill_lru_hits, prefill_demand_misses,
+ * prefill_demand_bytes (the fields of qwen38::P1LayerStats) */
+void *moe_p1_create(void);
+void moe_p1_destroy(void *h);
+int moe_p1_init(void *h, int num_threads);                     /* P1IoScheduler::init */
+int moe_p1_shutdown(void *h);                                  /* ::shutdown */
+int moe_p1_num_threads(void *h);
+/* ::set_wait_reader_callback: fn(user, layer) is called, without the scheduler lock, when a
+ * slot allocation finds only slots pinned by a GPU reader; it should wait for that reader and
+ * unpin (moe_p1_unpin_layer_slots) */
+int moe_p1_set_wait_reader_callback(void *h, void (*fn)(void *user, int layer), void *user);
+int moe_p1_layer_init(void *h, int layer, int fd, int capacity, int num_tensors, const uint64_t *base_offsets,
+                      const uint64_t *row_bytes, const uint64_t *base_ptrs, uint64_t slot_inds_ptr);
+int moe_p1_layer_init_pool(void *h, int layer, int capacity, int num_tensors, const uint64_t *src_ptrs,
+                           const uint64_t *row_bytes, const uint64_t *slot_ptrs, uint64_t slot_inds_ptr,
+                           int slots_on_device, int device);
+int moe_p1_resize_layer(void *h, int layer, int new_capacity, const uint64_t *new_base_ptrs, uint64_t slot_inds_ptr,
+                        const int32_t *ordered_eids, const int32_t *ordered_slots, int count);
+int moe_p1_reset_cache(void *h, int layer);
+int moe_p1_reset_stats(void *h, int layer);
+int moe_p1_start_prefetch(void *h, int layer, const int32_t *pred_eids, int pred_count, int max_fetch);
+/* returns the number of the k slots still loading (wait with moe_p1_wait_layer_urgent) */
+int moe_p1_step_decode(void *h, int layer, const uint32_t *eids, int k, uint32_t *out_slots);
+int moe_p1_wait_layer_urgent(void *h, int layer);
+int moe_p1_wait_layer_all(void *h, int layer);
+int moe_p1_wait_all(void *h);
+int moe_p1_unpin_layer_slots(void *h, int layer);
+int moe_p1_pin_slots(void *h, int layer, const uint32_t *slots, int count);
+int moe_p1_unpin_slots(void *h, int layer, const uint32_t *slots, int count);
+int moe_p1_get_slot_pin_count(void *h, int layer, int slot);
+/* ::force_invalidate with the handle's std::mt19937_64 (seeded by moe_p1_seed); returns the count */
+int moe_p1_seed(void *h, uint64_t seed);
+int moe_p1_force_invalidate(void *h, int layer, double rate);
+int moe_p1_load_sync(void *h, int layer, const int32_t *eids, const int32_t *slots, int count, int is_prefill);
+int moe_p1_get_lru_state(void *h, int layer, int32_t *out_eids, int32_t *out_slots, int *out_count);
+int moe_p1_set_lru_state(void *h, int layer, const int32_t *ordered_eids, const int32_t *ordered_slots, int count,
+                         uint64_t add_prefill_requests, uint64_t add_prefill_hits, uint64_t add_prefill_misses);
+int moe_p1_get_layer_stats(void *h, int layer, uint64_t *out_stats);
+int moe_p1_get_total_stats(void *h, int num_layers, uint64_t *out_stats);
+uint64_t moe_p1_copy_errors(void *h);                          /* failed device copies so far */
+
+/*
  * Device-side error word (bit 1: a bounded mbarrier/flag wait gave up, bit 2: invalid
  * input seen by a kernel, bit 4: an expert-parallel peer did not signal within 2 s). Returns the current value (>= 0) and clears it when `clear`.
  * Kernels never trap: they record the condition here and skip the affected work.

@@ -95,6 +95,42 @@ SIGNATURES: dict[str, tuple] = {
 }
 
 
+# the P1 I/O scheduler (moe_p1_<method>): method -> (restype, argtypes); io_sched.P1IoScheduler
+# binds the same table to any library exporting these functions under a prefix
+P1_READER_FN = ctypes.CFUNCTYPE(None, ctypes.c_void_p, ctypes.c_int)
+P1_SIGNATURES: dict[str, tuple] = {
+    "create": (P, []),
+    "destroy": (None, [P]),
+    "init": (I, [P, I]),
+    "shutdown": (I, [P]),
+    "num_threads": (I, [P]),
+    "set_wait_reader_callback": (I, [P, P1_READER_FN, P]),
+    "layer_init": (I, [P, I, I, I, I, P, P, P, U64]),
+    "layer_init_pool": (I, [P, I, I, I, P, P, P, U64, I, I]),
+    "resize_layer": (I, [P, I, I, P, U64, P, P, I]),
+    "reset_cache": (I, [P, I]),
+    "reset_stats": (I, [P, I]),
+    "start_prefetch": (I, [P, I, P, I, I]),
+    "step_decode": (I, [P, I, P, I, P]),
+    "wait_layer_urgent": (I, [P, I]),
+    "wait_layer_all": (I, [P, I]),
+    "wait_all": (I, [P]),
+    "unpin_layer_slots": (I, [P, I]),
+    "pin_slots": (I, [P, I, P, I]),
+    "unpin_slots": (I, [P, I, P, I]),
+    "get_slot_pin_count": (I, [P, I, I]),
+    "seed": (I, [P, U64]),
+    "force_invalidate": (I, [P, I, ctypes.c_double]),
+    "load_sync": (I, [P, I, P, P, I, I]),
+    "get_lru_state": (I, [P, I, P, P, P]),
+    "set_lru_state": (I, [P, I, P, P, I, U64, U64, U64]),
+    "get_layer_stats": (I, [P, I, P]),
+    "get_total_stats": (I, [P, I, P]),
+    "copy_errors": (U64, [P]),
+}
+SIGNATURES.update({"moe_p1_" + k: v for k, v in P1_SIGNATURES.items()})
+
+
 def load() -> ctypes.CDLL:
     global _lib
     if _lib is not None:
