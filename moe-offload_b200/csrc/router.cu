@@ -302,91 +302,114 @@ __global__ void __launch_bounds__(kThreads) router_kernel(RouterArgs a) {
 // ---------------------------------------------------------------- batched path (T >= 1024)
 //
 // For many tokens the router is a GEMM: logits[T][E] = x . W^T. Tiles of 64 tokens x 128
-// rows per CTA, every thread a 4 x 8 micro-tile of double accumulators; the operands are
-// converted exactly to double once when staged in shared memory, so each term is an exact
-// product and the sum is a double sum (the same arithmetic as the per-token kernel, in
-// another order: the bf16 rounding of the result differs only for a value within ~2^-45 of
-// a rounding midpoint). Then one block per token runs router_tail.
+// rows per CTA on the fp64 tensor cores (mma.sync m8n8k4 .f64); the operands are converted
+// exactly to double once when staged in shared memory, so each term is an exact product and
+// the sum is a double sum (the same arithmetic as the per-token kernel, in another order:
+// the bf16 rounding of the result differs only for a value within ~2^-45 of a rounding
+// midpoint). Then one block per token runs router_tail.
 constexpr int kGT = 64, kGE = 128, kGK = 32;      // tokens, rows, K per stage
 constexpr int kGemmMinT = 1024;                    // batches from this size use the GEMM
 constexpr size_t kGemmSmem = (size_t)kGK * (kGT + kGE) * sizeof(double);
 
+// fp64 tensor-core MMA: D(8x8) += A(8x4, row) * B(4x8, col); lane (g = lane >> 2, q = lane & 3)
+// holds A[g][q], B[q][g] and D[g][2q], D[g][2q+1]
+__device__ __forceinline__ void dmma_884(double &d0, double &d1, double a, double b) {
+    asm volatile("mma.sync.aligned.m8n8k4.row.col.f64.f64.f64.f64 {%0,%1}, {%2}, {%3}, {%0,%1};"
+                 : "+d"(d0), "+d"(d1)
+                 : "d"(a), "d"(b));
+}
+
+// Tile: 64 tokens x 128 router rows per CTA, K in stages of 32. Operands are converted exactly
+// to double when staged, as [k-block of 4][token or row][4] so that every fragment load of a
+// warp touches each bank pair exactly twice (conflict-free). Warp w computes tokens
+// (w & 1) * 32 .. +32 and rows (w >> 1) * 32 .. +32 as 4 x 4 tiles of fp64 MMAs: exact
+// products of bf16 values summed in double, as in the per-token kernel.
 __global__ void __launch_bounds__(256) router_gemm_kernel(RouterArgs a) {
     extern __shared__ double gsm[];
-    double *xs = gsm;                  // [kGK][kGT]
-    double *ws = gsm + kGK * kGT;      // [kGK][kGE]
-    const int tid = threadIdx.x;
+    double *xs = gsm;                  // [kGK / 4][kGT][4]
+    double *ws = gsm + kGK * kGT;      // [kGK / 4][kGE][4]
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int g = lane >> 2, q = lane & 3;
     const int t0 = blockIdx.y * kGT, r0 = blockIdx.x * kGE;
+    const int wt0 = (warp & 1) * 32, wr0 = (warp >> 1) * 32;
     const int rows = a.E * (a.M > 0 ? 2 : 1);
-    const int tt = tid & 15, te = tid >> 4;         // tokens tt*4 .. +3, rows te*8 .. +7
     const uint16_t *w = static_cast<const uint16_t *>(a.w);
     const uint16_t *wn = static_cast<const uint16_t *>(a.wn);
     pdl_wait();
     pdl_launch_dependents();
-    double acc[4][8];
+    double acc[4][4][2];
 #pragma unroll
     for (int i = 0; i < 4; ++i)
 #pragma unroll
-        for (int j = 0; j < 8; ++j) acc[i][j] = 0.0;
-    for (int k0 = 0; k0 < a.H; k0 += kGK) {
-        // x tile: 64 tokens x 32 values (8 per thread), w tile: 128 rows x 32 values (16 per thread)
-        {
-            const int tok = tid >> 2, c = (tid & 3) * 8;
-            const int gt = t0 + tok;
-            uint4 v = make_uint4(0u, 0u, 0u, 0u);
-            if (gt < a.T && k0 + c < a.H) v = *reinterpret_cast<const uint4 *>(a.x + (size_t)gt * a.H + k0 + c);
-            const uint32_t vv[4] = {v.x, v.y, v.z, v.w};
+        for (int j = 0; j < 4; ++j) acc[i][j][0] = acc[i][j][1] = 0.0;
+    // global -> registers for stage k0 (x: 8 values of one token, w: 8 values of two rows per
+    // thread), issued one stage ahead so the loads overlap the previous stage's MMAs
+    const int ltok = tid >> 2, lrow = tid >> 2, lc = (tid & 3) * 8;
+    auto load_stage = [&](int k0, uint4 &vx, uint4 (&vw)[2]) {
+        const int gt = t0 + ltok;
+        vx = make_uint4(0u, 0u, 0u, 0u);
+        if (gt < a.T && k0 + lc < a.H) vx = *reinterpret_cast<const uint4 *>(a.x + (size_t)gt * a.H + k0 + lc);
 #pragma unroll
-            for (int q = 0; q < 4; ++q) {
-                xs[(c + 2 * q) * kGT + tok] = (double)__uint_as_float(vv[q] << 16);
-                xs[(c + 2 * q + 1) * kGT + tok] = (double)__uint_as_float(vv[q] & 0xffff0000u);
+        for (int hh = 0; hh < 2; ++hh) {
+            const int gr = r0 + lrow + 64 * hh;
+            vw[hh] = make_uint4(0u, 0u, 0u, 0u);
+            if (gr < rows && k0 + lc < a.H) {
+                const uint16_t *src = (gr < a.E) ? w + (size_t)gr * a.H : wn + (size_t)(gr - a.E) * a.H;
+                vw[hh] = *reinterpret_cast<const uint4 *>(src + k0 + lc);
             }
         }
+    };
+    // 8 bf16 values (k = lc .. lc + 7) -> two [4] groups of doubles at k-blocks lc/4, lc/4 + 1
+    auto stage_vals = [&](double *base, int nrow, int row, const uint4 &v) {
+        const uint32_t vv[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
-            const int rr = (tid >> 2) + 64 * h, c = (tid & 3) * 8;
-            const int gr = r0 + rr;
-            uint4 v = make_uint4(0u, 0u, 0u, 0u);
-            if (gr < rows && k0 + c < a.H) {
-                const uint16_t *src = (gr < a.E) ? w + (size_t)gr * a.H : wn + (size_t)(gr - a.E) * a.H;
-                v = *reinterpret_cast<const uint4 *>(src + k0 + c);
-            }
-            const uint32_t vv[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-            for (int q = 0; q < 4; ++q) {
-                ws[(c + 2 * q) * kGE + rr] = (double)__uint_as_float(vv[q] << 16);
-                ws[(c + 2 * q + 1) * kGE + rr] = (double)__uint_as_float(vv[q] & 0xffff0000u);
-            }
+            double *d = base + ((size_t)((lc >> 2) + h) * nrow + row) * 4;
+            d[0] = (double)__uint_as_float(vv[2 * h] << 16);
+            d[1] = (double)__uint_as_float(vv[2 * h] & 0xffff0000u);
+            d[2] = (double)__uint_as_float(vv[2 * h + 1] << 16);
+            d[3] = (double)__uint_as_float(vv[2 * h + 1] & 0xffff0000u);
         }
+    };
+    uint4 nx, nw[2];
+    load_stage(0, nx, nw);
+    for (int k0 = 0; k0 < a.H; k0 += kGK) {
+        stage_vals(xs, kGT, ltok, nx);
+        stage_vals(ws, kGE, lrow, nw[0]);
+        stage_vals(ws, kGE, lrow + 64, nw[1]);
+        if (k0 + kGK < a.H) load_stage(k0 + kGK, nx, nw);
         __syncthreads();
-#pragma unroll 4
-        for (int k = 0; k < kGK; ++k) {
-            double xa[4], wb[8];
+#pragma unroll 2
+        for (int kb = 0; kb < kGK / 4; ++kb) {
+            double af[4], bfr[4];
 #pragma unroll
-            for (int i = 0; i < 4; ++i) xa[i] = xs[k * kGT + tt * 4 + i];
+            for (int i = 0; i < 4; ++i) af[i] = xs[((size_t)kb * kGT + wt0 + i * 8 + g) * 4 + q];
 #pragma unroll
-            for (int j = 0; j < 8; ++j) wb[j] = ws[k * kGE + te * 8 + j];
+            for (int j = 0; j < 4; ++j) bfr[j] = ws[((size_t)kb * kGE + wr0 + j * 8 + g) * 4 + q];
 #pragma unroll
             for (int i = 0; i < 4; ++i)
 #pragma unroll
-                for (int j = 0; j < 8; ++j) acc[i][j] = fma(xa[i], wb[j], acc[i][j]);
+                for (int j = 0; j < 4; ++j) dmma_884(acc[i][j][0], acc[i][j][1], af[i], bfr[j]);
         }
         __syncthreads();
     }
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
-        const int gt = t0 + tt * 4 + i;
+        const int gt = t0 + wt0 + i * 8 + g;
         if (gt >= a.T) continue;
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-            const int gr = r0 + te * 8 + j;
-            if (gr >= rows) continue;
-            uint16_t l = f64_to_bf16_bits(acc[i][j]);
-            if (gr >= a.E) {
-                if (a.pred_bias) l = f32_to_bf16_bits(bf16_bits_to_f32(l) + a.pred_bias[gr - a.E]);
-                a.plogits[(size_t)gt * a.E + gr - a.E] = l;
-            } else {
-                a.logits[(size_t)gt * a.E + gr] = l;
+        for (int j = 0; j < 4; ++j) {
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                const int gr = r0 + wr0 + j * 8 + 2 * q + h;
+                if (gr >= rows) continue;
+                uint16_t l = f64_to_bf16_bits(acc[i][j][h]);
+                if (gr >= a.E) {
+                    if (a.pred_bias) l = f32_to_bf16_bits(bf16_bits_to_f32(l) + a.pred_bias[gr - a.E]);
+                    a.plogits[(size_t)gt * a.E + gr - a.E] = l;
+                } else {
+                    a.logits[(size_t)gt * a.E + gr] = l;
+                }
             }
         }
     }
