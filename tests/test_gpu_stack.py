@@ -65,6 +65,27 @@ def test_persistent_stack_vs_oracle(dev, L, H, I, E, K, ctas):
     assert int(__import__("moe_offload_b200")._lib.call("moe_device_error", 1)) == 0
 
 
+def test_persistent_stack_results_independent_of_cta_count(dev):
+    """All SMs (CTAs without a work item, other phase-B row blocks and logit-replica spread) vs
+    exactly one CTA per item: every layer's routing, scores and output bits agree."""
+    from moe_offload_b200.stack import PersistentStack
+    from moe_offload_b200.synthetic import np_bf16_normal, np_to_bf16_tensor
+    rng = np.random.default_rng(33)
+    L, H, I, E, K = 6, 2048, 768, 64, 8
+    layers = _dev_layers(_np_layers(rng, L, E, H, I), dev)
+    a = PersistentStack(layers, K, dev, keep_layer_inputs=True)
+    b = PersistentStack(layers, K, dev, num_ctas=K * I // 64, keep_layer_inputs=True)
+    for _ in range(4):
+        x = np_to_bf16_tensor(np_bf16_normal(rng, (1, H)), dev)
+        a.step_device(x)
+        b.step_device(x)
+        torch.cuda.synchronize()
+        assert torch.equal(a.inds, b.inds)
+        assert torch.equal(a.scores, b.scores)
+        assert torch.equal(a.hs, b.hs)
+    assert int(__import__("moe_offload_b200")._lib.call("moe_device_error", 1)) == 0
+
+
 def test_persistent_stack_matches_layer_path(dev):
     """Same weights and input through the per-layer kernels: indices identical, outputs close."""
     from moe_offload_b200.stack import DecodeStack, PersistentStack
