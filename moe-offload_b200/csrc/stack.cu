@@ -165,13 +165,28 @@ MOE_D uint32_t f2ord(float f) {
 }
 MOE_D float ord2f(uint32_t o) { return __uint_as_float((o & 0x80000000u) ? (o & 0x7fffffffu) : ~o); }
 
+// warp 0, lane k holding the MLX-position-k selection (bf16 probability << 16 | expert):
+// sequential bf16 sum of the K probabilities in MLX order, then bf16(p / S) per expert
+MOE_D void renorm_mlx(uint32_t sel, int K, uint32_t *comp, uint32_t *sinds, float *sscores) {
+    const int lane = threadIdx.x & 31;
+    if (lane < K) comp[lane] = sel;
+    __syncwarp();
+    float S = bf16_bits_to_f32((uint16_t)(comp[0] >> 16));
+#pragma unroll 4
+    for (int k = 1; k < K; ++k) S = bf16r(S + bf16_bits_to_f32((uint16_t)(comp[k] >> 16)));
+    if (lane < K) {
+        sinds[lane] = sel & 0xffffu;
+        sscores[lane] = bf16r(__fdiv_rn(bf16_bits_to_f32((uint16_t)(sel >> 16)), S));
+    }
+}
+
 // Softmax (double, one bf16 rounding per probability) + MLX-order top-k + renorm of one
 // token's logits. kKeysT logits per thread: av[j] holds the fp64 logit accumulator of expert
-// tid + j * kThreads; xmul rescales them (power of two). Every warp selects its K largest
-// keys; warp 0 merges the sorted lists and writes the K experts in MLX order (ascending
+// tid + j * kThreads; xmul rescales them (power of two). With one key per thread warp 0
+// selects the K largest of all keys directly; with more, every warp selects its K largest and
+// warp 0 merges the sorted lists. Warp 0 writes the K experts in MLX order (ascending
 // probability, then index) with their renormalised scores to sinds / sscores. All selection
-// rounds are branch-free. Four block synchronisations; the results are visible to the whole
-// block on return.
+// rounds are branch-free; the results are visible to the whole block on return.
 template <int kKeysT>
 MOE_D void route(const double (&av)[kKeysT], double xmul, int E, int K, uint32_t *redu, double *redd,
                  uint32_t *cand, uint32_t *comp, uint32_t *sinds, float *sscores) {
@@ -215,49 +230,66 @@ MOE_D void route(const double (&av)[kKeysT], double xmul, int E, int K, uint32_t
         key[j] = (e < E) ? ((((uint32_t)f64_to_bf16_bits(ev[j] / s)) << 16) | (uint32_t)e) + 1u : 0u;
         lmax = max(lmax, key[j]);
     }
-    // this warp's K largest, descending, lane r holding the r-th
-    uint32_t mine = 0;
-#pragma unroll 1
-    for (int r = 0; r < K; ++r) {
-        const uint32_t w = __reduce_max_sync(0xffffffffu, lmax);
-        mine = (lane == r) ? w : mine;
-        lmax = 0;
+    if constexpr (kKeysT == 1) {
+        // E <= kThreads: all keys to shared memory; warp 0 holds kThreads/32 of them per lane
+        // and runs K rounds of (lane max -> warp max -> the owner clears it): the r-th winner
+        // is MLX position K-1-r
+        cand[tid] = key[0];
+        __syncthreads();
+        if (warp == 0) {
+            constexpr int kPer = kThreads / 32;
+            uint32_t kk[kPer];
 #pragma unroll
-        for (int j = 0; j < kKeysT; ++j) {
-            key[j] = (key[j] == w) ? 0u : key[j];
-            lmax = max(lmax, key[j]);
+            for (int i = 0; i < kPer; ++i) kk[i] = cand[lane + 32 * i];
+            uint32_t sel = 0;
+#pragma unroll 1
+            for (int r = 0; r < K; ++r) {
+                uint32_t m = kk[0];
+#pragma unroll
+                for (int i = 1; i < kPer; ++i) m = max(m, kk[i]);
+                const uint32_t w = __reduce_max_sync(0xffffffffu, m);
+                sel = (lane == K - 1 - r) ? w - 1u : sel;
+#pragma unroll
+                for (int i = 0; i < kPer; ++i) kk[i] = (kk[i] == w) ? 0u : kk[i];
+            }
+            renorm_mlx(sel, K, comp, sinds, sscores);
         }
-    }
-    if (lane < K) cand[warp * K + lane] = mine;
-    __syncthreads();
-    if (warp == 0) {
-        // merge of the kWarps sorted lists: lane w < kWarps holds the head of list w and has the
-        // element after it loaded already; K rounds of one warp-wide max
-        const int lw = lane < kWarps ? lane : 0;
-        uint32_t head = (lane < kWarps) ? cand[lw * K] : 0u;
-        uint32_t nxt = (lane < kWarps && K > 1) ? cand[lw * K + 1] : 0u;
-        int ptr = 1;                                  // list position of nxt
-        uint32_t sel = 0;
+    } else {
+        // this warp's K largest, descending, lane r holding the r-th
+        uint32_t mine = 0;
 #pragma unroll 1
         for (int r = 0; r < K; ++r) {
-            const uint32_t w = __reduce_max_sync(0xffffffffu, head);
-            sel = (lane == K - 1 - r) ? w - 1u : sel;         // lane k: MLX position k (ascending)
-            const bool win = head == w;
-            head = win ? nxt : head;
-            ptr += win ? 1 : 0;
-            const uint32_t ld = cand[lw * K + min(ptr, K - 1)];
-            nxt = win ? ((ptr < K) ? ld : 0u) : nxt;
+            const uint32_t w = __reduce_max_sync(0xffffffffu, lmax);
+            mine = (lane == r) ? w : mine;
+            lmax = 0;
+#pragma unroll
+            for (int j = 0; j < kKeysT; ++j) {
+                key[j] = (key[j] == w) ? 0u : key[j];
+                lmax = max(lmax, key[j]);
+            }
         }
-        __syncwarp();
-        if (lane < K) comp[lane] = sel;
-        __syncwarp();
-        // renorm: sequential bf16 sum in MLX order, then bf16(p / S)
-        float S = bf16_bits_to_f32((uint16_t)(comp[0] >> 16));
-#pragma unroll 4
-        for (int k = 1; k < K; ++k) S = bf16r(S + bf16_bits_to_f32((uint16_t)(comp[k] >> 16)));
-        if (lane < K) {
-            sinds[lane] = sel & 0xffffu;
-            sscores[lane] = bf16r(__fdiv_rn(bf16_bits_to_f32((uint16_t)(sel >> 16)), S));
+        if (lane < K) cand[warp * K + lane] = mine;
+        __syncthreads();
+        if (warp == 0) {
+            // merge of the kWarps sorted lists: lane w < kWarps holds the head of list w and has the
+            // element after it loaded already; K rounds of one warp-wide max
+            const int lw = lane < kWarps ? lane : 0;
+            uint32_t head = (lane < kWarps) ? cand[lw * K] : 0u;
+            uint32_t nxt = (lane < kWarps && K > 1) ? cand[lw * K + 1] : 0u;
+            int ptr = 1;                                  // list position of nxt
+            uint32_t sel = 0;
+#pragma unroll 1
+            for (int r = 0; r < K; ++r) {
+                const uint32_t w = __reduce_max_sync(0xffffffffu, head);
+                sel = (lane == K - 1 - r) ? w - 1u : sel;         // lane k: MLX position k (ascending)
+                const bool win = head == w;
+                head = win ? nxt : head;
+                ptr += win ? 1 : 0;
+                const uint32_t ld = cand[lw * K + min(ptr, K - 1)];
+                nxt = win ? ((ptr < K) ? ld : 0u) : nxt;
+            }
+            __syncwarp();
+            renorm_mlx(sel, K, comp, sinds, sscores);
         }
     }
     __syncthreads();
