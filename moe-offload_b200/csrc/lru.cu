@@ -182,6 +182,19 @@ __global__ void __launch_bounds__(kLruThreads) lru_kernel(LruArgs a) {
     __syncthreads();
     Lru L;
     L.bind(sm, a.E, a.cap);
+    if (a.op == kOpPrefetch) {
+        // the residency snapshot of expert_io.c:536-541 by every warp at once: 32 experts per
+        // ballot, one 32-bit half of a bitmap word per warp step (words past E come out zero)
+        const int lane = threadIdx.x & 31;
+        uint32_t *pre32 = reinterpret_cast<uint32_t *>(L.pre);
+#pragma unroll 1
+        for (int base = threadIdx.x - lane; base < L.nb * 64; base += blockDim.x) {
+            const int e = base + lane;
+            const unsigned bal = __ballot_sync(0xffffffffu, e < a.E && L.e2s[e] >= 0);
+            if (lane == 0) pre32[base >> 5] = bal;
+        }
+        __syncthreads();
+    }
     if (threadIdx.x == 0) {
         LruHeader *h = L.h;
         const int E = a.E;
@@ -271,14 +284,11 @@ __global__ void __launch_bounds__(kLruThreads) lru_kernel(LruArgs a) {
                 }
                 break;
             }
-            case kOpPrefetch: {  // expert_io.c:527-581
+            case kOpPrefetch: {  // expert_io.c:527-581 (L.pre: the snapshot taken above)
                 for (int b = 0; b < L.nb; ++b) {
-                    L.pre[b] = 0;
                     L.pred[b] = 0;
                     L.fet[b] = 0;
                 }
-                for (int e = 0; e < E; ++e)
-                    if (L.e2s[e] >= 0) L.pre[e >> 6] |= 1ull << (e & 63);
                 h->has_snap = 1;
                 uint64_t prot[kLruMaxE / 64];
                 for (int b = 0; b < L.nb; ++b) prot[b] = 0;

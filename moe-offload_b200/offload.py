@@ -381,6 +381,7 @@ class OffloadStack:
                                                 prefetch_stream=ps) for l in range(1, self.L)]
         self.capacities = capacities
         self.hs = [torch.empty((1, self.H), dtype=torch.bfloat16, device=self.device) for _ in range(self.L + 1)]
+        self.xn = [torch.empty((1, self.H), dtype=torch.bfloat16, device=self.device) for _ in range(self.L)]
         self.r_out = [{} for _ in range(self.L)]
         self.pred_bias = None
 
@@ -398,8 +399,10 @@ class OffloadStack:
         for l in range(self.L):
             x = self.hs[l]
             xin = x
-            if self.norm:
-                xin = _pow2_normalize_dev(x)
+            if self.norm:                              # one kernel (moe_pow2_rows), graph-safe buffer
+                xin = self.xn[l]
+                call("moe_pow2_rows", x.data_ptr(), 1, self.H, xin.data_ptr(),
+                     torch.cuda.current_stream(self.device).cuda_stream)
             nxt = self.routers[l + 1] if (self.prefetch and l + 1 < self.L) else None
             pb = self.pred_bias[l + 1] if (nxt is not None and self.pred_bias is not None) else None
             r = ops.router_topk(xin, self.routers[l], self.K, w_next=nxt, M=self.M if nxt is not None else 0,
