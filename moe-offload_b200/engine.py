@@ -18,30 +18,38 @@ from __future__ import annotations
 
 import hashlib
 import time
+from pathlib import Path
 from typing import Any
 
 import torch
 
+from . import checkpoint
 from .offload import HostExpertPool, OffloadStack, compute_layer_capacities
 from .synthetic import C2, StackConfig, dev_bf16_normal, dev_stack
 
 
 class OffloadEngine:
     """loader.py:1004-1343: OffloadEngine(model_path, budget_gb, budget_pct, alloc_mode, prefetch,
-    prefetch_top_m, prefetch_cap). model_path is accepted for signature parity and recorded;
+    prefetch_top_m, prefetch_cap). When model_path is a directory in the reference's layout
+    (experts-XX.safetensors per layer, routers in base-*.safetensors, checkpoint.load_model_dir)
+    the stack is loaded from it (top_k from its config.json or the top_k argument); otherwise
     the stack comes from `config` (synthetic weights, seed config.seed)."""
 
     def __init__(self, model_path=None, budget_gb: float | None = None, budget_pct: float | None = 20.0,
                  alloc_mode: str = "even", prefetch: bool = True, prefetch_top_m: int = 12, prefetch_cap: int = 3,
-                 *, config: StackConfig = C2, device="cuda:0"):
+                 *, config: StackConfig = C2, device="cuda:0", top_k: int | None = None):
         t0 = time.perf_counter()
         self.model_path = model_path
+        self.device = torch.device(device)
+        loaded = None
+        if model_path is not None and (Path(model_path) / checkpoint.shard_name(0)).exists():
+            loaded = checkpoint.load_model_dir(model_path, self.device, top_k=top_k)
+            config = loaded["config"]
         self.config = config
         self.alloc_mode = alloc_mode
         self.prefetch = prefetch
         self.prefetch_top_m = prefetch_top_m
         self.prefetch_cap = prefetch_cap
-        self.device = torch.device(device)
         L, E = config.layers, config.experts
         self.num_layers, self.num_experts = L, E
         self.capacities = compute_layer_capacities(budget_gb=budget_gb, budget_pct=budget_pct, alloc_mode=alloc_mode,
@@ -49,13 +57,16 @@ class OffloadEngine:
         self.total_cached_slots = sum(self.capacities.values())
         self.cache_budget_bytes = self.total_cached_slots * config.expert_bytes
         self.layer0_pinned_bytes = E * config.expert_bytes
-        layers = dev_stack(config, self.device)
-        routers = [ly.router for ly in layers]
-        pools = [HostExpertPool.from_layer(layers[l]) for l in range(1, L)]
-        layer0 = layers[0]
-        for l in range(1, L):
-            layers[l] = None
-        torch.cuda.empty_cache()
+        if loaded is not None:
+            routers, layer0, pools = loaded["routers"], loaded["layer0"], loaded["pools"]
+        else:
+            layers = dev_stack(config, self.device)
+            routers = [ly.router for ly in layers]
+            pools = [HostExpertPool.from_layer(layers[l]) for l in range(1, L)]
+            layer0 = layers[0]
+            for l in range(1, L):
+                layers[l] = None
+            torch.cuda.empty_cache()
         self.stack = OffloadStack(routers, layer0, pools, self.capacities, config.top_k, self.device,
                                   prefetch=prefetch, prefetch_top_m=prefetch_top_m, prefetch_cap=prefetch_cap,
                                   expert_bytes=config.expert_bytes)
