@@ -691,7 +691,18 @@ extern "C" int moe_stack_decode(const void *layers, int L, int H, int I, int E, 
     const void *kern = (E <= kThreads) ? (sb_fp16 ? (const void *)stack_kernel<true, 1> : (const void *)stack_kernel<false, 1>)
                                        : (sb_fp16 ? (const void *)stack_kernel<true, kMaxE / kThreads>
                                                   : (const void *)stack_kernel<false, kMaxE / kThreads>);
-    MOE_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)S.total));
+    // raise the kernel's shared-memory limit once per (kernel, size): not per launch, and
+    // not while a launch is being captured
+    static const void *set_kern[4] = {};
+    static size_t set_bytes[4] = {};
+    static int set_dev[4] = {-1, -1, -1, -1};
+    const int ki = (E <= kThreads ? 0 : 2) + (sb_fp16 ? 1 : 0);
+    if (set_kern[ki] != kern || set_bytes[ki] < S.total || set_dev[ki] != dev) {
+        MOE_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)S.total));
+        set_kern[ki] = kern;
+        set_bytes[ki] = S.total;
+        set_dev[ki] = dev;
+    }
     MOE_CUDA_TRY(cudaLaunchCooperativeKernel(kern, dim3(G), dim3(kThreads), kargs, S.total, st));
     return MOE_OK;
 }

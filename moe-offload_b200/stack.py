@@ -144,6 +144,8 @@ class PersistentStack:
         self.hs = (torch.empty((self.L + 1, self.H), dtype=torch.bfloat16, device=self.device)
                    if keep_layer_inputs else None)
         self.launches_per_step = 1
+        self._decode_graph = None        # host-facing step as one CUDA graph (decode)
+        self._graph_failed = False
 
     def step_device(self, x: torch.Tensor | None = None) -> torch.Tensor:
         if x is not None:
@@ -154,13 +156,48 @@ class PersistentStack:
                    self.ws.numel(), self.num_ctas, torch.cuda.current_stream(self.device).cuda_stream)
         return self.y
 
+    def _capture_decode(self) -> None:
+        """Records the host-facing step (H2D copy from a fixed pinned buffer, workspace reset +
+        persistent launch, D2H copy into a fixed pinned buffer) as one CUDA graph, so a token
+        costs one graph launch instead of four host-issued operations."""
+        self._h_pin = torch.zeros((1, self.H), dtype=torch.bfloat16, pin_memory=True)
+        self._o_pin = torch.empty((1, self.H), dtype=torch.bfloat16, pin_memory=True)
+        s = torch.cuda.Stream(device=self.device)
+        s.wait_stream(torch.cuda.current_stream(self.device))
+        try:
+            with torch.cuda.stream(s):
+                self.x_in.copy_(self._h_pin, non_blocking=True)      # warm-up outside the graph
+                self.step_device()
+                self._o_pin.copy_(self.y, non_blocking=True)
+            s.synchronize()
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=s):
+                self.x_in.copy_(self._h_pin, non_blocking=True)
+                self.step_device()
+                self._o_pin.copy_(self.y, non_blocking=True)
+            self._decode_graph = g
+        except RuntimeError:
+            # a driver that cannot capture a cooperative launch: keep the direct path
+            self._graph_failed = True
+            torch.cuda.synchronize(self.device)
+        torch.cuda.current_stream(self.device).wait_stream(s)
+
     def decode(self, h_host: torch.Tensor, out_host: torch.Tensor | None = None) -> torch.Tensor:
-        """Host-facing decode step: pinned host hidden state [1,H] bf16 in, host result out."""
+        """Host-facing decode step: host hidden state [1,H] bf16 in, host result out (the
+        result also stays in self.y). Runs the captured graph when available."""
         cur = torch.cuda.current_stream(self.device)
-        self.x_in.copy_(h_host, non_blocking=True)
-        y = self.step_device()
+        if self._decode_graph is None and not self._graph_failed:
+            self._capture_decode()
         if out_host is None:
             out_host = torch.empty((1, self.H), dtype=torch.bfloat16, pin_memory=True)
+        if self._decode_graph is not None:
+            self._h_pin.copy_(h_host)
+            self._decode_graph.replay()
+            cur.synchronize()
+            out_host.copy_(self._o_pin)
+            return out_host
+        self.x_in.copy_(h_host, non_blocking=True)
+        y = self.step_device()
         out_host.copy_(y, non_blocking=True)
         cur.synchronize()
         return out_host

@@ -86,6 +86,27 @@ def test_persistent_stack_results_independent_of_cta_count(dev):
     assert int(__import__("moe_offload_b200")._lib.call("moe_device_error", 1)) == 0
 
 
+def test_persistent_stack_host_decode_graph(dev):
+    """The host-facing decode (H2D, launch and D2H captured as one graph) returns the same bits
+    as the device-side step, token after token."""
+    from moe_offload_b200.stack import PersistentStack
+    from moe_offload_b200.synthetic import np_bf16_normal, np_to_bf16_tensor
+    rng = np.random.default_rng(41)
+    L, H, I, E, K = 3, 2048, 768, 64, 8
+    layers = _dev_layers(_np_layers(rng, L, E, H, I), dev)
+    st = PersistentStack(layers, K, dev)
+    out = torch.empty((1, H), dtype=torch.bfloat16, pin_memory=True)
+    for _ in range(4):
+        x = np_to_bf16_tensor(np_bf16_normal(rng, (1, H)), dev)
+        y_dev = st.step_device(x).clone()
+        inds_dev = st.inds.clone()
+        torch.cuda.synchronize()
+        st.decode(x.cpu().pin_memory(), out)
+        assert torch.equal(out, y_dev.cpu())
+        assert torch.equal(st.inds, inds_dev)
+    assert st._decode_graph is not None or st._graph_failed
+
+
 def test_persistent_stack_matches_layer_path(dev):
     """Same weights and input through the per-layer kernels: indices identical, outputs close."""
     from moe_offload_b200.stack import DecodeStack, PersistentStack
