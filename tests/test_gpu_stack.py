@@ -32,9 +32,11 @@ def _dev_layers(np_layers, dev):
                         to_device_qmatrix(ly["u"], dev), to_device_qmatrix(ly["d"], dev)) for ly in np_layers]
 
 
-# ctas = 0: all SMs (CTAs without a work item exist); (2, 512, 256, 32, 4, 16): one item per CTA
+# ctas = 0: all SMs (CTAs without a work item exist); (2, 512, 256, 32, 4, 16): one item per CTA;
+# (2, 3072, 768, 512, 10, 0): the c1 layer shape of the bench (512 experts, top-10)
 @pytest.mark.parametrize("L,H,I,E,K,ctas", [(3, 3072, 768, 64, 10, 0), (6, 2048, 768, 64, 8, 0),
-                                           (2, 1024, 256, 32, 4, 40), (2, 512, 256, 32, 4, 16)])
+                                           (2, 1024, 256, 32, 4, 40), (2, 512, 256, 32, 4, 16),
+                                           (2, 3072, 768, 512, 10, 0)])
 def test_persistent_stack_vs_oracle(dev, L, H, I, E, K, ctas):
     from moe_offload_b200.ops import pow2_normalize
     from moe_offload_b200.stack import PersistentStack
