@@ -830,8 +830,8 @@ private:
             for (int j = 0; j < task.nseg; ++j) moved += copy_row(L, task.seg[j], failed);
         }
         if (!task.prefill && moved) L_[task.layer].bytes.fetch_add(moved, std::memory_order_relaxed);
+        if (failed) copy_errors_.fetch_add(1, std::memory_order_relaxed);
         std::unique_lock<std::mutex> lk(mu_);
-        if (failed) copy_errors_++;
         bool any_done = false;
         for (int j = 0; j < task.nseg; ++j) {
             const OpPtr &op = task.seg[j].op;
@@ -941,7 +941,7 @@ private:
     std::mt19937_64 rng_;
 
 public:
-    uint64_t copy_errors_ = 0;
+    std::atomic<uint64_t> copy_errors_{0};
 };
 
 Scheduler *H(void *h) { return static_cast<Scheduler *>(h); }
@@ -1114,4 +1114,6 @@ extern "C" int moe_p1_get_total_stats(void *h, int num_layers, uint64_t *out) {
     return MOE_OK;
 }
 
-extern "C" uint64_t moe_p1_copy_errors(void *h) { return h ? H(h)->copy_errors_ : 0; }
+extern "C" uint64_t moe_p1_copy_errors(void *h) {
+    return h ? H(h)->copy_errors_.load(std::memory_order_relaxed) : 0;
+}
