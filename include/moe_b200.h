@@ -267,6 +267,39 @@ int moe_combine_rows(const void *yk, int T, int K, int H, const void *scores, co
 int moe_pow2_rows(const void *x, int T, int H, void *xn, void *stream);
 
 /* ------------------------------------------------------------------------------------ */
+/* Shared expert and affine-quantised linear layers (csrc/shared.cu).                      */
+/* ------------------------------------------------------------------------------------ */
+
+/*
+ * y [T, N] bf16 = x [T, Kin] bf16 . W^T with W an affine-quantised matrix in MLX layout:
+ * codes u32 [N, Kin*bits/32], scales/biases [N, Kin/group_size] (bf16, or fp16 with
+ * sb_fp16 = 1). Replaces QLinear::forward (mlx-qwen38/cpp/src/kernels.cpp:997-1019, a
+ * quantized_matmul with transpose=True). bits 2, 4 or 8; group_size a multiple of 32/bits
+ * that divides Kin; at most 384 groups per row. Arithmetic: per group, float sums of q*x and
+ * of x in input order; scale*sum(qx) + bias*sum(x) in double; the double sum over groups in
+ * group order, rounded to float then bf16.
+ */
+int moe_affine_linear(const void *x, int T, int Kin, int N, const void *w, const void *scales, const void *biases,
+                      int bits, int group_size, int sb_fp16, void *y, void *stream);
+
+/* bytes of device workspace moe_shared_expert needs for T tokens (0 for bad sizes) */
+size_t moe_shared_expert_workspace_bytes(int T, int H, int I);
+
+/*
+ * The layer's shared expert (mlx-qwen38/cpp/src/engine.cpp:394-400, loader.py:909-910):
+ *   g = x.Wg^T, u = x.Wu^T ([T, I]), act = bf16(bf16(g*bf16(sigmoid(g)))*u),
+ *   o = act.Wd^T ([T, H]), gl = x.We^T ([T, 1]), y = bf16(bf16(sigmoid(gl)) * o).
+ * Wg/Wu/Wd share `bits`/`group_size` (4-bit g64 in the reference's models); the scalar gate
+ * We has its own (8-bit g64). y [T, H] bf16 is the `shared_y` addend of moe_experts_down /
+ * moe_decode_layer. workspace >= moe_shared_expert_workspace_bytes(T, H, I).
+ */
+int moe_shared_expert(const void *x, int T, int H, int I, const void *wg, const void *sg, const void *bg,
+                      const void *wu, const void *su, const void *bu, const void *wd, const void *sd, const void *bd,
+                      int bits, int group_size, const void *weg, const void *seg, const void *beg, int gate_bits,
+                      int gate_group_size, int sb_fp16, void *y, void *workspace, size_t workspace_bytes,
+                      void *stream);
+
+/* ------------------------------------------------------------------------------------ */
 /* Expert parallelism: one process per GPU, experts split in contiguous blocks.           */
 /* ------------------------------------------------------------------------------------ */
 

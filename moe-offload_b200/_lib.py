@@ -51,6 +51,9 @@ SIGNATURES: dict[str, tuple] = {
     "moe_prefill_experts_slots": (I, [P, I, I, I, I, I, P] + [P] * 9 + [I, P, P, SZ, P]),
     "moe_combine_rows": (I, [P, I, I, I, P, P, P, P]),
     "moe_pow2_rows": (I, [P, I, I, P, P]),
+    "moe_affine_linear": (I, [P, I, I, I, P, P, P, I, I, I, P, P]),
+    "moe_shared_expert_workspace_bytes": (SZ, [I, I, I]),
+    "moe_shared_expert": (I, [P, I, I, I] + [P] * 9 + [I, I, P, P, P, I, I, I, P, P, SZ, P]),
     "moe_ep_buffer_bytes": (SZ, [I, I, I]),
     "moe_ep_buffer_alloc": (I, [SZ, P, P]),
     "moe_ep_buffer_open": (I, [P, P]),

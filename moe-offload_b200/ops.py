@@ -174,6 +174,67 @@ def experts_down(act: torch.Tensor, slots: torch.Tensor, down: QMatrix, scores=N
     return y, yk
 
 
+# ----------------------------------------------------------------------------- shared expert
+
+def _lin_dims(name: str, m: QMatrix, dev):
+    m.check(name, dev)
+    if m.w.dim() != 2:
+        raise ValueError(f"{name}.w must be 2-D [N, K*bits/32], got {tuple(m.w.shape)}")
+    return m.w.shape[0], m.w.shape[1] * 32 // m.bits
+
+
+def affine_linear(x: torch.Tensor, w: QMatrix, *, y=None, stream=None) -> torch.Tensor:
+    """y [T, N] = x [T, K] . W^T for one affine-quantised matrix (QLinear::forward,
+    cpp/src/kernels.cpp:997-1019)."""
+    _need(x, "x", (torch.bfloat16,))
+    N, K = _lin_dims("w", w, x.device)
+    T = x.numel() // K if x.shape[-1] == K else -1
+    if T < 1:
+        raise ValueError(f"x has shape {tuple(x.shape)}, expected [..., {K}]")
+    if y is None:
+        y = torch.empty((T, N), dtype=torch.bfloat16, device=x.device)
+    call("moe_affine_linear", x.data_ptr(), T, K, N, w.w.data_ptr(), w.s.data_ptr(), w.b.data_ptr(), w.bits,
+         w.group_size, w.sb_fp16, y.data_ptr(), _stream(stream))
+    return y
+
+
+_SWS: dict = {}
+
+
+def shared_expert(x: torch.Tensor, gate: QMatrix, up: QMatrix, down: QMatrix, expert_gate: QMatrix, *,
+                  y=None, stream=None) -> torch.Tensor:
+    """shared_y [T, H] = sigmoid(x . We^T) * down(SwiGLU(x . Wg^T, x . Wu^T)): the layer's
+    shared expert (engine.cpp:394-400, loader.py:909-910), the addend of experts_down /
+    decode_layer."""
+    _need(x, "x", (torch.bfloat16,))
+    dev = x.device
+    I, H = _lin_dims("gate", gate, dev)
+    if _lin_dims("up", up, dev) != (I, H) or _lin_dims("down", down, dev) != (H, I) or \
+            _lin_dims("expert_gate", expert_gate, dev) != (1, H):
+        raise ValueError("shared expert matrices disagree on H / I")
+    if (up.bits, down.bits, up.group_size, down.group_size) != (gate.bits,) * 2 + (gate.group_size,) * 2:
+        raise ValueError("gate/up/down must share bits and group_size")
+    if len({gate.sb_fp16, up.sb_fp16, down.sb_fp16, expert_gate.sb_fp16}) != 1:
+        raise ValueError("scales/biases of the shared expert must share one dtype")
+    T = x.numel() // H
+    if x.shape[-1] != H or T < 1:
+        raise ValueError(f"x has shape {tuple(x.shape)}, expected [..., {H}]")
+    need = call("moe_shared_expert_workspace_bytes", T, H, I)
+    key = (dev, stream)
+    ws = _SWS.get(key)
+    if ws is None or ws.numel() < need:
+        ws = torch.empty(need, dtype=torch.uint8, device=dev)
+        _SWS[key] = ws
+    if y is None:
+        y = torch.empty((T, H), dtype=torch.bfloat16, device=dev)
+    call("moe_shared_expert", x.data_ptr(), T, H, I, gate.w.data_ptr(), gate.s.data_ptr(), gate.b.data_ptr(),
+         up.w.data_ptr(), up.s.data_ptr(), up.b.data_ptr(), down.w.data_ptr(), down.s.data_ptr(),
+         down.b.data_ptr(), gate.bits, gate.group_size, expert_gate.w.data_ptr(), expert_gate.s.data_ptr(),
+         expert_gate.b.data_ptr(), expert_gate.bits, expert_gate.group_size, gate.sb_fp16, y.data_ptr(),
+         ws.data_ptr(), ws.numel(), _stream(stream))
+    return y
+
+
 # ----------------------------------------------------------------------------- fused layer
 
 _DWS: dict = {}

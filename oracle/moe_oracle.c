@@ -347,6 +347,67 @@ int orc_experts(const uint16_t *x, int T, int H, int I, int K, const uint32_t *s
     return 0;
 }
 
+/* ------------------------------------------------------------------------------------ */
+/* shared expert (engine.cpp:394-400, loader.py:909-910) and QLinear (kernels.cpp:997-1019) */
+/* ------------------------------------------------------------------------------------ */
+
+/* y [T, N] = bf16(float(x [T, Kin] . W^T)), W affine-quantised [N, Kin*bits/32] + s/b
+ * [N, Kin/gs]; qdot_row's arithmetic (float sums per group in input order, double over
+ * groups in group order) */
+int orc_affine_linear(const uint16_t *x, int T, int Kin, int N, const uint32_t *w, const uint16_t *s,
+                      const uint16_t *b, int bits, int gs, int sb_fp16, uint16_t *y) {
+    if (bits != 2 && bits != 4 && bits != 8) return -22;
+    if (T <= 0 || Kin <= 0 || N <= 0 || gs <= 0 || Kin % gs || gs % (32 / bits)) return -22;
+    const size_t wrow = (size_t)Kin / (32 / bits), srow = (size_t)Kin / gs;
+    float *xf = (float *)malloc(sizeof(float) * (size_t)Kin);
+    if (!xf) return -12;
+    for (int t = 0; t < T; ++t) {
+        for (int k = 0; k < Kin; ++k) xf[k] = bf16_to_f32(x[(size_t)t * Kin + k]);
+#pragma omp parallel for schedule(static)
+        for (int n = 0; n < N; ++n)
+            y[(size_t)t * N + n] = f32_to_bf16((float)qdot_row(w + n * wrow, s + n * srow, b + n * srow, sb_fp16,
+                                                               xf, Kin, bits, gs));
+    }
+    free(xf);
+    return 0;
+}
+
+/*
+ * shared_y [T, H] = bf16(bf16(sigmoid(gl)) * o), o = down(act), act = SwiGLU(gate(x), up(x)),
+ * gl = expert_gate(x) [T, 1]. act [T, I] and o [T, H] are optional outputs (NULL to skip).
+ */
+int orc_shared_expert(const uint16_t *x, int T, int H, int I, const uint32_t *wg, const uint16_t *sg,
+                      const uint16_t *bg, const uint32_t *wu, const uint16_t *su, const uint16_t *bu,
+                      const uint32_t *wd, const uint16_t *sd, const uint16_t *bd, int bits, int gs,
+                      const uint32_t *we, const uint16_t *se, const uint16_t *be, int gbits, int ggs,
+                      int sb_fp16, uint16_t *y, uint16_t *act_out, uint16_t *o_out) {
+    size_t ti = (size_t)T * I, th = (size_t)T * H;
+    uint16_t *g = (uint16_t *)malloc(2 * ti), *u = (uint16_t *)malloc(2 * ti), *act = (uint16_t *)malloc(2 * ti);
+    uint16_t *o = (uint16_t *)malloc(2 * th), *gl = (uint16_t *)malloc(2 * (size_t)T);
+    int rc = (g && u && act && o && gl) ? 0 : -12;
+    if (!rc) rc = orc_affine_linear(x, T, H, I, wg, sg, bg, bits, gs, sb_fp16, g);
+    if (!rc) rc = orc_affine_linear(x, T, H, I, wu, su, bu, bits, gs, sb_fp16, u);
+    if (!rc) {
+        for (size_t i = 0; i < ti; ++i) act[i] = f32_to_bf16(swiglu_bf16(bf16_to_f32(g[i]), bf16_to_f32(u[i])));
+        rc = orc_affine_linear(act, T, I, H, wd, sd, bd, bits, gs, sb_fp16, o);
+    }
+    if (!rc) rc = orc_affine_linear(x, T, H, 1, we, se, be, gbits, ggs, sb_fp16, gl);
+    if (!rc) {
+        for (size_t i = 0; i < th; ++i) {
+            float sig = bf(sigmoidf_ref(bf16_to_f32(gl[i / H])));
+            y[i] = f32_to_bf16(sig * bf16_to_f32(o[i]));
+        }
+        if (act_out) memcpy(act_out, act, 2 * ti);
+        if (o_out) memcpy(o_out, o, 2 * th);
+    }
+    free(g);
+    free(u);
+    free(act);
+    free(o);
+    free(gl);
+    return rc;
+}
+
 /* number of OpenMP threads the oracle uses (1 when built without OpenMP) */
 int orc_num_threads(void) {
 #ifdef _OPENMP

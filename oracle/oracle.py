@@ -42,7 +42,8 @@ def lib() -> ctypes.CDLL:
         L.orc_f32_to_bf16.restype = ctypes.c_uint16
         L.orc_num_threads.restype = I
         L.orc_set_num_threads.argtypes = [I]
-        for f in ("orc_router_logits", "orc_softmax_topk", "orc_topm_sorted", "orc_experts"):
+        for f in ("orc_router_logits", "orc_softmax_topk", "orc_topm_sorted", "orc_experts",
+                  "orc_affine_linear", "orc_shared_expert"):
             getattr(L, f).restype = I
         _LIB = L
     return _LIB
@@ -143,6 +144,43 @@ def experts(x_bf16, slots, scores_bf16, gate, up, down, bits: int = 2, group_siz
                            _p(su), _p(bu), _p(wd), _p(sd), _p(bd), bits, group_size, int(sb_fp16),
                            _p(ad), _p(rs), _p(y), _p(act), _p(yk)), "experts")
     return {"y": y, "act": act, "yk": yk}
+
+
+
+# ---------------------------------------------------------------- shared expert
+
+def affine_linear(x_bf16, w, bits: int, group_size: int, sb_fp16: bool = False):
+    """y [T, N] bf16 bits = x [T, K] . W^T for W = (codes u32 [N, K*bits/32], scales, biases)."""
+    x = np.ascontiguousarray(x_bf16, dtype=np.uint16)
+    wq, s, b = (np.ascontiguousarray(a) for a in w)
+    N = wq.shape[0]
+    K = wq.shape[1] * 32 // bits
+    x = x.reshape(-1, K)
+    T = x.shape[0]
+    y = np.empty((T, N), dtype=np.uint16)
+    _chk(lib().orc_affine_linear(_p(x), T, K, N, _p(wq), _p(s), _p(b), bits, group_size, int(sb_fp16), _p(y)),
+         "affine_linear")
+    return y
+
+
+def shared_expert(x_bf16, gate, up, down, expert_gate, bits: int = 4, group_size: int = 64, gate_bits: int = 8,
+                  gate_group_size: int = 64, sb_fp16: bool = False):
+    """The shared expert (engine.cpp:394-400). gate/up/down/expert_gate: (codes, scales, biases)
+    2-D matrices. Returns dict(y=[T, H], act=[T, I], o=[T, H]) as bf16 bits."""
+    wg, sg, bg = (np.ascontiguousarray(a) for a in gate)
+    wu, su, bu = (np.ascontiguousarray(a) for a in up)
+    wd, sd, bd = (np.ascontiguousarray(a) for a in down)
+    we, se, be = (np.ascontiguousarray(a) for a in expert_gate)
+    I, H = wg.shape[0], wg.shape[1] * 32 // bits
+    x = np.ascontiguousarray(x_bf16, dtype=np.uint16).reshape(-1, H)
+    T = x.shape[0]
+    y = np.empty((T, H), dtype=np.uint16)
+    act = np.empty((T, I), dtype=np.uint16)
+    o = np.empty((T, H), dtype=np.uint16)
+    _chk(lib().orc_shared_expert(_p(x), T, H, I, _p(wg), _p(sg), _p(bg), _p(wu), _p(su), _p(bu), _p(wd), _p(sd),
+                                 _p(bd), bits, group_size, _p(we), _p(se), _p(be), gate_bits, gate_group_size,
+                                 int(sb_fp16), _p(y), _p(act), _p(o)), "shared_expert")
+    return {"y": y, "act": act, "o": o}
 
 
 def ref_lru_lib(version: int = 1):
