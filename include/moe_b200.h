@@ -300,6 +300,31 @@ int moe_shared_expert(const void *x, int T, int H, int I, const void *wg, const 
                       void *stream);
 
 /* ------------------------------------------------------------------------------------ */
+/* Hyper-connection mixer before the MoE block (csrc/hc.cu).                              */
+/* ------------------------------------------------------------------------------------ */
+
+/* bytes of device workspace moe_hc_mix needs (0 for bad sizes) */
+size_t moe_hc_workspace_bytes(int T, int HC, int H, int R);
+
+/*
+ * One call of Qwen38Engine::run_hc (mlx-qwen38/cpp/src/kernels.cpp:1363-1560) with
+ * affine-quantised mixer matrices, for T rows of HC streams of H values:
+ *   h [T, HC*H] bf16; branch [T, H] and gate [T, HC] bf16 (both NULL = no write);
+ *   norm_w [HC*H] bf16 (the norm scales 1 + norm_w); eps the RMS epsilon;
+ *   down [R, HC*H], up [HC*H, R], inject [HC, HC*H] (codes u32 + scales/biases, NULL inject =
+ *   the use_combine=False mixer, inj then zeros).
+ * Outputs: written [T, HC*H] (h plus the write; required with a write, untouched without),
+ * mixed [T, H] (the block input), inj [T, HC] (the next write's gate; may be NULL).
+ * T <= 16 uses the reference's decode rounding (unrounded dot products), T > 16 its prefill
+ * rounding. HC must be 4. workspace >= moe_hc_workspace_bytes(T, HC, H, R).
+ */
+int moe_hc_mix(const void *h, int T, int HC, int H, int R, const void *branch, const void *gate, const void *norm_w,
+               float eps, const void *wd, const void *sd, const void *bd, int dbits, int dgs, const void *wu,
+               const void *su, const void *bu, int ubits, int ugs, const void *wi, const void *si, const void *bi,
+               int ibits, int igs, int sb_fp16, void *written, void *mixed, void *inj, void *workspace,
+               size_t workspace_bytes, void *stream);
+
+/* ------------------------------------------------------------------------------------ */
 /* Expert parallelism: one process per GPU, experts split in contiguous blocks.           */
 /* ------------------------------------------------------------------------------------ */
 

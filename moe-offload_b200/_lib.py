@@ -54,6 +54,9 @@ SIGNATURES: dict[str, tuple] = {
     "moe_affine_linear": (I, [P, I, I, I, P, P, P, I, I, I, P, P]),
     "moe_shared_expert_workspace_bytes": (SZ, [I, I, I]),
     "moe_shared_expert": (I, [P, I, I, I] + [P] * 9 + [I, I, P, P, P, I, I, I, P, P, SZ, P]),
+    "moe_hc_workspace_bytes": (SZ, [I, I, I, I]),
+    "moe_hc_mix": (I, [P, I, I, I, I, P, P, P, ctypes.c_float] + [P] * 3 + [I, I] + [P] * 3 + [I, I] + [P] * 3 +
+                   [I, I, I, P, P, P, P, SZ, P]),
     "moe_ep_buffer_bytes": (SZ, [I, I, I]),
     "moe_ep_buffer_alloc": (I, [SZ, P, P]),
     "moe_ep_buffer_open": (I, [P, P]),

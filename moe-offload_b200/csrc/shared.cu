@@ -24,183 +24,61 @@
 #include <cuda_runtime.h>
 
 #include "common.cuh"
+#include "qlinear.cuh"
 #include "../../include/moe_b200.h"
 
 namespace {
 
-constexpr int kLinWarps = 4;                     // output rows per block (one warp each)
-constexpr int kLinThreads = kLinWarps * 32;
-constexpr int kLinTok = 4;                       // tokens per pass over a row
-constexpr int kMaxGroups = 384;                  // groups per row staged in shared memory
+using namespace moe_qlin;
 
-// q (< 2^23) as float without an int -> float conversion: the float with exponent 2^23 and
-// mantissa q is exactly 2^23 + q, so subtracting 2^23 leaves q exactly
-MOE_D float code_f32(uint32_t q) { return __uint_as_float(0x4B000000u | q) - 8388608.0f; }
-
-template <int kBits, int kGs>
-struct Group {
-    static constexpr int kPer = 32 / kBits;      // codes per word
-    static constexpr int kWords = kGs / kPer;    // words per group (2 .. 32)
-    static constexpr uint32_t kMask = (1u << kBits) - 1u;
-
-    MOE_D static void load(const uint32_t *gw, uint32_t (&wv)[kWords]) {
-        if constexpr (kWords % 4 == 0) {
-#pragma unroll
-            for (int c = 0; c < kWords / 4; ++c) {
-                const uint4 v = __ldg(reinterpret_cast<const uint4 *>(gw) + c);
-                wv[4 * c] = v.x, wv[4 * c + 1] = v.y, wv[4 * c + 2] = v.z, wv[4 * c + 3] = v.w;
-            }
-        } else {
-#pragma unroll
-            for (int c = 0; c < kWords / 2; ++c) {
-                const uint2 v = __ldg(reinterpret_cast<const uint2 *>(gw) + c);
-                wv[2 * c] = v.x, wv[2 * c + 1] = v.y;
-            }
-        }
-    }
-
-    // acc = sum q x, xs = sum x over the group, both in input order; xg: the group's kGs bf16
-    MOE_D static void dot(const uint32_t (&wv)[kWords], const uint16_t *xg, float &acc, float &xs) {
-        acc = 0.f, xs = 0.f;
-#pragma unroll
-        for (int c = 0; c < kGs / 8; ++c) {
-            const uint4 v = __ldg(reinterpret_cast<const uint4 *>(xg) + c);
-            const uint32_t pk[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-            for (int i = 0; i < 8; ++i) {
-                const int k = 8 * c + i;
-                const float xv = __uint_as_float((i & 1) ? (pk[i >> 1] & 0xffff0000u) : (pk[i >> 1] << 16));
-                const float q = code_f32((wv[k / kPer] >> (kBits * (k % kPer))) & kMask);
-                acc = fmaf(q, xv, acc);          // q x is exact: one rounding, as acc + q x
-                xs += xv;
-            }
-        }
-    }
-};
-
-template <bool kFp16>
-MOE_D double group_value(const uint16_t *s, const uint16_t *b, int g, float acc, float xs) {
-    const double sc = (double)sb_to_f32<kFp16>(__ldg(s + g)), bi = (double)sb_to_f32<kFp16>(__ldg(b + g));
-    return fma(sc, (double)acc, bi * (double)xs);
-}
-
-// Stages the group values of kMats rows (row r of matrix m: w[m], s[m], b[m]) for tokens
-// t0 .. t0+nt-1 into sv[(m * kLinTok + j) * ng + g].
-template <int kBits, int kGs, bool kFp16, int kMats>
-MOE_D void stage_rows(const uint16_t *x, int Kin, int t0, int nt, const uint32_t *const (&w)[kMats],
-                      const uint16_t *const (&s)[kMats], const uint16_t *const (&b)[kMats], int ng, int lane,
-                      double *sv) {
-    using G = Group<kBits, kGs>;
-    uint32_t cur[kMats][G::kWords], nxt[kMats][G::kWords];
-    if (lane < ng) {
-#pragma unroll
-        for (int m = 0; m < kMats; ++m) G::load(w[m] + (size_t)lane * G::kWords, cur[m]);
-    }
-#pragma unroll 1
-    for (int g = lane; g < ng; g += 32) {
-        const int gn = g + 32;
-        if (gn < ng) {
-#pragma unroll
-            for (int m = 0; m < kMats; ++m) G::load(w[m] + (size_t)gn * G::kWords, nxt[m]);
-        }
-#pragma unroll 1
-        for (int j = 0; j < nt; ++j) {
-            const uint16_t *xg = x + (size_t)(t0 + j) * Kin + (size_t)g * kGs;
-#pragma unroll
-            for (int m = 0; m < kMats; ++m) {
-                float acc, xs;
-                G::dot(cur[m], xg, acc, xs);
-                sv[(m * kLinTok + j) * ng + g] = group_value<kFp16>(s[m], b[m], g, acc, xs);
-            }
-        }
-        if (gn < ng) {
-#pragma unroll
-            for (int m = 0; m < kMats; ++m)
-#pragma unroll
-                for (int q = 0; q < G::kWords; ++q) cur[m][q] = nxt[m][q];
-        }
-    }
-}
-
-MOE_D double sum_in_order(const double *v, int n) {
-    double total = 0.0;
-    for (int g = 0; g < n; ++g) total += v[g];
-    return total;
-}
-
-MOE_D uint16_t row_out(double total) { return f32_to_bf16_bits((float)total); }
-
-MOE_D float sigmoid_bf16(float v) { return bf16r(1.0f / (1.0f + expf(-v))); }
-
-// One row of any width and group size (runtime bits / gs): the scalar expert gate. The
-// (group, token) pairs are spread over the lanes; within a group the sums run in input order,
-// eight codes per 16-byte load of x, so the values equal the templated path's.
-template <bool kFp16>
-MOE_D void generic_row(const uint16_t *x, int T, int Kin, const uint32_t *w, const uint16_t *s, const uint16_t *b,
-                       int bits, int gs, int lane, double *sv, uint16_t *y) {
-    const int lper = bits == 2 ? 4 : (bits == 4 ? 3 : 2), ng = Kin / gs;   // log2(32 / bits)
-    const uint32_t mask = (1u << bits) - 1u;
-#pragma unroll 1
-    for (int t0 = 0; t0 < T; t0 += kLinTok) {
-        const int nt = min(kLinTok, T - t0);
-#pragma unroll 1
-        for (int it = lane; it < ng * nt; it += 32) {
-            const int g = it % ng, j = it / ng;
-            const uint16_t *xg = x + (size_t)(t0 + j) * Kin + (size_t)g * gs;
-            float acc = 0.f, xs = 0.f;
-#pragma unroll 1
-            for (int k0 = 0; k0 < gs; k0 += 8) {
-                const uint4 v = __ldg(reinterpret_cast<const uint4 *>(xg + k0));
-                const uint32_t pk[4] = {v.x, v.y, v.z, v.w};
-                uint32_t wd[8];
-#pragma unroll
-                for (int i = 0; i < 8; ++i) wd[i] = __ldg(w + (((size_t)g * gs + k0 + i) >> lper));
-#pragma unroll
-                for (int i = 0; i < 8; ++i) {
-                    const int k = g * gs + k0 + i;
-                    const float xv = __uint_as_float((i & 1) ? (pk[i >> 1] & 0xffff0000u) : (pk[i >> 1] << 16));
-                    const uint32_t sh = (uint32_t)(bits * (k & ((1 << lper) - 1)));
-                    acc = fmaf(code_f32((wd[i] >> sh) & mask), xv, acc);
-                    xs += xv;
-                }
-            }
-            sv[j * ng + g] = group_value<kFp16>(s, b, g, acc, xs);
-        }
-        __syncwarp();
-        if (lane < nt) y[t0 + lane] = row_out(sum_in_order(sv + lane * ng, ng));
-        __syncwarp();
-    }
-}
-
-// y[t][n] = bf16(float(row total)) (gl == nullptr), or bf16(bf16(sigmoid(gl[t])) * that)
+// y[t][n] = bf16(float(row total)) (gl == nullptr), or bf16(bf16(sigmoid(gl[t])) * that), or,
+// with yf != nullptr, float(row total) to yf
 template <int kBits, int kGs, bool kFp16>
 __global__ void __launch_bounds__(kLinThreads) affine_linear_kernel(const uint16_t *__restrict__ x, int T, int Kin,
                                                                     int N, const uint32_t *__restrict__ w,
                                                                     const uint16_t *__restrict__ s,
                                                                     const uint16_t *__restrict__ b,
                                                                     const uint16_t *__restrict__ gl,
-                                                                    uint16_t *__restrict__ y) {
-    extern __shared__ double sgrp[];             // [kLinWarps][kLinTok][ng]
+                                                                    uint16_t *__restrict__ y, float *__restrict__ yf,
+                                                                    int stage) {
+    extern __shared__ __align__(16) unsigned char lin_smem_raw[];
     const int wib = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int n = blockIdx.x * kLinWarps + wib;
-    if (n >= N) return;                          // whole warps leave; no block-wide barrier follows
+    const bool active = n < N;                   // idle warps still take part in the x staging
     const int ng = Kin / kGs;
-    double *sv = sgrp + (size_t)wib * kLinTok * ng;
-    const uint32_t *const wr[1] = {w + (size_t)n * (Kin / Group<kBits, kGs>::kPer)};
-    const uint16_t *const sr[1] = {s + (size_t)n * ng};
-    const uint16_t *const br[1] = {b + (size_t)n * ng};
+    const LinSmem L = lin_smem(1, ng, T, Kin);
+    double *sv = reinterpret_cast<double *>(lin_smem_raw) + (size_t)wib * kLinTok * ng;
+    uint16_t *sx = reinterpret_cast<uint16_t *>(lin_smem_raw + L.grp);
+    const int nrow = active ? n : 0;
+    const uint32_t *const wr[1] = {w + (size_t)nrow * (Kin / Group<kBits, kGs>::kPer)};
+    const uint16_t *const sr[1] = {s + (size_t)nrow * ng};
+    const uint16_t *const br[1] = {b + (size_t)nrow * ng};
 #pragma unroll 1
     for (int t0 = 0; t0 < T; t0 += kLinTok) {
         const int nt = min(kLinTok, T - t0);
-        stage_rows<kBits, kGs, kFp16, 1>(x, Kin, t0, nt, wr, sr, br, ng, lane, sv);
-        __syncwarp();
-        if (lane < nt) {
-            const int t = t0 + lane;
-            uint16_t o = row_out(sum_in_order(sv + lane * ng, ng));
-            if (gl) o = f32_to_bf16_bits(sigmoid_bf16(bf16_bits_to_f32(gl[t])) * bf16_bits_to_f32(o));
-            y[(size_t)t * N + n] = o;
+        const uint16_t *xs = x + (size_t)t0 * Kin;
+        if (stage) {
+            __syncthreads();                     // the previous pass is done with sx
+            stage_x(sx, x, Kin, t0, nt);
+            __syncthreads();
+            xs = sx;
         }
-        __syncwarp();
+        if (active) {
+            stage_rows<kBits, kGs, kFp16, 1>(xs, Kin, nt, wr, sr, br, ng, lane, sv);
+            __syncwarp();
+            if (lane < nt) {
+                const int t = t0 + lane;
+                const double total = sum_in_order(sv + lane * ng, ng);
+                if (yf) {
+                    yf[(size_t)t * N + n] = (float)total;
+                } else {
+                    uint16_t o = row_out(total);
+                    if (gl) o = f32_to_bf16_bits(__fmul_rn(sigmoid_bf16(bf16_bits_to_f32(gl[t])), bf16_bits_to_f32(o)));
+                    y[(size_t)t * N + n] = o;
+                }
+            }
+            __syncwarp();
+        }
     }
 }
 
@@ -212,36 +90,47 @@ __global__ void __launch_bounds__(kLinThreads) gateup_swiglu_kernel(
     const uint16_t *__restrict__ sg, const uint16_t *__restrict__ bg, const uint32_t *__restrict__ wu,
     const uint16_t *__restrict__ su, const uint16_t *__restrict__ bu, const uint32_t *__restrict__ we,
     const uint16_t *__restrict__ se, const uint16_t *__restrict__ be, int ebits, int egs,
-    uint16_t *__restrict__ act, uint16_t *__restrict__ gl) {
-    extern __shared__ double sgrp[];             // [kLinWarps][2][kLinTok][ng]
+    uint16_t *__restrict__ act, uint16_t *__restrict__ gl, int stage) {
+    extern __shared__ __align__(16) unsigned char lin_smem_raw[];
     const int wib = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int i = blockIdx.x * kLinWarps + wib;
-    if (i > I) return;
-    const int ng = H / kGs;
-    double *sv = sgrp + (size_t)wib * 2 * kLinTok * ng;
-    if (i == I) {                                // the scalar expert gate
-        generic_row<kFp16>(x, T, H, we, se, be, ebits, egs, lane, sv, gl);
-        return;
-    }
+    const int ng = H / kGs, nge = H / egs;
+    const LinSmem L = lin_smem(2, max(ng, (nge + 1) / 2), T, H);
+    double *sv = reinterpret_cast<double *>(lin_smem_raw) + (size_t)wib * 2 * kLinTok * max(ng, (nge + 1) / 2);
+    uint16_t *sx = reinterpret_cast<uint16_t *>(lin_smem_raw + L.grp);
     constexpr int per = Group<kBits, kGs>::kPer;
-    const uint32_t *const wr[2] = {wg + (size_t)i * (H / per), wu + (size_t)i * (H / per)};
-    const uint16_t *const sr[2] = {sg + (size_t)i * ng, su + (size_t)i * ng};
-    const uint16_t *const br[2] = {bg + (size_t)i * ng, bu + (size_t)i * ng};
+    const int irow = i < I ? i : 0;
+    const uint32_t *const wr[2] = {wg + (size_t)irow * (H / per), wu + (size_t)irow * (H / per)};
+    const uint16_t *const sr[2] = {sg + (size_t)irow * ng, su + (size_t)irow * ng};
+    const uint16_t *const br[2] = {bg + (size_t)irow * ng, bu + (size_t)irow * ng};
 #pragma unroll 1
     for (int t0 = 0; t0 < T; t0 += kLinTok) {
         const int nt = min(kLinTok, T - t0);
-        stage_rows<kBits, kGs, kFp16, 2>(x, H, t0, nt, wr, sr, br, ng, lane, sv);
-        __syncwarp();
-        // lanes 0..nt-1 add the gate rows, lanes kLinTok..kLinTok+nt-1 the up rows
-        const int j = lane & (kLinTok - 1), m = lane / kLinTok;
-        float v = 0.f;
-        if (m < 2 && j < nt) v = bf16_bits_to_f32(row_out(sum_in_order(sv + (m * kLinTok + j) * ng, ng)));
-        const float uv = __shfl_down_sync(0xffffffffu, v, kLinTok);
-        if (lane < nt) {
-            const float gv = v;
-            act[(size_t)(t0 + lane) * I + i] = f32_to_bf16_bits(bf16r(bf16r(gv * sigmoid_bf16(gv)) * uv));
+        const uint16_t *xs = x + (size_t)t0 * H;
+        if (stage) {
+            __syncthreads();
+            stage_x(sx, x, H, t0, nt);
+            __syncthreads();
+            xs = sx;
         }
-        __syncwarp();
+        if (i == I) {                            // the scalar expert gate
+            stage_row_generic<kFp16>(xs, H, nt, we, se, be, ebits, egs, lane, sv);
+            __syncwarp();
+            if (lane < nt) gl[t0 + lane] = row_out(sum_in_order(sv + lane * nge, nge));
+            __syncwarp();
+        } else if (i < I) {
+            stage_rows<kBits, kGs, kFp16, 2>(xs, H, nt, wr, sr, br, ng, lane, sv);
+            __syncwarp();
+            // lanes 0..nt-1 add the gate rows, lanes kLinTok..kLinTok+nt-1 the up rows
+            const int j = lane & (kLinTok - 1), m = lane / kLinTok;
+            float v = 0.f;
+            if (m < 2 && j < nt) v = bf16_bits_to_f32(row_out(sum_in_order(sv + (m * kLinTok + j) * ng, ng)));
+            const float uv = __shfl_down_sync(0xffffffffu, v, kLinTok);
+            if (lane < nt)
+                act[(size_t)(t0 + lane) * I + i] =
+                    f32_to_bf16_bits(bf16r(__fmul_rn(bf16r(__fmul_rn(v, sigmoid_bf16(v))), uv)));
+            __syncwarp();
+        }
     }
 }
 
@@ -273,15 +162,15 @@ int prepare_smem(K kern, size_t bytes) {
 
 template <int kBits, int kGs, bool kFp16>
 int launch_lin_t(const void *x, int T, int Kin, int N, const void *w, const void *s, const void *b, const void *gl,
-                 void *y, cudaStream_t st) {
+                 void *y, float *yf, cudaStream_t st) {
     auto kern = affine_linear_kernel<kBits, kGs, kFp16>;
-    const size_t smem = (size_t)kLinWarps * kLinTok * (Kin / kGs) * sizeof(double);
-    int rc = prepare_smem(kern, smem);
+    const LinSmem L = lin_smem(1, Kin / kGs, T, Kin);
+    int rc = prepare_smem(kern, L.total());
     if (rc) return rc;
-    kern<<<(N + kLinWarps - 1) / kLinWarps, kLinThreads, smem, st>>>(
+    kern<<<(N + kLinWarps - 1) / kLinWarps, kLinThreads, L.total(), st>>>(
         static_cast<const uint16_t *>(x), T, Kin, N, static_cast<const uint32_t *>(w),
         static_cast<const uint16_t *>(s), static_cast<const uint16_t *>(b), static_cast<const uint16_t *>(gl),
-        static_cast<uint16_t *>(y));
+        static_cast<uint16_t *>(y), yf, L.xbytes > 0);
     MOE_CUDA_TRY(cudaGetLastError());
     return MOE_OK;
 }
@@ -297,15 +186,15 @@ struct GateUpArgs {
 template <int kBits, int kGs, bool kFp16>
 int launch_gateup_t(const GateUpArgs &a, cudaStream_t st) {
     auto kern = gateup_swiglu_kernel<kBits, kGs, kFp16>;
-    const int ng = std::max(a.H / kGs, a.H / a.egs);
-    const size_t smem = (size_t)kLinWarps * 2 * kLinTok * ng * sizeof(double);
-    int rc = prepare_smem(kern, smem);
+    const LinSmem L = lin_smem(2, std::max(a.H / kGs, (a.H / a.egs + 1) / 2), a.T, a.H);
+    int rc = prepare_smem(kern, L.total());
     if (rc) return rc;
     auto u16 = [](const void *p) { return static_cast<const uint16_t *>(p); };
     auto u32 = [](const void *p) { return static_cast<const uint32_t *>(p); };
-    kern<<<(a.I + 1 + kLinWarps - 1) / kLinWarps, kLinThreads, smem, st>>>(
+    kern<<<(a.I + 1 + kLinWarps - 1) / kLinWarps, kLinThreads, L.total(), st>>>(
         u16(a.x), a.T, a.H, a.I, u32(a.wg), u16(a.sg), u16(a.bg), u32(a.wu), u16(a.su), u16(a.bu), u32(a.we),
-        u16(a.se), u16(a.be), a.ebits, a.egs, static_cast<uint16_t *>(a.act), static_cast<uint16_t *>(a.gl));
+        u16(a.se), u16(a.be), a.ebits, a.egs, static_cast<uint16_t *>(a.act), static_cast<uint16_t *>(a.gl),
+        L.xbytes > 0);
     MOE_CUDA_TRY(cudaGetLastError());
     return MOE_OK;
 }
@@ -327,8 +216,8 @@ int dispatch(int bits, int gs, int sb_fp16, A &&...args) {
 template <int kBits, int kGs, bool kFp16>
 struct LinRun {
     static int run(const void *x, int T, int Kin, int N, const void *w, const void *s, const void *b, const void *gl,
-                   void *y, cudaStream_t st) {
-        return launch_lin_t<kBits, kGs, kFp16>(x, T, Kin, N, w, s, b, gl, y, st);
+                   void *y, float *yf, cudaStream_t st) {
+        return launch_lin_t<kBits, kGs, kFp16>(x, T, Kin, N, w, s, b, gl, y, yf, st);
     }
 };
 
@@ -339,12 +228,22 @@ struct GateUpRun {
 
 }  // namespace
 
+int moe_qlin_check(const char *who, const void *x, int T, int Kin, int N, const void *w, const void *s,
+                   const void *b, int bits, int gs, const void *y) {
+    return check_lin(who, x, T, Kin, N, w, s, b, bits, gs, y);
+}
+
+int moe_qlin_linear(const void *x, int T, int Kin, int N, const void *w, const void *s, const void *b, int bits,
+                    int gs, int sb_fp16, const void *gl, void *y, float *yf, cudaStream_t st) {
+    return dispatch<LinRun>(bits, gs, sb_fp16, x, T, Kin, N, w, s, b, gl, y, yf, st);
+}
+
 extern "C" int moe_affine_linear(const void *x, int T, int Kin, int N, const void *w, const void *scales,
                                  const void *biases, int bits, int group_size, int sb_fp16, void *y, void *stream) {
     int rc = check_lin("affine_linear", x, T, Kin, N, w, scales, biases, bits, group_size, y);
     if (rc) return rc;
     return dispatch<LinRun>(bits, group_size, sb_fp16, x, T, Kin, N, w, scales, biases, nullptr, y,
-                            as_stream(stream));
+                            static_cast<float *>(nullptr), as_stream(stream));
 }
 
 extern "C" size_t moe_shared_expert_workspace_bytes(int T, int H, int I) {
@@ -372,5 +271,6 @@ extern "C" int moe_shared_expert(const void *x, int T, int H, int I, const void 
     cudaStream_t st = as_stream(stream);
     const GateUpArgs a{x, T, H, I, wg, sg, bg, wu, su, bu, weg, seg, beg, gate_bits, gate_group_size, act, gl};
     if ((rc = dispatch<GateUpRun>(bits, group_size, sb_fp16, a, st))) return rc;
-    return dispatch<LinRun>(bits, group_size, sb_fp16, act, T, I, H, wd, sd, bd, gl, y, st);
+    return dispatch<LinRun>(bits, group_size, sb_fp16, act, T, I, H, wd, sd, bd, gl, y, static_cast<float *>(nullptr),
+                            st);
 }

@@ -235,6 +235,62 @@ def shared_expert(x: torch.Tensor, gate: QMatrix, up: QMatrix, down: QMatrix, ex
     return y
 
 
+# ----------------------------------------------------------------------------- hyper-connections
+
+_HWS: dict = {}
+
+
+def hc_mix(h: torch.Tensor, norm_w: torch.Tensor, down: QMatrix, up: QMatrix, inject=None, *, write=None,
+           eps: float = 1e-6, hc: int = 4, stream=None):
+    """run_hc (kernels.cpp:1363-1560) for quantised mixer matrices: returns (mixed [T, H],
+    written [T, hc*H], inj [T, hc]). h: [..., hc*H] bf16; write: (branch [..., H],
+    gate [..., hc]) or None (then written is h itself); inject None = the mixer without inject
+    weights (inj zeros). T <= 16 rows follow the reference's decode rounding, more rows its
+    prefill rounding."""
+    _need(h, "h", (torch.bfloat16,))
+    dev = h.device
+    R, W = _lin_dims("down", down, dev)
+    if _lin_dims("up", up, dev) != (W, R):
+        raise ValueError("up must be [hc*H, R] for down [R, hc*H]")
+    if inject is not None and _lin_dims("inject", inject, dev) != (hc, W):
+        raise ValueError(f"inject must be [{hc}, {W}]")
+    if h.shape[-1] != W:
+        raise ValueError(f"h has shape {tuple(h.shape)}, expected [..., {W}]")
+    _need(norm_w, "norm_w", (torch.bfloat16,), dev)
+    if norm_w.numel() != W:
+        raise ValueError(f"norm_w has {norm_w.numel()} values, expected {W}")
+    H = W // hc
+    T = h.numel() // W
+    mixed = torch.empty((T, H), dtype=torch.bfloat16, device=dev)
+    inj = torch.empty((T, hc), dtype=torch.bfloat16, device=dev)
+    branch = gate = written = None
+    if write is not None:
+        branch, gate = write
+        _need(branch, "branch", (torch.bfloat16,), dev)
+        _need(gate, "gate", (torch.bfloat16,), dev)
+        if branch.numel() != T * H or gate.numel() != T * hc:
+            raise ValueError("write tensors must be [T, H] and [T, hc]")
+        written = torch.empty((T, W), dtype=torch.bfloat16, device=dev)
+    need = call("moe_hc_workspace_bytes", T, hc, H, R)
+    key = (dev, stream)
+    ws = _HWS.get(key)
+    if ws is None or ws.numel() < need:
+        ws = torch.empty(need, dtype=torch.uint8, device=dev)
+        _HWS[key] = ws
+    i_w = i_s = i_b = None
+    i_bits, i_gs = 8, 64
+    if inject is not None:
+        i_w, i_s, i_b, i_bits, i_gs = inject.w, inject.s, inject.b, inject.bits, inject.group_size
+    if len({down.sb_fp16, up.sb_fp16} | ({inject.sb_fp16} if inject is not None else set())) != 1:
+        raise ValueError("mixer matrices must share one scale dtype")
+    call("moe_hc_mix", h.data_ptr(), T, hc, H, R, _ptr(branch), _ptr(gate), norm_w.data_ptr(), float(eps),
+         down.w.data_ptr(), down.s.data_ptr(), down.b.data_ptr(), down.bits, down.group_size, up.w.data_ptr(),
+         up.s.data_ptr(), up.b.data_ptr(), up.bits, up.group_size, _ptr(i_w), _ptr(i_s), _ptr(i_b), i_bits, i_gs,
+         down.sb_fp16, _ptr(written), mixed.data_ptr(), inj.data_ptr(), ws.data_ptr(), ws.numel(),
+         _stream(stream))
+    return mixed, (written if written is not None else h.reshape(T, W)), inj
+
+
 # ----------------------------------------------------------------------------- fused layer
 
 _DWS: dict = {}

@@ -408,6 +408,116 @@ int orc_shared_expert(const uint16_t *x, int T, int H, int I, const uint32_t *wg
     return rc;
 }
 
+/* ------------------------------------------------------------------------------------ */
+/* hyper-connection mixer before the MoE block (Qwen38Engine::run_hc, kernels.cpp:1363-1560) */
+/* ------------------------------------------------------------------------------------ */
+
+/* row totals of an affine-quantised matrix [N, Kin] times x [Kin] (floats), double results */
+static void qrows(const uint32_t *w, const uint16_t *s, const uint16_t *b, int sb_fp16, int bits, int gs,
+                  const float *x, int Kin, int N, double *out) {
+    const size_t wrow = (size_t)Kin / (32 / bits), srow = (size_t)Kin / gs;
+#pragma omp parallel for schedule(static)
+    for (int n = 0; n < N; ++n) out[n] = qdot_row(w + n * wrow, s + n * srow, b + n * srow, sb_fp16, x, Kin, bits, gs);
+}
+
+/*
+ * One call of run_hc for T rows with hc_count HC streams of `H` values and low rank R:
+ *   written = h (+ bf16(branch[t] * gate[t][c]) on stream c, rounded sums)   kernels.cpp:1380-1386
+ *   normed  = per-stream RMS norm * (1 + norm_w)                              kernels.cpp:1042-1061
+ *   d = down(normed) [R], v = d / HC, mix = silu(v)                           kernels.cpp:1387-1390
+ *   u = up(mix) [HC*H], mixed[h] = mean_c sigmoid(u[c*H+h]) * normed[c*H+h]   kernels.cpp:1390-1393
+ *   inj = 2 * sigmoid(inject(normed) / HC) [HC]                               kernels.cpp:1397-1399
+ * Roundings follow the reference's two quantised paths: T <= 16 (the fused decode kernels,
+ * kernels.cpp:1404-1516) keeps d, u and the inject dot products unrounded and rounds mix,
+ * mixed and inj once; T > 16 (the prefill path, kernels.cpp:1518-1559 and the tail/inject
+ * kernel at 788-846) rounds d and u to bf16, evaluates silu(v) and the stream sum with a bf16
+ * rounding after every op, and rounds the inject value twice before its sigmoid.
+ * RMS statistics: double sum of squares, rs = float(1 / sqrt(ss / H + eps)),
+ * normed = bf16(float(x * rs) * (1 + w)).
+ * branch/gate NULL = no write; inject NULL = the use_combine=False mixer (inj zeros).
+ */
+int orc_hc_mix(const uint16_t *h, int T, int HC, int H, int R, const uint16_t *branch, const uint16_t *gate,
+               const uint16_t *norm_w, float eps, const uint32_t *wd, const uint16_t *sd, const uint16_t *bd,
+               int dbits, int dgs, const uint32_t *wu, const uint16_t *su, const uint16_t *bu, int ubits, int ugs,
+               const uint32_t *wi, const uint16_t *si, const uint16_t *bi, int ibits, int igs, int sb_fp16,
+               uint16_t *written, uint16_t *normed_out, uint16_t *mixed, uint16_t *inj) {
+    if (T <= 0 || HC <= 0 || H <= 0 || R <= 0) return -22;
+    const int W = HC * H, prefill = T > 16;
+    float *x = (float *)malloc(sizeof(float) * W), *nf = (float *)malloc(sizeof(float) * W);
+    float *mf = (float *)malloc(sizeof(float) * R);
+    double *dv = (double *)malloc(sizeof(double) * (W > R ? W : R)), *iv = (double *)malloc(sizeof(double) * HC);
+    if (!x || !nf || !mf || !dv || !iv) { free(x); free(nf); free(mf); free(dv); free(iv); return -12; }
+    for (int t = 0; t < T; ++t) {
+        const uint16_t *hr = h + (size_t)t * W;
+        for (int c = 0; c < HC; ++c)
+            for (int i = 0; i < H; ++i) {
+                const int n = c * H + i;
+                float v = bf16_to_f32(hr[n]);
+                if (branch && gate) {
+                    float p = bf(bf16_to_f32(branch[(size_t)t * H + i]) * bf16_to_f32(gate[(size_t)t * HC + c]));
+                    v = bf(v + p);
+                }
+                x[n] = v;
+                if (written) written[(size_t)t * W + n] = f32_to_bf16(v);
+            }
+        for (int c = 0; c < HC; ++c) {
+            double ss = 0.0;
+            for (int i = 0; i < H; ++i) ss += (double)x[c * H + i] * (double)x[c * H + i];
+            const float rs = (float)(1.0 / sqrt(ss / H + (double)eps));
+            for (int i = 0; i < H; ++i) {
+                const int n = c * H + i;
+                const float y = x[n] * rs;
+                nf[n] = bf(y * (1.0f + bf16_to_f32(norm_w[n])));
+                if (normed_out) normed_out[(size_t)t * W + n] = f32_to_bf16(nf[n]);
+            }
+        }
+        qrows(wd, sd, bd, sb_fp16, dbits, dgs, nf, W, R, dv);
+        for (int r = 0; r < R; ++r) {
+            if (prefill) {
+                const float v = bf(bf((float)dv[r]) / (float)HC);
+                mf[r] = bf(v * bf(sigmoidf_ref(v)));
+            } else {
+                const float v = (float)dv[r] / (float)HC;
+                mf[r] = bf(v * sigmoidf_ref(v));
+            }
+        }
+        qrows(wu, su, bu, sb_fp16, ubits, ugs, mf, R, W, dv);
+        for (int i = 0; i < H; ++i) {
+            float acc = 0.f;
+            for (int c = 0; c < HC; ++c) {
+                const int n = c * H + i;
+                if (prefill) {
+                    const float p = bf(bf(sigmoidf_ref(bf((float)dv[n]))) * nf[n]);
+                    acc = c == 0 ? p : bf(acc + p);
+                } else {
+                    const float p = sigmoidf_ref((float)dv[n]) * nf[n];
+                    acc = c == 0 ? p : acc + p;
+                }
+            }
+            mixed[(size_t)t * H + i] = f32_to_bf16(prefill ? acc * (1.0f / (float)HC) : acc / (float)HC);
+        }
+        if (inj) {
+            if (wi) qrows(wi, si, bi, sb_fp16, ibits, igs, nf, W, HC, iv);
+            for (int c = 0; c < HC; ++c) {
+                float o = 0.f;
+                if (wi && prefill) {
+                    const float q = bf(bf((float)iv[c]) / (float)HC);
+                    o = 2.0f * bf(sigmoidf_ref(q));
+                } else if (wi) {
+                    o = 2.0f * sigmoidf_ref((float)iv[c] / (float)HC);
+                }
+                inj[(size_t)t * HC + c] = f32_to_bf16(o);
+            }
+        }
+    }
+    free(x);
+    free(nf);
+    free(mf);
+    free(dv);
+    free(iv);
+    return 0;
+}
+
 /* number of OpenMP threads the oracle uses (1 when built without OpenMP) */
 int orc_num_threads(void) {
 #ifdef _OPENMP

@@ -41,9 +41,12 @@ def lib() -> ctypes.CDLL:
         L.orc_f32_to_bf16.argtypes = [ctypes.c_float]
         L.orc_f32_to_bf16.restype = ctypes.c_uint16
         L.orc_num_threads.restype = I
+        L.orc_hc_mix.argtypes = [ctypes.c_void_p, I, I, I, I, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
+                                 ctypes.c_float] + [ctypes.c_void_p] * 3 + [I, I] + [ctypes.c_void_p] * 3 + [I, I] + \
+            [ctypes.c_void_p] * 3 + [I, I, I] + [ctypes.c_void_p] * 4
         L.orc_set_num_threads.argtypes = [I]
         for f in ("orc_router_logits", "orc_softmax_topk", "orc_topm_sorted", "orc_experts",
-                  "orc_affine_linear", "orc_shared_expert"):
+                  "orc_affine_linear", "orc_shared_expert", "orc_hc_mix"):
             getattr(L, f).restype = I
         _LIB = L
     return _LIB
@@ -181,6 +184,37 @@ def shared_expert(x_bf16, gate, up, down, expert_gate, bits: int = 4, group_size
                                  _p(bd), bits, group_size, _p(we), _p(se), _p(be), gate_bits, gate_group_size,
                                  int(sb_fp16), _p(y), _p(act), _p(o)), "shared_expert")
     return {"y": y, "act": act, "o": o}
+
+
+
+# ---------------------------------------------------------------- hyper-connection mixer
+
+def hc_mix(h_bf16, norm_w, down, up, inject=None, branch=None, gate=None, hc: int = 4, eps: float = 1e-6,
+           bits: int = 8, group_size: int = 64, sb_fp16: bool = False):
+    """run_hc (kernels.cpp:1363-1560) for T rows of HC*H stream values. down/up/inject:
+    (codes, scales, biases) with `bits` / `group_size`; inject None = the mixer without inject
+    weights; branch [T, H] and gate [T, HC] bf16 = the write. Returns dict(mixed=[T, H],
+    written=[T, HC*H], normed=[T, HC*H], inj=[T, HC]) as bf16 bits."""
+    wd, sd, bd = (np.ascontiguousarray(a) for a in down)
+    wu, su, bu = (np.ascontiguousarray(a) for a in up)
+    R = wd.shape[0]
+    W = wu.shape[0]
+    H = W // hc
+    h = np.ascontiguousarray(h_bf16, dtype=np.uint16).reshape(-1, W)
+    T = h.shape[0]
+    wi = si = bi = None
+    if inject is not None:
+        wi, si, bi = (np.ascontiguousarray(a) for a in inject)
+    br = None if branch is None else np.ascontiguousarray(branch, dtype=np.uint16).reshape(T, H)
+    gt = None if gate is None else np.ascontiguousarray(gate, dtype=np.uint16).reshape(T, hc)
+    nw = np.ascontiguousarray(norm_w, dtype=np.uint16).reshape(-1)
+    out = {"mixed": np.empty((T, H), np.uint16), "written": np.empty((T, W), np.uint16),
+           "normed": np.empty((T, W), np.uint16), "inj": np.empty((T, hc), np.uint16)}
+    _chk(lib().orc_hc_mix(_p(h), T, hc, H, R, _p(br), _p(gt), _p(nw), eps, _p(wd), _p(sd), _p(bd), bits, group_size,
+                          _p(wu), _p(su), _p(bu), bits, group_size, _p(wi), _p(si), _p(bi), bits, group_size,
+                          int(sb_fp16), _p(out["written"]), _p(out["normed"]), _p(out["mixed"]), _p(out["inj"])),
+         "hc_mix")
+    return out
 
 
 def ref_lru_lib(version: int = 1):

@@ -15,14 +15,14 @@ def pytest_configure(config):
     config.addinivalue_line("markers", "gpu: needs a CUDA device (B200, sm_100a)")
 
 
-def load_moe_fixture():
-    """The reference's golden MoE tensors (tests/golden/moe_fixture.safetensors) as numpy;
-    bf16 tensors come back as uint16 bit patterns, uint32 as uint32."""
+def load_moe_fixture(name: str = "moe_fixture.safetensors"):
+    """The reference's golden tensors (tests/golden/<name>) as numpy; bf16 tensors come back
+    as uint16 bit patterns, uint32 as uint32."""
     import torch
     from safetensors.torch import load_file
 
     out = {}
-    for k, v in load_file(os.path.join(GOLDEN, "moe_fixture.safetensors")).items():
+    for k, v in load_file(os.path.join(GOLDEN, name)).items():
         if v.dtype == torch.bfloat16:
             out[k] = v.view(torch.int16).numpy().view(np.uint16).copy()
         elif v.dtype == torch.uint32:
@@ -35,6 +35,11 @@ def load_moe_fixture():
 @pytest.fixture(scope="session")
 def moe_fixture():
     return load_moe_fixture()
+
+
+@pytest.fixture(scope="session")
+def hc_fixture():
+    return load_moe_fixture("hc_fixture.safetensors")
 
 
 @pytest.fixture(scope="session")

@@ -13,6 +13,16 @@ moe_fixture.safetensors
     prefill input x_pre [1,20,256]; MLX outputs inds_*, scores_*, sh_* (shared expert) and
     y_* (block output). Copied byte-for-byte, no recomputation.
 
+hc_fixture.safetensors
+    The `hc.*` and `pred_next.*` tensors of the same file (gen_fixtures.py:105-177,
+    685-705; checked by test_kernels.cpp:57-92,216-283): the hyper-connection mixer in front
+    of the MoE block with hidden 2560, 4 streams, low rank 320, 8-bit affine g64 down / up /
+    inject matrices; inputs h_in [1,rows,10240], branch br_in [1,rows,2560] and gate gt_in
+    [1,rows,4] for rows 1, 8 and 18; MLX outputs m_* (mixed input), h_write (written
+    stream), inj_* (inject weights), mix_* (the use_combine=False mixer), and the next-layer
+    top-12 predictions of an 8-bit 64-expert gate on m. h_nowrite and h_mix_write are left
+    out when they equal h_in / h_write (the generator asserts which).
+
 lru_trace.npz
     Hit/miss/slot/LRU-order trace of the reference's own LRU slot cache
     (mlx-qwen38/expert_io.c, compiled unmodified by oracle/Makefile into
@@ -44,6 +54,25 @@ def make_moe_fixture(ref_root: str) -> None:
     dst = os.path.join(HERE, "moe_fixture.safetensors")
     save_file(keep, dst, metadata={"source": "mlx-qwen38/cpp/tests/fixtures.safetensors (moe.* keys)"})
     print(f"wrote {dst}: {len(keep)} tensors, {os.path.getsize(dst)} bytes")
+
+
+def make_hc_fixture(ref_root: str) -> None:
+    import torch
+    from safetensors.torch import load_file, save_file
+
+    src = os.path.join(ref_root, "mlx-qwen38", "cpp", "tests", "fixtures.safetensors")
+    allt = load_file(src)
+    keep = {k: v.contiguous() for k, v in allt.items() if k.startswith(("hc.", "pred_next."))}
+    dropped = []
+    for tag in ("r1", "r8", "r18"):
+        for k, same in ((f"hc.{tag}.h_nowrite", f"hc.{tag}.h_in"), (f"hc.{tag}.h_mix_write", f"hc.{tag}.h_write")):
+            if torch.equal(keep[k].view(torch.int16), keep[same].view(torch.int16)):
+                del keep[k]
+                dropped.append(f"{k}=={same}")
+    dst = os.path.join(HERE, "hc_fixture.safetensors")
+    save_file(keep, dst, metadata={"source": "mlx-qwen38/cpp/tests/fixtures.safetensors (hc.*, pred_next.* keys)",
+                                   "dropped_equal": ",".join(dropped)})
+    print(f"wrote {dst}: {len(keep)} tensors, {os.path.getsize(dst)} bytes; dropped {dropped}")
 
 
 def lru_sequence(seed: int, n_layers: int, steps: int, E: int, K: int, M: int):
@@ -158,6 +187,7 @@ def main() -> int:
     ap.add_argument("--ref", default=os.environ.get("MOE_REF_ROOT", "/root/reference"))
     args = ap.parse_args()
     make_moe_fixture(args.ref)
+    make_hc_fixture(args.ref)
     lib = os.path.join(ROOT, "oracle", "_ref", "libexpert_io_ref.so")
     if not os.path.exists(lib):
         print("oracle/_ref/libexpert_io_ref.so missing: run `make -C oracle` first", file=sys.stderr)
