@@ -45,11 +45,12 @@ def parse():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
-    ap.add_argument("--config", choices=["c1", "c2", "c3", "c3n", "c4", "p1"], default="c1",
+    ap.add_argument("--config", choices=["c1", "c2", "c3", "c3n", "c4", "p1", "f3"], default="c1",
                     help="c1: resident stack (the headline); c2: offload stack with the LRU slot caches; "
                          "c3: 2048-token prefill through the resident 28-layer stack; c3n: the Nemotron-shaped "
                          "prefill layer (240 experts, top-9, 1024 tokens); c4: expert-parallel decode (experts "
-                         "split across the ranks); p1: the P1 I/O scheduler filling c2-shaped expert slots")
+                         "split across the ranks); p1: the P1 I/O scheduler filling c2-shaped expert slots; f3: the "
+                         "hyper-connection mixer + shared expert in front of each of the 28 MoE blocks, decode")
     ap.add_argument("--batch", type=int, default=0, help="c4: tokens per decode step (default: one per GPU)")
     ap.add_argument("--layers", type=int, default=0,
                     help="profiling aid: run only the first N layers of the stack (0 = all 28)")
@@ -392,6 +393,122 @@ def run_p1(args, rank: int, world: int, local_rank: int) -> None:
     print(json.dumps(line), flush=True)
 
 
+def run_f3(args, rank: int, world: int, local_rank: int) -> None:
+    """The step in front of every MoE block, decode (one token): the hyper-connection mixer
+    (run_hc with a write: 4 streams of H = 3072, rank 320, 8-bit g64 down / up / inject) and the
+    shared expert on its output (gate / up / down 4-bit g64 with I = 768, an 8-bit scalar gate),
+    for 28 layers with their own weights (347 MB, beyond L2). Five launches per layer, captured
+    as one CUDA graph per step. `value` = tokens/s through the 28 layers; roofline = algorithmic
+    weight bytes per token / step time against the HBM peak (the kernels are latency-bound at one
+    token); e2e adds the pinned host -> device copy of the token's streams and the read-back of
+    the last layer's shared output."""
+    import numpy as np
+    import torch
+
+    from moe_offload_b200 import ops
+    from moe_offload_b200.ops import QMatrix
+
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    L, HC, H, R, I = 28, 4, 3072, 320, 768
+    g = torch.Generator(device=dev)
+    g.manual_seed(3)
+
+    def qm(N, K, bits, scale):
+        w = torch.randint(-(2 ** 31), 2 ** 31 - 1, (N, K * bits // 32), dtype=torch.int32, device=dev, generator=g)
+        sc = (torch.rand((N, K // 64), device=dev, generator=g) * scale + scale / 10).to(torch.bfloat16)
+        b = (torch.randn((N, K // 64), device=dev, generator=g) * scale * 4).to(torch.bfloat16)
+        return QMatrix(w, sc, b, bits, 64)
+
+    layers = []
+    for _ in range(L):
+        layers.append({"nw": (torch.randn(HC * H, device=dev, generator=g) * 0.05).to(torch.bfloat16),
+                       "down": qm(R, HC * H, 8, 2e-4), "up": qm(HC * H, R, 8, 2e-3), "inj": qm(HC, HC * H, 8, 2e-4),
+                       "sg": qm(I, H, 4, 2e-3), "su": qm(I, H, 4, 2e-3), "sd": qm(H, I, 4, 2e-3),
+                       "se": qm(1, H, 8, 2e-4)})
+    wbytes = sum(m.w.numel() * 4 + m.s.numel() * 4 for lay in layers for m in lay.values() if isinstance(m, QMatrix))
+    h = (torch.randn((1, HC * H), device=dev, generator=g) * 0.3).to(torch.bfloat16)
+    br = (torch.randn((1, H), device=dev, generator=g) * 0.3).to(torch.bfloat16)
+    gt = (torch.randn((1, HC), device=dev, generator=g) * 0.5).to(torch.bfloat16)
+    sh = torch.empty((1, H), dtype=torch.bfloat16, device=dev)
+    st = torch.cuda.Stream(dev)
+
+    def step():
+        for lay in layers:
+            mixed, _, _ = ops.hc_mix(h, lay["nw"], lay["down"], lay["up"], lay["inj"], write=(br, gt), stream=st)
+            ops.shared_expert(mixed, lay["sg"], lay["su"], lay["sd"], lay["se"], y=sh, stream=st)
+
+    with torch.cuda.stream(st):
+        step()
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=st):
+            step()
+        for _ in range(args.warmup):
+            graph.replay()
+        torch.cuda.synchronize()
+        clk = ClockSampler(local_rank)
+        clk.start()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(st)
+        for _ in range(args.steps):
+            graph.replay()
+        e1.record(st)
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / args.steps
+        e2e = None
+        if not args.no_e2e:
+            hp = torch.empty((1, HC * H), dtype=torch.bfloat16).pin_memory()
+            hp.copy_(h.cpu())
+            op = torch.empty((1, H), dtype=torch.bfloat16).pin_memory()
+            t0 = time.perf_counter()
+            for _ in range(args.steps):
+                h.copy_(hp, non_blocking=True)
+                graph.replay()
+                op.copy_(sh, non_blocking=True)
+                st.synchronize()
+            dt = time.perf_counter() - t0
+            e2e = {"value": round(args.steps / dt, 2), "unit": "tok/s", "h2d_bytes_per_step": hp.numel() * 2,
+                   "d2h_bytes_per_step": op.numel() * 2}
+        clocks = clk.stop()
+    peak, src = peaks()
+    achieved = wbytes / (ms / 1000.0) / 1e9
+    cpu = None
+    if not args.no_cpu:
+        from oracle import oracle as orc
+        rng = np.random.default_rng(4)
+        lay = layers[0]
+        tonp = lambda m: (m.w.cpu().numpy().view(np.uint32), m.s.view(torch.int16).cpu().numpy().view(np.uint16),
+                          m.b.view(torch.int16).cpu().numpy().view(np.uint16))
+        nw = lay["nw"].view(torch.int16).cpu().numpy().view(np.uint16)
+        mats = {k: tonp(lay[k]) for k in ("down", "up", "inj", "sg", "su", "sd", "se")}
+        hx = h.view(torch.int16).cpu().numpy().view(np.uint16)
+        bx = br.view(torch.int16).cpu().numpy().view(np.uint16)
+        gx = gt.view(torch.int16).cpu().numpy().view(np.uint16)
+        orc.set_threads(os.cpu_count() or 1)
+        n, t0 = 0, time.perf_counter()
+        while time.perf_counter() - t0 < 8.0:
+            o = orc.hc_mix(hx, nw, mats["down"], mats["up"], mats["inj"], branch=bx, gate=gx)
+            orc.shared_expert(o["mixed"], mats["sg"], mats["su"], mats["sd"], mats["se"])
+            n += 1
+        per = (time.perf_counter() - t0) / n
+        cpu = {"value": round(1.0 / (L * per), 3), "unit": "tok/s", "cores": orc.num_threads(), "kind": "port",
+               "sample": f"{n} token-layers (mixer + shared expert of one layer) in 8 s, extrapolated x{L}; "
+                         "C restatement"}
+    line = {"metric": "MoE-block front (hyper-connection mixer + shared expert) decode tok/s, 28 layers",
+            "value": round(1000.0 / ms, 2), "unit": "tok/s", "n_gpus": 1, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "u8/u4 codes x bf16 -> f32/f64", "data": "synthetic",
+            "config": {"workload": "f3_hc4x3072_r320_shared768_28layers", "layers": L, "streams": HC, "hidden": H,
+                       "rank": R, "shared_inter": I, "tokens": 1, "l2": "weights of 28 layers (347 MB) > L2"},
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 2), "peak": peak, "unit": "GB/s",
+                         "frac": round(achieved / peak, 4), "traffic": None,
+                         "algorithmic_bytes_per_step": wbytes, "peak_source": src},
+            "clocks": clocks, "gpu_launches": 5 * L * args.steps, "e2e": e2e, "cpu_baseline": cpu}
+    del graph
+    print(json.dumps(line), flush=True)
+
+
 def run_c2(args, rank: int, world: int, local_rank: int) -> None:
     """the 28 x 512 x top-10 stack with the offload cache on (layer 0
     pinned, 102 slots per cached layer, experts in a pinned host pool, synthetic Zipf(1.1)
@@ -719,6 +836,8 @@ def main() -> int:
             run_c2(args, rank, world, local_rank)
         elif args.config == "p1":
             run_p1(args, rank, world, local_rank)
+        elif args.config == "f3":
+            run_f3(args, rank, world, local_rank)
         elif args.config in ("c3", "c3n"):
             run_c3(args, rank, world, local_rank)
         elif args.config == "c4":

@@ -12,9 +12,10 @@
 // arithmetic of qlinear.cuh; the RMS statistic is a double sum of squares with
 // rs = float(1 / sqrt(ss / H + eps)).
 //
-// Launches: norm (one block per row and stream) -> down and inject rows (float totals) ->
-// activation (silu, inject sigmoid) -> up rows of the four streams of one hidden index in one
-// warp, with the stream sum in its epilogue.
+// Launches (programmatic dependent launch, each kernel loading its weights before it waits on
+// the previous one): norm (one block per row and stream) -> down and inject rows in one launch
+// (float totals) -> up rows of the four streams of each hidden index, the silu of the down
+// totals formed while staging them and the stream sum and inject sigmoid in the epilogue.
 #include <cstdint>
 #include <utility>
 
@@ -46,6 +47,8 @@ __global__ void __launch_bounds__(kNormThreads) hc_norm_kernel(const uint16_t *_
     __shared__ float srs;
     const int c = blockIdx.x, t = blockIdx.y, W = kHc * H;
     const size_t base = (size_t)t * W + (size_t)c * H;
+    pdl_launch_dependents();
+    pdl_wait();                                  // h, branch and gate come from earlier kernels
     const float gv = branch ? bf16_bits_to_f32(ldu16(gate + (size_t)t * kHc + c)) : 0.f;
     double ss = 0.0;
     for (int i = threadIdx.x; i < H; i += kNormThreads) {
@@ -76,137 +79,111 @@ __global__ void __launch_bounds__(kNormThreads) hc_norm_kernel(const uint16_t *_
     }
 }
 
-// mix = silu(d / HC) [T, R] and inj = 2 * sigmoid(iv / HC) [T, HC] in the row count's regime
-__global__ void hc_act_kernel(const float *__restrict__ dv, const float *__restrict__ iv, int T, int R, int prefill,
-                              uint16_t *__restrict__ mix, uint16_t *__restrict__ inj) {
-    const int n = T * R, ni = T * kHc;
-    for (int k = blockIdx.x * blockDim.x + threadIdx.x; k < n + ni; k += gridDim.x * blockDim.x) {
-        if (k < n) {
-            const float d = dv[k];
-            float o;
-            if (prefill) {
-                const float v = bf16r(__fdiv_rn(bf16r(d), (float)kHc));
-                o = __fmul_rn(v, sigmoid_bf16(v));
-            } else {
-                const float v = __fdiv_rn(d, (float)kHc);
-                o = __fmul_rn(v, sigmoidf(v));
-            }
-            mix[k] = f32_to_bf16_bits(o);
-        } else if (inj) {
-            const int q = k - n;
-            float o = 0.f;
-            if (iv) {
-                if (prefill) o = __fmul_rn(2.0f, sigmoid_bf16(bf16r(__fdiv_rn(bf16r(iv[q]), (float)kHc))));
-                else o = __fmul_rn(2.0f, sigmoidf(__fdiv_rn(iv[q], (float)kHc)));
-            }
-            inj[q] = f32_to_bf16_bits(o);
-        }
+// mix = silu(d / HC) in the row count's regime
+MOE_D float hc_mix_value(float d, int prefill) {
+    if (prefill) {
+        const float v = bf16r(__fdiv_rn(bf16r(d), (float)kHc));
+        return __fmul_rn(v, sigmoid_bf16(v));
     }
+    const float v = __fdiv_rn(d, (float)kHc);
+    return __fmul_rn(v, sigmoidf(v));
 }
 
-// mixed[t][h] = mean_c sigmoid(u[t][c*H + h]) * normed[t][c*H + h], u = mix . Wu^T; one warp
-// per hidden index h takes the four up rows c*H + h
+// inj = 2 * sigmoid(iv / HC) in the row count's regime
+MOE_D float hc_inj_value(float iv, int prefill) {
+    if (prefill) return __fmul_rn(2.0f, sigmoid_bf16(bf16r(__fdiv_rn(bf16r(iv), (float)kHc))));
+    return __fmul_rn(2.0f, sigmoidf(__fdiv_rn(iv, (float)kHc)));
+}
+
+// mixed[t][h] = mean_c sigmoid(u[t][c*H + h]) * normed[t][c*H + h], u = mix . Wu^T: a block
+// takes `rows` hidden indices h with the four up rows c*H + h each, items (h, c, group) one per
+// thread; the mix rows (silu of the down totals dv) are formed while staging them; block 0 also
+// writes inj from the inject totals iv
 template <int kBits, int kGs, bool kFp16>
-__global__ void __launch_bounds__(kLinThreads) hc_up_tail_kernel(const uint16_t *__restrict__ mix, int T, int R,
-                                                                 int H, const uint32_t *__restrict__ wu,
-                                                                 const uint16_t *__restrict__ su,
-                                                                 const uint16_t *__restrict__ bu,
-                                                                 const uint16_t *__restrict__ normed, int prefill,
-                                                                 uint16_t *__restrict__ mixed, int stage) {
+__global__ void __launch_bounds__(max_block(kGs)) hc_up_tail_kernel(const float *__restrict__ dv,
+                                                                    const float *__restrict__ iv, int T, int R, int H,
+                                                                    const uint32_t *__restrict__ wu,
+                                                                    const uint16_t *__restrict__ su,
+                                                                    const uint16_t *__restrict__ bu,
+                                                                    const uint16_t *__restrict__ normed, int prefill,
+                                                                    uint16_t *__restrict__ mixed,
+                                                                    uint16_t *__restrict__ inj) {
     extern __shared__ __align__(16) unsigned char lin_smem_raw[];
-    const int wib = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int hi = blockIdx.x * kLinWarps + wib;
-    const bool active = hi < H;
+    using GI = GroupItem<kBits, kGs, kFp16>;
     const int ng = R / kGs, W = kHc * H;
-    const LinSmem L = lin_smem(kHc, ng, T, R);
-    double *sv = reinterpret_cast<double *>(lin_smem_raw) + (size_t)wib * kHc * kLinTok * ng;
-    uint16_t *sx = reinterpret_cast<uint16_t *>(lin_smem_raw + L.grp);
-    constexpr int per = Group<kBits, kGs>::kPer;
-    const int hr = active ? hi : 0;
-    const uint32_t *wr[kHc];
-    const uint16_t *sr[kHc], *br[kHc];
-#pragma unroll
-    for (int c = 0; c < kHc; ++c) {
-        const size_t row = (size_t)c * H + hr;
-        wr[c] = wu + row * (R / per);
-        sr[c] = su + row * ng;
-        br[c] = bu + row * ng;
+    const FlatShape F = flat_shape(kHc, ng, T, R);
+    double *sv = reinterpret_cast<double *>(lin_smem_raw);              // [rows][kHc][kLinTok][ng]
+    uint16_t *sx = reinterpret_cast<uint16_t *>(lin_smem_raw + F.grp);
+    const int c = (threadIdx.x / ng) % kHc, r = threadIdx.x / (kHc * ng), g = threadIdx.x % ng;
+    const int hi = blockIdx.x * F.rows + r;
+    const bool item = r < F.rows && hi < H;
+    GI it;
+    if (item) {
+        const size_t row = (size_t)c * H + hi;
+        it.load(wu + row * (R / GI::kPer), su + row * ng, bu + row * ng, g);
     }
-    const uint32_t *const(&wrc)[kHc] = wr;
-    const uint16_t *const(&src)[kHc] = sr;
-    const uint16_t *const(&brc)[kHc] = br;
+    pdl_launch_dependents();
+    pdl_wait();                                  // dv, iv and normed come from earlier kernels
+    if (blockIdx.x == 0 && inj)
+        for (int q = threadIdx.x; q < T * kHc; q += blockDim.x)
+            inj[q] = f32_to_bf16_bits(iv ? hc_inj_value(iv[q], prefill) : 0.f);
 #pragma unroll 1
     for (int t0 = 0; t0 < T; t0 += kLinTok) {
         const int nt = min(kLinTok, T - t0);
-        const uint16_t *xs = mix + (size_t)t0 * R;
-        if (stage) {
-            __syncthreads();
-            stage_x(sx, mix, R, t0, nt);
-            __syncthreads();
-            xs = sx;
-        }
-        if (active) {
-            stage_rows_spread<kBits, kGs, kFp16, kHc>(xs, R, nt, wrc, src, brc, ng, lane, sv);
-            __syncwarp();
-            const int j = lane & (kLinTok - 1), m = lane / kLinTok;     // lane = m * kLinTok + j
-            float u = 0.f;
-            if (m < kHc && j < nt) {
-                u = (float)sum_in_order(sv + (m * kLinTok + j) * ng, ng);
-                if (prefill) u = bf16r(u);
-            }
-            float uc[kHc];
+        __syncthreads();                         // the previous pass is done with sx and sv
+        for (int k = threadIdx.x; k < nt * R; k += blockDim.x)   // mix rows t0 .. t0+nt-1
+            sx[k] = f32_to_bf16_bits(hc_mix_value(dv[(size_t)t0 * R + k], prefill));
+        __syncthreads();
+        if (item)
+            for (int j = 0; j < nt; ++j)
+                sv[((r * kHc + c) * kLinTok + j) * ng + g] = it.value(sx + (size_t)j * R + (size_t)g * kGs);
+        __syncthreads();
+        for (int q = threadIdx.x; q < F.rows * nt; q += blockDim.x) {
+            const int rr = q / nt, j = q - rr * nt, hh = blockIdx.x * F.rows + rr;
+            if (hh >= H) continue;
+            const size_t t = (size_t)(t0 + j);
+            float acc = 0.f;
 #pragma unroll
-            for (int c = 0; c < kHc; ++c) uc[c] = __shfl_sync(0xffffffffu, u, c * kLinTok + j);
-            if (lane < nt) {
-                const size_t t = (size_t)(t0 + lane);
-                float acc = 0.f;
-#pragma unroll
-                for (int c = 0; c < kHc; ++c) {
-                    const float nv = bf16_bits_to_f32(ldu16(normed + t * W + (size_t)c * H + hi));
-                    if (prefill) {
-                        const float p = bf16r(__fmul_rn(sigmoid_bf16(uc[c]), nv));
-                        acc = c == 0 ? p : bf16r(__fadd_rn(acc, p));
-                    } else {
-                        const float p = __fmul_rn(sigmoidf(uc[c]), nv);
-                        acc = c == 0 ? p : __fadd_rn(acc, p);
-                    }
+            for (int cc = 0; cc < kHc; ++cc) {
+                float u = (float)sum_in_order(sv + ((rr * kHc + cc) * kLinTok + j) * ng, ng);
+                const float nv = bf16_bits_to_f32(ldu16(normed + t * W + (size_t)cc * H + hh));
+                if (prefill) {
+                    u = bf16r(u);
+                    const float p = bf16r(__fmul_rn(sigmoid_bf16(u), nv));
+                    acc = cc == 0 ? p : bf16r(__fadd_rn(acc, p));
+                } else {
+                    const float p = __fmul_rn(sigmoidf(u), nv);
+                    acc = cc == 0 ? p : __fadd_rn(acc, p);
                 }
-                mixed[t * H + hi] =
-                    f32_to_bf16_bits(prefill ? __fmul_rn(acc, 1.0f / (float)kHc) : __fdiv_rn(acc, (float)kHc));
             }
-            __syncwarp();
+            mixed[t * H + hh] = f32_to_bf16_bits(prefill ? __fmul_rn(acc, 1.0f / (float)kHc) : __fdiv_rn(acc, (float)kHc));
         }
     }
 }
 
-template <typename K>
-int prepare_smem(K kern, size_t bytes) {
-    if (bytes > 48 * 1024)
-        MOE_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes));
-    return MOE_OK;
-}
+struct UpTailArgs {
+    const float *dv, *iv;
+    int T, R, H;
+    const void *wu, *su, *bu, *normed;
+    int prefill;
+    void *mixed, *inj;
+};
 
 template <int kBits, int kGs, bool kFp16>
-int launch_up_tail(const void *mix, int T, int R, int H, const void *wu, const void *su, const void *bu,
-                   const void *normed, int prefill, void *mixed, cudaStream_t st) {
-    auto kern = hc_up_tail_kernel<kBits, kGs, kFp16>;
-    const LinSmem L = lin_smem(kHc, R / kGs, T, R);
-    int rc = prepare_smem(kern, L.total());
-    if (rc) return rc;
-    kern<<<(H + kLinWarps - 1) / kLinWarps, kLinThreads, L.total(), st>>>(
-        static_cast<const uint16_t *>(mix), T, R, H, static_cast<const uint32_t *>(wu),
-        static_cast<const uint16_t *>(su), static_cast<const uint16_t *>(bu), static_cast<const uint16_t *>(normed),
-        prefill, static_cast<uint16_t *>(mixed), L.xbytes > 0);
-    MOE_CUDA_TRY(cudaGetLastError());
+int launch_up_tail(const UpTailArgs &a, cudaStream_t st) {
+    const FlatShape F = flat_shape(kHc, a.R / kGs, a.T, a.R);   // the mix rows always fit: R <= kMaxHcRank
+    MOE_CUDA_TRY(launch_pdl_v(hc_up_tail_kernel<kBits, kGs, kFp16>, dim3((a.H + F.rows - 1) / F.rows),
+                              dim3(F.threads), F.smem(), st, a.dv, a.iv, a.T, a.R, a.H,
+                              static_cast<const uint32_t *>(a.wu), static_cast<const uint16_t *>(a.su),
+                              static_cast<const uint16_t *>(a.bu), static_cast<const uint16_t *>(a.normed), a.prefill,
+                              static_cast<uint16_t *>(a.mixed), static_cast<uint16_t *>(a.inj)));
     return MOE_OK;
 }
 
-int dispatch_up_tail(int bits, int gs, int sb_fp16, const void *mix, int T, int R, int H, const void *wu,
-                     const void *su, const void *bu, const void *normed, int prefill, void *mixed, cudaStream_t st) {
-#define MOE_HC_CASE(B, G)                                                                                    \
-    if (bits == B && gs == G)                                                                                \
-        return sb_fp16 ? launch_up_tail<B, G, true>(mix, T, R, H, wu, su, bu, normed, prefill, mixed, st)   \
-                       : launch_up_tail<B, G, false>(mix, T, R, H, wu, su, bu, normed, prefill, mixed, st);
+int dispatch_up_tail(int bits, int gs, int sb_fp16, const UpTailArgs &a, cudaStream_t st) {
+#define MOE_HC_CASE(B, G)                                                                          \
+    if (bits == B && gs == G)                                                                      \
+        return sb_fp16 ? launch_up_tail<B, G, true>(a, st) : launch_up_tail<B, G, false>(a, st);
     MOE_HC_CASE(2, 32) MOE_HC_CASE(2, 64) MOE_HC_CASE(2, 128)
     MOE_HC_CASE(4, 32) MOE_HC_CASE(4, 64) MOE_HC_CASE(4, 128)
     MOE_HC_CASE(8, 32) MOE_HC_CASE(8, 64) MOE_HC_CASE(8, 128)
@@ -214,8 +191,10 @@ int dispatch_up_tail(int bits, int gs, int sb_fp16, const void *mix, int T, int 
     return moe_set_error(MOE_EINVAL, "hc_mix: no up kernel for bits=%d group_size=%d", bits, gs);
 }
 
+constexpr int kMaxHcRank = 8192;                 // the up pass stages kLinTok rows of R mix values
+
 struct HcWs {
-    size_t normed, dv, iv, mix, total;
+    size_t normed, dv, iv, total;
 };
 
 HcWs hc_ws(int T, int HC, int H, int R) {
@@ -223,8 +202,7 @@ HcWs hc_ws(int T, int HC, int H, int R) {
     w.normed = 0;
     w.dv = al256((size_t)T * HC * H * 2);
     w.iv = w.dv + al256((size_t)T * R * 4);
-    w.mix = w.iv + al256((size_t)T * HC * 4);
-    w.total = w.mix + al256((size_t)T * R * 2);
+    w.total = w.iv + al256((size_t)T * HC * 4);
     return w;
 }
 
@@ -252,27 +230,30 @@ extern "C" int moe_hc_mix(const void *h, int T, int HC, int H, int R, const void
     char *p = static_cast<char *>(workspace);
     uint16_t *normed = reinterpret_cast<uint16_t *>(p + L.normed);
     float *dv = reinterpret_cast<float *>(p + L.dv), *iv = reinterpret_cast<float *>(p + L.iv);
-    uint16_t *mix = reinterpret_cast<uint16_t *>(p + L.mix);
     const int W = HC * H;
+    if (R > kMaxHcRank) return moe_set_error(MOE_EINVAL, "hc_mix: rank %d above %d", R, kMaxHcRank);
     int rc = moe_qlin_check("hc_mix down", normed, T, W, R, wd, sd, bd, dbits, dgs, mixed);
-    if (!rc) rc = moe_qlin_check("hc_mix up", mix, T, R, W, wu, su, bu, ubits, ugs, mixed);
+    if (!rc) rc = moe_qlin_check("hc_mix up", normed, T, R, W, wu, su, bu, ubits, ugs, mixed);
     if (!rc && wi) rc = moe_qlin_check("hc_mix inject", normed, T, W, HC, wi, si, bi, ibits, igs, mixed);
     if (rc) return rc;
+    if (kHc * (R / ugs) > max_block(ugs))
+        return moe_set_error(MOE_EINVAL, "hc_mix: %d up groups per row (at most %d)", R / ugs, max_block(ugs) / kHc);
     if (reinterpret_cast<uintptr_t>(h) % 2 || (written && reinterpret_cast<uintptr_t>(written) % 2))
         return moe_set_error(MOE_EINVAL, "hc_mix: misaligned bf16 buffers");
     cudaStream_t st = as_stream(stream);
     const int prefill = T > kPrefillRows;
-    if ((rc = prepare_smem(hc_norm_kernel, (size_t)H * sizeof(float)))) return rc;
-    hc_norm_kernel<<<dim3(HC, T), kNormThreads, (size_t)H * sizeof(float), st>>>(
-        static_cast<const uint16_t *>(h), static_cast<const uint16_t *>(branch), static_cast<const uint16_t *>(gate),
-        static_cast<const uint16_t *>(norm_w), eps, H, static_cast<uint16_t *>(written), normed);
-    MOE_CUDA_TRY(cudaGetLastError());
-    if ((rc = moe_qlin_linear(normed, T, W, R, wd, sd, bd, dbits, dgs, sb_fp16, nullptr, nullptr, dv, st))) return rc;
-    if (wi && (rc = moe_qlin_linear(normed, T, W, HC, wi, si, bi, ibits, igs, sb_fp16, nullptr, nullptr, iv, st)))
-        return rc;
-    const int nact = T * (R + HC);
-    hc_act_kernel<<<(nact + 255) / 256, 256, 0, st>>>(dv, wi ? iv : nullptr, T, R, prefill, mix,
-                                                      static_cast<uint16_t *>(inj));
-    MOE_CUDA_TRY(cudaGetLastError());
-    return dispatch_up_tail(ubits, ugs, sb_fp16, mix, T, R, H, wu, su, bu, normed, prefill, mixed, st);
+    MOE_CUDA_TRY(launch_pdl_v(hc_norm_kernel, dim3(HC, T), dim3(kNormThreads), (size_t)H * sizeof(float), st,
+                              static_cast<const uint16_t *>(h), static_cast<const uint16_t *>(branch),
+                              static_cast<const uint16_t *>(gate), static_cast<const uint16_t *>(norm_w), eps, H,
+                              static_cast<uint16_t *>(written), normed));
+    if (wi && ibits == dbits && igs == dgs) {    // down and inject rows in one launch
+        rc = moe_qlin_linear(normed, T, W, R, wd, sd, bd, dbits, dgs, sb_fp16, nullptr, nullptr, dv, st, wi, si, bi,
+                             HC, iv);
+    } else {
+        rc = moe_qlin_linear(normed, T, W, R, wd, sd, bd, dbits, dgs, sb_fp16, nullptr, nullptr, dv, st);
+        if (!rc && wi) rc = moe_qlin_linear(normed, T, W, HC, wi, si, bi, ibits, igs, sb_fp16, nullptr, nullptr, iv, st);
+    }
+    if (rc) return rc;
+    const UpTailArgs a{dv, wi ? iv : nullptr, T, R, H, wu, su, bu, normed, prefill, mixed, inj};
+    return dispatch_up_tail(ubits, ugs, sb_fp16, a, st);
 }

@@ -12,11 +12,11 @@
 // and then to bf16. With that order fixed the output does not depend on the launch shape.
 // SwiGLU and the gate product round to bf16 after every op.
 //
-// Kernels: one warp per output row, lane l on groups l, l + 32, ... (the words of the next
-// group are loaded before the current one is used); group values are staged in shared memory
-// and lane j adds token j's in group order. The shared expert is two launches: gate + up +
-// SwiGLU (+ one extra warp for the scalar expert gate), then down with the sigmoid(gate) scale
-// in its epilogue.
+// Kernels (qlinear.cuh): one thread per (matrix, row, group) item, its codes loaded before the
+// kernel waits on its predecessor (programmatic dependent launch); group values in shared
+// memory, added in group order by one thread per (row, token). The shared expert is two
+// launches: gate + up + SwiGLU (+ one block for the scalar expert gate), then down with the
+// sigmoid(gate) scale in its epilogue.
 #include <algorithm>
 #include <cstdint>
 #include <utility>
@@ -32,104 +32,122 @@ namespace {
 using namespace moe_qlin;
 
 // y[t][n] = bf16(float(row total)) (gl == nullptr), or bf16(bf16(sigmoid(gl[t])) * that), or,
-// with yf != nullptr, float(row total) to yf
+// with yf != nullptr, float(row total) to yf; rows N .. N+N2-1 are the rows of a second matrix
+// (w2, s2, b2), written as float totals to yf2. Block: `rows` rows x ng groups, one per thread.
 template <int kBits, int kGs, bool kFp16>
-__global__ void __launch_bounds__(kLinThreads) affine_linear_kernel(const uint16_t *__restrict__ x, int T, int Kin,
-                                                                    int N, const uint32_t *__restrict__ w,
-                                                                    const uint16_t *__restrict__ s,
-                                                                    const uint16_t *__restrict__ b,
-                                                                    const uint16_t *__restrict__ gl,
-                                                                    uint16_t *__restrict__ y, float *__restrict__ yf,
-                                                                    int stage) {
+__global__ void __launch_bounds__(max_block(kGs)) affine_linear_kernel(
+    const uint16_t *__restrict__ x, int T, int Kin, int N, const uint32_t *__restrict__ w,
+    const uint16_t *__restrict__ s, const uint16_t *__restrict__ b, const uint16_t *__restrict__ gl,
+    uint16_t *__restrict__ y, float *__restrict__ yf, const uint32_t *__restrict__ w2, const uint16_t *__restrict__ s2,
+    const uint16_t *__restrict__ b2, int N2, float *__restrict__ yf2) {
     extern __shared__ __align__(16) unsigned char lin_smem_raw[];
-    const int wib = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int n = blockIdx.x * kLinWarps + wib;
-    const bool active = n < N;                   // idle warps still take part in the x staging
+    using GI = GroupItem<kBits, kGs, kFp16>;
     const int ng = Kin / kGs;
-    const LinSmem L = lin_smem(1, ng, T, Kin);
-    double *sv = reinterpret_cast<double *>(lin_smem_raw) + (size_t)wib * kLinTok * ng;
-    uint16_t *sx = reinterpret_cast<uint16_t *>(lin_smem_raw + L.grp);
-    const int nrow = active ? n : 0;
-    const uint32_t *const wr[1] = {w + (size_t)nrow * (Kin / Group<kBits, kGs>::kPer)};
-    const uint16_t *const sr[1] = {s + (size_t)nrow * ng};
-    const uint16_t *const br[1] = {b + (size_t)nrow * ng};
+    const FlatShape F = flat_shape(1, ng, T, Kin);
+    double *sv = reinterpret_cast<double *>(lin_smem_raw);              // [rows][kLinTok][ng]
+    uint16_t *sx = reinterpret_cast<uint16_t *>(lin_smem_raw + F.grp);
+    const int r = threadIdx.x / ng, g = threadIdx.x - r * ng;
+    const int n = blockIdx.x * F.rows + r;
+    const bool item = r < F.rows && n < N + N2;
+    GI it;
+    if (item) {
+        const bool second = n >= N;
+        const size_t row = second ? n - N : n;
+        it.load((second ? w2 : w) + row * (Kin / GI::kPer), (second ? s2 : s) + row * ng,
+                (second ? b2 : b) + row * ng, g);
+    }
+    pdl_launch_dependents();
+    pdl_wait();                                  // x (and gl) come from earlier kernels
 #pragma unroll 1
     for (int t0 = 0; t0 < T; t0 += kLinTok) {
         const int nt = min(kLinTok, T - t0);
         const uint16_t *xs = x + (size_t)t0 * Kin;
-        if (stage) {
-            __syncthreads();                     // the previous pass is done with sx
+        __syncthreads();                         // the previous pass is done with sx and sv
+        if (F.xbytes) {
             stage_x(sx, x, Kin, t0, nt);
             __syncthreads();
             xs = sx;
         }
-        if (active) {
-            stage_rows<kBits, kGs, kFp16, 1>(xs, Kin, nt, wr, sr, br, ng, lane, sv);
-            __syncwarp();
-            if (lane < nt) {
-                const int t = t0 + lane;
-                const double total = sum_in_order(sv + lane * ng, ng);
-                if (yf) {
-                    yf[(size_t)t * N + n] = (float)total;
-                } else {
-                    uint16_t o = row_out(total);
-                    if (gl) o = f32_to_bf16_bits(__fmul_rn(sigmoid_bf16(bf16_bits_to_f32(gl[t])), bf16_bits_to_f32(o)));
-                    y[(size_t)t * N + n] = o;
-                }
+        if (item)
+            for (int j = 0; j < nt; ++j) sv[(r * kLinTok + j) * ng + g] = it.value(xs + (size_t)j * Kin + (size_t)g * kGs);
+        __syncthreads();
+        for (int q = threadIdx.x; q < F.rows * nt; q += blockDim.x) {
+            const int rr = q / nt, j = q - rr * nt, nn = blockIdx.x * F.rows + rr, t = t0 + j;
+            if (nn >= N + N2) continue;
+            const double total = sum_in_order(sv + (rr * kLinTok + j) * ng, ng);
+            if (nn >= N) {
+                yf2[(size_t)t * N2 + (nn - N)] = (float)total;
+            } else if (yf) {
+                yf[(size_t)t * N + nn] = (float)total;
+            } else {
+                uint16_t o = row_out(total);
+                if (gl) o = f32_to_bf16_bits(__fmul_rn(sigmoid_bf16(bf16_bits_to_f32(gl[t])), bf16_bits_to_f32(o)));
+                y[(size_t)t * N + nn] = o;
             }
-            __syncwarp();
         }
     }
 }
 
 // act[t][i] = bf16(bf16(g * bf16(sigmoid(g))) * u) with g, u rows i of the gate / up
-// projections; the warp of row I computes gl[t] = x[t] . We (runtime bits / group size).
+// projections: items (row, matrix, group). The last block computes gl[t] = x[t] . We (the
+// scalar expert gate, runtime bits / group size).
 template <int kBits, int kGs, bool kFp16>
-__global__ void __launch_bounds__(kLinThreads) gateup_swiglu_kernel(
+__global__ void __launch_bounds__(max_block(kGs)) gateup_swiglu_kernel(
     const uint16_t *__restrict__ x, int T, int H, int I, const uint32_t *__restrict__ wg,
     const uint16_t *__restrict__ sg, const uint16_t *__restrict__ bg, const uint32_t *__restrict__ wu,
     const uint16_t *__restrict__ su, const uint16_t *__restrict__ bu, const uint32_t *__restrict__ we,
     const uint16_t *__restrict__ se, const uint16_t *__restrict__ be, int ebits, int egs,
-    uint16_t *__restrict__ act, uint16_t *__restrict__ gl, int stage) {
+    uint16_t *__restrict__ act, uint16_t *__restrict__ gl) {
     extern __shared__ __align__(16) unsigned char lin_smem_raw[];
-    const int wib = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int i = blockIdx.x * kLinWarps + wib;
+    using GI = GroupItem<kBits, kGs, kFp16>;
     const int ng = H / kGs, nge = H / egs;
-    const LinSmem L = lin_smem(2, max(ng, (nge + 1) / 2), T, H);
-    double *sv = reinterpret_cast<double *>(lin_smem_raw) + (size_t)wib * 2 * kLinTok * max(ng, (nge + 1) / 2);
-    uint16_t *sx = reinterpret_cast<uint16_t *>(lin_smem_raw + L.grp);
-    constexpr int per = Group<kBits, kGs>::kPer;
-    const int irow = i < I ? i : 0;
-    const uint32_t *const wr[2] = {wg + (size_t)irow * (H / per), wu + (size_t)irow * (H / per)};
-    const uint16_t *const sr[2] = {sg + (size_t)irow * ng, su + (size_t)irow * ng};
-    const uint16_t *const br[2] = {bg + (size_t)irow * ng, bu + (size_t)irow * ng};
+    FlatShape F = flat_shape(2, ng, T, H);
+    const size_t gate_grp = (size_t)kLinTok * nge * sizeof(double);   // the gate block's values
+    if (gate_grp > F.grp) F.grp = gate_grp;
+    double *sv = reinterpret_cast<double *>(lin_smem_raw);              // [rows][2][kLinTok][ng]
+    uint16_t *sx = reinterpret_cast<uint16_t *>(lin_smem_raw + F.grp);
+    const bool gate_block = blockIdx.x == gridDim.x - 1;
+    const int m = (threadIdx.x / ng) & 1, r = threadIdx.x / (2 * ng), g = threadIdx.x % ng;
+    const int i = blockIdx.x * F.rows + r;
+    const bool item = !gate_block && r < F.rows && i < I;
+    GI it;
+    if (item) {
+        const size_t row = i;
+        it.load((m ? wu : wg) + row * (H / GI::kPer), (m ? su : sg) + row * ng, (m ? bu : bg) + row * ng, g);
+    }
+    pdl_launch_dependents();
+    pdl_wait();                                  // x comes from earlier kernels
 #pragma unroll 1
     for (int t0 = 0; t0 < T; t0 += kLinTok) {
         const int nt = min(kLinTok, T - t0);
         const uint16_t *xs = x + (size_t)t0 * H;
-        if (stage) {
-            __syncthreads();
+        __syncthreads();
+        if (F.xbytes) {
             stage_x(sx, x, H, t0, nt);
             __syncthreads();
             xs = sx;
         }
-        if (i == I) {                            // the scalar expert gate
-            stage_row_generic<kFp16>(xs, H, nt, we, se, be, ebits, egs, lane, sv);
-            __syncwarp();
-            if (lane < nt) gl[t0 + lane] = row_out(sum_in_order(sv + lane * nge, nge));
-            __syncwarp();
-        } else if (i < I) {
-            stage_rows<kBits, kGs, kFp16, 2>(xs, H, nt, wr, sr, br, ng, lane, sv);
-            __syncwarp();
-            // lanes 0..nt-1 add the gate rows, lanes kLinTok..kLinTok+nt-1 the up rows
-            const int j = lane & (kLinTok - 1), m = lane / kLinTok;
-            float v = 0.f;
-            if (m < 2 && j < nt) v = bf16_bits_to_f32(row_out(sum_in_order(sv + (m * kLinTok + j) * ng, ng)));
-            const float uv = __shfl_down_sync(0xffffffffu, v, kLinTok);
-            if (lane < nt)
-                act[(size_t)(t0 + lane) * I + i] =
-                    f32_to_bf16_bits(bf16r(__fmul_rn(bf16r(__fmul_rn(v, sigmoid_bf16(v))), uv)));
-            __syncwarp();
+        if (gate_block) {                        // [kLinTok][nge] values of the scalar gate
+            for (int q = threadIdx.x; q < nge * nt; q += blockDim.x) {
+                const int j = q / nge, ge = q - j * nge;
+                sv[j * nge + ge] = generic_group_value<kFp16>(xs + (size_t)j * H + (size_t)ge * egs, we, se, be, ebits,
+                                                              egs, ge);
+            }
+            __syncthreads();
+            if ((int)threadIdx.x < nt) gl[t0 + threadIdx.x] = row_out(sum_in_order(sv + threadIdx.x * nge, nge));
+            continue;
+        }
+        if (item)
+            for (int j = 0; j < nt; ++j)
+                sv[((r * 2 + m) * kLinTok + j) * ng + g] = it.value(xs + (size_t)j * H + (size_t)g * kGs);
+        __syncthreads();
+        for (int q = threadIdx.x; q < F.rows * nt; q += blockDim.x) {
+            const int rr = q / nt, j = q - rr * nt, ii = blockIdx.x * F.rows + rr;
+            if (ii >= I) continue;
+            const float gv = bf16_bits_to_f32(row_out(sum_in_order(sv + ((rr * 2) * kLinTok + j) * ng, ng)));
+            const float uv = bf16_bits_to_f32(row_out(sum_in_order(sv + ((rr * 2 + 1) * kLinTok + j) * ng, ng)));
+            act[(size_t)(t0 + j) * I + ii] =
+                f32_to_bf16_bits(bf16r(__fmul_rn(bf16r(__fmul_rn(gv, sigmoid_bf16(gv))), uv)));
         }
     }
 }
@@ -144,34 +162,26 @@ int check_lin(const char *who, const void *x, int T, int Kin, int N, const void 
     if (gs != 32 && gs != 64 && gs != 128)
         return moe_set_error(MOE_EINVAL, "%s: group_size=%d (32, 64 or 128 supported)", who, gs);
     if (Kin % gs) return moe_set_error(MOE_EINVAL, "%s: group_size %d does not divide K=%d", who, gs, Kin);
-    if (Kin / gs > kMaxGroups)
-        return moe_set_error(MOE_EINVAL, "%s: %d groups per row (at most %d)", who, Kin / gs, kMaxGroups);
+    const int gmax = kMaxGroups < max_block(gs) ? kMaxGroups : max_block(gs);
+    if (Kin / gs > gmax) return moe_set_error(MOE_EINVAL, "%s: %d groups per row (at most %d)", who, Kin / gs, gmax);
     const uintptr_t wa = (gs * bits / 8) % 16 ? 8 : 16;      // the group's word loads
     if (reinterpret_cast<uintptr_t>(x) % 16 || reinterpret_cast<uintptr_t>(w) % wa)
         return moe_set_error(MOE_EINVAL, "%s: x must be 16-byte and codes %d-byte aligned", who, (int)wa);
     return MOE_OK;
 }
 
-// the dynamic shared memory of one block; above the 48 KB default the kernel is opted in
-template <typename K>
-int prepare_smem(K kern, size_t bytes) {
-    if (bytes > 48 * 1024)
-        MOE_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes));
-    return MOE_OK;
-}
-
 template <int kBits, int kGs, bool kFp16>
 int launch_lin_t(const void *x, int T, int Kin, int N, const void *w, const void *s, const void *b, const void *gl,
-                 void *y, float *yf, cudaStream_t st) {
-    auto kern = affine_linear_kernel<kBits, kGs, kFp16>;
-    const LinSmem L = lin_smem(1, Kin / kGs, T, Kin);
-    int rc = prepare_smem(kern, L.total());
-    if (rc) return rc;
-    kern<<<(N + kLinWarps - 1) / kLinWarps, kLinThreads, L.total(), st>>>(
-        static_cast<const uint16_t *>(x), T, Kin, N, static_cast<const uint32_t *>(w),
-        static_cast<const uint16_t *>(s), static_cast<const uint16_t *>(b), static_cast<const uint16_t *>(gl),
-        static_cast<uint16_t *>(y), yf, L.xbytes > 0);
-    MOE_CUDA_TRY(cudaGetLastError());
+                 void *y, float *yf, const void *w2, const void *s2, const void *b2, int N2, float *yf2,
+                 cudaStream_t st) {
+    const FlatShape F = flat_shape(1, Kin / kGs, T, Kin);
+    const int rows = N + N2;
+    MOE_CUDA_TRY(launch_pdl_v(affine_linear_kernel<kBits, kGs, kFp16>, dim3((rows + F.rows - 1) / F.rows),
+                              dim3(F.threads), F.smem(), st, static_cast<const uint16_t *>(x), T, Kin, N,
+                              static_cast<const uint32_t *>(w), static_cast<const uint16_t *>(s),
+                              static_cast<const uint16_t *>(b), static_cast<const uint16_t *>(gl),
+                              static_cast<uint16_t *>(y), yf, static_cast<const uint32_t *>(w2),
+                              static_cast<const uint16_t *>(s2), static_cast<const uint16_t *>(b2), N2, yf2));
     return MOE_OK;
 }
 
@@ -185,17 +195,15 @@ struct GateUpArgs {
 
 template <int kBits, int kGs, bool kFp16>
 int launch_gateup_t(const GateUpArgs &a, cudaStream_t st) {
-    auto kern = gateup_swiglu_kernel<kBits, kGs, kFp16>;
-    const LinSmem L = lin_smem(2, std::max(a.H / kGs, (a.H / a.egs + 1) / 2), a.T, a.H);
-    int rc = prepare_smem(kern, L.total());
-    if (rc) return rc;
+    FlatShape F = flat_shape(2, a.H / kGs, a.T, a.H);
+    // the gate block keeps [kLinTok][H / egs] values in the same region (as the kernel computes)
+    F.grp = std::max(F.grp, (size_t)kLinTok * (a.H / a.egs) * sizeof(double));
     auto u16 = [](const void *p) { return static_cast<const uint16_t *>(p); };
     auto u32 = [](const void *p) { return static_cast<const uint32_t *>(p); };
-    kern<<<(a.I + 1 + kLinWarps - 1) / kLinWarps, kLinThreads, L.total(), st>>>(
-        u16(a.x), a.T, a.H, a.I, u32(a.wg), u16(a.sg), u16(a.bg), u32(a.wu), u16(a.su), u16(a.bu), u32(a.we),
-        u16(a.se), u16(a.be), a.ebits, a.egs, static_cast<uint16_t *>(a.act), static_cast<uint16_t *>(a.gl),
-        L.xbytes > 0);
-    MOE_CUDA_TRY(cudaGetLastError());
+    MOE_CUDA_TRY(launch_pdl_v(gateup_swiglu_kernel<kBits, kGs, kFp16>, dim3((a.I + F.rows - 1) / F.rows + 1),
+                              dim3(F.threads), F.smem(), st, u16(a.x), a.T, a.H, a.I, u32(a.wg), u16(a.sg), u16(a.bg),
+                              u32(a.wu), u16(a.su), u16(a.bu), u32(a.we), u16(a.se), u16(a.be), a.ebits, a.egs,
+                              static_cast<uint16_t *>(a.act), static_cast<uint16_t *>(a.gl)));
     return MOE_OK;
 }
 
@@ -216,8 +224,9 @@ int dispatch(int bits, int gs, int sb_fp16, A &&...args) {
 template <int kBits, int kGs, bool kFp16>
 struct LinRun {
     static int run(const void *x, int T, int Kin, int N, const void *w, const void *s, const void *b, const void *gl,
-                   void *y, float *yf, cudaStream_t st) {
-        return launch_lin_t<kBits, kGs, kFp16>(x, T, Kin, N, w, s, b, gl, y, yf, st);
+                   void *y, float *yf, const void *w2, const void *s2, const void *b2, int N2, float *yf2,
+                   cudaStream_t st) {
+        return launch_lin_t<kBits, kGs, kFp16>(x, T, Kin, N, w, s, b, gl, y, yf, w2, s2, b2, N2, yf2, st);
     }
 };
 
@@ -234,16 +243,18 @@ int moe_qlin_check(const char *who, const void *x, int T, int Kin, int N, const 
 }
 
 int moe_qlin_linear(const void *x, int T, int Kin, int N, const void *w, const void *s, const void *b, int bits,
-                    int gs, int sb_fp16, const void *gl, void *y, float *yf, cudaStream_t st) {
-    return dispatch<LinRun>(bits, gs, sb_fp16, x, T, Kin, N, w, s, b, gl, y, yf, st);
+                    int gs, int sb_fp16, const void *gl, void *y, float *yf, cudaStream_t st, const void *w2,
+                    const void *s2, const void *b2, int N2, float *yf2) {
+    if (N2 > 0 && !(w2 && s2 && b2 && yf2)) return moe_set_error(MOE_EINVAL, "affine linear: second matrix incomplete");
+    return dispatch<LinRun>(bits, gs, sb_fp16, x, T, Kin, N, w, s, b, gl, y, yf, w2, s2, b2, N2 > 0 ? N2 : 0, yf2, st);
 }
 
 extern "C" int moe_affine_linear(const void *x, int T, int Kin, int N, const void *w, const void *scales,
                                  const void *biases, int bits, int group_size, int sb_fp16, void *y, void *stream) {
     int rc = check_lin("affine_linear", x, T, Kin, N, w, scales, biases, bits, group_size, y);
     if (rc) return rc;
-    return dispatch<LinRun>(bits, group_size, sb_fp16, x, T, Kin, N, w, scales, biases, nullptr, y,
-                            static_cast<float *>(nullptr), as_stream(stream));
+    return moe_qlin_linear(x, T, Kin, N, w, scales, biases, bits, group_size, sb_fp16, nullptr, y, nullptr,
+                           as_stream(stream));
 }
 
 extern "C" size_t moe_shared_expert_workspace_bytes(int T, int H, int I) {
@@ -266,11 +277,13 @@ extern "C" int moe_shared_expert(const void *x, int T, int H, int I, const void 
     if (!rc) rc = check_lin("shared_expert down_proj", workspace, T, I, H, wd, sd, bd, bits, group_size, y);
     if (!rc) rc = check_lin("shared_expert gate", x, T, H, 1, weg, seg, beg, gate_bits, gate_group_size, y);
     if (rc) return rc;
+    if (2 * (H / group_size) > max_block(group_size))
+        return moe_set_error(MOE_EINVAL, "shared_expert: %d groups per row (at most %d)", H / group_size,
+                             max_block(group_size) / 2);
     char *p = static_cast<char *>(workspace);
     void *act = p, *gl = p + al256((size_t)T * I * 2);
     cudaStream_t st = as_stream(stream);
     const GateUpArgs a{x, T, H, I, wg, sg, bg, wu, su, bu, weg, seg, beg, gate_bits, gate_group_size, act, gl};
     if ((rc = dispatch<GateUpRun>(bits, group_size, sb_fp16, a, st))) return rc;
-    return dispatch<LinRun>(bits, group_size, sb_fp16, act, T, I, H, wd, sd, bd, gl, y, static_cast<float *>(nullptr),
-                            st);
+    return moe_qlin_linear(act, T, I, H, wd, sd, bd, bits, group_size, sb_fp16, gl, y, nullptr, st);
 }
