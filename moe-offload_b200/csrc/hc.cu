@@ -30,7 +30,7 @@ namespace {
 using namespace moe_qlin;
 
 constexpr int kHc = 4;                           // streams (hc_count of the reference's models)
-constexpr int kNormThreads = 256;
+constexpr int kNormThreads = 1024;                  // few values per thread: the norm has only HC x T blocks
 constexpr int kPrefillRows = 16;                 // run_hc: rows <= 16 take the fused decode kernels
 
 MOE_D uint16_t ldu16(const uint16_t *p) { return __ldg(p); }

@@ -95,7 +95,8 @@ struct GroupItem {
     }
 };
 
-// The same group value for a row of any width and group size (runtime bits / gs).
+// The same group value for a row of any width and group size (runtime bits / gs); the row may
+// sit in shared or global memory (plain loads).
 template <bool kFp16>
 MOE_D double generic_group_value(const uint16_t *xg, const uint32_t *wrow, const uint16_t *srow,
                                  const uint16_t *brow, int bits, int gs, int g) {
@@ -108,7 +109,7 @@ MOE_D double generic_group_value(const uint16_t *xg, const uint32_t *wrow, const
         const uint32_t pk[4] = {v.x, v.y, v.z, v.w};
         uint32_t wd[8];
 #pragma unroll
-        for (int i = 0; i < 8; ++i) wd[i] = __ldg(wrow + (((size_t)g * gs + k0 + i) >> lper));
+        for (int i = 0; i < 8; ++i) wd[i] = wrow[((size_t)g * gs + k0 + i) >> lper];
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
             const int k = g * gs + k0 + i;
@@ -118,7 +119,7 @@ MOE_D double generic_group_value(const uint16_t *xg, const uint32_t *wrow, const
             xsum = __fadd_rn(xsum, xv);
         }
     }
-    return group_value<kFp16>(__ldg(srow + g), __ldg(brow + g), acc, xsum);
+    return group_value<kFp16>(srow[g], brow[g], acc, xsum);
 }
 
 MOE_D double sum_in_order(const double *v, int n) {

@@ -107,6 +107,14 @@ __global__ void __launch_bounds__(max_block(kGs)) gateup_swiglu_kernel(
     double *sv = reinterpret_cast<double *>(lin_smem_raw);              // [rows][2][kLinTok][ng]
     uint16_t *sx = reinterpret_cast<uint16_t *>(lin_smem_raw + F.grp);
     const bool gate_block = blockIdx.x == gridDim.x - 1;
+    // the gate block's copy of the scalar gate row: codes, then scales, then biases
+    uint32_t *gw = reinterpret_cast<uint32_t *>(lin_smem_raw + F.grp + F.xbytes);
+    const int gwords = H * ebits / 32;
+    uint16_t *gsc = reinterpret_cast<uint16_t *>(gw + gwords), *gbi = gsc + nge;
+    if (gate_block) {                            // weights only: copied before the wait
+        for (int k = threadIdx.x; k < gwords; k += blockDim.x) gw[k] = __ldg(we + k);
+        for (int k = threadIdx.x; k < nge; k += blockDim.x) gsc[k] = __ldg(se + k), gbi[k] = __ldg(be + k);
+    }
     const int m = (threadIdx.x / ng) & 1, r = threadIdx.x / (2 * ng), g = threadIdx.x % ng;
     const int i = blockIdx.x * F.rows + r;
     const bool item = !gate_block && r < F.rows && i < I;
@@ -130,8 +138,8 @@ __global__ void __launch_bounds__(max_block(kGs)) gateup_swiglu_kernel(
         if (gate_block) {                        // [kLinTok][nge] values of the scalar gate
             for (int q = threadIdx.x; q < nge * nt; q += blockDim.x) {
                 const int j = q / nge, ge = q - j * nge;
-                sv[j * nge + ge] = generic_group_value<kFp16>(xs + (size_t)j * H + (size_t)ge * egs, we, se, be, ebits,
-                                                              egs, ge);
+                sv[j * nge + ge] = generic_group_value<kFp16>(xs + (size_t)j * H + (size_t)ge * egs, gw, gsc, gbi,
+                                                              ebits, egs, ge);
             }
             __syncthreads();
             if ((int)threadIdx.x < nt) gl[t0 + threadIdx.x] = row_out(sum_in_order(sv + threadIdx.x * nge, nge));
@@ -198,10 +206,12 @@ int launch_gateup_t(const GateUpArgs &a, cudaStream_t st) {
     FlatShape F = flat_shape(2, a.H / kGs, a.T, a.H);
     // the gate block keeps [kLinTok][H / egs] values in the same region (as the kernel computes)
     F.grp = std::max(F.grp, (size_t)kLinTok * (a.H / a.egs) * sizeof(double));
+    // plus the gate block's copy of the scalar gate row (codes, scales, biases)
+    const size_t gate_row = (size_t)a.H * a.ebits / 8 + (size_t)(a.H / a.egs) * 4;
     auto u16 = [](const void *p) { return static_cast<const uint16_t *>(p); };
     auto u32 = [](const void *p) { return static_cast<const uint32_t *>(p); };
     MOE_CUDA_TRY(launch_pdl_v(gateup_swiglu_kernel<kBits, kGs, kFp16>, dim3((a.I + F.rows - 1) / F.rows + 1),
-                              dim3(F.threads), F.smem(), st, u16(a.x), a.T, a.H, a.I, u32(a.wg), u16(a.sg), u16(a.bg),
+                              dim3(F.threads), F.smem() + gate_row, st, u16(a.x), a.T, a.H, a.I, u32(a.wg), u16(a.sg), u16(a.bg),
                               u32(a.wu), u16(a.su), u16(a.bu), u32(a.we), u16(a.se), u16(a.be), a.ebits, a.egs,
                               static_cast<uint16_t *>(a.act), static_cast<uint16_t *>(a.gl)));
     return MOE_OK;
