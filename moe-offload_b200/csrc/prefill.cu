@@ -289,7 +289,9 @@ constexpr int kTile = kBM * 128;                 // one 128-row x 128-byte tile:
 constexpr uint32_t kTmemCols = 512;
 // TMEM columns: accumulators [0, 128) (gate, or down rows 0..127 of the tile) and [128, 256)
 // (up, or down rows 128..255); the dequantised A operand of K-block stage s at 256 + 64 s
-// (matrix 0: +0, matrix 1: +32; 32 columns = 64 bf16 of K)
+// (matrix 0: +0, matrix 1: +32; 32 columns = 64 bf16 of K). A tile of at most 64 tokens uses
+// one half of each accumulator range (columns +0 or +64, alternating), so its MMAs can run while
+// the epilogue still drains the previous tile from the other half; a wider tile takes both.
 constexpr uint32_t kTmemA = 256, kTmemAStage = 64;
 
 struct GemmArgs {
@@ -306,9 +308,9 @@ struct GemmSmem {
     static constexpr size_t raw = 0;                                       // [kRS][kNM] tiles
     static constexpr size_t b = raw + (size_t)kRS * kNM * kTile;           // [kBS] tiles
     static constexpr size_t bars = b + (size_t)kBS * kTile;
-    // raw_full, raw_empty [kRS]; full, empty [kKS]; b_full, b_empty [kBS]; acc_full, acc_empty;
-    // tmem slot
-    static constexpr size_t total = bars + (2 * kRS + 2 * kKS + 2 * kBS + 2) * 8 + 16;
+    // raw_full, raw_empty [kRS]; full, empty [kKS]; b_full, b_empty [kBS]; acc_full, acc_empty
+    // [2] (accumulator halves); tmem slot
+    static constexpr size_t total = bars + (2 * kRS + 2 * kKS + 2 * kBS + 4) * 8 + 16;
     static constexpr size_t alloc = total + 1024;      // + alignment slack
 };
 
@@ -327,9 +329,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     uint64_t *empty = full + kKS;
     uint64_t *b_full = empty + kKS;
     uint64_t *b_empty = b_full + kBS;
-    uint64_t *acc_full = b_empty + kBS;
-    uint64_t *acc_empty = acc_full + 1;
-    uint32_t *tslot = reinterpret_cast<uint32_t *>(acc_empty + 1);
+    uint64_t *acc_full = b_empty + kBS;          // [2]
+    uint64_t *acc_empty = acc_full + 2;          // [2]
+    uint32_t *tslot = reinterpret_cast<uint32_t *>(acc_empty + 2);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
 
     if (tid == 0) {
@@ -345,8 +347,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             mbar_init(&b_full[i], 1);
             mbar_init(&b_empty[i], 1);
         }
-        mbar_init(acc_full, 1);
-        mbar_init(acc_empty, 4);
+        for (int h = 0; h < 2; ++h) {
+            mbar_init(&acc_full[h], 1);
+            mbar_init(&acc_empty[h], 4);
+        }
         fence_barrier_init();
     }
     if (warp == 1) {
@@ -393,12 +397,17 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         }
     } else if (warp == 1) {
         // ------------------------------------------------------------ MMA issuer
-        uint32_t g = 0, tc = 0;
+        uint32_t g = 0, use0 = 0, use1 = 0, nxt = 0;  // acquisitions of each accumulator half
         for (int ti = blockIdx.x; ti < ntiles; ti += gridDim.x) {
             const Tile tl = a.tiles[ti];
             const int BN = (tl.n + 15) & ~15;
             const uint32_t idesc = instr_desc_bf16(BN);
-            mbar_wait(acc_empty, (tc & 1u) ^ 1u);
+            const bool wide = BN > 64;
+            const uint32_t h = nxt;
+            if (wide || h == 0) mbar_wait(&acc_empty[0], (use0 & 1u) ^ 1u), ++use0;
+            if (wide || h == 1) mbar_wait(&acc_empty[1], (use1 & 1u) ^ 1u), ++use1;
+            const uint32_t col = wide ? 0u : 64u * h;
+            if (!wide) nxt ^= 1u;
             tc_fence_after();
             for (int kb = 0; kb < nkb; ++kb) {
                 const int s = g % kKS, sb = g % kBS;
@@ -413,7 +422,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                     for (int mm = 0; mm < 2; ++mm)
 #pragma unroll
                         for (int j = 0; j < kBK / 16; ++j)
-                            mma_bf16_ts(tmem + 128u * mm, at + 32u * mm + 8u * j, desc_sw128(b0 + 32u * j), idesc,
+                            mma_bf16_ts(tmem + 128u * mm + col, at + 32u * mm + 8u * j, desc_sw128(b0 + 32u * j), idesc,
                                         (kb > 0 || j > 0) ? 1u : 0u);
                     mma_commit(&empty[s]);
                     mma_commit(&b_empty[sb]);
@@ -421,17 +430,24 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                 __syncwarp();
                 ++g;
             }
-            if (lane == 0) mma_commit(acc_full);
+            if (lane == 0) {
+                if (wide || h == 0) mma_commit(&acc_full[0]);
+                if (wide || h == 1) mma_commit(&acc_full[1]);
+            }
             __syncwarp();
-            ++tc;
         }
     } else if (warp >= kEpiWarp0 && warp < kEpiWarp0 + 4) {
         // ------------------------------------------------------------ epilogue
         const int quarter = warp & 3;                 // TMEM lanes 32*quarter .. +31
-        uint32_t tc = 0;
+        uint32_t f0 = 0, f1 = 0, nxt = 0;          // the MMA issuer's half assignment, replayed
         for (int ti = blockIdx.x; ti < ntiles; ti += gridDim.x) {
             const Tile tl = a.tiles[ti];
-            mbar_wait(acc_full, tc & 1u);
+            const bool wide = ((tl.n + 15) & ~15) > 64;
+            const uint32_t h = nxt;
+            if (wide || h == 0) mbar_wait(&acc_full[0], f0 & 1u), ++f0;
+            if (wide || h == 1) mbar_wait(&acc_full[1], f1 & 1u), ++f1;
+            const uint32_t col = wide ? 0u : 64u * h;
+            if (!wide) nxt ^= 1u;
             tc_fence_after();
             const int row = tl.row0 + quarter * 32 + lane;
             const uint32_t taddr = tmem + ((uint32_t)(quarter * 32) << 16);
@@ -439,8 +455,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             const int acol = (row & ~15) + kperm_pos(row & 15);
             for (int c0 = 0; c0 < tl.n; c0 += 16) {
                 float gv[16], uv[16];
-                tmem_ld16(taddr + c0, gv);
-                tmem_ld16(taddr + 128 + c0, uv);
+                tmem_ld16(taddr + col + c0, gv);
+                tmem_ld16(taddr + 128 + col + c0, uv);
 #pragma unroll
                 for (int j = 0; j < 16; ++j) {
                     const int tok = c0 + j;
@@ -460,8 +476,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             }
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(acc_empty);
-            ++tc;
+            if (lane == 0) {
+                if (wide || h == 0) mbar_arrive(&acc_empty[0]);
+                if (wide || h == 1) mbar_arrive(&acc_empty[1]);
+            }
         }
     } else if (warp >= kDqWarp0) {
         // ------------------------------------------------------------ dequantisation
