@@ -30,7 +30,7 @@ lru_trace.npz
     layer, top-k expert draws with Zipf popularity and token-to-token reuse, interleaved
     with next-layer top-M prefetch calls, plus a prefill-style set_lru_state in the middle.
 
-Usage:  python tests/golden/make_golden.py [--ref /root/reference]
+Usage:  python tests/golden/make_golden.py [--ref <checkout of Jakevin/moe-offload>]
 """
 from __future__ import annotations
 
