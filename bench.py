@@ -141,6 +141,8 @@ class CpuLayer:
         self.rand = lambda: np_bf16_normal(self.rng, (1, H))
         orc.set_threads(os.cpu_count() or 1)
         self.cores = orc.num_threads()
+        # algorithmic bytes of one token-layer (10 experts + the router), for the effective GB/s
+        self.layer_bytes = C1.top_k * C1.expert_bytes + C1.router_bytes
 
     def token_layer(self) -> float:
         x = self.rand()
@@ -162,10 +164,18 @@ def cpu_layer_sample(seconds: float = 12.0) -> dict:
         ts.append(cl.token_layer())
     per_layer = statistics.mean(ts)
     return {"value": round(1.0 / (cl.cfg.layers * per_layer), 4), "unit": UNIT, "cores": cl.cores,
-            "kind": "port",
+            "kind": "port", "effective_gbs": round(cl.layer_bytes / per_layer / 1e9, 2),
             "sample": f"{len(ts)} token-layers of the c1 shape (1 of 28 layers: 512-expert router, top-10 "
                       f"2-bit experts, combine) in {seconds:.0f}s, extrapolated x28 layers; C restatement "
                       f"(MLX is not installable here)"}
+
+
+def c1_config(cfg, world: int) -> dict:
+    """The workload description both arms print for the c1 stack (same dict, same keys)."""
+    return {"workload": cfg.name, "layers": cfg.layers, "hidden": cfg.hidden, "experts": cfg.experts,
+            "top_k": cfg.top_k, "inter": cfg.inter, "batch": 1, "group_size": cfg.group_size,
+            "scales": "fp16", "router": "bf16", "parallelism": f"replicas x{world}",
+            "l2": "inputs larger than L2: 707 MB of weights per step, 31.7 GB resident"}
 
 
 def run_reference(args, rank: int, world: int) -> None:
@@ -182,13 +192,13 @@ def run_reference(args, rank: int, world: int) -> None:
     v = 1.0 / (cl.cfg.layers * per_layer)
     cfg = cl.cfg
     cpu = {"value": round(v, 4), "unit": UNIT, "cores": cl.cores, "kind": "port",
+           "effective_gbs": round(cl.layer_bytes / per_layer / 1e9, 2),
            "sample": f"{args.steps} token-layers (1 of 28 layers each), extrapolated x28; C restatement"}
     line = {"metric": METRIC, "value": round(v, 4), "unit": UNIT, "n_gpus": args.gpus, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(1000.0 * per_layer * cfg.layers, 3),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "u2 codes x bf16 -> f32",
             "data": "synthetic", "impl": "reference",
-            "config": {"workload": cfg.name, "layers": cfg.layers, "hidden": cfg.hidden, "experts": cfg.experts,
-                       "top_k": cfg.top_k, "inter": cfg.inter, "batch": 1},
+            "config": c1_config(cfg, args.gpus),
             "cpu_baseline": cpu,
             "e2e": {"value": round(v, 4), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
@@ -301,11 +311,7 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
         line = {"metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world, "steps": args.steps,
                 "warmup": args.warmup, "ms_per_step": round(t_ms / args.steps, 4), "higher_is_better": True,
                 "scaling": "weak", "vs_baseline": None, "dtype": "u2 codes x bf16 -> f32", "data": "synthetic",
-                "config": {"workload": cfg.name, "layers": cfg.layers, "hidden": cfg.hidden, "experts": cfg.experts,
-                           "top_k": cfg.top_k, "inter": cfg.inter, "batch": 1, "group_size": cfg.group_size,
-                           "scales": "fp16", "router": "bf16", "parallelism": f"replicas x{world}",
-                           "layout": "packed experts (moe_pack_experts), transposed routers",
-                           "l2": "inputs larger than L2: 707 MB of weights per step, 31.7 GB resident"},
+                "config": c1_config(cfg, world),
                 "roofline": roof, "clocks": clocks, "gpu_launches": stack.launches_per_step * args.steps,
                 "device_error": dev_err, "e2e": e2e, "cpu_baseline": cpu}
         print(json.dumps(line), flush=True)

@@ -87,7 +87,10 @@ int moe_router_topk(const void *x, int T, int H, int E, int K,
  * Scratch lives in a fixed array of 257 KiB that every device which loads the library holds
  * until the process exits; limits: T <= 256 and T * E <= 65536, larger sizes return
  * MOE_EINVAL. The first call on a device looks up that device's copy of the array (make it
- * with the device current, before any stream capture). Every call shares the array and it
+ * with the device current, before any stream capture); the lookup is repeated when the
+ * device's context has changed since (after a cudaDeviceReset, which reloads the module at
+ * a new address), so that first call after a reset must come before any stream capture
+ * too. Every call shares the array and it
  * keeps the last call's contents (the per-token tickets are cleared at the start of each
  * call); calls that overlap on the GPU race. Allocates nothing (no cudaMalloc/cudaFree).
  */

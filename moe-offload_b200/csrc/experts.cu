@@ -128,7 +128,10 @@ __global__ void __launch_bounds__(kGuWarps * 32) gateup_kernel(GuArgs a) {
         }
     }
     __syncthreads();
-    const bool wok = sok && xok && mbar_wait(&bars[1], 0);
+    // the weight copies were issued whenever the slot is valid: wait for them even when the x
+    // wait failed, so no bulk copy is still writing shared memory when the CTA exits
+    const bool wdone = sok && mbar_wait(&bars[1], 0);
+    const bool wok = wdone && xok;
 
     const uint16_t *sgs = reinterpret_cast<const uint16_t *>(wsm + 2 * cb);
     const uint16_t *bgs = sgs + 8 * ng, *sus = bgs + 8 * ng, *bus = sus + 8 * ng;
@@ -305,7 +308,10 @@ __global__ void __launch_bounds__(kMaxK * 32) down_kernel(DnArgs a) {
         }
     }
     __syncthreads();
-    const bool wok = sok && aok && mbar_wait(&bars[1 + k], 0);
+    // wait for this expert's weight copies whenever they were issued (even after a failed
+    // activation wait), so no bulk copy is in flight when the CTA exits
+    const bool wdone = sok && mbar_wait(&bars[1 + k], 0);
+    const bool wok = wdone && aok;
 
     const uint16_t *sds = reinterpret_cast<const uint16_t *>(my + cb);
     const uint16_t *bds = sds + 16 * ng;

@@ -7,6 +7,8 @@
 // framework's allocator so that any further cudaMalloc fails. This file gives those
 // callers moe_router_topk_noalloc, which keeps the same scratch in a fixed-size array that
 // is part of the library image on each device.
+#include <cuda.h>
+
 #include <mutex>
 
 #include "common.cuh"
@@ -31,10 +33,26 @@ namespace {
 constexpr int kMaxDevices = 64;
 std::mutex g_scratch_mu;
 unsigned char *g_scratch_dev[kMaxDevices] = {};
+unsigned long long g_scratch_ctx[kMaxDevices] = {};   // unique id of the context the address belongs to
+using CtxGetCurrentFn = CUresult (*)(CUcontext *);
+using CtxGetIdFn = CUresult (*)(CUcontext, unsigned long long *);
+CtxGetCurrentFn g_ctx_get_current = nullptr;
+CtxGetIdFn g_ctx_get_id = nullptr;
+
+// unique id of the calling thread's current context, 0 if none is bound
+unsigned long long current_ctx_id() {
+    CUcontext ctx = nullptr;
+    unsigned long long id = 0;
+    if (g_ctx_get_current(&ctx) != CUDA_SUCCESS || !ctx) return 0;
+    if (g_ctx_get_id(ctx, &id) != CUDA_SUCCESS) return 0;
+    return id;
+}
 
 // Device address of this device's copy of the scratch array. In host code the array's name
-// is only a host-side handle, so the address is looked up once per device (with that device
-// current) through cudaGetSymbolAddress and cached.
+// is only a host-side handle, so the address is looked up through cudaGetSymbolAddress with
+// the device current and cached together with the context it belongs to. A cudaDeviceReset
+// between two calls destroys that context and reloads the module at a new address; the
+// cached address is then stale, so a changed current context triggers a fresh lookup.
 int scratch_for_current_device(unsigned char **out) {
     int dev = -1;
     cudaError_t e = cudaGetDevice(&dev);
@@ -42,11 +60,29 @@ int scratch_for_current_device(unsigned char **out) {
     if (dev < 0 || dev >= kMaxDevices)
         return moe_set_error(MOE_ENODEV, "router_topk_noalloc: device %d out of range", dev);
     std::lock_guard<std::mutex> lock(g_scratch_mu);
-    if (!g_scratch_dev[dev]) {
+    if (!g_ctx_get_current || !g_ctx_get_id) {
+        void *f1 = nullptr, *f2 = nullptr;
+        cudaDriverEntryPointQueryResult q1, q2;
+        e = cudaGetDriverEntryPoint("cuCtxGetCurrent", &f1, cudaEnableDefault, &q1);
+        if (e != cudaSuccess) return moe_set_cuda_error(e);
+        e = cudaGetDriverEntryPoint("cuCtxGetId", &f2, cudaEnableDefault, &q2);
+        if (e != cudaSuccess) return moe_set_cuda_error(e);
+        if (q1 != cudaDriverEntryPointSuccess || !f1 || q2 != cudaDriverEntryPointSuccess || !f2)
+            return moe_set_error(MOE_ECUDA, "router_topk_noalloc: context queries not available from the driver");
+        g_ctx_get_current = reinterpret_cast<CtxGetCurrentFn>(f1);
+        g_ctx_get_id = reinterpret_cast<CtxGetIdFn>(f2);
+    }
+    // 0 on a host thread where the runtime has not bound the primary context yet; the
+    // symbol lookup below binds it
+    unsigned long long id = current_ctx_id();
+    if (id == 0 || !g_scratch_dev[dev] || g_scratch_ctx[dev] != id) {
         void *p = nullptr;
         e = cudaGetSymbolAddress(&p, g_router_noalloc_scratch);
         if (e != cudaSuccess) return moe_set_cuda_error(e);
+        id = current_ctx_id();
+        if (id == 0) return moe_set_error(MOE_ECUDA, "router_topk_noalloc: no current CUDA context");
         g_scratch_dev[dev] = static_cast<unsigned char *>(p);
+        g_scratch_ctx[dev] = id;
     }
     *out = g_scratch_dev[dev];
     return MOE_OK;

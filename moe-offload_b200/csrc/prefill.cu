@@ -118,6 +118,35 @@ MOE_D void mbar_arrive(uint64_t *bar) {
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
 }
 
+// Bounded wait that also gives up once another warp of the CTA has aborted (the flag is
+// polled every 1024 tries). On its own timeout it records the device error and raises the
+// CTA's abort flag. Warp-uniform result: every lane of the calling warp must call it.
+MOE_D bool wait_or_abort(uint64_t *bar, uint32_t parity, volatile int *abort) {
+    bool ok = false, gave_up = false;
+#pragma unroll 1
+    for (uint32_t i = 0; i < kMbarSpinLimit; ++i) {
+        if (mbar_try_wait(bar, parity)) {
+            ok = true;
+            break;
+        }
+        if ((i & 1023u) == 1023u && *abort) {
+            gave_up = true;
+            break;
+        }
+    }
+    ok = __all_sync(0xffffffffu, ok);
+    if (!ok) {                                             // warp-uniform branch
+        const bool timed_out = !__any_sync(0xffffffffu, gave_up);
+        if ((threadIdx.x & 31) == 0) {
+            if (timed_out) atomicOr(&g_moe_device_error, MOE_DEVERR_MBAR_TIMEOUT);
+            *abort = 1;
+        }
+    }
+    return ok;
+}
+
+MOE_D bool aborted(volatile int *abort) { return __any_sync(0xffffffffu, *abort != 0); }
+
 // 2-D tiled TMA load (no multicast) completing on an mbarrier; x is the innermost coordinate
 MOE_D void tma_load_2d(void *dst, const CUtensorMap *map, int x, int y, uint64_t *bar) {
     asm volatile(
@@ -309,8 +338,8 @@ struct GemmSmem {
     static constexpr size_t b = raw + (size_t)kRS * kNM * kTile;           // [kBS] tiles
     static constexpr size_t bars = b + (size_t)kBS * kTile;
     // raw_full, raw_empty [kRS]; full, empty [kKS]; b_full, b_empty [kBS]; acc_full, acc_empty
-    // [2] (accumulator halves); tmem slot
-    static constexpr size_t total = bars + (2 * kRS + 2 * kKS + 2 * kBS + 4) * 8 + 16;
+    // [2] (accumulator halves); drain (MMA completion after an abort); tmem slot, abort flag
+    static constexpr size_t total = bars + (2 * kRS + 2 * kKS + 2 * kBS + 5) * 8 + 16;
     static constexpr size_t alloc = total + 1024;      // + alignment slack
 };
 
@@ -331,7 +360,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     uint64_t *b_empty = b_full + kBS;
     uint64_t *acc_full = b_empty + kBS;          // [2]
     uint64_t *acc_empty = acc_full + 2;          // [2]
-    uint32_t *tslot = reinterpret_cast<uint32_t *>(acc_empty + 2);
+    uint64_t *drain = acc_empty + 2;             // [1]
+    uint32_t *tslot = reinterpret_cast<uint32_t *>(drain + 1);
+    // set by the first failed wait of any role: every role then stops, the epilogue stores
+    // nothing, and the producer / MMA issuer drain what they already issued before exit
+    volatile int *abort = reinterpret_cast<volatile int *>(tslot + 1);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
 
     if (tid == 0) {
@@ -351,6 +384,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             mbar_init(&acc_full[h], 1);
             mbar_init(&acc_empty[h], 4);
         }
+        mbar_init(drain, 1);
+        *abort = 0;
         fence_barrier_init();
     }
     if (warp == 1) {
@@ -368,14 +403,18 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     if (warp == 0) {
         // ------------------------------------------------------------ TMA producer
         uint32_t g = 0, rc = 0;
-        for (int ti = blockIdx.x; ti < ntiles; ti += gridDim.x) {
+        bool stop = false;
+        for (int ti = blockIdx.x; ti < ntiles && !stop; ti += gridDim.x) {
             const Tile tl = a.tiles[ti];
             const int wrow = tl.e * a.R + tl.row0;
             const int nbox = (tl.n + 15) >> 4;
             for (int kb = 0; kb < nkb; ++kb) {
                 if (kb % kRawK == 0) {
                     const int rs = rc % kRS;
-                    mbar_wait(&raw_empty[rs], ((rc / kRS) & 1u) ^ 1u);
+                    if (aborted(abort) || !wait_or_abort(&raw_empty[rs], ((rc / kRS) & 1u) ^ 1u, abort)) {
+                        stop = true;
+                        break;
+                    }
                     if (lane == 0) {
                         mbar_arrive_expect_tx(&raw_full[rs], kNM * kTile);
                         tma_load_2d(smem + SL::raw + (size_t)(rs * kNM) * kTile, &map_w0, kb * 4, wrow, &raw_full[rs]);
@@ -385,7 +424,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                     ++rc;
                 }
                 const int s = g % kBS;
-                mbar_wait(&b_empty[s], ((g / kBS) & 1u) ^ 1u);
+                if (!wait_or_abort(&b_empty[s], ((g / kBS) & 1u) ^ 1u, abort)) {
+                    stop = true;
+                    break;
+                }
                 unsigned char *bst = smem + SL::b + (size_t)s * kTile;
                 if (lane == 0) mbar_arrive_expect_tx(&b_full[s], (uint32_t)nbox * 2048u);
                 __syncwarp();
@@ -395,24 +437,41 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                 ++g;
             }
         }
+        if (aborted(abort)) {
+            // no bulk copy may still be writing shared memory when the CTA exits: wait (bounded)
+            // for the last load issued into every stage; earlier ones completed before their
+            // stage was reissued
+            for (uint32_t i = rc > (uint32_t)kRS ? rc - kRS : 0u; i < rc; ++i) mbar_wait(&raw_full[i % kRS], (i / kRS) & 1u);
+            for (uint32_t i = g > (uint32_t)kBS ? g - kBS : 0u; i < g; ++i) mbar_wait(&b_full[i % kBS], (i / kBS) & 1u);
+        }
     } else if (warp == 1) {
         // ------------------------------------------------------------ MMA issuer
         uint32_t g = 0, use0 = 0, use1 = 0, nxt = 0;  // acquisitions of each accumulator half
-        for (int ti = blockIdx.x; ti < ntiles; ti += gridDim.x) {
+        bool stop = false, issued = false;
+        for (int ti = blockIdx.x; ti < ntiles && !stop; ti += gridDim.x) {
             const Tile tl = a.tiles[ti];
             const int BN = (tl.n + 15) & ~15;
             const uint32_t idesc = instr_desc_bf16(BN);
             const bool wide = BN > 64;
             const uint32_t h = nxt;
-            if (wide || h == 0) mbar_wait(&acc_empty[0], (use0 & 1u) ^ 1u), ++use0;
-            if (wide || h == 1) mbar_wait(&acc_empty[1], (use1 & 1u) ^ 1u), ++use1;
+            if (aborted(abort)) break;
+            if (wide || h == 0) {
+                if (!wait_or_abort(&acc_empty[0], (use0 & 1u) ^ 1u, abort)) break;
+                ++use0;
+            }
+            if (wide || h == 1) {
+                if (!wait_or_abort(&acc_empty[1], (use1 & 1u) ^ 1u, abort)) break;
+                ++use1;
+            }
             const uint32_t col = wide ? 0u : 64u * h;
             if (!wide) nxt ^= 1u;
             tc_fence_after();
             for (int kb = 0; kb < nkb; ++kb) {
                 const int s = g % kKS, sb = g % kBS;
-                mbar_wait(&b_full[sb], (g / kBS) & 1u);
-                mbar_wait(&full[s], (g / kKS) & 1u);
+                if (!wait_or_abort(&b_full[sb], (g / kBS) & 1u, abort) || !wait_or_abort(&full[s], (g / kKS) & 1u, abort)) {
+                    stop = true;
+                    break;
+                }
                 tc_fence_after();
                 if (lane == 0) {
                     const uint32_t at = tmem + kTmemA + (uint32_t)s * kTmemAStage;
@@ -427,14 +486,22 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                     mma_commit(&empty[s]);
                     mma_commit(&b_empty[sb]);
                 }
+                issued = true;
                 __syncwarp();
                 ++g;
             }
+            if (stop) break;
             if (lane == 0) {
                 if (wide || h == 0) mma_commit(&acc_full[0]);
                 if (wide || h == 1) mma_commit(&acc_full[1]);
             }
             __syncwarp();
+        }
+        if (aborted(abort) && issued) {
+            // every MMA this thread issued must finish before the accumulators are freed
+            if (lane == 0) mma_commit(drain);
+            __syncwarp();
+            mbar_wait(drain, 0);
         }
     } else if (warp >= kEpiWarp0 && warp < kEpiWarp0 + 4) {
         // ------------------------------------------------------------ epilogue
@@ -444,8 +511,15 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             const Tile tl = a.tiles[ti];
             const bool wide = ((tl.n + 15) & ~15) > 64;
             const uint32_t h = nxt;
-            if (wide || h == 0) mbar_wait(&acc_full[0], f0 & 1u), ++f0;
-            if (wide || h == 1) mbar_wait(&acc_full[1], f1 & 1u), ++f1;
+            if (aborted(abort)) break;            // no stores of accumulators that may be incomplete
+            if (wide || h == 0) {
+                if (!wait_or_abort(&acc_full[0], f0 & 1u, abort)) break;
+                ++f0;
+            }
+            if (wide || h == 1) {
+                if (!wait_or_abort(&acc_full[1], f1 & 1u, abort)) break;
+                ++f1;
+            }
             const uint32_t col = wide ? 0u : 64u * h;
             if (!wide) nxt ^= 1u;
             tc_fence_after();
@@ -508,10 +582,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         };
         uint32_t g = 0, rc = 0;
         if ((int)blockIdx.x < ntiles) load_sb(a.tiles[blockIdx.x], 0);
-        for (int ti = blockIdx.x; ti < ntiles; ti += gridDim.x) {
+        bool stop = false;
+        for (int ti = blockIdx.x; ti < ntiles && !stop; ti += gridDim.x) {
             const Tile tl = a.tiles[ti];
             const bool rok = tl.row0 + roff < a.R;
-            for (int st = 0; st < nst; ++st) {
+            for (int st = 0; st < nst && !stop; ++st) {
 #pragma unroll
                 for (int i = 0; i < kRawK; ++i) {
                     cs[i] = ns[i];
@@ -520,13 +595,19 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                 if (st + 1 < nst) load_sb(tl, st + 1);
                 else if (ti + (int)gridDim.x < ntiles) load_sb(a.tiles[ti + gridDim.x], 0);
                 const int rs = rc % kRS;
-                mbar_wait(&raw_full[rs], (rc / kRS) & 1u);
+                if (aborted(abort) || !wait_or_abort(&raw_full[rs], (rc / kRS) & 1u, abort)) {
+                    stop = true;
+                    break;
+                }
                 const unsigned char *rbase = smem + SL::raw + (size_t)(rs * kNM + m) * kTile;
 #pragma unroll
                 for (int i = 0; i < kRawK; ++i) {
                     if (st * kRawK + i < nkb) {
                         const int s = g % kKS;
-                        mbar_wait(&empty[s], ((g / kKS) & 1u) ^ 1u);
+                        if (!wait_or_abort(&empty[s], ((g / kKS) & 1u) ^ 1u, abort)) {
+                            stop = true;
+                            break;
+                        }
                         tc_fence_after();
                         uint4 q = *reinterpret_cast<const uint4 *>(rbase + sw128(r, i));
                         if (!rok) q = make_uint4(0u, 0u, 0u, 0u);
@@ -546,6 +627,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                     }
                 }
                 __syncwarp();
+                if (stop) break;
                 if (lane == 0) mbar_arrive(&raw_empty[rs]);
                 ++rc;
             }

@@ -184,7 +184,9 @@ def make_lru_trace(lib_path: str) -> None:
 
 def main() -> int:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default=os.environ.get("MOE_REF_ROOT", "/root/reference"))
+    # the reference checkout: $MOE_REF_ROOT, else a directory named `reference` beside this repository
+    ap.add_argument("--ref", default=os.environ.get("MOE_REF_ROOT",
+                                                    os.path.join(os.path.dirname(ROOT), "reference")))
     args = ap.parse_args()
     make_moe_fixture(args.ref)
     make_hc_fixture(args.ref)

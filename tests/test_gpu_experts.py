@@ -55,8 +55,9 @@ def test_fixture_experts(moe_fixture, dev):
         assert _rel(act, ref["act"]) < 2e-3
         assert _rel(yk, ref["yk"]) < 5e-3
         assert _rel(y, ref["y"]) < REL_TOL
-        # and against the reference's MLX output (its own residual, see the oracle tests)
-        assert _rel(y, fx[f"moe.y_{tag}"].reshape(-1, 256)) < 1.5e-2
+        # and against the reference's MLX output: within the north-star 1e-2 (MLX's own residual
+        # against the exact arithmetic is 0.95 % decode / 0.48 % prefill, see the oracle tests)
+        assert _rel(y, fx[f"moe.y_{tag}"].reshape(-1, 256)) < 1e-2
 
 
 @pytest.mark.parametrize("T,H,I,E,K", [(1, 3072, 768, 24, 10), (2, 2048, 768, 16, 8), (1, 2688, 1856, 12, 9),
