@@ -98,6 +98,7 @@ SIGNATURES: dict[str, tuple] = {
     "c_get_decode_totals": (None, [I, P]),
     "moe_stack_workspace_bytes": (SZ, [I, I, I, I]),
     "moe_stack_decode": (I, [P, I, I, I, I, I, I, I, P, P, P, P, P, P, SZ, I, P]),
+    "moe_stack_decode_ex": (I, [P, I, I, I, I, I, I, I, P, P, P, P, P, P, SZ, I, I, P, P]),
 }
 
 
