@@ -52,8 +52,6 @@ def parse():
                          "split across the ranks); p1: the P1 I/O scheduler filling c2-shaped expert slots; f3: the "
                          "hyper-connection mixer + shared expert in front of each of the 28 MoE blocks, decode")
     ap.add_argument("--batch", type=int, default=0, help="c4: tokens per decode step (default: one per GPU)")
-    ap.add_argument("--no-speculate", action="store_true",
-                    help="c1: run the persistent kernel without speculative next-layer copies")
     ap.add_argument("--layers", type=int, default=0,
                     help="profiling aid: run only the first N layers of the stack (0 = all 28)")
     return ap.parse_args()
@@ -225,7 +223,7 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
         import dataclasses
         cfg = dataclasses.replace(cfg, name=f"{cfg.name}_first{args.layers}", layers=args.layers)
     layers = dev_stack(cfg, dev)
-    stack = PersistentStack(layers, cfg.top_k, dev, release_unpacked=True, speculate=not args.no_speculate)
+    stack = PersistentStack(layers, cfg.top_k, dev, release_unpacked=True)
     del layers
     torch.cuda.empty_cache()
     gen = torch.Generator(device=dev)
@@ -241,7 +239,6 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
     for i in range(args.warmup):
         stack.step_device(h0[i])
     torch.cuda.synchronize()
-    stack.spec_stats.zero_()
     barrier()
     clk = ClockSampler(local_rank)
     clk.start()
@@ -263,10 +260,6 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
     value = world * args.steps / (t_ms / 1000.0)
     from moe_offload_b200 import _lib
     dev_err = int(_lib.call("moe_device_error", 1))
-    hit = stack.prediction_hit_rate()
-    spec = {"enabled": not args.no_speculate,
-            "prediction_hit_rate": None if hit is None else round(hit, 4),
-            "predictor": "top-10 of router_{l+1} . h_l (the reference's next-layer predictor), timed steps"}
 
     e2e = None
     if not args.no_e2e:
@@ -320,7 +313,7 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
                 "scaling": "weak", "vs_baseline": None, "dtype": "u2 codes x bf16 -> f32", "data": "synthetic",
                 "config": c1_config(cfg, world),
                 "roofline": roof, "clocks": clocks, "gpu_launches": stack.launches_per_step * args.steps,
-                "device_error": dev_err, "speculation": spec, "e2e": e2e, "cpu_baseline": cpu}
+                "device_error": dev_err, "e2e": e2e, "cpu_baseline": cpu}
         print(json.dumps(line), flush=True)
 
 
@@ -577,10 +570,6 @@ def run_c2(args, rank: int, world: int, local_rank: int) -> None:
     peak_h2d = h2d_peak_gbs(dev)
     from moe_offload_b200 import _lib
     dev_err = int(_lib.call("moe_device_error", 1))
-    hit = stack.prediction_hit_rate()
-    spec = {"enabled": not args.no_speculate,
-            "prediction_hit_rate": None if hit is None else round(hit, 4),
-            "predictor": "top-10 of router_{l+1} . h_l (the reference's next-layer predictor), timed steps"}
     value = args.steps / (t_ms / 1000.0)
     line = {"metric": "MoE decode tok/s (28-layer offload stack, 20 % LRU slot caches)", "value": round(value, 2),
             "unit": UNIT, "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
@@ -704,10 +693,6 @@ def run_c3(args, rank: int, world: int, local_rank: int) -> None:
             "router_ms_per_layer": round(router_ms, 4), "peak_source": tf_src}
     from moe_offload_b200 import _lib
     dev_err = int(_lib.call("moe_device_error", 1))
-    hit = stack.prediction_hit_rate()
-    spec = {"enabled": not args.no_speculate,
-            "prediction_hit_rate": None if hit is None else round(hit, 4),
-            "predictor": "top-10 of router_{l+1} . h_l (the reference's next-layer predictor), timed steps"}
     cpu = None
     if not args.no_cpu:
         cpu = cpu_layer_sample()
@@ -788,10 +773,6 @@ def run_c4(args, rank: int, world: int, local_rank: int) -> None:
     value = B * args.steps / (t_ms / 1000.0)
     from moe_offload_b200 import _lib
     dev_err = int(_lib.call("moe_device_error", 1))
-    hit = stack.prediction_hit_rate()
-    spec = {"enabled": not args.no_speculate,
-            "prediction_hit_rate": None if hit is None else round(hit, 4),
-            "predictor": "top-10 of router_{l+1} . h_l (the reference's next-layer predictor), timed steps"}
 
     e2e = None
     if not args.no_e2e:

@@ -202,21 +202,6 @@ int moe_stack_decode(const void *layers, int L, int H, int I, int E, int K, int 
                      const void *x, void *y, uint32_t *inds_out, void *scores_out, void *hs_out,
                      void *workspace, size_t workspace_bytes, int num_ctas, void *stream);
 
-/* moe_stack_decode with options. flags: MOE_STACK_SPECULATE (moe_stack_decode's default) lets
- * the CTAs without a work item (num_ctas - K * I/64 of them) compute each next layer's
- * predicted experts -- the top-K of router_{l+1} . h_l, the reference's next-layer predictor
- * (mlx-qwen38/loader.py:237-242, 950-956) -- while the layer runs, and every other CTA start
- * copying its slice of the next layer's predicted experts into shared memory as soon as it
- * is done with the current layer; a mispredicted slice is dropped and fetched again. The
- * prediction only decides which copies start early: outputs, indices and scores are
- * bit-identical with and without it. It is used when L > 1, E <= 512, E % 8 == 0 and
- * num_ctas > K * I/64 (else the call runs without it). spec_stats (device, or NULL): [0] +=
- * experts routed in layers that had a prediction, [1] += those that were predicted. */
-#define MOE_STACK_SPECULATE 1
-int moe_stack_decode_ex(const void *layers, int L, int H, int I, int E, int K, int sb_fp16, int norm,
-                        const void *x, void *y, uint32_t *inds_out, void *scores_out, void *hs_out,
-                        void *workspace, size_t workspace_bytes, int num_ctas, int flags,
-                        unsigned int *spec_stats, void *stream);
 
 /* ------------------------------------------------------------------------------------ */
 /* Prefill: T tokens through one layer's routed experts as expert-grouped tcgen05 GEMMs.  */

@@ -9,7 +9,8 @@ import os
 import threading
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.path.join(HERE, "libmoe_b200.so")
+# MOE_B200_LIB selects another build of the same library (the profiling build of build.py --trace)
+LIB_PATH = os.environ.get("MOE_B200_LIB") or os.path.join(HERE, "libmoe_b200.so")
 
 P = ctypes.c_void_p
 I = ctypes.c_int
@@ -98,7 +99,6 @@ SIGNATURES: dict[str, tuple] = {
     "c_get_decode_totals": (None, [I, P]),
     "moe_stack_workspace_bytes": (SZ, [I, I, I, I]),
     "moe_stack_decode": (I, [P, I, I, I, I, I, I, I, P, P, P, P, P, P, SZ, I, P]),
-    "moe_stack_decode_ex": (I, [P, I, I, I, I, I, I, I, P, P, P, P, P, P, SZ, I, I, P, P]),
 }
 
 

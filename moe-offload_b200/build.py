@@ -38,14 +38,23 @@ def _stale(obj: str, src: str) -> bool:
     return any(os.path.getmtime(d) > t for d in deps)
 
 
-def build(verbose: bool = False, ptxas_info: bool = False, jobs: int = 8) -> str:
-    os.makedirs(OBJ, exist_ok=True)
+TRACE_LIB = os.path.join(HERE, "libmoe_b200_trace.so")
+TRACE_OBJ = os.path.join(HERE, "_build_trace")
+
+
+def build(verbose: bool = False, ptxas_info: bool = False, jobs: int = 8, trace: bool = False) -> str:
+    """Builds libmoe_b200.so; trace=True builds the profiling variant libmoe_b200_trace.so
+    instead (the persistent decode kernel records per-phase timestamps, MOE_STACK_TRACE)."""
+    obj_dir, lib = (TRACE_OBJ, TRACE_LIB) if trace else (OBJ, LIB)
+    os.makedirs(obj_dir, exist_ok=True)
     objs, cmds = [], []
     for src in sources():
-        obj = os.path.join(OBJ, os.path.basename(src) + ".o")
+        obj = os.path.join(obj_dir, os.path.basename(src) + ".o")
         objs.append(obj)
         if _stale(obj, src) or ptxas_info:
             extra = ["-Xptxas", "-v"] if ptxas_info else []
+            if trace:
+                extra.append("-DMOE_STACK_TRACE")
             cmds.append([NVCC] + _flags() + extra + ["-c", src, "-o", obj])
     procs = []
     for cmd in cmds:
@@ -55,12 +64,12 @@ def build(verbose: bool = False, ptxas_info: bool = False, jobs: int = 8) -> str
         if len(procs) >= jobs:
             _drain(procs, verbose or ptxas_info)
     _drain(procs, verbose or ptxas_info)
-    if cmds or not os.path.exists(LIB):
-        link = [NVCC] + ARCH + ["-shared", "-rdc=true", "-o", LIB] + objs
+    if cmds or not os.path.exists(lib):
+        link = [NVCC] + ARCH + ["-shared", "-rdc=true", "-o", lib] + objs
         if verbose:
             print(" ".join(link))
         subprocess.run(link, check=True)
-    return LIB
+    return lib
 
 
 def _drain(procs, show: bool) -> None:
@@ -75,5 +84,4 @@ def _drain(procs, show: bool) -> None:
 
 
 if __name__ == "__main__":
-    build(verbose="-v" in sys.argv, ptxas_info="--ptxas" in sys.argv)
-    print(LIB)
+    print(build(verbose="-v" in sys.argv, ptxas_info="--ptxas" in sys.argv, trace="--trace" in sys.argv))

@@ -34,11 +34,6 @@ MOE_D void mma_u8s8_16832(int d[4], uint32_t a0, uint32_t a1, uint32_t a2, uint3
         : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
-// Exact int -> float for |v| < 2^22 without the conversion unit: the integer is added into
-// the mantissa of 1.5 * 2^23 and that constant subtracted again (both steps exact). Every
-// integer dot of a 64-code group fits: |sum q * u| <= 64 * 3 * 2^14 < 2^22.
-MOE_D float i2f_small(int v) { return __int_as_float(0x4B400000 + v) - 12582912.0f; }
-
 // Does lane L hold a non-zero B fragment (column n = L>>2 belongs to lane quad t = n>>1)?
 MOE_D bool rec_lane_active(int lane) { return (lane & 3) == (lane >> 3); }
 // entry part (hi = 0, lo = 1) of an active lane

@@ -4,35 +4,20 @@
 //
 //   phase A  every CTA loads the layer's router logits (fp64 accumulators, see phase B) and
 //            h_l through L2, rounds the logits once to bf16 and runs the softmax / MLX-order
-//            top-k / renorm itself. Work item q = (item position p, activation group G of 64
-//            values), K * I/64 items over the CTAs: position p holds one of the K routed
-//            experts (see speculation below). The CTA fetches the item's packed slice with
-//            1-D TMA bulk copies (8 gate/up units + the down slice), builds the int8 MMA
-//            records of h_l while they are in flight, runs the 8 units (one warp pair each,
-//            as soon as its bytes land), keeps the 64 SwiGLU activations in shared memory,
-//            builds their one record, and runs the down slice: a split-K partial of the
-//            expert's output over all H rows, written to global memory   -> grid barrier
+//            top-k / renorm itself. Work item q = (routed expert k, activation group G of
+//            64 values), K * I/64 items over the CTAs: the CTA fetches the item's packed
+//            slice with 1-D TMA bulk copies (8 gate/up units + the down slice), builds the
+//            int8 MMA records of h_l while they are in flight, runs the 8 units (one warp
+//            pair each, as soon as its bytes land), keeps the 64 SwiGLU activations in
+//            shared memory, builds their one record, and runs the down slice: a split-K
+//            partial of expert k's output over all H rows, written to global memory
+//                                                                     -> grid barrier
 //   phase B  each CTA owns 8-row blocks of h: sums the I/64 partials of every routed
 //            expert for its rows (fixed order), rounds each expert output to bf16,
 //            combines with the routing scores and the residual into its rows of h_{l+1}
 //            (kept in shared memory across layers), and adds its rows' contribution to
 //            layer l+1's router logits (transposed router slices fetched during phase A,
 //            exact products, fp64 atomics)                             -> grid barrier
-//
-// Speculative next-layer copies (the reference's router prefetch, mlx-qwen38/loader.py:
-// 950-977, moved inside the kernel): a layer's 22 MB of expert slices take ~7 us to land
-// after they are requested, longer than any other phase, and the request can only go out
-// once the layer's routing is known. So the CTAs without a work item (G - K*I/64 of them)
-// compute layer l+1's predicted experts while layer l runs -- the top-K of
-// router_{l+1} . h_l, the reference's predictor, as fp32 partial sums over row blocks,
-// published by the last of them -- and every item CTA, right after its down slice, issues
-// the copy of its item for layer l+1's predicted expert at its position. The copy then
-// lands during the barrier, phase B, the next barrier and the next routing. At layer l+1
-// the routed experts that were predicted keep their predicted positions and the others take
-// the positions freed by mispredictions; a CTA whose position changed expert drains its
-// copy and fetches the right slice. Which expert sits at which position never changes a
-// value: phase B combines the experts in MLX order wherever their partials are, so results
-// are bit-identical with and without speculation.
 //
 // The router logit of expert e is the double-precision sum of per-CTA partial sums, each an
 // exact product sum; the bf16 rounding of that value equals the single rounding of the
@@ -60,9 +45,12 @@ constexpr uint32_t kGridSpinLimit = 1u << 24;
 constexpr int kAccCopies = 4;               // replicas of the logit accumulators (spread the atomics)
 static_assert(kWarps == 2 * kUnits, "one warp pair per unit");
 
-// Phase timestamps for profiling builds (compiled with -DMOE_STACK_TRACE): thread 0 of every
-// CTA records %globaltimer at fixed points of every layer into g_stack_trace[cta][layer][slot],
-// read back with moe_stack_trace_read. Off in the library build.
+// Phase timestamps for profiling builds (compiled with -DMOE_STACK_TRACE, see build.py
+// --trace): thread 0 of every CTA records %globaltimer at fixed points of every layer into
+// g_stack_trace[cta][layer][slot], read back with moe_stack_trace_read. Slots: 0 layer start,
+// 1 routed, 2 slice copies issued, 3 gate/up units done (after the block barrier), 4 item
+// work done, 6 first grid barrier passed, 7 phase B done, 10 down-slice bytes waited for,
+// 14 unit bytes waited for, 15 unit MMA loop done. The library build compiles them out.
 #ifdef MOE_STACK_TRACE
 constexpr int kTraceCtas = 160, kTraceLayers = 64, kTraceSlots = 16;
 __device__ unsigned long long g_stack_trace[kTraceCtas * kTraceLayers * kTraceSlots];
@@ -73,15 +61,9 @@ MOE_D void stamp(int layer, int slot) {
         g_stack_trace[((size_t)blockIdx.x * kTraceLayers + layer) * kTraceSlots + slot] = t;
     }
 }
-MOE_D void trace_value(int layer, int slot, unsigned long long v) {
-    if (threadIdx.x == 0 && blockIdx.x < kTraceCtas && layer < kTraceLayers)
-        g_stack_trace[((size_t)blockIdx.x * kTraceLayers + layer) * kTraceSlots + slot] = v;
-}
 #define STAMP(l, s) stamp((l), (s))
-#define TRACE_VALUE(l, s, v) trace_value((l), (s), (v))
 #else
 #define STAMP(l, s) ((void)0)
-#define TRACE_VALUE(l, s, v) ((void)0)
 #endif
 
 // device-side copy of moe_stack_layer (include/moe_b200.h), same layout
@@ -118,14 +100,8 @@ struct StackArgs {
     int norm;                             // power-of-two RMS normalisation of each layer's input
     uint16_t *hbuf;                       // [2][H]
     float *yp;                            // [K][I/64][H] partial down outputs (work item q = k * I/64 + G)
-    unsigned int *bar;                    // [3] grid barrier counter, prediction CTAs done, prediction
-                                          // published (= layer + 1); zero at launch
-    float *pacc;                          // [2][E] predicted logits of the next layer, zero at launch
-    uint32_t *plist;                      // [2][kMaxK] predicted experts of the next layer
-    unsigned int *spec_stats;             // [2] += (predicted experts, correctly predicted), or null
-    int spec;                             // speculative next-layer copies (host checked the conditions)
+    unsigned int *bar;                    // grid barrier counter, zero at launch
     unsigned int region;                  // bytes of the weight region in shared memory
-    unsigned int rsl;                     // bytes of the router-slice region in shared memory
 };
 
 // stride (in entries) of the entry-major record table of h: = 4 (mod 16) so that the eight
@@ -133,14 +109,13 @@ struct StackArgs {
 MOE_HD int rec_stride(int ngroups) { return (ngroups + 15) / 16 * 16 + 4; }
 
 struct SmemLayout {
-    size_t bars, region, rsl, xrec, xscale, xsum, arec, ascale, sact, ypart, hown, red, cand, comp, redu, redd,
-        sinds, sscores, xpos, posof, scr, sflag, dtr, total;
-    MOE_HD SmemLayout(int H, int I, int K, size_t region_bytes, size_t rsl_bytes) {
+    size_t bars, region, xrec, xscale, xsum, arec, ascale, sact, ypart, hown, red, cand, comp, redu, redd, sinds,
+        sscores, dtr, total;
+    MOE_HD SmemLayout(int H, int I, int K, size_t region_bytes) {
         const int ngH = H / 64, ngI = I / 64;
         bars = 0;                                                 // 16 mbarriers
         region = 128;
-        rsl = region + al128(region_bytes);                       // router slices of phase B
-        xrec = rsl + al128(rsl_bytes);
+        xrec = region + al128(region_bytes);
         xscale = xrec + (size_t)16 * rec_stride(ngH) * 8;
         xsum = xscale + al16((size_t)ngH * 4);
         arec = xsum + al128((size_t)ngH * 4);
@@ -155,11 +130,7 @@ struct SmemLayout {
         redd = redu + kWarps * 4;
         sinds = redd + kWarps * 8;
         sscores = sinds + kMaxK * 4;
-        xpos = sscores + kMaxK * 4;                               // expert at each item position
-        posof = xpos + kMaxK * 4;                                 // item position of MLX position k
-        scr = posof + kMaxK * 4;
-        sflag = scr + kMaxK * 4;                                  // [4] block-wide flags
-        dtr = al16(sflag + 16);                                   // [kWarps][64] int dot products
+        dtr = al16(sscores + kMaxK * 4);                          // [kWarps][64] int dot products
         total = dtr + (size_t)kWarps * 64 * 4;
     }
 };
@@ -170,19 +141,15 @@ MOE_D unsigned int ld_acquire(const unsigned int *p) {
     return v;
 }
 
-// Grid-wide barrier for a cooperative launch, split into arrival and wait so that a CTA can
-// work between the two: the counter only grows within a launch; barrier n waits for
-// (n + 1) * gridDim.x arrivals. Bounded: on timeout the device error word records it and the
-// CTA proceeds.
-MOE_D void grid_arrive(unsigned int *bar) {
+// Grid-wide barrier for a cooperative launch: the counter only grows within a launch;
+// barrier n waits for (n + 1) * gridDim.x arrivals. Bounded: on timeout the device error word
+// records it and the CTA proceeds.
+MOE_D void grid_sync(unsigned int *bar, unsigned int n) {
     __syncthreads();
-    // release: the block's writes (ordered before by the block barrier) become visible to
-    // every CTA whose acquire load observes this arrival
-    if (threadIdx.x == 0) asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(bar) : "memory");
-}
-
-MOE_D void grid_wait(unsigned int *bar, unsigned int n) {
     if (threadIdx.x == 0) {
+        // release: the block's writes (ordered before by the block barrier) become visible
+        // to every CTA whose acquire load observes this arrival
+        asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(bar) : "memory");
         const unsigned int target = (n + 1) * gridDim.x;
         uint32_t it = 0;
 #pragma unroll 1
@@ -194,15 +161,6 @@ MOE_D void grid_wait(unsigned int *bar, unsigned int n) {
         }
     }
     __syncthreads();
-}
-
-MOE_D void grid_sync(unsigned int *bar, unsigned int n) {
-    grid_arrive(bar);
-    grid_wait(bar, n);
-}
-
-MOE_D void st_release(unsigned int *p, unsigned int v) {
-    asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 
 // barrier over the two warps of unit pair p (named barriers 1..kUnits)
@@ -387,13 +345,13 @@ MOE_D void router_partial(uint64_t *rbar, uint32_t &rphase, const unsigned char 
     }
 }
 
-// issues the copies of expert e's slice of activation group G (threads 0..kUnits, one copy
-// each: the 8 gate/up units and the down slice)
-MOE_D void issue_item(const StackLayer &ly, const PackDims &P, uint32_t e, int G, unsigned char *region,
-                      uint64_t *ubar, uint64_t *dbar) {
+// issues the copies of work item q's packed slice (threads 0..kUnits)
+MOE_D void issue_item(const StackLayer &ly, const PackDims &P, const uint32_t *sinds, int q, int ngI,
+                      unsigned char *region, uint64_t *ubar, uint64_t *dbar) {
     const int tid = threadIdx.x;
     if (tid > kUnits) return;
-    const unsigned char *src = ly.experts + (size_t)e * P.ebytes + (size_t)G * P.gbytes;
+    const int k = q / ngI, G = q % ngI;
+    const unsigned char *src = ly.experts + (size_t)sinds[k] * P.ebytes + (size_t)G * P.gbytes;
     if (tid < kUnits) {
         mbar_arrive_expect_tx(&ubar[tid], P.ub);
         tma_load_1d(region + (size_t)tid * P.ub, src + (size_t)tid * P.ub, P.ub, &ubar[tid]);
@@ -403,168 +361,7 @@ MOE_D void issue_item(const StackLayer &ly, const PackDims &P, uint32_t e, int G
     }
 }
 
-// the router rows of this CTA's 8-row blocks (phase B's share of the next layer's logits)
-MOE_D void issue_router_slices(const StackLayer &ly, unsigned char *rsl, int b0, int nb, int E, uint64_t *rbar) {
-    if (nb <= 0) return;
-    const uint32_t rsb = 8u * (uint32_t)E * 2u;
-    mbar_arrive_expect_tx(rbar, rsb * (uint32_t)nb);
-#pragma unroll 1
-    for (int bi = 0; bi < nb; ++bi)
-        tma_load_1d(rsl + (size_t)bi * rsb, ly.router_t + (size_t)(b0 + bi) * 8 * E, rsb, rbar);
-}
-
-// the same nine copies issued by one thread (the speculative copy, issued while the rest of
-// the block waits at the grid barrier)
-MOE_D void issue_item_one_thread(const StackLayer &ly, const PackDims &P, uint32_t e, int G, unsigned char *region,
-                                 uint64_t *ubar, uint64_t *dbar) {
-    const unsigned char *src = ly.experts + (size_t)e * P.ebytes + (size_t)G * P.gbytes;
-#pragma unroll 1
-    for (int u = 0; u < kUnits; ++u) {
-        mbar_arrive_expect_tx(&ubar[u], P.ub);
-        tma_load_1d(region + (size_t)u * P.ub, src + (size_t)u * P.ub, P.ub, &ubar[u]);
-    }
-    mbar_arrive_expect_tx(dbar, P.dbytes);
-    tma_load_1d(region + P.dco, src + P.dco, P.dbytes, dbar);
-}
-
-// Warp 0: which routed expert each item position holds. Without a prediction position p
-// holds MLX position p. With one (plist: the K predicted experts, position p = plist[p]),
-// a routed expert that was predicted keeps its predicted position, and the routed experts
-// that were not predicted take the positions of the mispredicted ones, both in ascending
-// order. xpos[p] = expert at position p; posof[k] = position of MLX position k. Returns (on
-// lane 0) the number of routed experts that were predicted.
-MOE_D int assign_positions(bool have_pred, const uint32_t *plist, int K, const uint32_t *sinds, uint32_t *xpos,
-                           uint32_t *posof, uint32_t *scr) {
-    const int lane = threadIdx.x & 31;
-    if (!have_pred) {
-        if (lane < K) {
-            xpos[lane] = sinds[lane];
-            posof[lane] = (uint32_t)lane;
-        }
-        __syncwarp();
-        return 0;
-    }
-    const uint32_t pe = lane < K ? __ldcg(plist + lane) : 0xffffffffu;
-    const uint32_t ae = lane < K ? sinds[lane] : 0xfffffffeu;
-    bool in_a = false, in_p = false;
-    uint32_t ppos = 0;
-#pragma unroll 1
-    for (int j = 0; j < K; ++j) {
-        const uint32_t aj = __shfl_sync(0xffffffffu, ae, j), pj = __shfl_sync(0xffffffffu, pe, j);
-        in_a |= pe == aj;
-        if (ae == pj) {
-            in_p = true;
-            ppos = (uint32_t)j;
-        }
-    }
-    const unsigned free_p = __ballot_sync(0xffffffffu, lane < K && !in_a);   // mispredicted positions
-    const unsigned miss_a = __ballot_sync(0xffffffffu, lane < K && !in_p);   // routed, not predicted
-    const unsigned lt = (1u << lane) - 1u;
-    if (lane < K && !in_p) scr[__popc(miss_a & lt)] = ae;
-    __syncwarp();
-    const uint32_t xp = (lane < K) ? (in_a ? pe : scr[__popc(free_p & lt)]) : 0u;
-    __syncwarp();
-    if (lane < K && !in_a) scr[__popc(free_p & lt)] = (uint32_t)lane;
-    __syncwarp();
-    const uint32_t po = in_p ? ppos : ((lane < K) ? scr[__popc(miss_a & lt)] : 0u);
-    // a well-formed prediction (K distinct experts) always yields a permutation of the routed
-    // experts; anything else (a prediction that never arrived) falls back to MLX positions,
-    // so every expert id and position used later stays in range
-    // xpos[posof[k]] == sinds[k] for every k (with distinct routed experts this makes posof a
-    // permutation, and xpos the routed experts)
-    const uint32_t back = __shfl_sync(0xffffffffu, xp, (int)(po & 31u));
-    bool valid = lane >= K || (po < (uint32_t)K && back == ae);
-    bool found = lane >= K;
-#pragma unroll 1
-    for (int j = 0; j < K; ++j) found |= xp == __shfl_sync(0xffffffffu, ae, j);
-    valid = __all_sync(0xffffffffu, valid && found);
-    if (lane < K) {
-        xpos[lane] = valid ? xp : sinds[lane];
-        posof[lane] = valid ? po : (uint32_t)lane;
-    }
-    __syncwarp();
-    return valid ? K - __popc(miss_a) : 0;
-}
-
-// Prediction CTA (one without a work item): adds its row block of router_{l+1} . h_l to the
-// predicted logits (fp32), and the last of the G - NQ prediction CTAs of the layer selects
-// their top-K (descending) into plist and publishes it by a release store of l + 1 to pflag.
-// The router rows were requested into `rows` at the start of the phase (pbar).
-MOE_D void predict_next(const unsigned char *rows, float *ph, int pr0, int prn, int E, int K, const uint16_t *hcur,
-                        uint64_t *pbar, uint32_t &pphase, float *pacc, unsigned int *pcnt, unsigned int pcnt_target,
-                        uint32_t *plist, unsigned int *pflag, unsigned int flag_value, uint32_t *cand, int *sflag) {
-    const int tl = (int)flag_value - 1;      // the layer (for the profiling timestamps)
-    (void)tl;
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-#pragma unroll 1
-    for (int r = tid; r < prn; r += kThreads) ph[r] = bf16_bits_to_f32(__ldcg(hcur + pr0 + r));
-    __syncthreads();
-    bool ok = true;
-    if (prn > 0) {                   // the rows were requested only when there are any
-        ok = mbar_wait(pbar, pphase);
-        pphase ^= 1u;
-    }
-    STAMP(tl, 10);
-    if (ok && prn > 0 && tid < E) {
-        const uint16_t *rr = reinterpret_cast<const uint16_t *>(rows);
-        float p0 = 0.f, p1 = 0.f, p2 = 0.f, p3 = 0.f;
-        int r = 0;
-#pragma unroll 1
-        for (; r + 4 <= prn; r += 4) {
-            const uint16_t w0 = rr[(r + 0) * E + tid], w1 = rr[(r + 1) * E + tid];
-            const uint16_t w2 = rr[(r + 2) * E + tid], w3 = rr[(r + 3) * E + tid];
-            p0 = fmaf(bf16_bits_to_f32(w0), ph[r + 0], p0);
-            p1 = fmaf(bf16_bits_to_f32(w1), ph[r + 1], p1);
-            p2 = fmaf(bf16_bits_to_f32(w2), ph[r + 2], p2);
-            p3 = fmaf(bf16_bits_to_f32(w3), ph[r + 3], p3);
-        }
-#pragma unroll 1
-        for (; r < prn; ++r) p0 = fmaf(bf16_bits_to_f32(rr[r * E + tid]), ph[r], p0);
-        atomicAdd(pacc + tid, (p0 + p1) + (p2 + p3));
-        __threadfence();
-    }
-    __syncthreads();
-    if (tid == 0) {
-        __threadfence();
-        sflag[3] = (atomicAdd(pcnt, 1u) + 1u == pcnt_target) ? 1 : 0;
-    }
-    __syncthreads();
-    STAMP(tl, 11);
-    if (!sflag[3]) return;
-    // the last one: every partial is in pacc
-    __threadfence();
-    uint32_t key = 0;
-    if (tid < E) {
-        // larger logit first; the low 11 bits carry the expert (ties: the larger index)
-        key = (f2ord(__ldcg(pacc + tid)) & 0xfffff800u) | (uint32_t)tid;
-        pacc[tid] = 0.f;             // ready for the layer that accumulates here next
-    }
-    cand[tid] = key;
-    __syncthreads();
-    if (warp == 0) {
-        constexpr int kPer = kThreads / 32;
-        uint32_t kk[kPer];
-#pragma unroll
-        for (int i = 0; i < kPer; ++i) kk[i] = cand[lane + 32 * i];
-        uint32_t sel = 0;
-#pragma unroll 1
-        for (int r = 0; r < K; ++r) {
-            uint32_t m = kk[0];
-#pragma unroll
-            for (int i = 1; i < kPer; ++i) m = max(m, kk[i]);
-            const uint32_t w = __reduce_max_sync(0xffffffffu, m);
-            sel = (lane == r) ? w : sel;
-#pragma unroll
-            for (int i = 0; i < kPer; ++i) kk[i] = (kk[i] == w) ? 0u : kk[i];
-        }
-        if (lane < K) plist[lane] = sel & 0x7ffu;
-        __threadfence();
-        __syncwarp();
-        if (lane == 0) st_release(pflag, flag_value);
-    }
-}
-
-template <bool kFp16, int kKeysT, bool kSpec>
+template <bool kFp16, int kKeysT>
 __global__ void __launch_bounds__(kThreads, 1) stack_kernel(StackArgs a) {
     extern __shared__ __align__(128) unsigned char smem[];
     const int H = a.H, I = a.I, E = a.E, K = a.K, L = a.L;
@@ -575,23 +372,14 @@ __global__ void __launch_bounds__(kThreads, 1) stack_kernel(StackArgs a) {
     const int ngH = H / 64, ngI = I / 64, NQ = K * ngI, NB = H / 8, NT = H / 16;
     const int xst = rec_stride(ngH);
     const PackDims P(H, I);
-    const SmemLayout S(H, I, K, a.region, a.rsl);
+    const SmemLayout S(H, I, K, a.region);
     const int b0 = (int)((long long)c * NB / G), nb = (int)((long long)(c + 1) * NB / G) - b0;
     const int nrows = nb * 8;
-    // speculation: CTAs c >= NQ have no work item and compute the next layer's prediction
-    // over rows [pr0, pr0 + prn) of h
-    constexpr bool spec = kSpec;             // the host launches kSpec only when the conditions hold
-    const int npred = G - NQ;
-    const bool pred_cta = spec && c >= NQ;
-    const int pr0 = pred_cta ? (int)((long long)(c - NQ) * H / npred) : 0;
-    const int prn = pred_cta ? (int)((long long)(c - NQ + 1) * H / npred) - pr0 : 0;
 
     uint64_t *ubar = reinterpret_cast<uint64_t *>(smem + S.bars);          // [kUnits]
     uint64_t *dbar = ubar + kUnits;                                         // [1]
     uint64_t *rbar = dbar + 1;                                              // [1]
-    uint64_t *pbar = rbar + 1;                                              // [1]
     unsigned char *region = smem + S.region;
-    unsigned char *rsl = smem + S.rsl;
     uint2 *xrec = reinterpret_cast<uint2 *>(smem + S.xrec);                // [16][xst]
     float *xscale = reinterpret_cast<float *>(smem + S.xscale);
     float *xsum = reinterpret_cast<float *>(smem + S.xsum);
@@ -607,21 +395,16 @@ __global__ void __launch_bounds__(kThreads, 1) stack_kernel(StackArgs a) {
     double *redd = reinterpret_cast<double *>(smem + S.redd);
     uint32_t *sinds = reinterpret_cast<uint32_t *>(smem + S.sinds);
     float *sscores = reinterpret_cast<float *>(smem + S.sscores);
-    uint32_t *xpos = reinterpret_cast<uint32_t *>(smem + S.xpos);
-    uint32_t *posof = reinterpret_cast<uint32_t *>(smem + S.posof);
-    uint32_t *scr = reinterpret_cast<uint32_t *>(smem + S.scr);
-    int *sflag = reinterpret_cast<int *>(smem + S.sflag);   // [0] speculative copy issued, [1] its expert
     int *dtr = reinterpret_cast<int *>(smem + S.dtr);
 
     if (tid == 0) {
-        for (int i = 0; i < kUnits + 3; ++i) mbar_init(&ubar[i], 1);
-        sflag[0] = 0;
+        for (int i = 0; i < kUnits + 2; ++i) mbar_init(&ubar[i], 1);
         fence_barrier_init();
     }
     __syncthreads();
 
     unsigned int nbar = 0;
-    uint32_t rphase = 0, qphase = 0, pphase = 0;
+    uint32_t rphase = 0, qphase = 0;
     const uint32_t rsb = 8u * (uint32_t)E * 2u;    // router slice of one 8-row block
 
     // --------------------------------------------------------------- prologue: h_0 and layer-0 logits
@@ -629,7 +412,7 @@ __global__ void __launch_bounds__(kThreads, 1) stack_kernel(StackArgs a) {
         mbar_arrive_expect_tx(rbar, rsb * nb);
 #pragma unroll 1
         for (int bi = 0; bi < nb; ++bi)
-            tma_load_1d(rsl + (size_t)bi * rsb, a.layers[0].router_t + (size_t)(b0 + bi) * 8 * E, rsb, rbar);
+            tma_load_1d(region + (size_t)bi * rsb, a.layers[0].router_t + (size_t)(b0 + bi) * 8 * E, rsb, rbar);
     }
     double ssp = 0.0;
 #pragma unroll 1
@@ -643,55 +426,18 @@ __global__ void __launch_bounds__(kThreads, 1) stack_kernel(StackArgs a) {
     ssp = block_sum_d(ssp, redd);
     if (tid == 0 && a.norm && nb > 0) atomicAdd(a.ss, ssp);
     __syncthreads();
-    if (nb > 0) router_partial(rbar, rphase, rsl, hown, nrows, E, a.acc + (size_t)(c % kAccCopies) * E);
+    if (nb > 0) router_partial(rbar, rphase, region, hown, nrows, E, a.acc + (size_t)(c % kAccCopies) * E);
     grid_sync(a.bar, nbar++);
 
 #pragma unroll 1
     for (int l = 0; l < L; ++l) {
         const StackLayer ly = a.layers[l];
-        const bool last = l + 1 == L;
-        const bool have_pred = spec && l > 0;         // layer l-1 predicted this layer's experts
-        const bool predict = spec && !last;           // this layer predicts layer l+1's
         const double *accl = a.acc + (size_t)(l & 1) * kAccCopies * E;
         const uint16_t *hcur = a.hbuf + (size_t)(l & 1) * H;
         uint16_t *hnext = a.hbuf + (size_t)((l + 1) & 1) * H;
         STAMP(l, 0);
-        TRACE_VALUE(l, 8, (unsigned long long)(mbar_try_wait(&ubar[0], qphase) ? 1 : 0) +
-                              2ull * (mbar_try_wait(dbar, qphase) ? 1 : 0));
 
         // ---------------------------------------------------------- phase A
-        // a prediction CTA's rows of the next router, first thing (the item CTAs' slices
-        // are requested after the routing, the router slices of phase B after the items)
-        if (tid == 0) {
-            if (predict && pred_cta && prn > 0) {
-                mbar_arrive_expect_tx(pbar, (uint32_t)prn * (uint32_t)E * 2u);
-                tma_load_1d(region, a.layers[l + 1].router_t + (size_t)pr0 * E, (uint32_t)prn * (uint32_t)E * 2u,
-                            pbar);
-            }
-        }
-        // the accumulators phase B of this layer adds into were last read by the previous
-        // layer's routing, which every CTA finished before the last barrier
-        // (done by the last CTA: one without a work item whenever there is one). Without
-        // speculation every CTA routes before the first barrier, so CTA 0 clears the
-        // accumulators in phase B instead, once its own router partial is added.
-        if (kSpec && c == G - 1) {
-            double *accz = a.acc + (size_t)((l + 1) & 1) * kAccCopies * E;
-#pragma unroll 1
-            for (int e = tid; e < kAccCopies * E; e += kThreads) accz[e] = 0.0;
-            if (tid == 0) a.ss[(l + 1) & 1] = 0.0;
-        }
-        if (predict && pred_cta) {
-            // prediction first (its result is wanted before the item CTAs reach the barrier),
-            // then arrive, then this CTA's own routing while the others finish their items
-            predict_next(region, reinterpret_cast<float *>(region + al16((size_t)prn * E * 2)), pr0, prn, E, K, hcur,
-                         pbar, pphase, a.pacc + (size_t)((l + 1) & 1) * E, a.bar + 1,
-                         (unsigned int)(l + 1) * (unsigned int)npred, a.plist + (size_t)((l + 1) & 1) * kMaxK,
-                         a.bar + 2, (unsigned int)(l + 1), cand, sflag);
-            STAMP(l, 12);
-            if (tid == 0) issue_router_slices(a.layers[l + 1], rsl, b0, nb, E, rbar);
-            grid_arrive(a.bar);
-        }
-
         // loads through L2 (written by other SMs): logits, h_l, sum of squares
         double av[kKeysT];
 #pragma unroll
@@ -713,56 +459,23 @@ __global__ void __launch_bounds__(kThreads, 1) stack_kernel(StackArgs a) {
         const double xmul = a.norm ? ldexp(1.0, -pow2_rms_shift(__ldcg(a.ss + (l & 1)), H)) : 1.0;
 
         route<kKeysT>(av, xmul, E, K, redu, redd, cand, comp, sinds, sscores);
-        if constexpr (kSpec) {
-            // item positions (without speculation position p is MLX position p: xpos = sinds)
-            if (warp == 0) {
-                const int hits =
-                    assign_positions(have_pred, a.plist + (size_t)(l & 1) * kMaxK, K, sinds, xpos, posof, scr);
-                if (c == 0 && lane == 0 && have_pred && a.spec_stats) {
-                    atomicAdd(a.spec_stats, (unsigned int)K);
-                    atomicAdd(a.spec_stats + 1, (unsigned int)hits);
-                }
-            }
-        }
+        STAMP(l, 1);
         if (c == 0 && tid < K) {
             a.inds_out[(size_t)l * K + tid] = sinds[tid];
             a.scores_out[(size_t)l * K + tid] = f32_to_bf16_bits(sscores[tid]);
         }
-        if constexpr (kSpec) __syncthreads();
-        STAMP(l, 1);
-        TRACE_VALUE(l, 9, (unsigned long long)(mbar_try_wait(&ubar[0], qphase) ? 1 : 0) +
-                              2ull * (mbar_try_wait(dbar, qphase) ? 1 : 0));
-
-        if (predict && pred_cta) {
-            grid_wait(a.bar, nbar++);
-        } else {
-            if (c < NQ) {
-                const uint32_t e = kSpec ? xpos[c / ngI] : sinds[c / ngI];
-                if (have_pred && sflag[0]) {
-                    // this CTA's copy of its predicted item is in flight or has landed: keep it
-                    // when the position's expert was predicted, else drain it and fetch the item
-                    TRACE_VALUE(l, 13, (unsigned long long)((uint32_t)sflag[1] != e ? 1 : 0));
-                    if ((uint32_t)sflag[1] != e) {
-                        if (tid < kUnits) mbar_wait(&ubar[tid], qphase);
-                        else if (tid == kUnits) mbar_wait(dbar, qphase);
-                        qphase ^= 1u;
-                        issue_item(ly, P, e, c % ngI, region, ubar, dbar);
-                    }
-                } else {
-                    issue_item(ly, P, e, c % ngI, region, ubar, dbar);
-                }
-            }
-            STAMP(l, 2);
-            // records of h_l * xmul (entry-major) while the copies are in flight
+        if (c < NQ) issue_item(ly, P, sinds, c, ngI, region, ubar, dbar);
+        STAMP(l, 2);
+        // records of h_l * xmul (entry-major) while the copies are in flight
 #pragma unroll
-            for (int p = 0; p < kHPass; ++p) {
-                const int Gp = (tid >> 4) + p * (kThreads / 16);
-                if (p * (kThreads / 16) < ngH)
-                    rec_from_regs(hq[p], Gp < ngH, xrec + Gp, xscale + Gp, xsum + Gp, (float)xmul, xst);
-            }
-            __syncthreads();
+        for (int p = 0; p < kHPass; ++p) {
+            const int Gp = (tid >> 4) + p * (kThreads / 16);
+            if (p * (kThreads / 16) < ngH)
+                rec_from_regs(hq[p], Gp < ngH, xrec + Gp, xscale + Gp, xsum + Gp, (float)xmul, xst);
+        }
+        __syncthreads();
 #pragma unroll 1
-            for (int q = c; q < NQ; q += G) {
+        for (int q = c; q < NQ; q += G) {
             // gate/up unit p = warp pair, H split in halves between the two warps
             {
                 const int p = warp >> 1, half = warp & 1;
@@ -786,9 +499,9 @@ __global__ void __launch_bounds__(kThreads, 1) stack_kernel(StackArgs a) {
                         int dg, du;
                         mma_step_i8t(wv, uv, xrec + Gj, xst, bact, part, dg, du);
                         const float sc = xscale[Gj], sm = xsum[Gj];
-                        accg += sb_to_f32<kFp16>((uint16_t)sb.x) * (i2f_small(dg) * sc) +
+                        accg += sb_to_f32<kFp16>((uint16_t)sb.x) * ((float)dg * sc) +
                                 sb_to_f32<kFp16>((uint16_t)(sb.x >> 16)) * sm;
-                        accu += sb_to_f32<kFp16>((uint16_t)sb.y) * (i2f_small(du) * sc) +
+                        accu += sb_to_f32<kFp16>((uint16_t)sb.y) * ((float)du * sc) +
                                 sb_to_f32<kFp16>((uint16_t)(sb.y >> 16)) * sm;
                     }
                 }
@@ -863,9 +576,9 @@ __global__ void __launch_bounds__(kThreads, 1) stack_kernel(StackArgs a) {
                         const int2 dd = *reinterpret_cast<const int2 *>(yb + j * 16 + rr);
                         const uint2 sp = *reinterpret_cast<const uint2 *>(ds + row);
                         float2 o;
-                        o.x = sb_to_f32<kFp16>((uint16_t)sp.x) * (i2f_small(dd.x) * asc) +
+                        o.x = sb_to_f32<kFp16>((uint16_t)sp.x) * ((float)dd.x * asc) +
                               sb_to_f32<kFp16>((uint16_t)(sp.x >> 16)) * asm_;
-                        o.y = sb_to_f32<kFp16>((uint16_t)sp.y) * (i2f_small(dd.y) * asc) +
+                        o.y = sb_to_f32<kFp16>((uint16_t)sp.y) * ((float)dd.y * asc) +
                               sb_to_f32<kFp16>((uint16_t)(sp.y >> 16)) * asm_;
                         if (!wok) o = make_float2(0.f, 0.f);
                         *reinterpret_cast<float2 *>(ypq + row) = o;
@@ -875,46 +588,27 @@ __global__ void __launch_bounds__(kThreads, 1) stack_kernel(StackArgs a) {
             }
             __syncthreads();
             qphase ^= 1u;
-            if (q + G < NQ)
-                issue_item(ly, P, kSpec ? xpos[(q + G) / ngI] : sinds[(q + G) / ngI], (q + G) % ngI, region, ubar,
-                           dbar);
-            }
-            STAMP(l, 4);
-            // the next layer's router slices of this CTA's rows (phase B) into their own region
-            if (tid == 0 && !last) issue_router_slices(a.layers[l + 1], rsl, b0, nb, E, rbar);
-            grid_arrive(a.bar);
-            if (predict && c < NQ && tid == 0) {
-                // the speculative copy of this CTA's item of layer l+1 into the consumed region,
-                // once the prediction CTAs have published the predicted experts
-                uint32_t it = 0;
-                bool ok = true;
-#pragma unroll 1
-                while (ld_acquire(a.bar + 2) < (unsigned int)(l + 1)) {
-                    if (++it > kGridSpinLimit) {
-                        atomicOr(&g_moe_device_error, MOE_DEVERR_MBAR_TIMEOUT);
-                        ok = false;
-                        break;
-                    }
-                }
-                const uint32_t pe = ok ? __ldcg(a.plist + (size_t)((l + 1) & 1) * kMaxK + c / ngI) : 0xffffffffu;
-                ok = ok && pe < (uint32_t)E;
-                if (ok) issue_item_one_thread(a.layers[l + 1], P, pe, c % ngI, region, ubar, dbar);
-                sflag[0] = ok ? 1 : 0;
-                sflag[1] = (int)pe;
-                STAMP(l, 5);
-            }
-            grid_wait(a.bar, nbar++);
+            if (q + G < NQ) issue_item(ly, P, sinds, q + G, ngI, region, ubar, dbar);
         }
+        STAMP(l, 4);
+        // next layer's router slices into the consumed weight region
+        if (tid == 0 && l + 1 < L && nb > 0) {
+            mbar_arrive_expect_tx(rbar, rsb * nb);
+#pragma unroll 1
+            for (int bi = 0; bi < nb; ++bi)
+                tma_load_1d(region + (size_t)bi * rsb, a.layers[l + 1].router_t + (size_t)(b0 + bi) * 8 * E, rsb,
+                            rbar);
+        }
+        grid_sync(a.bar, nbar++);
         STAMP(l, 6);
 
         // ---------------------------------------------------------- phase B
-        // expert outputs for this CTA's rows: thread (k, r) sums the I/64 partials of MLX
-        // position k (at item position posof[k]) in a fixed order straight from L2 and rounds
-        // once to bf16
+        // expert outputs for this CTA's rows: thread (k, r) sums the I/64 partials of work
+        // items (k, 0..) in a fixed order straight from L2 and rounds once to bf16
 #pragma unroll 1
         for (int x = tid; x < K * nrows; x += kThreads) {
             const int k = x / nrows, r = x % nrows;
-            const float *src = a.yp + (size_t)(kSpec ? posof[k] : (uint32_t)k) * ngI * H + b0 * 8 + r;
+            const float *src = a.yp + (size_t)k * ngI * H + b0 * 8 + r;
             float v[16];                           // all partial loads of a row in flight at once
             float yk = 0.f;
 #pragma unroll 1
@@ -950,9 +644,9 @@ __global__ void __launch_bounds__(kThreads, 1) stack_kernel(StackArgs a) {
         if (tid == 0 && a.norm && nb > 0 && l + 1 < L) atomicAdd(a.ss + ((l + 1) & 1), ssn);
         __syncthreads();
         if (l + 1 < L && nb > 0)
-            router_partial(rbar, rphase, rsl, hown, nrows, E,
+            router_partial(rbar, rphase, region, hown, nrows, E,
                            a.acc + ((size_t)((l + 1) & 1) * kAccCopies + c % kAccCopies) * E);
-        if (!kSpec && c == 0) {   // layer l's accumulators were consumed in phase A; ready them for l + 2
+        if (c == 0) {   // layer l's accumulators were consumed in phase A; ready them for l + 2
             double *accz = a.acc + (size_t)(l & 1) * kAccCopies * E;
 #pragma unroll 1
             for (int e = tid; e < kAccCopies * E; e += kThreads) accz[e] = 0.0;
@@ -965,15 +659,12 @@ __global__ void __launch_bounds__(kThreads, 1) stack_kernel(StackArgs a) {
 
 struct StackWs {
     double *acc, *ss;
-    float *pacc;
     uint16_t *hbuf;
     float *yp;
     unsigned int *bar;
-    uint32_t *plist;
     size_t bytes;
 };
 
-// acc + ss | pacc | barrier words: the prefix that must be zero before every launch
 StackWs carve(void *base, int H, int I, int E, int K) {
     StackWs w{};
     char *p = static_cast<char *>(base);
@@ -981,16 +672,15 @@ StackWs carve(void *base, int H, int I, int E, int K) {
     auto take = [&](size_t n) { char *q = p ? p + off : nullptr; off += al256(n); return q; };
     w.acc = reinterpret_cast<double *>(take((size_t)(2 * kAccCopies * E + 2) * 8));
     w.ss = w.acc + 2 * kAccCopies * E;
-    w.pacc = reinterpret_cast<float *>(take((size_t)2 * E * 4));
     w.bar = reinterpret_cast<unsigned int *>(take(256));
-    w.plist = reinterpret_cast<uint32_t *>(take((size_t)2 * kMaxK * 4));
     w.hbuf = reinterpret_cast<uint16_t *>(take((size_t)2 * H * 2));
     w.yp = reinterpret_cast<float *>(take((size_t)K * (I / 64) * H * 4));
     w.bytes = off;
     return w;
 }
 
-size_t zero_prefix(int E) { return al256((size_t)(2 * kAccCopies * E + 2) * 8) + al256((size_t)2 * E * 4) + 256; }
+// bytes of the acc + barrier prefix that must be zero before every launch
+size_t zero_prefix(int E) { return al256((size_t)(2 * kAccCopies * E + 2) * 8) + 256; }
 
 }  // namespace
 
@@ -999,15 +689,13 @@ extern "C" size_t moe_stack_workspace_bytes(int H, int I, int E, int K) {
     return carve(nullptr, H, I, E, K).bytes;
 }
 
-extern "C" int moe_stack_decode_ex(const void *layers, int L, int H, int I, int E, int K, int sb_fp16, int norm,
-                                   const void *x, void *y, uint32_t *inds_out, void *scores_out, void *hs_out,
-                                   void *workspace, size_t workspace_bytes, int num_ctas, int flags,
-                                   unsigned int *spec_stats, void *stream) {
+extern "C" int moe_stack_decode(const void *layers, int L, int H, int I, int E, int K, int sb_fp16,
+                                int norm, const void *x, void *y, uint32_t *inds_out, void *scores_out, void *hs_out,
+                                void *workspace, size_t workspace_bytes, int num_ctas, void *stream) {
     if (!layers || !x || !y || !inds_out || !scores_out || !workspace)
         return moe_set_error(MOE_EINVAL, "stack_decode: null pointer");
     if (L <= 0 || H % 256 || H > kMaxH || I % 64 || I <= 0 || E <= 0 || E > kMaxE || K <= 0 || K > kMaxK || K > E)
         return moe_set_error(MOE_EINVAL, "stack_decode: bad sizes L=%d H=%d I=%d E=%d K=%d", L, H, I, E, K);
-    if (flags & ~MOE_STACK_SPECULATE) return moe_set_error(MOE_EINVAL, "stack_decode: unknown flags 0x%x", flags);
     const size_t need = moe_stack_workspace_bytes(H, I, E, K);
     if (workspace_bytes < need)
         return moe_set_error(MOE_EINVAL, "stack_decode: workspace of %zu bytes needed, %zu given", need,
@@ -1017,46 +705,29 @@ extern "C" int moe_stack_decode_ex(const void *layers, int L, int H, int I, int 
     MOE_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
     const int G = num_ctas > 0 ? num_ctas : sms;
     if (G > sms) return moe_set_error(MOE_EINVAL, "stack_decode: %d CTAs > %d SMs", G, sms);
-    const int NB = H / 8, nbmax = (NB + G - 1) / G;
-    if (nbmax > kMaxBlocks)
-        return moe_set_error(MOE_EINVAL, "stack_decode: %d CTAs too few for %d row blocks", G, NB);
+    if ((H / 8 + G - 1) / G > kMaxBlocks)
+        return moe_set_error(MOE_EINVAL, "stack_decode: %d CTAs too few for %d row blocks", G, H / 8);
     const PackDims P(H, I);
-    const size_t region = P.gbytes;
-    const size_t rsl = (size_t)nbmax * 8 * E * 2;
-    const SmemLayout S(H, I, K, region, rsl);
+    const size_t region = std::max((size_t)P.gbytes, (size_t)kMaxBlocks * 8 * E * 2);
+    const SmemLayout S(H, I, K, region);
     if (S.total > 227 * 1024)
         return moe_set_error(MOE_EINVAL, "stack_decode: %zu bytes of shared memory needed", S.total);
-    // speculation needs CTAs without a work item (at most one item per CTA), one key per
-    // thread in the prediction's selection, and each prediction CTA's router rows + h values
-    // within the weight region
-    const int NQ = K * (I / 64), npred = G - NQ;
-    bool spec = (flags & MOE_STACK_SPECULATE) && L > 1 && npred > 0 && E <= kThreads && E % 8 == 0;
-    if (spec) {
-        const size_t prmax = ((size_t)H + npred - 1) / npred;
-        spec = al16(prmax * E * 2) + prmax * 4 <= region;
-    }
     StackWs w = carve(workspace, H, I, E, K);
     auto st = as_stream(stream);
     MOE_CUDA_TRY(cudaMemsetAsync(workspace, 0, zero_prefix(E), st));
     StackArgs a{static_cast<const StackLayer *>(layers), L, H, I, E, K, static_cast<const uint16_t *>(x),
                 static_cast<uint16_t *>(y), inds_out, static_cast<uint16_t *>(scores_out),
-                static_cast<uint16_t *>(hs_out), w.acc, w.ss, norm, w.hbuf, w.yp, w.bar, w.pacc, w.plist, spec_stats,
-                spec ? 1 : 0, (unsigned int)region, (unsigned int)rsl};
+                static_cast<uint16_t *>(hs_out), w.acc, w.ss, norm, w.hbuf, w.yp, w.bar, (unsigned int)region};
     void *kargs[] = {&a};
-    // speculation only exists with one key per thread (E <= kThreads)
-    const void *kern = (E <= kThreads)
-                           ? (spec ? (sb_fp16 ? (const void *)stack_kernel<true, 1, true>
-                                              : (const void *)stack_kernel<false, 1, true>)
-                                   : (sb_fp16 ? (const void *)stack_kernel<true, 1, false>
-                                              : (const void *)stack_kernel<false, 1, false>))
-                           : (sb_fp16 ? (const void *)stack_kernel<true, kMaxE / kThreads, false>
-                                      : (const void *)stack_kernel<false, kMaxE / kThreads, false>);
+    const void *kern = (E <= kThreads) ? (sb_fp16 ? (const void *)stack_kernel<true, 1> : (const void *)stack_kernel<false, 1>)
+                                       : (sb_fp16 ? (const void *)stack_kernel<true, kMaxE / kThreads>
+                                                  : (const void *)stack_kernel<false, kMaxE / kThreads>);
     // raise the kernel's shared-memory limit once per (kernel, size): not per launch, and
     // not while a launch is being captured
-    static const void *set_kern[6] = {};
-    static size_t set_bytes[6] = {};
-    static int set_dev[6] = {-1, -1, -1, -1, -1, -1};
-    const int ki = (E <= kThreads ? (spec ? 4 : 0) : 2) + (sb_fp16 ? 1 : 0);
+    static const void *set_kern[4] = {};
+    static size_t set_bytes[4] = {};
+    static int set_dev[4] = {-1, -1, -1, -1};
+    const int ki = (E <= kThreads ? 0 : 2) + (sb_fp16 ? 1 : 0);
     if (set_kern[ki] != kern || set_bytes[ki] < S.total || set_dev[ki] != dev) {
         MOE_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)S.total));
         set_kern[ki] = kern;
@@ -1067,14 +738,9 @@ extern "C" int moe_stack_decode_ex(const void *layers, int L, int H, int I, int 
     return MOE_OK;
 }
 
-extern "C" int moe_stack_decode(const void *layers, int L, int H, int I, int E, int K, int sb_fp16, int norm,
-                                const void *x, void *y, uint32_t *inds_out, void *scores_out, void *hs_out,
-                                void *workspace, size_t workspace_bytes, int num_ctas, void *stream) {
-    return moe_stack_decode_ex(layers, L, H, I, E, K, sb_fp16, norm, x, y, inds_out, scores_out, hs_out, workspace,
-                               workspace_bytes, num_ctas, MOE_STACK_SPECULATE, nullptr, stream);
-}
-
 #ifdef MOE_STACK_TRACE
+// copies the phase timestamps of the last launch (kTraceCtas x kTraceLayers x kTraceSlots
+// u64, ns) to host memory
 extern "C" int moe_stack_trace_read(unsigned long long *host, size_t n) {
     const size_t total = (size_t)kTraceCtas * kTraceLayers * kTraceSlots;
     MOE_CUDA_TRY(cudaMemcpyFromSymbol(host, g_stack_trace, (n < total ? n : total) * sizeof(unsigned long long)));

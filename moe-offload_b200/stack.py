@@ -112,8 +112,7 @@ class PersistentStack:
     reference)."""
 
     def __init__(self, layers: list[ExpertLayer], top_k: int, device, num_ctas: int = 0,
-                 keep_layer_inputs: bool = False, norm: bool = True, release_unpacked: bool = False,
-                 speculate: bool = True):
+                 keep_layer_inputs: bool = False, norm: bool = True, release_unpacked: bool = False):
         from ._lib import call
 
         self.norm = norm
@@ -145,28 +144,17 @@ class PersistentStack:
         self.hs = (torch.empty((self.L + 1, self.H), dtype=torch.bfloat16, device=self.device)
                    if keep_layer_inputs else None)
         self.launches_per_step = 1
-        # speculative next-layer copies (MOE_STACK_SPECULATE); spec_stats accumulates (experts
-        # routed in layers with a prediction, of those predicted) over every step
-        self.flags = 1 if speculate else 0
-        self.spec_stats = torch.zeros(2, dtype=torch.int32, device=self.device)
         self._decode_graph = None        # host-facing step as one CUDA graph (decode)
         self._graph_failed = False
 
     def step_device(self, x: torch.Tensor | None = None) -> torch.Tensor:
         if x is not None:
             self.x_in.copy_(x)
-        self._call("moe_stack_decode_ex", self.desc.data_ptr(), self.L, self.H, self.I, self.E, self.K,
+        self._call("moe_stack_decode", self.desc.data_ptr(), self.L, self.H, self.I, self.E, self.K,
                    self.sb_fp16, int(self.norm), self.x_in.data_ptr(), self.y.data_ptr(), self.inds.data_ptr(),
                    self.scores.data_ptr(), None if self.hs is None else self.hs.data_ptr(), self.ws.data_ptr(),
-                   self.ws.numel(), self.num_ctas, self.flags, self.spec_stats.data_ptr(),
-                   torch.cuda.current_stream(self.device).cuda_stream)
+                   self.ws.numel(), self.num_ctas, torch.cuda.current_stream(self.device).cuda_stream)
         return self.y
-
-    def prediction_hit_rate(self) -> float | None:
-        """Fraction of the routed experts (layers 1..L-1, every step so far) whose slices were
-        copied speculatively (predicted by the previous layer), or None before any."""
-        n, hit = (int(v) for v in self.spec_stats.cpu())
-        return hit / n if n else None
 
     def _capture_decode(self) -> None:
         """Records the host-facing step (H2D copy from a fixed pinned buffer, workspace reset +
