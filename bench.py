@@ -515,14 +515,19 @@ def run_f3(args, rank: int, world: int, local_rank: int) -> None:
     print(json.dumps(line), flush=True)
 
 
+PRED_RECALL = 0.836     # recall@10 of the reference's next-layer predictor (its README.md:35)
+
+
 def run_c2(args, rank: int, world: int, local_rank: int) -> None:
     """the 28 x 512 x top-10 stack with the offload cache on (layer 0
     pinned, 102 slots per cached layer, experts in a pinned host pool, synthetic Zipf(1.1)
     routing with 30 % reuse injected as the routed experts while the router still runs,
-    router-driven prefetch of the top-12 predictions capped at 3 per layer)."""
+    next-layer prefetch of the top-12 of a predictor with the reference's recall@10, capped
+    at 3 per layer)."""
     import torch
 
-    from moe_offload_b200.offload import HostExpertPool, OffloadStack, compute_layer_capacities, zipf_routing
+    from moe_offload_b200.offload import (HostExpertPool, OffloadStack, compute_layer_capacities,
+                                          synthetic_predictions, zipf_routing)
     from moe_offload_b200.synthetic import C2, dev_bf16_normal, dev_stack
 
     dev = torch.device("cuda", local_rank)
@@ -542,14 +547,16 @@ def run_c2(args, rank: int, world: int, local_rank: int) -> None:
                          prefetch_cap=3, expert_bytes=cfg.expert_bytes)
     T = args.warmup + args.steps
     routing, bias = zipf_routing(seed=cfg.seed, layers=L, tokens=T, E=cfg.experts, K=cfg.top_k)
-    stack.pred_bias = torch.from_numpy(bias).to(dev)
+    # prefetch driven by a predictor of the reference's measured recall@10 (83.6 %)
+    preds = synthetic_predictions(routing, bias, recall=PRED_RECALL, M=12, seed=cfg.seed)
     inject = torch.from_numpy(routing).to(dev)
+    pred_dev = torch.from_numpy(preds).to(dev)
     gen = torch.Generator(device=dev)
     gen.manual_seed(cfg.seed)
     h = dev_bf16_normal((T, 1, cfg.hidden), dev, gen)
-    stack.capture()          # the warm-up token of the capture runs through the caches too
+    stack.capture(pred_injected=True)    # the warm-up token of the capture runs through the caches too
     for t in range(args.warmup):
-        stack.decode_graph(h[t], inject[t])
+        stack.decode_graph(h[t], inject[t], pred_dev[t])
     torch.cuda.synchronize()
     stack.reset_stats()
     torch.cuda.synchronize()
@@ -558,7 +565,7 @@ def run_c2(args, rank: int, world: int, local_rank: int) -> None:
     s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     s.record()
     for t in range(args.warmup, T):
-        stack.decode_graph(h[t], inject[t])
+        stack.decode_graph(h[t], inject[t], pred_dev[t])
     e.record()
     torch.cuda.synchronize()
     clocks = clk.stop()
@@ -578,8 +585,11 @@ def run_c2(args, rank: int, world: int, local_rank: int) -> None:
             "config": {"workload": cfg.name, "layers": L, "hidden": cfg.hidden, "experts": cfg.experts,
                        "top_k": cfg.top_k, "inter": cfg.inter, "capacity": caps[1], "layer0": "pinned",
                        "routing": "Zipf(1.1) per layer + 30 % reuse, injected; router runs",
-                       "prefetch": "top-12 next-layer router prediction (+ Zipf bias), cap 3"},
+                       "prefetch": f"top-12 ranked predictions of recall@10 {PRED_RECALL} (the reference's "
+                                   "measured predictor recall; offload.synthetic_predictions), cap 3; the "
+                                   "router's own next-layer prediction still runs"},
             "cache": {"lru_hit_rate": round(tot["decode_lru_hits"] / req, 4),
+                      "prefetch_hit_rate": round(tot["decode_prefetch_hits"] / req, 4),
                       "effective_hit_rate": round((tot["decode_lru_hits"] + tot["decode_prefetch_hits"]) / req, 4),
                       "demand_misses_per_token": round(tot["decode_demand_misses"] / args.steps, 2),
                       "fill_bytes_per_token": int(fill_bytes / args.steps)},

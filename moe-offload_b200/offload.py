@@ -393,8 +393,12 @@ class OffloadStack:
         for c in self.layers[1:]:
             c.reset_stats()
 
-    def decode_token(self, h: torch.Tensor, inject: torch.Tensor | None = None) -> torch.Tensor:
-        """h [1, H] bf16 (device) -> output of the last layer; inject: device int32 [L, K]."""
+    def decode_token(self, h: torch.Tensor, inject: torch.Tensor | None = None,
+                     pred_inject: torch.Tensor | None = None) -> torch.Tensor:
+        """h [1, H] bf16 (device) -> output of the last layer; inject: device int32 [L, K]
+        routed experts; pred_inject: device int32 [L, M], row l the ranked prediction of layer
+        l+1's experts that drives its prefetch (the router's own prediction is still computed,
+        as in the reference, but not used)."""
         self.hs[0].copy_(h)
         for l in range(self.L):
             x = self.hs[l]
@@ -414,7 +418,8 @@ class OffloadStack:
             else:
                 self.layers[l].forward_combined(xin, eids, r["scores"], resid=x, y=self.hs[l + 1])
             if nxt is not None:
-                self.layers[l + 1].start_prefetch(r["pred"].view(-1), self.prefetch_cap)
+                pred = pred_inject[l] if pred_inject is not None else r["pred"].view(-1)
+                self.layers[l + 1].start_prefetch(pred, self.prefetch_cap)
         return self.hs[self.L]
 
     def prefill(self, h: torch.Tensor) -> torch.Tensor:
@@ -441,26 +446,36 @@ class OffloadStack:
             x = y
         return x
 
-    def capture(self) -> None:
+    def capture(self, pred_injected: bool = False) -> None:
         """Records one decode_token as a CUDA graph over static input buffers (the token's
-        hidden state and injected experts); decode_graph() then replays it. Every step of
-        the token is device-side, so the graph needs no host decisions."""
+        hidden state, injected experts and, with pred_injected, injected predictions);
+        decode_graph() then replays it. Every step of the token is device-side, so the graph
+        needs no host decisions."""
         self.h_static = torch.zeros((1, self.H), dtype=torch.bfloat16, device=self.device)
         self.inj_static = torch.zeros((self.L, self.K), dtype=torch.int32, device=self.device)
+        self.pred_static = torch.full((self.L, self.M), -1, dtype=torch.int32, device=self.device) \
+            if pred_injected else None
         s = torch.cuda.Stream(device=self.device)
         s.wait_stream(torch.cuda.current_stream(self.device))
         with torch.cuda.stream(s):
-            self.decode_token(self.h_static, self.inj_static)       # warm: workspaces, attributes
+            self.decode_token(self.h_static, self.inj_static, self.pred_static)   # warm: workspaces, attributes
         s.synchronize()
         self.graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(self.graph, stream=s):
-            self.decode_token(self.h_static, self.inj_static)
+            self.decode_token(self.h_static, self.inj_static, self.pred_static)
         torch.cuda.current_stream(self.device).wait_stream(s)
 
-    def decode_graph(self, h: torch.Tensor, inject: torch.Tensor | None) -> torch.Tensor:
+    def decode_graph(self, h: torch.Tensor, inject: torch.Tensor | None,
+                     pred: torch.Tensor | None = None) -> torch.Tensor:
+        """Replays the captured token: h [1, H], inject [L, K] routed experts and (when the
+        graph was captured with pred_injected) pred [L, M] predictions, all device tensors."""
         self.h_static.copy_(h)
         if inject is not None:
             self.inj_static.copy_(inject)
+        if pred is not None:
+            if self.pred_static is None:
+                raise ValueError("capture(pred_injected=True) first")
+            self.pred_static.copy_(pred)
         self.graph.replay()
         return self.hs[self.L]
 
@@ -522,3 +537,42 @@ def zipf_routing(seed: int, layers: int, tokens: int, E: int, K: int, s: float =
     for l in range(layers):
         bias[l, perms[l]] = np.log(pop).astype(np.float32) - math.log(pop[-1])
     return out, bias
+
+
+def synthetic_predictions(routing: np.ndarray, bias: np.ndarray, recall: float = 0.836, M: int = 12,
+                          seed: int = 0) -> np.ndarray:
+    """A next-layer predictor of stated recall for the synthetic c2 routing (the reference
+    measured recall@10 = 83.6 % for its router-based predictor, README.md:35). For token t and
+    layer l < L-1, row [t, l] ranks M candidates for layer l+1's experts routing[t, l+1]: each
+    of the K routed experts is kept with probability `recall`, each dropped one is replaced by
+    a distinct non-routed expert drawn from the layer's Zipf popularity (exp(bias)); the K
+    kept-or-replacement entries come first in random order, then M-K more distinct popular
+    non-routed experts. Row [t, L-1] is -1 (nothing to predict). int32 [tokens, layers, M]."""
+    rng = np.random.default_rng(seed)
+    T, L, K = routing.shape
+    E = bias.shape[1]
+    pop = np.exp(bias.astype(np.float64))
+    pop /= pop.sum(axis=1, keepdims=True)
+    out = np.full((T, L, M), -1, dtype=np.int32)
+    for t in range(T):
+        for l in range(L - 1):
+            true = [int(e) for e in routing[t, l + 1]]
+            taken = set(true)
+            head = []
+            for e in true:
+                if rng.random() < recall:
+                    head.append(e)
+                else:
+                    head.append(-1)
+
+            def draw() -> int:
+                while True:
+                    c = int(rng.choice(E, p=pop[l + 1]))
+                    if c not in taken:
+                        taken.add(c)
+                        return c
+            head = [e if e >= 0 else draw() for e in head]
+            rng.shuffle(head)
+            tail = [draw() for _ in range(M - K)]
+            out[t, l] = head + tail
+    return out
