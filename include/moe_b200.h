@@ -477,16 +477,22 @@ void c_layer_get_stats(int layer_idx, uint64_t *out_stats);
 void c_get_decode_totals(int num_layers, uint64_t *out6);
 
 /*
- * P1 I/O scheduler (replaces qwen38::P1IoScheduler, mlx-qwen38/cpp/src/io_sched.h:46-245;
- * semantics of mlx-qwen38/cpp/src/io_sched.cpp, tested by mlx-qwen38/cpp/tests/test_io_sched.cpp):
- * URGENT / PREFETCH copy queues drained by worker threads and by waiting callers, prefetch
- * cancel / promote, per-slot pins with a reader-wait callback, LRU slot cache per layer
- * (layers 0..63, experts 0..511, up to 9 tensors per expert). Each method of the reference
- * class is one function taking the handle; void methods return 0 (or a negative status for a
- * null handle / pointer). Rows come from a file (fd, byte offsets: moe_p1_layer_init, the
- * reference's form, host slot buffers) or from a host pool (addresses of expert 0 of every
- * tensor: moe_p1_layer_init_pool) into host or device slot buffers (device copies run on a
- * non-blocking stream of the executing thread).
+ * P1 I/O scheduler (replaces qwen38::P1IoScheduler, mlx-qwen38/cpp/src/io_sched.h:46-245, with
+ * the observable behaviour of mlx-qwen38/cpp/src/io_sched.cpp, tested by
+ * mlx-qwen38/cpp/tests/test_io_sched.cpp): URGENT / PREFETCH read queues, prefetch cancel /
+ * promote, per-slot pins with a reader-wait callback, an LRU slot cache per layer (layers
+ * 0..63, experts 0..511, up to 9 tensors per expert). The scheduler's whole state lives in
+ * device memory (the device that is current at moe_p1_create); every method is one control
+ * kernel on that state, and the rows it takes from the queues are copied by a copy kernel
+ * (pool sources, device slots) or by the calling host thread (file sources or host slots).
+ * Each method of the reference class is one function taking the handle; void methods return
+ * 0 (or a negative status). Rows come from a file (fd, byte offsets: moe_p1_layer_init, the
+ * reference's form) or from a pool of num_experts experts (addresses of expert 0 of every
+ * tensor, pinned host or device memory: moe_p1_layer_init_pool) into host or device slot
+ * buffers. Workers: without moe_p1_init nothing is taken until a caller waits (the
+ * reference's behaviour without workers, deterministic); after moe_p1_init(n) every queued
+ * row is taken at the end of each call. The wait-reader callback may only wait for readers
+ * and unpin; a call that finds only pinned slots evictable resumes after it returns.
  */
 #define MOE_P1_STATS 16
 /* stats order: decode_requests, lru_hits, urgent_reads, prefetch_issued, prefetch_cancelled,
@@ -504,9 +510,9 @@ int moe_p1_num_threads(void *h);
 int moe_p1_set_wait_reader_callback(void *h, void (*fn)(void *user, int layer), void *user);
 int moe_p1_layer_init(void *h, int layer, int fd, int capacity, int num_tensors, const uint64_t *base_offsets,
                       const uint64_t *row_bytes, const uint64_t *base_ptrs, uint64_t slot_inds_ptr);
-int moe_p1_layer_init_pool(void *h, int layer, int capacity, int num_tensors, const uint64_t *src_ptrs,
-                           const uint64_t *row_bytes, const uint64_t *slot_ptrs, uint64_t slot_inds_ptr,
-                           int slots_on_device, int device);
+int moe_p1_layer_init_pool(void *h, int layer, int capacity, int num_tensors, int num_experts,
+                           const uint64_t *src_ptrs, const uint64_t *row_bytes, const uint64_t *slot_ptrs,
+                           uint64_t slot_inds_ptr, int slots_on_device, int device);
 int moe_p1_resize_layer(void *h, int layer, int new_capacity, const uint64_t *new_base_ptrs, uint64_t slot_inds_ptr,
                         const int32_t *ordered_eids, const int32_t *ordered_slots, int count);
 int moe_p1_reset_cache(void *h, int layer);
@@ -530,7 +536,8 @@ int moe_p1_set_lru_state(void *h, int layer, const int32_t *ordered_eids, const 
                          uint64_t add_prefill_requests, uint64_t add_prefill_hits, uint64_t add_prefill_misses);
 int moe_p1_get_layer_stats(void *h, int layer, uint64_t *out_stats);
 int moe_p1_get_total_stats(void *h, int num_layers, uint64_t *out_stats);
-uint64_t moe_p1_copy_errors(void *h);                          /* failed device copies so far */
+uint64_t moe_p1_copy_errors(void *h);          /* rows that could not be copied (short reads, bad ids) */
+uint64_t moe_p1_launches(void *h);             /* control and copy kernels launched so far */
 
 /*
  * Device-side error word (bit 1: a bounded mbarrier/flag wait gave up, bit 2: invalid

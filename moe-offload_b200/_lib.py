@@ -113,7 +113,7 @@ P1_SIGNATURES: dict[str, tuple] = {
     "num_threads": (I, [P]),
     "set_wait_reader_callback": (I, [P, P1_READER_FN, P]),
     "layer_init": (I, [P, I, I, I, I, P, P, P, U64]),
-    "layer_init_pool": (I, [P, I, I, I, P, P, P, U64, I, I]),
+    "layer_init_pool": (I, [P, I, I, I, I, P, P, P, U64, I, I]),
     "resize_layer": (I, [P, I, I, P, U64, P, P, I]),
     "reset_cache": (I, [P, I]),
     "reset_stats": (I, [P, I]),
@@ -134,6 +134,7 @@ P1_SIGNATURES: dict[str, tuple] = {
     "get_layer_stats": (I, [P, I, P]),
     "get_total_stats": (I, [P, I, P]),
     "copy_errors": (U64, [P]),
+    "launches": (U64, [P]),
 }
 SIGNATURES.update({"moe_p1_" + k: v for k, v in P1_SIGNATURES.items()})
 

@@ -1,12 +1,14 @@
 """P1 I/O scheduler: the reference's qwen38::P1IoScheduler (mlx-qwen38/cpp/src/io_sched.h:46-245)
-with the same methods, backed by libmoe_b200's moe_p1_* functions (csrc/io_sched.cpp).
+with the same methods, backed by libmoe_b200's moe_p1_* functions (csrc/p1_device.cu).
 
-Two copy queues per scheduler (URGENT before PREFETCH) drained by worker threads and by any
-caller that waits; per-layer LRU slot caches with prefetch cancel / promote, pins held for a
-GPU reader (step_decode pins the k slots it returns; unpin_layer_slots releases them once the
-reader is done) and a reader-wait callback used when only pinned slots could be evicted. Rows
-come from a file (layer_init: the reference's form) or from a pinned host pool
-(layer_init_pool) and land in host or device slot buffers.
+The scheduler's state -- every layer's LRU slot cache, pin counts and in-flight reads, the
+URGENT and PREFETCH read queues -- lives in device memory, and each method runs as one control
+kernel on it: prefetch cancel / promote, pins held for a GPU reader (step_decode pins the k
+slots it returns; unpin_layer_slots releases them once the reader is done) and the reader-wait
+callback when only pinned slots could be evicted (the call stops, the callback runs on the
+host, the call resumes). Rows come from a file (layer_init: the reference's form) or from a
+pool of experts (layer_init_pool, pinned host or device memory) and land in host or device
+slot buffers; pool rows bound for device slots are copied by a copy kernel.
 
 The class takes any library exporting the moe_p1_* signatures under a prefix, so the parity
 tests run the same calls against a build of the reference scheduler."""
@@ -106,9 +108,11 @@ class P1IoScheduler:
 
     def layer_init_pool(self, layer_idx: int, capacity: int, src_ptrs: Sequence[int], row_bytes: Sequence[int],
                         slot_ptrs: Sequence[int], slot_inds_ptr: int = 0, on_device: bool = False,
-                        device: int = 0) -> None:
-        self._call("layer_init_pool", layer_idx, capacity, len(row_bytes), _u64s(src_ptrs), _u64s(row_bytes),
-                   _u64s(slot_ptrs), slot_inds_ptr, int(on_device), device)
+                        device: int = 0, *, num_experts: int) -> None:
+        """Rows from a pool of `num_experts` experts (src_ptrs: expert 0 of every tensor, in
+        pinned host or device memory) into slot buffers (device memory with on_device)."""
+        self._call("layer_init_pool", layer_idx, capacity, len(row_bytes), num_experts, _u64s(src_ptrs),
+                   _u64s(row_bytes), _u64s(slot_ptrs), slot_inds_ptr, int(on_device), device)
 
     def resize_layer(self, layer_idx: int, new_capacity: int, new_base_ptrs: Sequence[int], slot_inds_ptr: int,
                      ordered_eids: Sequence[int], ordered_slots: Sequence[int]) -> None:
@@ -187,4 +191,9 @@ class P1IoScheduler:
 
     def copy_errors(self) -> int:
         f = self._fn.get("copy_errors")
+        return int(f(self._h)) if f else 0
+
+    def launches(self) -> int:
+        """Kernels launched so far (control and row-copy kernels; 0 for the reference)."""
+        f = self._fn.get("launches")
         return int(f(self._h)) if f else 0

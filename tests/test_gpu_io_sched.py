@@ -1,7 +1,8 @@
 """P1 I/O scheduler with device slot buffers: expert rows copied from a pinned host pool into
-slot buffers in HBM (cudaMemcpyAsync on each executing thread's stream). The decisions are
-compared with the reference scheduler (mlx-qwen38/cpp/src/io_sched.cpp, file -> host buffers)
-on identical calls; the device bytes are read back and compared with the pool."""
+slot buffers in HBM by the scheduler's copy kernel (the rows its control kernel took from the
+queues). The decisions are compared with the reference scheduler (mlx-qwen38/cpp/src/
+io_sched.cpp, file -> host buffers) on identical calls; the device bytes are read back and
+compared with the pool."""
 import ctypes
 import os
 import random
@@ -87,7 +88,8 @@ def test_device_slots_match_reference_decisions(pool):
     hbufs = {l: HostSlots(caps[l]) for l in LAYERS}
     for l in LAYERS:
         ours.layer_init_pool(l, caps[l], [p.data_ptr() for p in host[l]], ROW_BYTES, dbufs[l].ptrs(),
-                             dbufs[l].slot_inds.ctypes.data, on_device=True, device=0)
+                             dbufs[l].slot_inds.ctypes.data, on_device=True, device=0,
+                             num_experts=N_EXPERTS)
         ref.layer_init(l, fd, caps[l], NT, offsets[l], ROW_BYTES, hbufs[l].ptrs(), hbufs[l].slot_inds.ctypes.data)
     for s in (ours, ref):
         s.seed(17)
@@ -138,7 +140,7 @@ def test_device_slots_threaded(pool):
     bufs = {l: DevSlots(cap, dev) for l in LAYERS}
     for l in LAYERS:
         s.layer_init_pool(l, cap, [p.data_ptr() for p in host[l]], ROW_BYTES, bufs[l].ptrs(),
-                          bufs[l].slot_inds.ctypes.data, on_device=True, device=0)
+                          bufs[l].slot_inds.ctypes.data, on_device=True, device=0, num_experts=N_EXPERTS)
     s.set_wait_reader_callback(lambda layer: s.unpin_layer_slots(layer))
     rng = random.Random(11)
     for step in range(120):

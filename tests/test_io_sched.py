@@ -1,6 +1,8 @@
-"""P1 I/O scheduler (moe_offload_b200.io_sched, csrc/io_sched.cpp) against the reference's own
-scheduler (mlx-qwen38/cpp/src/io_sched.cpp, built into oracle/_ref/libref_iosched.so by
-oracle/Makefile). CPU only: rows are read from a synthetic expert file into host slot buffers.
+"""P1 I/O scheduler (moe_offload_b200.io_sched; state and decisions on the GPU, csrc/p1_device.cu)
+against the reference's own scheduler (mlx-qwen38/cpp/src/io_sched.cpp, built into
+oracle/_ref/libref_iosched.so by oracle/Makefile). Rows are read from a synthetic expert file
+into host slot buffers. The reference's runs of its own scenarios need no GPU; every run of
+ours is marked gpu (its scheduler state lives in device memory).
 
 The first three tests restate the scenarios of the reference's test_io_sched.cpp:142-445
 (queued cancel + promote with exact counters, pin waits through the reader callback, a
@@ -88,7 +90,7 @@ def _init_layer(s, fd, offsets, layer, slots):
     s.layer_init(layer, fd, slots.cap, NT, offsets[layer], ROW_BYTES, slots.ptrs(), slots.inds_ptr())
 
 
-@pytest.mark.parametrize("which", ["ours", "reference"])
+@pytest.mark.parametrize("which", [pytest.param("ours", marks=pytest.mark.gpu), "reference"])
 def test_cancel_and_promote(expert_file, ref_lib, which):
     fd, offsets = expert_file
     s = dict(_impls(ref_lib))[which]()
@@ -116,7 +118,7 @@ def test_cancel_and_promote(expert_file, ref_lib, which):
     s.close()
 
 
-@pytest.mark.parametrize("which", ["ours", "reference"])
+@pytest.mark.parametrize("which", [pytest.param("ours", marks=pytest.mark.gpu), "reference"])
 def test_pin_waits_and_reader_callback(expert_file, ref_lib, which):
     fd, offsets = expert_file
     s = dict(_impls(ref_lib))[which]()
@@ -156,7 +158,7 @@ def test_pin_waits_and_reader_callback(expert_file, ref_lib, which):
     s.close()
 
 
-@pytest.mark.parametrize("which", ["ours", "reference"])
+@pytest.mark.parametrize("which", [pytest.param("ours", marks=pytest.mark.gpu), "reference"])
 def test_high_concurrency_stress(expert_file, ref_lib, which):
     fd, offsets = expert_file
     cap0, k, m, pcap, steps = 12, 4, 6, 3, 250
@@ -241,6 +243,7 @@ def _cmp_stats(a, b, where):
     assert a == b, f"{where}: {a} vs {b}"
 
 
+@pytest.mark.gpu
 @pytest.mark.parametrize("seed", [1, 2, 3, 4, 5, 6])
 def test_differential_against_reference(expert_file, ref_lib, seed):
     """Same random calls, no workers: every observable result equal to the reference's."""
@@ -337,6 +340,7 @@ def test_differential_against_reference(expert_file, ref_lib, seed):
         s.close()
 
 
+@pytest.mark.gpu
 def test_step_decode_rejects_bad_expert_ids():
     from moe_offload_b200._lib import MoeError
     s = P1IoScheduler()
