@@ -1,7 +1,7 @@
 """Expert shards in the reference's checkpoint layout (moe_offload_b200.checkpoint): write a
 shard, read it back, cross-check with the safetensors package, locate expert rows the way the
 reference's CachedSwitchGLU does (loader.py:329-366), and fill slots from the shard with the
-P1 scheduler (file source, as the reference's engine does). CPU only."""
+P1 scheduler (file source, as the reference's engine does; the only test here that needs a GPU)."""
 import os
 
 import numpy as np
@@ -76,7 +76,9 @@ def test_rows_at_reference_offsets(shard):
         os.close(fd)
 
 
+@pytest.mark.gpu
 def test_p1_scheduler_fills_slots_from_the_shard(shard):
+    """Rows at the shard's offsets through the P1 scheduler (its state lives on the GPU)."""
     from moe_offload_b200.io_sched import P1IoScheduler
     path, mats = shard
     offs, rb = ck.shard_rows(path, 3, GS)
