@@ -6,11 +6,12 @@
 A step is one decode token through all 28 layers (router -> 2-bit gate/up + SwiGLU -> 2-bit
 down + combine, h_{l+1} = h_l + MoE_l(h_l)) with a fresh N(0,1) hidden state per step
 (seed 1), expert weights random-init with the BASELINE distributions (synthetic: the
-reference's checkpoints are not available). For N > 1 (torchrun) every rank decodes its own
-token stream through its own replica of the stack (31.7 GB of experts fits one B200 many
-times over, so independent requests are the throughput-optimal way to use N GPUs; no
-collective on the data path), so per-GPU work is fixed: weak scaling. Expert parallelism
-(experts split across the ranks, outputs exchanged over NVLink every layer) is `--config c4`.
+reference's checkpoints are not available). For N > 1 (torchrun) the run is BASELINE config 4,
+expert parallelism: the experts of every layer split across the N GPUs (512/N each), a batch
+of 8 tokens per GPU (B = 8N) owned in blocks by the ranks, every layer a routed all-to-all over
+NVLink (each token's row to the ranks holding its experts, each output row back to its owner,
+MLX-order combine) -- per-GPU work fixed: weak scaling. `--replicas` runs N independent copies
+of the c1 stack instead (one token stream per GPU, no exchange).
 
 The step is ONE launch of the persistent kernel (moe_stack_decode: all 28 layers inside,
 experts in the packed layout). Prints one JSON line (rank 0). `value` is whole-job tokens/s
@@ -51,7 +52,10 @@ def parse():
                          "prefill layer (240 experts, top-9, 1024 tokens); c4: expert-parallel decode (experts "
                          "split across the ranks); p1: the P1 I/O scheduler filling c2-shaped expert slots; f3: the "
                          "hyper-connection mixer + shared expert in front of each of the 28 MoE blocks, decode")
-    ap.add_argument("--batch", type=int, default=0, help="c4: tokens per decode step (default: one per GPU)")
+    ap.add_argument("--batch", type=int, default=0, help="c4: tokens per step (default: 8 per GPU; 4096 = c4's prefill)")
+    ap.add_argument("--replicas", action="store_true",
+                    help="--gpus N > 1: N independent replicas of the c1 stack instead of expert parallelism")
+    ap.add_argument("--no-check", action="store_true", help="c4: skip the bit-exact check of layer 0")
     ap.add_argument("--layers", type=int, default=0,
                     help="profiling aid: run only the first N layers of the stack (0 = all 28)")
     return ap.parse_args()
@@ -178,6 +182,19 @@ def c1_config(cfg, world: int) -> dict:
             "l2": "inputs larger than L2: 707 MB of weights per step, 31.7 GB resident"}
 
 
+def c4_config(cfg, world: int, B: int, sharded: bool, L: int | None = None) -> dict:
+    """The workload description both arms print for the expert-parallel run (--gpus N > 1)."""
+    return {"workload": f"{cfg.name}_batch{B}", "layers": L or cfg.layers, "hidden": cfg.hidden,
+            "experts": cfg.experts, "top_k": cfg.top_k, "inter": cfg.inter, "batch": B,
+            "group_size": cfg.group_size, "scales": "fp16", "router": "bf16 (replicated)",
+            "parallelism": f"ep{world} (experts {cfg.experts}/{world} per GPU" +
+                           (f", tokens {B}/{world} per GPU)" if sharded else ", tokens replicated)"),
+            "exchange": ("routed all-to-all: peer stores over NVLink (dispatch once per token and rank, each "
+                         "output row returned once) + epoch flags, no library collective") if sharded else
+                        "every output row stored in every rank over NVLink + epoch flags",
+            "l2": "inputs larger than L2"}
+
+
 def run_reference(args, rank: int, world: int) -> None:
     """--impl reference: the reference computes this path with MLX, which is not installable
     here; its CPU restatement (oracle port) runs on all host cores on rank 0 only. One step
@@ -198,7 +215,8 @@ def run_reference(args, rank: int, world: int) -> None:
             "warmup": args.warmup, "ms_per_step": round(1000.0 * per_layer * cfg.layers, 3),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "u2 codes x bf16 -> f32",
             "data": "synthetic", "impl": "reference",
-            "config": c1_config(cfg, args.gpus),
+            "config": c1_config(cfg, args.gpus) if (world == 1 or args.replicas) else
+                      c4_config(cfg, world, args.batch or 8 * world, (args.batch or 8 * world) >= 4 * world),
             "cpu_baseline": cpu,
             "e2e": {"value": round(v, 4), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
@@ -728,28 +746,41 @@ def run_c3(args, rank: int, world: int, local_rank: int) -> None:
 
 def run_c4(args, rank: int, world: int, local_rank: int) -> None:
     """the 28 x 512 x top-10 stack with the experts split across the N
-    ranks (512/N each, contiguous blocks), the routers replicated, decode batches of B tokens
-    (default B = N: a fixed expert load per GPU as N grows). A step = the batch through all 28
-    layers: per layer router + top-k, local experts, and one kernel that exchanges the expert
-    outputs over NVLink (peer stores) and combines them -- the whole step one CUDA graph."""
+    ranks (512/N each, contiguous blocks), the routers replicated. A step = a batch of B tokens
+    through all 28 layers, the whole step one CUDA graph per rank. Batches of at least 4 tokens
+    per rank run token-sharded (each rank owns B/N tokens; per layer a routed all-to-all:
+    dispatch of each token's row to the ranks holding its experts, local experts, return of
+    each output row to its token's owner, MLX-order combine); smaller batches run with the
+    tokens replicated (one NVLink exchange + combine per layer). Default B = 8 * N: a fixed
+    number of tokens (and so of expert bytes) per GPU as N grows. B = 4096 is c4's prefill."""
     import torch
     import torch.distributed as dist
 
-    from moe_offload_b200.ep import EPDecodeStack, expert_shard
+    from moe_offload_b200.ep import (A2A_MIN_TOKENS_PER_RANK, EPA2AStack, EPDecodeStack, ep_a2a_layer,
+                                     expert_bounds, expert_shard, local_tokens)
     from moe_offload_b200.synthetic import C4, dev_bf16_normal, dev_stack_shard
 
     dev = torch.device("cuda", local_rank)
     torch.cuda.set_device(dev)
     cfg = C4
     L = args.layers or cfg.layers
-    B = args.batch or world
+    B = args.batch or 8 * world
+    sharded = B >= A2A_MIN_TOKENS_PER_RANK * world
     first, n = expert_shard(cfg.experts, rank, world)
     layers = dev_stack_shard(cfg, dev, first, n, layers=L)
     gen = torch.Generator(device=dev)
     gen.manual_seed(cfg.seed)                       # the same batch on every rank
     n_in = args.warmup + args.steps
     h0 = dev_bf16_normal((n_in, B, cfg.hidden), dev, gen)
-    st = EPDecodeStack(layers, cfg.experts, first, cfg.top_k, B, dev)
+    if sharded:
+        ef = expert_bounds(cfg.experts, world)
+        g0, tn = local_tokens(B, world, rank)
+        st = EPA2AStack(layers, cfg.experts, ef, cfg.top_k, B, dev)
+        xin = h0[:, g0:g0 + tn]
+    else:
+        st = EPDecodeStack(layers, cfg.experts, first, cfg.top_k, B, dev)
+        g0, tn = 0, B
+        xin = h0
     torch.cuda.synchronize()
 
     def barrier():
@@ -757,7 +788,7 @@ def run_c4(args, rank: int, world: int, local_rank: int) -> None:
             dist.barrier()
 
     for i in range(args.warmup):
-        st.step_device(h0[i])
+        st.step_device(xin[i])
     torch.cuda.synchronize()
     barrier()
     clk = ClockSampler(local_rank)
@@ -767,15 +798,24 @@ def run_c4(args, rank: int, world: int, local_rank: int) -> None:
     s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     s.record()
     for i in range(args.steps):
-        st.step_device(h0[args.warmup + i])
+        st.step_device(xin[args.warmup + i])
     e.record()
     torch.cuda.synchronize()
     barrier()
     clocks = clk.stop()
     t_ms = s.elapsed_time(e)
-    # expert bytes this rank had to read in the last step: its unique routed experts per layer
-    inds = st.inds.cpu().numpy()
-    uniq = sum(len({int(v) for v in inds[l].ravel() if first <= v < first + n}) for l in range(L))
+    # routing of the whole batch in the last step (every rank's tokens): each rank's unique
+    # local experts per layer give the expert bytes the step had to read
+    inds_local = st.inds[:, :max(tn, 1)].clone() if sharded else st.inds.clone()
+    if sharded and world > 1:
+        parts = [torch.zeros_like(inds_local) for _ in range(world)]
+        dist.all_gather(parts, inds_local)
+        counts = [local_tokens(B, world, q)[1] for q in range(world)]
+        inds_all = torch.cat([p[:, :c] for p, c in zip(parts, counts)], dim=1)
+    else:
+        inds_all = inds_local
+    ia = inds_all.cpu().numpy()
+    uniq = sum(len({int(v) for v in ia[l].ravel() if first <= v < first + n}) for l in range(L))
     stats = torch.tensor([t_ms, float(uniq)], dtype=torch.float64, device=dev)
     if world > 1:
         tmax = stats[:1].clone()
@@ -791,8 +831,8 @@ def run_c4(args, rank: int, world: int, local_rank: int) -> None:
 
     e2e = None
     if not args.no_e2e:
-        hh = h0.cpu().pin_memory()
-        out_host = torch.empty((B, cfg.hidden), dtype=torch.bfloat16, pin_memory=True)
+        hh = xin.cpu().pin_memory()
+        out_host = torch.empty((max(tn, 1), cfg.hidden), dtype=torch.bfloat16, pin_memory=True)[:tn]
         for i in range(min(args.warmup, 3)):
             st.decode(hh[i], out_host)
         torch.cuda.synchronize()
@@ -809,30 +849,57 @@ def run_c4(args, rank: int, world: int, local_rank: int) -> None:
             tt = torch.tensor([t2], device=dev)
             dist.all_reduce(tt, op=dist.ReduceOp.MAX)
             t2 = float(tt.item())
+        cls = "EPA2AStack" if sharded else "EPDecodeStack"
         e2e = {"value": round(B * args.steps / (t2 / 1000.0), 2), "unit": UNIT,
-               "h2d_bytes_per_step": B * cfg.hidden * 2, "d2h_bytes_per_step": B * cfg.hidden * 2,
-               "api": "moe_offload_b200.ep.EPDecodeStack.decode (pinned host in/out, sync per step, every rank)"}
+               "h2d_bytes_per_step": tn * cfg.hidden * 2, "d2h_bytes_per_step": tn * cfg.hidden * 2,
+               "api": f"moe_offload_b200.ep.{cls}.decode (each rank: its tokens from pinned host memory in, "
+                      "out, sync per step)"}
+
+    # bit-exact check on a small slice: layer 0 on the first batch through the expert-parallel
+    # layer, against the single-GPU layer with all 512 experts on rank 0
+    check = None
+    if sharded and not args.no_check:
+        from moe_offload_b200 import ops
+        from moe_offload_b200.ep import ExchangeBuffers
+        xb = ExchangeBuffers(B, cfg.top_k, cfg.hidden, dev, a2a=True)
+        o = ep_a2a_layer(xin[0], layers[0], cfg.experts, ef, cfg.top_k, B, xb, norm=True, resid=xin[0])
+        torch.cuda.synchronize()
+        ok = torch.tensor([1.0], device=dev)
+        if rank == 0:
+            import dataclasses
+            full = [dev_stack_shard(cfg, dev, *expert_shard(cfg.experts, q, world), layers=1)[0] for q in range(world)]
+            cat = lambda f: torch.cat([f(ly) for ly in full])
+            from moe_offload_b200.ops import QMatrix
+            qm = lambda nm: QMatrix(cat(lambda ly: getattr(ly, nm).w), cat(lambda ly: getattr(ly, nm).s),
+                                    cat(lambda ly: getattr(ly, nm).b), 2, 64)
+            ref = ops.prefill_layer if B >= 32 else ops.decode_layer
+            r = ref(h0[0], layers[0].router, qm("gate"), qm("up"), qm("down"), cfg.top_k, norm=True, resid=h0[0])
+            torch.cuda.synchronize()
+            eq = all(torch.equal(o[k], r[k][g0:g0 + tn]) for k in ("inds", "scores", "y"))
+            ok.fill_(1.0 if eq else 0.0)
+            del full, r
+        xb.close()
+        check = {"layer0_rank0_tokens_bit_exact_vs_single_gpu": bool(ok.item() == 1.0),
+                 "reference": "ops.prefill_layer" if B >= 32 else "ops.decode_layer"}
     peak, peak_kind = peaks()
     step_bytes = uniq_all * cfg.expert_bytes + world * L * cfg.router_bytes
     achieved = step_bytes / (t_ms / 1000.0 / args.steps) / 1e9
-    roof = {"kernel": "expert-parallel step (router, gate/up, down, NVLink exchange + combine per layer)",
+    roof = {"kernel": ("token-sharded expert-parallel step (router, dispatch all-to-all, local experts, return "
+                       "all-to-all + combine per layer)") if sharded else
+                      "expert-parallel step (router, gate/up, down, NVLink exchange + combine per layer)",
             "bound": "hbm", "achieved": round(achieved, 1), "peak": round(peak * world, 1), "unit": "GB/s",
             "frac": round(achieved / (peak * world), 4), "traffic": None,
             "algorithmic_bytes_per_launch": int(step_bytes), "peak_source": f"{peak_kind} x {world} GPUs",
-            "unique_experts_per_layer": round(uniq_all / L, 2)}
+            "unique_experts_per_layer": round(uniq_all / L, 2),
+            "unique_expert_bytes_per_layer": int(uniq_all / L * cfg.expert_bytes)}
     if rank == 0:
         line = {"metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world, "steps": args.steps,
                 "warmup": args.warmup, "ms_per_step": round(t_ms / args.steps, 4), "higher_is_better": True,
                 "scaling": "weak" if not args.batch else "strong", "vs_baseline": None,
                 "dtype": "u2 codes x bf16 -> f32", "data": "synthetic",
-                "config": {"workload": f"{cfg.name}_batch{B}", "layers": L, "hidden": cfg.hidden,
-                           "experts": cfg.experts, "top_k": cfg.top_k, "inter": cfg.inter, "batch": B,
-                           "group_size": cfg.group_size, "scales": "fp16", "router": "bf16 (replicated)",
-                           "parallelism": f"ep{world} (experts {cfg.experts}/{world} per GPU)",
-                           "exchange": "peer stores over NVLink + epoch flags (CUDA IPC), no library collective",
-                           "l2": "inputs larger than L2"},
+                "config": c4_config(cfg, world, B, sharded, L),
                 "roofline": roof, "clocks": clocks, "gpu_launches": st.launches_per_step * args.steps,
-                "device_error": dev_err, "e2e": e2e, "cpu_baseline": None}
+                "device_error": dev_err, "check": check, "e2e": e2e, "cpu_baseline": None}
         print(json.dumps(line), flush=True)
     st.close()
 
@@ -848,7 +915,7 @@ def main() -> int:
         import torch
         import torch.distributed as dist
         torch.cuda.set_device(local_rank)
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180),
                                 device_id=torch.device("cuda", local_rank))
     try:
         if args.impl == "reference":
@@ -861,7 +928,7 @@ def main() -> int:
             run_f3(args, rank, world, local_rank)
         elif args.config in ("c3", "c3n"):
             run_c3(args, rank, world, local_rank)
-        elif args.config == "c4":
+        elif args.config == "c4" or (world > 1 and args.config == "c1" and not args.replicas):
             run_c4(args, rank, world, local_rank)
         else:
             run_ours(args, rank, world, local_rank)

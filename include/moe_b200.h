@@ -373,6 +373,37 @@ int moe_ep_decode_layer(const void *x, int T, int H, int I, int E, int K, int e_
                         void *const *peers, int rank, int nranks, uint32_t *out_inds, void *out_scores,
                         void *y, void *workspace, size_t workspace_bytes, void *stream);
 
+/*
+ * Token-sharded expert parallelism (routed all-to-all) for batches with several tokens per
+ * GPU. Rank r of nranks owns tokens [first, first + n) of the batch (moe_ep_a2a_local_tokens:
+ * contiguous blocks of ceil(T / nranks)) and experts [e_first[r], e_first[r + 1]) (e_first:
+ * host array of nranks + 1 boundaries, e_first[0] = 0, e_first[nranks] = E). Per call, on
+ * every rank: power-of-two normalisation and router / top-k of its own tokens; ONE kernel
+ * stores each own token's normalised row into the exchange buffer of every rank owning one
+ * of its routed experts (once per token and rank) and its routing row into every rank's
+ * table, then waits (bounded, epoch flags) for every rank; the local experts over all tokens
+ * routed to them (grouped tcgen05 GEMMs for T >= 32, int8 GEMVs below); ONE kernel stores each
+ * computed (token, k) output row into its token owner's exchange buffer, waits, and the owner
+ * combines y = bf16(resid + sum_k bf16(yk * score_k)) in MLX order. Results equal the same call
+ * with nranks = 1 bit for bit. x, resid, y: [n][H] of this rank's tokens; out_inds u32 /
+ * out_scores bf16 [n][K]. peers: device array of every rank's exchange buffer (this rank's
+ * own at [rank]); own_buffer: this rank's buffer (host-known device address). Exchange
+ * buffers of moe_ep_a2a_buffer_bytes(T, K, H, nranks) from moe_ep_buffer_alloc; every rank
+ * makes the same calls in the same order with the same T. No reference counterpart (the
+ * reference runs on one device); replaces the per-layer block of mlx-qwen38/loader.py:903-922.
+ */
+size_t moe_ep_a2a_buffer_bytes(int T, int K, int H, int nranks);
+size_t moe_ep_a2a_workspace_bytes(int T, int H, int I, int E, int K, int nranks);
+/* number of tokens rank owns, *first = its first token */
+int moe_ep_a2a_local_tokens(int T, int nranks, int rank, int *first);
+int moe_ep_a2a_layer(const void *x, int T, int H, int I, int E, int K, const int *e_first,
+                     const void *router_w, const uint32_t *wg, const void *sg, const void *bg,
+                     const uint32_t *wu, const void *su, const void *bu, const uint32_t *wd,
+                     const void *sd, const void *bd, int sb_fp16, int norm, const void *resid,
+                     void *const *peers, const void *own_buffer, int rank, int nranks,
+                     uint32_t *out_inds, void *out_scores, void *y, void *workspace,
+                     size_t workspace_bytes, void *stream);
+
 /* ------------------------------------------------------------------------------------ */
 /* Per-layer LRU expert-slot cache with its state on the GPU.                             */
 /* ------------------------------------------------------------------------------------ */

@@ -65,6 +65,10 @@ SIGNATURES: dict[str, tuple] = {
     "moe_ep_buffer_free": (I, [P]),
     "moe_ep_workspace_bytes": (SZ, [I, I, I, I, I]),
     "moe_ep_decode_layer": (I, [P, I, I, I, I, I, I, I, P] + [P] * 9 + [I, I, P, P, I, I, P, P, P, P, SZ, P]),
+    "moe_ep_a2a_buffer_bytes": (SZ, [I, I, I, I]),
+    "moe_ep_a2a_workspace_bytes": (SZ, [I, I, I, I, I, I]),
+    "moe_ep_a2a_local_tokens": (I, [I, I, I, P]),
+    "moe_ep_a2a_layer": (I, [P, I, I, I, I, I, P, P] + [P] * 9 + [I, I, P, P, P, I, I, P, P, P, P, SZ, P]),
     "moe_lru_state_bytes": (SZ, [I, I]),
     "moe_lru_init": (I, [P, I, I, U64, P]),
     "moe_lru_reset": (I, [P, I, I, I, P]),

@@ -29,6 +29,7 @@
 // Reference semantics: the decode body of the reference's hook (mlx-qwen38/loader.py:903-922)
 // with the experts split across devices, as the expert-parallel configuration asks; the
 // reference itself runs on one device.
+#include <stddef.h>
 #include <string.h>
 
 #include <algorithm>
@@ -190,6 +191,224 @@ EpWs carve(void *base, int T, int H, int I, int E, int K) {
     return w;
 }
 
+// ====================================================================================
+// Token-sharded expert parallelism: routed all-to-all dispatch and combine.
+//
+// For batches with several tokens per GPU (c4's decode batches of 8 per GPU and its 4,096-
+// token prefill) every rank owns a contiguous block of ceil(T/N) tokens and their hidden
+// states. Per layer, rank r:
+//   router     the power-of-two normalised rows of its own tokens, exact softmax / top-k
+//   dispatch   ONE kernel: each own token's normalised row is stored (peer stores over NVLink)
+//              into the receive rows of every rank that owns one of its routed experts -- once
+//              per (token, rank), however many of its experts that rank holds -- and its
+//              routing row (experts, scores) into every rank's routing table; epoch flags, a
+//              bounded wait for every rank's signal
+//   experts    the rank's experts over every token routed to them (rows from the receive
+//              buffer, routing from the table): grouped tensor-core GEMMs for batches of 32
+//              tokens or more, per-slot int8 GEMVs below
+//   combine    ONE kernel: each expert output row (token, k) computed here is stored into the
+//              owning rank's return rows; signal, bounded wait, then the owner combines its
+//              tokens in MLX order with the residual
+// Every (token, k) output crosses NVLink once (the replicated path above stores every row in
+// every rank), and the results equal the single-GPU layer bit for bit (each row is computed
+// by the same kernels with the same arithmetic, each output slot has one writer).
+//
+// The buffers need no double buffering: a rank writes layer l+1's rows and routing into a
+// peer only after every rank signalled the combine of layer l, which a rank does only after
+// its expert kernels of layer l (the last readers of rows and routing) have finished; it
+// writes layer l+1's returned rows only after every rank signalled the dispatch of l+1, sent
+// only after that rank's combine of layer l (the last reader of the returned rows).
+// ====================================================================================
+
+struct A2aHeader {
+    unsigned long long flag_d[kMaxRanks];   // dispatch epochs signalled into this buffer
+    unsigned long long flag_c[kMaxRanks];   // combine epochs
+    unsigned int arrive_d, arrive_c;        // CTAs of the running kernels that have stored
+    unsigned int epoch;                     // layers this rank has completed
+};
+constexpr size_t kA2aHeaderBytes = 512;
+static_assert(sizeof(A2aHeader) <= kA2aHeaderBytes, "a2a header size");
+
+// after the header: received rows [T][H], routing [T][K] (u32 experts, u16 scores),
+// returned expert rows [Tl][K][H] of this rank's tokens
+struct A2aRegion {
+    size_t rows, inds, scores, back, bytes;
+    MOE_HD A2aRegion(int T, int Tl, int K, int H) {
+        rows = kA2aHeaderBytes;
+        inds = rows + al256((size_t)T * H * 2);
+        scores = inds + al256((size_t)T * K * 4);
+        back = scores + al256((size_t)T * K * 2);
+        bytes = back + al256((size_t)Tl * K * H * 2);
+    }
+};
+
+struct A2aArgs {
+    unsigned char *const *peers;
+    int rank, nranks, T, Tl, K, H;
+    int e_first[kMaxRanks + 1];             // rank q holds experts [e_first[q], e_first[q + 1])
+    int g0, tn;                             // this rank's tokens [g0, g0 + tn)
+    const uint16_t *xn;                     // [tn][H] own normalised rows
+    const uint32_t *inds;                   // [tn][K] own routing
+    const uint16_t *scores;                 // [tn][K]
+    const uint16_t *yk;                     // [T][K][H] expert outputs computed here (combine)
+    const uint16_t *resid;                  // [tn][H] or null (combine)
+    uint16_t *y;                            // [tn][H] (combine)
+};
+
+MOE_D int owner_of_expert(const A2aArgs &a, uint32_t e) {
+    int q = 0;
+#pragma unroll 1
+    while (q + 1 < a.nranks && (uint32_t)a.e_first[q + 1] <= e) ++q;
+    return q;
+}
+
+// the last CTA to arrive signals `e` into flag[rank] of every rank's header; every CTA's
+// thread 0 then waits (bounded, 2 s) until every rank has signalled into this rank's header
+MOE_D void a2a_signal_wait(const A2aArgs &a, unsigned int *arrive, size_t flag_off, unsigned int e) {
+    unsigned char *own = a.peers[a.rank];
+    if (threadIdx.x == 0) {
+        const unsigned int old = atomicAdd(arrive, 1u);
+        if (old + 1u == gridDim.x) {
+            *arrive = 0u;
+            __threadfence_system();
+            for (int p = 0; p < a.nranks; ++p)
+                st_release_sys(reinterpret_cast<unsigned long long *>(a.peers[p] + flag_off) + a.rank, e);
+        }
+        const unsigned long long *flags = reinterpret_cast<const unsigned long long *>(own + flag_off);
+        const unsigned long long t0 = globaltimer_ns();
+        for (int q = 0; q < a.nranks; ++q) {
+#pragma unroll 1
+            while (ld_acquire_sys(flags + q) < e) {
+                if (globaltimer_ns() - t0 > kPeerWaitNs) {
+                    atomicOr(&g_moe_device_error, MOE_DEVERR_PEER_TIMEOUT);
+                    break;
+                }
+            }
+        }
+    }
+    __syncthreads();
+}
+
+__global__ void __launch_bounds__(kExThreads) a2a_dispatch_kernel(A2aArgs a) {
+    unsigned char *own = a.peers[a.rank];
+    A2aHeader *hdr = reinterpret_cast<A2aHeader *>(own);
+    __shared__ unsigned int s_epoch;
+    if (threadIdx.x == 0) s_epoch = *reinterpret_cast<volatile unsigned int *>(&hdr->epoch) + 1u;
+    __syncthreads();
+    const unsigned int e = s_epoch;
+    const A2aRegion R(a.T, a.Tl, a.K, a.H);
+    const int cpr = a.H / 8;
+    const size_t stride = (size_t)gridDim.x * blockDim.x;
+    bool stored = false;
+    // rows: (token, destination rank, 16-byte chunk); a destination gets a row once
+    const size_t nrow = (size_t)a.tn * a.nranks * cpr;
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < nrow; i += stride) {
+        const int t = (int)(i / ((size_t)a.nranks * cpr));
+        const int q = (int)((i / cpr) % a.nranks);
+        const int c = (int)(i % cpr);
+        bool to_q = false;
+        for (int k = 0; k < a.K && !to_q; ++k) to_q = owner_of_expert(a, a.inds[(size_t)t * a.K + k]) == q;
+        if (!to_q) continue;
+        const uint4 v = *reinterpret_cast<const uint4 *>(a.xn + (size_t)t * a.H + (size_t)c * 8);
+        *reinterpret_cast<uint4 *>(a.peers[q] + R.rows + ((size_t)(a.g0 + t) * a.H + (size_t)c * 8) * 2) = v;
+        stored = true;
+    }
+    // the routing rows of this rank's tokens into every rank's table
+    const size_t nrt = (size_t)a.tn * a.K * a.nranks;
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < nrt; i += stride) {
+        const int q = (int)(i % a.nranks);
+        const size_t tk = i / a.nranks;
+        const size_t gk = (size_t)a.g0 * a.K + tk;
+        *reinterpret_cast<uint32_t *>(a.peers[q] + R.inds + gk * 4) = a.inds[tk];
+        *reinterpret_cast<uint16_t *>(a.peers[q] + R.scores + gk * 2) = a.scores[tk];
+        stored = true;
+    }
+    if (stored) __threadfence_system();
+    __syncthreads();
+    a2a_signal_wait(a, &hdr->arrive_d, offsetof(A2aHeader, flag_d), e);
+}
+
+__global__ void __launch_bounds__(kExThreads) a2a_combine_kernel(A2aArgs a) {
+    unsigned char *own = a.peers[a.rank];
+    A2aHeader *hdr = reinterpret_cast<A2aHeader *>(own);
+    __shared__ unsigned int s_epoch;
+    if (threadIdx.x == 0) s_epoch = *reinterpret_cast<volatile unsigned int *>(&hdr->epoch) + 1u;
+    __syncthreads();
+    const unsigned int e = s_epoch;
+    const A2aRegion R(a.T, a.Tl, a.K, a.H);
+    const uint32_t *inds = reinterpret_cast<const uint32_t *>(own + R.inds);
+    const uint32_t lo = (uint32_t)a.e_first[a.rank], hi = (uint32_t)a.e_first[a.rank + 1];
+    const int cpr = a.H / 8;
+    const size_t stride = (size_t)gridDim.x * blockDim.x;
+    bool stored = false;
+    // every (token, k) computed here goes back to the token's owner, once
+    const size_t nw = (size_t)a.T * a.K * cpr;
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < nw; i += stride) {
+        const size_t gk = i / cpr;
+        const int c = (int)(i % cpr);
+        const uint32_t ex = __ldcg(inds + gk);
+        if (ex < lo || ex >= hi) continue;
+        const int g = (int)(gk / a.K), k = (int)(gk % a.K);
+        const int o = g / a.Tl;
+        const uint4 v = *reinterpret_cast<const uint4 *>(a.yk + gk * a.H + (size_t)c * 8);
+        const size_t dst = ((size_t)(g - o * a.Tl) * a.K + k) * a.H + (size_t)c * 8;
+        *reinterpret_cast<uint4 *>(a.peers[o] + R.back + dst * 2) = v;
+        stored = true;
+    }
+    if (stored) __threadfence_system();
+    __syncthreads();
+    a2a_signal_wait(a, &hdr->arrive_c, offsetof(A2aHeader, flag_c), e);
+    // the epoch advances once every CTA has read it (they all passed the wait above)
+    if (blockIdx.x == 0 && threadIdx.x == 0) hdr->epoch = e;
+    // this rank's tokens: sequential bf16 sum over k in MLX order, then the residual
+    const uint16_t *back = reinterpret_cast<const uint16_t *>(own + R.back);
+    const size_t n = (size_t)a.tn * a.H;
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
+        const size_t t = i / a.H, h = i % a.H;
+        float acc = 0.f;
+        for (int k = 0; k < a.K; ++k) {
+            const float yv = bf16_bits_to_f32(__ldcg(back + (t * a.K + k) * a.H + h));
+            const float pk = bf16r(yv * bf16_bits_to_f32(a.scores[t * a.K + k]));
+            acc = (k == 0) ? pk : bf16r(acc + pk);
+        }
+        if (a.resid) acc = bf16r(bf16_bits_to_f32(a.resid[i]) + acc);
+        a.y[i] = f32_to_bf16_bits(acc);
+    }
+}
+
+struct A2aWs {
+    unsigned int *tickets;
+    uint16_t *logits, *xn, *act, *yk;
+    void *pws;
+    size_t pws_bytes, bytes;
+};
+
+A2aWs carve_a2a(void *base, int T, int Tl, int H, int I, int E, int K) {
+    A2aWs w{};
+    char *p = static_cast<char *>(base);
+    size_t off = 0;
+    auto take = [&](size_t n) { char *q = p ? p + off : nullptr; off += al256(n); return q; };
+    w.tickets = reinterpret_cast<unsigned int *>(take((size_t)Tl * 4));
+    w.logits = reinterpret_cast<uint16_t *>(take((size_t)Tl * E * 2));
+    w.xn = reinterpret_cast<uint16_t *>(take((size_t)Tl * H * 2));
+    w.yk = reinterpret_cast<uint16_t *>(take((size_t)T * K * H * 2));
+    if (T >= kEpGemmT) {
+        w.pws_bytes = moe_prefill_workspace_bytes(T, H, I, E, K);
+        w.pws = take(w.pws_bytes);
+    } else {
+        w.act = reinterpret_cast<uint16_t *>(take((size_t)T * K * I * 2));
+    }
+    w.bytes = off;
+    return w;
+}
+
+int local_tokens(int T, int nranks, int rank, int *g0) {
+    const int Tl = (T + nranks - 1) / nranks;
+    *g0 = std::min(T, rank * Tl);
+    return std::min(T, *g0 + Tl) - *g0;
+}
+
+
 }  // namespace
 
 extern "C" size_t moe_ep_buffer_bytes(int T, int K, int H) {
@@ -298,5 +517,111 @@ extern "C" int moe_ep_decode_layer(const void *x, int T, int H, int I, int E, in
     const int grid = (int)std::min<size_t>((size_t)sms, std::max<size_t>(2, (chunks + 4 * kExThreads - 1) / (4 * kExThreads)));
     MOE_CUDA_TRY(cudaLaunchCooperativeKernel((const void *)exchange_combine_kernel, dim3(grid), dim3(kExThreads), kargs,
                                              0, as_stream(stream)));
+    return MOE_OK;
+}
+
+extern "C" size_t moe_ep_a2a_buffer_bytes(int T, int K, int H, int nranks) {
+    if (T <= 0 || K <= 0 || H <= 0 || nranks <= 0) return 0;
+    return A2aRegion(T, (T + nranks - 1) / nranks, K, H).bytes;
+}
+
+extern "C" size_t moe_ep_a2a_workspace_bytes(int T, int H, int I, int E, int K, int nranks) {
+    if (T <= 0 || H <= 0 || I <= 0 || E <= 0 || K <= 0 || nranks <= 0) return 0;
+    return carve_a2a(nullptr, T, (T + nranks - 1) / nranks, H, I, E, K).bytes;
+}
+
+extern "C" int moe_ep_a2a_local_tokens(int T, int nranks, int rank, int *first) {
+    if (T <= 0 || nranks <= 0 || rank < 0 || rank >= nranks || !first) return 0;
+    return local_tokens(T, nranks, rank, first);
+}
+
+extern "C" int moe_ep_a2a_layer(const void *x, int T, int H, int I, int E, int K, const int *e_first,
+                                const void *router_w, const uint32_t *wg, const void *sg, const void *bg,
+                                const uint32_t *wu, const void *su, const void *bu, const uint32_t *wd, const void *sd,
+                                const void *bd, int sb_fp16, int norm, const void *resid, void *const *peers,
+                                const void *own_buffer, int rank, int nranks, uint32_t *out_inds, void *out_scores,
+                                void *y, void *workspace, size_t workspace_bytes, void *stream) {
+    if (!router_w || !peers || !own_buffer || !workspace || !e_first)
+        return moe_set_error(MOE_EINVAL, "ep_a2a_layer: null pointer");
+    if (nranks < 1 || nranks > kMaxRanks || rank < 0 || rank >= nranks)
+        return moe_set_error(MOE_EINVAL, "ep_a2a_layer: rank %d of %d (at most %d ranks)", rank, nranks, kMaxRanks);
+    if (T <= 0 || H % 64 || I % 64 || K <= 0 || K > E || e_first[0] != 0 || e_first[nranks] != E)
+        return moe_set_error(MOE_EINVAL, "ep_a2a_layer: bad sizes T=%d H=%d I=%d E=%d K=%d or expert split", T, H,
+                             I, E, K);
+    for (int q = 0; q < nranks; ++q)
+        if (e_first[q + 1] <= e_first[q])
+            return moe_set_error(MOE_EINVAL, "ep_a2a_layer: rank %d holds no experts", q);
+    const size_t need = moe_ep_a2a_workspace_bytes(T, H, I, E, K, nranks);
+    if (workspace_bytes < need)
+        return moe_set_error(MOE_EINVAL, "ep_a2a_layer: workspace of %zu bytes needed, %zu given", need,
+                             workspace_bytes);
+    const int Tl = (T + nranks - 1) / nranks;
+    int g0 = 0;
+    const int tn = local_tokens(T, nranks, rank, &g0);
+    if (tn > 0 && (!x || !out_inds || !out_scores || !y))
+        return moe_set_error(MOE_EINVAL, "ep_a2a_layer: null token buffers");
+    A2aWs w = carve_a2a(workspace, T, Tl, H, I, E, K);
+    const int e0 = e_first[rank], n = e_first[rank + 1] - e_first[rank];
+    const A2aRegion R(T, Tl, K, H);
+    const unsigned char *own = static_cast<const unsigned char *>(own_buffer);
+    const uint16_t *rows = reinterpret_cast<const uint16_t *>(own + R.rows);
+    const uint32_t *all_inds = reinterpret_cast<const uint32_t *>(own + R.inds);
+    int rc;
+    // own tokens: normalised rows and their routing
+    if (tn > 0) {
+        if (norm) {
+            rc = moe_pow2_rows_launch(x, tn, H, w.xn, stream);
+            if (rc) return rc;
+        } else {
+            MOE_CUDA_TRY(cudaMemcpyAsync(w.xn, x, (size_t)tn * H * 2, cudaMemcpyDeviceToDevice, as_stream(stream)));
+        }
+        rc = moe_router_launch(w.xn, tn, H, E, K, router_w, nullptr, nullptr, 16, 64, 0, nullptr, nullptr, nullptr, 0,
+                               nullptr, nullptr, nullptr, out_inds, out_scores, nullptr, w.tickets, w.logits, nullptr,
+                               nullptr, nullptr, nullptr, 0, stream);
+        if (rc) return rc;
+    }
+    int dev = 0, sms = 0;
+    MOE_CUDA_TRY(cudaGetDevice(&dev));
+    MOE_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+    A2aArgs a{};
+    a.peers = reinterpret_cast<unsigned char *const *>(peers);
+    a.rank = rank;
+    a.nranks = nranks;
+    a.T = T;
+    a.Tl = Tl;
+    a.K = K;
+    a.H = H;
+    for (int q = 0; q <= nranks; ++q) a.e_first[q] = e_first[q];
+    a.g0 = g0;
+    a.tn = tn;
+    a.xn = w.xn;
+    a.inds = out_inds;
+    a.scores = static_cast<const uint16_t *>(out_scores);
+    a.yk = w.yk;
+    a.resid = static_cast<const uint16_t *>(resid);
+    a.y = static_cast<uint16_t *>(y);
+    void *kargs[] = {&a};
+    const size_t dchunks = (size_t)std::max(tn, 1) * nranks * (H / 8);
+    const int gd =
+        (int)std::min<size_t>((size_t)sms, std::max<size_t>(2, (dchunks + 4 * kExThreads - 1) / (4 * kExThreads)));
+    MOE_CUDA_TRY(cudaLaunchCooperativeKernel((const void *)a2a_dispatch_kernel, dim3(gd), dim3(kExThreads), kargs, 0,
+                                             as_stream(stream)));
+    // this rank's experts over every token routed to them (rows and routing in its buffer)
+    if (T >= kEpGemmT) {
+        rc = moe_prefill_experts_ex(rows, T, H, I, n, K, all_inds, (uint32_t)e0, 0, nullptr, wg, sg, bg, wu, su, bu, wd,
+                                    sd, bd, sb_fp16, nullptr, nullptr, w.yk, nullptr, w.pws, w.pws_bytes, stream);
+    } else {
+        rc = moe_experts_gateup_ex(rows, nullptr, nullptr, nullptr, T, H, I, K, n, all_inds, wg, sg, bg, wu, su, bu, 2,
+                                   64, sb_fp16, w.act, nullptr, nullptr, nullptr, nullptr, stream, (uint32_t)e0);
+        if (rc) return rc;
+        rc = moe_experts_down_ex(w.act, nullptr, nullptr, nullptr, T, H, I, K, n, all_inds, nullptr, wd, sd, bd, 2, 64,
+                                 sb_fp16, nullptr, nullptr, nullptr, w.yk, stream, (uint32_t)e0);
+    }
+    if (rc) return rc;
+    const size_t cchunks = (size_t)T * K * (H / 8) / nranks + (size_t)std::max(tn, 1) * H / 8;
+    const int gc =
+        (int)std::min<size_t>((size_t)sms, std::max<size_t>(2, (cchunks + 4 * kExThreads - 1) / (4 * kExThreads)));
+    MOE_CUDA_TRY(cudaLaunchCooperativeKernel((const void *)a2a_combine_kernel, dim3(gc), dim3(kExThreads), kargs, 0,
+                                             as_stream(stream)));
     return MOE_OK;
 }

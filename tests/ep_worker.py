@@ -2,7 +2,8 @@
 torch.distributed.run, one process per GPU): every rank builds the same seeded numpy stack,
 keeps its block of the experts, runs the expert-parallel decode (layer calls and the
 graph-captured stack) and checks that its results equal, bit for bit, the single-GPU
-decode layers run on its own GPU with all experts. Exits non-zero on a mismatch."""
+decode layers run on its own GPU with all experts; then the same for the token-sharded layer
+(routed all-to-all), its own block of the batch. Exits non-zero on a mismatch."""
 import datetime
 import json
 import os
@@ -60,6 +61,37 @@ def main() -> int:
         if not torch.equal(y, h):
             bad.append("stack output")
     st.close()
+
+    # token-sharded (routed all-to-all): this rank's block of a 40-token batch (grouped GEMMs)
+    # and of an 8-token batch (GEMVs), layer calls and the graph-captured stack, against the
+    # single-GPU layers on the whole batch
+    from moe_offload_b200.ep import EPA2AStack, ep_a2a_layer, expert_bounds, local_tokens
+    ef = expert_bounds(E, world)
+    for TT in (40, 8):
+        xa = np_to_bf16_tensor(np_bf16_normal(rng, (TT, H)), dev)
+        g0, nt = local_tokens(TT, world, rank)
+        xb2 = ExchangeBuffers(TT, K, H, dev, a2a=True)
+        for rep in range(2):
+            o = ep_a2a_layer(xa[g0:g0 + nt], local[0], E, ef, K, TT, xb2, norm=True, resid=xa[g0:g0 + nt])
+            ref = ops.decode_layer if TT < 32 else ops.prefill_layer
+            r = ref(xa, full[0].router, full[0].gate, full[0].up, full[0].down, K, norm=True, resid=xa)
+            torch.cuda.synchronize()
+            for key in ("inds", "scores", "y"):
+                if not torch.equal(o[key], r[key][g0:g0 + nt]):
+                    bad.append(f"a2a layer {key} T={TT} call {rep}")
+        xb2.close()
+        sa = EPA2AStack(local, E, ef, K, TT, dev)
+        for _ in range(2):
+            xa = np_to_bf16_tensor(np_bf16_normal(rng, (TT, H)), dev)
+            y = sa.step_device(xa[g0:g0 + nt]).clone()
+            h = xa
+            for ly in full:
+                fn = ops.decode_layer if TT < 32 else ops.prefill_layer
+                h = fn(h, ly.router, ly.gate, ly.up, ly.down, K, norm=True, resid=h)["y"]
+            torch.cuda.synchronize()
+            if not torch.equal(y, h[g0:g0 + nt]):
+                bad.append(f"a2a stack output T={TT}")
+        sa.close()
     err = int(_lib.call("moe_device_error", 1))
     if err:
         bad.append(f"device error word {err}")

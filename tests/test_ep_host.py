@@ -23,6 +23,21 @@ def test_expert_shard_partitions_all_experts(E, world):
     assert max(sizes) - min(sizes) <= 1
 
 
+@pytest.mark.parametrize("T,world", [(64, 8), (40, 2), (7, 3), (3, 8), (4096, 8), (1, 1)])
+def test_token_blocks_partition_the_batch(T, world):
+    """Token-sharded EP: contiguous blocks of ceil(T/world) tokens cover the batch once (the
+    last ranks may get fewer or none), and the expert bounds cover every expert once."""
+    from moe_offload_b200.ep import expert_bounds, local_tokens
+    seen = []
+    for r in range(world):
+        first, n = local_tokens(T, world, r)
+        assert 0 <= n <= -(-T // world)
+        seen.extend(range(first, first + n))
+    assert seen == list(range(T))
+    ef = expert_bounds(512, world)
+    assert ef[0] == 0 and ef[-1] == 512 and all(a < b for a, b in zip(ef, ef[1:]))
+
+
 def test_expert_shard_rejects_bad_splits():
     from moe_offload_b200.ep import expert_shard
     with pytest.raises(ValueError):
