@@ -56,6 +56,9 @@ def parse():
     ap.add_argument("--replicas", action="store_true",
                     help="--gpus N > 1: N independent replicas of the c1 stack instead of expert parallelism")
     ap.add_argument("--no-check", action="store_true", help="c4: skip the bit-exact check of layer 0")
+    ap.add_argument("--ep-mode", choices=["auto", "sharded", "replicated"], default="auto",
+                    help="c4: tokens sharded (routed all-to-all) or replicated on every rank; auto: sharded "
+                         "from 4 tokens per GPU")
     ap.add_argument("--layers", type=int, default=0,
                     help="profiling aid: run only the first N layers of the stack (0 = all 28)")
     return ap.parse_args()
@@ -765,7 +768,7 @@ def run_c4(args, rank: int, world: int, local_rank: int) -> None:
     cfg = C4
     L = args.layers or cfg.layers
     B = args.batch or 8 * world
-    sharded = B >= A2A_MIN_TOKENS_PER_RANK * world
+    sharded = (B >= A2A_MIN_TOKENS_PER_RANK * world) if args.ep_mode == "auto" else args.ep_mode == "sharded"
     first, n = expert_shard(cfg.experts, rank, world)
     layers = dev_stack_shard(cfg, dev, first, n, layers=L)
     gen = torch.Generator(device=dev)

@@ -229,13 +229,21 @@ struct A2aHeader {
 constexpr size_t kA2aHeaderBytes = 512;
 static_assert(sizeof(A2aHeader) <= kA2aHeaderBytes, "a2a header size");
 
-// after the header: received rows [T][H], routing [T][K] (u32 experts, u16 scores),
-// returned expert rows [Tl][K][H] of this rank's tokens
+// after the header: received rows [T][H] (batches of kEpGemmT tokens or more: the GEMMs
+// take bf16 rows) or received int8 MMA records of the rows [T][H/64][128 B] with their scales
+// and sums [T][pad4(H/64)] (smaller batches: the GEMV kernels take records, built once by the
+// owner's router), routing [T][K] (u32 experts, u16 scores), returned expert rows [Tl][K][H]
+// of this rank's tokens
 struct A2aRegion {
-    size_t rows, inds, scores, back, bytes;
+    size_t rows, rec, rscale, rsum, inds, scores, back, bytes;
     MOE_HD A2aRegion(int T, int Tl, int K, int H) {
+        const size_t ng = (size_t)H / 64, fb = (size_t)pad4((int)ng) * 4;
         rows = kA2aHeaderBytes;
-        inds = rows + al256((size_t)T * H * 2);
+        rec = rows;                                   // the two forms share the space
+        rscale = rec + al256((size_t)T * ng * 128);
+        rsum = rscale + al256((size_t)T * fb);
+        const size_t payload = std::max(al256((size_t)T * H * 2), rsum + al256((size_t)T * fb) - rows);
+        inds = rows + payload;
         scores = inds + al256((size_t)T * K * 4);
         back = scores + al256((size_t)T * K * 2);
         bytes = back + al256((size_t)Tl * K * H * 2);
@@ -247,7 +255,9 @@ struct A2aArgs {
     int rank, nranks, T, Tl, K, H;
     int e_first[kMaxRanks + 1];             // rank q holds experts [e_first[q], e_first[q + 1])
     int g0, tn;                             // this rank's tokens [g0, g0 + tn)
-    const uint16_t *xn;                     // [tn][H] own normalised rows
+    const uint16_t *xn;                     // [tn][H] own normalised rows (rows form)
+    const uint2 *xrec;                      // [tn][H/64][16] own records (records form), or null
+    const float *xscale, *xsum;             // [tn][pad4(H/64)]
     const uint32_t *inds;                   // [tn][K] own routing
     const uint16_t *scores;                 // [tn][K]
     const uint16_t *yk;                     // [T][K][H] expert outputs computed here (combine)
@@ -300,17 +310,37 @@ __global__ void __launch_bounds__(kExThreads) a2a_dispatch_kernel(A2aArgs a) {
     const int cpr = a.H / 8;
     const size_t stride = (size_t)gridDim.x * blockDim.x;
     bool stored = false;
-    // rows: (token, destination rank, 16-byte chunk); a destination gets a row once
-    const size_t nrow = (size_t)a.tn * a.nranks * cpr;
+    // payload per token: the bf16 row, or its records (8 chunks of 16 bytes per 64-value group)
+    // followed by the group scales and sums; (token, destination rank, 16-byte chunk), a
+    // destination gets a token's payload once
+    const int ng = a.H / 64, fw = pad4(ng);
+    const int rec_chunks = ng * 8, f_chunks = fw / 4;
+    const int pay = a.xrec ? rec_chunks + 2 * f_chunks : cpr;
+    const size_t nrow = (size_t)a.tn * a.nranks * pay;
     for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < nrow; i += stride) {
-        const int t = (int)(i / ((size_t)a.nranks * cpr));
-        const int q = (int)((i / cpr) % a.nranks);
-        const int c = (int)(i % cpr);
+        const int t = (int)(i / ((size_t)a.nranks * pay));
+        const int q = (int)((i / pay) % a.nranks);
+        const int c = (int)(i % pay);
         bool to_q = false;
         for (int k = 0; k < a.K && !to_q; ++k) to_q = owner_of_expert(a, a.inds[(size_t)t * a.K + k]) == q;
         if (!to_q) continue;
-        const uint4 v = *reinterpret_cast<const uint4 *>(a.xn + (size_t)t * a.H + (size_t)c * 8);
-        *reinterpret_cast<uint4 *>(a.peers[q] + R.rows + ((size_t)(a.g0 + t) * a.H + (size_t)c * 8) * 2) = v;
+        const size_t g = (size_t)(a.g0 + t);
+        const uint4 *src;
+        unsigned char *dst;
+        if (!a.xrec) {
+            src = reinterpret_cast<const uint4 *>(a.xn + (size_t)t * a.H) + c;
+            dst = a.peers[q] + R.rows + (g * a.H) * 2 + (size_t)c * 16;
+        } else if (c < rec_chunks) {
+            src = reinterpret_cast<const uint4 *>(a.xrec + (size_t)t * ng * 16) + c;
+            dst = a.peers[q] + R.rec + g * ng * 128 + (size_t)c * 16;
+        } else if (c < rec_chunks + f_chunks) {
+            src = reinterpret_cast<const uint4 *>(a.xscale + (size_t)t * fw) + (c - rec_chunks);
+            dst = a.peers[q] + R.rscale + g * fw * 4 + (size_t)(c - rec_chunks) * 16;
+        } else {
+            src = reinterpret_cast<const uint4 *>(a.xsum + (size_t)t * fw) + (c - rec_chunks - f_chunks);
+            dst = a.peers[q] + R.rsum + g * fw * 4 + (size_t)(c - rec_chunks - f_chunks) * 16;
+        }
+        *reinterpret_cast<uint4 *>(dst) = *src;
         stored = true;
     }
     // the routing rows of this rank's tokens into every rank's table
@@ -379,6 +409,8 @@ __global__ void __launch_bounds__(kExThreads) a2a_combine_kernel(A2aArgs a) {
 struct A2aWs {
     unsigned int *tickets;
     uint16_t *logits, *xn, *act, *yk;
+    uint2 *xrec;                            // own records (batches below kEpGemmT)
+    float *xscale, *xsum;
     void *pws;
     size_t pws_bytes, bytes;
 };
@@ -397,6 +429,9 @@ A2aWs carve_a2a(void *base, int T, int Tl, int H, int I, int E, int K) {
         w.pws = take(w.pws_bytes);
     } else {
         w.act = reinterpret_cast<uint16_t *>(take((size_t)T * K * I * 2));
+        w.xrec = reinterpret_cast<uint2 *>(take((size_t)Tl * (H / 64) * 128));
+        w.xscale = reinterpret_cast<float *>(take((size_t)Tl * pad4(H / 64) * 4));
+        w.xsum = reinterpret_cast<float *>(take((size_t)Tl * pad4(H / 64) * 4));
     }
     w.bytes = off;
     return w;
@@ -567,17 +602,26 @@ extern "C" int moe_ep_a2a_layer(const void *x, int T, int H, int I, int E, int K
     const uint16_t *rows = reinterpret_cast<const uint16_t *>(own + R.rows);
     const uint32_t *all_inds = reinterpret_cast<const uint32_t *>(own + R.inds);
     int rc;
-    // own tokens: normalised rows and their routing
+    const bool gemm = T >= kEpGemmT;
+    // own tokens: routing, and what the experts take -- normalised bf16 rows (GEMMs), or the
+    // int8 records of the normalised rows built by the router (GEMVs)
     if (tn > 0) {
-        if (norm) {
-            rc = moe_pow2_rows_launch(x, tn, H, w.xn, stream);
-            if (rc) return rc;
+        if (gemm) {
+            if (norm) {
+                rc = moe_pow2_rows_launch(x, tn, H, w.xn, stream);
+                if (rc) return rc;
+            } else {
+                MOE_CUDA_TRY(
+                    cudaMemcpyAsync(w.xn, x, (size_t)tn * H * 2, cudaMemcpyDeviceToDevice, as_stream(stream)));
+            }
+            rc = moe_router_launch(w.xn, tn, H, E, K, router_w, nullptr, nullptr, 16, 64, 0, nullptr, nullptr, nullptr,
+                                   0, nullptr, nullptr, nullptr, out_inds, out_scores, nullptr, w.tickets, w.logits,
+                                   nullptr, nullptr, nullptr, nullptr, 0, stream);
         } else {
-            MOE_CUDA_TRY(cudaMemcpyAsync(w.xn, x, (size_t)tn * H * 2, cudaMemcpyDeviceToDevice, as_stream(stream)));
+            rc = moe_router_launch(x, tn, H, E, K, router_w, nullptr, nullptr, 16, 64, 0, nullptr, nullptr, nullptr, 0,
+                                   nullptr, nullptr, nullptr, out_inds, out_scores, nullptr, w.tickets, w.logits,
+                                   nullptr, w.xrec, w.xscale, w.xsum, norm, stream);
         }
-        rc = moe_router_launch(w.xn, tn, H, E, K, router_w, nullptr, nullptr, 16, 64, 0, nullptr, nullptr, nullptr, 0,
-                               nullptr, nullptr, nullptr, out_inds, out_scores, nullptr, w.tickets, w.logits, nullptr,
-                               nullptr, nullptr, nullptr, 0, stream);
         if (rc) return rc;
     }
     int dev = 0, sms = 0;
@@ -595,24 +639,29 @@ extern "C" int moe_ep_a2a_layer(const void *x, int T, int H, int I, int E, int K
     a.g0 = g0;
     a.tn = tn;
     a.xn = w.xn;
+    a.xrec = gemm ? nullptr : w.xrec;
+    a.xscale = gemm ? nullptr : w.xscale;
+    a.xsum = gemm ? nullptr : w.xsum;
     a.inds = out_inds;
     a.scores = static_cast<const uint16_t *>(out_scores);
     a.yk = w.yk;
     a.resid = static_cast<const uint16_t *>(resid);
     a.y = static_cast<uint16_t *>(y);
     void *kargs[] = {&a};
-    const size_t dchunks = (size_t)std::max(tn, 1) * nranks * (H / 8);
+    const size_t dchunks = (size_t)std::max(tn, 1) * nranks * (H / 8 + 32);
     const int gd =
         (int)std::min<size_t>((size_t)sms, std::max<size_t>(2, (dchunks + 4 * kExThreads - 1) / (4 * kExThreads)));
     MOE_CUDA_TRY(cudaLaunchCooperativeKernel((const void *)a2a_dispatch_kernel, dim3(gd), dim3(kExThreads), kargs, 0,
                                              as_stream(stream)));
     // this rank's experts over every token routed to them (rows and routing in its buffer)
-    if (T >= kEpGemmT) {
+    if (gemm) {
         rc = moe_prefill_experts_ex(rows, T, H, I, n, K, all_inds, (uint32_t)e0, 0, nullptr, wg, sg, bg, wu, su, bu, wd,
                                     sd, bd, sb_fp16, nullptr, nullptr, w.yk, nullptr, w.pws, w.pws_bytes, stream);
     } else {
-        rc = moe_experts_gateup_ex(rows, nullptr, nullptr, nullptr, T, H, I, K, n, all_inds, wg, sg, bg, wu, su, bu, 2,
-                                   64, sb_fp16, w.act, nullptr, nullptr, nullptr, nullptr, stream, (uint32_t)e0);
+        rc = moe_experts_gateup_ex(rows, own + R.rec, reinterpret_cast<const float *>(own + R.rscale),
+                                   reinterpret_cast<const float *>(own + R.rsum), T, H, I, K, n, all_inds, wg, sg, bg,
+                                   wu, su, bu, 2, 64, sb_fp16, w.act, nullptr, nullptr, nullptr, nullptr, stream,
+                                   (uint32_t)e0);
         if (rc) return rc;
         rc = moe_experts_down_ex(w.act, nullptr, nullptr, nullptr, T, H, I, K, n, all_inds, nullptr, wd, sd, bd, 2, 64,
                                  sb_fp16, nullptr, nullptr, nullptr, w.yk, stream, (uint32_t)e0);
