@@ -436,6 +436,28 @@ int moe_lru_step(void *state, int E, int cap, const uint32_t *eids, int k, uint3
 int moe_lru_prefetch(void *state, int E, int cap, const int32_t *pred, int n, int max_fetch,
                      int32_t *out_fetch, void *stream);
 
+/* Device bytes of the per-token I/O accounting record shared by every layer
+ * (cpp/third_party/expert_io.c:97-111): {int32 enabled, int32 current token (-1: none),
+ * 8 pad bytes, u64 counters[9] in c_end_decode_token order}. Allocate 16-byte aligned device
+ * memory of this size, zero it and set the token to -1. */
+size_t moe_lru_acct_bytes(void);
+
+/* moe_lru_step with per-token accounting and the scheduled-step variant. acct: null or the
+ * record above; with enabled != 0 the step adds its LRU hits, prefetch hits, wasted
+ * prefetches and demand misses, and (token >= 0) its demand re-reads of experts evicted at
+ * most 16 / 64 tokens earlier, and stamps evicted experts with the token
+ * (cpp/third_party/expert_io.c:745-806). sched != 0 (cpp/third_party/expert_io.c:1129-1270):
+ * eviction also skips the experts the layer's last prefetch fetched, and out_miss must hold
+ * 1 + 3k entries: after the lists, hit flags [k] (1: the expert was resident) in request
+ * order. */
+int moe_lru_step_ex(void *state, int E, int cap, const uint32_t *eids, int k, uint32_t *out_slots,
+                    int32_t *out_miss, void *acct, int sched, void *stream);
+
+/* moe_lru_prefetch with accounting (prefetch loads; prefetch re-reads, token >= 0) and, with
+ * sched != 0, a prediction listed twice fetched once (cpp/third_party/expert_io.c:1290-1340). */
+int moe_lru_prefetch_ex(void *state, int E, int cap, const int32_t *pred, int n, int max_fetch,
+                        int32_t *out_fetch, void *acct, int sched, void *stream);
+
 /* out = device i32 [1 + 2*cap] {count, eids (LRU -> MRU) .., slots ..}
  * (expert_io.c:726-747, c_layer_get_lru_state). */
 int moe_lru_get_state(void *state, int E, int cap, int32_t *out, void *stream);
@@ -506,6 +528,31 @@ void c_layer_set_lru_state(int layer_idx, const int32_t *ordered_eids, const int
                            uint64_t add_prefill_requests, uint64_t add_prefill_hits, uint64_t add_prefill_misses);
 void c_layer_get_stats(int layer_idx, uint64_t *out_stats);
 void c_get_decode_totals(int num_layers, uint64_t *out6);
+
+/* The newer reference's additions (cpp/src/expert_io.h:8-12, 87-106; behaviour of
+ * cpp/third_party/expert_io.c:1002-1396). Accounting is off by default; when on, every step
+ * and prefetch counts into one record shared by all layers, read per token: */
+void c_set_io_accounting(int enabled);           /* off also ends the token in progress */
+void c_begin_decode_token(int token_idx);        /* token_idx unused: tokens are counted */
+/* out10 = {LRU hits, demand misses, prefetch loads, prefetch hits, wasted prefetches,
+ * demand re-reads within 16 / 64 tokens, prefetch re-reads within 16 / 64 tokens, bytes
+ * filled into slots} since c_begin_decode_token */
+void c_end_decode_token(uint64_t *out10);
+/* bytes of this module's own buffers: device LRU states and staging buffers */
+uint64_t c_get_native_buffer_bytes(void);
+/* the last recorded hit/miss split of layer_idx (a scheduled step with flag 4 whose demand
+ * missed some but not all experts): hit slots, miss slots, and for each request its index
+ * in hits ++ misses */
+void c_layer_get_split_inds(int layer_idx, uint32_t *out_hit_slots, uint32_t *out_miss_slots,
+                            int32_t *out_inv_order);
+/* One call per layer (cpp/third_party/expert_io.c:1094-1396): demand step of layer_idx
+ * (> 0; k capped at 16; its last prefetch's experts stay protected) and, unless flags & 2,
+ * the deduplicated prefetch of pred [n_pred <= 64] into next_layer (> 0, at most
+ * prefetch_cap, 32 when out of 1..31). Demand fills are queued before prefetch fills;
+ * flags & 1, or no demand miss, waits for all fills; flags & 4 records the split above.
+ * Returns the demand misses; c_layer_wait_demand waits for the fills. */
+int c_layer_decode_step_sched(int layer_idx, const int32_t *eids, int k, const int32_t *pred, int n_pred,
+                              int next_layer, int prefetch_cap, int flags);
 
 /*
  * P1 I/O scheduler (replaces qwen38::P1IoScheduler, mlx-qwen38/cpp/src/io_sched.h:46-245, with

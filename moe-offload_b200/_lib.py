@@ -74,6 +74,9 @@ SIGNATURES: dict[str, tuple] = {
     "moe_lru_reset": (I, [P, I, I, I, P]),
     "moe_lru_step": (I, [P, I, I, P, I, P, P, P]),
     "moe_lru_prefetch": (I, [P, I, I, P, I, I, P, P]),
+    "moe_lru_acct_bytes": (SZ, []),
+    "moe_lru_step_ex": (I, [P, I, I, P, I, P, P, P, I, P]),
+    "moe_lru_prefetch_ex": (I, [P, I, I, P, I, I, P, P, I, P]),
     "moe_lru_get_state": (I, [P, I, I, P, P]),
     "moe_lru_set_state": (I, [P, I, I, P, P, I, U64, U64, U64, P]),
     "moe_lru_get_stats": (I, [P, I, I, P, P]),
@@ -101,6 +104,12 @@ SIGNATURES: dict[str, tuple] = {
     "c_layer_set_lru_state": (None, [I, P, P, I, U64, U64, U64]),
     "c_layer_get_stats": (None, [I, P]),
     "c_get_decode_totals": (None, [I, P]),
+    "c_set_io_accounting": (None, [I]),
+    "c_begin_decode_token": (None, [I]),
+    "c_end_decode_token": (None, [P]),
+    "c_get_native_buffer_bytes": (U64, []),
+    "c_layer_get_split_inds": (None, [I, P, P, P]),
+    "c_layer_decode_step_sched": (I, [I, P, I, P, I, I, I, I]),
     "moe_stack_workspace_bytes": (SZ, [I, I, I, I]),
     "moe_stack_decode": (I, [P, I, I, I, I, I, I, I, P, P, P, P, P, P, SZ, I, P]),
 }

@@ -12,6 +12,13 @@
 // variants and for prefetches, waited by c_layer_wait_demand / c_layer_wait_prefetch or at
 // the start of the next call, as the reference's wait_async_batch does). slot_inds_ptr may
 // be device memory (written by the kernel) or host memory (written after the read-back).
+//
+// The newer reference's additions (cpp/third_party/expert_io.c:1002-1396, declared in
+// cpp/src/expert_io.h:87-106) are here too: per-token I/O accounting (c_set_io_accounting,
+// c_begin_decode_token, c_end_decode_token) kept in one device LruAcct that every layer's LRU
+// kernel updates, the single-call scheduled step c_layer_decode_step_sched (demand step of one
+// layer protecting its in-flight prefetch, then the next layer's deduplicated prefetch, demand
+// fills queued before prefetch fills) and its hit/miss split records (c_layer_get_split_inds).
 #include <algorithm>
 #include <cstring>
 #include <mutex>
@@ -30,6 +37,10 @@ constexpr int kMaxTensors = 9;
 constexpr int kRefExperts = 512;                   // the reference's NUM_EXPERTS
 constexpr uint64_t kRefExpertBytes = 1536000ull;   // the reference's EXPERT_BYTES (stats unit)
 constexpr int kListMax = 1 + 2 * 2048;
+constexpr int kEidsMax = 128;                      // staged eids: a demand step's 16, then 64 predictions
+constexpr int kSchedK = 16;                        // the scheduled step's cap on k
+constexpr int kPrefList = 128;                     // offset of the prefetch list in the list buffers
+constexpr int kFlagSyncDemand = 1, kFlagNoPrefetch = 2, kFlagSplit = 4;   // cpp/src/expert_io.h:8-12
 
 struct CompatLayer {
     bool init = false;
@@ -44,6 +55,19 @@ struct CompatLayer {
     void *state = nullptr;
 };
 
+// the last hit/miss split of a layer's scheduled step: written only by a split step, kept
+// through layer re-initialisation, as the reference's per-layer split arrays are
+struct SplitRecord {
+    int hit = 0, miss = 0, k = 0;
+    uint32_t hit_slots[kSchedK] = {}, miss_slots[kSchedK] = {};
+    int32_t inv[kSchedK] = {};
+};
+
+// host mirror of the device LruAcct header (lru.cu); counters live only on the device
+struct AcctHeader {
+    int32_t enabled, cur_token, pad0, pad1;
+};
+
 struct Compat {
     std::mutex mu;
     bool io = false;
@@ -54,7 +78,16 @@ struct Compat {
     int32_t *h_list = nullptr, *d_list = nullptr, *h_ord = nullptr, *d_ord = nullptr;
     uint32_t *h_slots = nullptr, *d_slots = nullptr;
     uint64_t *h_stats = nullptr, *d_stats = nullptr;
+    // per-token accounting: device record (header + 9 counters), its pinned staging copy,
+    // the token step counter and the filled bytes of the token in progress
+    void *d_acct = nullptr;
+    unsigned char *h_acct = nullptr;
+    size_t acct_bytes = 0;
+    AcctHeader acct{0, -1, 0, 0};
+    int32_t token_step = 0;
+    uint64_t tok_fill_bytes = 0;
     CompatLayer L[kMaxLayers];
+    SplitRecord split[kMaxLayers];
 };
 
 Compat g;
@@ -66,8 +99,8 @@ bool ensure_io() {
     bool good = ok(cudaStreamCreateWithFlags(&g.st, cudaStreamNonBlocking)) &&
                 ok(cudaStreamCreateWithFlags(&g.copy, cudaStreamNonBlocking)) &&
                 ok(cudaEventCreateWithFlags(&g.fills, cudaEventDisableTiming)) &&
-                ok(cudaHostAlloc(&g.h_eids, 64 * 4, cudaHostAllocDefault)) &&
-                ok(cudaMalloc(&g.d_eids, 64 * 4)) &&
+                ok(cudaHostAlloc(&g.h_eids, kEidsMax * 4, cudaHostAllocDefault)) &&
+                ok(cudaMalloc(&g.d_eids, kEidsMax * 4)) &&
                 ok(cudaHostAlloc(&g.h_list, kListMax * 4, cudaHostAllocDefault)) &&
                 ok(cudaMalloc(&g.d_list, kListMax * 4)) &&
                 ok(cudaHostAlloc(&g.h_ord, 2 * 2048 * 4, cudaHostAllocDefault)) &&
@@ -76,8 +109,29 @@ bool ensure_io() {
                 ok(cudaMalloc(&g.d_slots, 64 * 4)) &&
                 ok(cudaHostAlloc(&g.h_stats, 18 * 8, cudaHostAllocDefault)) &&
                 ok(cudaMalloc(&g.d_stats, 18 * 8));
+    if (good) {
+        g.acct_bytes = moe_lru_acct_bytes();
+        good = ok(cudaMalloc(&g.d_acct, g.acct_bytes)) &&
+               ok(cudaHostAlloc(reinterpret_cast<void **>(&g.h_acct), g.acct_bytes, cudaHostAllocDefault));
+        if (good) {
+            std::memset(g.h_acct, 0, g.acct_bytes);
+            std::memcpy(g.h_acct, &g.acct, sizeof(AcctHeader));
+            good = ok(cudaMemcpyAsync(g.d_acct, g.h_acct, g.acct_bytes, cudaMemcpyHostToDevice, g.st)) &&
+                   ok(cudaStreamSynchronize(g.st));
+        }
+    }
     g.io = good;
     return good;
+}
+
+// push the host accounting header (and, with zero_counters, cleared counters) to the device
+void push_acct(bool zero_counters) {
+    if (!g.io) return;
+    if (zero_counters) std::memset(g.h_acct, 0, g.acct_bytes);
+    std::memcpy(g.h_acct, &g.acct, sizeof(AcctHeader));
+    cudaMemcpyAsync(g.d_acct, g.h_acct, zero_counters ? g.acct_bytes : sizeof(AcctHeader), cudaMemcpyHostToDevice,
+                    g.st);
+    cudaStreamSynchronize(g.st);
 }
 
 CompatLayer *layer(int i) {
@@ -93,15 +147,24 @@ void wait_fills() {
     }
 }
 
-// fills of list h_list (stride) on the copy stream; async: leave them pending
-void issue_fills(CompatLayer *L, int stride, bool async) {
-    if (!L->have_pool || g.h_list[0] <= 0) return;
-    if (moe_fill_slots_host(g.h_list, stride, L->E, L->cap, L->nt, L->src, L->dst, L->row_bytes, g.copy) != 0)
+// fills of a host list {count, eids[stride], slots[stride]} on the copy stream; async: leave
+// them pending. With accounting on, their bytes count as the token's read bytes (the
+// reference's g_tok_pread_bytes).
+void issue_fills(CompatLayer *L, const int32_t *list, int stride, bool async) {
+    if (!L->have_pool || list[0] <= 0) return;
+    if (moe_fill_slots_host(list, stride, L->E, L->cap, L->nt, L->src, L->dst, L->row_bytes, g.copy) != 0)
         return;
+    if (g.acct.enabled) {
+        uint64_t eb = 0;
+        for (int t = 0; t < L->nt; ++t) eb += L->row_bytes[t];
+        g.tok_fill_bytes += (uint64_t)list[0] * eb;
+    }
     cudaEventRecord(g.fills, g.copy);
     g.fills_pending = true;
     if (!async) wait_fills();
 }
+
+void issue_fills(CompatLayer *L, int stride, bool async) { issue_fills(L, g.h_list, stride, async); }
 
 int layer_init(int li, int E, int cap, uint64_t expert_bytes, int nt, const uint64_t *row_bytes,
                const uint64_t *base_ptrs, const uint64_t *host_ptrs, uint64_t slot_inds_ptr) {
@@ -137,6 +200,11 @@ int layer_init(int li, int E, int cap, uint64_t expert_bytes, int nt, const uint
     if (int rc = moe_lru_init(L.state, E, cap, expert_bytes, g.st)) return rc;
     if (!ok(cudaStreamSynchronize(g.st))) return moe_set_error(MOE_ECUDA, "c_layer_init: sync");
     L.init = true;
+    if (li == 1) {    // the reference's init resets the cache, and layer 1's reset the token count
+        g.token_step = 0;
+        g.acct.cur_token = -1;
+        push_acct(false);
+    }
     return MOE_OK;
 }
 
@@ -187,6 +255,11 @@ void c_layer_reset_cache(int layer_idx) {
     wait_fills();
     moe_lru_reset(L->state, L->E, L->cap, 0, g.st);
     cudaStreamSynchronize(g.st);
+    if (layer_idx == 1) {    // cpp/third_party/expert_io.c:570-573: layer 1 restarts the token count
+        g.token_step = 0;
+        g.acct.cur_token = -1;
+        push_acct(false);
+    }
 }
 
 void c_layer_reset_stats(int layer_idx) {
@@ -217,8 +290,8 @@ void c_layer_start_prefetch(int layer_idx, const int32_t *pred_eids, int pred_co
     const int mf = (max_fetch > 0 && max_fetch < 32) ? max_fetch : 32;
     if (pred_count > 0) std::memcpy(g.h_eids, pred_eids, (size_t)pred_count * 4);
     cudaMemcpyAsync(g.d_eids, g.h_eids, (size_t)pred_count * 4, cudaMemcpyHostToDevice, g.st);
-    if (moe_lru_prefetch(L->state, L->E, L->cap, reinterpret_cast<const int32_t *>(g.d_eids), pred_count, mf,
-                         g.d_list, g.st) != 0)
+    if (moe_lru_prefetch_ex(L->state, L->E, L->cap, reinterpret_cast<const int32_t *>(g.d_eids), pred_count, mf,
+                            g.d_list, g.d_acct, 0, g.st) != 0)
         return;
     cudaMemcpyAsync(g.h_list, g.d_list, (size_t)(1 + 2 * mf) * 4, cudaMemcpyDeviceToHost, g.st);
     cudaStreamSynchronize(g.st);
@@ -233,7 +306,7 @@ int c_layer_step_decode_ex(int layer_idx, const uint32_t *eids, int k, int async
     std::memcpy(g.h_eids, eids, (size_t)k * 4);
     cudaMemcpyAsync(g.d_eids, g.h_eids, (size_t)k * 4, cudaMemcpyHostToDevice, g.st);
     uint32_t *out = (L->slot_inds && L->slots_on_device) ? L->slot_inds : g.d_slots;
-    if (moe_lru_step(L->state, L->E, L->cap, g.d_eids, k, out, g.d_list, g.st) != 0) return 0;
+    if (moe_lru_step_ex(L->state, L->E, L->cap, g.d_eids, k, out, g.d_list, g.d_acct, 0, g.st) != 0) return 0;
     cudaMemcpyAsync(g.h_list, g.d_list, (size_t)(1 + 2 * k) * 4, cudaMemcpyDeviceToHost, g.st);
     if (L->slot_inds && !L->slots_on_device)
         cudaMemcpyAsync(g.h_slots, g.d_slots, (size_t)k * 4, cudaMemcpyDeviceToHost, g.st);
@@ -371,6 +444,135 @@ void c_get_decode_totals(int num_layers, uint64_t *out6) {
     out6[3] = req;
     out6[4] = dem_b;
     out6[5] = pref_b;
+}
+
+// cpp/third_party/expert_io.c:1002-1008
+void c_set_io_accounting(int enabled) {
+    std::lock_guard<std::mutex> lk(g.mu);
+    if (!ensure_io()) return;
+    wait_fills();
+    g.acct.enabled = enabled ? 1 : 0;
+    if (!g.acct.enabled) g.acct.cur_token = -1;
+    push_acct(false);
+}
+
+// cpp/third_party/expert_io.c:1010-1024: the token index argument is not used; tokens are
+// numbered by a counter that resetting layer 1's cache restarts
+void c_begin_decode_token(int token_idx) {
+    (void)token_idx;
+    std::lock_guard<std::mutex> lk(g.mu);
+    if (!ensure_io()) return;
+    wait_fills();
+    g.acct.cur_token = g.token_step++;
+    g.tok_fill_bytes = 0;
+    push_acct(true);
+}
+
+// cpp/third_party/expert_io.c:1026-1038: {LRU hits, demand misses, prefetch loads, prefetch
+// hits, wasted prefetches, demand re-reads <=16 / <=64 tokens, prefetch re-reads <=16 / <=64,
+// bytes read}; the bytes are those of the slot fills issued while accounting was on
+void c_end_decode_token(uint64_t *out10) {
+    std::lock_guard<std::mutex> lk(g.mu);
+    if (!out10) return;
+    std::memset(out10, 0, 10 * sizeof(uint64_t));
+    if (!g.io) return;
+    wait_fills();
+    cudaMemcpyAsync(g.h_acct, g.d_acct, g.acct_bytes, cudaMemcpyDeviceToHost, g.st);
+    if (!ok(cudaStreamSynchronize(g.st))) return;
+    std::memcpy(out10, g.h_acct + sizeof(AcctHeader), 9 * sizeof(uint64_t));
+    out10[9] = g.tok_fill_bytes;
+}
+
+// cpp/third_party/expert_io.c:1040-1042 reports the bytes of the module's static tables; here
+// the module's own allocations: every layer's device LRU state plus the staging buffers
+uint64_t c_get_native_buffer_bytes(void) {
+    std::lock_guard<std::mutex> lk(g.mu);
+    if (!g.io) return 0;
+    uint64_t b = 2ull * (kEidsMax * 4 + kListMax * 4 + 2 * 2048 * 4 + 64 * 4 + 18 * 8) + 2ull * g.acct_bytes;
+    for (int i = 0; i < kMaxLayers; ++i)
+        if (g.L[i].init) b += moe_lru_state_bytes(g.L[i].E, g.L[i].cap);
+    return b;
+}
+
+// cpp/third_party/expert_io.c:1062-1082
+void c_layer_get_split_inds(int layer_idx, uint32_t *out_hit_slots, uint32_t *out_miss_slots,
+                            int32_t *out_inv_order) {
+    std::lock_guard<std::mutex> lk(g.mu);
+    if (layer_idx < 0 || layer_idx >= kMaxLayers) return;
+    const SplitRecord &r = g.split[layer_idx];
+    if (r.hit > 0 && out_hit_slots) std::memcpy(out_hit_slots, r.hit_slots, (size_t)r.hit * 4);
+    if (r.miss > 0 && out_miss_slots) std::memcpy(out_miss_slots, r.miss_slots, (size_t)r.miss * 4);
+    if (r.k > 0 && out_inv_order) std::memcpy(out_inv_order, r.inv, (size_t)r.k * 4);
+}
+
+// cpp/third_party/expert_io.c:1094-1396. One call per layer: the demand step of `layer_idx`
+// (k capped at 16; the experts the layer's last prefetch fetched stay protected), then the
+// next layer's prefetch of `pred` (duplicates fetched once, at most prefetch_cap), both LRU
+// kernels back to back on the library stream with one read-back; demand fills are queued on
+// the copy stream before the prefetch fills. Layer 0 (pinned) takes no demand step. Returns
+// the demand misses of `layer_idx`. flags: 1 wait for every fill before returning, 2 no
+// prefetch, 4 record the hit/miss split for c_layer_get_split_inds.
+int c_layer_decode_step_sched(int layer_idx, const int32_t *eids, int k, const int32_t *pred, int n_pred,
+                              int next_layer, int prefetch_cap, int flags) {
+    std::lock_guard<std::mutex> lk(g.mu);
+    if (!g.io) return 0;
+    wait_fills();
+    CompatLayer *L = (layer_idx > 0) ? layer(layer_idx) : nullptr;
+    const bool demand = L && eids && k > 0;
+    if (demand && k > kSchedK) k = kSchedK;
+    CompatLayer *Ln = (!(flags & kFlagNoPrefetch) && next_layer > 0) ? layer(next_layer) : nullptr;
+    const bool pref = Ln && pred && n_pred > 0 && n_pred <= 64 && prefetch_cap > 0;
+    const int mf = (prefetch_cap > 0 && prefetch_cap < 32) ? prefetch_cap : 32;
+    uint32_t *out = nullptr;
+    if (demand) {
+        std::memcpy(g.h_eids, eids, (size_t)k * 4);
+        out = (L->slot_inds && L->slots_on_device) ? L->slot_inds : g.d_slots;
+    }
+    if (pref) std::memcpy(reinterpret_cast<int32_t *>(g.h_eids) + 16, pred, (size_t)n_pred * 4);
+    if (!demand && !pref) return 0;
+    cudaMemcpyAsync(g.d_eids, g.h_eids, (size_t)(16 + (pref ? n_pred : 0)) * 4, cudaMemcpyHostToDevice, g.st);
+    if (demand && moe_lru_step_ex(L->state, L->E, L->cap, g.d_eids, k, out, g.d_list, g.d_acct, 1, g.st) != 0)
+        return 0;
+    if (pref && moe_lru_prefetch_ex(Ln->state, Ln->E, Ln->cap, reinterpret_cast<const int32_t *>(g.d_eids) + 16,
+                                    n_pred, mf, g.d_list + kPrefList, g.d_acct, 1, g.st) != 0)
+        return 0;
+    if (demand) {
+        cudaMemcpyAsync(g.h_list, g.d_list, (size_t)(1 + 3 * k) * 4, cudaMemcpyDeviceToHost, g.st);
+        if (out != L->slot_inds || (flags & kFlagSplit))
+            cudaMemcpyAsync(g.h_slots, out, (size_t)k * 4, cudaMemcpyDeviceToHost, g.st);
+    }
+    if (pref)
+        cudaMemcpyAsync(g.h_list + kPrefList, g.d_list + kPrefList, (size_t)(1 + 2 * mf) * 4, cudaMemcpyDeviceToHost,
+                        g.st);
+    if (!ok(cudaStreamSynchronize(g.st))) return 0;
+    int n_missing = 0;
+    if (demand) {
+        n_missing = g.h_list[0];
+        if (n_missing < 0) return 0;
+        if (L->slot_inds && !L->slots_on_device) std::memcpy(L->slot_inds, g.h_slots, (size_t)k * 4);
+        if ((flags & kFlagSplit) && n_missing > 0 && n_missing < k) {   // expert_io.c:1256-1275
+            const int32_t *hit = g.h_list + 1 + 2 * k;
+            SplitRecord &r = g.split[layer_idx];
+            int nh = 0, nm = 0;
+            const int n_hit = k - n_missing;
+            for (int i = 0; i < k; ++i) {
+                if (hit[i]) {
+                    r.hit_slots[nh] = g.h_slots[i];
+                    r.inv[i] = nh++;
+                } else {
+                    r.miss_slots[nm] = g.h_slots[i];
+                    r.inv[i] = n_hit + nm++;
+                }
+            }
+            r.hit = n_hit;
+            r.miss = n_missing;
+            r.k = k;
+        }
+        issue_fills(L, g.h_list, k, true);
+    }
+    if (pref) issue_fills(Ln, g.h_list + kPrefList, mf, true);
+    if ((flags & kFlagSyncDemand) || n_missing == 0) wait_fills();
+    return n_missing;
 }
 
 }  // extern "C"

@@ -13,7 +13,13 @@
 //
 // Device state of one layer (moe_lru_state_bytes): a header, then int16 tables and u64
 // bitmaps sized by E and cap, then 18 u64 counters in the order of c_layer_get_stats
-// (expert_io.c:791-812).
+// (expert_io.c:791-812), then each expert's last eviction token (the newer reference's
+// per-token I/O accounting, cpp/third_party/expert_io.c:91-112, 504-520).
+//
+// Per-token accounting (optional, off unless an LruAcct is passed): the decode token in
+// progress and nine counters -- LRU hits, demand misses, prefetch loads, prefetch hits,
+// wasted prefetches, demand and prefetch re-reads of experts evicted at most 16 / 64 tokens
+// earlier -- shared by every layer of a process, as the reference keeps them.
 #include <algorithm>
 
 #include "common.cuh"
@@ -31,7 +37,7 @@ struct LruHeader {
 };
 
 struct LruLayout {
-    size_t e2s, s2e, prev, next, freel, pre, pred, fet, stats, total;
+    size_t e2s, s2e, prev, next, freel, pre, pred, fet, stats, last_ev, total;
     MOE_HD LruLayout(int E, int cap) {
         const size_t nb = (size_t)(E + 63) / 64;
         e2s = sizeof(LruHeader);
@@ -43,8 +49,19 @@ struct LruLayout {
         pred = pre + nb * 8;
         fet = pred + nb * 8;
         stats = fet + nb * 8;
-        total = al16(stats + 18 * 8);
+        last_ev = al16(stats + 18 * 8);
+        total = al16(last_ev + (size_t)E * 4);
     }
+};
+
+// the per-token accounting shared by every layer (moe_lru_acct_bytes)
+enum AcctCounter {
+    kTokLruHits = 0, kTokDemandMisses, kTokPrefLoads, kTokPrefHits, kTokWasted, kTokDemRe16, kTokDemRe64,
+    kTokPrefRe16, kTokPrefRe64, kTokCounters
+};
+struct LruAcct {
+    int32_t enabled, cur_token, pad0, pad1;   // cur_token < 0: no token in progress
+    uint64_t c[kTokCounters];
 };
 
 enum Stat {
@@ -59,7 +76,25 @@ struct Lru {
     LruHeader *h;
     int16_t *e2s, *s2e, *prev, *next, *freel;
     uint64_t *pre, *pred, *fet, *stats;
+    int32_t *last_ev;
+    LruAcct *acct;                       // null or accounting off: nothing recorded
     int nb;
+
+    MOE_D bool accounting() const { return acct && acct->enabled && acct->cur_token >= 0; }
+    MOE_D void evicted(int eid) {
+        if (accounting()) last_ev[eid] = acct->cur_token;
+    }
+    // an expert read again: count it against the token it was evicted at
+    MOE_D void reread(int eid, int c16, int c64) {
+        if (!accounting()) return;
+        const int ev = last_ev[eid];
+        if (ev >= 0 && acct->cur_token >= ev) {
+            const int dist = acct->cur_token - ev;
+            if (dist <= 16) ++acct->c[c16];
+            if (dist <= 64) ++acct->c[c64];
+        }
+        last_ev[eid] = -1;
+    }
 
     MOE_D void bind(unsigned char *base, int E, int cap) {
         const LruLayout Ly(E, cap);
@@ -73,6 +108,8 @@ struct Lru {
         pred = reinterpret_cast<uint64_t *>(base + Ly.pred);
         fet = reinterpret_cast<uint64_t *>(base + Ly.fet);
         stats = reinterpret_cast<uint64_t *>(base + Ly.stats);
+        last_ev = reinterpret_cast<int32_t *>(base + Ly.last_ev);
+        acct = nullptr;
         nb = (E + 63) / 64;
     }
 
@@ -104,7 +141,11 @@ struct Lru {
         append_mru(s);
     }
     MOE_D static bool has(const uint64_t *bm, int e) { return (bm[e >> 6] >> (e & 63)) & 1ull; }
-    MOE_D int alloc(const uint64_t *prot) {
+    // keep: experts that must stay resident even when every resident expert is protected (the
+    // scheduled step's own experts, which also protects prefetched ones; with k + fetched > cap
+    // the reference's oldest-goes fallback can evict one of the step's experts and then indexes
+    // its tables with -1 -- here the oldest expert outside `keep` goes instead)
+    MOE_D int alloc(const uint64_t *prot, const uint64_t *keep = nullptr) {
         if (h->free_count > 0) return freel[--h->free_count];
         for (int cur = h->head; cur >= 0; cur = next[cur]) {
             const int eid = s2e[cur];
@@ -112,13 +153,23 @@ struct Lru {
                 remove(cur);
                 e2s[eid] = -1;
                 s2e[cur] = -1;
+                evicted(eid);
                 return cur;
             }
         }
-        const int victim = h->head;             // every resident expert is protected: the oldest goes
+        int victim = h->head;                   // every resident expert is protected: the oldest goes
+        if (keep)
+            for (int cur = h->head; cur >= 0; cur = next[cur])
+                if (s2e[cur] < 0 || !has(keep, s2e[cur])) {
+                    victim = cur;
+                    break;
+                }
         const int eid = s2e[victim];
         remove(victim);
-        if (eid >= 0) e2s[eid] = -1;
+        if (eid >= 0) {
+            e2s[eid] = -1;
+            evicted(eid);
+        }
         s2e[victim] = -1;
         return victim;
     }
@@ -158,7 +209,10 @@ MOE_D void copy16(void *dst, const void *src, size_t bytes) {
     for (size_t i = threadIdx.x; i < bytes / 16; i += blockDim.x) d[i] = s[i];
 }
 
-enum Op { kOpReset = 0, kOpResetStats, kOpStep, kOpPrefetch, kOpGetState, kOpSetState, kOpStats, kOpAddStat };
+enum Op {
+    kOpReset = 0, kOpResetStats, kOpStep, kOpPrefetch, kOpGetState, kOpSetState, kOpStats, kOpAddStat,
+    kOpStepSched, kOpPrefetchSched
+};
 
 struct LruArgs {
     unsigned char *state;
@@ -173,6 +227,7 @@ struct LruArgs {
                                // get: [1 + 2*cap] {count, eids (LRU->MRU).., slots..}
     uint64_t *out_stats;       // stats: [18]
     uint64_t add_req, add_hits, add_misses;
+    LruAcct *acct;             // per-token accounting shared by all layers, or null
 };
 
 __global__ void __launch_bounds__(kLruThreads) lru_kernel(LruArgs a) {
@@ -182,7 +237,8 @@ __global__ void __launch_bounds__(kLruThreads) lru_kernel(LruArgs a) {
     __syncthreads();
     Lru L;
     L.bind(sm, a.E, a.cap);
-    if (a.op == kOpPrefetch) {
+    L.acct = a.acct;
+    if (a.op == kOpPrefetch || a.op == kOpPrefetchSched) {
         // the residency snapshot of expert_io.c:536-541 by every warp at once: 32 experts per
         // ballot, one 32-bit half of a bitmap word per warp step (words past E come out zero)
         const int lane = threadIdx.x & 31;
@@ -199,20 +255,23 @@ __global__ void __launch_bounds__(kLruThreads) lru_kernel(LruArgs a) {
         LruHeader *h = L.h;
         const int E = a.E;
         switch (a.op) {
-            case kOpReset: {     // expert_io.c:450-468
+            case kOpReset: {     // expert_io.c:450-468 (+ cpp/third_party/expert_io.c:560)
                 L.reset_tables();
                 h->free_count = h->cap;
                 for (int i = 0; i < h->cap; ++i) L.freel[i] = (int16_t)(h->cap - 1 - i);
+                for (int i = 0; i < E; ++i) L.last_ev[i] = -1;
                 break;
             }
             case kOpResetStats: {   // expert_io.c:470-495
                 for (int i = 0; i < 18; ++i) L.stats[i] = 0;
                 break;
             }
-            case kOpStep: {      // expert_io.c:583-676
+            case kOpStep:        // expert_io.c:583-676 (+ accounting, cpp/third_party/expert_io.c:745-806)
+            case kOpStepSched: { // cpp/third_party/expert_io.c:1129-1270 (the step half of decode_step_sched)
+                const bool sched = a.op == kOpStepSched;
                 const int k = a.n;
                 L.stats[kDecReq] += (uint64_t)k;
-                uint64_t act[kLruMaxE / 64];
+                uint64_t act[kLruMaxE / 64], prot[kLruMaxE / 64];
                 for (int b = 0; b < L.nb; ++b) act[b] = 0;
                 bool bad = false;
                 for (int i = 0; i < k; ++i) {
@@ -225,7 +284,12 @@ __global__ void __launch_bounds__(kLruThreads) lru_kernel(LruArgs a) {
                     a.out_list[0] = -1;
                     break;
                 }
+                // the scheduled step also protects the experts the last prefetch is bringing in
+                for (int b = 0; b < L.nb; ++b) prot[b] = act[b] | ((sched && h->has_snap) ? L.fet[b] : 0ull);
+                const bool acc = a.acct && a.acct->enabled;
                 int miss_e[kLruMaxK], miss_s[kLruMaxK], nm = 0;
+                uint8_t hit[kLruMaxK];
+                uint64_t tok_lru = 0, tok_pref = 0;
                 if (h->has_snap) {
                     uint64_t ov = 0, ta = 0, tp = 0, mh = 0, tam = 0, tf = 0;
                     for (int b = 0; b < L.nb; ++b) {
@@ -245,28 +309,42 @@ __global__ void __launch_bounds__(kLruThreads) lru_kernel(LruArgs a) {
                     L.stats[kMissPrefFetched] += tf;
                     for (int i = 0; i < k; ++i) {
                         const int e = (int)a.eids[i];
-                        if (L.e2s[e] >= 0) {
-                            if (Lru::has(L.pre, e)) ++L.stats[kDecLruHits];
-                            else ++L.stats[kDecPrefHits];
+                        hit[i] = L.e2s[e] >= 0;
+                        if (hit[i]) {
+                            if (Lru::has(L.pre, e)) { ++L.stats[kDecLruHits]; ++tok_lru; }
+                            else { ++L.stats[kDecPrefHits]; ++tok_pref; }
                         } else {
                             ++L.stats[kDecMiss];
                             miss_e[nm++] = e;
                         }
+                    }
+                    if (acc) {
+                        a.acct->c[kTokLruHits] += tok_lru;
+                        a.acct->c[kTokPrefHits] += tok_pref;
+                        if (tf >= tok_pref) a.acct->c[kTokWasted] += tf - tok_pref;
+                        a.acct->c[kTokDemandMisses] += (uint64_t)nm;
                     }
                     h->has_snap = 0;
                 } else {
                     for (int i = 0; i < k; ++i) {
                         const int e = (int)a.eids[i];
-                        if (L.e2s[e] >= 0) {
+                        hit[i] = L.e2s[e] >= 0;
+                        if (hit[i]) {
                             ++L.stats[kDecLruHits];
+                            ++tok_lru;
                         } else {
                             ++L.stats[kDecMiss];
                             miss_e[nm++] = e;
                         }
                     }
+                    if (acc) {
+                        a.acct->c[kTokLruHits] += tok_lru;
+                        a.acct->c[kTokDemandMisses] += (uint64_t)nm;
+                    }
                 }
                 for (int i = 0; i < nm; ++i) {
-                    const int s = L.alloc(act);
+                    const int s = L.alloc(prot, sched ? act : nullptr);
+                    L.reread(miss_e[i], kTokDemRe16, kTokDemRe64);
                     L.insert(miss_e[i], s);
                     miss_s[i] = s;
                 }
@@ -282,9 +360,13 @@ __global__ void __launch_bounds__(kLruThreads) lru_kernel(LruArgs a) {
                     a.out_list[1 + i] = miss_e[i];
                     a.out_list[1 + k + i] = miss_s[i];
                 }
+                if (sched)
+                    for (int i = 0; i < k; ++i) a.out_list[1 + 2 * k + i] = hit[i];
                 break;
             }
-            case kOpPrefetch: {  // expert_io.c:527-581 (L.pre: the snapshot taken above)
+            case kOpPrefetch:    // expert_io.c:527-581 (L.pre: the snapshot taken above; + accounting)
+            case kOpPrefetchSched: {   // cpp/third_party/expert_io.c:1290-1340: duplicates counted once
+                const bool sched = a.op == kOpPrefetchSched;
                 for (int b = 0; b < L.nb; ++b) {
                     L.pred[b] = 0;
                     L.fet[b] = 0;
@@ -299,7 +381,7 @@ __global__ void __launch_bounds__(kLruThreads) lru_kernel(LruArgs a) {
                     if (e < 0 || e >= E) continue;
                     L.pred[e >> 6] |= 1ull << (e & 63);
                     prot[e >> 6] |= 1ull << (e & 63);
-                    if (L.e2s[e] < 0 && nm < cap_fetch) {
+                    if (L.e2s[e] < 0 && nm < cap_fetch && !(sched && Lru::has(L.fet, e))) {
                         miss[nm++] = e;
                         L.fet[e >> 6] |= 1ull << (e & 63);
                     }
@@ -309,10 +391,12 @@ __global__ void __launch_bounds__(kLruThreads) lru_kernel(LruArgs a) {
                 for (int i = 0; i < nm; ++i) {      // reverse rank order: the best prediction is newest
                     const int e = miss[nm - 1 - i];
                     const int s = L.alloc(prot);
+                    L.reread(e, kTokPrefRe16, kTokPrefRe64);
                     L.insert(e, s);
                     a.out_list[1 + i] = e;
                     a.out_list[1 + a.max_fetch + i] = s;
                 }
+                if (a.acct && a.acct->enabled) a.acct->c[kTokPrefLoads] += (uint64_t)nm;
                 L.stats[kDecPrefBytes] += (uint64_t)nm * h->expert_bytes;
                 break;
             }
@@ -340,6 +424,7 @@ __global__ void __launch_bounds__(kLruThreads) lru_kernel(LruArgs a) {
                     if (e < 0 || e >= E || s < 0 || s >= h->cap) { bad = true; break; }
                     used[s] = 1;
                     L.insert(e, s);
+                    L.last_ev[e] = -1;
                 }
                 if (bad) atomicOr(&g_moe_device_error, MOE_DEVERR_BAD_INPUT);
                 h->free_count = 0;
@@ -422,8 +507,10 @@ extern "C" int moe_lru_reset(void *state, int E, int cap, int what, void *stream
     return lru_launch(a, stream);
 }
 
-extern "C" int moe_lru_step(void *state, int E, int cap, const uint32_t *eids, int k, uint32_t *out_slots,
-                            int32_t *out_miss, void *stream) {
+extern "C" size_t moe_lru_acct_bytes(void) { return sizeof(LruAcct); }
+
+extern "C" int moe_lru_step_ex(void *state, int E, int cap, const uint32_t *eids, int k, uint32_t *out_slots,
+                               int32_t *out_miss, void *acct, int sched, void *stream) {
     if (int rc = check_dims(E, cap)) return rc;
     if (k <= 0 || k > kLruMaxK || k > cap || !eids || !out_slots || !out_miss)
         return moe_set_error(MOE_EINVAL, "lru_step: bad arguments (k=%d cap=%d)", k, cap);
@@ -431,16 +518,22 @@ extern "C" int moe_lru_step(void *state, int E, int cap, const uint32_t *eids, i
     a.state = static_cast<unsigned char *>(state);
     a.E = E;
     a.cap = cap;
-    a.op = kOpStep;
+    a.op = sched ? kOpStepSched : kOpStep;
     a.eids = eids;
     a.n = k;
     a.out_slots = out_slots;
     a.out_list = out_miss;
+    a.acct = static_cast<LruAcct *>(acct);
     return lru_launch(a, stream);
 }
 
-extern "C" int moe_lru_prefetch(void *state, int E, int cap, const int32_t *pred, int n, int max_fetch,
-                                int32_t *out_fetch, void *stream) {
+extern "C" int moe_lru_step(void *state, int E, int cap, const uint32_t *eids, int k, uint32_t *out_slots,
+                            int32_t *out_miss, void *stream) {
+    return moe_lru_step_ex(state, E, cap, eids, k, out_slots, out_miss, nullptr, 0, stream);
+}
+
+extern "C" int moe_lru_prefetch_ex(void *state, int E, int cap, const int32_t *pred, int n, int max_fetch,
+                                   int32_t *out_fetch, void *acct, int sched, void *stream) {
     if (int rc = check_dims(E, cap)) return rc;
     if (n < 0 || n > kLruMaxPred || (n > 0 && !pred) || !out_fetch || max_fetch <= 0 || max_fetch > 32)
         return moe_set_error(MOE_EINVAL, "lru_prefetch: bad arguments (n=%d max_fetch=%d)", n, max_fetch);
@@ -448,12 +541,18 @@ extern "C" int moe_lru_prefetch(void *state, int E, int cap, const int32_t *pred
     a.state = static_cast<unsigned char *>(state);
     a.E = E;
     a.cap = cap;
-    a.op = kOpPrefetch;
+    a.op = sched ? kOpPrefetchSched : kOpPrefetch;
     a.eids = reinterpret_cast<const uint32_t *>(pred);
     a.n = n;
     a.max_fetch = max_fetch;
     a.out_list = out_fetch;
+    a.acct = static_cast<LruAcct *>(acct);
     return lru_launch(a, stream);
+}
+
+extern "C" int moe_lru_prefetch(void *state, int E, int cap, const int32_t *pred, int n, int max_fetch,
+                                int32_t *out_fetch, void *stream) {
+    return moe_lru_prefetch_ex(state, E, cap, pred, n, max_fetch, out_fetch, nullptr, 0, stream);
 }
 
 extern "C" int moe_lru_get_state(void *state, int E, int cap, int32_t *out, void *stream) {
