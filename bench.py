@@ -59,6 +59,8 @@ def parse():
     ap.add_argument("--ep-mode", choices=["auto", "sharded", "replicated"], default="auto",
                     help="c4: tokens sharded (routed all-to-all) or replicated on every rank; auto: sharded "
                          "from 4 tokens per GPU")
+    ap.add_argument("--prefetch-ctas", type=int, default=32,
+                    help="c2: CTAs of each prefetch fill kernel (0 = one per SM)")
     ap.add_argument("--layers", type=int, default=0,
                     help="profiling aid: run only the first N layers of the stack (0 = all 28)")
     return ap.parse_args()
@@ -571,6 +573,8 @@ def run_c2(args, rank: int, world: int, local_rank: int) -> None:
                                     expert_bytes=cfg.expert_bytes)
     stack = OffloadStack(routers, layer0, pools, caps, cfg.top_k, dev, prefetch=True, prefetch_top_m=12,
                          prefetch_cap=3, expert_bytes=cfg.expert_bytes)
+    for c in stack.layers[1:]:
+        c.prefetch_ctas = args.prefetch_ctas
     T = args.warmup + args.steps
     routing, bias = zipf_routing(seed=cfg.seed, layers=L, tokens=T, E=cfg.experts, K=cfg.top_k)
     # prefetch driven by a predictor of the reference's measured recall@10 (83.6 %)
@@ -613,7 +617,8 @@ def run_c2(args, rank: int, world: int, local_rank: int) -> None:
                        "routing": "Zipf(1.1) per layer + 30 % reuse, injected; router runs",
                        "prefetch": f"top-12 ranked predictions of recall@10 {PRED_RECALL} (the reference's "
                                    "measured predictor recall; offload.synthetic_predictions), cap 3; the "
-                                   "router's own next-layer prediction still runs"},
+                                   "router's own next-layer prediction still runs",
+                       "prefetch_fill_ctas": args.prefetch_ctas},
             "cache": {"lru_hit_rate": round(tot["decode_lru_hits"] / req, 4),
                       "prefetch_hit_rate": round(tot["decode_prefetch_hits"] / req, 4),
                       "effective_hit_rate": round((tot["decode_lru_hits"] + tot["decode_prefetch_hits"]) / req, 4),

@@ -118,14 +118,29 @@ class HostExpertPool:
 
 
 class CachedSwitchGLU:
-    """LRU-cached routed experts of one layer (reference CachedSwitchGLU, loader.py:306-748)."""
+    """LRU-cached routed experts of one layer (reference CachedSwitchGLU, loader.py:306-748).
 
-    def __init__(self, layer_idx: int, capacity: int, pool: HostExpertPool, device, top_k: int,
-                 expert_bytes: int | None = None, prefetch_stream: torch.cuda.Stream | None = None):
+    CachedSwitchGLU(shard_path, layer_idx, capacity) as in the reference (loader.py:311): the
+    layer's nine expert tensors are read from the experts-XX.safetensors shard at shard_path
+    into a pinned host pool (checkpoint.load_expert_pool) and `capacity` slots are allocated
+    in HBM. Keywords: pool (an already loaded HostExpertPool; shard_path may then be None),
+    device (default: the current CUDA device), top_k (default 10, the reference's TOP_K),
+    group_size, expert_bytes (the byte-counter unit; default the pool's expert size) and
+    prefetch_stream."""
+
+    def __init__(self, shard_path, layer_idx: int, capacity: int, *, pool: HostExpertPool | None = None,
+                 device=None, top_k: int = 10, group_size: int = 64, expert_bytes: int | None = None,
+                 prefetch_stream: torch.cuda.Stream | None = None):
+        if pool is None:
+            if shard_path is None:
+                raise ValueError("CachedSwitchGLU needs a shard path or a pool")
+            from . import checkpoint
+            pool = checkpoint.load_expert_pool(shard_path, layer_idx, group_size)
+        self.shard_path = shard_path
         self.layer_idx = layer_idx
         self.capacity = int(capacity)
         self.pool = pool
-        self.device = torch.device(device)
+        self.device = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
         self.E = pool.E
         self.K = top_k
         if not (0 < top_k <= self.capacity <= self.E):
@@ -148,6 +163,9 @@ class CachedSwitchGLU:
         self.pstream = prefetch_stream or torch.cuda.Stream(device=self.device)
         self._pevent = torch.cuda.Event()
         self._pending = False
+        # CTAs of the prefetch fill kernel (0: one per SM). A few dozen keep the host link
+        # saturated and leave the SMs to the expert kernels the fill overlaps.
+        self.prefetch_ctas = 0
         self._act = torch.empty((1, top_k, self.gate.w.shape[1]), dtype=torch.bfloat16, device=self.device)
         call("moe_lru_init", self.state.data_ptr(), self.E, self.capacity, self.expert_bytes, self._cs())
 
@@ -228,7 +246,7 @@ class CachedSwitchGLU:
         call("moe_lru_prefetch", self.state.data_ptr(), self.E, self.capacity, pred.data_ptr(), n, max_fetch,
              self._pref.data_ptr(), ps)
         call("moe_fill_slots", self._pref.data_ptr(), max_fetch, self.E, self.capacity, 9, self._src, self._dst,
-             self._rows, 0, ps)
+             self._rows, self.prefetch_ctas, ps)
         self._pevent.record(self.pstream)
         self._pending = True
 
@@ -260,12 +278,18 @@ class CachedSwitchGLU:
         return yk.view(1, 1, K, -1)
 
     def forward_combined(self, x: torch.Tensor, indices: torch.Tensor, scores: torch.Tensor, *,
-                         resid=None, y=None) -> torch.Tensor:
-        """The hook's fused form: sum_k scores_k * expert_k(x) (+ resid), x [1, H]."""
-        slots = self.step(indices)
+                         addend=None, resid=None, y=None) -> torch.Tensor:
+        """The hook's fused form: sum_k scores_k * expert_k(x) (+ addend, e.g. the shared
+        expert's output) (+ resid), x [1, H]."""
+        return self.combine_slots(x, self.step(indices), scores, addend=addend, resid=resid, y=y)
+
+    def combine_slots(self, x: torch.Tensor, slots: torch.Tensor, scores: torch.Tensor, *,
+                      addend=None, resid=None, y=None) -> torch.Tensor:
+        """forward_combined after its LRU step: the experts on the given slot ids."""
         K = self.K
         act = ops.experts_gateup(x, slots.view(1, K), self.gate, self.up, act=self._act)
-        out, _ = ops.experts_down(act, slots.view(1, K), self.down, scores.view(1, K), resid=resid, y=y)
+        out, _ = ops.experts_down(act, slots.view(1, K), self.down, scores.view(1, K), addend=addend, resid=resid,
+                                  y=y)
         return out
 
     # ---------------------------------------------------------------- prefill
@@ -377,8 +401,9 @@ class OffloadStack:
         self.H = routers[0].shape[1]
         self.E = routers[0].shape[0]
         ps = torch.cuda.Stream(device=self.device)
-        self.layers = [None] + [CachedSwitchGLU(l, capacities[l], pools[l - 1], self.device, top_k, expert_bytes,
-                                                prefetch_stream=ps) for l in range(1, self.L)]
+        self.layers = [None] + [CachedSwitchGLU(None, l, capacities[l], pool=pools[l - 1], device=self.device,
+                                                top_k=top_k, expert_bytes=expert_bytes, prefetch_stream=ps)
+                                for l in range(1, self.L)]
         self.capacities = capacities
         self.hs = [torch.empty((1, self.H), dtype=torch.bfloat16, device=self.device) for _ in range(self.L + 1)]
         self.xn = [torch.empty((1, self.H), dtype=torch.bfloat16, device=self.device) for _ in range(self.L)]
@@ -412,14 +437,19 @@ class OffloadStack:
             r = ops.router_topk(xin, self.routers[l], self.K, w_next=nxt, M=self.M if nxt is not None else 0,
                                 pred_bias=pb, out=self.r_out[l])
             eids = inject[l].view(1, self.K) if inject is not None else r["inds"]
+            # The cache calls keep the reference's order (layer l's step, then layer l+1's
+            # prefetch); layer l's expert kernels are issued after both, so the next layer's
+            # prefetch fill crosses the host link while they run. The two calls touch different
+            # layers' caches, so every LRU state sequence is the reference's.
+            slots = eids if l == 0 else self.layers[l].step(eids)
+            if nxt is not None:
+                pred = pred_inject[l] if pred_inject is not None else r["pred"].view(-1)
+                self.layers[l + 1].start_prefetch(pred, self.prefetch_cap)
             if l == 0:
                 act = ops.experts_gateup(xin, eids, self.layer0.gate, self.layer0.up)
                 ops.experts_down(act, eids, self.layer0.down, r["scores"], resid=x, y=self.hs[l + 1])
             else:
-                self.layers[l].forward_combined(xin, eids, r["scores"], resid=x, y=self.hs[l + 1])
-            if nxt is not None:
-                pred = pred_inject[l] if pred_inject is not None else r["pred"].view(-1)
-                self.layers[l + 1].start_prefetch(pred, self.prefetch_cap)
+                self.layers[l].combine_slots(xin, slots, r["scores"], resid=x, y=self.hs[l + 1])
         return self.hs[self.L]
 
     def prefill(self, h: torch.Tensor) -> torch.Tensor:

@@ -216,7 +216,7 @@ def test_cached_layer_matches_resident_layer(dev):
     g, u, d = np_qmatrix(rng, E, I, H), np_qmatrix(rng, E, I, H), np_qmatrix(rng, E, H, I)
     res = ExpertLayer(np_to_bf16_tensor(np_bf16_normal(rng, (E, H), 0.02), dev), to_device_qmatrix(g, dev),
                       to_device_qmatrix(u, dev), to_device_qmatrix(d, dev))
-    cache = CachedSwitchGLU(1, cap, HostExpertPool.from_layer(res), dev, K)
+    cache = CachedSwitchGLU(None, 1, cap, pool=HostExpertPool.from_layer(res), device=dev, top_k=K)
     hot = rng.permutation(E)[:24]
     for step in range(40):
         x = np_to_bf16_tensor(np_bf16_normal(rng, (1, 1, H)), dev)
