@@ -405,6 +405,29 @@ int moe_ep_a2a_layer(const void *x, int T, int H, int I, int E, int K, const int
                      size_t workspace_bytes, void *stream);
 
 /* ------------------------------------------------------------------------------------ */
+/* K50 expert pack (one directory per layer: codes.bin, scales.bf16, bias.bf16,          */
+/* index.json; replaces ExpertPackCpp, mlx-qwen38/cpp/src/loader.cpp:1187-1470).          */
+/* ------------------------------------------------------------------------------------ */
+
+/* Opens a layer directory and parses its index; NULL on error (moe_last_error()). */
+void *moe_k50_open(const char *layer_dir);
+void moe_k50_close(void *pack);
+/* Number of expert records of a projection ("gate_proj", ...), or of dense records ("dense"). */
+int moe_k50_count(void *pack, const char *proj);
+/* Name of dense record i, NUL-terminated into out. */
+int moe_k50_dense_name(void *pack, int i, char *out, size_t out_bytes);
+/* Record of (proj, expert) -- expert < 0: the dense record named proj -- as out8 = {bits,
+ * group_size, rows, cols, uint32 code words per row, groups per row, kind (0 tern, 1 2t,
+ * 2 "2", 3 "3", 4 "4", 5 "6", 6 "8"), unit (0 hot, 1 warm, 2 mid, 3 cold, 4 dense, -1 other)}
+ * of its materialised form (ExpertPackCpp::materialize_as_affine2, loader.cpp:1379-1470). */
+int moe_k50_record(void *pack, const char *proj, int expert, int64_t *out8);
+/* Materialises the record into host buffers: codes uint32 [rows][words], scales / biases bf16
+ * bits [rows][groups]. "tern": base-3 digits unpacked into 2-bit codes, biases = -scales;
+ * other kinds: codes as stored, biases from bias.bf16 (or -scales when it has none). */
+int moe_k50_materialize(void *pack, const char *proj, int expert, uint32_t *codes, uint16_t *scales,
+                        uint16_t *biases);
+
+/* ------------------------------------------------------------------------------------ */
 /* Per-layer LRU expert-slot cache with its state on the GPU.                             */
 /* ------------------------------------------------------------------------------------ */
 

@@ -18,6 +18,7 @@ SZ = ctypes.c_size_t
 U64 = ctypes.c_uint64
 U32 = ctypes.c_uint32
 I32 = ctypes.c_int32
+CP = ctypes.c_char_p
 
 _lock = threading.Lock()
 _lib = None
@@ -75,6 +76,12 @@ SIGNATURES: dict[str, tuple] = {
     "moe_lru_step": (I, [P, I, I, P, I, P, P, P]),
     "moe_lru_prefetch": (I, [P, I, I, P, I, I, P, P]),
     "moe_lru_acct_bytes": (SZ, []),
+    "moe_k50_open": (P, [CP]),
+    "moe_k50_close": (None, [P]),
+    "moe_k50_count": (I, [P, CP]),
+    "moe_k50_dense_name": (I, [P, I, P, SZ]),
+    "moe_k50_record": (I, [P, CP, I, P]),
+    "moe_k50_materialize": (I, [P, CP, I, P, P, P]),
     "moe_lru_step_ex": (I, [P, I, I, P, I, P, P, P, I, P]),
     "moe_lru_prefetch_ex": (I, [P, I, I, P, I, I, P, P, I, P]),
     "moe_lru_get_state": (I, [P, I, I, P, P]),
