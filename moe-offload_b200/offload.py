@@ -162,7 +162,9 @@ class CachedSwitchGLU:
         self._rows = (ctypes.c_uint64 * 9)(*pool.row_bytes)
         self.pstream = prefetch_stream or torch.cuda.Stream(device=self.device)
         self._pevent = torch.cuda.Event()
+        self._pevent_lru = torch.cuda.Event()
         self._pending = False
+        self._pending_lru = False
         # CTAs of the prefetch fill kernel (0: one per SM). A few dozen keep the host link
         # saturated and leave the SMs to the expert kernels the fill overlaps.
         self.prefetch_ctas = 0
@@ -238,33 +240,52 @@ class CachedSwitchGLU:
     def start_prefetch(self, pred: torch.Tensor, max_fetch: int = 3) -> None:
         """Router-driven prefetch (c_layer_start_prefetch): pred = device int32 [M] ranked
         predictions. The LRU insertion and the fills run on the prefetch stream, after the
-        work that produced `pred` on the current stream."""
+        work that produced `pred` on the current stream. Two events mark its halves: the LRU
+        update (what this layer's next LRU step needs) and the fills (what its next demand
+        fill, which may overwrite a slot being filled, and its expert kernels need)."""
         self.wait_prefetch()
         n = int(pred.numel())
         self.pstream.wait_stream(torch.cuda.current_stream(self.device))
         ps = self.pstream.cuda_stream
         call("moe_lru_prefetch", self.state.data_ptr(), self.E, self.capacity, pred.data_ptr(), n, max_fetch,
              self._pref.data_ptr(), ps)
+        self._pevent_lru.record(self.pstream)
         call("moe_fill_slots", self._pref.data_ptr(), max_fetch, self.E, self.capacity, 9, self._src, self._dst,
              self._rows, self.prefetch_ctas, ps)
         self._pevent.record(self.pstream)
         self._pending = True
+        self._pending_lru = True
 
     def wait_prefetch(self) -> None:
+        """The current stream waits for the whole pending prefetch (LRU update and fills)."""
         if self._pending:
             torch.cuda.current_stream(self.device).wait_event(self._pevent)
             self._pending = False
+            self._pending_lru = False
 
     # ---------------------------------------------------------------- decode
     def step(self, indices: torch.Tensor) -> torch.Tensor:
         """LRU step + demand fill for device int32 indices [.., K]: the slot ids ([1, 1, K])."""
-        self.wait_prefetch()
-        cs = self._cs()
+        slots = self.step_lru(indices)
+        self.fill_demand()
+        return slots
+
+    def step_lru(self, indices: torch.Tensor) -> torch.Tensor:
+        """The LRU step alone (after the pending prefetch's LRU update, not its fills): slot ids
+        into the slot buffer, the miss list for fill_demand."""
+        if self._pending_lru:
+            torch.cuda.current_stream(self.device).wait_event(self._pevent_lru)
+            self._pending_lru = False
         call("moe_lru_step", self.state.data_ptr(), self.E, self.capacity, indices.data_ptr(), self.K,
-             self._slot_inds_buf.data_ptr(), self._miss.data_ptr(), cs)
-        call("moe_fill_slots", self._miss.data_ptr(), self.K, self.E, self.capacity, 9, self._src, self._dst,
-             self._rows, 0, cs)
+             self._slot_inds_buf.data_ptr(), self._miss.data_ptr(), self._cs())
         return self._slot_inds_buf
+
+    def fill_demand(self) -> None:
+        """The fills of the last step_lru's misses, after the pending prefetch's fills (a miss
+        may take a slot a prefetch is still filling; the later write must win)."""
+        self.wait_prefetch()
+        call("moe_fill_slots", self._miss.data_ptr(), self.K, self.E, self.capacity, 9, self._src, self._dst,
+             self._rows, 0, self._cs())
 
     def __call__(self, x: torch.Tensor, indices: torch.Tensor) -> torch.Tensor:
         """x [1, 1, H] bf16, indices [1, 1, K] int32 (device) -> unweighted expert outputs
@@ -438,13 +459,18 @@ class OffloadStack:
                                 pred_bias=pb, out=self.r_out[l])
             eids = inject[l].view(1, self.K) if inject is not None else r["inds"]
             # The cache calls keep the reference's order (layer l's step, then layer l+1's
-            # prefetch); layer l's expert kernels are issued after both, so the next layer's
-            # prefetch fill crosses the host link while they run. The two calls touch different
-            # layers' caches, so every LRU state sequence is the reference's.
-            slots = eids if l == 0 else self.layers[l].step(eids)
+            # prefetch). Layer l+1's prefetch is issued between layer l's LRU step and its
+            # demand fill, so the prefetch's LRU update runs beside the demand fill and its fill
+            # crosses the host link while layer l's expert kernels run; the LRU step itself
+            # waits only for the prefetch's LRU update, the demand fill for its fills. The two
+            # calls touch different layers' caches, so every LRU state sequence is the
+            # reference's.
+            slots = eids if l == 0 else self.layers[l].step_lru(eids)
             if nxt is not None:
                 pred = pred_inject[l] if pred_inject is not None else r["pred"].view(-1)
                 self.layers[l + 1].start_prefetch(pred, self.prefetch_cap)
+            if l > 0:
+                self.layers[l].fill_demand()
             if l == 0:
                 act = ops.experts_gateup(xin, eids, self.layer0.gate, self.layer0.up)
                 ops.experts_down(act, eids, self.layer0.down, r["scores"], resid=x, y=self.hs[l + 1])
