@@ -431,15 +431,18 @@ def run_f3(args, rank: int, world: int, local_rank: int) -> None:
     """The step in front of every MoE block, decode (one token): the hyper-connection mixer
     (run_hc with a write: 4 streams of H = 3072, rank 320, 8-bit g64 down / up / inject) and the
     shared expert on its output (gate / up / down 4-bit g64 with I = 768, an 8-bit scalar gate),
-    for 28 layers with their own weights (347 MB, beyond L2). Five launches per layer, captured
-    as one CUDA graph per step. `value` = tokens/s through the 28 layers; roofline = algorithmic
-    weight bytes per token / step time against the HBM peak (the kernels are latency-bound at one
-    token); e2e adds the pinned host -> device copy of the token's streams and the read-back of
-    the last layer's shared output."""
+    for 28 chained layers with their own weights (347 MB, beyond L2): each layer's mixer writes
+    the previous layer's block output (here the shared expert's) into the streams. The step is
+    ONE launch of moe_f3_stack_decode (all layers, four grid barriers per layer); the same chain
+    as five launches per layer (moe_hc_mix + moe_shared_expert, one CUDA graph) is timed beside
+    it and must give the same bits. `value` = tokens/s through the 28 layers; roofline =
+    algorithmic weight bytes per token / step time against the HBM peak; e2e adds the pinned
+    host -> device copy of the token's streams and the read-back of the last block output."""
     import numpy as np
     import torch
 
     from moe_offload_b200 import ops
+    from moe_offload_b200.hooks import hc_write
     from moe_offload_b200.ops import QMatrix
 
     dev = torch.device("cuda", local_rank)
@@ -461,26 +464,53 @@ def run_f3(args, rank: int, world: int, local_rank: int) -> None:
                        "sg": qm(I, H, 4, 2e-3), "su": qm(I, H, 4, 2e-3), "sd": qm(H, I, 4, 2e-3),
                        "se": qm(1, H, 8, 2e-4)})
     wbytes = sum(m.w.numel() * 4 + m.s.numel() * 4 for lay in layers for m in lay.values() if isinstance(m, QMatrix))
-    h = (torch.randn((1, HC * H), device=dev, generator=g) * 0.3).to(torch.bfloat16)
-    br = (torch.randn((1, H), device=dev, generator=g) * 0.3).to(torch.bfloat16)
-    gt = (torch.randn((1, HC), device=dev, generator=g) * 0.5).to(torch.bfloat16)
-    sh = torch.empty((1, H), dtype=torch.bfloat16, device=dev)
+    h = (torch.randn(HC * H, device=dev, generator=g) * 0.3).to(torch.bfloat16)
+    br = (torch.randn(H, device=dev, generator=g) * 0.3).to(torch.bfloat16)
+    gt = (torch.randn(HC, device=dev, generator=g) * 0.5).to(torch.bfloat16)
     st = torch.cuda.Stream(dev)
+    stack = ops.F3Stack(layers, dev)
+    out = {}
+    chain_out = {}
 
     def step():
+        stack.decode(h, br, gt, out=out, stream=st)
+
+    def step_chain():
+        state, write = h.view(1, -1), (br.view(1, -1), gt.view(1, -1))
         for lay in layers:
-            mixed, _, _ = ops.hc_mix(h, lay["nw"], lay["down"], lay["up"], lay["inj"], write=(br, gt), stream=st)
-            ops.shared_expert(mixed, lay["sg"], lay["su"], lay["sd"], lay["se"], y=sh, stream=st)
+            mixed, written, inj = ops.hc_mix(state, lay["nw"], lay["down"], lay["up"], lay["inj"], write=write,
+                                             stream=st)
+            sh = ops.shared_expert(mixed, lay["sg"], lay["su"], lay["sd"], lay["se"], stream=st)
+            state, write = written, (sh, inj)
+        chain_out["state"] = hc_write(state, write[0], write[1])
+        chain_out["branch"] = write[0]
+
+    def timed(graph, n):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(st)
+        for _ in range(n):
+            graph.replay()
+        e1.record(st)
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / n
 
     with torch.cuda.stream(st):
         step()
+        step_chain()
         torch.cuda.synchronize()
+        gchain = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gchain, stream=st):
+            step_chain()
         graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(graph, stream=st):
             step()
         for _ in range(args.warmup):
+            gchain.replay()
             graph.replay()
         torch.cuda.synchronize()
+        same = bool(torch.equal(out["state"], chain_out["state"].view(-1)) and
+                    torch.equal(out["branch"], chain_out["branch"].view(-1)))
+        chain_ms = timed(gchain, args.steps)
         clk = ClockSampler(local_rank)
         clk.start()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -492,14 +522,14 @@ def run_f3(args, rank: int, world: int, local_rank: int) -> None:
         ms = e0.elapsed_time(e1) / args.steps
         e2e = None
         if not args.no_e2e:
-            hp = torch.empty((1, HC * H), dtype=torch.bfloat16).pin_memory()
+            hp = torch.empty(HC * H, dtype=torch.bfloat16).pin_memory()
             hp.copy_(h.cpu())
-            op = torch.empty((1, H), dtype=torch.bfloat16).pin_memory()
+            op = torch.empty(H, dtype=torch.bfloat16).pin_memory()
             t0 = time.perf_counter()
             for _ in range(args.steps):
                 h.copy_(hp, non_blocking=True)
                 graph.replay()
-                op.copy_(sh, non_blocking=True)
+                op.copy_(out["branch"], non_blocking=True)
                 st.synchronize()
             dt = time.perf_counter() - t0
             e2e = {"value": round(args.steps / dt, 2), "unit": "tok/s", "h2d_bytes_per_step": hp.numel() * 2,
@@ -516,9 +546,9 @@ def run_f3(args, rank: int, world: int, local_rank: int) -> None:
                           m.b.view(torch.int16).cpu().numpy().view(np.uint16))
         nw = lay["nw"].view(torch.int16).cpu().numpy().view(np.uint16)
         mats = {k: tonp(lay[k]) for k in ("down", "up", "inj", "sg", "su", "sd", "se")}
-        hx = h.view(torch.int16).cpu().numpy().view(np.uint16)
-        bx = br.view(torch.int16).cpu().numpy().view(np.uint16)
-        gx = gt.view(torch.int16).cpu().numpy().view(np.uint16)
+        hx = h.view(1, -1).view(torch.int16).cpu().numpy().view(np.uint16)
+        bx = br.view(1, -1).view(torch.int16).cpu().numpy().view(np.uint16)
+        gx = gt.view(1, -1).view(torch.int16).cpu().numpy().view(np.uint16)
         orc.set_threads(os.cpu_count() or 1)
         n, t0 = 0, time.perf_counter()
         while time.perf_counter() - t0 < 8.0:
@@ -534,12 +564,15 @@ def run_f3(args, rank: int, world: int, local_rank: int) -> None:
             "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "u8/u4 codes x bf16 -> f32/f64", "data": "synthetic",
             "config": {"workload": "f3_hc4x3072_r320_shared768_28layers", "layers": L, "streams": HC, "hidden": H,
-                       "rank": R, "shared_inter": I, "tokens": 1, "l2": "weights of 28 layers (347 MB) > L2"},
+                       "rank": R, "shared_inter": I, "tokens": 1, "l2": "weights of 28 layers (347 MB) > L2",
+                       "chained": "each layer's mixer writes the previous layer's shared-expert output"},
+            "per_layer_launches": {"ms_per_step": round(chain_ms, 4), "value": round(1000.0 / chain_ms, 2),
+                                   "launches_per_step": 5 * L, "same_bits": same},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 2), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "traffic": None,
                          "algorithmic_bytes_per_step": wbytes, "peak_source": src},
-            "clocks": clocks, "gpu_launches": 5 * L * args.steps, "e2e": e2e, "cpu_baseline": cpu}
-    del graph
+            "clocks": clocks, "gpu_launches": args.steps, "e2e": e2e, "cpu_baseline": cpu}
+    del graph, gchain
     print(json.dumps(line), flush=True)
 
 

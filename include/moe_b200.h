@@ -405,6 +405,40 @@ int moe_ep_a2a_layer(const void *x, int T, int H, int I, int E, int K, const int
                      size_t workspace_bytes, void *stream);
 
 /* ------------------------------------------------------------------------------------ */
+/* Mixer + shared expert for all layers in one launch per token (decode).                */
+/* ------------------------------------------------------------------------------------ */
+
+/* One layer's weights (device pointers, MLX affine layout, bf16 or fp16 scales/biases as
+ * sb_fp16 says): the mixer's norm weight (bf16 [4H]), down [R][4H], up [4H][R] and inject
+ * [4][4H] (8-bit, group 64; inject may be NULL), the shared expert's gate / up [I][H] and
+ * down [H][I] (4-bit, group 64) and its scalar gate [1][H] (8-bit, group 64). */
+typedef struct {
+    const void *norm_w;
+    const void *wd, *sd, *bd, *wu, *su, *bu, *wi, *si, *bi;
+    const void *wsg, *ssg, *bsg, *wsu, *ssu, *bsu, *wsd, *ssd, *bsd, *wse, *sse, *bse;
+} moe_f3_layer;
+
+/* Workspace bytes for moe_f3_stack_decode. */
+size_t moe_f3_stack_workspace_bytes(int H, int R, int I);
+
+/*
+ * One token through L layers of the step in front of each MoE block, the block's output being
+ * the shared expert: per layer (mixed, state, inj) = moe_hc_mix(state, write = (branch, inj of
+ * the layer before)), branch = moe_shared_expert(mixed), with the same bits as those two calls
+ * (decode regime), in ONE cooperative launch (one CTA per SM, or num_ctas; four grid barriers
+ * per layer). layers: device array [L] of moe_f3_layer. h: the first layer's streams bf16
+ * [4H]; branch0 / gate0: a pending write (bf16 [H] / [4]) or both NULL. Outputs: state_out
+ * [4H] (the last block's output written into the streams), branch_out [H] and inj_out [4] (the
+ * last block output and its stream gate; inj_out may be NULL), branch_all [L][H] (every
+ * layer's block output) or NULL. H, R, I multiples of 64; buffers 16-byte aligned. Replaces
+ * the per-layer run_hc + shared-expert launches of Qwen38Engine (mlx-qwen38/cpp/src/
+ * engine.cpp:390-400, kernels.cpp:1363-1560) for a decode step.
+ */
+int moe_f3_stack_decode(const void *layers, int L, int H, int R, int I, int sb_fp16, float eps, const void *h,
+                        const void *branch0, const void *gate0, void *state_out, void *branch_out, void *inj_out,
+                        void *branch_all, void *workspace, size_t workspace_bytes, int num_ctas, void *stream);
+
+/* ------------------------------------------------------------------------------------ */
 /* K50 expert pack (one directory per layer: codes.bin, scales.bf16, bias.bf16,          */
 /* index.json; replaces ExpertPackCpp, mlx-qwen38/cpp/src/loader.cpp:1187-1470).          */
 /* ------------------------------------------------------------------------------------ */

@@ -23,6 +23,7 @@
 
 #include "common.cuh"
 #include "qlinear.cuh"
+#include "hcmath.cuh"
 #include "../../include/moe_b200.h"
 
 namespace {
@@ -77,22 +78,6 @@ __global__ void __launch_bounds__(kNormThreads) hc_norm_kernel(const uint16_t *_
         const float sc = __fadd_rn(1.0f, bf16_bits_to_f32(ldu16(norm_w + (size_t)c * H + i)));
         normed[base + i] = f32_to_bf16_bits(__fmul_rn(y, sc));
     }
-}
-
-// mix = silu(d / HC) in the row count's regime
-MOE_D float hc_mix_value(float d, int prefill) {
-    if (prefill) {
-        const float v = bf16r(__fdiv_rn(bf16r(d), (float)kHc));
-        return __fmul_rn(v, sigmoid_bf16(v));
-    }
-    const float v = __fdiv_rn(d, (float)kHc);
-    return __fmul_rn(v, sigmoidf(v));
-}
-
-// inj = 2 * sigmoid(iv / HC) in the row count's regime
-MOE_D float hc_inj_value(float iv, int prefill) {
-    if (prefill) return __fmul_rn(2.0f, sigmoid_bf16(bf16r(__fdiv_rn(bf16r(iv), (float)kHc))));
-    return __fmul_rn(2.0f, sigmoidf(__fdiv_rn(iv, (float)kHc)));
 }
 
 // mixed[t][h] = mean_c sigmoid(u[t][c*H + h]) * normed[t][c*H + h], u = mix . Wu^T: a block

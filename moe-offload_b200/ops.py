@@ -433,3 +433,70 @@ def prefill_layer(x: torch.Tensor, router: torch.Tensor, gate: QMatrix, up: QMat
          down.b.data_ptr(), gate.sb_fp16, int(norm), _ptr(resid), o["inds"].data_ptr(), o["scores"].data_ptr(),
          o["y"].data_ptr(), ws.data_ptr(), ws.numel(), _stream(stream))
     return o
+
+
+# ----------------------------------------------------------------------------- mixer + shared, all layers
+
+class F3Stack:
+    """The step in front of every MoE block for a decode token, all layers in one launch
+    (moe_f3_stack_decode): per layer the hyper-connection mixer with the previous block's write
+    and the shared expert on its output, the shared expert's output being the block output
+    (the same bits as hc_mix + shared_expert per layer). layers: dicts with "nw" (bf16 [4H]),
+    "down" [R, 4H], "up" [4H, R], "inj" [4, 4H] or None (8-bit g64), "sg" / "su" [I, H], "sd"
+    [H, I] (4-bit g64), "se" [1, H] (8-bit g64), all QMatrix with one scale dtype."""
+
+    KEYS = ("down", "up", "inj", "sg", "su", "sd", "se")
+
+    def __init__(self, layers: list[dict], device, eps: float = 1e-6, num_ctas: int = 0):
+        self.device = torch.device(device)
+        self.L = len(layers)
+        ly0 = layers[0]
+        R, W = ly0["down"].w.shape[0], ly0["down"].w.shape[1] * 32 // ly0["down"].bits
+        self.H, self.R, self.I = W // 4, R, ly0["sg"].w.shape[0]
+        self.eps, self.num_ctas = float(eps), int(num_ctas)
+        sbs = set()
+        rows = []
+        for ly in layers:
+            want = {"down": (8, R, W), "up": (8, W, R), "inj": (8, 4, W), "sg": (4, self.I, self.H),
+                    "su": (4, self.I, self.H), "sd": (4, self.H, self.I), "se": (8, 1, self.H)}
+            if ly["nw"].data_ptr() % 16:
+                raise ValueError("f3 layer: norm weight must be 16-byte aligned")
+            ptrs = [ly["nw"].data_ptr()]
+            for k in self.KEYS:
+                q = ly.get(k)
+                if q is None:
+                    if k != "inj":
+                        raise ValueError(f"f3 layer: {k} missing")
+                    ptrs += [0, 0, 0]
+                    continue
+                bits, n, kin = want[k]
+                if q.bits != bits or q.group_size != 64 or q.w.shape[0] != n or q.w.shape[1] * 32 // q.bits != kin:
+                    raise ValueError(f"f3 layer: {k} must be {bits}-bit g64 [{n}, {kin}]")
+                q.check(k, self.device)
+                sbs.add(q.sb_fp16)
+                ptrs += [q.w.data_ptr(), q.s.data_ptr(), q.b.data_ptr()]
+            rows.append(ptrs)
+        if len(sbs) != 1:
+            raise ValueError("f3 layers: one scale dtype expected")
+        self.sb_fp16 = sbs.pop()
+        self.layers = layers                       # the table points into these tensors
+        self.table = torch.tensor(rows, dtype=torch.int64, device=self.device)
+        nb = int(call("moe_f3_stack_workspace_bytes", self.H, self.R, self.I))
+        self.ws = torch.empty(nb, dtype=torch.uint8, device=self.device)
+
+    def decode(self, h: torch.Tensor, branch=None, gate=None, *, want_all: bool = False, out=None, stream=None):
+        """h bf16 [4H] (or [1, 4H]); branch / gate: the pending write (bf16 [H] / [4]) or None.
+        Returns (state [4H] after the last block's write, last block output [H], its gate [4],
+        every layer's block output [L, H] or None)."""
+        _need(h, "h", (torch.bfloat16,), self.device)
+        o = out if out is not None else {}
+        st = o.setdefault("state", torch.empty(4 * self.H, dtype=torch.bfloat16, device=self.device))
+        br = o.setdefault("branch", torch.empty(self.H, dtype=torch.bfloat16, device=self.device))
+        inj = o.setdefault("inj", torch.empty(4, dtype=torch.bfloat16, device=self.device))
+        alls = None
+        if want_all:
+            alls = o.setdefault("all", torch.empty((self.L, self.H), dtype=torch.bfloat16, device=self.device))
+        call("moe_f3_stack_decode", self.table.data_ptr(), self.L, self.H, self.R, self.I, self.sb_fp16, self.eps,
+             h.data_ptr(), _ptr(branch), _ptr(gate), st.data_ptr(), br.data_ptr(), inj.data_ptr(), _ptr(alls),
+             self.ws.data_ptr(), self.ws.numel(), self.num_ctas, _stream(stream))
+        return st, br, inj, alls
