@@ -44,8 +44,9 @@ def test_fixture_router_8bit(moe_fixture, dev):
 
 @pytest.mark.parametrize("T,H,E,K,M", [(1, 3072, 512, 10, 12), (4, 2048, 64, 8, 0), (3, 2688, 240, 9, 12),
                                        (2, 256, 16, 4, 12),
-                                       # batched path (T >= 1024: tiled double-precision GEMM + per-token selection)
-                                       (1024, 3072, 512, 10, 12), (1100, 2688, 240, 9, 0), (1030, 1000, 100, 6, 7)])
+                                       # batched path (T >= 256: tiled double-precision GEMM + per-token selection)
+                                       (1024, 3072, 512, 10, 12), (1100, 2688, 240, 9, 0), (1030, 1000, 100, 6, 7),
+                                       (512, 3072, 512, 10, 0), (256, 1024, 64, 4, 12)])
 def test_router_bf16_bit_exact(dev, T, H, E, K, M):
     from moe_offload_b200 import ops
     from moe_offload_b200.synthetic import np_bf16_normal, np_to_bf16_tensor
