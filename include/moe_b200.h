@@ -425,8 +425,8 @@ size_t moe_f3_stack_workspace_bytes(int H, int R, int I);
  * One token through L layers of the step in front of each MoE block, the block's output being
  * the shared expert: per layer (mixed, state, inj) = moe_hc_mix(state, write = (branch, inj of
  * the layer before)), branch = moe_shared_expert(mixed), with the same bits as those two calls
- * (decode regime), in ONE cooperative launch (one CTA per SM, or num_ctas; four grid barriers
- * per layer). layers: device array [L] of moe_f3_layer. h: the first layer's streams bf16
+ * (decode regime), in ONE cooperative launch (one CTA per SM, or num_ctas >= 128; five grid
+ * barriers per layer). layers: device array [L] of moe_f3_layer. h: the first layer's streams bf16
  * [4H]; branch0 / gate0: a pending write (bf16 [H] / [4]) or both NULL. Outputs: state_out
  * [4H] (the last block's output written into the streams), branch_out [H] and inj_out [4] (the
  * last block output and its stream gate; inj_out may be NULL), branch_all [L][H] (every

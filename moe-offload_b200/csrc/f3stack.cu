@@ -6,24 +6,27 @@
 // csrc/stack.cu). Replaces, per token, the five launches per layer of moe_hc_mix +
 // moe_shared_expert with the same arithmetic, bit for bit (one token: the decode regime).
 //
-// Per layer, with G CTAs of 512 threads (one per SM) and four grid barriers:
-//   P0  every CTA: the write (stream c of the state gets bf16(branch * gate_c) added) and the
-//       per-stream RMS norm of all four streams, redundantly, into its shared memory (the norm
-//       reproduces hc_norm_kernel's reduction tree: 1024 strided partial sums, a xor-shuffle
-//       tree per 32, the 32 warp sums in order); CTA 0 stores the written state
+// Per layer, with G >= 128 CTAs of 512 threads (one per SM) and five grid barriers:
+//   P0a the write (stream c of the state gets bf16(branch * gate_c) added) and the sums of the
+//       per-stream RMS norm, split exactly as hc_norm_kernel's reduction tree: CTA 32c + w
+//       takes virtual warp w of stream c (virtual thread v sums its values v, v + 1024, ... in
+//       order, a xor-shuffle tree per 32) and stores the written state    | barrier
+//   P0b every CTA: the 32 warp sums in order, and the normed values of all 4 streams into its
+//       shared memory (its loads issued together)
 //   P1  mixer down (R rows) and inject (4 rows) over the 4H normed values: CTA j owns rows
 //       j, j+G, ...; one thread per (row, group) item, group values in double, row totals in
 //       group order (float totals)                                             | barrier
 //   P2  mix = silu(down / 4) of all R totals (every CTA), mixer up for the hidden indices the
 //       CTA owns (their four stream rows), mixed = mean_c sigmoid(up_c) * normed_c; CTA 0
 //       forms inj = 2 sigmoid(inject / 4)                                       | barrier
-//   P3  shared gate + up rows the CTA owns, SwiGLU with MLX's bf16 roundings; the last CTA
-//       also the scalar expert gate                                              | barrier
-//   P4  shared down rows the CTA owns, scaled by bf16(sigmoid(gate)): the block output
-//                                                                                | barrier
-// After the last layer CTA 0 applies the last block's write to the state. Every item's group
-// value and every row total is formed exactly as in the per-kernel path (qlinear.cuh), so the
-// result does not depend on G. Grid barriers are bounded: a timeout sets the device error word.
+//   P3  shared gate + up rows the CTA owns, SwiGLU with MLX's bf16 roundings; the scalar
+//       expert gate's group values, spread over the CTAs with the fewest rows  | barrier
+//   P4  the gate (its group values summed in order), shared down rows the CTA owns scaled by
+//       bf16(sigmoid(gate)): the block output                                   | barrier
+// The first weight item of every phase is loaded before the barrier in front of it. After the
+// last layer CTA 0 applies the last block's write to the state. Every item's group value and
+// every row total is formed exactly as in the per-kernel path (qlinear.cuh), so the result does
+// not depend on G. Grid barriers are bounded: a timeout sets the device error word.
 #include <cstdint>
 
 #include <cuda_runtime.h>
@@ -45,14 +48,14 @@ constexpr uint32_t kF3SpinLimit = 1u << 24;
 
 struct F3Args {
     const moe_f3_layer *layers;
-    int L, H, R, I, sb_fp16;
+    int L, H, R, I;
     float eps;
     const uint16_t *h0, *branch0, *gate0;
     uint16_t *state_out, *branch_out, *inj_out, *branch_all;
     float *dv, *iv;
     double *ssum;                                // [4 streams][32 virtual warps] of the norm's tree
     double *gsum;                                // the scalar expert gate's group values
-    uint16_t *mixed, *act, *gl, *state, *branch, *inj;
+    uint16_t *mixed, *act, *state, *branch, *inj;
     unsigned int *bar;
 };
 
@@ -111,7 +114,7 @@ MOE_D void stage_l2(uint16_t *dst, const uint16_t *src, int n) {
 }
 
 struct Smem {
-    size_t normed, sxv, sx, sv, spart, total;
+    size_t normed, sx, sv, spart, total;
     MOE_HD Smem(int H, int R, int I, int G) {
         const int W = kHcStreams * H;
         const int rpc1 = (R + kHcStreams + G - 1) / G, rpc2 = (H + G - 1) / G, rpc3 = (I + G - 1) / G;
@@ -123,8 +126,7 @@ struct Smem {
         items = items > i4 ? items : i4;
         const int xmax = R > H ? (R > I ? R : I) : (H > I ? H : I);
         normed = 0;
-        sxv = al128((size_t)W * 2);
-        sx = sxv;
+        sx = al128((size_t)W * 2);
         sv = sx + al128((size_t)xmax * 2);
         spart = sv + al128(items * 8);
         total = spart + al128((size_t)(kHcStreams * 32 > H / 64 ? kHcStreams * 32 : H / 64) * 8);
@@ -391,7 +393,7 @@ __global__ void __launch_bounds__(kF3Threads, 1) f3_stack_kernel(F3Args a) {
 }
 
 struct F3Ws {
-    size_t dv, iv, ssum, gsum, mixed, act, gl, state, branch, inj, bar, total;
+    size_t dv, iv, ssum, gsum, mixed, act, state, branch, inj, bar, total;
     F3Ws(int H, int R, int I) {
         const size_t W = (size_t)kHcStreams * H;
         dv = 0;
@@ -400,8 +402,7 @@ struct F3Ws {
         gsum = ssum + al256(kHcStreams * 32 * 8);
         mixed = gsum + al256((size_t)(H / 64) * 8);
         act = mixed + al256((size_t)H * 2);
-        gl = act + al256((size_t)I * 2);
-        state = gl + 256;
+        state = act + al256((size_t)I * 2);
         branch = state + al256(2 * W * 2);
         inj = branch + al256(2 * (size_t)H * 2);
         bar = inj + 256;
@@ -447,7 +448,7 @@ extern "C" int moe_f3_stack_decode(const void *layers, int L, int H, int R, int 
     char *p = static_cast<char *>(workspace);
     F3Args a{};
     a.layers = static_cast<const moe_f3_layer *>(layers);
-    a.L = L, a.H = H, a.R = R, a.I = I, a.sb_fp16 = sb_fp16, a.eps = eps;
+    a.L = L, a.H = H, a.R = R, a.I = I, a.eps = eps;
     a.h0 = static_cast<const uint16_t *>(h);
     a.branch0 = static_cast<const uint16_t *>(branch0);
     a.gate0 = static_cast<const uint16_t *>(gate0);
@@ -461,7 +462,6 @@ extern "C" int moe_f3_stack_decode(const void *layers, int L, int H, int R, int 
     a.gsum = reinterpret_cast<double *>(p + w.gsum);
     a.mixed = reinterpret_cast<uint16_t *>(p + w.mixed);
     a.act = reinterpret_cast<uint16_t *>(p + w.act);
-    a.gl = reinterpret_cast<uint16_t *>(p + w.gl);
     a.state = reinterpret_cast<uint16_t *>(p + w.state);
     a.branch = reinterpret_cast<uint16_t *>(p + w.branch);
     a.inj = reinterpret_cast<uint16_t *>(p + w.inj);
