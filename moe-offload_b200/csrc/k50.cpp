@@ -22,6 +22,7 @@
 
 #include <cstdint>
 #include <cstring>
+#include <exception>
 #include <fstream>
 #include <map>
 #include <memory>
@@ -294,6 +295,7 @@ void *moe_k50_open(const char *layer_dir) {
     ss << f.rdbuf();
     const std::string text = ss.str();
     Json js(text);
+    try {    // no C++ exception may cross the C ABI (a number too large for int64, out of memory)
     js.object([&](const std::string &top) {
         if (top == "experts") {
             js.object([&](const std::string &proj) {
@@ -312,6 +314,9 @@ void *moe_k50_open(const char *layer_dir) {
             js.skip();
         }
     });
+    } catch (const std::exception &) {
+        js.bad = true;
+    }
     if (js.bad) {
         moe_set_error(MOE_EINVAL, "k50_open: %s/index.json is not a K50 index (parse error near byte %zu)",
                       layer_dir, js.i);

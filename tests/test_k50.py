@@ -105,6 +105,10 @@ def test_bad_packs(tmp_path):
     (tmp_path / "L01" / "index.json").write_text('{"experts": {"gate_proj": [{"expert": 0, "kind": }]}}')
     with pytest.raises(MoeError):
         k50.K50Pack(tmp_path / "L01")
+    # a number beyond int64 is refused, not thrown through the C ABI
+    (tmp_path / "L01" / "index.json").write_text('{"experts": {"gate_proj": [{"expert": 0, "code_off": 1' + '0' * 30 + '}]}}')
+    with pytest.raises(MoeError):
+        k50.K50Pack(tmp_path / "L01")
 
 
 def test_pool_refuses_wider_codes(tmp_path):
