@@ -4,6 +4,10 @@
 //   2. the prefill GEMM's per-K-block pattern: 8 MMAs (two accumulators, A in 4 TMEM stages,
 //      B in 8 shared-memory stages) followed by 0 / 1 / 2 commits, issued by one lane or by a
 //      whole warp's loop with mbarrier waits, with zero or random operands
+//   3. cta_group::2 on CTA pairs (clusters of 2, 74 pairs): M = 256 (128 rows in each CTA's
+//      TMEM), N = 32 .. 256, issued by the even CTA; and the same K-block pattern as 2. with
+//      M = 256, N = 64, each commit sent to both CTAs' mbarriers (two plain commits, the
+//      second to the peer's barrier through mapa)
 // Every wait is bounded (a timeout sets a device flag, reported at the end). Build and run:
 //   nvcc -gencode arch=compute_100a,code=sm_100a -O3 -o tcgen05_issue_rate \
 //       moe-offload_b200/microbench/tcgen05_issue_rate.cu && ./tcgen05_issue_rate
@@ -184,6 +188,134 @@ void run_kblock(long long *d) {
     printf("commits/kblock %d mma %d flags %d random %d: %.1f cycles per K-block\n", C, MMA, F, (int)RND, avg / 148 / nkb);
 }
 
+// ------------------------------------------------------------------ cta_group::2
+__device__ __forceinline__ void cluster_sync_all() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ uint32_t cluster_rank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+__device__ __forceinline__ uint32_t peer_addr(uint32_t local, uint32_t rank) {
+    uint32_t p;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(p) : "r"(local), "r"(rank));
+    return p;
+}
+__device__ __forceinline__ void mma2_ts(uint32_t d, uint32_t a, uint64_t b, uint32_t id, uint32_t acc) {
+    asm volatile("{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n tcgen05.mma.cta_group::2.kind::f16 [%0], [%1], %2, %3, p;\n}\n"
+                 ::"r"(d), "r"(a), "l"(b), "r"(id), "r"(acc));
+}
+// commit to a shared::cluster mbarrier address (this CTA's or, through mapa, the peer's)
+__device__ __forceinline__ void commit2(uint32_t bar) {
+    asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ bool wait_parity(uint64_t *bar, uint32_t par) {
+    uint32_t ok = 0;
+    for (uint32_t i = 0; i < (1u << 26) && !ok; ++i)
+        asm volatile("{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+                     : "=r"(ok) : "r"(saddr(bar)), "r"(par) : "memory");
+    return ok != 0;
+}
+
+// KB = 0: R x 4 back-to-back MMAs of M = 256 x N per iteration; KB > 0: the K-block pattern
+// (8 MMAs of N into two accumulators, A in 4 TMEM stages, B in 8 shared stages) with KB - 1
+// commit pairs per K-block
+template <int N, int R, int KB>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(128) rate2(int iters, long long *out) {
+    extern __shared__ __align__(1024) unsigned char sm[];
+    unsigned char *base = (unsigned char *)(((uintptr_t)sm + 1023) & ~(uintptr_t)1023);
+    __shared__ uint64_t bars[16];
+    __shared__ uint64_t fin;
+    __shared__ uint32_t tslot;
+    for (int i = threadIdx.x; i < 8 * 8192 / 4; i += blockDim.x) ((uint32_t *)base)[i] = 0;
+    const uint32_t rank = cluster_rank();
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < 16; ++i) asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(saddr(&bars[i])));
+        asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(saddr(&fin)));
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (threadIdx.x < 32) {
+        asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], 512;" ::"r"(saddr(&tslot)));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;");
+    }
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    cluster_sync_all();
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    const uint32_t tm = tslot;
+    if (threadIdx.x == 0) {
+        long long t0 = clock64();
+        if (rank == 0) {
+            if constexpr (KB == 0) {
+                constexpr uint32_t id = idesc(256, N);
+                uint64_t bd[4];
+                for (int j = 0; j < 4; ++j) bd[j] = desc_sw128(saddr(base) + 32u * j);
+                for (int it = 0; it < iters; ++it) {
+#pragma unroll
+                    for (int r = 0; r < R; ++r)
+#pragma unroll
+                        for (int j = 0; j < 4; ++j) mma2_ts(tm + r * N, tm + 384u + 8u * j, bd[j], id, 1u);
+                }
+            } else {
+                constexpr uint32_t id = idesc(256, N);
+                for (int kb = 0; kb < iters; ++kb) {
+                    const int s = kb & 3, sb = kb & 7;
+                    const uint32_t at = tm + 256u + 64u * s;
+                    const uint32_t b0 = saddr(base + 8192 * sb);
+#pragma unroll
+                    for (int mm = 0; mm < 2; ++mm)
+#pragma unroll
+                        for (int j = 0; j < 4; ++j)
+                            mma2_ts(tm + 128u * mm, at + 32u * mm + 8u * j, desc_sw128(b0 + 32u * j), id, (kb | j) != 0);
+                    if (KB >= 2) {
+                        commit2(saddr(&bars[s]));
+                        commit2(peer_addr(saddr(&bars[s]), 1));
+                    }
+                    if (KB >= 3) {
+                        commit2(saddr(&bars[8 + sb]));
+                        commit2(peer_addr(saddr(&bars[8 + sb]), 1));
+                    }
+                }
+            }
+            commit2(saddr(&fin));
+            commit2(peer_addr(saddr(&fin), 1));
+        }
+        const bool ok = wait_parity(&fin, 0);
+        long long t1 = clock64();
+        if (!ok) atomicOr(&g_err, 4u);
+        out[blockIdx.x] = t1 - t0;
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    cluster_sync_all();
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    if (threadIdx.x < 32) asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, 512;" ::"r"(tm));
+}
+
+template <int N, int R, int KB>
+void run_rate2(long long *d) {
+    const int smem = 8 * 8192 + 1024, iters = KB ? 512 : 64;
+    cudaFuncSetAttribute(rate2<N, R, KB>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    rate2<N, R, KB><<<148, 128, smem>>>(iters, d);
+    cudaError_t e = cudaDeviceSynchronize();
+    if (e != cudaSuccess) { printf("error %s\n", cudaGetErrorString(e)); exit(1); }
+    long long h[148];
+    cudaMemcpy(h, d, sizeof(h), cudaMemcpyDeviceToHost);
+    double avg = 0;
+    for (int i = 0; i < 148; i += 2) avg += h[i];
+    avg /= 74;
+    if (KB == 0) {
+        const double per = avg / (iters * 4.0 * R);
+        printf("cta_group::2 A-tmem M 256 N %3d R %d: %.1f cycles/mma, %.0f MAC/clk per SM\n", N, R, per,
+               128.0 * N * 16 / per);
+    } else {
+        printf("cta_group::2 K-block (8 MMAs M 256 N %d) + %d commit pairs: %.1f cycles per K-block\n", N, KB - 1,
+               avg / iters);
+    }
+}
+
 int main() {
     long long *d;
     cudaMalloc(&d, 148 * sizeof(long long));
@@ -194,6 +326,9 @@ int main() {
     run_kblock<0, true, 0>(d); run_kblock<1, true, 0>(d); run_kblock<2, true, 0>(d);
     run_kblock<2, true, 0, true>(d);
     run_kblock<2, true, 2>(d); run_kblock<2, true, 7>(d); run_kblock<2, false, 7>(d);
+    run_rate2<32, 8, 0>(d); run_rate2<64, 1, 0>(d); run_rate2<64, 4, 0>(d); run_rate2<128, 2, 0>(d);
+    run_rate2<256, 1, 0>(d);
+    run_rate2<64, 1, 1>(d); run_rate2<64, 1, 2>(d); run_rate2<64, 1, 3>(d);
     unsigned int err = 0;
     cudaMemcpyFromSymbol(&err, g_err, 4);
     printf("device error word %u (0: every wait completed)\n", err);
