@@ -20,15 +20,18 @@
 //               16-row boxes of expert-ordered rows (gate/up: x rows gathered into position
 //               order by one copy kernel; down: the act rows), 128-byte swizzled
 //   warps 6-13  dequantise one K-block of codes to bf16, w = bf16(s * q + b) with one
-//               rounding, into the 128-byte-swizzled K-major layout the MMA reads: the four
-//               values of a (row, group) are built once and every pair of codes becomes a
-//               bf16x2 word with one byte permute (selectors built 8 codes at a time)
+//               rounding, into TMEM (the A operand, lane = weight row): the four values of a
+//               (row, group) are built once and every pair of codes becomes a bf16x2 word with
+//               one byte permute (selectors built 8 codes at a time)
 //   warp 1      one thread issues the tcgen05.mma (K = 16 each) into TMEM; the accumulators
 //               are double-buffered across tiles
 //   warps 2-5   epilogue: tcgen05.ld of the accumulators, SwiGLU with MLX's bf16 roundings
 //               (gate/up) or the bf16 rounding (down), stores to global
 // Stages hand over through mbarriers (TMA transaction counts, tcgen05.commit, warp
-// arrivals); every wait is bounded.
+// arrivals); every wait is bounded. A K-block stage (its dequantised weights in TMEM and its
+// token rows in shared memory) is one unit: the dequant warps wait for the tokens before they
+// arrive, so the MMA thread waits on one barrier per K-block and frees the stage with one
+// commit (two waits and two commits cost ~9 % more).
 #include <cuda.h>
 
 #include "common.cuh"
@@ -56,13 +59,6 @@ MOE_HD uint32_t instr_desc_bf16(int n) {
     return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(kBM >> 4) << 24);
 }
 
-MOE_D void mma_bf16(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
-    asm volatile(
-        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
-        " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(d_tmem),
-        "l"(a), "l"(b), "r"(idesc), "r"(acc));
-}
-
 // A from tensor memory (lane = row, two bf16 of K per 32-bit column), B from shared memory
 MOE_D void mma_bf16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b, uint32_t idesc, uint32_t acc) {
     asm volatile(
@@ -88,16 +84,7 @@ MOE_D void tmem_ld16(uint32_t taddr, float (&v)[16]) {
     for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
 
-// this warp's 32 TMEM lanes, 16 / 32 consecutive 32-bit columns from taddr
-MOE_D void tmem_st16(uint32_t taddr, const uint32_t (&v)[16]) {
-    asm volatile(
-        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(
-            taddr),
-        "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]),
-        "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
-        : "memory");
-}
-
+// this warp's 32 TMEM lanes, 32 consecutive 32-bit columns from taddr
 MOE_D void tmem_st32(uint32_t taddr, const uint32_t (&v)[32]) {
     asm volatile(
         "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
@@ -309,8 +296,9 @@ __global__ void gather_rows_kernel(const uint16_t *x, const int *src_of, int TK,
 
 constexpr int kRawK = 8;                         // K-blocks per raw code stage (128 B of codes per row)
 constexpr int kRS = 2;                           // raw code stages
-constexpr int kKS = 4;                           // A stages (dequantised weights in TMEM)
-constexpr int kBS = 8;                           // B stages (activation rows in shared memory, TMA)
+// K-block stages: the dequantised weights of stage s in TMEM (A) and the token rows of the
+// same K-block in shared memory (B, TMA) are one unit, freed by one commit
+constexpr int kKS = 4;
 constexpr int kGemmThreads = 448;                // 14 warps
 constexpr int kDqWarp0 = 6, kDqWarps = 8;
 constexpr int kEpiWarp0 = 2;
@@ -335,11 +323,11 @@ template <bool kGateUp>
 struct GemmSmem {
     static constexpr int kNM = 2;   // weight matrices per tile: gate + up, or two 128-row blocks of down
     static constexpr size_t raw = 0;                                       // [kRS][kNM] tiles
-    static constexpr size_t b = raw + (size_t)kRS * kNM * kTile;           // [kBS] tiles
-    static constexpr size_t bars = b + (size_t)kBS * kTile;
-    // raw_full, raw_empty [kRS]; full, empty [kKS]; b_full, b_empty [kBS]; acc_full, acc_empty
-    // [2] (accumulator halves); drain (MMA completion after an abort); tmem slot, abort flag
-    static constexpr size_t total = bars + (2 * kRS + 2 * kKS + 2 * kBS + 5) * 8 + 16;
+    static constexpr size_t b = raw + (size_t)kRS * kNM * kTile;           // [kKS] tiles
+    static constexpr size_t bars = b + (size_t)kKS * kTile;
+    // raw_full, raw_empty [kRS]; full, empty, b_full [kKS]; acc_full, acc_empty [2]
+    // (accumulator halves); drain (MMA completion after an abort); tmem slot, abort flag
+    static constexpr size_t total = bars + (2 * kRS + 3 * kKS + 5) * 8 + 16;
     static constexpr size_t alloc = total + 1024;      // + alignment slack
 };
 
@@ -357,8 +345,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     uint64_t *full = raw_empty + kRS;
     uint64_t *empty = full + kKS;
     uint64_t *b_full = empty + kKS;
-    uint64_t *b_empty = b_full + kBS;
-    uint64_t *acc_full = b_empty + kBS;          // [2]
+    uint64_t *acc_full = b_full + kKS;           // [2]
     uint64_t *acc_empty = acc_full + 2;          // [2]
     uint64_t *drain = acc_empty + 2;             // [1]
     uint32_t *tslot = reinterpret_cast<uint32_t *>(drain + 1);
@@ -373,12 +360,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             mbar_init(&raw_empty[i], kDqWarps);
         }
         for (int i = 0; i < kKS; ++i) {
-            mbar_init(&full[i], kDqWarps);
-            mbar_init(&empty[i], 1);
-        }
-        for (int i = 0; i < kBS; ++i) {
-            mbar_init(&b_full[i], 1);
-            mbar_init(&b_empty[i], 1);
+            mbar_init(&full[i], kDqWarps);       // dequantised stage written and its tokens landed
+            mbar_init(&empty[i], 1);             // the stage's MMAs done (one commit)
+            mbar_init(&b_full[i], 1);            // the stage's token rows landed (TMA)
         }
         for (int h = 0; h < 2; ++h) {
             mbar_init(&acc_full[h], 1);
@@ -423,8 +407,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                     }
                     ++rc;
                 }
-                const int s = g % kBS;
-                if (!wait_or_abort(&b_empty[s], ((g / kBS) & 1u) ^ 1u, abort)) {
+                const int s = g % kKS;
+                if (!wait_or_abort(&empty[s], ((g / kKS) & 1u) ^ 1u, abort)) {
                     stop = true;
                     break;
                 }
@@ -442,7 +426,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             // for the last load issued into every stage; earlier ones completed before their
             // stage was reissued
             for (uint32_t i = rc > (uint32_t)kRS ? rc - kRS : 0u; i < rc; ++i) mbar_wait(&raw_full[i % kRS], (i / kRS) & 1u);
-            for (uint32_t i = g > (uint32_t)kBS ? g - kBS : 0u; i < g; ++i) mbar_wait(&b_full[i % kBS], (i / kBS) & 1u);
+            for (uint32_t i = g > (uint32_t)kKS ? g - kKS : 0u; i < g; ++i) mbar_wait(&b_full[i % kKS], (i / kKS) & 1u);
         }
     } else if (warp == 1) {
         // ------------------------------------------------------------ MMA issuer
@@ -467,24 +451,25 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             if (!wide) nxt ^= 1u;
             tc_fence_after();
             for (int kb = 0; kb < nkb; ++kb) {
-                const int s = g % kKS, sb = g % kBS;
-                if (!wait_or_abort(&b_full[sb], (g / kBS) & 1u, abort) || !wait_or_abort(&full[s], (g / kKS) & 1u, abort)) {
+                const int s = g % kKS;
+                // full[s]: the dequantised stage and (waited for by the dequant warps) its tokens
+                if (!wait_or_abort(&full[s], (g / kKS) & 1u, abort)) {
                     stop = true;
                     break;
                 }
                 tc_fence_after();
                 if (lane == 0) {
                     const uint32_t at = tmem + kTmemA + (uint32_t)s * kTmemAStage;
-                    const uint32_t b0 = smem_addr(smem + SL::b + (size_t)sb * kTile);
-                    // one accumulator at a time: consecutive MMAs into the same TMEM columns
+                    const uint64_t bd = desc_sw128(smem_addr(smem + SL::b + (size_t)s * kTile));
+                    const uint32_t d0 = tmem + col, acc0 = kb > 0 ? 1u : 0u;
+                    // one accumulator at a time: consecutive MMAs into the same TMEM columns; a
+                    // K = 16 step moves the B start address 32 bytes (2 units of the descriptor)
 #pragma unroll
                     for (int mm = 0; mm < 2; ++mm)
 #pragma unroll
                         for (int j = 0; j < kBK / 16; ++j)
-                            mma_bf16_ts(tmem + 128u * mm + col, at + 32u * mm + 8u * j, desc_sw128(b0 + 32u * j), idesc,
-                                        (kb > 0 || j > 0) ? 1u : 0u);
+                            mma_bf16_ts(d0 + 128u * mm, at + 32u * mm + 8u * j, bd + 2u * j, idesc, j > 0 ? 1u : acc0);
                     mma_commit(&empty[s]);
-                    mma_commit(&b_empty[sb]);
                 }
                 issued = true;
                 __syncwarp();
@@ -620,6 +605,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                         dq_word(q.w, tlo, thi, out + 24);
                         tmem_st32(tcol + (uint32_t)s * kTmemAStage, out);
                         tmem_st_wait();
+                        // the MMA thread waits only for full[s]: it also stands for the stage's
+                        // token rows, which every dequant warp waits for before arriving
+                        if (!wait_or_abort(&b_full[s], (g / kKS) & 1u, abort)) {
+                            stop = true;
+                            break;
+                        }
                         tc_fence_before();
                         __syncwarp();
                         if (lane == 0) mbar_arrive(&full[s]);
