@@ -438,6 +438,42 @@ int moe_f3_stack_decode(const void *layers, int L, int H, int R, int I, int sb_f
                         const void *branch0, const void *gate0, void *state_out, void *branch_out, void *inj_out,
                         void *branch_all, void *workspace, size_t workspace_bytes, int num_ctas, void *stream);
 
+/* One layer of moe_f3moe_stack_decode: its mixer + shared expert (as moe_f3_layer) and its
+ * routed block (as moe_stack_layer: the transposed router [H][E] bf16 and the E packed experts). */
+typedef struct {
+    moe_f3_layer mix;
+    const void *router_t;
+    const void *experts;
+} moe_f3moe_layer;
+
+/* Workspace bytes for moe_f3moe_stack_decode (Is: the shared expert's intermediate size,
+ * I: the routed experts'). */
+size_t moe_f3moe_stack_workspace_bytes(int H, int R, int Is, int I, int E, int K);
+
+/*
+ * The MoE half of L decoder layers on one token in ONE cooperative launch: per layer
+ *   (mixed, state, inj) = moe_hc_mix(state, write = (branch, inj of the layer before))
+ *   routing of mixed (router logits, precise softmax, MLX-order top-k, renorm: moe_router_topk)
+ *   shared = moe_shared_expert(mixed)
+ *   branch = sum_k bf16(expert_k(mixed) * s_k) + shared   (moe_experts_gateup / moe_experts_down
+ *            with the shared output as the addend: the reference's routed + shared combine,
+ *            loader.py:909-914, engine.cpp:390-400)
+ * with the same bits as those calls (decode regime; router logits as in moe_stack_decode:
+ * exact partial dot products summed in double). layers: device array [L] of moe_f3moe_layer;
+ * sb_fp16_mix / sb_fp16_experts: fp16 (1) or bf16 (0) scales of the mixer + shared weights /
+ * of the packed experts. h, branch0, gate0, state_out, branch_out, inj_out, branch_all as in
+ * moe_f3_stack_decode; inds_out u32 [L][K] and scores_out bf16 [L][K] as in moe_stack_decode;
+ * mixed_all bf16 [L][H] (every layer's mixer output, the block input) or NULL.
+ * One CTA per SM (num_ctas = 0) or num_ctas >= 128, five grid barriers per layer. Requires
+ * H % 256 == 0, H <= 4096, R, Is, I multiples of 64, E <= 512 and a multiple of 8, K <= 32; buffers
+ * 16-byte aligned.
+ */
+int moe_f3moe_stack_decode(const void *layers, int L, int H, int R, int Is, int I, int E, int K, int sb_fp16_mix,
+                           int sb_fp16_experts, float eps, const void *h, const void *branch0, const void *gate0,
+                           void *state_out, void *branch_out, void *inj_out, uint32_t *inds_out, void *scores_out,
+                           void *branch_all, void *mixed_all, void *workspace, size_t workspace_bytes, int num_ctas,
+                           void *stream);
+
 /* ------------------------------------------------------------------------------------ */
 /* K50 expert pack (one directory per layer: codes.bin, scales.bf16, bias.bf16,          */
 /* index.json; replaces ExpertPackCpp, mlx-qwen38/cpp/src/loader.cpp:1187-1470).          */

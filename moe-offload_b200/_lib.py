@@ -78,6 +78,8 @@ SIGNATURES: dict[str, tuple] = {
     "moe_lru_acct_bytes": (SZ, []),
     "moe_f3_stack_workspace_bytes": (SZ, [I, I, I]),
     "moe_f3_stack_decode": (I, [P, I, I, I, I, I, ctypes.c_float, P, P, P, P, P, P, P, P, SZ, I, P]),
+    "moe_f3moe_stack_workspace_bytes": (SZ, [I, I, I, I, I, I]),
+    "moe_f3moe_stack_decode": (I, [P] + [I] * 9 + [ctypes.c_float] + [P] * 11 + [SZ, I, P]),
     "moe_k50_open": (P, [CP]),
     "moe_k50_close": (None, [P]),
     "moe_k50_count": (I, [P, CP]),

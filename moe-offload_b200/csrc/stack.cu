@@ -29,6 +29,7 @@
 #include <algorithm>
 
 #include "common.cuh"
+#include "f3core.cuh"
 #include "gemv_i8.cuh"
 
 namespace {
@@ -112,7 +113,7 @@ struct SmemLayout {
     size_t bars, region, xrec, xscale, xsum, arec, ascale, sact, ypart, hown, red, cand, comp, redu, redd, sinds,
         sscores, dtr, total;
     MOE_HD SmemLayout(int H, int I, int K, size_t region_bytes) {
-        const int ngH = H / 64, ngI = I / 64;
+        const int ngH = H / 64;
         bars = 0;                                                 // 16 mbarriers
         region = 128;
         xrec = region + al128(region_bytes);
@@ -361,15 +362,141 @@ MOE_D void issue_item(const StackLayer &ly, const PackDims &P, const uint32_t *s
     }
 }
 
+// Work item q = (routed expert k, activation group G of 64 values) of phase A, once its
+// packed slice is being copied into `region` (issue_item; the unit and down copies complete on
+// ubar[] / dbar at parity qphase): the 8 gate/up units (one warp pair each, as soon as its
+// bytes land) on the records of the layer input, the 64 SwiGLU activations and their one
+// record, and the down slice: a split-K partial of expert k's output over all H rows into
+// yp[q][H]. Ends with a block barrier (the region may be reissued after it).
+template <bool kFp16>
+MOE_D void run_item(int q, int l, const PackDims &P, unsigned char *region, uint64_t *ubar, uint64_t *dbar,
+                    uint32_t qphase, const uint2 *xrec, const float *xscale, const float *xsum, int xst, float *red,
+                    uint16_t *sact, uint2 *arec, float *ascale, int *dtr, float *yp, int H) {
+    (void)l;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int g = lane >> 2, t = lane & 3;
+    const int ngH = H / 64, NT = H / 16;
+    // gate/up unit p = warp pair, H split in halves between the two warps
+    {
+        const int p = warp >> 1, half = warp & 1;
+        const bool wok = mbar_wait(&ubar[p], qphase);
+        STAMP(l, 14);
+        const unsigned char *ubase = region + (size_t)p * P.ub;
+        const uint4 *gc = reinterpret_cast<const uint4 *>(ubase);
+        const uint4 *uc = reinterpret_cast<const uint4 *>(ubase + 2 * H);
+        const uint2 *sr = reinterpret_cast<const uint2 *>(ubase + 4 * H);
+        const int nsteps = ngH >> 2;
+        const int s0 = half * nsteps / 2, s1 = (half + 1) * nsteps / 2;
+        const bool bact = rec_lane_active(lane);
+        const int part = rec_lane_part(lane);
+        float accg = 0.f, accu = 0.f;
+        if (wok) {
+#pragma unroll 1
+            for (int j = s0; j < s1; ++j) {
+                const int Gj = 4 * j + t;
+                const uint4 wv = gc[j * 32 + lane], uv = uc[j * 32 + lane];
+                const uint2 sb = sr[j * 32 + lane];
+                int dg, du;
+                mma_step_i8t(wv, uv, xrec + Gj, xst, bact, part, dg, du);
+                const float sc = xscale[Gj], sm = xsum[Gj];
+                accg += sb_to_f32<kFp16>((uint16_t)sb.x) * ((float)dg * sc) +
+                        sb_to_f32<kFp16>((uint16_t)(sb.x >> 16)) * sm;
+                accu += sb_to_f32<kFp16>((uint16_t)sb.y) * ((float)du * sc) +
+                        sb_to_f32<kFp16>((uint16_t)(sb.y >> 16)) * sm;
+            }
+        }
+        STAMP(l, 15);
+        accg += __shfl_xor_sync(0xffffffffu, accg, 1);
+        accu += __shfl_xor_sync(0xffffffffu, accu, 1);
+        accg += __shfl_xor_sync(0xffffffffu, accg, 2);
+        accu += __shfl_xor_sync(0xffffffffu, accu, 2);
+        if (t == 0) {
+            red[((p * 2 + half) * 8 + g) * 2 + 0] = accg;
+            red[((p * 2 + half) * 8 + g) * 2 + 1] = accu;
+        }
+        pair_sync(p);
+        if (half == 0 && lane < 8) {
+            const float gs = red[((p * 2) * 8 + lane) * 2 + 0] + red[((p * 2 + 1) * 8 + lane) * 2 + 0];
+            const float us = red[((p * 2) * 8 + lane) * 2 + 1] + red[((p * 2 + 1) * 8 + lane) * 2 + 1];
+            const float gv = bf16r(gs), uv = bf16r(us);
+            const float sig = bf16r(1.0f / (1.0f + expf(-gv)));
+            const float avv = wok ? bf16r(bf16r(gv * sig) * uv) : 0.f;
+            sact[p * 8 + lane] = f32_to_bf16_bits(avv);
+        }
+    }
+    __syncthreads();
+    STAMP(l, 3);
+    // the one record of the 64 activations
+    if (warp == 0) {
+        const uint2 qv = (lane < 16) ? reinterpret_cast<const uint2 *>(sact)[lane] : make_uint2(0u, 0u);
+        rec_from_regs(qv, lane < 16, arec, ascale, ascale + 1, 1.0f);
+    }
+    __syncthreads();
+    // down slice: split-K partial of expert k's output over all H rows. One MMA pair per
+    // 16 rows: lane (g, t) feeds word t of rows g and g+8; B columns 0 / 1 carry the
+    // record's hi / lo parts (lanes 0..7), so D columns 0 / 1 of lane quad t = 0 hold
+    // the row's integer dot. A warp runs the MMAs of up to four of its tiles, parks the
+    // 64 dots in its transpose buffer, and then every lane finishes two adjacent rows
+    // (one 8-byte scale load, one 8-byte store) instead of 8 lanes per tile.
+    {
+        const bool wok = mbar_wait(dbar, qphase);
+        STAMP(l, 10);
+        const uint32_t *dc = reinterpret_cast<const uint32_t *>(region + P.dco);
+        const uint32_t *ds = reinterpret_cast<const uint32_t *>(region + P.dso);
+        const int n = lane >> 2;
+        const uint2 bx = (lane < 8) ? arec[(0 * 4 + t) * 2 + n] : make_uint2(0u, 0u);
+        const uint2 by = (lane < 8) ? arec[(1 * 4 + t) * 2 + n] : make_uint2(0u, 0u);
+        const float asc = ascale[0], asm_ = ascale[1];
+        float *ypq = yp + (size_t)q * H;
+        int *yb = dtr + warp * 64;
+        const int ntw = NT / kWarps;               // tiles per warp (H is a multiple of 256)
+#pragma unroll 1
+        for (int j0 = 0; j0 < ntw; j0 += 4) {
+            const int jn = min(4, ntw - j0);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                if (j < jn) {                      // warp-uniform
+                    const int tile = warp + (j0 + j) * kWarps;
+                    const uint32_t wa = dc[tile * 64 + lane], wb = dc[tile * 64 + 32 + lane];
+                    int dx[4] = {0, 0, 0, 0}, dy[4] = {0, 0, 0, 0};
+                    mma_u8s8_16832(dx, wa & 0x03030303u, wb & 0x03030303u, (wa >> 2) & 0x03030303u,
+                                   (wb >> 2) & 0x03030303u, bx.x, bx.y);
+                    mma_u8s8_16832(dy, wa & 0x30303030u, wb & 0x30303030u, (wa >> 2) & 0x30303030u,
+                                   (wb >> 2) & 0x30303030u, by.x, by.y);
+                    if (t == 0) {
+                        yb[j * 16 + g] = (dx[0] + (dy[0] >> 4)) * 128 + (dx[1] + (dy[1] >> 4));
+                        yb[j * 16 + 8 + g] = (dx[2] + (dy[2] >> 4)) * 128 + (dx[3] + (dy[3] >> 4));
+                    }
+                }
+            }
+            __syncwarp();
+            const int j = lane >> 3, rr = 2 * (lane & 7);
+            if (j < jn) {
+                const int row = (warp + (j0 + j) * kWarps) * 16 + rr;
+                const int2 dd = *reinterpret_cast<const int2 *>(yb + j * 16 + rr);
+                const uint2 sp = *reinterpret_cast<const uint2 *>(ds + row);
+                float2 o;
+                o.x = sb_to_f32<kFp16>((uint16_t)sp.x) * ((float)dd.x * asc) +
+                      sb_to_f32<kFp16>((uint16_t)(sp.x >> 16)) * asm_;
+                o.y = sb_to_f32<kFp16>((uint16_t)sp.y) * ((float)dd.y * asc) +
+                      sb_to_f32<kFp16>((uint16_t)(sp.y >> 16)) * asm_;
+                if (!wok) o = make_float2(0.f, 0.f);
+                *reinterpret_cast<float2 *>(ypq + row) = o;
+            }
+            __syncwarp();
+        }
+    }
+    __syncthreads();
+}
+
 template <bool kFp16, int kKeysT>
 __global__ void __launch_bounds__(kThreads, 1) stack_kernel(StackArgs a) {
     extern __shared__ __align__(128) unsigned char smem[];
     const int H = a.H, I = a.I, E = a.E, K = a.K, L = a.L;
     const int G = gridDim.x, c = blockIdx.x;
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int g = lane >> 2, t = lane & 3;
-    // NB: 8-row blocks of h (phase B); NT: 16-row MMA tiles of the down slice (phase A)
-    const int ngH = H / 64, ngI = I / 64, NQ = K * ngI, NB = H / 8, NT = H / 16;
+    const int tid = threadIdx.x;
+    // NB: 8-row blocks of h (phase B)
+    const int ngH = H / 64, ngI = I / 64, NQ = K * ngI, NB = H / 8;
     const int xst = rec_stride(ngH);
     const PackDims P(H, I);
     const SmemLayout S(H, I, K, a.region);
@@ -476,117 +603,8 @@ __global__ void __launch_bounds__(kThreads, 1) stack_kernel(StackArgs a) {
         __syncthreads();
 #pragma unroll 1
         for (int q = c; q < NQ; q += G) {
-            // gate/up unit p = warp pair, H split in halves between the two warps
-            {
-                const int p = warp >> 1, half = warp & 1;
-                const bool wok = mbar_wait(&ubar[p], qphase);
-                STAMP(l, 14);
-                const unsigned char *ubase = region + (size_t)p * P.ub;
-                const uint4 *gc = reinterpret_cast<const uint4 *>(ubase);
-                const uint4 *uc = reinterpret_cast<const uint4 *>(ubase + 2 * H);
-                const uint2 *sr = reinterpret_cast<const uint2 *>(ubase + 4 * H);
-                const int nsteps = ngH >> 2;
-                const int s0 = half * nsteps / 2, s1 = (half + 1) * nsteps / 2;
-                const bool bact = rec_lane_active(lane);
-                const int part = rec_lane_part(lane);
-                float accg = 0.f, accu = 0.f;
-                if (wok) {
-#pragma unroll 1
-                    for (int j = s0; j < s1; ++j) {
-                        const int Gj = 4 * j + t;
-                        const uint4 wv = gc[j * 32 + lane], uv = uc[j * 32 + lane];
-                        const uint2 sb = sr[j * 32 + lane];
-                        int dg, du;
-                        mma_step_i8t(wv, uv, xrec + Gj, xst, bact, part, dg, du);
-                        const float sc = xscale[Gj], sm = xsum[Gj];
-                        accg += sb_to_f32<kFp16>((uint16_t)sb.x) * ((float)dg * sc) +
-                                sb_to_f32<kFp16>((uint16_t)(sb.x >> 16)) * sm;
-                        accu += sb_to_f32<kFp16>((uint16_t)sb.y) * ((float)du * sc) +
-                                sb_to_f32<kFp16>((uint16_t)(sb.y >> 16)) * sm;
-                    }
-                }
-                STAMP(l, 15);
-                accg += __shfl_xor_sync(0xffffffffu, accg, 1);
-                accu += __shfl_xor_sync(0xffffffffu, accu, 1);
-                accg += __shfl_xor_sync(0xffffffffu, accg, 2);
-                accu += __shfl_xor_sync(0xffffffffu, accu, 2);
-                if (t == 0) {
-                    red[((p * 2 + half) * 8 + g) * 2 + 0] = accg;
-                    red[((p * 2 + half) * 8 + g) * 2 + 1] = accu;
-                }
-                pair_sync(p);
-                if (half == 0 && lane < 8) {
-                    const float gs = red[((p * 2) * 8 + lane) * 2 + 0] + red[((p * 2 + 1) * 8 + lane) * 2 + 0];
-                    const float us = red[((p * 2) * 8 + lane) * 2 + 1] + red[((p * 2 + 1) * 8 + lane) * 2 + 1];
-                    const float gv = bf16r(gs), uv = bf16r(us);
-                    const float sig = bf16r(1.0f / (1.0f + expf(-gv)));
-                    const float avv = wok ? bf16r(bf16r(gv * sig) * uv) : 0.f;
-                    sact[p * 8 + lane] = f32_to_bf16_bits(avv);
-                }
-            }
-            __syncthreads();
-            STAMP(l, 3);
-            // the one record of the 64 activations
-            if (warp == 0) {
-                const uint2 qv = (lane < 16) ? reinterpret_cast<const uint2 *>(sact)[lane] : make_uint2(0u, 0u);
-                rec_from_regs(qv, lane < 16, arec, ascale, ascale + 1, 1.0f);
-            }
-            __syncthreads();
-            // down slice: split-K partial of expert k's output over all H rows. One MMA pair per
-            // 16 rows: lane (g, t) feeds word t of rows g and g+8; B columns 0 / 1 carry the
-            // record's hi / lo parts (lanes 0..7), so D columns 0 / 1 of lane quad t = 0 hold
-            // the row's integer dot. A warp runs the MMAs of up to four of its tiles, parks the
-            // 64 dots in its transpose buffer, and then every lane finishes two adjacent rows
-            // (one 8-byte scale load, one 8-byte store) instead of 8 lanes per tile.
-            {
-                const bool wok = mbar_wait(dbar, qphase);
-                STAMP(l, 10);
-                const uint32_t *dc = reinterpret_cast<const uint32_t *>(region + P.dco);
-                const uint32_t *ds = reinterpret_cast<const uint32_t *>(region + P.dso);
-                const int n = lane >> 2;
-                const uint2 bx = (lane < 8) ? arec[(0 * 4 + t) * 2 + n] : make_uint2(0u, 0u);
-                const uint2 by = (lane < 8) ? arec[(1 * 4 + t) * 2 + n] : make_uint2(0u, 0u);
-                const float asc = ascale[0], asm_ = ascale[1];
-                float *ypq = a.yp + (size_t)q * H;
-                int *yb = dtr + warp * 64;
-                const int ntw = NT / kWarps;               // tiles per warp (H is a multiple of 256)
-#pragma unroll 1
-                for (int j0 = 0; j0 < ntw; j0 += 4) {
-                    const int jn = min(4, ntw - j0);
-#pragma unroll
-                    for (int j = 0; j < 4; ++j) {
-                        if (j < jn) {                      // warp-uniform
-                            const int tile = warp + (j0 + j) * kWarps;
-                            const uint32_t wa = dc[tile * 64 + lane], wb = dc[tile * 64 + 32 + lane];
-                            int dx[4] = {0, 0, 0, 0}, dy[4] = {0, 0, 0, 0};
-                            mma_u8s8_16832(dx, wa & 0x03030303u, wb & 0x03030303u, (wa >> 2) & 0x03030303u,
-                                           (wb >> 2) & 0x03030303u, bx.x, bx.y);
-                            mma_u8s8_16832(dy, wa & 0x30303030u, wb & 0x30303030u, (wa >> 2) & 0x30303030u,
-                                           (wb >> 2) & 0x30303030u, by.x, by.y);
-                            if (t == 0) {
-                                yb[j * 16 + g] = (dx[0] + (dy[0] >> 4)) * 128 + (dx[1] + (dy[1] >> 4));
-                                yb[j * 16 + 8 + g] = (dx[2] + (dy[2] >> 4)) * 128 + (dx[3] + (dy[3] >> 4));
-                            }
-                        }
-                    }
-                    __syncwarp();
-                    const int j = lane >> 3, rr = 2 * (lane & 7);
-                    if (j < jn) {
-                        const int row = (warp + (j0 + j) * kWarps) * 16 + rr;
-                        const int2 dd = *reinterpret_cast<const int2 *>(yb + j * 16 + rr);
-                        const uint2 sp = *reinterpret_cast<const uint2 *>(ds + row);
-                        float2 o;
-                        o.x = sb_to_f32<kFp16>((uint16_t)sp.x) * ((float)dd.x * asc) +
-                              sb_to_f32<kFp16>((uint16_t)(sp.x >> 16)) * asm_;
-                        o.y = sb_to_f32<kFp16>((uint16_t)sp.y) * ((float)dd.y * asc) +
-                              sb_to_f32<kFp16>((uint16_t)(sp.y >> 16)) * asm_;
-                        if (!wok) o = make_float2(0.f, 0.f);
-                        *reinterpret_cast<float2 *>(ypq + row) = o;
-                    }
-                    __syncwarp();
-                }
-            }
-            __syncthreads();
+            run_item<kFp16>(q, l, P, region, ubar, dbar, qphase, xrec, xscale, xsum, xst, red, sact, arec, ascale, dtr,
+                            a.yp, H);
             qphase ^= 1u;
             if (q + G < NQ) issue_item(ly, P, sinds, q + G, ngI, region, ubar, dbar);
         }
@@ -656,6 +674,278 @@ __global__ void __launch_bounds__(kThreads, 1) stack_kernel(StackArgs a) {
         if (l + 1 < L) grid_sync(a.bar, nbar++);
     }
 }
+
+
+// ------------------------------------------------------------------ mixer + routed block + shared expert
+//
+// One token through L whole MoE decoder-layer halves in ONE cooperative launch (one CTA of 512
+// threads per SM, at least 128). Per layer, five grid barriers:
+//   P0a the write of the previous block into the streams and the norm's sums (f3core.cuh)   | barrier
+//   P0b the norm into shared memory; P1 mixer down + inject rows                            | barrier
+//   P2  mixer up + tail for the hidden indices j, j + G, ... this CTA owns (mixed), and their
+//       contribution to the layer's router logits: the CTA's rows of the transposed router,
+//       fetched during the previous phase B, exact products, fp64 atomics                  | barrier
+//   A   every CTA: logits -> precise softmax -> MLX-order top-k -> renorm; the routed work
+//       items' slices copied in (as stack_kernel's phase A) while the CTA runs the shared
+//       expert's gate / up rows and scalar gate groups; then the routed items (run_item) on
+//       the records of mixed                                                                | barrier
+//   B   the CTA's 8-row blocks of H: the shared down rows (scaled by the gate's sigmoid), the
+//       routed partial sums, and branch = sum_k bf16(y_k * s_k) + shared (one bf16 rounding,
+//       moe_experts_down with the shared output as its addend); the next layer's router rows
+//       are fetched                                                                          | barrier
+// The normed streams and the router rows live in the weight region, which the routed items
+// only use in phase A. After the last layer CTA 0 applies the last block's write.
+
+// device-side copy of moe_f3moe_layer (include/moe_b200.h), same layout
+struct F3MoeLayer {
+    moe_f3_layer mix;
+    const uint16_t *router_t;             // [H][E] bf16 (router transposed)
+    const unsigned char *experts;         // [E] packed experts (moe_pack_experts)
+};
+static_assert(sizeof(F3MoeLayer) == sizeof(moe_f3moe_layer), "layer descriptor layout");
+
+struct F3MoeArgs {
+    const F3MoeLayer *layers;
+    int L, H, R, Is, I, E, K;
+    float eps;
+    const uint16_t *h0, *branch0, *gate0;
+    uint16_t *state_out, *branch_out, *inj_out, *branch_all, *mixed_all;
+    uint32_t *inds_out;                   // [L][K]
+    uint16_t *scores_out;                 // [L][K]
+    moe_f3::F3Bufs bufs;
+    uint16_t *state, *branch, *inj;       // [2][4H], [2][H], [2][4] (double-buffered by layer)
+    double *acc;                          // [2][kAccCopies][E] router logit accumulators, zero at launch
+    float *yp;                            // [K][I/64][H] partial down outputs
+    unsigned int *bar;                    // grid barrier counter, zero at launch
+    unsigned int region;                  // bytes of the weight region in shared memory
+};
+
+// shared memory: the routed block's layout followed by the mixer's staging buffers, this
+// CTA's mixed values and its phase-B shared-expert outputs; inside the weight region the
+// normed streams (offset 0) and the CTA's router rows (rslice)
+struct F3MoeSmem {
+    SmemLayout S;
+    size_t sx, sv, spart, own, total, rslice;
+    MOE_HD F3MoeSmem(int H, int R, int Is, int I, int K, int G, size_t region) : S(H, I, K, region) {
+        const moe_f3::F3Smem F(H, R, Is, G, (size_t)kMaxBlocks * 8 * (Is / 64));
+        sx = al128(S.total);
+        sv = sx + (F.sv - F.sx);
+        spart = sv + (F.spart - F.sv);
+        own = spart + (F.total - F.spart);
+        total = own + al128((size_t)((H + G - 1) / G) * 4);
+        rslice = al128((size_t)moe_qlin::kHcStreams * H * 2);
+    }
+    // weight region bytes: the largest work item slice, or the normed streams + router rows
+    MOE_HD static size_t region_bytes(int H, int I, int E, int G) {
+        const size_t item = (size_t)PackDims(H, I).gbytes;
+        const size_t mix = al128((size_t)moe_qlin::kHcStreams * H * 2) + (size_t)((H + G - 1) / G) * E * 2;
+        return item > mix ? item : mix;
+    }
+};
+
+template <bool kFp16Mix, bool kFp16Exp>
+__global__ void __launch_bounds__(kThreads, 1) f3moe_kernel(F3MoeArgs a) {
+    using namespace moe_f3;
+    extern __shared__ __align__(128) unsigned char smem[];
+    const int H = a.H, I = a.I, E = a.E, K = a.K, L = a.L, W = kHcStreams * H;
+    const int G = gridDim.x, c = blockIdx.x, tid = threadIdx.x;
+    const int ngH = H / 64, ngI = I / 64, NQ = K * ngI, NB = H / 8;
+    const int xst = rec_stride(ngH);
+    const PackDims P(H, I);
+    const F3MoeSmem M(H, a.R, a.Is, I, K, G, a.region);
+    const SmemLayout &S = M.S;
+    const int b0 = (int)((long long)c * NB / G), nb = (int)((long long)(c + 1) * NB / G) - b0;
+    const int nrows = nb * 8;
+
+    uint64_t *ubar = reinterpret_cast<uint64_t *>(smem + S.bars);          // [kUnits]
+    uint64_t *dbar = ubar + kUnits;                                         // [1]
+    uint64_t *rbar = dbar + 1;                                              // [1]
+    unsigned char *region = smem + S.region;
+    uint2 *xrec = reinterpret_cast<uint2 *>(smem + S.xrec);                // [16][xst]
+    float *xscale = reinterpret_cast<float *>(smem + S.xscale);
+    float *xsum = reinterpret_cast<float *>(smem + S.xsum);
+    uint2 *arec = reinterpret_cast<uint2 *>(smem + S.arec);
+    float *ascale = reinterpret_cast<float *>(smem + S.ascale);
+    uint16_t *sact = reinterpret_cast<uint16_t *>(smem + S.sact);
+    float *ypart = reinterpret_cast<float *>(smem + S.ypart);
+    float *red = reinterpret_cast<float *>(smem + S.red);
+    uint32_t *cand = reinterpret_cast<uint32_t *>(smem + S.cand);
+    uint32_t *comp = reinterpret_cast<uint32_t *>(smem + S.comp);
+    uint32_t *redu = reinterpret_cast<uint32_t *>(smem + S.redu);
+    double *redd = reinterpret_cast<double *>(smem + S.redd);
+    uint32_t *sinds = reinterpret_cast<uint32_t *>(smem + S.sinds);
+    float *sscores = reinterpret_cast<float *>(smem + S.sscores);
+    int *dtr = reinterpret_cast<int *>(smem + S.dtr);
+    float *own = reinterpret_cast<float *>(smem + M.own);                  // this CTA's mixed values
+    unsigned char *rslice = region + M.rslice;                              // [nh][E] router rows
+    __shared__ float srs[kHcStreams];
+    F3Phases<kFp16Mix> f(H, a.R, a.Is, a.bufs, region, smem + M.sx, smem + M.sv, smem + M.spart, srs);
+
+    if (tid == 0) {
+        for (int i = 0; i < kUnits + 2; ++i) mbar_init(&ubar[i], 1);
+        fence_barrier_init();
+    }
+    __syncthreads();
+
+    unsigned int nbar = 0;
+    uint32_t rphase = 0, qphase = 0;
+    const uint32_t rrow = (uint32_t)E * 2u;
+    // this CTA's rows of layer l's transposed router (hidden indices c, c + G, ...)
+    auto fetch_router_rows = [&](int l) {
+        if (tid == 0 && f.nh > 0) {
+            mbar_arrive_expect_tx(rbar, rrow * (uint32_t)f.nh);
+#pragma unroll 1
+            for (int q = 0; q < f.nh; ++q)
+                tma_load_1d(rslice + (size_t)q * rrow, a.layers[l].router_t + (size_t)(c + q * G) * E, rrow, rbar);
+        }
+    };
+    fetch_router_rows(0);
+    f.prefetch_mixer_down(a.layers[0].mix);
+
+#pragma unroll 1
+    for (int l = 0; l < L; ++l) {
+        const F3MoeLayer &ly = a.layers[l];
+        const moe_f3_layer &Ly = ly.mix;
+        const uint16_t *hin = l == 0 ? a.h0 : a.state + (size_t)(l & 1) * W;
+        const uint16_t *br = l == 0 ? a.branch0 : a.branch + (size_t)((l - 1) & 1) * H;
+        const uint16_t *gt = l == 0 ? a.gate0 : a.inj + (size_t)((l - 1) & 1) * kHcStreams;
+        uint16_t *wout = a.state + (size_t)((l + 1) & 1) * W;
+        double *accl = a.acc + (size_t)(l & 1) * kAccCopies * E;
+
+        // ---------------------------------------------------------- P0a, P0b + P1, P2
+        f.write_and_sums(hin, br, gt, wout);
+        grid_sync(a.bar, nbar++);
+        f.norm(Ly, wout, a.eps);
+        f.mixer_down(Ly);
+        grid_sync(a.bar, nbar++);
+        f.mixer_up(Ly, a.inj + (size_t)(l & 1) * kHcStreams, own);
+        __syncthreads();
+        if (a.mixed_all)
+            for (int q = tid; q < f.nh; q += kThreads) a.mixed_all[(size_t)l * H + c + q * G] = f32_to_bf16_bits(own[q]);
+        if (f.nh > 0) router_partial(rbar, rphase, rslice, own, f.nh, E, accl + (size_t)(c % kAccCopies) * E);
+        grid_sync(a.bar, nbar++);
+
+        // ---------------------------------------------------------- phase A
+        double av[1] = {0.0};
+        if (tid < E) {
+#pragma unroll
+            for (int r = 0; r < kAccCopies; ++r) av[0] += __ldcg(accl + (size_t)r * E + tid);
+        }
+        uint2 hq[kHPass];
+#pragma unroll
+        for (int p = 0; p < kHPass; ++p) {
+            const int Gp = (tid >> 4) + p * (kThreads / 16);
+            hq[p] = (Gp < ngH) ? __ldcg(reinterpret_cast<const uint2 *>(a.bufs.mixed + (size_t)Gp * 64) + (tid & 15))
+                               : make_uint2(0u, 0u);
+        }
+        route<1>(av, 1.0, E, K, redu, redd, cand, comp, sinds, sscores);
+        if (c == 0 && tid < K) {
+            a.inds_out[(size_t)l * K + tid] = sinds[tid];
+            a.scores_out[(size_t)l * K + tid] = f32_to_bf16_bits(sscores[tid]);
+        }
+        const StackLayer sl{ly.router_t, ly.experts};
+        if (c < NQ) issue_item(sl, P, sinds, c, ngI, region, ubar, dbar);
+        // records of mixed while the copies are in flight; the shared expert's gate / up rows
+#pragma unroll
+        for (int p = 0; p < kHPass; ++p) {
+            const int Gp = (tid >> 4) + p * (kThreads / 16);
+            if (p * (kThreads / 16) < ngH) rec_from_regs(hq[p], Gp < ngH, xrec + Gp, xscale + Gp, xsum + Gp, 1.0f, xst);
+        }
+        stage_l2(f.sx, a.bufs.mixed, H);
+        __syncthreads();
+        f.shared_gate_up(Ly, false);
+        __syncthreads();
+#pragma unroll 1
+        for (int q = c; q < NQ; q += G) {
+            run_item<kFp16Exp>(q, l, P, region, ubar, dbar, qphase, xrec, xscale, xsum, xst, red, sact, arec, ascale,
+                               dtr, a.yp, H);
+            qphase ^= 1u;
+            if (q + G < NQ) issue_item(sl, P, sinds, q + G, ngI, region, ubar, dbar);
+        }
+        grid_sync(a.bar, nbar++);
+
+        // ---------------------------------------------------------- phase B
+        if (l + 1 < L) fetch_router_rows(l + 1);      // the region is free until the next phase A
+        const float gsig = f.stage_down();
+        f.shared_down_items(Ly, b0 * 8, 1, nrows, false);
+#pragma unroll 1
+        for (int x = tid; x < K * nrows; x += kThreads) {
+            const int k = x / nrows, r = x % nrows;
+            const float *src = a.yp + (size_t)k * ngI * H + b0 * 8 + r;
+            float v[16];
+            float yk = 0.f;
+#pragma unroll 1
+            for (int g0 = 0; g0 < ngI; g0 += 16) {
+#pragma unroll
+                for (int i = 0; i < 16; ++i) v[i] = (g0 + i < ngI) ? __ldcg(src + (size_t)(g0 + i) * H) : 0.f;
+#pragma unroll
+                for (int i = 0; i < 16; ++i)
+                    if (g0 + i < ngI) yk += v[i];
+            }
+            ypart[k * nrows + r] = bf16r(yk);
+        }
+        __syncthreads();
+        uint16_t *bro = a.branch + (size_t)(l & 1) * H;
+#pragma unroll 1
+        for (int r = tid; r < nrows; r += kThreads) {
+            const int row = b0 * 8 + r;
+            float accv = 0.f;
+#pragma unroll 4
+            for (int k = 0; k < K; ++k) {
+                const float pk = bf16r(ypart[k * nrows + r] * sscores[k]);
+                accv = (k == 0) ? pk : bf16r(accv + pk);
+            }
+            accv = bf16r(accv + bf16_bits_to_f32(f.shared_down_out(r, gsig)));
+            const uint16_t hb = f32_to_bf16_bits(accv);
+            bro[row] = hb;
+            if (a.branch_all) a.branch_all[(size_t)l * H + row] = hb;
+        }
+        if (l + 1 < L) f.prefetch_mixer_down(a.layers[l + 1].mix);
+        if (c == 0) {   // layer l's logits were consumed in phase A; ready the buffer for l + 2
+            double *accz = a.acc + (size_t)(l & 1) * kAccCopies * E;
+#pragma unroll 1
+            for (int e = tid; e < kAccCopies * E; e += kThreads) accz[e] = 0.0;
+        }
+        grid_sync(a.bar, nbar++);
+    }
+
+    // the last block's write into the state, and the last block output and gate
+    if (c == 0) {
+        const int l = L - 1;
+        const uint16_t *st = a.state + (size_t)((l + 1) & 1) * W;
+        const uint16_t *br = a.branch + (size_t)(l & 1) * H;
+        const uint16_t *gt = a.inj + (size_t)(l & 1) * kHcStreams;
+        for (int q = tid; q < W; q += kThreads) {
+            const int cc = q / H, i = q - cc * H;
+            const float gv = bf16_bits_to_f32(__ldcg(gt + cc));
+            const float p = bf16r(__fmul_rn(bf16_bits_to_f32(__ldcg(br + i)), gv));
+            a.state_out[q] = f32_to_bf16_bits(bf16r(__fadd_rn(bf16_bits_to_f32(__ldcg(st + q)), p)));
+        }
+        for (int q = tid; q < H; q += kThreads) a.branch_out[q] = __ldcg(br + q);
+        if (tid < kHcStreams && a.inj_out) a.inj_out[tid] = __ldcg(gt + tid);
+    }
+}
+
+struct F3MoeWs {
+    size_t acc, bar, dv, iv, ssum, gsum, mixed, act, state, branch, inj, yp, total, zero;
+    F3MoeWs(int H, int R, int Is, int I, int E, int K) {
+        const size_t W = (size_t)moe_qlin::kHcStreams * H;
+        acc = 0;
+        bar = acc + al256((size_t)2 * kAccCopies * E * 8);
+        zero = bar + 256;                                // acc + barrier: zero before every launch
+        dv = zero;
+        iv = dv + al256((size_t)R * 4);
+        ssum = iv + al256(moe_qlin::kHcStreams * 4);
+        gsum = ssum + al256(moe_qlin::kHcStreams * 32 * 8);
+        mixed = gsum + al256((size_t)(H / 64) * 8);
+        act = mixed + al256((size_t)H * 2);
+        state = act + al256((size_t)Is * 2);
+        branch = state + al256(2 * W * 2);
+        inj = branch + al256(2 * (size_t)H * 2);
+        yp = inj + 256;
+        total = yp + al256((size_t)K * (I / 64) * H * 4);
+    }
+};
 
 struct StackWs {
     double *acc, *ss;
@@ -735,6 +1025,84 @@ extern "C" int moe_stack_decode(const void *layers, int L, int H, int I, int E, 
         set_dev[ki] = dev;
     }
     MOE_CUDA_TRY(cudaLaunchCooperativeKernel(kern, dim3(G), dim3(kThreads), kargs, S.total, st));
+    return MOE_OK;
+}
+
+extern "C" size_t moe_f3moe_stack_workspace_bytes(int H, int R, int Is, int I, int E, int K) {
+    if (H <= 0 || R <= 0 || Is <= 0 || I <= 0 || E <= 0 || K <= 0) return 0;
+    return F3MoeWs(H, R, Is, I, E, K).total;
+}
+
+extern "C" int moe_f3moe_stack_decode(const void *layers, int L, int H, int R, int Is, int I, int E, int K,
+                                      int sb_fp16_mix, int sb_fp16_experts, float eps, const void *h,
+                                      const void *branch0, const void *gate0, void *state_out, void *branch_out,
+                                      void *inj_out, uint32_t *inds_out, void *scores_out, void *branch_all,
+                                      void *mixed_all, void *workspace, size_t workspace_bytes, int num_ctas,
+                                      void *stream) {
+    if (!layers || !h || !state_out || !branch_out || !inds_out || !scores_out || !workspace)
+        return moe_set_error(MOE_EINVAL, "f3moe_stack_decode: null pointer");
+    if (L <= 0 || H % 256 || H > kMaxH || R <= 0 || R % 64 || Is <= 0 || Is % 64 || I <= 0 || I % 64 || E <= 0 ||
+        E % 8 || E > kThreads || K <= 0 || K > kMaxK || K > E)
+        return moe_set_error(MOE_EINVAL, "f3moe_stack_decode: bad sizes L=%d H=%d R=%d Is=%d I=%d E=%d K=%d", L, H, R, Is,
+                             I, E, K);
+    if ((branch0 == nullptr) != (gate0 == nullptr))
+        return moe_set_error(MOE_EINVAL, "f3moe_stack_decode: the first write needs both branch and gate");
+    if (!(eps >= 0.f)) return moe_set_error(MOE_EINVAL, "f3moe_stack_decode: eps must be >= 0");
+    const F3MoeWs w(H, R, Is, I, E, K);
+    if (workspace_bytes < w.total)
+        return moe_set_error(MOE_EINVAL, "f3moe_stack_decode: workspace of %zu bytes needed, %zu given", w.total,
+                             workspace_bytes);
+    const void *bufs[] = {h, branch0, state_out, branch_out, workspace, branch_all, mixed_all};
+    for (const void *p : bufs)
+        if (reinterpret_cast<uintptr_t>(p) % 16)
+            return moe_set_error(MOE_EINVAL, "f3moe_stack_decode: buffers must be 16-byte aligned");
+    int dev = 0, sms = 0;
+    MOE_CUDA_TRY(cudaGetDevice(&dev));
+    MOE_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+    const int G = num_ctas > 0 ? (num_ctas < sms ? num_ctas : sms) : sms;
+    if (G < moe_qlin::kHcStreams * 32)
+        return moe_set_error(MOE_EINVAL, "f3moe_stack_decode: %d CTAs (the norm takes %d)", G,
+                             moe_qlin::kHcStreams * 32);
+    if ((H / 8 + G - 1) / G > kMaxBlocks)
+        return moe_set_error(MOE_EINVAL, "f3moe_stack_decode: %d CTAs too few for %d row blocks", G, H / 8);
+    const size_t region = F3MoeSmem::region_bytes(H, I, E, G);
+    const F3MoeSmem M(H, R, Is, I, K, G, region);
+    if (M.total > 227 * 1024)
+        return moe_set_error(MOE_EINVAL, "f3moe_stack_decode: %zu bytes of shared memory needed", M.total);
+    auto st = as_stream(stream);
+    MOE_CUDA_TRY(cudaMemsetAsync(workspace, 0, w.zero, st));
+    char *p = static_cast<char *>(workspace);
+    F3MoeArgs a{};
+    a.layers = static_cast<const F3MoeLayer *>(layers);
+    a.L = L, a.H = H, a.R = R, a.Is = Is, a.I = I, a.E = E, a.K = K, a.eps = eps;
+    a.h0 = static_cast<const uint16_t *>(h);
+    a.branch0 = static_cast<const uint16_t *>(branch0);
+    a.gate0 = static_cast<const uint16_t *>(gate0);
+    a.state_out = static_cast<uint16_t *>(state_out);
+    a.branch_out = static_cast<uint16_t *>(branch_out);
+    a.inj_out = static_cast<uint16_t *>(inj_out);
+    a.branch_all = static_cast<uint16_t *>(branch_all);
+    a.mixed_all = static_cast<uint16_t *>(mixed_all);
+    a.inds_out = inds_out;
+    a.scores_out = static_cast<uint16_t *>(scores_out);
+    a.bufs.dv = reinterpret_cast<float *>(p + w.dv);
+    a.bufs.iv = reinterpret_cast<float *>(p + w.iv);
+    a.bufs.ssum = reinterpret_cast<double *>(p + w.ssum);
+    a.bufs.gsum = reinterpret_cast<double *>(p + w.gsum);
+    a.bufs.mixed = reinterpret_cast<uint16_t *>(p + w.mixed);
+    a.bufs.act = reinterpret_cast<uint16_t *>(p + w.act);
+    a.state = reinterpret_cast<uint16_t *>(p + w.state);
+    a.branch = reinterpret_cast<uint16_t *>(p + w.branch);
+    a.inj = reinterpret_cast<uint16_t *>(p + w.inj);
+    a.acc = reinterpret_cast<double *>(p + w.acc);
+    a.yp = reinterpret_cast<float *>(p + w.yp);
+    a.bar = reinterpret_cast<unsigned int *>(p + w.bar);
+    a.region = (unsigned int)region;
+    void *kern = sb_fp16_mix ? (sb_fp16_experts ? (void *)f3moe_kernel<true, true> : (void *)f3moe_kernel<true, false>)
+                             : (sb_fp16_experts ? (void *)f3moe_kernel<false, true> : (void *)f3moe_kernel<false, false>);
+    MOE_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)M.total));
+    void *kargs[] = {&a};
+    MOE_CUDA_TRY(cudaLaunchCooperativeKernel(kern, dim3(G), dim3(kThreads), kargs, M.total, st));
     return MOE_OK;
 }
 

@@ -437,6 +437,95 @@ def prefill_layer(x: torch.Tensor, router: torch.Tensor, gate: QMatrix, up: QMat
 
 # ----------------------------------------------------------------------------- mixer + shared, all layers
 
+def f3_layer_rows(layers: list[dict], device):
+    """Checks mixer + shared-expert layers (F3Stack's dict form) and returns (H, R, I, sb_fp16,
+    rows): rows[l] = the 22 device pointers of moe_f3_layer (norm weight, then codes, scales,
+    biases of down, up, inject (0 when absent), shared gate, up, down and the scalar gate)."""
+    ly0 = layers[0]
+    R, W = ly0["down"].w.shape[0], ly0["down"].w.shape[1] * 32 // ly0["down"].bits
+    H, I = W // 4, ly0["sg"].w.shape[0]
+    sbs = set()
+    rows = []
+    for ly in layers:
+        want = {"down": (8, R, W), "up": (8, W, R), "inj": (8, 4, W), "sg": (4, I, H), "su": (4, I, H),
+                "sd": (4, H, I), "se": (8, 1, H)}
+        if ly["nw"].data_ptr() % 16:
+            raise ValueError("f3 layer: norm weight must be 16-byte aligned")
+        ptrs = [ly["nw"].data_ptr()]
+        for k in F3Stack.KEYS:
+            q = ly.get(k)
+            if q is None:
+                if k != "inj":
+                    raise ValueError(f"f3 layer: {k} missing")
+                ptrs += [0, 0, 0]
+                continue
+            bits, n, kin = want[k]
+            if q.bits != bits or q.group_size != 64 or q.w.shape[0] != n or q.w.shape[1] * 32 // q.bits != kin:
+                raise ValueError(f"f3 layer: {k} must be {bits}-bit g64 [{n}, {kin}]")
+            q.check(k, device)
+            sbs.add(q.sb_fp16)
+            ptrs += [q.w.data_ptr(), q.s.data_ptr(), q.b.data_ptr()]
+        rows.append(ptrs)
+    if len(sbs) != 1:
+        raise ValueError("f3 layers: one scale dtype expected")
+    return H, R, I, sbs.pop(), rows
+
+
+class F3MoeStack:
+    """The MoE half of every decoder layer for a decode token, all layers in ONE launch
+    (moe_f3moe_stack_decode): per layer the hyper-connection mixer with the previous block's
+    write, the routed block on the mixer output (router, precise softmax, MLX-order top-k,
+    renorm, experts) and the shared expert, the block output being the routed combine with the
+    shared output as its addend (loader.py:909-914). mix_layers: F3Stack's dicts; routed:
+    ExpertLayer per layer (router [E, H] bf16, 2-bit g64 experts), packed once here."""
+
+    def __init__(self, mix_layers: list[dict], routed: list, top_k: int, device, eps: float = 1e-6,
+                 num_ctas: int = 0):
+        from .stack import pack_layer_experts
+        if len(mix_layers) != len(routed):
+            raise ValueError("one routed layer per mixer layer expected")
+        self.device = torch.device(device)
+        self.L, self.K = len(routed), int(top_k)
+        self.eps, self.num_ctas = float(eps), int(num_ctas)
+        self.H, self.R, self.Is, self.sb_mix, rows = f3_layer_rows(mix_layers, self.device)
+        self.E, H = routed[0].router.shape
+        self.I = routed[0].gate.w.shape[1]
+        if H != self.H:
+            raise ValueError(f"routed layers of H={H}, mixer layers of H={self.H}")
+        self.sb_exp = routed[0].gate.sb_fp16
+        self.router_t = [ly.router.t().contiguous() for ly in routed]
+        self.packed = [pack_layer_experts(ly, self.device) for ly in routed]
+        self.mix_layers = mix_layers                   # the table points into these tensors
+        table = [r + [rt.data_ptr(), pk.data_ptr()] for r, rt, pk in zip(rows, self.router_t, self.packed)]
+        self.table = torch.tensor(table, dtype=torch.int64, device=self.device)
+        nb = int(call("moe_f3moe_stack_workspace_bytes", self.H, self.R, self.Is, self.I, self.E, self.K))
+        self.ws = torch.empty(nb, dtype=torch.uint8, device=self.device)
+        self.launches_per_step = 1
+
+    def decode(self, h: torch.Tensor, branch=None, gate=None, *, want_all: bool = False, out=None, stream=None):
+        """h bf16 [4H]; branch / gate: the pending write (bf16 [H] / [4]) or None. Returns a dict:
+        state [4H] (after the last block's write), branch [H] and inj [4] (the last block output
+        and its gate), inds [L, K] / scores [L, K] (every layer's routing), and with want_all
+        branch_all [L, H] and mixed_all [L, H] (every layer's block output and block input)."""
+        _need(h, "h", (torch.bfloat16,), self.device)
+        o = out if out is not None else {}
+        dv, bf = self.device, torch.bfloat16
+        st = o.setdefault("state", torch.empty(4 * self.H, dtype=bf, device=dv))
+        br = o.setdefault("branch", torch.empty(self.H, dtype=bf, device=dv))
+        inj = o.setdefault("inj", torch.empty(4, dtype=bf, device=dv))
+        inds = o.setdefault("inds", torch.empty((self.L, self.K), dtype=torch.int32, device=dv))
+        scores = o.setdefault("scores", torch.empty((self.L, self.K), dtype=bf, device=dv))
+        ball = mall = None
+        if want_all:
+            ball = o.setdefault("branch_all", torch.empty((self.L, self.H), dtype=bf, device=dv))
+            mall = o.setdefault("mixed_all", torch.empty((self.L, self.H), dtype=bf, device=dv))
+        call("moe_f3moe_stack_decode", self.table.data_ptr(), self.L, self.H, self.R, self.Is, self.I, self.E, self.K,
+             int(self.sb_mix), int(self.sb_exp), self.eps, h.data_ptr(), _ptr(branch), _ptr(gate), st.data_ptr(),
+             br.data_ptr(), inj.data_ptr(), inds.data_ptr(), scores.data_ptr(), _ptr(ball), _ptr(mall),
+             self.ws.data_ptr(), self.ws.numel(), self.num_ctas, _stream(stream))
+        return o
+
+
 class F3Stack:
     """The step in front of every MoE block for a decode token, all layers in one launch
     (moe_f3_stack_decode): per layer the hyper-connection mixer with the previous block's write
@@ -450,35 +539,8 @@ class F3Stack:
     def __init__(self, layers: list[dict], device, eps: float = 1e-6, num_ctas: int = 0):
         self.device = torch.device(device)
         self.L = len(layers)
-        ly0 = layers[0]
-        R, W = ly0["down"].w.shape[0], ly0["down"].w.shape[1] * 32 // ly0["down"].bits
-        self.H, self.R, self.I = W // 4, R, ly0["sg"].w.shape[0]
         self.eps, self.num_ctas = float(eps), int(num_ctas)
-        sbs = set()
-        rows = []
-        for ly in layers:
-            want = {"down": (8, R, W), "up": (8, W, R), "inj": (8, 4, W), "sg": (4, self.I, self.H),
-                    "su": (4, self.I, self.H), "sd": (4, self.H, self.I), "se": (8, 1, self.H)}
-            if ly["nw"].data_ptr() % 16:
-                raise ValueError("f3 layer: norm weight must be 16-byte aligned")
-            ptrs = [ly["nw"].data_ptr()]
-            for k in self.KEYS:
-                q = ly.get(k)
-                if q is None:
-                    if k != "inj":
-                        raise ValueError(f"f3 layer: {k} missing")
-                    ptrs += [0, 0, 0]
-                    continue
-                bits, n, kin = want[k]
-                if q.bits != bits or q.group_size != 64 or q.w.shape[0] != n or q.w.shape[1] * 32 // q.bits != kin:
-                    raise ValueError(f"f3 layer: {k} must be {bits}-bit g64 [{n}, {kin}]")
-                q.check(k, self.device)
-                sbs.add(q.sb_fp16)
-                ptrs += [q.w.data_ptr(), q.s.data_ptr(), q.b.data_ptr()]
-            rows.append(ptrs)
-        if len(sbs) != 1:
-            raise ValueError("f3 layers: one scale dtype expected")
-        self.sb_fp16 = sbs.pop()
+        self.H, self.R, self.I, self.sb_fp16, rows = f3_layer_rows(layers, self.device)
         self.layers = layers                       # the table points into these tensors
         self.table = torch.tensor(rows, dtype=torch.int64, device=self.device)
         nb = int(call("moe_f3_stack_workspace_bytes", self.H, self.R, self.I))
