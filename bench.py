@@ -46,12 +46,13 @@ def parse():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
-    ap.add_argument("--config", choices=["c1", "c2", "c3", "c3n", "c4", "p1", "f3"], default="c1",
+    ap.add_argument("--config", choices=["c1", "c2", "c3", "c3n", "c4", "p1", "f3", "f3moe"], default="c1",
                     help="c1: resident stack (the headline); c2: offload stack with the LRU slot caches; "
                          "c3: 2048-token prefill through the resident 28-layer stack; c3n: the Nemotron-shaped "
                          "prefill layer (240 experts, top-9, 1024 tokens); c4: expert-parallel decode (experts "
                          "split across the ranks); p1: the P1 I/O scheduler filling c2-shaped expert slots; f3: the "
-                         "hyper-connection mixer + shared expert in front of each of the 28 MoE blocks, decode")
+                         "hyper-connection mixer + shared expert in front of each of the 28 MoE blocks, decode; "
+                         "f3moe: the mixer, the routed block and the shared expert of all 28 layers in one launch")
     ap.add_argument("--batch", type=int, default=0, help="c4: tokens per step (default: 8 per GPU; 4096 = c4's prefill)")
     ap.add_argument("--replicas", action="store_true",
                     help="--gpus N > 1: N independent replicas of the c1 stack instead of expert parallelism")
@@ -427,6 +428,25 @@ def run_p1(args, rank: int, world: int, local_rank: int) -> None:
     print(json.dumps(line), flush=True)
 
 
+def f3_mix_layers(dev, g, L, HC, H, R, I):
+    """Synthetic mixer + shared-expert weights of L layers (8-bit g64 mixer down / up / inject,
+    4-bit g64 shared gate / up / down, an 8-bit scalar gate; bf16 scales and biases)."""
+    import torch
+
+    from moe_offload_b200.ops import QMatrix
+
+    def qm(N, K, bits, scale):
+        w = torch.randint(-(2 ** 31), 2 ** 31 - 1, (N, K * bits // 32), dtype=torch.int32, device=dev, generator=g)
+        sc = (torch.rand((N, K // 64), device=dev, generator=g) * scale + scale / 10).to(torch.bfloat16)
+        b = (torch.randn((N, K // 64), device=dev, generator=g) * scale * 4).to(torch.bfloat16)
+        return QMatrix(w, sc, b, bits, 64)
+
+    return [{"nw": (torch.randn(HC * H, device=dev, generator=g) * 0.05).to(torch.bfloat16),
+             "down": qm(R, HC * H, 8, 2e-4), "up": qm(HC * H, R, 8, 2e-3), "inj": qm(HC, HC * H, 8, 2e-4),
+             "sg": qm(I, H, 4, 2e-3), "su": qm(I, H, 4, 2e-3), "sd": qm(H, I, 4, 2e-3), "se": qm(1, H, 8, 2e-4)}
+            for _ in range(L)]
+
+
 def run_f3(args, rank: int, world: int, local_rank: int) -> None:
     """The step in front of every MoE block, decode (one token): the hyper-connection mixer
     (run_hc with a write: 4 streams of H = 3072, rank 320, 8-bit g64 down / up / inject) and the
@@ -450,19 +470,7 @@ def run_f3(args, rank: int, world: int, local_rank: int) -> None:
     L, HC, H, R, I = 28, 4, 3072, 320, 768
     g = torch.Generator(device=dev)
     g.manual_seed(3)
-
-    def qm(N, K, bits, scale):
-        w = torch.randint(-(2 ** 31), 2 ** 31 - 1, (N, K * bits // 32), dtype=torch.int32, device=dev, generator=g)
-        sc = (torch.rand((N, K // 64), device=dev, generator=g) * scale + scale / 10).to(torch.bfloat16)
-        b = (torch.randn((N, K // 64), device=dev, generator=g) * scale * 4).to(torch.bfloat16)
-        return QMatrix(w, sc, b, bits, 64)
-
-    layers = []
-    for _ in range(L):
-        layers.append({"nw": (torch.randn(HC * H, device=dev, generator=g) * 0.05).to(torch.bfloat16),
-                       "down": qm(R, HC * H, 8, 2e-4), "up": qm(HC * H, R, 8, 2e-3), "inj": qm(HC, HC * H, 8, 2e-4),
-                       "sg": qm(I, H, 4, 2e-3), "su": qm(I, H, 4, 2e-3), "sd": qm(H, I, 4, 2e-3),
-                       "se": qm(1, H, 8, 2e-4)})
+    layers = f3_mix_layers(dev, g, L, HC, H, R, I)
     wbytes = sum(m.w.numel() * 4 + m.s.numel() * 4 for lay in layers for m in lay.values() if isinstance(m, QMatrix))
     h = (torch.randn(HC * H, device=dev, generator=g) * 0.3).to(torch.bfloat16)
     br = (torch.randn(H, device=dev, generator=g) * 0.3).to(torch.bfloat16)
@@ -572,6 +580,164 @@ def run_f3(args, rank: int, world: int, local_rank: int) -> None:
                          "frac": round(achieved / peak, 4), "traffic": None,
                          "algorithmic_bytes_per_step": wbytes, "peak_source": src},
             "clocks": clocks, "gpu_launches": args.steps, "e2e": e2e, "cpu_baseline": cpu}
+    del graph, gchain
+    print(json.dumps(line), flush=True)
+
+
+def run_f3moe(args, rank: int, world: int, local_rank: int) -> None:
+    """The whole MoE half of every decoder layer at decode (one token), fused: the f3 step
+    (hyper-connection mixer with the previous block's write, 4 streams of H = 3072, rank 320,
+    8-bit; shared expert I = 768 4-bit with an 8-bit scalar gate) and the c1 routed block (512
+    experts top-10, I = 768, 2-bit g64 fp16 scales, bf16 router) on the mixer output, combined
+    as moe_experts_down with the shared output as its addend, for 28 chained layers. The step is
+    ONE launch of moe_f3moe_stack_decode (five grid barriers per layer); the same chain as
+    per-layer launches (moe_hc_mix, moe_router_topk, moe_shared_expert, moe_experts_gateup,
+    moe_experts_down: 8 kernels per layer, one CUDA graph) is timed beside it. roofline =
+    algorithmic bytes per token (mixer + shared weights, the router and the 10 routed experts'
+    bytes of every layer) / step time against the HBM peak; e2e adds the pinned host copies of
+    the token's streams in and the last block output out."""
+    import numpy as np
+    import torch
+
+    from moe_offload_b200 import ops
+    from moe_offload_b200._lib import call
+    from moe_offload_b200.ops import QMatrix
+    from moe_offload_b200.synthetic import C1, dev_stack
+
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    L = args.layers or C1.layers
+    HC, H, R, Is, K = 4, C1.hidden, 320, 768, C1.top_k
+    g = torch.Generator(device=dev)
+    g.manual_seed(3)
+    mix = f3_mix_layers(dev, g, L, HC, H, R, Is)
+    routed = dev_stack(C1, dev, layers=L)
+    E, I = C1.experts, C1.inter
+    mix_bytes = sum(m.w.numel() * 4 + m.s.numel() * 4 for lay in mix for m in lay.values() if isinstance(m, QMatrix))
+    routed_bytes = L * (K * int(call("moe_packed_expert_bytes", H, I)) + E * H * 2)
+    wbytes = mix_bytes + routed_bytes
+    resident_gb = (mix_bytes + L * E * int(call("moe_packed_expert_bytes", H, I))) / 1e9
+    h = (torch.randn(HC * H, device=dev, generator=g) * 0.3).to(torch.bfloat16)
+    br = (torch.randn(H, device=dev, generator=g) * 0.3).to(torch.bfloat16)
+    gt = (torch.randn(HC, device=dev, generator=g) * 0.5).to(torch.bfloat16)
+    st = torch.cuda.Stream(dev)
+    stack = ops.F3MoeStack(mix, routed, K, dev)
+    out, chain_out = {}, {}
+    r_out = [{} for _ in range(L)]
+
+    def step():
+        stack.decode(h, br, gt, out=out, stream=st)
+
+    def step_chain():
+        state, write = h.view(1, -1), (br.view(1, -1), gt.view(1, -1))
+        inds = []
+        for lay, rl, ro in zip(mix, routed, r_out):
+            mixed, written, inj = ops.hc_mix(state, lay["nw"], lay["down"], lay["up"], lay["inj"], write=write,
+                                             stream=st)
+            r = ops.router_topk(mixed, rl.router, K, out=ro, stream=st)
+            sh = ops.shared_expert(mixed, lay["sg"], lay["su"], lay["sd"], lay["se"], stream=st)
+            act = ops.experts_gateup(mixed, r["inds"], rl.gate, rl.up, stream=st)
+            y, _ = ops.experts_down(act, r["inds"], rl.down, r["scores"], addend=sh, stream=st)
+            inds.append(r["inds"])
+            state, write = written, (y, inj)
+        chain_out["branch"] = write[0]
+        chain_out["inds"] = inds
+
+    def timed(graph, n):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(st)
+        for _ in range(n):
+            graph.replay()
+        e1.record(st)
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / n
+
+    with torch.cuda.stream(st):
+        step()
+        step_chain()
+        torch.cuda.synchronize()
+        gchain = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gchain, stream=st):
+            step_chain()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=st):
+            step()
+        for _ in range(args.warmup):
+            gchain.replay()
+            graph.replay()
+        torch.cuda.synchronize()
+        ci = torch.stack([x.view(-1) for x in chain_out["inds"]])
+        layers_same = int((ci == out["inds"]).all(dim=1).sum())
+        rel = float((out["branch"].float() - chain_out["branch"].view(-1).float()).norm() /
+                    chain_out["branch"].float().norm())
+        chain_ms = timed(gchain, args.steps)
+        clk = ClockSampler(local_rank)
+        clk.start()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(st)
+        for _ in range(args.steps):
+            graph.replay()
+        e1.record(st)
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / args.steps
+        dev_err = int(call("moe_device_error", 1))
+        e2e = None
+        if not args.no_e2e:
+            hp = torch.empty(HC * H, dtype=torch.bfloat16).pin_memory()
+            hp.copy_(h.cpu())
+            op = torch.empty(H, dtype=torch.bfloat16).pin_memory()
+            t0 = time.perf_counter()
+            for _ in range(args.steps):
+                h.copy_(hp, non_blocking=True)
+                graph.replay()
+                op.copy_(out["branch"], non_blocking=True)
+                st.synchronize()
+            dt = time.perf_counter() - t0
+            e2e = {"value": round(args.steps / dt, 2), "unit": "tok/s", "h2d_bytes_per_step": hp.numel() * 2,
+                   "d2h_bytes_per_step": op.numel() * 2}
+        clocks = clk.stop()
+    peak, src = peaks()
+    achieved = wbytes / (ms / 1000.0) / 1e9
+    cpu = None
+    if not args.no_cpu:
+        from oracle import oracle as orc
+        lay = mix[0]
+        tonp = lambda m: (m.w.cpu().numpy().view(np.uint32), m.s.view(torch.int16).cpu().numpy().view(np.uint16),
+                          m.b.view(torch.int16).cpu().numpy().view(np.uint16))
+        nw = lay["nw"].view(torch.int16).cpu().numpy().view(np.uint16)
+        mats = {k: tonp(lay[k]) for k in ("down", "up", "inj", "sg", "su", "sd", "se")}
+        hx = h.view(1, -1).view(torch.int16).cpu().numpy().view(np.uint16)
+        bx = br.view(1, -1).view(torch.int16).cpu().numpy().view(np.uint16)
+        gx = gt.view(1, -1).view(torch.int16).cpu().numpy().view(np.uint16)
+        orc.set_threads(os.cpu_count() or 1)
+        n, t0 = 0, time.perf_counter()
+        while time.perf_counter() - t0 < 6.0:
+            o = orc.hc_mix(hx, nw, mats["down"], mats["up"], mats["inj"], branch=bx, gate=gx)
+            orc.shared_expert(o["mixed"], mats["sg"], mats["su"], mats["sd"], mats["se"])
+            n += 1
+        mix_per = (time.perf_counter() - t0) / n
+        routed_cpu = cpu_layer_sample(6.0)
+        routed_per = 1.0 / (routed_cpu["value"] * C1.layers)
+        cpu = {"value": round(1.0 / (L * (mix_per + routed_per)), 3), "unit": "tok/s", "cores": orc.num_threads(),
+               "kind": "port",
+               "sample": f"{n} token-layers of the mixer + shared expert in 6 s plus the routed block's own sample "
+                         f"({routed_cpu['sample']}), per-layer times added and extrapolated x{L}; C restatement"}
+    line = {"metric": "MoE half of the decoder layer (mixer + routed + shared expert) decode tok/s, 28 layers",
+            "value": round(1000.0 / ms, 2), "unit": "tok/s", "n_gpus": 1, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "u8/u4/u2 codes x bf16 -> f32/f64", "data": "synthetic",
+            "config": {"workload": "f3moe_hc4x3072_r320_shared768_routed512top10_28layers", "layers": L,
+                       "streams": HC, "hidden": H, "rank": R, "shared_inter": Is, "experts": E, "top_k": K,
+                       "inter": I, "tokens": 1, "l2": f"weights of {L} layers ({resident_gb:.1f} GB) > L2",
+                       "chained": "each layer's mixer writes the previous layer's block output"},
+            "per_layer_launches": {"ms_per_step": round(chain_ms, 4), "value": round(1000.0 / chain_ms, 2),
+                                   "launches_per_step": 8 * L, "layers_same_routing": layers_same,
+                                   "final_branch_rel": round(rel, 5)},
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 2), "peak": peak, "unit": "GB/s",
+                         "frac": round(achieved / peak, 4), "traffic": None,
+                         "algorithmic_bytes_per_step": wbytes, "mix_shared_bytes_per_step": mix_bytes,
+                         "routed_bytes_per_step": routed_bytes, "peak_source": src},
+            "clocks": clocks, "gpu_launches": args.steps, "device_error": dev_err, "e2e": e2e, "cpu_baseline": cpu}
     del graph, gchain
     print(json.dumps(line), flush=True)
 
@@ -967,6 +1133,8 @@ def main() -> int:
             run_p1(args, rank, world, local_rank)
         elif args.config == "f3":
             run_f3(args, rank, world, local_rank)
+        elif args.config == "f3moe":
+            run_f3moe(args, rank, world, local_rank)
         elif args.config in ("c3", "c3n"):
             run_c3(args, rank, world, local_rank)
         elif args.config == "c4" or (world > 1 and args.config == "c1" and not args.replicas):

@@ -48,10 +48,13 @@ static_assert(kWarps == 2 * kUnits, "one warp pair per unit");
 
 // Phase timestamps for profiling builds (compiled with -DMOE_STACK_TRACE, see build.py
 // --trace): thread 0 of every CTA records %globaltimer at fixed points of every layer into
-// g_stack_trace[cta][layer][slot], read back with moe_stack_trace_read. Slots: 0 layer start,
-// 1 routed, 2 slice copies issued, 3 gate/up units done (after the block barrier), 4 item
-// work done, 6 first grid barrier passed, 7 phase B done, 10 down-slice bytes waited for,
-// 14 unit bytes waited for, 15 unit MMA loop done. The library build compiles them out.
+// g_stack_trace[cta][layer][slot], read back with moe_stack_trace_read. stack_kernel's slots:
+// 0 layer start, 1 routed, 2 slice copies issued, 3 gate/up units done (after the block
+// barrier), 4 item work done, 6 first grid barrier passed, 7 phase B done, 10 down-slice bytes
+// waited for, 14 unit bytes waited for, 15 unit MMA loop done. f3moe_kernel's: 0 layer start,
+// 1 write + norm sums done, 2 barrier passed, 5 mixer down done, 6 barrier, 7 mixer up + router
+// partial done, 8 barrier, 9 routed, 11 shared gate / up done, 3 / 10 / 14 / 15 as above,
+// 4 items done, 12 barrier, 13 phase B done. The library build compiles them out.
 #ifdef MOE_STACK_TRACE
 constexpr int kTraceCtas = 160, kTraceLayers = 64, kTraceSlots = 16;
 __device__ unsigned long long g_stack_trace[kTraceCtas * kTraceLayers * kTraceSlots];
@@ -813,17 +816,24 @@ __global__ void __launch_bounds__(kThreads, 1) f3moe_kernel(F3MoeArgs a) {
         double *accl = a.acc + (size_t)(l & 1) * kAccCopies * E;
 
         // ---------------------------------------------------------- P0a, P0b + P1, P2
+        STAMP(l, 0);
         f.write_and_sums(hin, br, gt, wout);
+        STAMP(l, 1);
         grid_sync(a.bar, nbar++);
+        STAMP(l, 2);
         f.norm(Ly, wout, a.eps);
         f.mixer_down(Ly);
+        STAMP(l, 5);
         grid_sync(a.bar, nbar++);
+        STAMP(l, 6);
         f.mixer_up(Ly, a.inj + (size_t)(l & 1) * kHcStreams, own);
         __syncthreads();
         if (a.mixed_all)
             for (int q = tid; q < f.nh; q += kThreads) a.mixed_all[(size_t)l * H + c + q * G] = f32_to_bf16_bits(own[q]);
         if (f.nh > 0) router_partial(rbar, rphase, rslice, own, f.nh, E, accl + (size_t)(c % kAccCopies) * E);
+        STAMP(l, 7);
         grid_sync(a.bar, nbar++);
+        STAMP(l, 8);
 
         // ---------------------------------------------------------- phase A
         double av[1] = {0.0};
@@ -839,6 +849,7 @@ __global__ void __launch_bounds__(kThreads, 1) f3moe_kernel(F3MoeArgs a) {
                                : make_uint2(0u, 0u);
         }
         route<1>(av, 1.0, E, K, redu, redd, cand, comp, sinds, sscores);
+        STAMP(l, 9);
         if (c == 0 && tid < K) {
             a.inds_out[(size_t)l * K + tid] = sinds[tid];
             a.scores_out[(size_t)l * K + tid] = f32_to_bf16_bits(sscores[tid]);
@@ -855,6 +866,7 @@ __global__ void __launch_bounds__(kThreads, 1) f3moe_kernel(F3MoeArgs a) {
         __syncthreads();
         f.shared_gate_up(Ly, false);
         __syncthreads();
+        STAMP(l, 11);
 #pragma unroll 1
         for (int q = c; q < NQ; q += G) {
             run_item<kFp16Exp>(q, l, P, region, ubar, dbar, qphase, xrec, xscale, xsum, xst, red, sact, arec, ascale,
@@ -862,7 +874,9 @@ __global__ void __launch_bounds__(kThreads, 1) f3moe_kernel(F3MoeArgs a) {
             qphase ^= 1u;
             if (q + G < NQ) issue_item(sl, P, sinds, q + G, ngI, region, ubar, dbar);
         }
+        STAMP(l, 4);
         grid_sync(a.bar, nbar++);
+        STAMP(l, 12);
 
         // ---------------------------------------------------------- phase B
         if (l + 1 < L) fetch_router_rows(l + 1);      // the region is free until the next phase A
@@ -906,6 +920,7 @@ __global__ void __launch_bounds__(kThreads, 1) f3moe_kernel(F3MoeArgs a) {
 #pragma unroll 1
             for (int e = tid; e < kAccCopies * E; e += kThreads) accz[e] = 0.0;
         }
+        STAMP(l, 13);
         grid_sync(a.bar, nbar++);
     }
 

@@ -8,6 +8,9 @@
 //      TMEM), N = 32 .. 256, issued by the even CTA; and the same K-block pattern as 2. with
 //      M = 256, N = 64, each commit sent to both CTAs' mbarriers (two plain commits, the
 //      second to the peer's barrier through mapa)
+//   4. hand-off latencies: tcgen05.commit -> the mbarrier phase seen by the issuing thread,
+//      with 0 or 8 MMAs (N = 64) in flight; an mbarrier ping-pong between two warps of a CTA,
+//      and between the two CTAs of a pair (remote arrive on the peer's barrier)
 // Every wait is bounded (a timeout sets a device flag, reported at the end). Build and run:
 //   nvcc -gencode arch=compute_100a,code=sm_100a -O3 -o tcgen05_issue_rate \
 //       moe-offload_b200/microbench/tcgen05_issue_rate.cu && ./tcgen05_issue_rate
@@ -316,6 +319,140 @@ void run_rate2(long long *d) {
     }
 }
 
+// ------------------------------------------------------------------ hand-off latencies
+__device__ __forceinline__ void arrive_local(uint64_t *bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(saddr(bar)) : "memory");
+}
+__device__ __forceinline__ void arrive_remote(uint32_t cluster_bar) {
+    asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cluster_bar) : "memory");
+}
+
+// commit latency: thread 0 issues NM MMAs (0 or 8) then a commit and waits for the phase
+template <int NM>
+__global__ void __launch_bounds__(128) commit_lat(int reps, long long *out) {
+    extern __shared__ __align__(1024) unsigned char sm[];
+    unsigned char *base = (unsigned char *)(((uintptr_t)sm + 1023) & ~(uintptr_t)1023);
+    __shared__ uint64_t bar;
+    __shared__ uint32_t tslot;
+    for (int i = threadIdx.x; i < 16 * 1024 / 4; i += blockDim.x) ((uint32_t *)base)[i] = 0;
+    if (threadIdx.x == 0) {
+        asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(saddr(&bar)));
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    }
+    if (threadIdx.x < 32) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 512;" ::"r"(saddr(&tslot)));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    }
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    const uint32_t tm = tslot;
+    if (threadIdx.x == 0) {
+        constexpr uint32_t id = idesc(128, 64);
+        long long tot = 0;
+        bool allok = true;
+        for (int r = 0; r < reps; ++r) {
+            long long t0 = clock64();
+#pragma unroll
+            for (int i = 0; i < NM; ++i) mma_ts_acc(tm + 128u * (i >> 2), tm + 256u + 8u * (i & 3), desc_sw128(saddr(base) + 32u * (i & 3)), id, 1u);
+            commit(&bar);
+            allok &= wait_parity(&bar, (uint32_t)(r & 1));
+            tot += clock64() - t0;
+        }
+        if (!allok) atomicOr(&g_err, 8u);
+        out[blockIdx.x] = tot / reps;
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    if (threadIdx.x < 32) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 512;" ::"r"(tm));
+}
+
+// ping-pong: lane 0 of warp 0 arrives on `ping` and waits on `pong`; lane 0 of the partner
+// (warp 1 of the same CTA, or warp 0 of the pair's other CTA) waits on `ping` and arrives on
+// `pong`. Reports one round trip (two hand-offs).
+template <bool PAIR>
+__global__ void __launch_bounds__(64) pingpong(int reps, long long *out) {
+    __shared__ uint64_t ping, pong;
+    uint32_t rank = 0;
+    if (PAIR) rank = cluster_rank();
+    if (threadIdx.x == 0) {
+        asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(saddr(&ping)));
+        asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(saddr(&pong)));
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    __syncthreads();
+    if (PAIR) cluster_sync_all();
+    const bool initiator = PAIR ? (rank == 0 && threadIdx.x == 0) : threadIdx.x == 0;
+    const bool partner = PAIR ? (rank == 1 && threadIdx.x == 0) : threadIdx.x == 32;
+    if (initiator) {
+        // PAIR: ping lives in the partner CTA, pong here
+        const uint32_t ping_addr = PAIR ? peer_addr(saddr(&ping), 1) : saddr(&ping);
+        long long t0 = clock64();
+        bool ok = true;
+        for (int r = 0; r < reps; ++r) {
+            if (PAIR) arrive_remote(ping_addr);
+            else arrive_local(&ping);
+            ok &= wait_parity(&pong, (uint32_t)(r & 1));
+        }
+        if (!ok) atomicOr(&g_err, 16u);
+        out[blockIdx.x] = (clock64() - t0) / reps;
+    } else if (partner) {
+        const uint32_t pong_addr = PAIR ? peer_addr(saddr(&pong), 0) : saddr(&pong);
+        bool ok = true;
+        for (int r = 0; r < reps; ++r) {
+            ok &= wait_parity(&ping, (uint32_t)(r & 1));
+            if (PAIR) arrive_remote(pong_addr);
+            else arrive_local(&pong);
+        }
+        if (!ok) atomicOr(&g_err, 32u);
+    }
+    __syncthreads();
+    if (PAIR) cluster_sync_all();
+}
+
+template <int NM>
+void run_commit_lat(long long *d) {
+    const int smem = 16 * 1024 + 1024, reps = 256;
+    cudaFuncSetAttribute(commit_lat<NM>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    commit_lat<NM><<<148, 128, smem>>>(reps, d);
+    cudaError_t e = cudaDeviceSynchronize();
+    if (e != cudaSuccess) { printf("error %s\n", cudaGetErrorString(e)); exit(1); }
+    long long h[148];
+    cudaMemcpy(h, d, sizeof(h), cudaMemcpyDeviceToHost);
+    double avg = 0;
+    for (int i = 0; i < 148; ++i) avg += h[i];
+    printf("commit -> phase seen by the issuer, %d MMAs before it: %.0f cycles\n", NM, avg / 148);
+}
+
+void run_pingpong(long long *d, bool pair) {
+    const int reps = 1024;
+    if (pair) {
+        cudaLaunchConfig_t cfg = {};
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = 2;
+        attr[0].val.clusterDim.y = 1;
+        attr[0].val.clusterDim.z = 1;
+        cfg.gridDim = dim3(148);
+        cfg.blockDim = dim3(64);
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        cudaLaunchKernelEx(&cfg, pingpong<true>, reps, d);
+    } else {
+        pingpong<false><<<148, 64>>>(reps, d);
+    }
+    cudaError_t e = cudaDeviceSynchronize();
+    if (e != cudaSuccess) { printf("error %s\n", cudaGetErrorString(e)); exit(1); }
+    long long h[148];
+    cudaMemcpy(h, d, sizeof(h), cudaMemcpyDeviceToHost);
+    double avg = 0;
+    int n = 0;
+    for (int i = 0; i < 148; i += pair ? 2 : 1, ++n) avg += h[i];
+    printf("mbarrier ping-pong round trip, %s: %.0f cycles\n", pair ? "two CTAs of a pair (remote arrive)" : "two warps of a CTA", avg / n);
+}
+
 int main() {
     long long *d;
     cudaMalloc(&d, 148 * sizeof(long long));
@@ -329,6 +466,8 @@ int main() {
     run_rate2<32, 8, 0>(d); run_rate2<64, 1, 0>(d); run_rate2<64, 4, 0>(d); run_rate2<128, 2, 0>(d);
     run_rate2<256, 1, 0>(d);
     run_rate2<64, 1, 1>(d); run_rate2<64, 1, 2>(d); run_rate2<64, 1, 3>(d);
+    run_commit_lat<0>(d); run_commit_lat<8>(d);
+    run_pingpong(d, false); run_pingpong(d, true);
     unsigned int err = 0;
     cudaMemcpyFromSymbol(&err, g_err, 4);
     printf("device error word %u (0: every wait completed)\n", err);

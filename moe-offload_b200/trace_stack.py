@@ -1,12 +1,14 @@
 """Per-phase timeline of the persistent decode kernel (profiling aid, not part of the op path).
 
     python moe-offload_b200/build.py --trace          # libmoe_b200_trace.so (MOE_STACK_TRACE)
-    python moe-offload_b200/trace_stack.py [--layers 28] [--steps 16]
+    python moe-offload_b200/trace_stack.py [--layers 28] [--steps 16] [--fused]
 
 Runs the c1 stack (synthetic BASELINE weights) through the profiling build of the library,
 whose kernel stamps %globaltimer at fixed points of every layer, and prints the median over
 the middle layers of each point's time from the layer's start (microseconds), over the work-
-item CTAs (the first K * I/64) and over the others.
+item CTAs (the first K * I/64) and over the others. --fused: the same routed layers behind the
+hyper-connection mixer and with the shared expert, in one launch (ops.F3MoeStack,
+f3moe_kernel's stamps).
 """
 from __future__ import annotations
 
@@ -20,6 +22,9 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(HERE)
 SLOTS = {"routed": 1, "copies_issued": 2, "unit_bytes_waited": 14, "unit_mma_done": 15, "gateup_done": 3,
          "down_bytes_waited": 10, "item_done": 4, "barrier1_passed": 6, "phaseB_done": 7}
+FUSED_SLOTS = {"write_norm_sums": 1, "bar0": 2, "mixer_down": 5, "bar1": 6, "mixer_up_router": 7, "bar2": 8,
+               "routed": 9, "shared_gate_up": 11, "unit_bytes_waited": 14, "gateup_done": 3,
+               "down_bytes_waited": 10, "items_done": 4, "barA": 12, "phaseB_done": 13}
 TRACE_CTAS, TRACE_LAYERS, TRACE_SLOTS = 160, 64, 16
 
 
@@ -27,6 +32,7 @@ def main() -> int:
     ap = argparse.ArgumentParser()
     ap.add_argument("--layers", type=int, default=28)
     ap.add_argument("--steps", type=int, default=16)
+    ap.add_argument("--fused", action="store_true")
     args = ap.parse_args()
     lib_path = os.path.join(HERE, "libmoe_b200_trace.so")
     if not os.path.exists(lib_path):
@@ -44,17 +50,28 @@ def main() -> int:
 
     dev = torch.device("cuda:0")
     cfg = dataclasses.replace(C1, layers=args.layers)
-    st = PersistentStack(dev_stack(cfg, dev), cfg.top_k, dev, release_unpacked=True)
     gen = torch.Generator(device=dev)
     gen.manual_seed(11)
-    h = dev_bf16_normal((8 + args.steps, 1, cfg.hidden), dev, gen)
+    slots = SLOTS
+    if args.fused:
+        from bench import f3_mix_layers
+        from moe_offload_b200.ops import F3MoeStack
+        slots = FUSED_SLOTS
+        mix = f3_mix_layers(dev, gen, cfg.layers, 4, cfg.hidden, 320, 768)
+        st = F3MoeStack(mix, dev_stack(cfg, dev), cfg.top_k, dev)
+        h = dev_bf16_normal((8 + args.steps, 4 * cfg.hidden), dev, gen)
+        step = lambda x: st.decode(x)
+    else:
+        st = PersistentStack(dev_stack(cfg, dev), cfg.top_k, dev, release_unpacked=True)
+        h = dev_bf16_normal((8 + args.steps, 1, cfg.hidden), dev, gen)
+        step = st.step_device
     for i in range(8):
-        st.step_device(h[i])
+        step(h[i])
     torch.cuda.synchronize()
     s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     s.record()
     for i in range(8, 8 + args.steps):
-        st.step_device(h[i])
+        step(h[i])
     e.record()
     torch.cuda.synchronize()
     us_per_token = s.elapsed_time(e) / args.steps * 1000.0
@@ -66,13 +83,13 @@ def main() -> int:
     G = torch.cuda.get_device_properties(dev).multi_processor_count
     NQ = cfg.top_k * cfg.inter // 64
     L = cfg.layers
-    per = {k: [] for k in SLOTS}
-    per_idle = {k: [] for k in SLOTS}
+    per = {k: [] for k in slots}
+    per_idle = {k: [] for k in slots}
     period = []
     for l in range(1, L - 1):
         t0 = t[:G, l, 0].min()
         period.append((t[:G, l + 1, 0].min() - t0) / 1000.0)
-        for k, slot in SLOTS.items():
+        for k, slot in slots.items():
             for dst, rows in ((per, t[:NQ, l, slot]), (per_idle, t[NQ:G, l, slot])):
                 v = rows[rows > 0]
                 if len(v):
