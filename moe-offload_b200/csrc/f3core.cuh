@@ -226,8 +226,9 @@ struct F3Phases {
     // P2: mix = silu(down / 4) of all R totals (every CTA), mixer up for the hidden indices
     // this CTA owns (their four stream rows), mixed = mean_c sigmoid(up_c) * normed_c; CTA 0
     // forms inj = 2 sigmoid(inject / 4). own_mixed (shared, nh floats) receives this CTA's
-    // mixed values (bf16-rounded) when given.                            -> grid barrier
-    MOE_D void mixer_up(const moe_f3_layer &Ly, uint16_t *injo, float *own_mixed) {
+    // mixed values (bf16-rounded) when given; prefetch_gate_up: load the first shared gate /
+    // up item (P3).                                                      -> grid barrier
+    MOE_D void mixer_up(const moe_f3_layer &Ly, uint16_t *injo, float *own_mixed, bool prefetch_gate_up = true) {
         for (int k = tid; k < R; k += kF3Threads) sx[k] = f32_to_bf16_bits(hc_mix_value(__ldcg(b.dv + k), 0));
         if (j == 0 && tid < kHcStreams) injo[tid] = f32_to_bf16_bits(Ly.wi ? hc_inj_value(__ldcg(b.iv + tid), 0) : 0.f);
         __syncthreads();
@@ -235,7 +236,7 @@ struct F3Phases {
             if (it != tid) load2(Ly, it, pf2);
             sv[it] = pf2.value(sx + (size_t)(it % ng2) * 64);
         }
-        if (tid < ni * 2 * ng3) load3(Ly, tid, pf3);
+        if (prefetch_gate_up && tid < ni * 2 * ng3) load3(Ly, tid, pf3);
         __syncthreads();
         for (int q = tid; q < nh; q += kF3Threads) {
             const int hh = j + q * G;
@@ -255,12 +256,12 @@ struct F3Phases {
 
     // P3: shared gate + up rows this CTA owns, SwiGLU with MLX's bf16 roundings; the scalar
     // expert gate's group values (8-bit g64) on the CTAs with the fewest rows. mixed must be
-    // staged in sx. prefetch_down: load the first round-robin shared down item (P4).
-    //                                                                     -> grid barrier
-    MOE_D void shared_gate_up(const moe_f3_layer &Ly, bool prefetch_down) {
+    // staged in sx. prefetched: mixer_up loaded the first item; prefetch_down: load the first
+    // round-robin shared down item (P4).                                  -> grid barrier
+    MOE_D void shared_gate_up(const moe_f3_layer &Ly, bool prefetch_down, bool prefetched = true) {
         const int per = 2 * ng3;
         for (int it = tid; it < ni * per; it += kF3Threads) {
-            if (it != tid) load3(Ly, it, pf3);
+            if (it != tid || !prefetched) load3(Ly, it, pf3);
             sv[it] = pf3.value(sx + (size_t)(it % ng3) * 64);
         }
         for (int q = tid; q < ngate; q += kF3Threads) {

@@ -689,13 +689,13 @@ __global__ void __launch_bounds__(kThreads, 1) stack_kernel(StackArgs a) {
 //       contribution to the layer's router logits: the CTA's rows of the transposed router,
 //       fetched during the previous phase B, exact products, fp64 atomics                  | barrier
 //   A   every CTA: logits -> precise softmax -> MLX-order top-k -> renorm; the routed work
-//       items' slices copied in (as stack_kernel's phase A) while the CTA runs the shared
-//       expert's gate / up rows and scalar gate groups; then the routed items (run_item) on
-//       the records of mixed                                                                | barrier
+//       items (run_item, as stack_kernel's phase A) on the records of mixed; then the shared
+//       expert's gate / up rows and scalar gate groups (at once on the CTAs without an item,
+//       while the others' copies are in flight)                                          | barrier
 //   B   the CTA's 8-row blocks of H: the shared down rows (scaled by the gate's sigmoid), the
 //       routed partial sums, and branch = sum_k bf16(y_k * s_k) + shared (one bf16 rounding,
-//       moe_experts_down with the shared output as its addend); the next layer's router rows
-//       are fetched                                                                          | barrier
+//       moe_experts_down with the shared output as its addend); then the next layer's router
+//       rows are fetched                                                                     | barrier
 // The normed streams and the router rows live in the weight region, which the routed items
 // only use in phase A. After the last layer CTA 0 applies the last block's write.
 
@@ -793,13 +793,14 @@ __global__ void __launch_bounds__(kThreads, 1) f3moe_kernel(F3MoeArgs a) {
     unsigned int nbar = 0;
     uint32_t rphase = 0, qphase = 0;
     const uint32_t rrow = (uint32_t)E * 2u;
-    // this CTA's rows of layer l's transposed router (hidden indices c, c + G, ...)
+    // this CTA's rows of layer l's transposed router (hidden indices c, c + G, ...): lane q of
+    // warp 0 copies row q (nh <= 32: H <= 32 G), after lane 0 has set the byte count
     auto fetch_router_rows = [&](int l) {
-        if (tid == 0 && f.nh > 0) {
-            mbar_arrive_expect_tx(rbar, rrow * (uint32_t)f.nh);
-#pragma unroll 1
-            for (int q = 0; q < f.nh; ++q)
-                tma_load_1d(rslice + (size_t)q * rrow, a.layers[l].router_t + (size_t)(c + q * G) * E, rrow, rbar);
+        if (tid < 32 && f.nh > 0) {
+            if (tid == 0) mbar_arrive_expect_tx(rbar, rrow * (uint32_t)f.nh);
+            __syncwarp();
+            if (tid < f.nh)
+                tma_load_1d(rslice + (size_t)tid * rrow, a.layers[l].router_t + (size_t)(c + tid * G) * E, rrow, rbar);
         }
     };
     fetch_router_rows(0);
@@ -826,7 +827,7 @@ __global__ void __launch_bounds__(kThreads, 1) f3moe_kernel(F3MoeArgs a) {
         STAMP(l, 5);
         grid_sync(a.bar, nbar++);
         STAMP(l, 6);
-        f.mixer_up(Ly, a.inj + (size_t)(l & 1) * kHcStreams, own);
+        f.mixer_up(Ly, a.inj + (size_t)(l & 1) * kHcStreams, own, false);
         __syncthreads();
         if (a.mixed_all)
             for (int q = tid; q < f.nh; q += kThreads) a.mixed_all[(size_t)l * H + c + q * G] = f32_to_bf16_bits(own[q]);
@@ -856,7 +857,9 @@ __global__ void __launch_bounds__(kThreads, 1) f3moe_kernel(F3MoeArgs a) {
         }
         const StackLayer sl{ly.router_t, ly.experts};
         if (c < NQ) issue_item(sl, P, sinds, c, ngI, region, ubar, dbar);
-        // records of mixed while the copies are in flight; the shared expert's gate / up rows
+        // records of mixed while the copies are in flight, then the routed items; then the shared
+        // expert's gate / up rows (first thing on the CTAs without an item, while the others'
+        // copies are in flight; after the item elsewhere, no longer competing with the copies)
 #pragma unroll
         for (int p = 0; p < kHPass; ++p) {
             const int Gp = (tid >> 4) + p * (kThreads / 16);
@@ -864,9 +867,6 @@ __global__ void __launch_bounds__(kThreads, 1) f3moe_kernel(F3MoeArgs a) {
         }
         stage_l2(f.sx, a.bufs.mixed, H);
         __syncthreads();
-        f.shared_gate_up(Ly, false);
-        __syncthreads();
-        STAMP(l, 11);
 #pragma unroll 1
         for (int q = c; q < NQ; q += G) {
             run_item<kFp16Exp>(q, l, P, region, ubar, dbar, qphase, xrec, xscale, xsum, xst, red, sact, arec, ascale,
@@ -875,13 +875,15 @@ __global__ void __launch_bounds__(kThreads, 1) f3moe_kernel(F3MoeArgs a) {
             if (q + G < NQ) issue_item(sl, P, sinds, q + G, ngI, region, ubar, dbar);
         }
         STAMP(l, 4);
+        f.shared_gate_up(Ly, false, false);
+        STAMP(l, 11);
         grid_sync(a.bar, nbar++);
         STAMP(l, 12);
 
         // ---------------------------------------------------------- phase B
-        if (l + 1 < L) fetch_router_rows(l + 1);      // the region is free until the next phase A
-        const float gsig = f.stage_down();
-        f.shared_down_items(Ly, b0 * 8, 1, nrows, false);
+        // the thread's first shared down item is loaded first; the routed partial sums run
+        // while it is in flight
+        if (tid < nrows * f.ng4) f.load4(Ly, tid, f.pf4, b0 * 8, 1);
 #pragma unroll 1
         for (int x = tid; x < K * nrows; x += kThreads) {
             const int k = x / nrows, r = x % nrows;
@@ -898,6 +900,8 @@ __global__ void __launch_bounds__(kThreads, 1) f3moe_kernel(F3MoeArgs a) {
             }
             ypart[k * nrows + r] = bf16r(yk);
         }
+        const float gsig = f.stage_down();
+        f.shared_down_items(Ly, b0 * 8, 1, nrows, true);
         __syncthreads();
         uint16_t *bro = a.branch + (size_t)(l & 1) * H;
 #pragma unroll 1
@@ -914,7 +918,10 @@ __global__ void __launch_bounds__(kThreads, 1) f3moe_kernel(F3MoeArgs a) {
             bro[row] = hb;
             if (a.branch_all) a.branch_all[(size_t)l * H + row] = hb;
         }
-        if (l + 1 < L) f.prefetch_mixer_down(a.layers[l + 1].mix);
+        if (l + 1 < L) {
+            f.prefetch_mixer_down(a.layers[l + 1].mix);
+            fetch_router_rows(l + 1);             // the region is free until the next phase A
+        }
         if (c == 0) {   // layer l's logits were consumed in phase A; ready the buffer for l + 2
             double *accz = a.acc + (size_t)(l & 1) * kAccCopies * E;
 #pragma unroll 1
@@ -1078,7 +1085,7 @@ extern "C" int moe_f3moe_stack_decode(const void *layers, int L, int H, int R, i
     if (G < moe_qlin::kHcStreams * 32)
         return moe_set_error(MOE_EINVAL, "f3moe_stack_decode: %d CTAs (the norm takes %d)", G,
                              moe_qlin::kHcStreams * 32);
-    if ((H / 8 + G - 1) / G > kMaxBlocks)
+    if ((H / 8 + G - 1) / G > kMaxBlocks || (H + G - 1) / G > 32)
         return moe_set_error(MOE_EINVAL, "f3moe_stack_decode: %d CTAs too few for %d row blocks", G, H / 8);
     const size_t region = F3MoeSmem::region_bytes(H, I, E, G);
     const F3MoeSmem M(H, R, Is, I, K, G, region);
