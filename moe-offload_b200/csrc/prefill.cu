@@ -186,13 +186,28 @@ struct Tile {
     int e, row0, pos0, n;   // expert, first weight row, first assignment position, tokens
 };
 
+// Warp-aggregated increment of ctr[e] by one per active lane: the lanes holding the same e
+// make one atomic (routing can send most tokens to one expert); returns this lane's value of
+// the counter before its own increment (the lanes of a group in lane order).
+MOE_D int warp_agg_add(int *ctr, uint32_t e, unsigned active) {
+    const unsigned grp = __match_any_sync(active, e);
+    const int leader = __ffs(grp) - 1, lane = threadIdx.x & 31;
+    int base = 0;
+    if (lane == leader) base = atomicAdd(ctr + e, __popc(grp));
+    base = __shfl_sync(grp, base, leader);
+    return base + __popc(grp & ((1u << lane) - 1u));
+}
+
 // expert ids are taken relative to e_begin (a rank's block of the experts); ids outside
 // [e_begin, e_begin + E) are skipped when `strict` is 0 and flagged as bad input otherwise
 __global__ void count_kernel(const uint32_t *inds, int TK, int E, uint32_t e_begin, int strict, int *counts) {
-    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < TK; i += gridDim.x * blockDim.x) {
-        const uint32_t e = inds[i] - e_begin;
-        if (e < (uint32_t)E) atomicAdd(&counts[e], 1);
-        else if (strict) atomicOr(&g_moe_device_error, MOE_DEVERR_BAD_INPUT);
+    for (int i0 = blockIdx.x * blockDim.x; i0 < TK; i0 += gridDim.x * blockDim.x) {
+        const int i = i0 + threadIdx.x;
+        const uint32_t e = i < TK ? inds[i] - e_begin : 0xffffffffu;
+        const bool ok = e < (uint32_t)E;
+        const unsigned active = __ballot_sync(0xffffffffu, ok);
+        if (ok) warp_agg_add(counts, e, active);
+        else if (i < TK && strict) atomicOr(&g_moe_device_error, MOE_DEVERR_BAD_INPUT);
     }
 }
 
@@ -263,10 +278,13 @@ __global__ void __launch_bounds__(1024) scan_kernel(const int *counts, int E, in
 // assignment i = t*K + k goes to position offsets[e] + (arrival order within e)
 __global__ void scatter_kernel(const uint32_t *inds, int TK, int E, uint32_t e_begin, const int *offsets, int *cursor,
                                int *pos_of, int *src_of) {
-    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < TK; i += gridDim.x * blockDim.x) {
-        const uint32_t e = inds[i] - e_begin;
-        if (e >= (uint32_t)E) continue;
-        const int p = offsets[e] + atomicAdd(&cursor[e], 1);
+    for (int i0 = blockIdx.x * blockDim.x; i0 < TK; i0 += gridDim.x * blockDim.x) {
+        const int i = i0 + threadIdx.x;
+        const uint32_t e = i < TK ? inds[i] - e_begin : 0xffffffffu;
+        const bool ok = e < (uint32_t)E;
+        const unsigned active = __ballot_sync(0xffffffffu, ok);
+        if (!ok) continue;
+        const int p = offsets[e] + warp_agg_add(cursor, e, active);
         pos_of[i] = p;
         src_of[p] = i;
     }
