@@ -311,7 +311,8 @@ __global__ void __launch_bounds__(kThreads) router_kernel(RouterArgs a) {
 // midpoint). Then one block per token runs router_tail.
 constexpr int kGT = 64, kGE = 128, kGK = 32;      // tokens, rows, K per stage
 constexpr int kGemmMinT = 256;                     // batches from this size use the GEMM
-constexpr size_t kGemmSmem = (size_t)kGK * (kGT + kGE) * sizeof(double);
+constexpr size_t kGemmStage = (size_t)kGK * (kGT + kGE);            // doubles per stage
+constexpr size_t kGemmSmem = 2 * kGemmStage * sizeof(double);      // two stages
 
 // fp64 tensor-core MMA: D(8x8) += A(8x4, row) * B(4x8, col); lane (g = lane >> 2, q = lane & 3)
 // holds A[g][q], B[q][g] and D[g][2q], D[g][2q+1]
@@ -323,13 +324,13 @@ __device__ __forceinline__ void dmma_884(double &d0, double &d1, double a, doubl
 
 // Tile: 64 tokens x 128 router rows per CTA, K in stages of 32. Operands are converted exactly
 // to double when staged, as [k-block of 4][token or row][4] so that every fragment load of a
-// warp touches each bank pair exactly twice (conflict-free). Warp w computes tokens
-// (w & 1) * 32 .. +32 and rows (w >> 1) * 32 .. +32 as 4 x 4 tiles of fp64 MMAs: exact
-// products of bf16 values summed in double, as in the per-token kernel.
+// warp touches each bank pair exactly twice (conflict-free), into one of two stage buffers:
+// one block barrier per stage (stage s+1 is written while another warp may still read stage s;
+// nobody writes stage s+2 = s before every warp has passed the barrier after stage s+1's
+// writes). Warp w computes tokens (w & 1) * 32 .. +32 and rows (w >> 1) * 32 .. +32 as 4 x 4
+// tiles of fp64 MMAs: exact products of bf16 values summed in double, as in the per-token kernel.
 __global__ void __launch_bounds__(256) router_gemm_kernel(RouterArgs a) {
     extern __shared__ double gsm[];
-    double *xs = gsm;                  // [kGK / 4][kGT][4]
-    double *ws = gsm + kGK * kGT;      // [kGK / 4][kGE][4]
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int g = lane >> 2, q = lane & 3;
     const int t0 = blockIdx.y * kGT, r0 = blockIdx.x * kGE;
@@ -375,7 +376,9 @@ __global__ void __launch_bounds__(256) router_gemm_kernel(RouterArgs a) {
     };
     uint4 nx, nw[2];
     load_stage(0, nx, nw);
-    for (int k0 = 0; k0 < a.H; k0 += kGK) {
+    for (int k0 = 0, sb = 0; k0 < a.H; k0 += kGK, sb ^= 1) {
+        double *xs = gsm + sb * kGemmStage;     // [kGK / 4][kGT][4]
+        double *ws = xs + kGK * kGT;            // [kGK / 4][kGE][4]
         stage_vals(xs, kGT, ltok, nx);
         stage_vals(ws, kGE, lrow, nw[0]);
         stage_vals(ws, kGE, lrow + 64, nw[1]);
@@ -393,7 +396,6 @@ __global__ void __launch_bounds__(256) router_gemm_kernel(RouterArgs a) {
 #pragma unroll
                 for (int j = 0; j < 4; ++j) dmma_884(acc[i][j][0], acc[i][j][1], af[i], bfr[j]);
         }
-        __syncthreads();
     }
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
