@@ -63,7 +63,8 @@ size_t moe_router_workspace_bytes(int T, int E, int M);
  *   x        bf16 [T, H]
  *   w        router weight: bf16 [E, H] when rbits == 16, else affine u32 [E, H*rbits/32]
  *            with w_scales/w_biases [E, H/group_size]
- *   wn       next layer's router (same format) or NULL; pred_bias fp32 [E] or NULL
+ *   wn       next layer's router in this router's format (an affine one behind a bf16 router
+ *            is refused: MOE_EINVAL) or NULL; pred_bias fp32 [E] or NULL
  *   out_logits bf16 [T, E] or NULL; out_probs bf16 [T, E] or NULL
  *   out_inds  u32 [T, K] (MLX argpartition order), out_scores bf16 [T, K]
  *   out_pred  u32 [T, M] sorted by value descending, or NULL

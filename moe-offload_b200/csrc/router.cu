@@ -477,6 +477,10 @@ int moe_router_launch(const void *x, int T, int H, int E, int K, const void *w,
         return moe_set_error(MOE_EINVAL, "router: bad prediction arguments M=%d", M);
     if (rbits == 16) {
         if (H % 8) return moe_set_error(MOE_EINVAL, "router: H=%d must be a multiple of 8", H);
+        // both routers are read in one format: an affine next-layer router (scales / biases
+        // given) behind a bf16 one would be read as bf16 past its codes
+        if (M > 0 && (wn_scales || wn_biases))
+            return moe_set_error(MOE_EINVAL, "router: the next-layer router must have this router's format");
         if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(w) |
              reinterpret_cast<uintptr_t>(wn)) & 15)
             return moe_set_error(MOE_EINVAL, "router: x/w must be 16-byte aligned");

@@ -75,6 +75,11 @@ def router_workspace(device, T: int, E: int, M: int) -> torch.Tensor:
     return ws
 
 
+def _router_format(w) -> tuple:
+    """(bits, group size, fp16 scales) of a router: bf16 tensors are (16, 0, False)."""
+    return (w.bits, w.group_size, bool(w.sb_fp16)) if isinstance(w, QMatrix) else (16, 0, False)
+
+
 def router_topk(x: torch.Tensor, w, K: int, *, w_next=None, M: int = 0, pred_bias=None,
                 want_logits: bool = False, want_probs: bool = False, out: dict | None = None,
                 stream=None) -> dict:
@@ -86,6 +91,17 @@ def router_topk(x: torch.Tensor, w, K: int, *, w_next=None, M: int = 0, pred_bia
     _need(x, "x", (torch.bfloat16,))
     T, H = x.shape
     dev = x.device
+    if M > 0 and w_next is not None and _router_format(w_next) != _router_format(w):
+        # one launch reads both routers in one format: a next-layer router of another format
+        # (e.g. an 8-bit router after bf16 ones) gets its own launch, which routes with it and
+        # returns its top-M (the same prediction the fused launch computes)
+        o = out if out is not None else {}
+        router_topk(x, w, K, want_logits=want_logits, want_probs=want_probs, out=o, stream=stream)
+        En = w_next.w.shape[0] if isinstance(w_next, QMatrix) else w_next.shape[0]
+        po = router_topk(x, w_next, min(K, En), w_next=w_next, M=M, pred_bias=pred_bias,
+                         out=o.setdefault("_next_route", {}), stream=stream)
+        o["pred"] = po["pred"]
+        return o
     if isinstance(w, QMatrix):
         w.check("w", dev)
         E = w.w.shape[0]
@@ -488,6 +504,8 @@ class F3MoeStack:
         self.L, self.K = len(routed), int(top_k)
         self.eps, self.num_ctas = float(eps), int(num_ctas)
         self.H, self.R, self.Is, self.sb_mix, rows = f3_layer_rows(mix_layers, self.device)
+        if not all(isinstance(ly.router, torch.Tensor) and ly.router.dtype == torch.bfloat16 for ly in routed):
+            raise ValueError("the fused stack reads bf16 [E, H] routers")
         self.E, H = routed[0].router.shape
         self.I = routed[0].gate.w.shape[1]
         if H != self.H:

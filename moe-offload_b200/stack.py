@@ -120,6 +120,8 @@ class PersistentStack:
         self.K = top_k
         self.device = torch.device(device)
         self.L = len(layers)
+        if not all(isinstance(ly.router, torch.Tensor) and ly.router.dtype == torch.bfloat16 for ly in layers):
+            raise ValueError("the persistent stack reads bf16 [E, H] routers; route affine ones per layer")
         self.E, self.H = layers[0].router.shape
         self.I = layers[0].gate.w.shape[1]
         self.sb_fp16 = layers[0].gate.sb_fp16

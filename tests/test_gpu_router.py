@@ -102,3 +102,53 @@ def test_router_repeated_calls_rearm_workspace(dev):
     for x, g in zip(xs, got):
         _, inds, _ = orc.softmax_topk(orc.router_logits(x, wn, E), K)
         assert np.array_equal(g.cpu().numpy().astype(np.uint32), inds)
+
+
+@pytest.mark.parametrize("fmt,nfmt", [(16, 8), (8, 16), (8, 4)])
+def test_router_prediction_with_other_format_next_router(dev, fmt, nfmt):
+    """A next-layer router of another format than the layer's own (an 8-bit router after bf16
+    ones, as in a checkpoint whose last layers keep their router at 8 bits): the prediction is
+    the next router's top-M of its own logits, and the layer's routing is unchanged."""
+    from moe_offload_b200 import ops
+    from moe_offload_b200.synthetic import np_bf16_normal, np_qmatrix, np_to_bf16_tensor, to_device_qmatrix
+    rng = np.random.default_rng(50 + fmt + nfmt)
+    T, H, E, K, M = 3, 1024, 64, 4, 12
+    x = np_bf16_normal(rng, (T, H))
+
+    def router(bits):
+        if bits == 16:
+            w = np_bf16_normal(rng, (E, H), 0.02)
+            return np_to_bf16_tensor(w, dev), lambda xx: orc.router_logits(xx, w, E)
+        wq = np_qmatrix(rng, 1, E, H, bits=bits, sb_fp16=False)
+        d = to_device_qmatrix(wq, dev, bits=bits, sb_fp16=False)
+        q = [a[0] for a in wq]
+        return (ops.QMatrix(d.w[0], d.s[0], d.b[0], bits, 64),
+                lambda xx: orc.router_logits(xx, q[0], E, rbits=bits, scales=q[1], biases=q[2], group_size=64))
+    w, lg_w = router(fmt)
+    wn, lg_wn = router(nfmt)
+    out = ops.router_topk(np_to_bf16_tensor(x, dev), w, K, w_next=wn, M=M)
+    torch.cuda.synchronize()
+    probs, inds, scores = orc.softmax_topk(lg_w(x), K)
+    assert np.array_equal(out["inds"].cpu().numpy().astype(np.uint32), inds)
+    assert np.array_equal(_np(out["scores"]), scores)
+    assert np.array_equal(out["pred"].cpu().numpy().astype(np.uint32), orc.topm_sorted(lg_wn(x), M))
+
+
+def test_router_abi_refuses_affine_next_router_behind_bf16(dev):
+    """The C entry point reads both routers in the layer router's format, so it refuses an
+    affine next-layer router (scales and biases given) behind a bf16 one."""
+    from moe_offload_b200 import _lib, ops
+    T, H, E, K, M = 1, 256, 16, 4, 4
+    x = torch.zeros((T, H), dtype=torch.bfloat16, device=dev)
+    w = torch.zeros((E, H), dtype=torch.bfloat16, device=dev)
+    wn = torch.zeros((E, H // 4), dtype=torch.int32, device=dev)
+    sb = torch.zeros((E, H // 64), dtype=torch.bfloat16, device=dev)
+    inds = torch.zeros((T, K), dtype=torch.int32, device=dev)
+    scores = torch.zeros((T, K), dtype=torch.bfloat16, device=dev)
+    pred = torch.zeros((T, M), dtype=torch.int32, device=dev)
+    ws = ops.router_workspace(dev, T, E, M)
+    with pytest.raises(_lib.MoeError, match="format"):
+        _lib.call("moe_router_topk", x.data_ptr(), T, H, E, K, w.data_ptr(), None, None, 16, 64, 0,
+                  wn.data_ptr(), sb.data_ptr(), sb.data_ptr(), M, None, None, None, inds.data_ptr(),
+                  scores.data_ptr(), pred.data_ptr(), ws.data_ptr(), ws.numel(),
+                  torch.cuda.current_stream(dev).cuda_stream)
