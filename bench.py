@@ -46,13 +46,14 @@ def parse():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
-    ap.add_argument("--config", choices=["c1", "c2", "c3", "c3n", "c4", "p1", "f3", "f3moe"], default="c1",
+    ap.add_argument("--config", choices=["c1", "c2", "c3", "c3n", "c4", "p1", "f3", "f3moe", "f4"], default="c1",
                     help="c1: resident stack (the headline); c2: offload stack with the LRU slot caches; "
                          "c3: 2048-token prefill through the resident 28-layer stack; c3n: the Nemotron-shaped "
                          "prefill layer (240 experts, top-9, 1024 tokens); c4: expert-parallel decode (experts "
                          "split across the ranks); p1: the P1 I/O scheduler filling c2-shaped expert slots; f3: the "
                          "hyper-connection mixer + shared expert in front of each of the 28 MoE blocks, decode; "
-                         "f3moe: the mixer, the routed block and the shared expert of all 28 layers in one launch")
+                         "f3moe: the mixer, the routed block and the shared expert of all 28 layers in one launch; "
+                         "f4: the greedy token loop (embedding, the c1 stack, a 248,320-id LM head, argmax)")
     ap.add_argument("--batch", type=int, default=0, help="c4: tokens per step (default: 8 per GPU; 4096 = c4's prefill)")
     ap.add_argument("--replicas", action="store_true",
                     help="--gpus N > 1: N independent replicas of the c1 stack instead of expert parallelism")
@@ -1111,6 +1112,107 @@ def run_c4(args, rank: int, world: int, local_rank: int) -> None:
     st.close()
 
 
+def run_f4(args, rank: int, world: int, local_rank: int) -> None:
+    """f4: the greedy decode loop of the reference's server / generate_greedy (server.py:113-199,
+    loader.py:1171-1190) around the c1 stack: per token the embedding row of the previous id,
+    the persistent stack launch (28 layers), the LM head over a 248,320-id vocabulary (the
+    reference model's, prompt_cache.py:149) and the argmax, captured as one CUDA graph per token
+    (tokens.ResidentTokenLoop). Synthetic seeded embedding / head tables of the model's shape.
+    `value`: tokens per second with the loop's id kept on the device (graph replays back to
+    back); `e2e`: the same loop reading every id back to the host before the next step, as the
+    reference does for its stop test."""
+    import torch
+
+    from moe_offload_b200 import _lib
+    from moe_offload_b200.stack import PersistentStack
+    from moe_offload_b200.synthetic import C1, dev_stack
+    from moe_offload_b200.tokens import ResidentTokenLoop, TokenHead
+
+    if world > 1:
+        raise SystemExit("f4 runs on one GPU")
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    cfg, V = C1, 248_320
+    layers = dev_stack(cfg, dev)
+    stack = PersistentStack(layers, cfg.top_k, dev, release_unpacked=True)
+    del layers
+    torch.cuda.empty_cache()
+    head = TokenHead.synthetic(V, cfg.hidden, dev, seed=cfg.seed + 101)
+    loop = ResidentTokenLoop(stack, head)
+    loop.start(65)
+    for _ in range(args.warmup):
+        loop.step()
+    torch.cuda.synchronize()
+    cur = torch.cuda.current_stream(dev)
+    clk = ClockSampler(local_rank)
+    clk.start()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(args.steps):
+        loop.graph.replay()
+    e.record()
+    torch.cuda.synchronize()
+    clocks = clk.stop()
+    t_ms = s.elapsed_time(e)
+    # the fused LM head + argmax alone (the step's largest read), and the stand-alone argmax
+    # over stored logits (moe_sample_tokens at temperature 0), for the step's split
+    saved = loop.cur.clone()
+    hs, he = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    hs.record()
+    for _ in range(args.steps):
+        head.argmax(stack.y, out=loop.cur)
+    he.record()
+    torch.cuda.synchronize()
+    head_ms = hs.elapsed_time(he) / args.steps
+    head.logits(stack.y, out=loop.logits)
+    ss, se = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ss.record()
+    for _ in range(args.steps):
+        head.sample(loop.logits, out=loop.cur)
+    se.record()
+    torch.cuda.synchronize()
+    argmax_ms = ss.elapsed_time(se) / args.steps
+    loop.cur.copy_(saved)
+    dev_err = int(_lib.call("moe_device_error", 1))
+    e2e = None
+    if not args.no_e2e:
+        ids = []
+        s2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s2.record()
+        for _ in range(args.steps):
+            ids.append(loop.step())
+        e2.record()
+        torch.cuda.synchronize()
+        t2 = s2.elapsed_time(e2)
+        e2e = {"value": round(args.steps / (t2 / 1000.0), 2), "unit": "tok/s", "h2d_bytes_per_step": 0,
+               "d2h_bytes_per_step": 4, "distinct_ids": len(set(ids)),
+               "api": "moe_offload_b200.tokens.ResidentTokenLoop.step (graph replay, next id read back per token)"}
+    peak, peak_kind = peaks()
+    stack_bytes = cfg.layers * (cfg.top_k * cfg.expert_bytes + cfg.router_bytes)
+    step_bytes = stack_bytes + head.head_bytes + cfg.hidden * 2
+    step_s = t_ms / 1000.0 / args.steps
+    achieved = step_bytes / step_s / 1e9
+    head_gbs = head.head_bytes / (head_ms / 1000.0) / 1e9
+    roof = {"kernel": "token step (embed + stack_kernel + lm_head_kernel with the argmax folded in)", "bound": "hbm",
+            "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s", "frac": round(achieved / peak, 4),
+            "traffic": None, "algorithmic_bytes_per_launch": step_bytes, "launch_us": round(step_s * 1e6, 2),
+            "peak_source": peak_kind,
+            "lm_head": {"us": round(head_ms * 1000, 2), "bytes": head.head_bytes, "gbs": round(head_gbs, 1),
+                        "frac": round(head_gbs / peak, 4)},
+            "separate_argmax_over_logits_us": round(argmax_ms * 1000, 2)}
+    line = {"metric": "greedy decode tok/s (embedding + 28-layer expert stack + 248,320-id LM head + argmax)",
+            "value": round(args.steps / (t_ms / 1000.0), 2), "unit": "tok/s", "n_gpus": 1, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(t_ms / args.steps, 4), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "u2 codes x bf16 -> f32; bf16 head -> f32 logits",
+            "data": "synthetic",
+            "config": {"workload": "f4_greedy_loop_c1_stack_vocab248320", "layers": cfg.layers, "hidden": cfg.hidden,
+                       "experts": cfg.experts, "top_k": cfg.top_k, "inter": cfg.inter, "vocab": V, "batch": 1,
+                       "l2": "inputs larger than L2: 2.2 GB read per token"},
+            "roofline": roof, "clocks": clocks, "gpu_launches": loop.launches_per_step * args.steps,
+            "device_error": dev_err, "e2e": e2e}
+    print(json.dumps(line), flush=True)
+
+
 def main() -> int:
     args = parse()
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -1135,6 +1237,8 @@ def main() -> int:
             run_f3(args, rank, world, local_rank)
         elif args.config == "f3moe":
             run_f3moe(args, rank, world, local_rank)
+        elif args.config == "f4":
+            run_f4(args, rank, world, local_rank)
         elif args.config in ("c3", "c3n"):
             run_c3(args, rank, world, local_rank)
         elif args.config == "c4" or (world > 1 and args.config == "c1" and not args.replicas):

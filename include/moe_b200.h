@@ -711,6 +711,56 @@ int moe_p1_get_total_stats(void *h, int num_layers, uint64_t *out_stats);
 uint64_t moe_p1_copy_errors(void *h);          /* rows that could not be copied (short reads, bad ids) */
 uint64_t moe_p1_launches(void *h);             /* control and copy kernels launched so far */
 
+/* ------------------------------------------------------------------------------------ */
+/* Token loop around the stack: embedding rows, LM-head logits, next-token choice.          */
+/* ------------------------------------------------------------------------------------ */
+
+/*
+ * out[t] = table[ids[t]] (bf16 rows of H). The prompt/next-token embedding lookup of the
+ * reference's decode loop (mlx-qwen38/server.py:148-151,184-185, loader.py:1150-1180: the
+ * model call on token ids). ids int32 on the device; an id outside [0, V) gives a zero row and
+ * sets bit 2 of the device error word. H % 8 == 0, table/out 16-byte aligned.
+ */
+int moe_embed_tokens(const void *table, int V, int H, const int32_t *ids, int T, void *out, void *stream);
+
+/*
+ * logits [T, V] fp32 = head [V, H] bf16 x rows [T, H] bf16 (T <= 4): the LM head that yields
+ * `out.logits` in the reference's loop (server.py:150-151,185). Every bf16 x bf16 product is
+ * exact in fp32; each row's products are summed in double in a fixed order and rounded once to
+ * fp32 (results do not depend on the launch configuration).
+ */
+int moe_lm_head_logits(const void *head, int V, int H, const void *x, int T, float *logits, void *stream);
+
+/* Bytes of workspace moe_lm_head_argmax needs (8 per token row). */
+size_t moe_lm_head_argmax_workspace_bytes(int T);
+
+/*
+ * The LM head and the greedy choice in one pass (loader.py:1171-1176: lm(cur_tok) then
+ * mx.argmax(out.logits[:, -1:, :])): ids[t] = the first index of the maximum of the logits
+ * moe_lm_head_logits computes (same values; logits may be NULL when only the ids are wanted).
+ * The workspace (8-byte aligned) must be zero-filled before its first use; every call leaves it
+ * zero-filled again, so calls that share one must not overlap on the GPU.
+ */
+int moe_lm_head_argmax(const void *head, int V, int H, const void *x, int T, float *logits, int32_t *ids,
+                       void *workspace, size_t workspace_bytes, void *stream);
+
+/* Bytes of workspace moe_sample_tokens needs (temperature > 0 only). */
+size_t moe_sample_workspace_bytes(int T, int V);
+
+/*
+ * Next token per row of logits [T, V] fp32, replacing server.py:93-110 `_sample_next_token`:
+ * temperature <= 0: argmax (the first index of the maximum, as mx.argmax);
+ * temperature > 0: scaled = logits / temperature; with 0 < top_p < 1 the candidates are the
+ * largest probabilities of softmax(scaled) whose mass reaches top_p (every token tied at the
+ * boundary probability is kept; the reference keeps the boundary tokens in its sort order);
+ * one categorical draw from softmax(scaled) over the candidates by the Gumbel-max rule, the
+ * uniform variate of (seed, counter, row, index) from a splitmix64 hash (a different random
+ * stream from MLX's; the same (seed, counter) gives the same tokens). top_p in (0, 1].
+ * ids int32 [T] on the device.
+ */
+int moe_sample_tokens(const float *logits, int T, int V, float temperature, float top_p, uint64_t seed,
+                      uint64_t counter, int32_t *ids, void *workspace, size_t workspace_bytes, void *stream);
+
 /*
  * Device-side error word (bit 1: a bounded mbarrier/flag wait gave up, bit 2: invalid
  * input seen by a kernel, bit 4: an expert-parallel peer did not signal within 2 s). Returns the current value (>= 0) and clears it when `clear`.

@@ -39,6 +39,12 @@ SIGNATURES: dict[str, tuple] = {
     "moe_router_workspace_bytes": (SZ, [I, I, I]),
     "moe_router_topk": (I, [P, I, I, I, I, P, P, P, I, I, I, P, P, P, I, P, P, P, P, P, P, P, SZ, P]),
     "moe_router_topk_noalloc": (I, [P, I, I, I, I, P, P, P, I, I, I, P, P, P, I, P, P, P, P, P, P, P]),
+    "moe_embed_tokens": (I, [P, I, I, P, I, P, P]),
+    "moe_lm_head_logits": (I, [P, I, I, P, I, P, P]),
+    "moe_lm_head_argmax_workspace_bytes": (SZ, [I]),
+    "moe_lm_head_argmax": (I, [P, I, I, P, I, P, P, P, SZ, P]),
+    "moe_sample_workspace_bytes": (SZ, [I, I]),
+    "moe_sample_tokens": (I, [P, I, I, ctypes.c_float, ctypes.c_float, U64, U64, P, P, SZ, P]),
     "moe_experts_gateup": (I, [P, I, I, I, I, I, P, P, P, P, P, P, P, I, I, I, P, P]),
     "moe_experts_down": (I, [P, I, I, I, I, I, P, P, P, P, P, I, I, I, P, P, P, P, P]),
     "moe_device_error": (I, [I]),

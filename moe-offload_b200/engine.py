@@ -11,8 +11,10 @@ the reference's result keys (prefill of the prompt's rows through every layer, t
 decode steps; windowed hit rates from the decode totals) and `collect_stats` with the
 reference's layout. A prompt is `prompt_tokens` rows of seeded N(0, 1) hidden states (from
 `user_content`: one row per UTF-8 byte when no count is given); a decode step feeds a fresh
-N(0, 1) row (there is no language-model head to produce the next token's embedding), so
-`generated_ids` and `generated_text` stay empty.
+N(0, 1) row, and `generated_ids` / `generated_text` stay empty. With `vocab_size` the engine
+also carries the token loop (`tokens.py`): a seeded embedding table and LM head of that many
+ids and a byte tokenizer, so the prompt is its UTF-8 byte ids, each decode step feeds the
+previous step's argmax id, and `generate_stream` yields ids as the reference's server loop does.
 """
 from __future__ import annotations
 
@@ -26,6 +28,8 @@ import torch
 from . import checkpoint
 from .offload import HostExpertPool, OffloadStack, compute_layer_capacities
 from .synthetic import C2, StackConfig, dev_bf16_normal, dev_stack
+from .tokens import ByteTokenizer, TokenHead
+from .tokens import generate_stream as _generate_stream
 
 
 class OffloadEngine:
@@ -37,7 +41,8 @@ class OffloadEngine:
 
     def __init__(self, model_path=None, budget_gb: float | None = None, budget_pct: float | None = 20.0,
                  alloc_mode: str = "even", prefetch: bool = True, prefetch_top_m: int = 12, prefetch_cap: int = 3,
-                 *, config: StackConfig = C2, device="cuda:0", top_k: int | None = None):
+                 *, config: StackConfig = C2, device="cuda:0", top_k: int | None = None,
+                 vocab_size: int | None = None):
         t0 = time.perf_counter()
         self.model_path = model_path
         self.device = torch.device(device)
@@ -71,6 +76,13 @@ class OffloadEngine:
                                   prefetch=prefetch, prefetch_top_m=prefetch_top_m, prefetch_cap=prefetch_cap,
                                   expert_bytes=config.expert_bytes)
         self.cached_modules = {l: self.stack.layers[l] for l in range(1, L)}
+        # token loop (server.py:113-199): a seeded embedding / LM head of vocab_size ids and the
+        # byte tokenizer, when asked for; without it the loop feeds seeded hidden rows
+        self.token_head = self.tokenizer = None
+        if vocab_size is not None:
+            self.token_head = TokenHead.synthetic(vocab_size, config.hidden, self.device, seed=config.seed + 101)
+            self.tokenizer = ByteTokenizer(vocab_size)
+        self._last_timings: dict[str, Any] = {}
         torch.cuda.synchronize(self.device)
         self.load_seconds = time.perf_counter() - t0
 
@@ -102,6 +114,18 @@ class OffloadEngine:
         return dev_bf16_normal((n, self.config.hidden), self.device, gen)
 
     # ------------------------------------------------------------------ generation
+    def generate_stream(self, prompt_ids: list[int], max_tokens: int, temperature: float = 0.0, top_p: float = 1.0,
+                        stop_ids=None, seed: int = 0):
+        """server.py:113-199 `_generate_stream_impl`: token ids of the continuation of prompt_ids,
+        one per decode step (greedy when temperature <= 0, else sampled with top_p), stopping at
+        the tokenizer's eos id, any of stop_ids, or max_tokens. Timings land in _last_timings."""
+        if self.token_head is None:
+            raise RuntimeError("this engine has no token head: construct it with vocab_size=...")
+        stops = {self.tokenizer.eos_token_id} | (set(int(x) for x in stop_ids) if stop_ids is not None else set())
+        self._last_timings = {}
+        return _generate_stream(self.stack, self.token_head, list(prompt_ids), max_tokens, temperature, top_p,
+                                stops, seed, self._last_timings)
+
     def generate_greedy(self, user_content: str = "", max_new_tokens: int = 128, reset_cache_before: bool = False,
                         reset_stats_before: bool = False, *, prompt_tokens: int | None = None) -> dict[str, Any]:
         """loader.py:1125-1244 with the same result keys."""
@@ -109,16 +133,32 @@ class OffloadEngine:
             self.reset_caches()
         if reset_stats_before:
             self.reset_stats()
-        n_prefill = prompt_tokens if prompt_tokens is not None else max(1, len(user_content.encode()))
         seed = int.from_bytes(hashlib.sha256(user_content.encode()).digest()[:4], "little")
-        prompt = self._rows(n_prefill, seed)
-        dec_rows = self._rows(max(1, max_new_tokens), seed + 1)
         dev = self.device
+        head = self.token_head
+        if head is not None:
+            # token loop: the prompt's byte ids (or prompt_tokens seeded byte ids), each decode step
+            # feeding the previous step's argmax id (loader.py:1150-1190)
+            if prompt_tokens is not None:
+                g = torch.Generator().manual_seed(seed)
+                prompt_ids = torch.randint(0, 256, (prompt_tokens,), generator=g).tolist()
+            else:
+                prompt_ids = self.tokenizer.encode(user_content) or [0]
+            n_prefill = len(prompt_ids)
+            ids_dev = torch.tensor(prompt_ids, dtype=torch.int32).to(dev)
+            prompt = head.embed(ids_dev)
+        else:
+            n_prefill = prompt_tokens if prompt_tokens is not None else max(1, len(user_content.encode()))
+            prompt = self._rows(n_prefill, seed)
+            dec_rows = self._rows(max(1, max_new_tokens), seed + 1)
+        generated_ids: list[int] = []
 
         # 1. prefill
         torch.cuda.synchronize(dev)
         t_pre0 = time.perf_counter()
-        self.stack.prefill(prompt)
+        out = self.stack.prefill(prompt)
+        if head is not None:
+            cur = head.argmax(out[-1:].contiguous())
         torch.cuda.synchronize(dev)
         prefill_sec = time.perf_counter() - t_pre0
 
@@ -129,8 +169,13 @@ class OffloadEngine:
         step_latencies_ms: list[float] = []
         t_dec0 = time.perf_counter()
         for d_idx in range(max_new_tokens):
+            if head is not None:
+                generated_ids.append(int(cur.item()))
             t_step0 = time.perf_counter()
-            self.stack.decode_token(dec_rows[d_idx:d_idx + 1])
+            if head is not None:
+                head.argmax(self.stack.decode_token(head.embed(cur)), out=cur)
+            else:
+                self.stack.decode_token(dec_rows[d_idx:d_idx + 1])
             torch.cuda.synchronize(dev)
             step_latencies_ms.append(round((time.perf_counter() - t_step0) * 1000.0, 3))
             if (d_idx + 1) == mid_tok:
@@ -165,8 +210,8 @@ class OffloadEngine:
             "steady_window_pure_hit_rate": round(w2_lru / w2_req, 5),
             "steady_window_effective_hit_rate": round((w2_lru + w2_pref) / w2_req, 5),
             "steady_window_tok_per_s": round((max_new_tokens - mid_tok) / max(1e-6, w2_sec), 3),
-            "generated_ids": [],
-            "generated_text": "",
+            "generated_ids": generated_ids,
+            "generated_text": self.tokenizer.decode(generated_ids) if head is not None else "",
             "step_latencies_ms": step_latencies_ms,
         }
 

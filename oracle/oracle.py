@@ -224,3 +224,86 @@ def ref_lru_lib(version: int = 1):
     if not os.path.exists(path):
         return None
     return ctypes.CDLL(path)
+
+
+# ---------------------------------------------------------------- token loop (numpy)
+#
+# The step after the routed block: the LM head and the next-token choice of the reference's
+# decode loop (mlx-qwen38/server.py:93-110 `_sample_next_token`, loader.py:1153-1180
+# `mx.argmax(out.logits[:, -1:, :])`), restated with the arithmetic the library documents for
+# moe_lm_head_logits / moe_sample_tokens: exact bf16 x bf16 products, double sums in the
+# kernel's fixed order (lane l of 32 takes the 8-element chunks l, l + 32, ... in order, then an
+# xor butterfly over the lanes), one rounding to fp32; argmax = first index of the maximum;
+# sampling = Gumbel-max over the top-p set with a splitmix64 hash of (seed, counter, row, index).
+
+def lm_head_logits(head_bf16: np.ndarray, x_bf16: np.ndarray) -> np.ndarray:
+    """head u16 [V, H], x u16 [T, H] -> fp32 [T, V]."""
+    w = bf16_to_f32(np.ascontiguousarray(head_bf16, dtype=np.uint16))
+    x = bf16_to_f32(np.ascontiguousarray(x_bf16, dtype=np.uint16))
+    V, H = w.shape
+    T = x.shape[0]
+    nch = H // 8
+    out = np.empty((T, V), dtype=np.float32)
+    for v0 in range(0, V, 256):
+        wv = w[v0:v0 + 256]
+        prod = (wv[None, :, :] * x[:, None, :]).astype(np.float64)          # exact products
+        prod = prod.reshape(T, wv.shape[0], nch, 8)
+        lanes = np.zeros((T, wv.shape[0], 32), dtype=np.float64)
+        for lane in range(32):
+            seq = prod[:, :, lane::32, :].reshape(T, wv.shape[0], -1)
+            if seq.shape[-1]:
+                lanes[:, :, lane] = np.cumsum(seq, axis=-1)[..., -1]          # sequential order
+        idx = np.arange(32)
+        for off in (16, 8, 4, 2, 1):
+            lanes = lanes + lanes[..., idx ^ off]
+        out[:, v0:v0 + 256] = lanes[..., 0].astype(np.float32)
+    return out
+
+
+def _mix64(z: np.ndarray) -> np.ndarray:
+    z = (z ^ (z >> np.uint64(30))) * np.uint64(0xbf58476d1ce4e5b9)
+    z = (z ^ (z >> np.uint64(27))) * np.uint64(0x94d049bb133111eb)
+    return z ^ (z >> np.uint64(31))
+
+
+def sample_uniform(seed: int, counter: int, row: int, V: int) -> np.ndarray:
+    """The library's uniform variates in (0, 1) for indices 0..V-1 of one row."""
+    with np.errstate(over="ignore"):
+        s = np.uint64(seed & 0xFFFFFFFFFFFFFFFF) ^ (np.uint64(counter & 0xFFFFFFFFFFFFFFFF) *
+                                                    np.uint64(0x9e3779b97f4a7c15))
+        base = _mix64(np.array([s], dtype=np.uint64))[0]
+        key = (np.uint64(row & 0xFFFFFFFF) << np.uint64(32)) | np.arange(V, dtype=np.uint64)
+        z = _mix64(base ^ key)
+    return ((z >> np.uint64(11)).astype(np.float64) + 0.5) * 2.0 ** -53
+
+
+def sample_tokens(logits: np.ndarray, temperature: float = 0.0, top_p: float = 1.0, seed: int = 0,
+                  counter: int = 0) -> np.ndarray:
+    """fp32 [T, V] -> int32 [T] (moe_sample_tokens' rule)."""
+    lg = np.ascontiguousarray(logits, dtype=np.float32)
+    T, V = lg.shape
+    out = np.empty(T, dtype=np.int32)
+    for t in range(T):
+        if not temperature > 0.0:
+            out[t] = int(np.argmax(lg[t]))
+            continue
+        s = lg[t] / np.float32(temperature)
+        p = np.exp(s - s.max()).astype(np.float32)
+        keep = p > 0
+        if 0.0 < top_p < 1.0:
+            z = float(p.astype(np.float64).sum())
+            need = top_p * z
+            lo, hi = 0, int(np.float32(1.0).view(np.uint32))
+            while lo < hi:
+                mid = lo + (hi - lo + 1) // 2
+                fm = np.uint32(mid).view(np.float32)
+                if float(p[p >= fm].astype(np.float64).sum()) >= need:
+                    lo = mid
+                else:
+                    hi = mid - 1
+            keep &= p >= np.uint32(lo).view(np.float32)
+        u = sample_uniform(seed, counter, t, V)
+        key = (s.astype(np.float64) - np.log(-np.log(u))).astype(np.float32)
+        key = np.where(keep, key, -np.inf).astype(np.float32)
+        out[t] = int(np.argmax(key))
+    return out
