@@ -1148,8 +1148,9 @@ def run_f4(args, rank: int, world: int, local_rank: int) -> None:
     clk.start()
     s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     s.record()
+    run = loop.graph.replay if loop.graph is not None else loop._body     # the graph, or the direct step
     for _ in range(args.steps):
-        loop.graph.replay()
+        run()
     e.record()
     torch.cuda.synchronize()
     clocks = clk.stop()

@@ -183,6 +183,7 @@ class ResidentTokenLoop:
         self.host_id = torch.zeros((1,), dtype=torch.int32, pin_memory=True)
         self.counter = 0
         self.graph = None
+        self._graph_failed = False
         # embed, stack, head (+ the argmax's id kernel when greedy) / head + sample
         self.launches_per_step = 4
 
@@ -201,22 +202,31 @@ class ResidentTokenLoop:
         self.cur.fill_(int(token_id))
         self.counter = 0
 
+    def _capture(self) -> None:
+        cur = torch.cuda.current_stream(self.head.device)
+        s = torch.cuda.Stream(device=self.head.device)
+        s.wait_stream(cur)
+        try:
+            with torch.cuda.stream(s):
+                save = self.cur.clone()
+                self._body()                                      # warm-up outside the graph
+                self.cur.copy_(save)
+            s.synchronize()
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=s):
+                self._body()
+            self.graph = g
+        except RuntimeError:
+            # a driver that cannot capture the cooperative stack launch: run the step directly
+            self._graph_failed = True
+            torch.cuda.synchronize(self.head.device)
+        cur.wait_stream(s)
+
     def step(self) -> int:
         self.counter += 1
-        if self.temperature <= 0.0:
-            if self.graph is None:
-                s = torch.cuda.Stream(device=self.head.device)
-                s.wait_stream(torch.cuda.current_stream(self.head.device))
-                with torch.cuda.stream(s):
-                    save = self.cur.clone()
-                    self._body()                                  # warm-up outside the graph
-                    self.cur.copy_(save)
-                s.synchronize()
-                g = torch.cuda.CUDAGraph()
-                with torch.cuda.graph(g, stream=s):
-                    self._body()
-                torch.cuda.current_stream(self.head.device).wait_stream(s)
-                self.graph = g
+        if self.temperature <= 0.0 and self.graph is None and not self._graph_failed:
+            self._capture()
+        if self.temperature <= 0.0 and self.graph is not None:
             self.graph.replay()
         else:
             self._body()
