@@ -250,7 +250,8 @@ sample_kernel(const float *__restrict__ logits, int V, float temperature, float 
         }
     }
     g = block_argmax(g, sv, si);
-    if (tid == 0) ids[t] = g.i < V ? g.i : m.i;
+    // no finite candidate (logits / temperature overflowed): the argmax of the scaled logits, else 0
+    if (tid == 0) ids[t] = g.i < V ? g.i : (m.i < V ? m.i : 0);
 }
 
 }  // namespace

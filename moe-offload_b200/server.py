@@ -23,7 +23,7 @@ import uuid
 from http.server import BaseHTTPRequestHandler, ThreadingHTTPServer
 from typing import Any, Iterator
 
-_DONE = object()
+MAX_BODY_BYTES = 16 << 20
 
 
 class GenerationWorker:
@@ -176,6 +176,10 @@ class Handler(BaseHTTPRequestHandler):
         srv = self.server
         try:
             n = int(self.headers.get("Content-Length", "0"))
+            if n > MAX_BODY_BYTES:
+                self.close_connection = True          # the unread body must not reach the next request
+                self._send_error_json(413, f"request body over {MAX_BODY_BYTES} bytes", "invalid_request_error")
+                return
             req = json.loads(self.rfile.read(n) or b"{}")
             if not isinstance(req, dict):
                 raise ValueError("the request body must be a JSON object")

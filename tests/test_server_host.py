@@ -124,3 +124,16 @@ def test_bad_requests(server, path, body, msg):
     st, _, data = _req(srv, "POST", path, body)
     out = json.loads(data)
     assert st == 400 and out["error"]["type"] == "invalid_request_error" and msg in out["error"]["message"]
+
+
+def test_oversized_body_refused(server):
+    srv, _ = server
+    from moe_offload_b200.server import MAX_BODY_BYTES
+    c = http.client.HTTPConnection("127.0.0.1", srv.server_address[1], timeout=10)
+    c.putrequest("POST", "/v1/completions")
+    c.putheader("Content-Type", "application/json")
+    c.putheader("Content-Length", str(MAX_BODY_BYTES + 1))
+    c.endheaders()
+    r = c.getresponse()
+    assert r.status == 413
+    c.close()
