@@ -896,6 +896,16 @@ def run_c3(args, rank: int, world: int, local_rank: int) -> None:
     router_ms = ev[0].elapsed_time(ev[1]) / n_rep
     experts_ms = ev[1].elapsed_time(ev[2]) / n_rep
 
+    # routing of one step, layer by layer: experts that receive at least one token (the bytes a
+    # layer's GEMMs must read; the synthetic distributions concentrate deep layers' routing)
+    active = []
+    h = h0[0]
+    for li, ly in enumerate(layers):
+        o = ops.prefill_layer(h, ly.router, ly.gate, ly.up, ly.down, cfg.top_k, norm=True, resid=h,
+                              out=bufs[li & 1])
+        active.append(int(torch.unique(o["inds"]).numel()))
+        h = o["y"]
+
     # e2e through the public API: the prompt's hidden states from pinned host memory, the
     # final hidden states back to pinned host memory, every step
     e2e = None
@@ -931,7 +941,10 @@ def run_c3(args, rank: int, world: int, local_rank: int) -> None:
             "frac": round(achieved / tf_peak, 4), "traffic": None,
             "algorithmic_flops_per_launch": flops_layer, "algorithmic_bytes_per_launch": bytes_layer,
             "launch_ms": round(experts_ms, 4), "hbm_frac": round(bytes_layer / (experts_ms / 1000.0) / 1e9 / hbm_peak, 4),
-            "router_ms_per_layer": round(router_ms, 4), "peak_source": tf_src}
+            "router_ms_per_layer": round(router_ms, 4), "peak_source": tf_src,
+            "active_experts_per_layer": {"layer0": active[0], "mean": round(sum(active) / len(active), 1),
+                                         "min": min(active), "max": max(active)},
+            "active_expert_bytes_per_layer": int(sum(active) / len(active) * cfg.expert_bytes)}
     from moe_offload_b200 import _lib
     dev_err = int(_lib.call("moe_device_error", 1))
     cpu = None
