@@ -58,9 +58,9 @@ class GenerationWorker:
                             pass
                     out_q.put(("done", dict(getattr(self.engine, "_last_timings", {}) or {})))
 
-    def stream(self, *args, **kwargs) -> Iterator[int]:
-        """Yields token ids; the generator's `timings` attribute is not available, read
-        `last_timings` after exhausting it."""
+    def stream(self, *args, timings: dict | None = None, **kwargs) -> Iterator[int]:
+        """Yields token ids; once the generation has ended, `timings` (when given) holds that
+        generation's prefill / decode timings."""
         out_q: queue.Queue = queue.Queue()
         cancel = threading.Event()
         self.jobs.put((args, kwargs, out_q, cancel))
@@ -73,14 +73,19 @@ class GenerationWorker:
                 elif kind == "err":
                     raise val
                 else:
-                    self.last_timings = val
+                    if timings is not None:
+                        timings.update(val)
                     finished = True
                     return
         finally:
             if not finished:
                 cancel.set()
-                while out_q.get()[0] != "done":
-                    pass
+                while True:
+                    kind, val = out_q.get()
+                    if kind == "done":
+                        if timings is not None:
+                            timings.update(val)
+                        break
 
 
 def _requested_max(req: dict, default: int) -> int:
@@ -225,7 +230,9 @@ class Handler(BaseHTTPRequestHandler):
         ids: list[int] = []
         text, sent, finish = "", 0, "length"
         t0 = time.perf_counter()
-        gen = srv.worker.stream(prompt_ids, max_tokens, temperature=temperature, top_p=top_p, seed=seed)
+        timings: dict = {}
+        gen = srv.worker.stream(prompt_ids, max_tokens, temperature=temperature, top_p=top_p, seed=seed,
+                                timings=timings)
         if stream:
             self.send_response(200)
             self.send_header("Content-Type", "text/event-stream")
@@ -248,7 +255,6 @@ class Handler(BaseHTTPRequestHandler):
                     break
         finally:
             gen.close()
-        timings = getattr(srv.worker, "last_timings", {}) or {}
         if finish == "length" and timings.get("stopped_by_token"):
             finish = "stop"
         usage = {"prompt_tokens": len(prompt_ids), "completion_tokens": len(ids),
