@@ -181,6 +181,30 @@ def cpu_layer_sample(seconds: float = 12.0) -> dict:
                       f"(MLX is not installable here)"}
 
 
+def cpu_token_sample(vocab: int, hidden: int, seconds: float = 12.0, head_rows: int = 32768) -> dict:
+    """Bounded CPU baseline of the f4 token step: the c1 stack's token-layers (as
+    cpu_layer_sample) plus the LM head as the reference's CPU path would run it, one fp32 BLAS
+    matrix-vector product (numpy, all BLAS threads) over `head_rows` rows of the head, scaled to
+    the vocabulary, and its argmax; the embedding lookup is negligible."""
+    import numpy as np
+
+    stack = cpu_layer_sample(seconds)
+    rng = np.random.default_rng(5)
+    w = rng.normal(0.0, 0.02, (head_rows, hidden)).astype(np.float32)
+    x = rng.normal(0.0, 1.0, (hidden,)).astype(np.float32)
+    int(np.argmax(w @ x))                                   # warm-up
+    reps = 5
+    t0 = time.perf_counter()
+    for _ in range(reps):
+        int(np.argmax(w @ x))
+    head_s = (time.perf_counter() - t0) / reps * vocab / head_rows
+    token_s = 1.0 / stack["value"] + head_s
+    return {"value": round(1.0 / token_s, 4), "unit": "tok/s", "cores": stack["cores"], "kind": "port",
+            "head_s_per_token": round(head_s, 5), "stack_tok_s": stack["value"],
+            "sample": stack["sample"] + f"; the LM head as an fp32 BLAS matvec over {head_rows} of {vocab} "
+                      f"rows (numpy), scaled to the vocabulary"}
+
+
 def c1_config(cfg, world: int) -> dict:
     """The workload description both arms print for the c1 stack (same dict, same keys)."""
     return {"workload": cfg.name, "layers": cfg.layers, "hidden": cfg.hidden, "experts": cfg.experts,
@@ -1223,7 +1247,8 @@ def run_f4(args, rank: int, world: int, local_rank: int) -> None:
                        "experts": cfg.experts, "top_k": cfg.top_k, "inter": cfg.inter, "vocab": V, "batch": 1,
                        "l2": "inputs larger than L2: 2.2 GB read per token"},
             "roofline": roof, "clocks": clocks, "gpu_launches": loop.launches_per_step * args.steps,
-            "device_error": dev_err, "e2e": e2e}
+            "device_error": dev_err, "e2e": e2e,
+            "cpu_baseline": None if args.no_cpu else cpu_token_sample(V, cfg.hidden)}
     print(json.dumps(line), flush=True)
 
 
